@@ -1,0 +1,256 @@
+/*
+ * kvmret — B200-native KVMem per-step KV retrieval path, C ABI.
+ *
+ * The path: score the current GQA query against per-block mean-key summaries,
+ * pick a deterministic block top-k (sink + mandatory pinning), diff it against
+ * the current working set, stage the selected 128-token blocks from the pinned
+ * host repository / HBM block pool into a chronologically ordered window with
+ * K re-rotated (RoPE) at its window position (dequant -> RoPE -> FWHT -> requant
+ * for q8_0 K), and append completed blocks back to the repository with their
+ * summaries.
+ *
+ * Every entry point returns an int status (KVMRET_OK == 0, negative on error);
+ * kvmret_last_error() describes the last failure on the calling thread. No C++
+ * exception crosses this boundary. Pointers named *_dev are device pointers,
+ * *_host are host pointers. A context is bound to one CUDA device and must not
+ * be used concurrently from two threads (the reference's rule for an execution
+ * state, src/adapter/llama-kvmem-hooks.h:46-50).
+ *
+ * Reference interfaces replaced (paths inside zyf32453/kvmem-llama.cpp) are
+ * cited per function.
+ */
+#ifndef KVMRET_H
+#define KVMRET_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVMRET_OK 0
+#define KVMRET_ERR_ARG (-1)     /* bad argument or size out of range */
+#define KVMRET_ERR_CUDA (-2)    /* a CUDA runtime call failed */
+#define KVMRET_ERR_STATE (-3)   /* call not valid in the current state */
+#define KVMRET_ERR_NOMEM (-4)   /* device or pinned host allocation failed */
+
+/* KV element formats; values are ggml_type ids (F16 = 1, Q4_0 = 2, Q8_0 = 8). */
+#define KVMRET_TYPE_F16 1
+#define KVMRET_TYPE_Q4_0 2
+#define KVMRET_TYPE_Q8_0 8
+
+typedef struct kvmret_ctx kvmret_ctx;
+typedef struct kvmret_table kvmret_table;
+
+/*
+ * Context configuration. Mirrors the parts of llama_kvmem_params
+ * (src/adapter/llama-kvmem-hooks.h:19-39), KvMemStoreConfig
+ * (kvmem/include/kvmem/kvmem_store.hpp:231-327) and the adapter's model
+ * geometry / RoPE config (src/adapter/llama-memory-kvmem.cpp:929-944) that the
+ * retrieval path reads.
+ */
+typedef struct kvmret_config {
+    uint32_t n_layer;        /* layers held by this context (a shard) */
+    uint32_t n_head;         /* query heads */
+    uint32_t n_head_kv;      /* KV heads */
+    uint32_t d_head;         /* head dim: 64, 128 or 256 */
+    uint32_t block_tokens;   /* tokens per block (reference default 128) */
+    uint32_t max_blocks;     /* history capacity in blocks */
+    uint32_t budget_blocks;  /* selection budget W (select_budget / block_tokens) */
+    uint32_t reserve_blocks; /* gen-reserve window slots beyond the budget */
+    uint32_t sink_blocks;    /* always-kept prefix (reference default 1) */
+    uint32_t recent_blocks;  /* always-kept suffix (reference default 0) */
+    uint32_t pool_blocks;    /* HBM raw-block pool slots; 0 -> budget + reserve */
+    int32_t k_type;          /* KVMRET_TYPE_F16 or KVMRET_TYPE_Q8_0 */
+    int32_t v_type;          /* KVMRET_TYPE_F16, _Q8_0 or _Q4_0 (copied as bytes) */
+    int32_t attn_rot_k;      /* FWHT on re-roped quantised K: -1 auto (on for
+                                quantised K, n_embd_head % 64 == 0), 0 off, 1 on */
+    int32_t tie_higher_id;   /* top-k tie-break: 1 higher id (reference), 0 lower */
+    int32_t pool_cache;      /* 1: keep evicted blocks in free pool slots as a cache */
+    int32_t immutable_source_k; /* KvMemStoreConfig::immutable_source_k (plan flags) */
+    uint32_t n_rot;          /* rotated dims (== d_head for NeoX full rotary) */
+    float freq_base;         /* rope_freq_base */
+    float freq_scale;        /* rope_freq_scale */
+    int32_t device;          /* CUDA device ordinal */
+} kvmret_config;
+
+/* Counters for one apply step; the KVMEM_RETR_SUM buckets of
+ * src/adapter/llama-memory-kvmem.cpp:4198-4216 that this path owns. */
+typedef struct kvmret_step_stats {
+    uint32_t n_selected;      /* blocks in the new window */
+    uint32_t n_stage_in;      /* plan.stage_in (newly in the working set) */
+    uint32_t n_stage_out;     /* plan.stage_out */
+    uint32_t n_skip;          /* plan remaps with skip set */
+    uint32_t n_h2d_blocks;    /* blocks copied host -> HBM pool this step */
+    uint32_t n_assembled;     /* window slots rewritten (new + moved) */
+    uint32_t n_moved;         /* window slots rewritten from a resident block */
+    uint32_t total_window_tokens;
+    uint64_t h2d_bytes;       /* host -> device bytes of the stage-in */
+    uint64_t assemble_bytes;  /* HBM bytes read + written by window assembly */
+} kvmret_step_stats;
+
+/* Defaults as the reference CLI/server recipes use them. */
+void kvmret_config_default(kvmret_config *cfg);
+
+/* Bytes of one token row of a format (e.g. q8_0 of 1024 elements = 1088). */
+uint64_t kvmret_row_bytes(int32_t type, uint32_t n_elems);
+
+const char *kvmret_last_error(void);
+const char *kvmret_version(void);
+
+/* ---- context (llama_kvmem_execution_create / kvmem_gpu_state_create,
+ *      src/adapter/llama-kvmem-stagein.cu:345-354; llama_memory_kvmem ctor,
+ *      src/adapter/llama-memory-kvmem.cpp:829-998) ---- */
+int kvmret_create(const kvmret_config *cfg, kvmret_ctx **out);
+void kvmret_destroy(kvmret_ctx *ctx);
+/* The context's compute stream (cudaStream_t). */
+void *kvmret_stream(kvmret_ctx *ctx);
+int kvmret_sync(kvmret_ctx *ctx);
+
+/* ---- host repository (RawKvStore, kvmem/include/kvmem/raw_kv_store.hpp:40-170):
+ *      pinned, mapped host memory laid out [block][layer][K rows | V rows]. ---- */
+void *kvmret_repo_host(kvmret_ctx *ctx);
+uint64_t kvmret_repo_unit_bytes(kvmret_ctx *ctx);  /* one (block, layer): K + V */
+uint64_t kvmret_repo_k_bytes(kvmret_ctx *ctx);     /* K part of a unit */
+
+/*
+ * Append tokens [pos0, pos0 + n_tok) for every layer of the context
+ * (S14 + S2). Replaces the harvest path: RawKvStore::write_layer_mean_k
+ * (kvmem/src/host/raw_kv_store.cpp:685-705), write_layer_k_gpu / v_gpu
+ * (:600-683), KvMemStore::register_append (kvmem/src/host/kvmem_store.cpp:
+ * 179-205) and harvest_full_blocks_async (src/adapter/llama-memory-kvmem.cpp:
+ * 3692-3729). pos0 must equal the current token count.
+ *   k_cap_dev: [n_layer][n_tok][n_head_kv * d_head] f16 pre-RoPE K (summary source)
+ *   k_rows_dev: [n_layer][n_tok][k row bytes] unrotated K in k_type (NULL: use
+ *               k_cap_dev, valid only when k_type is F16)
+ *   v_rows_dev: [n_layer][n_tok][v row bytes] V in v_type
+ * The summary of every touched block is its F32 token-order mean.
+ */
+int kvmret_append(kvmret_ctx *ctx, uint32_t pos0, uint32_t n_tok, const uint16_t *k_cap_dev,
+                  const void *k_rows_dev, const void *v_rows_dev);
+uint32_t kvmret_n_blocks(kvmret_ctx *ctx);
+uint32_t kvmret_n_tokens(kvmret_ctx *ctx);
+/* Summaries in the order the reference's mean_k returns them:
+ * out [n_blocks][n_layer][n_head_kv * d_head] f32 (host). */
+int kvmret_get_summaries(kvmret_ctx *ctx, float *out_host);
+
+/* ---- query accumulation (S1): q_sum_ / q_count_ of the adapter,
+ *      src/adapter/llama-memory-kvmem.cpp:3417-3432, reset :3300-3315,
+ *      llama_kvmem_get_query / set_query (src/adapter/llama-kvmem-hooks.h:247-248). ---- */
+int kvmret_query_reset(kvmret_ctx *ctx);
+/* q_dev: [n_layer][n_rows][n_head * d_head], f16 or f32. */
+int kvmret_query_add_f16(kvmret_ctx *ctx, const uint16_t *q_dev, uint32_t n_rows);
+int kvmret_query_add_f32(kvmret_ctx *ctx, const float *q_dev, uint32_t n_rows);
+/* Host copies of the accumulator: q_sum [n_layer][n_head * d_head], q_count [n_layer]. */
+int kvmret_query_set(kvmret_ctx *ctx, const float *q_sum_host, const uint32_t *q_count_host);
+int kvmret_query_get(kvmret_ctx *ctx, float *q_sum_host, uint32_t *q_count_host);
+
+/* ---- scoring (S3): llama_memory_kvmem::score_retrieval,
+ *      src/adapter/llama-memory-kvmem.cpp:4149-4196 ---- */
+/* Score every block; if scores_host != NULL copy the n_blocks f64 scores out. */
+int kvmret_score(kvmret_ctx *ctx, double *scores_host);
+/* Layer-sharded form: per-(layer, block) terms layer_sum / n_head_kv (f64) of
+ * this context's layers into its contribution buffer, without the reduction. */
+int kvmret_score_layers(kvmret_ctx *ctx);
+/* Device pointer to the contribution buffer [n_layer][contrib_stride] f64 and
+ * the per-layer "has query" flags [n_layer] u8. */
+const double *kvmret_contrib_dev(kvmret_ctx *ctx);
+const uint8_t *kvmret_layer_active_dev(kvmret_ctx *ctx);
+uint32_t kvmret_contrib_stride(kvmret_ctx *ctx);
+/* Reduce gathered contributions of ALL layers of the model, in layer order:
+ *   contrib_all_dev [n_layer_all][stride] f64, active_all_dev [n_layer_all] u8. */
+int kvmret_score_reduce(kvmret_ctx *ctx, const double *contrib_all_dev,
+                        const uint8_t *active_all_dev, uint32_t n_layer_all, uint32_t stride);
+
+/* ---- selection (S5/S6): llama_memory_kvmem::preview_retrieval
+ *      (src/adapter/llama-memory-kvmem.cpp:4327-4347) -> KvMemRuntime::
+ *      preview_reselect -> KvMemStore::pick_topk_blocks
+ *      (kvmem/src/host/kvmem_store.cpp:357-359, 482-623) ---- */
+/* Top-k over the current scores (after kvmret_score or kvmret_score_reduce).
+ * mandatory: block ids that consume budget, kept newest-first (retrieval_mandatory,
+ * src/adapter/llama-memory-kvmem.cpp:4306-4325). ids_out (capacity
+ * budget_blocks) receives the selection ascending; *n_out its length. */
+int kvmret_select(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
+                  uint32_t *ids_out, uint32_t *n_out);
+/* kvmret_score + kvmret_select. */
+int kvmret_preview(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
+                   uint32_t *ids_out, uint32_t *n_out);
+
+/* ---- apply (S7-S13): llama_memory_kvmem::apply_selection
+ *      (src/adapter/llama-memory-kvmem.cpp:4424-4543): KvMemStore::set_selection
+ *      (kvmem/src/host/kvmem_store.cpp:758-882), layout_gpu_slots_by_orig_pos
+ *      (src/adapter/llama-memory-kvmem.cpp:1958-2289), write_block_to_gpu
+ *      (:4000-4071) and kvmem_stagein_flush (src/adapter/llama-kvmem-stagein.cu:
+ *      669-790). Enqueued on the context stream; the window is valid once the
+ *      stream reaches this point. ---- */
+int kvmret_apply_selection(kvmret_ctx *ctx, const uint32_t *ids, uint32_t n_ids,
+                           kvmret_step_stats *stats);
+/* llama_kvmem_apply_retrieval (src/adapter/llama-memory-kvmem.cpp:4778-4782,
+ * apply_retrieval :4419-4422): preview + apply. ids_out may be NULL. */
+int kvmret_apply_retrieval(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
+                           uint32_t *ids_out, uint32_t *n_out, kvmret_step_stats *stats);
+
+/* The last plan's remap rows, 7 int32 each: block_id, n_tokens, from_base,
+ * to_base, working_k_resident, skip, raw_refresh (KvMemRemap,
+ * kvmem/include/kvmem/kvmem_store.hpp:75-95). Capacity budget_blocks rows. */
+int kvmret_last_plan(kvmret_ctx *ctx, int32_t *remaps_out, uint32_t *n_remaps,
+                     uint32_t *stage_in_out, uint32_t *n_stage_in,
+                     uint32_t *stage_out_out, uint32_t *n_stage_out);
+
+/* ---- window (where attention reads; the llama_kv_cache K/V layer tensors) ---- */
+/* Device base of layer `layer`'s K / V window: rows of kvmret_row_bytes(type,
+ * n_head_kv * d_head), cell = window_slot * block_tokens + token. */
+void *kvmret_window_k(kvmret_ctx *ctx, uint32_t layer);
+void *kvmret_window_v(kvmret_ctx *ctx, uint32_t layer);
+uint32_t kvmret_window_slots(kvmret_ctx *ctx);
+/* Current window: block id and RoPE base of each occupied slot (host). */
+int kvmret_window_layout(kvmret_ctx *ctx, uint32_t *ids_out, int32_t *bases_out, uint32_t *n_out);
+/* Copy window slots [slot0, slot0 + n_slots) of one layer's K (is_v = 0) or V
+ * to host memory after the context stream drains (read_gpu_block,
+ * src/adapter/llama-memory-kvmem.cpp:4600-4650). */
+int kvmret_window_read(kvmret_ctx *ctx, uint32_t layer, int is_v, uint32_t slot0,
+                       uint32_t n_slots, void *out_host);
+
+/* ---- stateless kernels on caller buffers (the kvmem_stagein_* / kvmem_d2d /
+ *      kvmem_meank surface, src/adapter/llama-kvmem-stagein.h:1-67). `stream`
+ *      is a cudaStream_t (NULL = legacy default stream). ---- */
+/* RoPE f16 K rows [n_tok][n_head_kv][d_head] at positions pos0 + t
+ * (kvmem_stagein_rope_neox, src/adapter/llama-kvmem-stagein.cu:534-569). */
+int kvmret_rope_f16(const uint16_t *k_dev, uint16_t *out_dev, uint32_t n_tok, uint32_t n_head_kv,
+                    uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                    float freq_scale, void *stream);
+/* q8_0 K rows: dequant -> RoPE at pos0 -> FWHT(fwht_n, 0 = off) -> q8_0
+ * (kvmem_stagein_enqueue_k + flush, src/adapter/llama-kvmem-stagein.cu:813-855, 746-785). */
+int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
+                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                     float freq_scale, uint32_t fwht_n, void *stream);
+/* Batched byte copies on the context stream, at most 8192 per call
+ * (kvmem_d2d_batched, src/adapter/llama-kvmem-stagein.cu:1002-1035, which uses
+ * its execution state's preallocated op buffer the same way). */
+int kvmret_d2d_batched(kvmret_ctx *ctx, const void *const *src, void *const *dst,
+                       const uint64_t *nbytes, int n);
+
+/* ---- host block table: the selection / plan logic alone, no GPU needed
+ *      (KvMemStore, kvmem/include/kvmem/kvmem_store.hpp:329-491). ---- */
+int kvmret_table_create(const kvmret_config *cfg, kvmret_table **out);
+void kvmret_table_destroy(kvmret_table *t);
+int kvmret_table_append(kvmret_table *t, uint32_t n_tokens);
+uint32_t kvmret_table_n_blocks(kvmret_table *t);
+/* The always-kept part of a selection: sink, mandatory newest-first, recent
+ * (kvmem/src/host/kvmem_store.cpp:497-534). kept_out [n_blocks] u8; returns
+ * via *need the number of blocks still to fill by score (0 when all fit). */
+int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_mandatory,
+                      uint8_t *kept_out, uint32_t *kept_count, uint32_t *need);
+/* set_selection + the runtime's spill/admit tier effect. remaps_out rows as
+ * kvmret_last_plan; counts_out[6]: n_stage_in, n_stage_out, n_remaps,
+ * total_window_tokens, selection_overlap_blocks, gpu_reused_blocks. */
+int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_ids,
+                               int force_raw_refresh, uint32_t *stage_in_out,
+                               uint32_t *stage_out_out, int32_t *remaps_out,
+                               uint32_t *counts_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVMRET_H */

@@ -1,0 +1,915 @@
+// Retrieval context: device state of one shard (layers) of one session and
+// the host orchestration of a retrieval step. Implements the C ABI of
+// include/kvmret.h; no C++ exception leaves this file.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "kvmret.h"
+#include "table.hpp"
+
+using kvmret::Job;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        const cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                                \
+            return fail(KVMRET_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_));            \
+    } while (0)
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+bool type_ok(int32_t t) {
+    return t == KVMRET_TYPE_F16 || t == KVMRET_TYPE_Q8_0 || t == KVMRET_TYPE_Q4_0;
+}
+
+// Host theta exactly as rope_neox_apply computes it (kvmem/src/host/rope.cpp:20-24).
+kvmret::Theta make_theta(uint32_t n_rot, float base, float scale) {
+    kvmret::Theta t{};
+    for (uint32_t i = 0; i < n_rot / 2 && i < 128; ++i) {
+        t.v[i] = std::pow(base, -2.0f * static_cast<float>(i) / static_cast<float>(n_rot));
+        t.v[i] *= scale;
+    }
+    return t;
+}
+
+// FWHT size applied to quantised K (kvmem_hadamard_nrot_k,
+// src/adapter/llama-kvmem-quant.h:238-244).
+uint32_t hadamard_nrot_k(uint32_t d_head) {
+    uint32_t nrot = 64;
+    do {
+        nrot *= 2;
+    } while (d_head % nrot == 0);
+    return nrot / 2;
+}
+
+}  // namespace
+
+struct kvmret_ctx {
+    kvmret_config cfg{};
+    // geometry
+    uint32_t E = 0, qdim = 0, ncap = 0, win_slots = 0, pool_slots = 0;
+    uint64_t k_row = 0, v_row = 0, unit_k = 0, unit = 0, slot_bytes = 0;
+    uint64_t win_k_layer = 0, win_v_layer = 0;
+    kvmret::AssembleGeom geom{};
+    kvmret::Theta theta{};
+    // device
+    float *summ = nullptr, *tail_sum = nullptr, *q_sum = nullptr, *qv = nullptr, *nq = nullptr;
+    uint32_t *q_count_dev = nullptr;
+    uint8_t *has_block = nullptr, *active = nullptr, *kept_dev = nullptr, *sel_dev = nullptr;
+    double *contrib = nullptr, *scores = nullptr;
+    uint8_t *pool = nullptr, *win_k = nullptr, *win_v = nullptr;
+    Job *jobs_dev = nullptr;
+    kvmret::CopyOp *ops_dev = nullptr;
+    // host
+    uint8_t *repo_host = nullptr, *repo_dev = nullptr, *pin_sel = nullptr;
+    std::vector<uint32_t> q_count;
+    bool q_dirty = true;
+    kvmret::BlockTable table;
+    kvmret::Plan last_plan;
+    // HBM pool: which block each slot holds and with how many tokens staged
+    std::vector<int32_t> block_slot;   // [ncap] pool slot or -1
+    std::vector<int32_t> slot_block;   // [pool_slots] block or -1
+    std::vector<uint32_t> slot_ntok;   // tokens staged in the slot
+    std::vector<uint64_t> slot_used;   // step of last use (cache eviction order)
+    std::vector<uint32_t> free_slots;  // LIFO
+    uint64_t step = 0;
+    // window: block, RoPE base and tokens of each slot
+    std::vector<int32_t> win_id, win_base;
+    std::vector<uint32_t> win_ntok;
+    cudaStream_t st = nullptr, st_copy = nullptr;
+    cudaEvent_t ev_prev = nullptr, ev_h2d = nullptr;
+
+    explicit kvmret_ctx(const kvmret::TableConfig &tc) : table(tc) {}
+};
+
+struct kvmret_table {
+    kvmret::BlockTable t;
+    explicit kvmret_table(const kvmret::TableConfig &c) : t(c) {}
+};
+
+namespace {
+
+kvmret::TableConfig table_config(const kvmret_config &c) {
+    kvmret::TableConfig tc;
+    tc.block_tokens = c.block_tokens;
+    tc.budget_blocks = c.budget_blocks;
+    tc.sink_blocks = c.sink_blocks;
+    tc.recent_blocks = c.recent_blocks;
+    tc.immutable_source_k = c.immutable_source_k != 0;
+    return tc;
+}
+
+int validate(const kvmret_config &c) {
+    if (c.n_layer == 0 || c.n_head == 0 || c.n_head_kv == 0 || c.n_head % c.n_head_kv)
+        return fail(KVMRET_ERR_ARG, "bad head geometry (n_layer %u, n_head %u, n_head_kv %u)",
+                    c.n_layer, c.n_head, c.n_head_kv);
+    if (c.d_head != 64 && c.d_head != 128 && c.d_head != 256)
+        return fail(KVMRET_ERR_ARG, "d_head %u not in {64, 128, 256}", c.d_head);
+    if (c.n_rot != c.d_head)
+        return fail(KVMRET_ERR_ARG, "n_rot %u must equal d_head %u (full NeoX rotary)", c.n_rot,
+                    c.d_head);
+    if (c.block_tokens == 0 || static_cast<uint64_t>(c.block_tokens) * c.d_head > 32768)
+        return fail(KVMRET_ERR_ARG, "block_tokens %u too large for d_head %u", c.block_tokens,
+                    c.d_head);
+    if (c.max_blocks == 0 || c.budget_blocks == 0)
+        return fail(KVMRET_ERR_ARG, "max_blocks and budget_blocks must be > 0");
+    if (c.k_type != KVMRET_TYPE_F16 && c.k_type != KVMRET_TYPE_Q8_0)
+        return fail(KVMRET_ERR_ARG, "k_type %d unsupported (f16 or q8_0)", c.k_type);
+    if (!type_ok(c.v_type)) return fail(KVMRET_ERR_ARG, "v_type %d unsupported", c.v_type);
+    const uint64_t kr = kvmret_row_bytes(c.k_type, c.n_head_kv * c.d_head);
+    const uint64_t vr = kvmret_row_bytes(c.v_type, c.n_head_kv * c.d_head);
+    if (kr % 16 || vr % 16)
+        return fail(KVMRET_ERR_ARG, "row bytes %llu / %llu not multiples of 16",
+                    (unsigned long long)kr, (unsigned long long)vr);
+    const uint32_t pool = c.pool_blocks ? c.pool_blocks : c.budget_blocks + c.reserve_blocks;
+    if (pool < c.budget_blocks)
+        return fail(KVMRET_ERR_ARG, "pool_blocks %u < budget_blocks %u", pool, c.budget_blocks);
+    if (c.freq_base <= 0.0f) return fail(KVMRET_ERR_ARG, "freq_base must be > 0");
+    return KVMRET_OK;
+}
+
+int ensure_qprep(kvmret_ctx *c) {
+    if (!c->q_dirty) return KVMRET_OK;
+    CK(cudaMemcpyAsync(c->q_count_dev, c->q_count.data(), c->q_count.size() * sizeof(uint32_t),
+                       cudaMemcpyHostToDevice, c->st));
+    CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, c->cfg.n_layer,
+                            c->cfg.n_head, c->cfg.n_head_kv, c->cfg.d_head, c->st));
+    c->q_dirty = false;
+    return KVMRET_OK;
+}
+
+void free_all(kvmret_ctx *c) {
+    if (c->cfg.device >= 0) cudaSetDevice(c->cfg.device);
+    if (c->st) cudaStreamSynchronize(c->st);
+    if (c->st_copy) cudaStreamSynchronize(c->st_copy);
+    void *dev[] = {c->summ, c->tail_sum, c->q_sum, c->qv, c->nq, c->q_count_dev, c->has_block,
+                   c->active, c->kept_dev, c->sel_dev, c->contrib, c->scores, c->pool,
+                   c->win_k, c->win_v, c->jobs_dev, c->ops_dev};
+    for (void *p : dev)
+        if (p) cudaFree(p);
+    if (c->repo_host) cudaFreeHost(c->repo_host);
+    if (c->pin_sel) cudaFreeHost(c->pin_sel);
+    if (c->ev_prev) cudaEventDestroy(c->ev_prev);
+    if (c->ev_h2d) cudaEventDestroy(c->ev_h2d);
+    if (c->st) cudaStreamDestroy(c->st);
+    if (c->st_copy) cudaStreamDestroy(c->st_copy);
+}
+
+template <typename T>
+int dmalloc(T **p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    const cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), bytes);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        return fail(e == cudaErrorMemoryAllocation ? KVMRET_ERR_NOMEM : KVMRET_ERR_CUDA,
+                    "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    return KVMRET_OK;
+}
+
+#define TRY(x)                                                                                \
+    do {                                                                                      \
+        const int r_ = (x);                                                                   \
+        if (r_ != KVMRET_OK) return r_;                                                       \
+    } while (0)
+
+int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
+    c->cfg = cfg;
+    const kvmret_config &k = c->cfg;
+    CK(cudaSetDevice(k.device));
+    c->E = k.n_head_kv * k.d_head;
+    c->qdim = k.n_head * k.d_head;
+    c->ncap = static_cast<uint32_t>(align_up(k.max_blocks, 128));
+    c->k_row = kvmret_row_bytes(k.k_type, c->E);
+    c->v_row = kvmret_row_bytes(k.v_type, c->E);
+    c->unit_k = align_up(static_cast<uint64_t>(k.block_tokens) * c->k_row, 256);
+    c->unit = c->unit_k + align_up(static_cast<uint64_t>(k.block_tokens) * c->v_row, 256);
+    c->slot_bytes = c->unit * k.n_layer;
+    c->win_slots = k.budget_blocks + k.reserve_blocks;
+    c->pool_slots = k.pool_blocks ? k.pool_blocks : c->win_slots;
+    c->win_k_layer = static_cast<uint64_t>(c->win_slots) * k.block_tokens * c->k_row;
+    c->win_v_layer = static_cast<uint64_t>(c->win_slots) * k.block_tokens * c->v_row;
+    c->theta = make_theta(k.n_rot, k.freq_base, k.freq_scale);
+    const bool quant_k = k.k_type != KVMRET_TYPE_F16;
+    const bool rot = k.attn_rot_k < 0 ? (quant_k && k.d_head % 64 == 0) : k.attn_rot_k != 0;
+    const uint32_t fwht_n = (rot && quant_k) ? hadamard_nrot_k(k.d_head) : 0;
+    kvmret::AssembleGeom &g = c->geom;
+    g.n_layer = k.n_layer;
+    g.n_head_kv = k.n_head_kv;
+    g.d_head = k.d_head;
+    g.block_tokens = k.block_tokens;
+    g.k_row = c->k_row;
+    g.v_row = c->v_row;
+    g.unit_k = c->unit_k;
+    g.unit = c->unit;
+    g.win_k_layer = c->win_k_layer;
+    g.win_v_layer = c->win_v_layer;
+    g.k_type = k.k_type;
+    g.fwht_n = fwht_n;
+    g.fwht_scale = fwht_n ? 1.0f / std::sqrt(static_cast<float>(fwht_n)) : 0.0f;
+
+    CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&c->st_copy, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&c->ev_prev, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&c->ev_h2d, cudaEventDisableTiming));
+
+    const size_t L = k.n_layer;
+    TRY(dmalloc(&c->summ, L * c->E * c->ncap * sizeof(float)));
+    TRY(dmalloc(&c->tail_sum, 2 * L * c->E * sizeof(float)));
+    TRY(dmalloc(&c->q_sum, L * c->qdim * sizeof(float)));
+    TRY(dmalloc(&c->qv, L * c->E * sizeof(float)));
+    TRY(dmalloc(&c->nq, L * k.n_head_kv * sizeof(float)));
+    TRY(dmalloc(&c->q_count_dev, L * sizeof(uint32_t)));
+    TRY(dmalloc(&c->has_block, c->ncap));
+    TRY(dmalloc(&c->active, L));
+    TRY(dmalloc(&c->kept_dev, c->ncap));
+    TRY(dmalloc(&c->sel_dev, c->ncap));
+    TRY(dmalloc(&c->contrib, L * c->ncap * sizeof(double)));
+    TRY(dmalloc(&c->scores, c->ncap * sizeof(double)));
+    TRY(dmalloc(&c->pool, static_cast<size_t>(c->pool_slots) * c->slot_bytes));
+    TRY(dmalloc(&c->win_k, L * c->win_k_layer));
+    TRY(dmalloc(&c->win_v, L * c->win_v_layer));
+    TRY(dmalloc(&c->jobs_dev, 2ull * c->win_slots * sizeof(Job)));
+    TRY(dmalloc(&c->ops_dev, 8192 * sizeof(kvmret::CopyOp)));
+    CK(cudaMemsetAsync(c->summ, 0, L * c->E * c->ncap * sizeof(float), c->st));
+    CK(cudaMemsetAsync(c->tail_sum, 0, 2 * L * c->E * sizeof(float), c->st));
+    CK(cudaMemsetAsync(c->q_sum, 0, L * c->qdim * sizeof(float), c->st));
+    CK(cudaMemsetAsync(c->has_block, 0, c->ncap, c->st));
+    CK(cudaMemsetAsync(c->contrib, 0, L * c->ncap * sizeof(double), c->st));
+    CK(cudaMemsetAsync(c->scores, 0, c->ncap * sizeof(double), c->st));
+
+    const size_t repo_bytes = static_cast<size_t>(k.max_blocks) * c->slot_bytes;
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&c->repo_host), repo_bytes,
+                                  cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+        c->repo_host = nullptr;
+        return fail(KVMRET_ERR_NOMEM, "pinned repository of %zu bytes: %s", repo_bytes,
+                    cudaGetErrorString(e));
+    }
+    CK(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->repo_dev), c->repo_host, 0));
+    e = cudaHostAlloc(reinterpret_cast<void **>(&c->pin_sel), c->ncap, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        c->pin_sel = nullptr;
+        return fail(KVMRET_ERR_NOMEM, "pinned staging: %s", cudaGetErrorString(e));
+    }
+    c->q_count.assign(L, 0);
+    c->block_slot.assign(c->ncap, -1);
+    c->slot_block.assign(c->pool_slots, -1);
+    c->slot_ntok.assign(c->pool_slots, 0);
+    c->slot_used.assign(c->pool_slots, 0);
+    c->free_slots.clear();
+    for (uint32_t s = c->pool_slots; s > 0; --s) c->free_slots.push_back(s - 1);
+    c->win_id.assign(c->win_slots, -1);
+    c->win_base.assign(c->win_slots, 0);
+    c->win_ntok.assign(c->win_slots, 0);
+    CK(cudaStreamSynchronize(c->st));
+    return KVMRET_OK;
+}
+
+// Pool slot for a block entering the window: a free slot (LIFO), else (cache
+// mode) the least recently used slot whose block is not in the new window.
+int32_t take_slot(kvmret_ctx *c, const std::vector<uint8_t> &in_new) {
+    if (!c->free_slots.empty()) {
+        const uint32_t s = c->free_slots.back();
+        c->free_slots.pop_back();
+        return static_cast<int32_t>(s);
+    }
+    int32_t best = -1;
+    for (uint32_t s = 0; s < c->pool_slots; ++s) {
+        const int32_t b = c->slot_block[s];
+        if (b >= 0 && in_new[b]) continue;
+        if (best < 0 || c->slot_used[s] < c->slot_used[best]) best = static_cast<int32_t>(s);
+    }
+    if (best >= 0 && c->slot_block[best] >= 0) c->block_slot[c->slot_block[best]] = -1;
+    return best;
+}
+
+int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_stats *stats) {
+    const uint32_t nb = c->table.n_blocks();
+    {  // bound the window before touching any state
+        std::vector<uint8_t> seen(nb, 0);
+        uint32_t uniq = 0;
+        for (uint32_t i = 0; i < n_ids; ++i)
+            if (ids[i] < nb && !seen[ids[i]]) {
+                seen[ids[i]] = 1;
+                ++uniq;
+            }
+        if (uniq > c->win_slots)
+            return fail(KVMRET_ERR_ARG, "selection of %u blocks exceeds %u window slots", uniq,
+                        c->win_slots);
+    }
+    c->last_plan = c->table.set_selection(ids, n_ids, false);
+    const kvmret::Plan &p = c->last_plan;
+    ++c->step;
+    std::vector<uint8_t> in_new(c->ncap, 0);
+    for (const auto &r : p.remaps) in_new[r.id] = 1;
+    // Release pool slots of blocks that left the window (kept as cache if asked).
+    if (!c->cfg.pool_cache) {
+        for (uint32_t s = 0; s < c->pool_slots; ++s) {
+            const int32_t b = c->slot_block[s];
+            if (b >= 0 && !in_new[b]) {
+                c->block_slot[b] = -1;
+                c->slot_block[s] = -1;
+                c->free_slots.push_back(s);
+            }
+        }
+    }
+    // Blocks without a current pool copy are staged from the host repository.
+    std::vector<std::pair<uint32_t, uint32_t>> h2d;  // (block, slot)
+    std::vector<uint8_t> fresh(c->ncap, 0);
+    const auto &blocks = c->table.blocks();
+    for (const auto &r : p.remaps) {
+        int32_t s = c->block_slot[r.id];
+        if (s < 0 || c->slot_ntok[s] != blocks[r.id].n_tok) {
+            if (s < 0) {
+                s = take_slot(c, in_new);
+                if (s < 0) return fail(KVMRET_ERR_STATE, "HBM pool exhausted");
+                c->slot_block[s] = static_cast<int32_t>(r.id);
+                c->block_slot[r.id] = s;
+            }
+            c->slot_ntok[s] = blocks[r.id].n_tok;
+            h2d.emplace_back(r.id, static_cast<uint32_t>(s));
+            fresh[r.id] = 1;
+        }
+        c->slot_used[s] = c->step;
+    }
+    // Window slots whose content changes: moved residents first, then fresh blocks.
+    std::vector<Job> moved, added;
+    uint32_t w = 0;
+    for (const auto &r : p.remaps) {
+        const bool same = c->win_id[w] == static_cast<int32_t>(r.id) && c->win_base[w] == r.to &&
+                          c->win_ntok[w] == r.n_tok && !fresh[r.id];
+        if (!same) {
+            Job j{static_cast<uint32_t>(c->block_slot[r.id]), w, r.to, r.n_tok};
+            (fresh[r.id] ? added : moved).push_back(j);
+        }
+        c->win_id[w] = static_cast<int32_t>(r.id);
+        c->win_base[w] = r.to;
+        c->win_ntok[w] = r.n_tok;
+        ++w;
+    }
+    for (; w < c->win_slots; ++w) {
+        c->win_id[w] = -1;
+        c->win_ntok[w] = 0;
+    }
+    // Enqueue: host->pool copies on the copy stream after the previous step's
+    // readers of the pool; resident moves immediately; fresh blocks after the copies.
+    if (!h2d.empty()) {
+        CK(cudaEventRecord(c->ev_prev, c->st));
+        CK(cudaStreamWaitEvent(c->st_copy, c->ev_prev, 0));
+        for (const auto &bs : h2d)
+            CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(bs.second) * c->slot_bytes,
+                               c->repo_host + static_cast<uint64_t>(bs.first) * c->slot_bytes,
+                               c->slot_bytes, cudaMemcpyHostToDevice, c->st_copy));
+        CK(cudaEventRecord(c->ev_h2d, c->st_copy));
+    }
+    std::vector<Job> all(moved);
+    all.insert(all.end(), added.begin(), added.end());
+    if (!all.empty())
+        CK(cudaMemcpyAsync(c->jobs_dev, all.data(), all.size() * sizeof(Job),
+                           cudaMemcpyHostToDevice, c->st));
+    CK(kvmret::launch_assemble(c->jobs_dev, static_cast<uint32_t>(moved.size()), c->pool,
+                               c->slot_bytes, c->win_k, c->win_v, c->theta, c->geom, c->st));
+    if (!h2d.empty()) CK(cudaStreamWaitEvent(c->st, c->ev_h2d, 0));
+    CK(kvmret::launch_assemble(c->jobs_dev + moved.size(), static_cast<uint32_t>(added.size()),
+                               c->pool, c->slot_bytes, c->win_k, c->win_v, c->theta, c->geom,
+                               c->st));
+    if (stats) {
+        std::memset(stats, 0, sizeof(*stats));
+        stats->n_selected = static_cast<uint32_t>(p.remaps.size());
+        stats->n_stage_in = static_cast<uint32_t>(p.stage_in.size());
+        stats->n_stage_out = static_cast<uint32_t>(p.stage_out.size());
+        for (const auto &r : p.remaps) stats->n_skip += r.skip ? 1u : 0u;
+        stats->n_h2d_blocks = static_cast<uint32_t>(h2d.size());
+        stats->n_assembled = static_cast<uint32_t>(all.size());
+        stats->n_moved = static_cast<uint32_t>(moved.size());
+        stats->total_window_tokens = p.window_tokens;
+        stats->h2d_bytes = static_cast<uint64_t>(h2d.size()) * c->slot_bytes;
+        uint64_t tok = 0;
+        for (const Job &j : all) tok += j.n_tok;
+        stats->assemble_bytes = 2ull * tok * (c->k_row + c->v_row) * c->cfg.n_layer;
+    }
+    return KVMRET_OK;
+}
+
+int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
+                uint32_t *n_out) {
+    if (!n_out) return fail(KVMRET_ERR_ARG, "n_out is NULL");
+    std::vector<uint8_t> kept;
+    uint32_t kept_count = 0;
+    const uint32_t need = c->table.keep(mandatory, n_mand, kept, kept_count);
+    const uint32_t n = c->table.n_blocks();
+    const uint8_t *sel = kept.data();
+    if (need > 0) {
+        CK(cudaMemcpyAsync(c->kept_dev, kept.data(), n, cudaMemcpyHostToDevice, c->st));
+        CK(kvmret::launch_select(c->scores, c->kept_dev, n, need, c->cfg.tie_higher_id,
+                                 c->sel_dev, c->st));
+        CK(cudaMemcpyAsync(c->pin_sel, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
+        CK(cudaStreamSynchronize(c->st));
+        sel = c->pin_sel;
+    }
+    uint32_t m = 0;
+    for (uint32_t i = 0; i < n; ++i)
+        if (sel[i]) {
+            if (ids_out) ids_out[m] = i;
+            ++m;
+        }
+    *n_out = m;
+    return KVMRET_OK;
+}
+
+int score_layers_impl(kvmret_ctx *c) {
+    TRY(ensure_qprep(c));
+    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, c->contrib, c->cfg.n_layer,
+                            c->cfg.n_head_kv, c->cfg.d_head, c->ncap, c->table.n_blocks(), c->st));
+    return KVMRET_OK;
+}
+
+int score_impl(kvmret_ctx *c, double *scores_host) {
+    TRY(score_layers_impl(c));
+    const uint32_t n = c->table.n_blocks();
+    CK(kvmret::launch_reduce(c->contrib, c->active, c->cfg.n_layer, c->ncap, c->has_block, n,
+                             c->scores, c->st));
+    if (scores_host) {
+        CK(cudaMemcpyAsync(scores_host, c->scores, n * sizeof(double), cudaMemcpyDeviceToHost,
+                           c->st));
+        CK(cudaStreamSynchronize(c->st));
+    }
+    return KVMRET_OK;
+}
+
+#define GUARD(expr)                                                                           \
+    try {                                                                                     \
+        expr;                                                                                 \
+    } catch (const std::bad_alloc &) {                                                        \
+        return fail(KVMRET_ERR_NOMEM, "host allocation failed");                             \
+    } catch (...) {                                                                           \
+        return fail(KVMRET_ERR_STATE, "internal error");                                     \
+    }
+
+#define NEED_CTX(c)                                                                           \
+    do {                                                                                      \
+        if (!(c)) return fail(KVMRET_ERR_ARG, "null context");                               \
+        const cudaError_t de_ = cudaSetDevice((c)->cfg.device);                               \
+        if (de_ != cudaSuccess)                                                               \
+            return fail(KVMRET_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(de_));        \
+    } while (0)
+
+}  // namespace
+
+extern "C" {
+
+void kvmret_config_default(kvmret_config *c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof(*c));
+    c->n_layer = 1;
+    c->n_head = 32;
+    c->n_head_kv = 8;
+    c->d_head = 128;
+    c->block_tokens = 128;
+    c->max_blocks = 256;
+    c->budget_blocks = 32;
+    c->reserve_blocks = 0;
+    c->sink_blocks = 1;
+    c->recent_blocks = 0;
+    c->pool_blocks = 0;
+    c->k_type = KVMRET_TYPE_F16;
+    c->v_type = KVMRET_TYPE_F16;
+    c->attn_rot_k = -1;
+    c->tie_higher_id = 1;
+    c->pool_cache = 0;
+    c->immutable_source_k = 0;
+    c->n_rot = 128;
+    c->freq_base = 1000000.0f;
+    c->freq_scale = 1.0f;
+    c->device = 0;
+}
+
+uint64_t kvmret_row_bytes(int32_t type, uint32_t n) {
+    switch (type) {
+    case KVMRET_TYPE_F16: return 2ull * n;
+    case KVMRET_TYPE_Q8_0: return n % 32 ? 0 : (n / 32) * 34ull;
+    case KVMRET_TYPE_Q4_0: return n % 32 ? 0 : (n / 32) * 18ull;
+    default: return 0;
+    }
+}
+
+const char *kvmret_last_error(void) { return g_err.c_str(); }
+const char *kvmret_version(void) { return "kvmret 0.1 sm_100a"; }
+
+int kvmret_create(const kvmret_config *cfg, kvmret_ctx **out) {
+    if (!cfg || !out) return fail(KVMRET_ERR_ARG, "null argument");
+    *out = nullptr;
+    TRY(validate(*cfg));
+    kvmret_ctx *c = nullptr;
+    GUARD(c = new kvmret_ctx(table_config(*cfg)));
+    int r = KVMRET_ERR_STATE;
+    try {
+        r = create_impl(*cfg, c);
+    } catch (...) {
+        r = fail(KVMRET_ERR_NOMEM, "host allocation failed during create");
+    }
+    if (r != KVMRET_OK) {
+        const std::string keep = g_err;
+        free_all(c);
+        delete c;
+        g_err = keep;
+        return r;
+    }
+    *out = c;
+    return KVMRET_OK;
+}
+
+void kvmret_destroy(kvmret_ctx *c) {
+    if (!c) return;
+    free_all(c);
+    delete c;
+}
+
+void *kvmret_stream(kvmret_ctx *c) { return c ? static_cast<void *>(c->st) : nullptr; }
+
+int kvmret_sync(kvmret_ctx *c) {
+    NEED_CTX(c);
+    CK(cudaStreamSynchronize(c->st));
+    CK(cudaStreamSynchronize(c->st_copy));
+    return KVMRET_OK;
+}
+
+void *kvmret_repo_host(kvmret_ctx *c) { return c ? c->repo_host : nullptr; }
+uint64_t kvmret_repo_unit_bytes(kvmret_ctx *c) { return c ? c->unit : 0; }
+uint64_t kvmret_repo_k_bytes(kvmret_ctx *c) { return c ? c->unit_k : 0; }
+uint32_t kvmret_n_blocks(kvmret_ctx *c) { return c ? c->table.n_blocks() : 0; }
+uint32_t kvmret_n_tokens(kvmret_ctx *c) { return c ? c->table.n_tokens() : 0; }
+
+int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *k_cap,
+                  const void *k_rows, const void *v_rows) {
+    NEED_CTX(c);
+    if (pos0 != c->table.n_tokens())
+        return fail(KVMRET_ERR_ARG, "append at %u, store holds %u tokens", pos0,
+                    c->table.n_tokens());
+    if (n_tok == 0) return KVMRET_OK;
+    const uint64_t cap = static_cast<uint64_t>(c->cfg.max_blocks) * c->cfg.block_tokens;
+    if (static_cast<uint64_t>(pos0) + n_tok > cap)
+        return fail(KVMRET_ERR_ARG, "append of %u tokens exceeds capacity %llu", n_tok,
+                    (unsigned long long)cap);
+    if (!k_cap || !v_rows) return fail(KVMRET_ERR_ARG, "k_cap and v_rows are required");
+    if (!k_rows) {
+        if (c->cfg.k_type != KVMRET_TYPE_F16)
+            return fail(KVMRET_ERR_ARG, "k_rows required for quantised K");
+        k_rows = k_cap;
+    }
+    kvmret::AppendArgs a{};
+    a.k_cap = k_cap;
+    a.k_rows = static_cast<const uint8_t *>(k_rows);
+    a.v_rows = static_cast<const uint8_t *>(v_rows);
+    a.pos0 = pos0;
+    a.n_tok = n_tok;
+    a.n_layer = c->cfg.n_layer;
+    a.n_head_kv = c->cfg.n_head_kv;
+    a.d_head = c->cfg.d_head;
+    a.block_tokens = c->cfg.block_tokens;
+    a.ncap = c->ncap;
+    a.k_row = c->k_row;
+    a.v_row = c->v_row;
+    a.unit_k = c->unit_k;
+    a.unit = c->unit;
+    a.summ = c->summ;
+    a.tail_sum = c->tail_sum;
+    a.has_block = c->has_block;
+    a.repo_dev = c->repo_dev;
+    CK(kvmret::launch_append(a, c->st));
+    GUARD(c->table.append(n_tok));
+    return KVMRET_OK;
+}
+
+int kvmret_get_summaries(kvmret_ctx *c, float *out) {
+    NEED_CTX(c);
+    if (!out) return fail(KVMRET_ERR_ARG, "null output");
+    const uint32_t n = c->table.n_blocks(), L = c->cfg.n_layer, E = c->E;
+    std::vector<float> tmp;
+    GUARD(tmp.resize(static_cast<size_t>(L) * E * c->ncap));
+    CK(cudaMemcpyAsync(tmp.data(), c->summ, tmp.size() * sizeof(float), cudaMemcpyDeviceToHost,
+                       c->st));
+    CK(cudaStreamSynchronize(c->st));
+    for (uint32_t b = 0; b < n; ++b)
+        for (uint32_t l = 0; l < L; ++l)
+            for (uint32_t e = 0; e < E; ++e)
+                out[(static_cast<size_t>(b) * L + l) * E + e] =
+                    tmp[(static_cast<size_t>(l) * E + e) * c->ncap + b];
+    return KVMRET_OK;
+}
+
+int kvmret_query_reset(kvmret_ctx *c) {
+    NEED_CTX(c);
+    CK(cudaMemsetAsync(c->q_sum, 0, static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
+                       c->st));
+    std::fill(c->q_count.begin(), c->q_count.end(), 0u);
+    c->q_dirty = true;
+    return KVMRET_OK;
+}
+
+static int query_add(kvmret_ctx *c, const void *q, bool f16, uint32_t n_rows) {
+    NEED_CTX(c);
+    if (!q) return fail(KVMRET_ERR_ARG, "null query");
+    if (n_rows == 0) return KVMRET_OK;
+    CK(kvmret::launch_query_add(c->q_sum, q, f16, c->cfg.n_layer, n_rows, c->qdim, c->st));
+    for (auto &x : c->q_count) x += n_rows;
+    c->q_dirty = true;
+    return KVMRET_OK;
+}
+
+int kvmret_query_add_f16(kvmret_ctx *c, const uint16_t *q, uint32_t n_rows) {
+    return query_add(c, q, true, n_rows);
+}
+int kvmret_query_add_f32(kvmret_ctx *c, const float *q, uint32_t n_rows) {
+    return query_add(c, q, false, n_rows);
+}
+
+int kvmret_query_set(kvmret_ctx *c, const float *q_sum, const uint32_t *q_count) {
+    NEED_CTX(c);
+    if (!q_sum || !q_count) return fail(KVMRET_ERR_ARG, "null query state");
+    CK(cudaMemcpyAsync(c->q_sum, q_sum,
+                       static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
+                       cudaMemcpyHostToDevice, c->st));
+    for (uint32_t l = 0; l < c->cfg.n_layer; ++l) c->q_count[l] = q_count[l];
+    c->q_dirty = true;
+    CK(cudaStreamSynchronize(c->st));
+    return KVMRET_OK;
+}
+
+int kvmret_query_get(kvmret_ctx *c, float *q_sum, uint32_t *q_count) {
+    NEED_CTX(c);
+    if (q_sum) {
+        CK(cudaMemcpyAsync(q_sum, c->q_sum,
+                           static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
+                           cudaMemcpyDeviceToHost, c->st));
+        CK(cudaStreamSynchronize(c->st));
+    }
+    if (q_count)
+        for (uint32_t l = 0; l < c->cfg.n_layer; ++l) q_count[l] = c->q_count[l];
+    return KVMRET_OK;
+}
+
+int kvmret_score(kvmret_ctx *c, double *scores_host) {
+    NEED_CTX(c);
+    return score_impl(c, scores_host);
+}
+
+int kvmret_score_layers(kvmret_ctx *c) {
+    NEED_CTX(c);
+    return score_layers_impl(c);
+}
+
+const double *kvmret_contrib_dev(kvmret_ctx *c) { return c ? c->contrib : nullptr; }
+const uint8_t *kvmret_layer_active_dev(kvmret_ctx *c) { return c ? c->active : nullptr; }
+uint32_t kvmret_contrib_stride(kvmret_ctx *c) { return c ? c->ncap : 0; }
+
+int kvmret_score_reduce(kvmret_ctx *c, const double *contrib_all, const uint8_t *active_all,
+                        uint32_t n_layer_all, uint32_t stride) {
+    NEED_CTX(c);
+    if (!contrib_all || !active_all || stride < c->table.n_blocks())
+        return fail(KVMRET_ERR_ARG, "bad contribution buffer");
+    CK(kvmret::launch_reduce(contrib_all, active_all, n_layer_all, stride, c->has_block,
+                             c->table.n_blocks(), c->scores, c->st));
+    return KVMRET_OK;
+}
+
+int kvmret_select(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
+                  uint32_t *n_out) {
+    NEED_CTX(c);
+    if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");
+    GUARD(return select_impl(c, mandatory, n_mand, ids_out, n_out));
+}
+
+int kvmret_preview(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
+                   uint32_t *n_out) {
+    NEED_CTX(c);
+    TRY(score_impl(c, nullptr));
+    return kvmret_select(c, mandatory, n_mand, ids_out, n_out);
+}
+
+int kvmret_apply_selection(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids,
+                           kvmret_step_stats *stats) {
+    NEED_CTX(c);
+    if (n_ids && !ids) return fail(KVMRET_ERR_ARG, "null id list");
+    GUARD(return apply_impl(c, ids, n_ids, stats));
+}
+
+int kvmret_apply_retrieval(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand,
+                           uint32_t *ids_out, uint32_t *n_out, kvmret_step_stats *stats) {
+    NEED_CTX(c);
+    std::vector<uint32_t> ids;
+    GUARD(ids.resize(c->cfg.budget_blocks > c->table.n_blocks() ? c->table.n_blocks()
+                                                                : c->cfg.budget_blocks));
+    uint32_t n = 0;
+    TRY(kvmret_preview(c, mandatory, n_mand, ids.data(), &n));
+    if (ids_out) std::copy(ids.begin(), ids.begin() + n, ids_out);
+    if (n_out) *n_out = n;
+    return kvmret_apply_selection(c, ids.data(), n, stats);
+}
+
+int kvmret_last_plan(kvmret_ctx *c, int32_t *remaps, uint32_t *n_remaps, uint32_t *stage_in,
+                     uint32_t *n_stage_in, uint32_t *stage_out, uint32_t *n_stage_out) {
+    if (!c) return fail(KVMRET_ERR_ARG, "null context");
+    const kvmret::Plan &p = c->last_plan;
+    if (n_remaps) *n_remaps = static_cast<uint32_t>(p.remaps.size());
+    if (remaps)
+        for (size_t i = 0; i < p.remaps.size(); ++i) {
+            const auto &r = p.remaps[i];
+            int32_t *o = remaps + 7 * i;
+            o[0] = static_cast<int32_t>(r.id);
+            o[1] = static_cast<int32_t>(r.n_tok);
+            o[2] = r.from;
+            o[3] = r.to;
+            o[4] = r.resident;
+            o[5] = r.skip;
+            o[6] = r.raw;
+        }
+    if (n_stage_in) *n_stage_in = static_cast<uint32_t>(p.stage_in.size());
+    if (stage_in) std::copy(p.stage_in.begin(), p.stage_in.end(), stage_in);
+    if (n_stage_out) *n_stage_out = static_cast<uint32_t>(p.stage_out.size());
+    if (stage_out) std::copy(p.stage_out.begin(), p.stage_out.end(), stage_out);
+    return KVMRET_OK;
+}
+
+void *kvmret_window_k(kvmret_ctx *c, uint32_t layer) {
+    return (c && layer < c->cfg.n_layer) ? c->win_k + layer * c->win_k_layer : nullptr;
+}
+void *kvmret_window_v(kvmret_ctx *c, uint32_t layer) {
+    return (c && layer < c->cfg.n_layer) ? c->win_v + layer * c->win_v_layer : nullptr;
+}
+uint32_t kvmret_window_slots(kvmret_ctx *c) { return c ? c->win_slots : 0; }
+
+int kvmret_window_layout(kvmret_ctx *c, uint32_t *ids, int32_t *bases, uint32_t *n_out) {
+    if (!c || !n_out) return fail(KVMRET_ERR_ARG, "null argument");
+    uint32_t n = 0;
+    while (n < c->win_slots && c->win_id[n] >= 0) {
+        if (ids) ids[n] = static_cast<uint32_t>(c->win_id[n]);
+        if (bases) bases[n] = c->win_base[n];
+        ++n;
+    }
+    *n_out = n;
+    return KVMRET_OK;
+}
+
+int kvmret_window_read(kvmret_ctx *c, uint32_t layer, int is_v, uint32_t slot0, uint32_t n_slots,
+                       void *out) {
+    NEED_CTX(c);
+    if (!out || layer >= c->cfg.n_layer || slot0 + static_cast<uint64_t>(n_slots) > c->win_slots)
+        return fail(KVMRET_ERR_ARG, "window read out of range");
+    const uint64_t row = is_v ? c->v_row : c->k_row;
+    const uint64_t span = static_cast<uint64_t>(c->cfg.block_tokens) * row;
+    const uint8_t *base = (is_v ? c->win_v + layer * c->win_v_layer
+                                : c->win_k + layer * c->win_k_layer) + slot0 * span;
+    CK(cudaStreamSynchronize(c->st));
+    CK(cudaMemcpy(out, base, n_slots * span, cudaMemcpyDeviceToHost));
+    return KVMRET_OK;
+}
+
+int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n_head_kv,
+                    uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                    float freq_scale, void *stream) {
+    if (!k || !out || n_head_kv == 0) return fail(KVMRET_ERR_ARG, "bad rope arguments");
+    if ((d_head != 64 && d_head != 128 && d_head != 256) || n_rot != d_head)
+        return fail(KVMRET_ERR_ARG, "rope needs d_head in {64,128,256} and n_rot == d_head");
+    if (n_tok == 0) return KVMRET_OK;
+    kvmret::AssembleGeom g{};
+    g.n_layer = 1;
+    g.n_head_kv = n_head_kv;
+    g.d_head = d_head;
+    g.block_tokens = 128;
+    g.k_row = 2ull * n_head_kv * d_head;
+    g.k_type = KVMRET_TYPE_F16;
+    const uint32_t jobs = (n_tok + 127) / 128;
+    CK(kvmret::launch_assemble(nullptr, jobs, reinterpret_cast<const uint8_t *>(k),
+                               128 * g.k_row, reinterpret_cast<uint8_t *>(out), nullptr,
+                               make_theta(n_rot, freq_base, freq_scale), g,
+                               static_cast<cudaStream_t>(stream), pos0, n_tok));
+    return KVMRET_OK;
+}
+
+int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
+                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                     float freq_scale, uint32_t fwht_n, void *stream) {
+    if (!k || !out || n_head_kv == 0) return fail(KVMRET_ERR_ARG, "bad rope arguments");
+    if ((d_head != 64 && d_head != 128 && d_head != 256) || n_rot != d_head)
+        return fail(KVMRET_ERR_ARG, "rope needs d_head in {64,128,256} and n_rot == d_head");
+    if (fwht_n != 0 && fwht_n != d_head)
+        return fail(KVMRET_ERR_ARG, "fwht_n must be 0 or d_head");
+    const uint64_t row = kvmret_row_bytes(KVMRET_TYPE_Q8_0, n_head_kv * d_head);
+    if (row % 16) return fail(KVMRET_ERR_ARG, "q8_0 row of %llu bytes not 16-aligned",
+                              (unsigned long long)row);
+    if (n_tok == 0) return KVMRET_OK;
+    kvmret::AssembleGeom g{};
+    g.n_layer = 1;
+    g.n_head_kv = n_head_kv;
+    g.d_head = d_head;
+    g.block_tokens = 128;
+    g.k_row = row;
+    g.k_type = KVMRET_TYPE_Q8_0;
+    g.fwht_n = fwht_n;
+    g.fwht_scale = fwht_n ? 1.0f / std::sqrt(static_cast<float>(fwht_n)) : 0.0f;
+    const uint32_t jobs = (n_tok + 127) / 128;
+    CK(kvmret::launch_assemble(nullptr, jobs, static_cast<const uint8_t *>(k), 128 * row,
+                               static_cast<uint8_t *>(out), nullptr,
+                               make_theta(n_rot, freq_base, freq_scale), g,
+                               static_cast<cudaStream_t>(stream), pos0, n_tok));
+    return KVMRET_OK;
+}
+
+int kvmret_d2d_batched(kvmret_ctx *c, const void *const *src, void *const *dst,
+                       const uint64_t *nbytes, int n) {
+    NEED_CTX(c);
+    if (n <= 0) return KVMRET_OK;
+    if (!src || !dst || !nbytes || n > 8192)
+        return fail(KVMRET_ERR_ARG, "bad batched copy (n %d, max 8192)", n);
+    std::vector<kvmret::CopyOp> ops;
+    GUARD(ops.resize(n));
+    for (int i = 0; i < n; ++i)
+        ops[i] = {static_cast<const uint8_t *>(src[i]), static_cast<uint8_t *>(dst[i]), nbytes[i]};
+    CK(cudaMemcpyAsync(c->ops_dev, ops.data(), n * sizeof(kvmret::CopyOp), cudaMemcpyHostToDevice,
+                       c->st));
+    CK(kvmret::launch_copy_ops(c->ops_dev, n, c->st));
+    return KVMRET_OK;
+}
+
+int kvmret_table_create(const kvmret_config *cfg, kvmret_table **out) {
+    if (!cfg || !out) return fail(KVMRET_ERR_ARG, "null argument");
+    GUARD(*out = new kvmret_table(table_config(*cfg)));
+    return KVMRET_OK;
+}
+void kvmret_table_destroy(kvmret_table *t) { delete t; }
+int kvmret_table_append(kvmret_table *t, uint32_t n) {
+    if (!t) return fail(KVMRET_ERR_ARG, "null table");
+    GUARD(t->t.append(n));
+    return KVMRET_OK;
+}
+uint32_t kvmret_table_n_blocks(kvmret_table *t) { return t ? t->t.n_blocks() : 0; }
+
+int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_mand,
+                      uint8_t *kept_out, uint32_t *kept_count, uint32_t *need) {
+    if (!t || (n_mand && !mandatory)) return fail(KVMRET_ERR_ARG, "null argument");
+    std::vector<uint8_t> kept;
+    uint32_t kc = 0, nd = 0;
+    GUARD(nd = t->t.keep(mandatory, n_mand, kept, kc));
+    if (kept_out) std::copy(kept.begin(), kept.end(), kept_out);
+    if (kept_count) *kept_count = kc;
+    if (need) *need = nd;
+    return KVMRET_OK;
+}
+
+int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_ids,
+                               int force_raw, uint32_t *stage_in, uint32_t *stage_out,
+                               int32_t *remaps, uint32_t *counts) {
+    if (!t || (n_ids && !ids)) return fail(KVMRET_ERR_ARG, "null argument");
+    kvmret::Plan p;
+    GUARD(p = t->t.set_selection(ids, n_ids, force_raw != 0));
+    if (stage_in) std::copy(p.stage_in.begin(), p.stage_in.end(), stage_in);
+    if (stage_out) std::copy(p.stage_out.begin(), p.stage_out.end(), stage_out);
+    if (remaps)
+        for (size_t i = 0; i < p.remaps.size(); ++i) {
+            const auto &r = p.remaps[i];
+            int32_t *o = remaps + 7 * i;
+            o[0] = static_cast<int32_t>(r.id);
+            o[1] = static_cast<int32_t>(r.n_tok);
+            o[2] = r.from;
+            o[3] = r.to;
+            o[4] = r.resident;
+            o[5] = r.skip;
+            o[6] = r.raw;
+        }
+    if (counts) {
+        counts[0] = static_cast<uint32_t>(p.stage_in.size());
+        counts[1] = static_cast<uint32_t>(p.stage_out.size());
+        counts[2] = static_cast<uint32_t>(p.remaps.size());
+        counts[3] = p.window_tokens;
+        counts[4] = p.overlap;
+        counts[5] = p.reused;
+    }
+    return KVMRET_OK;
+}
+
+}  // extern "C"

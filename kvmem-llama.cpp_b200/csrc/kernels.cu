@@ -1,0 +1,583 @@
+// sm_100a kernels of the retrieval path. The file is compiled with
+// -fmad=false and every floating-point operation whose rounding the reference
+// fixes is written with an explicit _rn intrinsic, so no multiply-add is
+// fused anywhere on this path.
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+
+#include "kvmret.h"
+
+namespace kvmret {
+namespace {
+
+constexpr int kTile = 128;  // blocks per scoring CTA (32 lanes x float4)
+
+__device__ __forceinline__ float h2f(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ uint16_t f2h(float f) {
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+// ---------------------------------------------------------------------------
+// S1: q_sum += rows, row order (llama-memory-kvmem.cpp:3417-3432).
+template <typename T>
+__global__ void query_add_kernel(float *__restrict__ q_sum, const T *__restrict__ rows,
+                                 uint32_t n_rows, uint32_t qdim) {
+    const uint32_t l = blockIdx.y;
+    const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= qdim) return;
+    float s = q_sum[static_cast<size_t>(l) * qdim + e];
+    const T *src = rows + static_cast<size_t>(l) * n_rows * qdim + e;
+    for (uint32_t r = 0; r < n_rows; ++r) {
+        float v;
+        if constexpr (sizeof(T) == 2) v = h2f(src[static_cast<size_t>(r) * qdim]);
+        else v = src[static_cast<size_t>(r) * qdim];
+        s = __fadd_rn(s, v);
+    }
+    q_sum[static_cast<size_t>(l) * qdim + e] = s;
+}
+
+// ---------------------------------------------------------------------------
+// S3 prologue (score_retrieval :4162-4185, hoisted): for each (layer, kv head)
+// qv[d] = (sum over the group's heads of q_sum, in head order) * invq and
+// nq = sequential sum of qv*qv. Both depend only on the query, so the
+// per-block loop of the reference recomputes the same values.
+__global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__restrict__ q_count,
+                             float *__restrict__ qv, float *__restrict__ nq,
+                             uint8_t *__restrict__ active, uint32_t n_head, uint32_t n_head_kv,
+                             uint32_t d_head) {
+    const uint32_t l = blockIdx.x;
+    const uint32_t g = n_head_kv == 0 ? 1 : n_head / n_head_kv;
+    const uint32_t cnt = q_count[l];
+    const float invq = __fdiv_rn(1.0f, static_cast<float>(cnt * (g > 1u ? g : 1u)));
+    const uint32_t E = n_head_kv * d_head;
+    const float *qs = q_sum + static_cast<size_t>(l) * n_head * d_head;
+    float *out = qv + static_cast<size_t>(l) * E;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
+        const uint32_t h = e / d_head, d = e % d_head;
+        float s = 0.0f;
+        for (uint32_t gi = 0; gi < g; ++gi) {
+            const uint32_t qh = h * g + gi;
+            if (qh >= n_head) break;
+            s = __fadd_rn(s, qs[static_cast<size_t>(qh) * d_head + d]);
+        }
+        out[e] = __fmul_rn(s, invq);
+    }
+    __syncthreads();
+    for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
+        float a = 0.0f;
+        for (uint32_t d = 0; d < d_head; ++d) {
+            const float v = out[h * d_head + d];
+            a = __fadd_rn(a, __fmul_rn(v, v));
+        }
+        nq[static_cast<size_t>(l) * n_head_kv + h] = a;
+    }
+    if (threadIdx.x == 0) active[l] = cnt != 0;
+}
+
+// ---------------------------------------------------------------------------
+// S3: one CTA = one layer x 128 blocks. Summaries are block-minor
+// [L][Hkv][D][ncap], so lane j of a warp walks blocks 4j..4j+3 with float4
+// loads: each d step of a warp reads 512 contiguous bytes, and each block's
+// dot / norm is accumulated strictly in d order (score_retrieval :4179-4185).
+template <int D>
+__global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ summ,
+                                                    const float *__restrict__ qv,
+                                                    const float *__restrict__ nq,
+                                                    const uint8_t *__restrict__ active,
+                                                    double *__restrict__ contrib,
+                                                    uint32_t n_head_kv, uint32_t ncap) {
+    extern __shared__ float smem[];
+    const uint32_t l = blockIdx.y;
+    const uint32_t b0 = blockIdx.x * kTile;
+    double *out = contrib + static_cast<size_t>(l) * ncap + b0;
+    if (!active[l]) {
+        for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) out[t] = 0.0;
+        return;
+    }
+    float *sq = smem;                       // [Hkv][D]
+    float *cosb = smem + n_head_kv * D;     // [Hkv][kTile]
+    for (uint32_t i = threadIdx.x; i < n_head_kv * D; i += blockDim.x)
+        sq[i] = qv[static_cast<size_t>(l) * n_head_kv * D + i];
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    const size_t dstep = ncap / 4;  // float4 stride between d rows
+    for (uint32_t h = warp; h < n_head_kv; h += nwarp) {
+        const float4 *p = reinterpret_cast<const float4 *>(
+                              summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
+                          lane;
+        const float *qh = sq + h * D;
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+        float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
+#pragma unroll 2
+        for (int dd = 0; dd < D; dd += 8) {
+            float4 k[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) k[u] = __ldg(p + static_cast<size_t>(dd + u) * dstep);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float q = qh[dd + u];
+                d0 = __fadd_rn(d0, __fmul_rn(q, k[u].x));
+                d1 = __fadd_rn(d1, __fmul_rn(q, k[u].y));
+                d2 = __fadd_rn(d2, __fmul_rn(q, k[u].z));
+                d3 = __fadd_rn(d3, __fmul_rn(q, k[u].w));
+                n0 = __fadd_rn(n0, __fmul_rn(k[u].x, k[u].x));
+                n1 = __fadd_rn(n1, __fmul_rn(k[u].y, k[u].y));
+                n2 = __fadd_rn(n2, __fmul_rn(k[u].z, k[u].z));
+                n3 = __fadd_rn(n3, __fmul_rn(k[u].w, k[u].w));
+            }
+        }
+        const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
+        float *cb = cosb + h * kTile + lane * 4;
+        cb[0] = __fdiv_rn(d0, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n0)), 1e-6f));
+        cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
+        cb[2] = __fdiv_rn(d2, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n2)), 1e-6f));
+        cb[3] = __fdiv_rn(d3, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n3)), 1e-6f));
+    }
+    __syncthreads();
+    // layer += cos (double, head order); term = layer / n_head_kv (:4186-4188).
+    for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) {
+        double layer = 0.0;
+        for (uint32_t h = 0; h < n_head_kv; ++h)
+            layer = __dadd_rn(layer, static_cast<double>(cosb[h * kTile + t]));
+        out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
+    }
+}
+
+// S3 epilogue (:4189-4193): acc over layers in order, score = acc / nlay.
+__global__ void reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
+                              uint32_t n_layer, uint32_t stride,
+                              const uint8_t *__restrict__ has_block, uint32_t n_blocks,
+                              double *__restrict__ scores) {
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    if (!has_block[b]) {
+        scores[b] = 0.0;
+        return;
+    }
+    double acc = 0.0;
+    uint32_t nlay = 0;
+    for (uint32_t l = 0; l < n_layer; ++l) {
+        if (!active[l]) continue;
+        acc = __dadd_rn(acc, contrib[static_cast<size_t>(l) * stride + b]);
+        ++nlay;
+    }
+    scores[b] = nlay ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
+}
+
+// ---------------------------------------------------------------------------
+// S6: exact rank selection. Block b (not kept) is chosen iff fewer than
+// `need` other candidates beat it under (score desc, id by tie rule) — the
+// same set nth_element returns for a strict total order
+// (kvmem_store.cpp:600-616). Scores are streamed through shared memory.
+constexpr int kSelChunk = 2048;
+__global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ scores,
+                                                     const uint8_t *__restrict__ kept,
+                                                     uint32_t n, uint32_t need, int tie_high,
+                                                     uint8_t *__restrict__ sel) {
+    __shared__ double ss[kSelChunk];
+    __shared__ uint8_t sk[kSelChunk];
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = b < n;
+    const bool cand = valid && !kept[b];
+    const double sb = valid ? scores[b] : 0.0;
+    uint32_t rank = 0;
+    for (uint32_t c0 = 0; c0 < n; c0 += kSelChunk) {
+        const uint32_t m = min(static_cast<uint32_t>(kSelChunk), n - c0);
+        for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
+            ss[i] = scores[c0 + i];
+            sk[i] = kept[c0 + i];
+        }
+        __syncthreads();
+        if (cand) {
+            for (uint32_t i = 0; i < m; ++i) {
+                if (sk[i]) continue;
+                const double sc = ss[i];
+                const uint32_t c = c0 + i;
+                const bool better = sc > sb || (sc == sb && (tie_high ? c > b : c < b));
+                rank += better ? 1u : 0u;
+            }
+        }
+        __syncthreads();
+    }
+    if (valid) sel[b] = kept[b] ? 1 : (rank < need ? 1 : 0);
+}
+
+// ---------------------------------------------------------------------------
+// RoPE table: cos/sin of (pos0 + t) * theta[i] for the job's tokens, in shared
+// memory, shared by every head and layer the CTA handles (rope.cpp:27-33; the
+// reference GPU kernel evaluates the same angle with sincosf,
+// llama-kvmem-stagein.cu:170-173). Entries of each 8-wide group are rotated by
+// the group index so the 8 threads of a head row hit distinct banks.
+__device__ __forceinline__ uint32_t tab_swz(uint32_t i) {
+    return (i & ~7u) | (((i & 7u) - (i >> 3)) & 7u);
+}
+
+template <int HALF>
+__device__ __forceinline__ void build_rope_table(float2 *tab, int32_t pos0, uint32_t n_tok,
+                                                 const float *__restrict__ theta) {
+    for (uint32_t idx = threadIdx.x; idx < n_tok * HALF; idx += blockDim.x) {
+        const uint32_t t = idx / HALF, i = idx % HALF;
+        const float pos = static_cast<float>(pos0 + static_cast<int32_t>(t));
+        float s, c;
+        sincosf(__fmul_rn(pos, theta[i]), &s, &c);
+        tab[t * HALF + tab_swz(i)] = make_float2(c, s);
+    }
+}
+
+// f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves.
+template <int D>
+__device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
+                                              uint8_t *__restrict__ dst, const float2 *tab,
+                                              uint32_t n_tok, uint32_t n_head_kv) {
+    constexpr int HALF = D / 2, CPR = HALF / 8;
+    const uint32_t n_items = n_tok * n_head_kv * CPR;
+    for (uint32_t w = threadIdx.x; w < n_items; w += blockDim.x) {
+        const uint32_t row = w / CPR, j = w % CPR, t = row / n_head_kv;
+        const uint4 *sp = reinterpret_cast<const uint4 *>(src + static_cast<size_t>(row) * D * 2);
+        const uint4 lo = __ldg(sp + j), hi = __ldg(sp + CPR + j);
+        const uint16_t *a = reinterpret_cast<const uint16_t *>(&lo);
+        const uint16_t *b = reinterpret_cast<const uint16_t *>(&hi);
+        uint4 olo, ohi;
+        uint16_t *oa = reinterpret_cast<uint16_t *>(&olo);
+        uint16_t *ob = reinterpret_cast<uint16_t *>(&ohi);
+        const float2 *tr = tab + t * HALF;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float2 cs = tr[tab_swz(j * 8 + e)];
+            const float x0 = h2f(a[e]), x1 = h2f(b[e]);
+            oa[e] = f2h(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
+            ob[e] = f2h(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
+        }
+        uint4 *dp = reinterpret_cast<uint4 *>(dst + static_cast<size_t>(row) * D * 2);
+        dp[j] = olo;
+        dp[CPR + j] = ohi;
+    }
+}
+
+// q8_0 K, one warp per (token, head) row held in shared memory, in place:
+// dequant (llama-kvmem-stagein.cu:133-143) -> RoPE -> FWHT (:105-131) ->
+// q8_0 (:181-199). Lane j holds elements EPL*j .. EPL*j + EPL - 1.
+template <int D>
+__device__ __forceinline__ void rope_row_q8(uint8_t *row, const float2 *tr, uint32_t lane,
+                                            uint32_t fwht_n, float fwht_scale) {
+    constexpr int EPL = D / 32, HALF = D / 2, LPB = 32 / EPL;  // lanes per q8 block
+    const uint32_t i0 = lane * EPL;
+    uint8_t *blk = row + (i0 / 32) * 34;
+    const uint32_t in_blk = i0 % 32;
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk));
+    float x[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+        x[e] = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + in_blk + e])), d);
+    // RoPE: pair (i, i + D/2) sits in lanes (j, j ^ 16).
+    const bool low = lane < 16;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const uint32_t ii = (low ? i0 : i0 - HALF) + e;
+        const float2 cs = tr[tab_swz(ii)];
+        x[e] = low ? __fsub_rn(__fmul_rn(x[e], cs.x), __fmul_rn(other, cs.y))
+                   : __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(x[e], cs.x));
+    }
+    if (fwht_n) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) x[e] = __fmul_rn(x[e], fwht_scale);
+#pragma unroll
+        for (int h = 1; h < EPL; h *= 2) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                if (e & h) continue;
+                const float a = x[e], b = x[e + h];
+                x[e] = __fadd_rn(a, b);
+                x[e + h] = __fsub_rn(a, b);
+            }
+        }
+#pragma unroll
+        for (int hl = 1; hl < 32; hl *= 2) {  // element stride hl * EPL
+            const bool upper = lane & hl;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                const float p = __shfl_xor_sync(0xffffffffu, x[e], hl);
+                x[e] = upper ? __fsub_rn(p, x[e]) : __fadd_rn(x[e], p);
+            }
+        }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(x[e]));
+#pragma unroll
+    for (int m = 1; m < LPB; m *= 2) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float dq = __fdiv_rn(amax, 127.0f);
+    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+        blk[2 + in_blk + e] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
+    if (in_blk == 0) *reinterpret_cast<uint16_t *>(blk) = f2h(dq);
+    __syncwarp();
+}
+
+__device__ __forceinline__ void copy16(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+                                       uint64_t nbytes) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    const uint64_t n = nbytes / 16;
+    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = __ldg(s + w);
+}
+
+constexpr int kAsmThreads = 512;
+constexpr int kQ8ChunkTok = 16;
+
+// S10-S13: CTA = one job x a range of layers. K re-roped from the pool's
+// unrotated copy at the job's window base; V copied.
+template <int D, bool Q8>
+__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(
+    const Job *__restrict__ jobs, const uint8_t *__restrict__ pool, uint64_t slot_bytes,
+    uint8_t *__restrict__ win_k, uint8_t *__restrict__ win_v, const __grid_constant__ Theta th,
+    const __grid_constant__ AssembleGeom g, uint32_t layers_per_cta, int32_t synth_pos0,
+    uint32_t synth_ntok) {
+    const float *theta = th.v;
+    constexpr int HALF = D / 2;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    float2 *tab = reinterpret_cast<float2 *>(smem_raw);
+    Job job;
+    if (jobs) {
+        job = jobs[blockIdx.x];
+    } else {  // stateless form: chunk i of a contiguous run of rows
+        job.pool_slot = blockIdx.x;
+        job.win_slot = blockIdx.x;
+        job.pos0 = synth_pos0 + static_cast<int32_t>(blockIdx.x * g.block_tokens);
+        job.n_tok = min(g.block_tokens, synth_ntok - blockIdx.x * g.block_tokens);
+    }
+    build_rope_table<HALF>(tab, job.pos0, job.n_tok, theta);
+    __syncthreads();
+    const uint32_t l0 = blockIdx.y * layers_per_cta;
+    const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
+    const uint8_t *slot = pool + static_cast<uint64_t>(job.pool_slot) * slot_bytes;
+    const uint64_t wk = static_cast<uint64_t>(job.win_slot) * g.block_tokens * g.k_row;
+    const uint64_t wv = static_cast<uint64_t>(job.win_slot) * g.block_tokens * g.v_row;
+    for (uint32_t l = l0; l < l1; ++l) {
+        const uint8_t *src = slot + static_cast<uint64_t>(l) * g.unit;
+        uint8_t *dk = win_k + static_cast<uint64_t>(l) * g.win_k_layer + wk;
+        if constexpr (!Q8) {
+            rope_rows_f16<D>(src, dk, tab, job.n_tok, g.n_head_kv);
+        } else {
+            uint8_t *stage = smem_raw + static_cast<size_t>(g.block_tokens) * HALF * sizeof(float2);
+            const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            const uint32_t nwarp = blockDim.x >> 5;
+            const uint64_t head_bytes = (D / 32) * 34;
+            for (uint32_t t0 = 0; t0 < job.n_tok; t0 += kQ8ChunkTok) {
+                const uint32_t nt = min(static_cast<uint32_t>(kQ8ChunkTok), job.n_tok - t0);
+                copy16(src + t0 * g.k_row, stage, nt * g.k_row);
+                __syncthreads();
+                for (uint32_t r = warp; r < nt * g.n_head_kv; r += nwarp) {
+                    const uint32_t tt = r / g.n_head_kv, h = r % g.n_head_kv;
+                    rope_row_q8<D>(stage + tt * g.k_row + h * head_bytes,
+                                   tab + (t0 + tt) * HALF, lane, g.fwht_n, g.fwht_scale);
+                }
+                __syncthreads();
+                copy16(stage, dk + t0 * g.k_row, nt * g.k_row);
+                __syncthreads();
+            }
+        }
+        if (g.v_row)
+            copy16(src + g.unit_k, win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv,
+                   static_cast<uint64_t>(job.n_tok) * g.v_row);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// S2 + S14: summaries of the appended tokens. CTA = (layer, touched block);
+// thread e sums its channel over the block's new tokens in token order,
+// continuing the trailing partial block's running sum
+// (raw_kv_store.cpp:215-234), and stores sum * (1 / tokens) (:1000-1005).
+__global__ void append_summary_kernel(AppendArgs a, const float *__restrict__ tail_in,
+                                      float *__restrict__ tail_out) {
+    const uint32_t l = blockIdx.x;
+    const uint32_t E = a.n_head_kv * a.d_head;
+    const uint32_t T = a.block_tokens;
+    const uint32_t b = a.pos0 / T + blockIdx.y;
+    const uint32_t tb = max(a.pos0, b * T);
+    const uint32_t te = min(a.pos0 + a.n_tok, (b + 1) * T);
+    const uint32_t off = tb - b * T;
+    const uint32_t cnt = off + (te - tb);
+    const float inv = __fdiv_rn(1.0f, static_cast<float>(cnt));
+    const uint16_t *src = a.k_cap + static_cast<size_t>(l) * a.n_tok * E;
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
+        float s = off == 0 ? 0.0f : tail_in[static_cast<size_t>(l) * E + e];
+        for (uint32_t t = tb; t < te; ++t)
+            s = __fadd_rn(s, h2f(src[static_cast<size_t>(t - a.pos0) * E + e]));
+        const uint32_t h = e / a.d_head, d = e % a.d_head;
+        a.summ[((static_cast<size_t>(l) * a.n_head_kv + h) * a.d_head + d) * a.ncap + b] =
+            __fmul_rn(s, inv);
+        if (cnt < T) tail_out[static_cast<size_t>(l) * E + e] = s;
+    }
+    if (l == 0 && threadIdx.x == 0) a.has_block[b] = 1;
+}
+
+// Repository rows: each (layer, token) K and V row goes to
+// repo[block][layer][K | V] + token offset, over the mapped host pointer.
+__global__ void append_repo_kernel(AppendArgs a) {
+    const uint32_t l = blockIdx.y;
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (warp >= a.n_tok) return;
+    const uint32_t pos = a.pos0 + warp;
+    const uint32_t b = pos / a.block_tokens, off = pos % a.block_tokens;
+    uint8_t *unit = a.repo_dev + (static_cast<uint64_t>(b) * a.n_layer + l) * a.unit;
+    const uint4 *ks = reinterpret_cast<const uint4 *>(
+        a.k_rows + (static_cast<uint64_t>(l) * a.n_tok + warp) * a.k_row);
+    uint4 *kd = reinterpret_cast<uint4 *>(unit + off * a.k_row);
+    for (uint64_t w = lane; w < a.k_row / 16; w += 32) kd[w] = __ldg(ks + w);
+    const uint4 *vs = reinterpret_cast<const uint4 *>(
+        a.v_rows + (static_cast<uint64_t>(l) * a.n_tok + warp) * a.v_row);
+    uint4 *vd = reinterpret_cast<uint4 *>(unit + a.unit_k + off * a.v_row);
+    for (uint64_t w = lane; w < a.v_row / 16; w += 32) vd[w] = __ldg(vs + w);
+}
+
+__global__ void copy_ops_kernel(const CopyOp *__restrict__ ops, int n) {
+    const int i = blockIdx.x;
+    if (i >= n) return;
+    const CopyOp op = ops[i];
+    if (!op.src || !op.dst || op.nbytes == 0) return;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(op.src) | reinterpret_cast<uintptr_t>(op.dst);
+    if ((al & 15u) == 0 && (op.nbytes & 15u) == 0) {
+        copy16(op.src, op.dst, op.nbytes);
+        return;
+    }
+    for (uint64_t j = threadIdx.x; j < op.nbytes; j += blockDim.x) op.dst[j] = op.src[j];
+}
+
+template <int D, bool Q8>
+cudaError_t launch_assemble_t(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
+                              uint64_t slot_bytes, uint8_t *win_k, uint8_t *win_v,
+                              const Theta &theta, const AssembleGeom &g, cudaStream_t st,
+                              int32_t synth_pos0, uint32_t synth_ntok) {
+    const uint32_t lpc = g.n_layer < 8 ? g.n_layer : 8;
+    const dim3 grid(n_jobs, (g.n_layer + lpc - 1) / lpc);
+    size_t smem = static_cast<size_t>(g.block_tokens) * (D / 2) * sizeof(float2);
+    if (Q8) smem += static_cast<size_t>(kQ8ChunkTok) * g.k_row;
+    auto kfn = assemble_kernel<D, Q8>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kfn<<<grid, kAsmThreads, smem, st>>>(jobs, pool, slot_bytes, win_k, win_v, theta, g, lpc,
+                                         synth_pos0, synth_ntok);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint32_t n_layer,
+                             uint32_t n_rows, uint32_t qdim, cudaStream_t st) {
+    const dim3 grid((qdim + 255) / 256, n_layer);
+    if (rows_f16)
+        query_add_kernel<uint16_t><<<grid, 256, 0, st>>>(q_sum, static_cast<const uint16_t *>(rows),
+                                                         n_rows, qdim);
+    else
+        query_add_kernel<float><<<grid, 256, 0, st>>>(q_sum, static_cast<const float *>(rows),
+                                                      n_rows, qdim);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
+                         uint8_t *active, uint32_t n_layer, uint32_t n_head, uint32_t n_head_kv,
+                         uint32_t d_head, cudaStream_t st) {
+    qprep_kernel<<<n_layer, 256, 0, st>>>(q_sum, q_count, qv, nq, active, n_head, n_head_kv,
+                                          d_head);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
+                         const uint8_t *active, double *contrib, uint32_t n_layer,
+                         uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
+                         cudaStream_t st) {
+    const uint32_t tiles = (n_blocks + kTile - 1) / kTile;
+    if (tiles == 0) return cudaSuccess;
+    const dim3 grid(tiles, n_layer);
+    const size_t smem = static_cast<size_t>(n_head_kv) * (d_head + kTile) * sizeof(float);
+    switch (d_head) {
+    case 64:
+        score_kernel<64><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        break;
+    case 128:
+        score_kernel<128><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        break;
+    case 256:
+        score_kernel<256><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        break;
+    default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
+                          uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
+                          double *scores, cudaStream_t st) {
+    if (n_blocks == 0) return cudaSuccess;
+    reduce_kernel<<<(n_blocks + 255) / 256, 256, 0, st>>>(contrib, active, n_layer, stride,
+                                                          has_block, n_blocks, scores);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
+                          uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
+    if (n_blocks == 0) return cudaSuccess;
+    select_kernel<<<(n_blocks + 255) / 256, 256, 0, st>>>(scores, kept, n_blocks, need,
+                                                          tie_higher_id, sel);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_assemble(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
+                            uint64_t pool_slot_bytes, uint8_t *win_k, uint8_t *win_v,
+                            const Theta &theta, const AssembleGeom &g, cudaStream_t st,
+                            int32_t synth_pos0, uint32_t synth_ntok) {
+    if (n_jobs == 0) return cudaSuccess;
+    const bool q8 = g.k_type == KVMRET_TYPE_Q8_0;
+    switch (g.d_head) {
+    case 64:
+        return q8 ? launch_assemble_t<64, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
+                  : launch_assemble_t<64, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
+    case 128:
+        return q8 ? launch_assemble_t<128, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
+                  : launch_assemble_t<128, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
+    case 256:
+        return q8 ? launch_assemble_t<256, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
+                  : launch_assemble_t<256, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {
+    if (a.n_tok == 0) return cudaSuccess;
+    const uint32_t T = a.block_tokens;
+    const uint32_t nb = (a.pos0 + a.n_tok - 1) / T - a.pos0 / T + 1;
+    // Ping-pong the tail sum: the first touched block reads the old tail
+    // while the last one may write the new tail in the same launch.
+    const size_t E = static_cast<size_t>(a.n_head_kv) * a.d_head;
+    float *tail_in = a.tail_sum;
+    float *tail_out = a.tail_sum + static_cast<size_t>(a.n_layer) * E;
+    append_summary_kernel<<<dim3(a.n_layer, nb), 256, 0, st>>>(a, tail_in, tail_out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpyAsync(tail_in, tail_out, static_cast<size_t>(a.n_layer) * E * sizeof(float),
+                        cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return e;
+    const uint32_t warps_per_cta = 8;
+    append_repo_kernel<<<dim3((a.n_tok + warps_per_cta - 1) / warps_per_cta, a.n_layer),
+                         warps_per_cta * 32, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_copy_ops(const CopyOp *ops, int n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    copy_ops_kernel<<<n, 256, 0, st>>>(ops, n);
+    return cudaGetLastError();
+}
+
+}  // namespace kvmret

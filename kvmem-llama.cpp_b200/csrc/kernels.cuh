@@ -1,0 +1,97 @@
+// Kernel launchers shared by the context and the C ABI. All launches are
+// asynchronous on the given stream and return the launch's cudaError_t.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace kvmret {
+
+// One window-assembly job: rebuild window slot `win_slot` of every layer in
+// [layer_begin, layer_end) from HBM pool slot `pool_slot`, K rotated at
+// positions pos0 .. pos0 + n_tok - 1.
+struct Job {
+    uint32_t pool_slot;
+    uint32_t win_slot;
+    int32_t pos0;
+    uint32_t n_tok;
+};
+static_assert(sizeof(Job) == 16, "Job is 16 bytes");
+
+// RoPE frequencies theta_i = freq_base^(-2i/n_rot) * freq_scale, computed on
+// the host exactly as the reference's host RoPE does; passed by value.
+struct Theta {
+    float v[128];
+};
+
+struct AssembleGeom {
+    uint32_t n_layer;
+    uint32_t n_head_kv;
+    uint32_t d_head;
+    uint32_t block_tokens;
+    uint64_t k_row;         // bytes per K token row (window and pool)
+    uint64_t v_row;         // bytes per V token row
+    uint64_t unit_k;        // pool/repo bytes of the K part of one (block, layer) unit
+    uint64_t unit;          // pool/repo bytes of one (block, layer) unit (K part + V part)
+    uint64_t win_k_layer;   // window K bytes per layer
+    uint64_t win_v_layer;   // window V bytes per layer
+    int32_t k_type;
+    uint32_t fwht_n;        // 0 = no Hadamard on requantised K
+    float fwht_scale;       // 1 / sqrt(fwht_n), computed on the host
+};
+
+// S1: q_sum[l][e] += sum over rows (row order), f16 or f32 rows [L][n_rows][qdim].
+cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint32_t n_layer,
+                             uint32_t n_rows, uint32_t qdim, cudaStream_t st);
+
+// S3 prologue: per (layer, kv head) the scaled group query and its squared norm.
+cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
+                         uint8_t *active, uint32_t n_layer, uint32_t n_head,
+                         uint32_t n_head_kv, uint32_t d_head, cudaStream_t st);
+
+// S3: per (layer, block) term layer_sum / n_head_kv.
+cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
+                         const uint8_t *active, double *contrib, uint32_t n_layer,
+                         uint32_t n_head_kv, uint32_t d_head, uint32_t ncap,
+                         uint32_t n_blocks, cudaStream_t st);
+
+// S3 epilogue: layer-ordered sum, / number of layers with a query.
+cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
+                          uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
+                          double *scores, cudaStream_t st);
+
+// S6: sel[b] = kept[b] || (rank of b among non-kept blocks < need).
+cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
+                          uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st);
+
+// S10-S13: window assembly from the HBM pool. With jobs == nullptr the jobs
+// are synthesised: job i covers tokens [i*T, min((i+1)*T, synth_ntok)) of a
+// contiguous run, pool slot i -> window slot i, positions from synth_pos0.
+cudaError_t launch_assemble(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
+                            uint64_t pool_slot_bytes, uint8_t *win_k, uint8_t *win_v,
+                            const Theta &theta, const AssembleGeom &g, cudaStream_t st,
+                            int32_t synth_pos0 = 0, uint32_t synth_ntok = 0);
+
+// S2 + S14: summaries of the appended tokens and the repository rows.
+struct AppendArgs {
+    const uint16_t *k_cap;   // [L][n][E] f16
+    const uint8_t *k_rows;   // [L][n][k_row]
+    const uint8_t *v_rows;   // [L][n][v_row]
+    uint32_t pos0, n_tok;
+    uint32_t n_layer, n_head_kv, d_head, block_tokens, ncap;
+    uint64_t k_row, v_row, unit_k, unit;
+    float *summ;             // [L][Hkv][D][ncap]
+    float *tail_sum;         // [L][E] running sum of the trailing partial block
+    uint8_t *has_block;      // [ncap]
+    uint8_t *repo_dev;       // device alias of the mapped pinned repository
+};
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t st);
+
+struct CopyOp {
+    const uint8_t *src;
+    uint8_t *dst;
+    uint64_t nbytes;
+};
+cudaError_t launch_copy_ops(const CopyOp *ops, int n, cudaStream_t st);
+
+}  // namespace kvmret

@@ -1,0 +1,76 @@
+// Host block table: block registry, the always-kept part of a selection and
+// the working-set diff (plan). Pure host C++; the GPU context drives it.
+//
+// Semantics follow KvMemStore (kvmem/include/kvmem/kvmem_store.hpp:329-491,
+// kvmem/src/host/kvmem_store.cpp) for the TopK policy without media ranges,
+// plus the tier effect of KvMemRuntime::spill_outgoing / admit_incoming
+// (kvmem/src/host/kvmem_runtime.cpp:225-249) with no CPU/NVMe tier.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+namespace kvmret {
+
+struct TableConfig {
+    uint32_t block_tokens = 128;
+    uint32_t budget_blocks = 0;
+    uint32_t sink_blocks = 1;
+    uint32_t recent_blocks = 0;
+    bool immutable_source_k = false;
+    uint32_t refresh_remaps = 8;             // immutable_refresh_remaps
+    uint64_t refresh_abs_delta = 262144;     // immutable_refresh_abs_delta_tokens
+    uint64_t max_baked = 262144;             // immutable_max_baked_position
+};
+
+struct Block {
+    uint32_t pos0 = 0;        // orig_pos_start
+    uint32_t n_tok = 0;
+    bool on_gpu = true;       // KvTier::GPU is the registration default
+    bool in_ws = false;       // in_working_set
+    int64_t baked = -1;       // baked_pos
+    uint32_t remap_count = 0;
+    uint64_t remap_delta = 0;
+};
+
+struct Remap {
+    uint32_t id, n_tok;
+    int32_t from, to;
+    bool resident, skip, raw;
+};
+
+struct Plan {
+    std::vector<uint32_t> stage_in, stage_out;
+    std::vector<Remap> remaps;
+    uint32_t window_tokens = 0;
+    uint32_t overlap = 0;
+    uint32_t reused = 0;
+};
+
+class BlockTable {
+public:
+    explicit BlockTable(const TableConfig &c) : cfg_(c) {}
+    const TableConfig &config() const { return cfg_; }
+    uint32_t n_blocks() const { return static_cast<uint32_t>(blocks_.size()); }
+    uint32_t n_tokens() const { return total_; }
+    const std::vector<Block> &blocks() const { return blocks_; }
+
+    // register_append: extend the partial tail block, then open new blocks.
+    void append(uint32_t n_tok);
+
+    // Always-kept ids of a top-k selection. kept[] is resized to n_blocks.
+    // Returns the count still to be filled by score (0 if everything fits, in
+    // which case kept[] marks every block).
+    uint32_t keep(const uint32_t *mandatory, uint32_t n_mandatory, std::vector<uint8_t> &kept,
+                  uint32_t &kept_count) const;
+
+    // set_selection (+ the runtime's tier effect). ids need not be sorted.
+    Plan set_selection(const uint32_t *ids, uint32_t n_ids, bool force_raw_refresh);
+
+private:
+    TableConfig cfg_;
+    std::vector<Block> blocks_;
+    uint32_t total_ = 0;
+};
+
+}  // namespace kvmret

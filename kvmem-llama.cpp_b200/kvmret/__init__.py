@@ -1,0 +1,383 @@
+"""Python binding of libkvmret (the C ABI in include/kvmret.h).
+
+This is a thin ctypes layer over the sm_100a library; every computation runs
+in libkvmret.so. There is no CPU fallback: importing this module raises if the
+library has not been built (``make -C kvmem-llama.cpp_b200/csrc``).
+
+Device buffers are passed as torch CUDA tensors (their data_ptr()). The
+library runs on its own CUDA stream; the wrapper synchronises torch's current
+stream before handing tensors over and the library stream before results are
+read back, so callers can mix both freely.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkvmret.so")
+
+TYPE_F16 = 1
+TYPE_Q4_0 = 2
+TYPE_Q8_0 = 8
+
+OK = 0
+
+
+class KvmretError(RuntimeError):
+    pass
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"libkvmret.so not built at {LIB_PATH}; run `make -C kvmem-llama.cpp_b200/csrc`")
+    return ctypes.CDLL(LIB_PATH)
+
+
+lib = _load()
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_uint32), ("n_head", ctypes.c_uint32),
+        ("n_head_kv", ctypes.c_uint32), ("d_head", ctypes.c_uint32),
+        ("block_tokens", ctypes.c_uint32), ("max_blocks", ctypes.c_uint32),
+        ("budget_blocks", ctypes.c_uint32), ("reserve_blocks", ctypes.c_uint32),
+        ("sink_blocks", ctypes.c_uint32), ("recent_blocks", ctypes.c_uint32),
+        ("pool_blocks", ctypes.c_uint32), ("k_type", ctypes.c_int32),
+        ("v_type", ctypes.c_int32), ("attn_rot_k", ctypes.c_int32),
+        ("tie_higher_id", ctypes.c_int32), ("pool_cache", ctypes.c_int32),
+        ("immutable_source_k", ctypes.c_int32), ("n_rot", ctypes.c_uint32),
+        ("freq_base", ctypes.c_float), ("freq_scale", ctypes.c_float),
+        ("device", ctypes.c_int32),
+    ]
+
+
+class StepStats(ctypes.Structure):
+    _fields_ = [
+        ("n_selected", ctypes.c_uint32), ("n_stage_in", ctypes.c_uint32),
+        ("n_stage_out", ctypes.c_uint32), ("n_skip", ctypes.c_uint32),
+        ("n_h2d_blocks", ctypes.c_uint32), ("n_assembled", ctypes.c_uint32),
+        ("n_moved", ctypes.c_uint32), ("total_window_tokens", ctypes.c_uint32),
+        ("h2d_bytes", ctypes.c_uint64), ("assemble_bytes", ctypes.c_uint64),
+    ]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+_P = ctypes.c_void_p
+_U32 = ctypes.c_uint32
+_I32 = ctypes.c_int32
+_U64 = ctypes.c_uint64
+_PU32 = ctypes.POINTER(ctypes.c_uint32)
+_PI32 = ctypes.POINTER(ctypes.c_int32)
+_PU8 = ctypes.POINTER(ctypes.c_uint8)
+_PF = ctypes.POINTER(ctypes.c_float)
+_PD = ctypes.POINTER(ctypes.c_double)
+
+# Every symbol the header declares, with its signature (restype, argtypes).
+SIGNATURES = {
+    "kvmret_config_default": (None, [ctypes.POINTER(Config)]),
+    "kvmret_row_bytes": (_U64, [_I32, _U32]),
+    "kvmret_last_error": (ctypes.c_char_p, []),
+    "kvmret_version": (ctypes.c_char_p, []),
+    "kvmret_create": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.POINTER(_P)]),
+    "kvmret_destroy": (None, [_P]),
+    "kvmret_stream": (_P, [_P]),
+    "kvmret_sync": (ctypes.c_int, [_P]),
+    "kvmret_repo_host": (_P, [_P]),
+    "kvmret_repo_unit_bytes": (_U64, [_P]),
+    "kvmret_repo_k_bytes": (_U64, [_P]),
+    "kvmret_append": (ctypes.c_int, [_P, _U32, _U32, _P, _P, _P]),
+    "kvmret_n_blocks": (_U32, [_P]),
+    "kvmret_n_tokens": (_U32, [_P]),
+    "kvmret_get_summaries": (ctypes.c_int, [_P, _PF]),
+    "kvmret_query_reset": (ctypes.c_int, [_P]),
+    "kvmret_query_add_f16": (ctypes.c_int, [_P, _P, _U32]),
+    "kvmret_query_add_f32": (ctypes.c_int, [_P, _P, _U32]),
+    "kvmret_query_set": (ctypes.c_int, [_P, _PF, _PU32]),
+    "kvmret_query_get": (ctypes.c_int, [_P, _PF, _PU32]),
+    "kvmret_score": (ctypes.c_int, [_P, _PD]),
+    "kvmret_score_layers": (ctypes.c_int, [_P]),
+    "kvmret_contrib_dev": (_P, [_P]),
+    "kvmret_layer_active_dev": (_P, [_P]),
+    "kvmret_contrib_stride": (_U32, [_P]),
+    "kvmret_score_reduce": (ctypes.c_int, [_P, _P, _P, _U32, _U32]),
+    "kvmret_select": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32]),
+    "kvmret_preview": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32]),
+    "kvmret_apply_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.POINTER(StepStats)]),
+    "kvmret_apply_retrieval": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32,
+                                              ctypes.POINTER(StepStats)]),
+    "kvmret_last_plan": (ctypes.c_int, [_P, _PI32, _PU32, _PU32, _PU32, _PU32, _PU32]),
+    "kvmret_window_k": (_P, [_P, _U32]),
+    "kvmret_window_v": (_P, [_P, _U32]),
+    "kvmret_window_slots": (_U32, [_P]),
+    "kvmret_window_layout": (ctypes.c_int, [_P, _PU32, _PI32, _PU32]),
+    "kvmret_window_read": (ctypes.c_int, [_P, _U32, ctypes.c_int, _U32, _U32, _P]),
+    "kvmret_rope_f16": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
+                                       ctypes.c_float, _P]),
+    "kvmret_rope_q8_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
+                                        ctypes.c_float, _U32, _P]),
+    "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
+                                          ctypes.POINTER(_U64), ctypes.c_int]),
+    "kvmret_table_create": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.POINTER(_P)]),
+    "kvmret_table_destroy": (None, [_P]),
+    "kvmret_table_append": (ctypes.c_int, [_P, _U32]),
+    "kvmret_table_n_blocks": (_U32, [_P]),
+    "kvmret_table_keep": (ctypes.c_int, [_P, _PU32, _U32, _PU8, _PU32, _PU32]),
+    "kvmret_table_set_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32,
+                                                  _PI32, _PU32]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+def _check(rc):
+    if rc != OK:
+        raise KvmretError(f"kvmret error {rc}: {lib.kvmret_last_error().decode()}")
+
+
+def _u32(a):
+    a = np.ascontiguousarray(a, dtype=np.uint32)
+    return a, a.ctypes.data_as(_PU32)
+
+
+def default_config(**kw) -> Config:
+    c = Config()
+    lib.kvmret_config_default(ctypes.byref(c))
+    for k, v in kw.items():
+        if not hasattr(c, k):
+            raise KeyError(k)
+        setattr(c, k, v)
+    return c
+
+
+def row_bytes(type_id: int, n: int) -> int:
+    return int(lib.kvmret_row_bytes(type_id, n))
+
+
+@dataclass
+class Plan:
+    remaps: np.ndarray      # [n][7] int32: id, n_tok, from, to, resident, skip, raw
+    stage_in: np.ndarray
+    stage_out: np.ndarray
+
+
+def _torch_sync():
+    import torch
+    if torch.cuda.is_available():
+        torch.cuda.current_stream().synchronize()
+
+
+class Retriever:
+    """One retrieval context (one session shard) on one GPU."""
+
+    def __init__(self, cfg: Config):
+        self.cfg = cfg
+        h = _P()
+        _check(lib.kvmret_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+        self.E = cfg.n_head_kv * cfg.d_head
+        self.qdim = cfg.n_head * cfg.d_head
+        self.k_row = row_bytes(cfg.k_type, self.E)
+        self.v_row = row_bytes(cfg.v_type, self.E)
+
+    def close(self):
+        if self.h:
+            lib.kvmret_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # --- state
+    @property
+    def n_blocks(self) -> int:
+        return int(lib.kvmret_n_blocks(self.h))
+
+    @property
+    def n_tokens(self) -> int:
+        return int(lib.kvmret_n_tokens(self.h))
+
+    @property
+    def stream_ptr(self) -> int:
+        return int(lib.kvmret_stream(self.h) or 0)
+
+    def sync(self):
+        _check(lib.kvmret_sync(self.h))
+
+    # --- append (S2 + S14)
+    def append(self, k_cap, v_rows, k_rows=None, pos0=None):
+        """k_cap: [L][n][E] f16 CUDA tensor; k_rows / v_rows: [L][n][row bytes] CUDA tensors."""
+        n = int(k_cap.shape[1])
+        pos0 = self.n_tokens if pos0 is None else pos0
+        _torch_sync()
+        _check(lib.kvmret_append(self.h, pos0, n, k_cap.data_ptr(),
+                                 None if k_rows is None else k_rows.data_ptr(),
+                                 v_rows.data_ptr()))
+
+    def summaries(self) -> np.ndarray:
+        out = np.zeros((self.n_blocks, self.cfg.n_layer, self.E), np.float32)
+        _check(lib.kvmret_get_summaries(self.h, out.ctypes.data_as(_PF)))
+        return out
+
+    def repo_view(self) -> np.ndarray:
+        """The pinned host repository as a flat uint8 array."""
+        unit = int(lib.kvmret_repo_unit_bytes(self.h))
+        n = self.cfg.max_blocks * self.cfg.n_layer * unit
+        ptr = lib.kvmret_repo_host(self.h)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_uint8)), (n,))
+
+    # --- query (S1)
+    def query_reset(self):
+        _check(lib.kvmret_query_reset(self.h))
+
+    def query_add(self, q):
+        """q: [L][n_rows][n_head*d_head] f16 or f32 CUDA tensor."""
+        import torch
+        _torch_sync()
+        fn = lib.kvmret_query_add_f16 if q.dtype == torch.float16 else lib.kvmret_query_add_f32
+        _check(fn(self.h, q.data_ptr(), int(q.shape[1])))
+
+    def query_set(self, q_sum: np.ndarray, q_count: np.ndarray):
+        q_sum = np.ascontiguousarray(q_sum, np.float32)
+        c, cp = _u32(q_count)
+        _check(lib.kvmret_query_set(self.h, q_sum.ctypes.data_as(_PF), cp))
+
+    def query_get(self):
+        s = np.zeros((self.cfg.n_layer, self.qdim), np.float32)
+        c = np.zeros(self.cfg.n_layer, np.uint32)
+        _check(lib.kvmret_query_get(self.h, s.ctypes.data_as(_PF), c.ctypes.data_as(_PU32)))
+        return s, c
+
+    # --- score / select / apply
+    def score(self) -> np.ndarray:
+        out = np.zeros(self.n_blocks, np.float64)
+        _check(lib.kvmret_score(self.h, out.ctypes.data_as(_PD)))
+        return out
+
+    def select(self, mandatory=()):
+        m, mp = _u32(list(mandatory))
+        ids = np.zeros(max(1, min(self.cfg.budget_blocks, self.n_blocks)), np.uint32)
+        n = _U32(0)
+        _check(lib.kvmret_select(self.h, mp, len(m), ids.ctypes.data_as(_PU32), ctypes.byref(n)))
+        return ids[: n.value].copy()
+
+    def preview(self, mandatory=()):
+        m, mp = _u32(list(mandatory))
+        ids = np.zeros(max(1, min(self.cfg.budget_blocks, self.n_blocks)), np.uint32)
+        n = _U32(0)
+        _check(lib.kvmret_preview(self.h, mp, len(m), ids.ctypes.data_as(_PU32), ctypes.byref(n)))
+        return ids[: n.value].copy()
+
+    def apply(self, ids) -> dict:
+        a, ap = _u32(ids)
+        st = StepStats()
+        _check(lib.kvmret_apply_selection(self.h, ap, len(a), ctypes.byref(st)))
+        return st.as_dict()
+
+    def apply_retrieval(self, mandatory=()):
+        m, mp = _u32(list(mandatory))
+        ids = np.zeros(max(1, min(self.cfg.budget_blocks, self.n_blocks)), np.uint32)
+        n = _U32(0)
+        st = StepStats()
+        _check(lib.kvmret_apply_retrieval(self.h, mp, len(m), ids.ctypes.data_as(_PU32),
+                                          ctypes.byref(n), ctypes.byref(st)))
+        return ids[: n.value].copy(), st.as_dict()
+
+    def last_plan(self) -> Plan:
+        cap = max(1, self.n_blocks)
+        rm = np.zeros((cap, 7), np.int32)
+        si = np.zeros(cap, np.uint32)
+        so = np.zeros(cap, np.uint32)
+        nr, ni, no = _U32(0), _U32(0), _U32(0)
+        _check(lib.kvmret_last_plan(self.h, rm.ctypes.data_as(_PI32), ctypes.byref(nr),
+                                    si.ctypes.data_as(_PU32), ctypes.byref(ni),
+                                    so.ctypes.data_as(_PU32), ctypes.byref(no)))
+        return Plan(rm[: nr.value].copy(), si[: ni.value].copy(), so[: no.value].copy())
+
+    # --- window
+    def window_layout(self):
+        cap = int(lib.kvmret_window_slots(self.h))
+        ids = np.zeros(cap, np.uint32)
+        bases = np.zeros(cap, np.int32)
+        n = _U32(0)
+        _check(lib.kvmret_window_layout(self.h, ids.ctypes.data_as(_PU32),
+                                        bases.ctypes.data_as(_PI32), ctypes.byref(n)))
+        return ids[: n.value].copy(), bases[: n.value].copy()
+
+    def window_read(self, layer: int, is_v: bool, slot0: int, n_slots: int) -> np.ndarray:
+        row = self.v_row if is_v else self.k_row
+        out = np.zeros(n_slots * self.cfg.block_tokens * row, np.uint8)
+        _check(lib.kvmret_window_read(self.h, layer, int(is_v), slot0, n_slots,
+                                      out.ctypes.data_as(_P)))
+        return out
+
+
+class Table:
+    """Host block table alone (selection keep-set and plan diff); needs no GPU."""
+
+    def __init__(self, cfg: Config):
+        h = _P()
+        _check(lib.kvmret_table_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.kvmret_table_destroy(self.h)
+            self.h = None
+
+    def append(self, n_tokens: int):
+        _check(lib.kvmret_table_append(self.h, n_tokens))
+
+    @property
+    def n_blocks(self) -> int:
+        return int(lib.kvmret_table_n_blocks(self.h))
+
+    def keep(self, mandatory=()):
+        m, mp = _u32(list(mandatory))
+        kept = np.zeros(max(1, self.n_blocks), np.uint8)
+        kc, need = _U32(0), _U32(0)
+        _check(lib.kvmret_table_keep(self.h, mp, len(m), kept.ctypes.data_as(_PU8),
+                                     ctypes.byref(kc), ctypes.byref(need)))
+        return kept[: self.n_blocks].copy(), kc.value, need.value
+
+    def set_selection(self, ids, force_raw_refresh=False):
+        a, ap = _u32(ids)
+        cap = max(1, self.n_blocks)
+        si = np.zeros(cap, np.uint32)
+        so = np.zeros(cap, np.uint32)
+        rm = np.zeros((cap, 7), np.int32)
+        counts = np.zeros(6, np.uint32)
+        _check(lib.kvmret_table_set_selection(self.h, ap, len(a), int(force_raw_refresh),
+                                              si.ctypes.data_as(_PU32), so.ctypes.data_as(_PU32),
+                                              rm.ctypes.data_as(_PI32),
+                                              counts.ctypes.data_as(_PU32)))
+        return (si[: counts[0]].copy(), so[: counts[1]].copy(), rm[: counts[2]].copy(),
+                counts.copy())
+
+
+def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, stream=0):
+    """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors."""
+    _torch_sync()
+    _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
+                               d_head, pos0, freq_base, freq_scale, stream or None))
+
+
+def rope_q8_0(k, out, n_tok, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, fwht_n=0,
+              stream=0):
+    """k, out: q8_0 rows [n_tok][n_head_kv*d_head/32*34] uint8 CUDA tensors."""
+    _torch_sync()
+    _check(lib.kvmret_rope_q8_0(k.data_ptr(), out.data_ptr(), n_tok, n_head_kv, d_head, d_head,
+                                pos0, freq_base, freq_scale, fwht_n, stream or None))

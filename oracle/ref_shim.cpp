@@ -1,0 +1,106 @@
+// C-ABI shim over the reference's own libkvmem, compiled from the reference
+// sources (kvmem/src/host/*.cpp) into oracle/_ref/. TEST INFRASTRUCTURE ONLY:
+// it lets the tests pin the oracle restatement against the reference code
+// itself (selection, plan, mean-K, RoPE). Nothing here is shipped.
+
+#include "kvmem/kvmem_runtime.hpp"
+#include "kvmem/kvmem_store.hpp"
+#include "kvmem/raw_kv_store.hpp"
+#include "kvmem/rope.hpp"
+
+#include <cstring>
+#include <vector>
+
+#define REF_API extern "C" __attribute__((visibility("default")))
+
+// kvmem_store.cpp pick_topk_blocks via a fresh store of n full blocks.
+REF_API uint32_t ref_pick_topk(const double *scores, uint32_t n, uint32_t block_tokens,
+                               uint32_t budget_blocks, uint32_t sink_blocks,
+                               uint32_t recent_blocks, const uint32_t *mandatory,
+                               uint32_t n_mandatory, uint32_t *out) {
+    kvmem::KvMemStoreConfig cfg;
+    cfg.block_tokens = block_tokens;
+    cfg.select_budget = budget_blocks * block_tokens;
+    cfg.sink_blocks = sink_blocks;
+    cfg.recent_blocks = recent_blocks;
+    kvmem::KvMemStore s(cfg);
+    s.register_append(n * block_tokens);
+    s.set_retrieval_scores(std::vector<double>(scores, scores + n));
+    std::vector<uint32_t> mand(mandatory, mandatory + n_mandatory);
+    const auto sel = s.pick_topk_blocks(mand);
+    for (size_t i = 0; i < sel.size(); ++i) out[i] = sel[i];
+    return static_cast<uint32_t>(sel.size());
+}
+
+struct RefRuntime {
+    kvmem::KvMemRuntime rt;
+    explicit RefRuntime(kvmem::KvMemRuntimeConfig c) : rt(std::move(c)) {}
+};
+
+REF_API void *ref_runtime_create(uint32_t block_tokens, uint32_t budget_blocks,
+                                 uint32_t sink_blocks, int immutable_source_k) {
+    kvmem::KvMemRuntimeConfig c;
+    c.store.block_tokens = block_tokens;
+    c.store.select_budget = budget_blocks * block_tokens;
+    c.store.sink_blocks = sink_blocks;
+    c.store.immutable_source_k = immutable_source_k != 0;
+    return new RefRuntime(c);
+}
+REF_API void ref_runtime_free(void *p) { delete static_cast<RefRuntime *>(p); }
+REF_API void ref_runtime_append(void *p, uint32_t n_tokens) {
+    static_cast<RefRuntime *>(p)->rt.register_append(n_tokens);
+}
+
+// prepare_selection (set_selection) + finish_reselect (spill then admit).
+REF_API void ref_runtime_select(void *p, const uint32_t *ids, uint32_t n_ids,
+                                int force_raw_refresh, uint32_t *stage_in,
+                                uint32_t *stage_out, int32_t *remaps, uint32_t *counts) {
+    auto &rt = static_cast<RefRuntime *>(p)->rt;
+    const auto plan = rt.prepare_selection(std::vector<uint32_t>(ids, ids + n_ids),
+                                           force_raw_refresh != 0);
+    rt.finish_reselect();
+    for (size_t i = 0; i < plan.stage_in.size(); ++i) stage_in[i] = plan.stage_in[i];
+    for (size_t i = 0; i < plan.stage_out.size(); ++i) stage_out[i] = plan.stage_out[i];
+    for (size_t i = 0; i < plan.remaps.size(); ++i) {
+        const auto &r = plan.remaps[i];
+        int32_t *o = remaps + 7 * i;
+        o[0] = static_cast<int32_t>(r.block_id);
+        o[1] = static_cast<int32_t>(r.n_tokens);
+        o[2] = r.from_base;
+        o[3] = r.to_base;
+        o[4] = r.working_k_resident ? 1 : 0;
+        o[5] = r.skip ? 1 : 0;
+        o[6] = r.raw_refresh ? 1 : 0;
+    }
+    counts[0] = static_cast<uint32_t>(plan.stage_in.size());
+    counts[1] = static_cast<uint32_t>(plan.stage_out.size());
+    counts[2] = static_cast<uint32_t>(plan.remaps.size());
+    counts[3] = plan.total_window_tokens;
+    counts[4] = plan.selection_overlap_blocks;
+    counts[5] = plan.gpu_reused_blocks;
+}
+
+// RawKvStore::write_layer_mean_k + mean_k for one (block, layer).
+REF_API void ref_mean_k_f32(const float *k_rows, uint32_t n_tok, uint32_t n_embd_k,
+                            uint32_t block_tokens, float *out) {
+    kvmem::RawKvStoreConfig c;
+    c.n_layer = 1;
+    c.n_embd_k = n_embd_k;
+    c.n_embd_v = n_embd_k;
+    c.block_tokens = block_tokens;
+    kvmem::RawKvStore s(c);
+    s.write_layer_mean_k(0, n_tok, 0, k_rows);
+    s.mean_k(0, 0, out);
+}
+
+REF_API void ref_rope_neox(const float *k, uint32_t n_tok, uint32_t n_head,
+                           uint32_t n_embd_head, uint32_t n_rot, int32_t pos0,
+                           float freq_base, float freq_scale, float *out) {
+    kvmem::RopeConfig c;
+    c.n_rot = n_rot;
+    c.n_embd_head = n_embd_head;
+    c.n_head_kv = n_head;
+    c.freq_base = freq_base;
+    c.freq_scale = freq_scale;
+    kvmem::rope_neox_apply(c, k, n_tok, pos0, out);
+}

@@ -1,0 +1,88 @@
+"""The product's host block table (libkvmret, no GPU needed) against the
+reference's libkvmem and the oracle: the always-kept part of a selection and
+the plan diff (stage-in / stage-out / remaps) must be bit-identical."""
+import numpy as np
+import pytest
+
+import kvmret
+import pyoracle as po
+
+needs_ref = pytest.mark.skipif(po.ref is None, reason="oracle/_ref not built")
+
+
+def _table(bt, budget, sink=1, recent=0, immutable=False):
+    c = kvmret.default_config(block_tokens=bt, budget_blocks=budget, sink_blocks=sink,
+                              recent_blocks=recent, immutable_source_k=int(immutable))
+    return kvmret.Table(c)
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_keep_plus_rank_fill_equals_oracle_topk(seed):
+    """keep() + the score fill the GPU runs (emulated here by an exact rank) == pick_topk."""
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(1, 400))
+    budget = int(rng.integers(1, 64))
+    sink = int(rng.integers(0, 3))
+    recent = int(rng.integers(0, 3))
+    t = _table(16, budget, sink, recent)
+    t.append(n * 16)
+    scores = rng.standard_normal(n)
+    if seed % 2:
+        scores = np.round(scores)
+    mand = list(rng.integers(0, n, size=int(rng.integers(0, 5))))
+    kept, kc, need = t.keep(mand)
+    cand = [i for i in range(n) if not kept[i]]
+    order = sorted(cand, key=lambda i: (-scores[i], -i))
+    sel = sorted(set(np.nonzero(kept)[0].tolist()) | set(order[:need]))
+    assert sel == list(po.pick_topk(scores, budget, sink, recent, mand, tie_higher_id=True))
+
+
+@pytest.mark.parametrize("immutable", [False, True])
+@pytest.mark.parametrize("seed", range(6))
+def test_plan_equals_oracle(seed, immutable):
+    rng = np.random.default_rng(200 + seed)
+    bt = 16
+    t = _table(bt, 1 << 20, immutable=immutable)
+    o = po.Store(bt, immutable)
+    n_tok = int(rng.integers(bt, bt * 80))
+    t.append(n_tok)
+    o.append(n_tok)
+    for step in range(15):
+        if rng.random() < 0.25:
+            extra = int(rng.integers(1, 2 * bt))
+            t.append(extra)
+            o.append(extra)
+            n_tok += extra
+        nb = (n_tok + bt - 1) // bt
+        ids = rng.choice(nb + 3, size=int(rng.integers(0, nb + 1)), replace=True)
+        force = bool(rng.random() < 0.1)
+        a = t.set_selection(ids, force)
+        b = o.set_selection(ids, force)
+        for x, y in zip(a, b):
+            assert np.array_equal(x, y)
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", range(6))
+def test_plan_equals_reference_runtime(seed):
+    rng = np.random.default_rng(300 + seed)
+    bt = 128
+    t = _table(bt, 1 << 20)
+    r = po.RefRuntime(bt, 1 << 20, 1, False)
+    t.append(bt * 300)
+    r.append(bt * 300)
+    for _ in range(10):
+        ids = rng.choice(300, size=int(rng.integers(1, 64)), replace=False)
+        a = t.set_selection(ids)
+        b = r.set_selection(ids)
+        for x, y in zip(a, b):
+            assert np.array_equal(x, y)
+
+
+def test_keep_all_fit_and_empty():
+    t = _table(128, 8)
+    kept, kc, need = t.keep()
+    assert len(kept) == 0 and kc == 0 and need == 0
+    t.append(128 * 3)
+    kept, kc, need = t.keep()
+    assert list(kept) == [1, 1, 1] and need == 0
