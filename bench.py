@@ -1,0 +1,475 @@
+#!/usr/bin/env python3
+"""Benchmark of the KVMem per-step retrieval path on B200 (BASELINE metric:
+retrieval+stage-in us per decode step, 64 layers, 256K history).
+
+One step = accumulate the decode query, score every block on every layer,
+reduce the per-layer terms in layer order (exchanged between ranks when the
+layers are sharded), select the top-k, diff the plan, stage newly selected
+blocks host -> HBM pool and rebuild every changed window slot (K re-roped at
+its window position, V copied).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each owning n_layer / N layers;
+the only cross-rank traffic is an NCCL all-gather of the per-(layer, block)
+score terms (f64) and per-layer query flags, 1 MiB total at 64 layers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "kvmem-llama.cpp_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "retrieval+stage-in µs/decode step (64 layers, 256K); KV GB/s vs HBM/link peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [l.split(",") for l in open(self.f.name).read().splitlines() if l.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1].split()[0]))
+                mx = float(r[2].split()[0])
+                for n, v in zip(names, r[5:9]):
+                    if "Active" in v and "Not" not in v:
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def link_gbps(nbytes=1 << 30, reps=3):
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    best = 1e30
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            d.copy_(h, non_blocking=True)
+            e1.record(s)
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    del h, d
+    return nbytes / best / 1e9
+
+
+# ---------------------------------------------------------------------------
+def cpu_sample(w, n_h2d, n_asm, threads, use_ref, budget_s=10.0):
+    """CPU time of one step of the same workload, from timed samples of each
+    component (restated score_retrieval; pick_topk / set_selection /
+    rope_neox_apply from the reference's libkvmem when built, else the
+    oracle's restatement; memcpy staging of the stage-in bytes into a pinned
+    slab), scaled by the step's unit counts."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    use_ref = use_ref and po.ref is not None
+    rng = np.random.default_rng(0)
+    L, N, E, T = w.n_layer, w.n_blocks, w.E, w.block_tokens
+    ls = 2  # layers scored per sample
+    mean = rng.standard_normal((N, ls, E)).astype(np.float32)
+    has = np.ones(N, np.uint8)
+    q_sum = rng.standard_normal((ls, w.qdim)).astype(np.float32)
+    q_count = np.ones(ls, np.uint32)
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+
+    def timed(fn, reps):
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    # S3: score N blocks x ls layers; threads split the blocks
+    parts = np.array_split(np.arange(N), threads)
+
+    def score_all():
+        list(pool.map(lambda ix: po.score(mean[ix], has[ix], q_sum, q_count, w.n_head,
+                                          w.n_head_kv, w.d_head), parts))
+    t_score = timed(score_all, 2) * (L / ls)
+    scores = po.score(mean, has, q_sum, q_count, w.n_head, w.n_head_kv, w.d_head)
+    # S6 + S7
+    if use_ref:
+        t_topk = timed(lambda: po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks), 5)
+        rt = po.RefRuntime(T, w.budget_blocks, w.sink_blocks)
+        rt.append(N * T)
+        ids = po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks)
+        t_plan = timed(lambda: rt.set_selection(ids), 5)
+    else:
+        t_topk = timed(lambda: po.pick_topk(scores, w.budget_blocks, w.sink_blocks), 5)
+        st = po.Store(T)
+        st.append(N * T)
+        ids = po.pick_topk(scores, w.budget_blocks, w.sink_blocks)
+        t_plan = timed(lambda: st.set_selection(ids), 5)
+    # S11: staging memcpy of one block's units (all layers) into a host slab
+    unit = T * E * 2 * 2
+    s_np = np.ones(L * unit, np.uint8)
+    d_np = np.zeros(L * unit, np.uint8)
+    chunks = np.array_split(np.arange(L * unit // 4096), threads)
+
+    def stage():
+        list(pool.map(lambda ix: np.copyto(d_np[ix[0] * 4096:(ix[-1] + 1) * 4096],
+                                           s_np[ix[0] * 4096:(ix[-1] + 1) * 4096]), chunks))
+    t_stage = timed(stage, 3) * n_h2d
+    # S12: RoPE of K block-layer units (f16 -> f32 -> rope -> f16)
+    kb = rng.standard_normal((threads, T, w.n_head_kv, w.d_head)).astype(np.float16)
+
+    def rope_unit(i):
+        x = kb[i].astype(np.float32)
+        if use_ref:
+            y = po.ref_rope_neox(x, 4096 + i, w.freq_base)
+        else:
+            y = po.rope_neox(x, 4096 + i, w.freq_base)
+        return y.astype(np.float16)
+
+    t_rope = timed(lambda: list(pool.map(rope_unit, range(threads))), 2) / threads
+    t_rope *= n_asm * L
+    pool.shutdown()
+    total = t_score + t_topk + t_plan + t_stage + t_rope
+    parts_s = {"score": t_score, "topk": t_topk, "plan": t_plan, "stage_memcpy": t_stage,
+               "rope": t_rope}
+    return total, parts_s, ("reference" if use_ref else "port")
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    threads = os.cpu_count() or 1
+    n_h2d, n_asm = args.churn_h2d, args.churn_asm
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(w, n_h2d, n_asm, threads, True)
+    parts = None
+    for _ in range(args.steps):
+        t, parts, kind = cpu_sample(w, n_h2d, n_asm, threads, True)
+        vals.append(t)
+    us = sum(vals) / len(vals) * 1e6
+    sample = (f"per step: restated score_retrieval on 2 of {w.n_layer} layers x {w.n_blocks} "
+              f"blocks (x{w.n_layer // 2}), pick_topk + set_selection on all blocks, memcpy "
+              f"staging of one block's {w.n_layer} layers (x{n_h2d} new blocks/step), "
+              f"rope_neox_apply of {threads} block-layers (x{n_asm} moved blocks x "
+              f"{w.n_layer} layers); "
+              f"{'libkvmem from reference sources' if po.ref is not None else 'oracle port'}")
+    line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/step",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": w.name, "threads": threads},
+            "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads,
+                             "kind": kind, "sample": sample,
+                             "parts_ms": {k: round(v * 1e3, 3) for k, v in parts.items()}},
+            "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, w):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kvmret
+    from kvmret import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    if w.n_layer % world:
+        raise SystemExit(f"{w.n_layer} layers do not split over {world} GPUs")
+    Ll = w.n_layer // world
+    layer0 = rank * Ll
+    T = w.block_tokens
+
+    cfg = kvmret.default_config(
+        n_layer=Ll, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head, block_tokens=T,
+        max_blocks=w.n_blocks, budget_blocks=w.budget_blocks, reserve_blocks=w.reserve_blocks,
+        sink_blocks=w.sink_blocks, k_type=w.k_type, v_type=w.v_type, n_rot=w.d_head,
+        freq_base=w.freq_base, pool_cache=int(args.pool_cache), device=local)
+    t_setup = time.perf_counter()
+    r = kvmret.Retriever(cfg)
+    hist = synth.TorchHistory(w, local, layer0=layer0, n_layer=Ll)
+    chunk = 64 * T
+    for t0 in range(0, w.n_tokens, chunk):
+        m = min(chunk, w.n_tokens - t0)
+        kc, vc = hist.chunk(t0, m)
+        r.append(kc, vc, pos0=t0)
+        r.sync()
+        del kc, vc
+    torch.cuda.synchronize()
+    t_setup = time.perf_counter() - t_setup
+    link = link_gbps()
+
+    stride = r.contrib_stride
+    contrib_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
+    active_loc = torch.zeros(Ll, dtype=torch.uint8, device="cuda")
+    contrib_all = contrib_loc if world == 1 else torch.zeros(w.n_layer * stride,
+                                                              dtype=torch.float64, device="cuda")
+    active_all = active_loc if world == 1 else torch.zeros(w.n_layer, dtype=torch.uint8,
+                                                           device="cuda")
+    ext = torch.cuda.ExternalStream(r.stream_ptr)
+    cur = torch.cuda.current_stream()
+
+    def step(q_dev):
+        r.query_reset()
+        r.query_add(q_dev)
+        r.score_layers(contrib_loc, active_loc)
+        if world > 1:
+            ev = torch.cuda.Event()
+            ev.record(ext)
+            cur.wait_event(ev)
+            dist.all_gather_into_tensor(contrib_all, contrib_loc)
+            dist.all_gather_into_tensor(active_all, active_loc)
+            ev2 = torch.cuda.Event()
+            ev2.record(cur)
+            ext.wait_event(ev2)
+        r.score_reduce(contrib_all, active_all, w.n_layer)
+        ids = r.select()
+        return r.apply(ids)
+
+    def queries(n):
+        out = []
+        for _ in range(n):
+            q = hist.next_query()[layer0:layer0 + Ll].contiguous()
+            out.append(q)
+        return out
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # clocks are sampled from before the warm-up until after the e2e loop
+    clocks = Clocks(local)
+    time.sleep(0.6)
+    # warm-up (the first step stages the whole window from the host)
+    for q in queries(args.warmup):
+        step(q)
+    r.sync()
+
+    # timed region: device time of exactly K steps on the library stream
+    qs = queries(args.steps)
+    torch.cuda.synchronize()
+    r.prof_enable(True)
+    barrier()
+    r.sync()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stats = []
+    e0.record(ext)
+    for q in qs:
+        stats.append(step(q))
+    e1.record(ext)
+    r.sync()
+    torch.cuda.synchronize()
+    barrier()
+    prof = r.prof_read()
+    r.prof_enable(False)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+
+    # e2e: host query buffer -> device every step, ids back on the host
+    qh = [q.cpu().pin_memory() for q in queries(args.steps)]
+    qd = torch.empty_like(qs[0])
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_stats = []
+    for q in qh:
+        qd.copy_(q, non_blocking=True)
+        e2e_stats.append(step(qd))
+    r.sync()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_us = e2e_s / args.steps * 1e6
+
+    def avg(key, ss):
+        return sum(s[key] for s in ss) / len(ss)
+
+    n_h2d = avg("n_h2d_blocks", stats)
+    n_moved = avg("n_moved", stats)
+    n_asm = avg("n_assembled", stats)
+    h2d_step = avg("h2d_bytes", stats)
+    asm_step = avg("assemble_bytes", stats)
+    score_step = prof["score_bytes"] / max(1, prof["n_score"])
+    hbm, peak_src = load_peaks()
+
+    # roofline of the dominant kernel (assembly of moved blocks), live event timing
+    n_launch = max(1, prof["n_asm_moved"])
+    asm_ms = prof["asm_moved_ms"] / n_launch
+    asm_bytes = prof["asm_moved_bytes"] / n_launch
+    achieved = asm_bytes / (asm_ms / 1e3) / 1e9 if asm_ms > 0 else 0.0
+    score_ms = prof["score_ms"] / max(1, prof["n_score"])
+    score_gbs = score_step / (score_ms / 1e3) / 1e9 if score_ms > 0 else 0.0
+    h2d_ms = prof["h2d_ms"] / max(1, prof["n_h2d"])
+    h2d_gbs = (prof["h2d_bytes"] / max(1, prof["n_h2d"])) / (h2d_ms / 1e3) / 1e9 if h2d_ms else 0
+    # step roofline: T = B_sum/BW_hbm + max(B_link/BW_link, (B_link + B_asm)/BW_hbm)
+    t_roof = score_step / (hbm * 1e9) + max(h2d_step / (link * 1e9),
+                                             (h2d_step + asm_step) / (hbm * 1e9))
+    kv_bytes = score_step + h2d_step + asm_step
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(ms_step * 1e3, 1), "unit": "us/step",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16" if w.k_type == kvmret.TYPE_F16 else "q8_0/q4_0",
+            "data": "synthetic: seeded N(0,1) x LogNormal(0,0.5) channel scale, "
+                    f"{w.n_planted} planted blocks, query drift {w.drift}/step",
+            "config": {
+                "workload": f"{w.name}: {w.n_layer} layers, {w.n_head}q/{w.n_head_kv}kv heads, "
+                            f"d{w.d_head}, {w.n_blocks} blocks x {T} tok ({w.n_tokens // 1024}K), "
+                            f"budget {w.budget_blocks} blocks, sink {w.sink_blocks}, gen-reserve "
+                            f"{w.reserve_blocks} slots",
+                "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
+                "l2": "inputs larger than L2 (summaries "
+                      f"{score_step / 2**20:.0f} MiB/step, window/pool GiB-scale)",
+                "pool_cache": bool(args.pool_cache)},
+            "roofline": {"kernel": "assemble (moved window slots)", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": None,
+                         "peak_source": peak_src,
+                         "avg_launch_ms": round(asm_ms, 4),
+                         "alg_bytes_per_launch": int(asm_bytes)},
+            "kernels": {
+                "score": {"ms": round(score_ms, 4), "GB/s": round(score_gbs, 1),
+                          "frac_hbm": round(score_gbs / hbm, 4)},
+                "assemble_new": {"ms": round(prof["asm_new_ms"] / max(1, prof["n_asm_new"]), 4),
+                                 "launches": prof["n_asm_new"]},
+                "h2d_stage_in": {"ms": round(h2d_ms, 4), "GB/s": round(h2d_gbs, 2),
+                                 "frac_link": round(h2d_gbs / link, 4) if link else None}},
+            "step_roofline": {"t_roof_us": round(t_roof * 1e6, 1),
+                              "t_meas_us": round(ms_step * 1e3, 1),
+                              "frac": round(t_roof * 1e3 / ms_step, 4),
+                              "link_gbs_measured": round(link, 2), "hbm_gbs": hbm,
+                              "B_sum": int(score_step), "B_link": int(h2d_step),
+                              "B_asm": int(asm_step)},
+            "kv_gbps": round(kv_bytes / (ms_step / 1e3) / 1e9, 1),
+            "churn": {"n_h2d_blocks": round(n_h2d, 2), "n_moved": round(n_moved, 2),
+                      "n_assembled": round(n_asm, 2)},
+            "e2e": {"value": round(e2e_us, 1), "unit": "us/step",
+                    "h2d_bytes_per_step": int(qs[0].numel() * 2 + h2d_step),
+                    "d2h_bytes_per_step": int(w.n_blocks)},
+            "gpu_launches": int(prof["launches"]),
+            "clocks": clk,
+            "setup_s": round(t_setup, 1),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            total, parts, kind = cpu_sample(w, max(1, round(n_h2d)), max(1, round(n_asm)), 1,
+                                            False)
+            line["cpu_baseline"] = {
+                "value": round(total * 1e6, 1), "unit": "us/step", "cores": 1, "kind": kind,
+                "sample": "restated score_retrieval on 2 layers x all blocks (scaled to "
+                          f"{w.n_layer}), pick_topk + set_selection, memcpy staging of one "
+                          f"block (x{round(n_h2d)}), host RoPE of 1 block-layer (x"
+                          f"{round(n_asm)} x {w.n_layer})",
+                "parts_ms": {k: round(v * 1e3, 3) for k, v in parts.items()}}
+    r.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--pool-cache", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (dev only)")
+    ap.add_argument("--budget", type=int, default=0, help="override budget blocks (dev only)")
+    ap.add_argument("--reserve", type=int, default=-1, help="override reserve slots (dev only)")
+    ap.add_argument("--churn-h2d", type=int, default=26,
+                    help="reference arm: new blocks per step (measured churn of config 2)")
+    ap.add_argument("--churn-asm", type=int, default=230,
+                    help="reference arm: rewritten window slots per step")
+    args = ap.parse_args()
+    from kvmret import synth
+    w = synth.CONFIGS[args.config]
+    if args.layers:
+        w = synth.scaled(w, n_layer=args.layers)
+    if args.budget:
+        w = synth.scaled(w, budget_blocks=args.budget)
+    if args.reserve >= 0:
+        w = synth.scaled(w, reserve_blocks=args.reserve)
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -151,8 +151,10 @@ int kvmret_query_get(kvmret_ctx *ctx, float *q_sum_host, uint32_t *q_count_host)
 /* Score every block; if scores_host != NULL copy the n_blocks f64 scores out. */
 int kvmret_score(kvmret_ctx *ctx, double *scores_host);
 /* Layer-sharded form: per-(layer, block) terms layer_sum / n_head_kv (f64) of
- * this context's layers into its contribution buffer, without the reduction. */
-int kvmret_score_layers(kvmret_ctx *ctx);
+ * this context's layers, without the reduction. contrib_out_dev (NULL = the
+ * context's own buffer) receives [n_layer][contrib_stride] f64 and
+ * active_out_dev (may be NULL) the per-layer "has query" flags [n_layer] u8. */
+int kvmret_score_layers(kvmret_ctx *ctx, double *contrib_out_dev, uint8_t *active_out_dev);
 /* Device pointer to the contribution buffer [n_layer][contrib_stride] f64 and
  * the per-layer "has query" flags [n_layer] u8. */
 const double *kvmret_contrib_dev(kvmret_ctx *ctx);
@@ -211,6 +213,25 @@ int kvmret_window_layout(kvmret_ctx *ctx, uint32_t *ids_out, int32_t *bases_out,
  * src/adapter/llama-memory-kvmem.cpp:4600-4650). */
 int kvmret_window_read(kvmret_ctx *ctx, uint32_t layer, int is_v, uint32_t slot0,
                        uint32_t n_slots, void *out_host);
+
+/* ---- per-step timing: the KVMEM_PERF retrieval buckets
+ *      (src/adapter/llama-memory-kvmem.cpp:4198-4216, struct
+ *      src/adapter/llama-memory-kvmem.h:357-382), measured with CUDA events on
+ *      the stream each kernel or copy runs on. ---- */
+typedef struct kvmret_prof {
+    uint64_t launches;        /* kernels launched by the context since reset */
+    uint32_t n_score, n_asm_moved, n_asm_new, n_h2d;   /* timed regions */
+    uint32_t dropped;         /* regions not timed (event pool exhausted) */
+    double score_ms;          /* scoring kernel */
+    double asm_moved_ms;      /* window assembly of resident (moved) blocks */
+    double asm_new_ms;        /* window assembly of freshly staged blocks */
+    double h2d_ms;            /* host -> HBM pool copies (copy stream) */
+    uint64_t score_bytes, asm_moved_bytes, asm_new_bytes, h2d_bytes;
+} kvmret_prof;
+/* Reset the counters and turn event timing on (1) or off (0). */
+int kvmret_prof_enable(kvmret_ctx *ctx, int on);
+/* Drain the streams, resolve the recorded events and return the totals. */
+int kvmret_prof_read(kvmret_ctx *ctx, kvmret_prof *out);
 
 /* ---- stateless kernels on caller buffers (the kvmem_stagein_* / kvmem_d2d /
  *      kvmem_meank surface, src/adapter/llama-kvmem-stagein.h:1-67). `stream`

@@ -83,6 +83,7 @@ struct kvmret_ctx {
     uint8_t *pool = nullptr, *win_k = nullptr, *win_v = nullptr;
     Job *jobs_dev = nullptr;
     kvmret::CopyOp *ops_dev = nullptr;
+    float2 *rope_tab = nullptr;  // cos/sin of every window position [pos][n_rot/2]
     // host
     uint8_t *repo_host = nullptr, *repo_dev = nullptr, *pin_sel = nullptr;
     std::vector<uint32_t> q_count;
@@ -101,6 +102,19 @@ struct kvmret_ctx {
     std::vector<uint32_t> win_ntok;
     cudaStream_t st = nullptr, st_copy = nullptr;
     cudaEvent_t ev_prev = nullptr, ev_h2d = nullptr;
+    static constexpr int kGroups = 8;  // fresh-block copy/assembly pipeline depth
+    cudaEvent_t ev_grp[kGroups] = {};
+    // timing (kvmret_prof_*): event pool and pending (begin, end, kind, bytes)
+    struct Region {
+        cudaEvent_t a, b;
+        int kind;
+        uint64_t bytes;
+    };
+    bool prof_on = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_next = 0;
+    std::vector<Region> pending;
+    kvmret_prof prof{};
 
     explicit kvmret_ctx(const kvmret::TableConfig &tc) : table(tc) {}
 };
@@ -157,8 +171,30 @@ int ensure_qprep(kvmret_ctx *c) {
                        cudaMemcpyHostToDevice, c->st));
     CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, c->cfg.n_layer,
                             c->cfg.n_head, c->cfg.n_head_kv, c->cfg.d_head, c->st));
+    c->prof.launches += 1;
     c->q_dirty = false;
     return KVMRET_OK;
+}
+
+enum { PR_SCORE = 0, PR_ASM_MOVED, PR_ASM_NEW, PR_H2D };
+constexpr size_t kEventPool = 8192;
+
+// Begin a timed region on stream `s`; returns the region index or -1.
+int prof_begin(kvmret_ctx *c, cudaStream_t s, int kind, uint64_t bytes) {
+    if (!c->prof_on) return -1;
+    if (c->ev_next + 2 > c->ev_pool.size()) {
+        ++c->prof.dropped;
+        return -1;
+    }
+    kvmret_ctx::Region r{c->ev_pool[c->ev_next], c->ev_pool[c->ev_next + 1], kind, bytes};
+    c->ev_next += 2;
+    if (cudaEventRecord(r.a, s) != cudaSuccess) return -1;
+    c->pending.push_back(r);
+    return static_cast<int>(c->pending.size() - 1);
+}
+
+void prof_end(kvmret_ctx *c, cudaStream_t s, int idx) {
+    if (idx >= 0) cudaEventRecord(c->pending[idx].b, s);
 }
 
 void free_all(kvmret_ctx *c) {
@@ -167,11 +203,14 @@ void free_all(kvmret_ctx *c) {
     if (c->st_copy) cudaStreamSynchronize(c->st_copy);
     void *dev[] = {c->summ, c->tail_sum, c->q_sum, c->qv, c->nq, c->q_count_dev, c->has_block,
                    c->active, c->kept_dev, c->sel_dev, c->contrib, c->scores, c->pool,
-                   c->win_k, c->win_v, c->jobs_dev, c->ops_dev};
+                   c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
     if (c->pin_sel) cudaFreeHost(c->pin_sel);
+    for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
+    for (cudaEvent_t e : c->ev_grp)
+        if (e) cudaEventDestroy(e);
     if (c->ev_prev) cudaEventDestroy(c->ev_prev);
     if (c->ev_h2d) cudaEventDestroy(c->ev_h2d);
     if (c->st) cudaStreamDestroy(c->st);
@@ -235,6 +274,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     CK(cudaStreamCreateWithFlags(&c->st_copy, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&c->ev_prev, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&c->ev_h2d, cudaEventDisableTiming));
+    for (auto &e : c->ev_grp) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
 
     const size_t L = k.n_layer;
     TRY(dmalloc(&c->summ, L * c->E * c->ncap * sizeof(float)));
@@ -254,6 +294,9 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     TRY(dmalloc(&c->win_v, L * c->win_v_layer));
     TRY(dmalloc(&c->jobs_dev, 2ull * c->win_slots * sizeof(Job)));
     TRY(dmalloc(&c->ops_dev, 8192 * sizeof(kvmret::CopyOp)));
+    const uint32_t n_pos = c->win_slots * k.block_tokens;
+    TRY(dmalloc(&c->rope_tab, static_cast<size_t>(n_pos) * (k.n_rot / 2) * sizeof(float2)));
+    CK(kvmret::launch_rope_table(c->rope_tab, n_pos, k.n_rot / 2, c->theta, c->st));
     CK(cudaMemsetAsync(c->summ, 0, L * c->E * c->ncap * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->tail_sum, 0, 2 * L * c->E * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->q_sum, 0, L * c->qdim * sizeof(float), c->st));
@@ -375,28 +418,60 @@ int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_s
         c->win_id[w] = -1;
         c->win_ntok[w] = 0;
     }
-    // Enqueue: host->pool copies on the copy stream after the previous step's
-    // readers of the pool; resident moves immediately; fresh blocks after the copies.
-    if (!h2d.empty()) {
-        CK(cudaEventRecord(c->ev_prev, c->st));
-        CK(cudaStreamWaitEvent(c->st_copy, c->ev_prev, 0));
-        for (const auto &bs : h2d)
-            CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(bs.second) * c->slot_bytes,
-                               c->repo_host + static_cast<uint64_t>(bs.first) * c->slot_bytes,
-                               c->slot_bytes, cudaMemcpyHostToDevice, c->st_copy));
-        CK(cudaEventRecord(c->ev_h2d, c->st_copy));
-    }
+    // Enqueue. Host->pool copies go on the copy stream after the previous
+    // step's readers of the pool, in up to kGroups groups; resident moves start
+    // at once on the compute stream; each group of fresh blocks is assembled as
+    // soon as its own copies have landed.
     std::vector<Job> all(moved);
     all.insert(all.end(), added.begin(), added.end());
     if (!all.empty())
         CK(cudaMemcpyAsync(c->jobs_dev, all.data(), all.size() * sizeof(Job),
                            cudaMemcpyHostToDevice, c->st));
-    CK(kvmret::launch_assemble(c->jobs_dev, static_cast<uint32_t>(moved.size()), c->pool,
-                               c->slot_bytes, c->win_k, c->win_v, c->theta, c->geom, c->st));
-    if (!h2d.empty()) CK(cudaStreamWaitEvent(c->st, c->ev_h2d, 0));
-    CK(kvmret::launch_assemble(c->jobs_dev + moved.size(), static_cast<uint32_t>(added.size()),
-                               c->pool, c->slot_bytes, c->win_k, c->win_v, c->theta, c->geom,
-                               c->st));
+    const size_t n_new = h2d.size();  // == added.size(), same order
+    const size_t groups = std::min<size_t>(n_new, kvmret_ctx::kGroups);
+    auto grp_begin = [&](size_t g) { return n_new * g / groups; };
+    if (n_new) {
+        CK(cudaEventRecord(c->ev_prev, c->st));
+        CK(cudaStreamWaitEvent(c->st_copy, c->ev_prev, 0));
+        const int pr = prof_begin(c, c->st_copy, PR_H2D, n_new * c->slot_bytes);
+        for (size_t g = 0; g < groups; ++g) {
+            for (size_t i = grp_begin(g); i < grp_begin(g + 1); ++i)
+                CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(h2d[i].second) * c->slot_bytes,
+                                   c->repo_host + static_cast<uint64_t>(h2d[i].first) * c->slot_bytes,
+                                   c->slot_bytes, cudaMemcpyHostToDevice, c->st_copy));
+            CK(cudaEventRecord(c->ev_grp[g], c->st_copy));
+        }
+        prof_end(c, c->st_copy, pr);
+    }
+    auto job_bytes = [&](const Job *v, size_t n) {
+        uint64_t tok = 0;
+        for (size_t i = 0; i < n; ++i) tok += v[i].n_tok;
+        return 2ull * tok * (c->k_row + c->v_row) * c->cfg.n_layer;
+    };
+    kvmret::AsmLaunch al{};
+    al.pool = c->pool;
+    al.slot_bytes = c->slot_bytes;
+    al.win_k = c->win_k;
+    al.win_v = c->win_v;
+    al.gtab = c->rope_tab;
+    al.theta = c->theta;
+    al.g = c->geom;
+    if (!moved.empty()) {
+        const int pr = prof_begin(c, c->st, PR_ASM_MOVED, job_bytes(moved.data(), moved.size()));
+        al.jobs = c->jobs_dev;
+        CK(kvmret::launch_assemble(al, static_cast<uint32_t>(moved.size()), c->st));
+        prof_end(c, c->st, pr);
+        c->prof.launches += 1;
+    }
+    for (size_t g = 0; g < groups; ++g) {
+        const size_t b = grp_begin(g), e = grp_begin(g + 1);
+        CK(cudaStreamWaitEvent(c->st, c->ev_grp[g], 0));
+        const int pr = prof_begin(c, c->st, PR_ASM_NEW, job_bytes(added.data() + b, e - b));
+        al.jobs = c->jobs_dev + moved.size() + b;
+        CK(kvmret::launch_assemble(al, static_cast<uint32_t>(e - b), c->st));
+        prof_end(c, c->st, pr);
+        c->prof.launches += 1;
+    }
     if (stats) {
         std::memset(stats, 0, sizeof(*stats));
         stats->n_selected = static_cast<uint32_t>(p.remaps.size());
@@ -427,6 +502,7 @@ int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
         CK(cudaMemcpyAsync(c->kept_dev, kept.data(), n, cudaMemcpyHostToDevice, c->st));
         CK(kvmret::launch_select(c->scores, c->kept_dev, n, need, c->cfg.tie_higher_id,
                                  c->sel_dev, c->st));
+        c->prof.launches += 1;
         CK(cudaMemcpyAsync(c->pin_sel, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
         CK(cudaStreamSynchronize(c->st));
         sel = c->pin_sel;
@@ -441,18 +517,27 @@ int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
     return KVMRET_OK;
 }
 
-int score_layers_impl(kvmret_ctx *c) {
+int score_layers_impl(kvmret_ctx *c, double *contrib_out, uint8_t *active_out) {
     TRY(ensure_qprep(c));
-    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, c->contrib, c->cfg.n_layer,
-                            c->cfg.n_head_kv, c->cfg.d_head, c->ncap, c->table.n_blocks(), c->st));
+    const uint32_t n = c->table.n_blocks();
+    const uint64_t bytes = static_cast<uint64_t>(c->cfg.n_layer) * c->E *
+                           ((n + 127) / 128 * 128) * sizeof(float);
+    const int pr = prof_begin(c, c->st, PR_SCORE, bytes);
+    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, contrib_out ? contrib_out : c->contrib,
+                            c->cfg.n_layer, c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st));
+    prof_end(c, c->st, pr);
+    c->prof.launches += n ? 1 : 0;
+    if (active_out)
+        CK(cudaMemcpyAsync(active_out, c->active, c->cfg.n_layer, cudaMemcpyDeviceToDevice, c->st));
     return KVMRET_OK;
 }
 
 int score_impl(kvmret_ctx *c, double *scores_host) {
-    TRY(score_layers_impl(c));
+    TRY(score_layers_impl(c, nullptr, nullptr));
     const uint32_t n = c->table.n_blocks();
     CK(kvmret::launch_reduce(c->contrib, c->active, c->cfg.n_layer, c->ncap, c->has_block, n,
                              c->scores, c->st));
+    c->prof.launches += n ? 1 : 0;
     if (scores_host) {
         CK(cudaMemcpyAsync(scores_host, c->scores, n * sizeof(double), cudaMemcpyDeviceToHost,
                            c->st));
@@ -601,6 +686,7 @@ int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *
     a.has_block = c->has_block;
     a.repo_dev = c->repo_dev;
     CK(kvmret::launch_append(a, c->st));
+    c->prof.launches += 2;
     GUARD(c->table.append(n_tok));
     return KVMRET_OK;
 }
@@ -636,6 +722,7 @@ static int query_add(kvmret_ctx *c, const void *q, bool f16, uint32_t n_rows) {
     if (!q) return fail(KVMRET_ERR_ARG, "null query");
     if (n_rows == 0) return KVMRET_OK;
     CK(kvmret::launch_query_add(c->q_sum, q, f16, c->cfg.n_layer, n_rows, c->qdim, c->st));
+    c->prof.launches += 1;
     for (auto &x : c->q_count) x += n_rows;
     c->q_dirty = true;
     return KVMRET_OK;
@@ -678,9 +765,9 @@ int kvmret_score(kvmret_ctx *c, double *scores_host) {
     return score_impl(c, scores_host);
 }
 
-int kvmret_score_layers(kvmret_ctx *c) {
+int kvmret_score_layers(kvmret_ctx *c, double *contrib_out, uint8_t *active_out) {
     NEED_CTX(c);
-    return score_layers_impl(c);
+    return score_layers_impl(c, contrib_out, active_out);
 }
 
 const double *kvmret_contrib_dev(kvmret_ctx *c) { return c ? c->contrib : nullptr; }
@@ -694,6 +781,43 @@ int kvmret_score_reduce(kvmret_ctx *c, const double *contrib_all, const uint8_t 
         return fail(KVMRET_ERR_ARG, "bad contribution buffer");
     CK(kvmret::launch_reduce(contrib_all, active_all, n_layer_all, stride, c->has_block,
                              c->table.n_blocks(), c->scores, c->st));
+    c->prof.launches += 1;
+    return KVMRET_OK;
+}
+
+int kvmret_prof_enable(kvmret_ctx *c, int on) {
+    NEED_CTX(c);
+    CK(cudaStreamSynchronize(c->st));
+    CK(cudaStreamSynchronize(c->st_copy));
+    if (on && c->ev_pool.empty()) {
+        GUARD(c->ev_pool.resize(kEventPool, nullptr));
+        for (auto &e : c->ev_pool) CK(cudaEventCreate(&e));
+    }
+    c->prof = kvmret_prof{};
+    c->pending.clear();
+    c->ev_next = 0;
+    c->prof_on = on != 0;
+    return KVMRET_OK;
+}
+
+int kvmret_prof_read(kvmret_ctx *c, kvmret_prof *out) {
+    NEED_CTX(c);
+    if (!out) return fail(KVMRET_ERR_ARG, "null output");
+    CK(cudaStreamSynchronize(c->st));
+    CK(cudaStreamSynchronize(c->st_copy));
+    for (const auto &r : c->pending) {
+        float ms = 0.0f;
+        CK(cudaEventElapsedTime(&ms, r.a, r.b));
+        switch (r.kind) {
+        case PR_SCORE: c->prof.score_ms += ms; ++c->prof.n_score; c->prof.score_bytes += r.bytes; break;
+        case PR_ASM_MOVED: c->prof.asm_moved_ms += ms; ++c->prof.n_asm_moved; c->prof.asm_moved_bytes += r.bytes; break;
+        case PR_ASM_NEW: c->prof.asm_new_ms += ms; ++c->prof.n_asm_new; c->prof.asm_new_bytes += r.bytes; break;
+        default: c->prof.h2d_ms += ms; ++c->prof.n_h2d; c->prof.h2d_bytes += r.bytes; break;
+        }
+    }
+    c->pending.clear();
+    c->ev_next = 0;
+    *out = c->prof;
     return KVMRET_OK;
 }
 
@@ -803,11 +927,15 @@ int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n
     g.block_tokens = 128;
     g.k_row = 2ull * n_head_kv * d_head;
     g.k_type = KVMRET_TYPE_F16;
-    const uint32_t jobs = (n_tok + 127) / 128;
-    CK(kvmret::launch_assemble(nullptr, jobs, reinterpret_cast<const uint8_t *>(k),
-                               128 * g.k_row, reinterpret_cast<uint8_t *>(out), nullptr,
-                               make_theta(n_rot, freq_base, freq_scale), g,
-                               static_cast<cudaStream_t>(stream), pos0, n_tok));
+    kvmret::AsmLaunch al{};
+    al.pool = reinterpret_cast<const uint8_t *>(k);
+    al.slot_bytes = 128 * g.k_row;
+    al.win_k = reinterpret_cast<uint8_t *>(out);
+    al.synth_pos0 = pos0;
+    al.synth_ntok = n_tok;
+    al.theta = make_theta(n_rot, freq_base, freq_scale);
+    al.g = g;
+    CK(kvmret::launch_assemble(al, (n_tok + 127) / 128, static_cast<cudaStream_t>(stream)));
     return KVMRET_OK;
 }
 
@@ -832,11 +960,15 @@ int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_k
     g.k_type = KVMRET_TYPE_Q8_0;
     g.fwht_n = fwht_n;
     g.fwht_scale = fwht_n ? 1.0f / std::sqrt(static_cast<float>(fwht_n)) : 0.0f;
-    const uint32_t jobs = (n_tok + 127) / 128;
-    CK(kvmret::launch_assemble(nullptr, jobs, static_cast<const uint8_t *>(k), 128 * row,
-                               static_cast<uint8_t *>(out), nullptr,
-                               make_theta(n_rot, freq_base, freq_scale), g,
-                               static_cast<cudaStream_t>(stream), pos0, n_tok));
+    kvmret::AsmLaunch al{};
+    al.pool = static_cast<const uint8_t *>(k);
+    al.slot_bytes = 128 * row;
+    al.win_k = static_cast<uint8_t *>(out);
+    al.synth_pos0 = pos0;
+    al.synth_ntok = n_tok;
+    al.theta = make_theta(n_rot, freq_base, freq_scale);
+    al.g = g;
+    CK(kvmret::launch_assemble(al, (n_tok + 127) / 128, static_cast<cudaStream_t>(stream)));
     return KVMRET_OK;
 }
 

@@ -206,25 +206,44 @@ __global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ 
 }
 
 // ---------------------------------------------------------------------------
-// RoPE table: cos/sin of (pos0 + t) * theta[i] for the job's tokens, in shared
-// memory, shared by every head and layer the CTA handles (rope.cpp:27-33; the
-// reference GPU kernel evaluates the same angle with sincosf,
-// llama-kvmem-stagein.cu:170-173). Entries of each 8-wide group are rotated by
-// the group index so the 8 threads of a head row hit distinct banks.
+// RoPE table: cos / sin of the float angle (pos0 + t) * theta[i]
+// (rope.cpp:27-33). The angle is the reference's float product; cos and sin
+// are evaluated in double and rounded once to float, i.e. correctly rounded,
+// so the table does not add the few-ulp error of a float sincos. Window
+// positions come from a per-context table built once at creation; the
+// stateless entry points evaluate the same expression on the fly. Entries of
+// each 8-wide group are rotated by the group index so the 8 threads of a head
+// row hit distinct shared-memory banks.
 __device__ __forceinline__ uint32_t tab_swz(uint32_t i) {
     return (i & ~7u) | (((i & 7u) - (i >> 3)) & 7u);
 }
 
+__device__ __forceinline__ float2 rope_cs(int32_t pos, float theta) {
+    const float ang = __fmul_rn(static_cast<float>(pos), theta);
+    double s, c;
+    sincos(static_cast<double>(ang), &s, &c);
+    return make_float2(__double2float_rn(c), __double2float_rn(s));
+}
+
 template <int HALF>
 __device__ __forceinline__ void build_rope_table(float2 *tab, int32_t pos0, uint32_t n_tok,
-                                                 const float *__restrict__ theta) {
+                                                 const float *__restrict__ theta,
+                                                 const float2 *__restrict__ gtab) {
     for (uint32_t idx = threadIdx.x; idx < n_tok * HALF; idx += blockDim.x) {
         const uint32_t t = idx / HALF, i = idx % HALF;
-        const float pos = static_cast<float>(pos0 + static_cast<int32_t>(t));
-        float s, c;
-        sincosf(__fmul_rn(pos, theta[i]), &s, &c);
-        tab[t * HALF + tab_swz(i)] = make_float2(c, s);
+        tab[t * HALF + tab_swz(i)] =
+            gtab ? gtab[static_cast<size_t>(pos0) * HALF + idx]
+                 : rope_cs(pos0 + static_cast<int32_t>(t), theta[i]);
     }
+}
+
+// Context table: cs[pos][i] for pos in [0, n_pos).
+__global__ void rope_table_kernel(float2 *__restrict__ cs, uint32_t n_pos, uint32_t half,
+                                  const __grid_constant__ Theta th) {
+    const size_t n = static_cast<size_t>(n_pos) * half;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < n;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x)
+        cs[idx] = rope_cs(static_cast<int32_t>(idx / half), th.v[idx % half]);
 }
 
 // f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves.
@@ -320,12 +339,22 @@ __device__ __forceinline__ void rope_row_q8(uint8_t *row, const float2 *tr, uint
     __syncwarp();
 }
 
+// 16-byte vector copies by the whole CTA. copy16 reads through the read-only
+// global path (__ldg), so its source must be global memory; copy16_from_smem
+// is the shared-memory-source form.
 __device__ __forceinline__ void copy16(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
                                        uint64_t nbytes) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
     const uint64_t n = nbytes / 16;
     for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = __ldg(s + w);
+}
+__device__ __forceinline__ void copy16_from_smem(const uint8_t *src, uint8_t *__restrict__ dst,
+                                                 uint64_t nbytes) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    const uint64_t n = nbytes / 16;
+    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = s[w];
 }
 
 constexpr int kAsmThreads = 512;
@@ -334,12 +363,17 @@ constexpr int kQ8ChunkTok = 16;
 // S10-S13: CTA = one job x a range of layers. K re-roped from the pool's
 // unrotated copy at the job's window base; V copied.
 template <int D, bool Q8>
-__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(
-    const Job *__restrict__ jobs, const uint8_t *__restrict__ pool, uint64_t slot_bytes,
-    uint8_t *__restrict__ win_k, uint8_t *__restrict__ win_v, const __grid_constant__ Theta th,
-    const __grid_constant__ AssembleGeom g, uint32_t layers_per_cta, int32_t synth_pos0,
-    uint32_t synth_ntok) {
-    const float *theta = th.v;
+__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_constant__ AsmLaunch a,
+                                                               uint32_t layers_per_cta) {
+    const AssembleGeom &g = a.g;
+    const Job *__restrict__ jobs = a.jobs;
+    const uint8_t *__restrict__ pool = a.pool;
+    const uint64_t slot_bytes = a.slot_bytes;
+    uint8_t *__restrict__ win_k = a.win_k;
+    uint8_t *__restrict__ win_v = a.win_v;
+    const float *theta = a.theta.v;
+    const int32_t synth_pos0 = a.synth_pos0;
+    const uint32_t synth_ntok = a.synth_ntok;
     constexpr int HALF = D / 2;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     float2 *tab = reinterpret_cast<float2 *>(smem_raw);
@@ -352,7 +386,7 @@ __global__ void __launch_bounds__(kAsmThreads) assemble_kernel(
         job.pos0 = synth_pos0 + static_cast<int32_t>(blockIdx.x * g.block_tokens);
         job.n_tok = min(g.block_tokens, synth_ntok - blockIdx.x * g.block_tokens);
     }
-    build_rope_table<HALF>(tab, job.pos0, job.n_tok, theta);
+    build_rope_table<HALF>(tab, job.pos0, job.n_tok, theta, a.gtab);
     __syncthreads();
     const uint32_t l0 = blockIdx.y * layers_per_cta;
     const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
@@ -379,7 +413,7 @@ __global__ void __launch_bounds__(kAsmThreads) assemble_kernel(
                                    tab + (t0 + tt) * HALF, lane, g.fwht_n, g.fwht_scale);
                 }
                 __syncthreads();
-                copy16(stage, dk + t0 * g.k_row, nt * g.k_row);
+                copy16_from_smem(stage, dk + t0 * g.k_row, nt * g.k_row);
                 __syncthreads();
             }
         }
@@ -451,21 +485,26 @@ __global__ void copy_ops_kernel(const CopyOp *__restrict__ ops, int n) {
     for (uint64_t j = threadIdx.x; j < op.nbytes; j += blockDim.x) op.dst[j] = op.src[j];
 }
 
+// Layers per CTA: up to 8 (one RoPE table serves them all), fewer when the
+// launch has few jobs so the grid still covers every SM several times.
+uint32_t layers_per_cta(uint32_t n_jobs, uint32_t n_layer) {
+    const uint64_t units = static_cast<uint64_t>(n_jobs) * n_layer;
+    uint64_t lpc = units / (148ull * 8);
+    lpc = lpc < 1 ? 1 : (lpc > 8 ? 8 : lpc);
+    return static_cast<uint32_t>(lpc < n_layer ? lpc : n_layer);
+}
+
 template <int D, bool Q8>
-cudaError_t launch_assemble_t(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
-                              uint64_t slot_bytes, uint8_t *win_k, uint8_t *win_v,
-                              const Theta &theta, const AssembleGeom &g, cudaStream_t st,
-                              int32_t synth_pos0, uint32_t synth_ntok) {
-    const uint32_t lpc = g.n_layer < 8 ? g.n_layer : 8;
-    const dim3 grid(n_jobs, (g.n_layer + lpc - 1) / lpc);
-    size_t smem = static_cast<size_t>(g.block_tokens) * (D / 2) * sizeof(float2);
-    if (Q8) smem += static_cast<size_t>(kQ8ChunkTok) * g.k_row;
+cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
+    const uint32_t lpc = layers_per_cta(n_jobs, a.g.n_layer);
+    const dim3 grid(n_jobs, (a.g.n_layer + lpc - 1) / lpc);
+    size_t smem = static_cast<size_t>(a.g.block_tokens) * (D / 2) * sizeof(float2);
+    if (Q8) smem += static_cast<size_t>(kQ8ChunkTok) * a.g.k_row;
     auto kfn = assemble_kernel<D, Q8>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kfn<<<grid, kAsmThreads, smem, st>>>(jobs, pool, slot_bytes, win_k, win_v, theta, g, lpc,
-                                         synth_pos0, synth_ntok);
+    kfn<<<grid, kAsmThreads, smem, st>>>(a, lpc);
     return cudaGetLastError();
 }
 
@@ -532,25 +571,25 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
     return cudaGetLastError();
 }
 
-cudaError_t launch_assemble(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
-                            uint64_t pool_slot_bytes, uint8_t *win_k, uint8_t *win_v,
-                            const Theta &theta, const AssembleGeom &g, cudaStream_t st,
-                            int32_t synth_pos0, uint32_t synth_ntok) {
+cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
     if (n_jobs == 0) return cudaSuccess;
-    const bool q8 = g.k_type == KVMRET_TYPE_Q8_0;
-    switch (g.d_head) {
-    case 64:
-        return q8 ? launch_assemble_t<64, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
-                  : launch_assemble_t<64, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
-    case 128:
-        return q8 ? launch_assemble_t<128, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
-                  : launch_assemble_t<128, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
-    case 256:
-        return q8 ? launch_assemble_t<256, true>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok)
-                  : launch_assemble_t<256, false>(jobs, n_jobs, pool, pool_slot_bytes, win_k, win_v, theta, g, st, synth_pos0, synth_ntok);
-    default:
-        return cudaErrorInvalidValue;
+    const bool q8 = a.g.k_type == KVMRET_TYPE_Q8_0;
+    switch (a.g.d_head) {
+    case 64: return q8 ? launch_assemble_t<64, true>(a, n_jobs, st)
+                       : launch_assemble_t<64, false>(a, n_jobs, st);
+    case 128: return q8 ? launch_assemble_t<128, true>(a, n_jobs, st)
+                        : launch_assemble_t<128, false>(a, n_jobs, st);
+    case 256: return q8 ? launch_assemble_t<256, true>(a, n_jobs, st)
+                        : launch_assemble_t<256, false>(a, n_jobs, st);
+    default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_rope_table(float2 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
+                              cudaStream_t st) {
+    if (n_pos == 0) return cudaSuccess;
+    rope_table_kernel<<<1184, 256, 0, st>>>(cs, n_pos, half, th);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {

@@ -64,13 +64,29 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st);
 
-// S10-S13: window assembly from the HBM pool. With jobs == nullptr the jobs
-// are synthesised: job i covers tokens [i*T, min((i+1)*T, synth_ntok)) of a
-// contiguous run, pool slot i -> window slot i, positions from synth_pos0.
-cudaError_t launch_assemble(const Job *jobs, uint32_t n_jobs, const uint8_t *pool,
-                            uint64_t pool_slot_bytes, uint8_t *win_k, uint8_t *win_v,
-                            const Theta &theta, const AssembleGeom &g, cudaStream_t st,
-                            int32_t synth_pos0 = 0, uint32_t synth_ntok = 0);
+// S10-S13: window assembly from the HBM pool. One launch rebuilds n_jobs
+// window slots on every layer. With jobs == nullptr the jobs are synthesised:
+// job i covers tokens [i*T, min((i+1)*T, synth_ntok)) of a contiguous run,
+// pool slot i -> window slot i, positions from synth_pos0. gtab (may be null:
+// evaluate on the fly) is the context's cos/sin table [position][n_rot/2],
+// covering every window position.
+struct AsmLaunch {
+    const Job *jobs;
+    const uint8_t *pool;
+    uint64_t slot_bytes;
+    uint8_t *win_k;
+    uint8_t *win_v;
+    const float2 *gtab;
+    int32_t synth_pos0;
+    uint32_t synth_ntok;
+    Theta theta;
+    AssembleGeom g;
+};
+cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st);
+
+// cos/sin table of positions [0, n_pos) for the window (see AsmLaunch::gtab).
+cudaError_t launch_rope_table(float2 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
+                              cudaStream_t st);
 
 // S2 + S14: summaries of the appended tokens and the repository rows.
 struct AppendArgs {

@@ -70,6 +70,21 @@ class StepStats(ctypes.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class Prof(ctypes.Structure):
+    _fields_ = [
+        ("launches", ctypes.c_uint64), ("n_score", ctypes.c_uint32),
+        ("n_asm_moved", ctypes.c_uint32), ("n_asm_new", ctypes.c_uint32),
+        ("n_h2d", ctypes.c_uint32), ("dropped", ctypes.c_uint32),
+        ("score_ms", ctypes.c_double), ("asm_moved_ms", ctypes.c_double),
+        ("asm_new_ms", ctypes.c_double), ("h2d_ms", ctypes.c_double),
+        ("score_bytes", ctypes.c_uint64), ("asm_moved_bytes", ctypes.c_uint64),
+        ("asm_new_bytes", ctypes.c_uint64), ("h2d_bytes", ctypes.c_uint64),
+    ]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 _P = ctypes.c_void_p
 _U32 = ctypes.c_uint32
 _I32 = ctypes.c_int32
@@ -103,7 +118,9 @@ SIGNATURES = {
     "kvmret_query_set": (ctypes.c_int, [_P, _PF, _PU32]),
     "kvmret_query_get": (ctypes.c_int, [_P, _PF, _PU32]),
     "kvmret_score": (ctypes.c_int, [_P, _PD]),
-    "kvmret_score_layers": (ctypes.c_int, [_P]),
+    "kvmret_score_layers": (ctypes.c_int, [_P, _P, _P]),
+    "kvmret_prof_enable": (ctypes.c_int, [_P, ctypes.c_int]),
+    "kvmret_prof_read": (ctypes.c_int, [_P, ctypes.POINTER(Prof)]),
     "kvmret_contrib_dev": (_P, [_P]),
     "kvmret_layer_active_dev": (_P, [_P]),
     "kvmret_contrib_stride": (_U32, [_P]),
@@ -273,6 +290,28 @@ class Retriever:
         n = _U32(0)
         _check(lib.kvmret_select(self.h, mp, len(m), ids.ctypes.data_as(_PU32), ctypes.byref(n)))
         return ids[: n.value].copy()
+
+    def score_layers(self, contrib_out=None, active_out=None):
+        """Per-(layer, block) terms into torch CUDA buffers (or the internal one)."""
+        _check(lib.kvmret_score_layers(self.h, None if contrib_out is None else
+                                       contrib_out.data_ptr(),
+                                       None if active_out is None else active_out.data_ptr()))
+
+    @property
+    def contrib_stride(self) -> int:
+        return int(lib.kvmret_contrib_stride(self.h))
+
+    def score_reduce(self, contrib_all, active_all, n_layer_all: int):
+        _check(lib.kvmret_score_reduce(self.h, contrib_all.data_ptr(), active_all.data_ptr(),
+                                       n_layer_all, self.contrib_stride))
+
+    def prof_enable(self, on=True):
+        _check(lib.kvmret_prof_enable(self.h, int(on)))
+
+    def prof_read(self) -> dict:
+        p = Prof()
+        _check(lib.kvmret_prof_read(self.h, ctypes.byref(p)))
+        return p.as_dict()
 
     def preview(self, mandatory=()):
         m, mp = _u32(list(mandatory))

@@ -1,0 +1,77 @@
+"""Shared helpers of the GPU parity tests."""
+import numpy as np
+
+import kvmret
+import pyoracle as po
+
+
+def config_for(w, **kw):
+    c = dict(n_layer=w.n_layer, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head,
+             block_tokens=w.block_tokens, max_blocks=w.n_blocks, budget_blocks=w.budget_blocks,
+             reserve_blocks=w.reserve_blocks, sink_blocks=w.sink_blocks, k_type=w.k_type,
+             v_type=w.v_type, n_rot=w.d_head, freq_base=w.freq_base)
+    c.update(kw)
+    return kvmret.default_config(**c)
+
+
+def f16_ulp_diff(a_bits, b_bits):
+    """Distance in f16 ulps between two arrays of f16 bit patterns."""
+    a = np.asarray(a_bits, np.uint16).astype(np.int32)
+    b = np.asarray(b_bits, np.uint16).astype(np.int32)
+    oa = np.where(a & 0x8000, 0x8000 - a, a)
+    ob = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(oa - ob)
+
+
+def q8_blocks_diff(a, b):
+    """(max |qs| LSB difference, max scale ulp difference) between q8_0 byte arrays."""
+    a = np.asarray(a, np.uint8).reshape(-1, 34)
+    b = np.asarray(b, np.uint8).reshape(-1, 34)
+    da = a[:, :2].copy().view(np.uint16).reshape(-1)
+    db = b[:, :2].copy().view(np.uint16).reshape(-1)
+    qa = a[:, 2:].view(np.int8).astype(np.int32)
+    qb = b[:, 2:].view(np.int8).astype(np.int32)
+    return int(np.abs(qa - qb).max(initial=0)), int(f16_ulp_diff(da, db).max(initial=0))
+
+
+def history_units(hist):
+    """K/V of a NumpyHistory as [N][L][T][E] f16 (block, layer) units."""
+    w = hist.w
+    L, N, T, E = w.n_layer, w.n_blocks, w.block_tokens, w.E
+    k = hist.k.reshape(L, N, T, E).transpose(1, 0, 2, 3)
+    v = hist.v.reshape(L, N, T, E).transpose(1, 0, 2, 3)
+    return k, v
+
+
+def append_history(r, hist, cuts, k_rows_fn=None, v_rows_fn=None):
+    """Append the history to a Retriever in chunks ending at token offsets `cuts`."""
+    import torch
+    w = hist.w
+    L, n, E = w.n_layer, w.n_tokens, w.E
+    k = hist.k.reshape(L, n, E)
+    v = hist.v.reshape(L, n, E)
+    t0 = 0
+    for t1 in list(cuts) + [n]:
+        if t1 <= t0:
+            continue
+        kc = torch.from_numpy(np.ascontiguousarray(k[:, t0:t1])).cuda()
+        if v_rows_fn is None:
+            vr = torch.from_numpy(np.ascontiguousarray(v[:, t0:t1])).cuda()
+        else:
+            vr = torch.from_numpy(np.ascontiguousarray(v_rows_fn(v[:, t0:t1]))).cuda()
+        kr = None
+        if k_rows_fn is not None:
+            kr = torch.from_numpy(np.ascontiguousarray(k_rows_fn(k[:, t0:t1]))).cuda()
+        r.append(kc, vr, k_rows=kr, pos0=t0)
+        t0 = t1
+    r.sync()
+
+
+def oracle_scores(hist, q_sum, q_count, n_blocks=None):
+    w = hist.w
+    k, _ = history_units(hist)
+    N = w.n_blocks if n_blocks is None else n_blocks
+    mean = po.mean_k(k[:N].reshape(N * w.n_layer, w.block_tokens, w.E)).reshape(
+        N, w.n_layer, w.E)
+    has = np.ones(N, np.uint8)
+    return po.score(mean, has, q_sum, q_count, w.n_head, w.n_head_kv, w.d_head), mean

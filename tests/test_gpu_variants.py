@@ -1,0 +1,166 @@
+"""GPU parity beyond config 1: q8_0 K / q4_0 V windows (dequant -> RoPE ->
+FWHT -> requant within 1 LSB), other head geometries (d_head 64 / 256, no
+GQA, odd group sizes), layers without a query, ties under both tie rules,
+mandatory pinning, the stateless RoPE entry points and batched copies."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import kvmret
+import pyoracle as po
+from kvm_helpers import (append_history, config_for, f16_ulp_diff, history_units,
+                         oracle_scores, q8_blocks_diff)
+from kvmret import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _quant_rows(fn, row_bytes):
+    def f(x):  # x [L][n][E] f16 -> [L][n][row_bytes] u8
+        L, n, E = x.shape
+        return fn(x.astype(np.float32)).reshape(L, n, row_bytes)
+    return f
+
+
+def test_q8_k_q4_v_window():
+    w = synth.scaled(synth.CONFIGS[3], n_layer=2, n_blocks=48, budget_blocks=12,
+                     reserve_blocks=4, n_planted=4, n_head=16)
+    hist = synth.NumpyHistory(w)
+    r = kvmret.Retriever(config_for(w))
+    kq = _quant_rows(po.quant_q8_0, 1088)
+    vq = _quant_rows(po.quant_q4_0, 576)
+    append_history(r, hist, cuts=[130, 3000], k_rows_fn=kq, v_rows_fn=vq)
+    L, n, E = w.n_layer, w.n_tokens, w.E
+    k_q8 = kq(hist.k.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * 1088)
+    v_q4 = vq(hist.v.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * 576)
+    q = hist.queries(3)
+    worst_q, worst_d = 0, 0
+    for s in range(3):
+        r.query_reset()
+        r.query_add(torch.from_numpy(q[s].reshape(L, 1, -1)).cuda())
+        got = r.score()
+        want, _ = oracle_scores(hist, q[s].reshape(L, -1).astype(np.float32),
+                                np.ones(L, np.uint32))
+        assert np.array_equal(got, want)  # summaries come from the f16 capture (F5)
+        ids = r.select()
+        assert list(ids) == list(po.pick_topk(want, w.budget_blocks, w.sink_blocks))
+        r.apply(ids)
+        lay_ids, bases = r.window_layout()
+        for l in range(L):
+            wk = r.window_read(l, False, 0, len(lay_ids)).reshape(len(lay_ids), -1)
+            wv = r.window_read(l, True, 0, len(lay_ids)).reshape(len(lay_ids), -1)
+            for i, (b, base) in enumerate(zip(lay_ids, bases)):
+                want_k = po.rope_block_q8_0(k_q8[l, b], w.block_tokens, w.n_head_kv, w.d_head,
+                                            int(base), w.freq_base, fwht_n=128)
+                dq, dd = q8_blocks_diff(wk[i], want_k)
+                worst_q, worst_d = max(worst_q, dq), max(worst_d, dd)
+                assert np.array_equal(wv[i], v_q4[l, b])
+    assert worst_q <= 1 and worst_d <= 1
+    r.close()
+
+
+@pytest.mark.parametrize("hq,hkv,d,t", [(8, 8, 64, 64), (32, 4, 256, 32), (12, 4, 128, 128),
+                                        (16, 2, 128, 16)])
+def test_geometries(hq, hkv, d, t):
+    w = synth.Workload("geo", n_layer=3, n_head=hq, n_head_kv=hkv, d_head=d, block_tokens=t,
+                       n_blocks=70, budget_blocks=9, sink_blocks=2, reserve_blocks=3,
+                       n_planted=3, seed=11)
+    hist = synth.NumpyHistory(w)
+    r = kvmret.Retriever(config_for(w))
+    append_history(r, hist, cuts=[t // 2, 5 * t + 3])
+    L = w.n_layer
+    q = hist.queries(2)
+    store = po.Store(t)
+    store.append(w.n_tokens)
+    for s in range(2):
+        # layer 1 carries no query rows this step: it must be skipped (q_count == 0)
+        q_sum = q[s].reshape(L, -1).astype(np.float32)
+        q_count = np.array([1, 0, 2], np.uint32)
+        q_sum[2] *= 2
+        r.query_set(q_sum, q_count)
+        got = r.score()
+        want, _ = oracle_scores(hist, q_sum, q_count)
+        assert np.array_equal(got, want)
+        ids = r.select(mandatory=[5, 60])
+        assert list(ids) == list(po.pick_topk(want, w.budget_blocks, 2, 0, [5, 60]))
+        r.apply(ids)
+        si, so, rm, c = store.set_selection(ids)
+        assert np.array_equal(r.last_plan().remaps, rm)
+    k, v = history_units(hist)
+    lay_ids, bases = r.window_layout()
+    for l in range(L):
+        wk = r.window_read(l, False, 0, len(lay_ids)).view(np.uint16).reshape(
+            len(lay_ids), t, hkv, d)
+        for i, (b, base) in enumerate(zip(lay_ids, bases)):
+            want = po.rope_block_f16(k[b, l].view(np.uint16).reshape(t, hkv, d), int(base),
+                                     w.freq_base)
+            assert f16_ulp_diff(wk[i], want).max() <= 2
+    r.close()
+
+
+@pytest.mark.parametrize("tie_higher", [1, 0])
+def test_ties_follow_tie_rule(tie_higher):
+    w = synth.Workload("ties", n_layer=2, n_head=8, n_head_kv=8, d_head=128, block_tokens=32,
+                       n_blocks=40, budget_blocks=10, sink_blocks=1, reserve_blocks=0,
+                       n_planted=0, seed=21)
+    hist = synth.NumpyHistory(w)
+    # blocks 10..29 are copies of block 9: twenty exactly tied scores
+    T = w.block_tokens
+    for b in range(10, 30):
+        hist.k[:, b * T:(b + 1) * T] = hist.k[:, 9 * T:10 * T]
+    # make block 9's content the best match so the tie straddles the cut
+    hist.k[:, 9 * T:30 * T] += hist.q0.astype(np.float16).reshape(
+        w.n_layer, 1, w.n_head_kv, w.d_head)
+    r = kvmret.Retriever(config_for(w, tie_higher_id=tie_higher))
+    append_history(r, hist, cuts=[])
+    r.query_reset()
+    r.query_add(torch.from_numpy(hist.q0.reshape(w.n_layer, 1, -1)).cuda())
+    got = r.score()
+    assert len(set(got[9:30].tolist())) == 1
+    ids = r.select()
+    want = po.pick_topk(got, w.budget_blocks, 1, 0, (), bool(tie_higher))
+    assert list(ids) == list(want)
+    tied = [i for i in ids if 9 <= i < 30]
+    assert tied == (list(range(30 - len(tied), 30)) if tie_higher else list(range(9, 9 + len(tied))))
+    r.close()
+
+
+def test_stateless_rope_f16_and_q8():
+    rng = np.random.default_rng(3)
+    n, hkv, d = 300, 8, 128
+    x = rng.standard_normal((n, hkv, d)).astype(np.float16)
+    k = torch.from_numpy(x).cuda()
+    out = torch.empty_like(k)
+    kvmret.rope_f16(k, out, 12345, hkv, d, 1e6)
+    torch.cuda.synchronize()
+    want = po.rope_block_f16(x.view(np.uint16), 12345, 1e6)
+    assert f16_ulp_diff(out.cpu().numpy().view(np.uint16), want).max() <= 2
+    q8 = po.quant_q8_0(x.astype(np.float32)).reshape(n, -1)
+    kq = torch.from_numpy(q8).cuda()
+    oq = torch.empty_like(kq)
+    kvmret.rope_q8_0(kq, oq, n, 777, hkv, d, 1e6, fwht_n=128)
+    torch.cuda.synchronize()
+    want8 = po.rope_block_q8_0(q8, n, hkv, d, 777, 1e6, fwht_n=128)
+    dq, dd = q8_blocks_diff(oq.cpu().numpy(), want8)
+    assert dq <= 1 and dd <= 1
+
+
+def test_d2d_batched():
+    w = synth.CONFIGS[1]
+    r = kvmret.Retriever(config_for(synth.scaled(w, n_blocks=8, budget_blocks=4)))
+    src = torch.arange(4096, dtype=torch.uint8, device="cuda").repeat(8)
+    dst = torch.zeros_like(src)
+    sizes = [16, 4096, 333, 1000]
+    offs = [0, 100, 5000, 20000]
+    S = (ctypes.c_void_p * 4)(*[src.data_ptr() + o for o in offs])
+    D = (ctypes.c_void_p * 4)(*[dst.data_ptr() + o + 7 for o in offs])
+    N = (ctypes.c_uint64 * 4)(*sizes)
+    torch.cuda.synchronize()
+    assert kvmret.lib.kvmret_d2d_batched(r.h, S, D, N, 4) == 0
+    r.sync()
+    s, d_ = src.cpu().numpy(), dst.cpu().numpy()
+    for o, z in zip(offs, sizes):
+        assert np.array_equal(d_[o + 7:o + 7 + z], s[o:o + z])
+    r.close()
