@@ -406,7 +406,10 @@ def run_ours(args, w):
                 "assemble_new": {"ms": round(prof["asm_new_ms"] / max(1, prof["n_asm_new"]), 4),
                                  "launches": prof["n_asm_new"]},
                 "h2d_stage_in": {"ms": round(h2d_ms, 4), "GB/s": round(h2d_gbs, 2),
-                                 "frac_link": round(h2d_gbs / link, 4) if link else None}},
+                                 "frac_link": round(h2d_gbs / link, 4) if link else None},
+                "host_handover": {"ms": round(prof["gap_ms"] / max(1, prof["n_gap"]), 4),
+                                  "what": "device idle from the end of select to the apply "
+                                          "enqueue (host plan + Python)"}},
             "step_roofline": {"t_roof_us": round(t_roof * 1e6, 1),
                               "t_meas_us": round(ms_step * 1e3, 1),
                               "frac": round(t_roof * 1e3 / ms_step, 4),
@@ -447,7 +450,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--pool-cache", action="store_true")
+    ap.add_argument("--no-pool-cache", dest="pool_cache", action="store_false",
+                    help="free a block's HBM pool slot as soon as it leaves the window (the "
+                         "reference's residency model); by default evicted blocks stay cached "
+                         "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (dev only)")
     ap.add_argument("--budget", type=int, default=0, help="override budget blocks (dev only)")

@@ -227,6 +227,8 @@ typedef struct kvmret_prof {
     double asm_new_ms;        /* window assembly of freshly staged blocks */
     double h2d_ms;            /* host -> HBM pool copies (copy stream) */
     uint64_t score_bytes, asm_moved_bytes, asm_new_bytes, h2d_bytes;
+    uint32_t n_gap;           /* select -> apply hand-overs timed */
+    double gap_ms;            /* device idle while the host plans (select end -> apply enqueue) */
 } kvmret_prof;
 /* Reset the counters and turn event timing on (1) or off (0). */
 int kvmret_prof_enable(kvmret_ctx *ctx, int on);

@@ -115,6 +115,7 @@ struct kvmret_ctx {
     size_t ev_next = 0;
     std::vector<Region> pending;
     kvmret_prof prof{};
+    int gap_open = -1;  // region opened at the end of select, closed by apply
 
     explicit kvmret_ctx(const kvmret::TableConfig &tc) : table(tc) {}
 };
@@ -176,7 +177,7 @@ int ensure_qprep(kvmret_ctx *c) {
     return KVMRET_OK;
 }
 
-enum { PR_SCORE = 0, PR_ASM_MOVED, PR_ASM_NEW, PR_H2D };
+enum { PR_SCORE = 0, PR_ASM_MOVED, PR_ASM_NEW, PR_H2D, PR_GAP };
 constexpr size_t kEventPool = 8192;
 
 // Begin a timed region on stream `s`; returns the region index or -1.
@@ -352,6 +353,8 @@ int32_t take_slot(kvmret_ctx *c, const std::vector<uint8_t> &in_new) {
 
 int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_stats *stats) {
     const uint32_t nb = c->table.n_blocks();
+    const int gap = c->gap_open;
+    c->gap_open = -1;
     {  // bound the window before touching any state
         std::vector<uint8_t> seen(nb, 0);
         uint32_t uniq = 0;
@@ -424,6 +427,7 @@ int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_s
     // soon as its own copies have landed.
     std::vector<Job> all(moved);
     all.insert(all.end(), added.begin(), added.end());
+    prof_end(c, c->st, gap);
     if (!all.empty())
         CK(cudaMemcpyAsync(c->jobs_dev, all.data(), all.size() * sizeof(Job),
                            cudaMemcpyHostToDevice, c->st));
@@ -504,6 +508,7 @@ int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
                                  c->sel_dev, c->st));
         c->prof.launches += 1;
         CK(cudaMemcpyAsync(c->pin_sel, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
+        c->gap_open = prof_begin(c, c->st, PR_GAP, 0);
         CK(cudaStreamSynchronize(c->st));
         sel = c->pin_sel;
     }
@@ -807,11 +812,13 @@ int kvmret_prof_read(kvmret_ctx *c, kvmret_prof *out) {
     CK(cudaStreamSynchronize(c->st_copy));
     for (const auto &r : c->pending) {
         float ms = 0.0f;
+        if (r.kind == PR_GAP && cudaEventQuery(r.b) != cudaSuccess) continue;  // never closed
         CK(cudaEventElapsedTime(&ms, r.a, r.b));
         switch (r.kind) {
         case PR_SCORE: c->prof.score_ms += ms; ++c->prof.n_score; c->prof.score_bytes += r.bytes; break;
         case PR_ASM_MOVED: c->prof.asm_moved_ms += ms; ++c->prof.n_asm_moved; c->prof.asm_moved_bytes += r.bytes; break;
         case PR_ASM_NEW: c->prof.asm_new_ms += ms; ++c->prof.n_asm_new; c->prof.asm_new_bytes += r.bytes; break;
+        case PR_GAP: c->prof.gap_ms += ms; ++c->prof.n_gap; break;
         default: c->prof.h2d_ms += ms; ++c->prof.n_h2d; c->prof.h2d_bytes += r.bytes; break;
         }
     }

@@ -11,7 +11,7 @@
 namespace kvmret {
 namespace {
 
-constexpr int kTile = 128;  // blocks per scoring CTA (32 lanes x float4)
+constexpr int kTile = 64;  // blocks per scoring CTA (32 lanes x float2)
 
 __device__ __forceinline__ float h2f(uint16_t h) {
     return __half2float(__ushort_as_half(h));
@@ -48,40 +48,39 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
                              float *__restrict__ qv, float *__restrict__ nq,
                              uint8_t *__restrict__ active, uint32_t n_head, uint32_t n_head_kv,
                              uint32_t d_head) {
-    const uint32_t l = blockIdx.x;
+    extern __shared__ float sv[];
+    const uint32_t l = blockIdx.x, h = blockIdx.y;
     const uint32_t g = n_head_kv == 0 ? 1 : n_head / n_head_kv;
     const uint32_t cnt = q_count[l];
     const float invq = __fdiv_rn(1.0f, static_cast<float>(cnt * (g > 1u ? g : 1u)));
-    const uint32_t E = n_head_kv * d_head;
     const float *qs = q_sum + static_cast<size_t>(l) * n_head * d_head;
-    float *out = qv + static_cast<size_t>(l) * E;
-    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
-        const uint32_t h = e / d_head, d = e % d_head;
+    for (uint32_t d = threadIdx.x; d < d_head; d += blockDim.x) {
         float s = 0.0f;
         for (uint32_t gi = 0; gi < g; ++gi) {
             const uint32_t qh = h * g + gi;
             if (qh >= n_head) break;
             s = __fadd_rn(s, qs[static_cast<size_t>(qh) * d_head + d]);
         }
-        out[e] = __fmul_rn(s, invq);
+        const float v = __fmul_rn(s, invq);
+        sv[d] = v;
+        qv[(static_cast<size_t>(l) * n_head_kv + h) * d_head + d] = v;
     }
     __syncthreads();
-    for (uint32_t h = threadIdx.x; h < n_head_kv; h += blockDim.x) {
+    if (threadIdx.x == 0) {
         float a = 0.0f;
-        for (uint32_t d = 0; d < d_head; ++d) {
-            const float v = out[h * d_head + d];
-            a = __fadd_rn(a, __fmul_rn(v, v));
-        }
+        for (uint32_t d = 0; d < d_head; ++d) a = __fadd_rn(a, __fmul_rn(sv[d], sv[d]));
         nq[static_cast<size_t>(l) * n_head_kv + h] = a;
+        if (h == 0) active[l] = cnt != 0;
     }
-    if (threadIdx.x == 0) active[l] = cnt != 0;
 }
 
 // ---------------------------------------------------------------------------
-// S3: one CTA = one layer x 128 blocks. Summaries are block-minor
-// [L][Hkv][D][ncap], so lane j of a warp walks blocks 4j..4j+3 with float4
-// loads: each d step of a warp reads 512 contiguous bytes, and each block's
+// S3: one CTA = one layer x kTile (64) blocks. Summaries are block-minor
+// [L][Hkv][D][ncap], so lane j of a warp walks blocks 2j, 2j+1 with float2
+// loads: each d step of a warp reads 256 contiguous bytes, and each block's
 // dot / norm is accumulated strictly in d order (score_retrieval :4179-4185).
+// Warp w handles heads w, w + 8, ...; the per-layer head sum is taken in head
+// order from shared memory.
 template <int D>
 __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ summ,
                                                     const float *__restrict__ qv,
@@ -103,38 +102,31 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
         sq[i] = qv[static_cast<size_t>(l) * n_head_kv * D + i];
     __syncthreads();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
-    const size_t dstep = ncap / 4;  // float4 stride between d rows
+    const size_t dstep = ncap / 2;  // float2 stride between d rows
     for (uint32_t h = warp; h < n_head_kv; h += nwarp) {
-        const float4 *p = reinterpret_cast<const float4 *>(
+        const float2 *p = reinterpret_cast<const float2 *>(
                               summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
                           lane;
         const float *qh = sq + h * D;
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-        float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
+        float d0 = 0.f, d1 = 0.f, n0 = 0.f, n1 = 0.f;
 #pragma unroll 2
-        for (int dd = 0; dd < D; dd += 8) {
-            float4 k[8];
+        for (int dd = 0; dd < D; dd += 16) {
+            float2 k[16];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) k[u] = __ldg(p + static_cast<size_t>(dd + u) * dstep);
+            for (int u = 0; u < 16; ++u) k[u] = __ldg(p + static_cast<size_t>(dd + u) * dstep);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 16; ++u) {
                 const float q = qh[dd + u];
                 d0 = __fadd_rn(d0, __fmul_rn(q, k[u].x));
                 d1 = __fadd_rn(d1, __fmul_rn(q, k[u].y));
-                d2 = __fadd_rn(d2, __fmul_rn(q, k[u].z));
-                d3 = __fadd_rn(d3, __fmul_rn(q, k[u].w));
                 n0 = __fadd_rn(n0, __fmul_rn(k[u].x, k[u].x));
                 n1 = __fadd_rn(n1, __fmul_rn(k[u].y, k[u].y));
-                n2 = __fadd_rn(n2, __fmul_rn(k[u].z, k[u].z));
-                n3 = __fadd_rn(n3, __fmul_rn(k[u].w, k[u].w));
             }
         }
         const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
-        float *cb = cosb + h * kTile + lane * 4;
+        float *cb = cosb + h * kTile + lane * 2;
         cb[0] = __fdiv_rn(d0, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n0)), 1e-6f));
         cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
-        cb[2] = __fdiv_rn(d2, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n2)), 1e-6f));
-        cb[3] = __fdiv_rn(d3, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n3)), 1e-6f));
     }
     __syncthreads();
     // layer += cos (double, head order); term = layer / n_head_kv (:4186-4188).
@@ -171,38 +163,28 @@ __global__ void reduce_kernel(const double *__restrict__ contrib, const uint8_t 
 // S6: exact rank selection. Block b (not kept) is chosen iff fewer than
 // `need` other candidates beat it under (score desc, id by tie rule) — the
 // same set nth_element returns for a strict total order
-// (kvmem_store.cpp:600-616). Scores are streamed through shared memory.
-constexpr int kSelChunk = 2048;
+// (kvmem_store.cpp:600-616). One warp per block: the lanes split the
+// candidates and the counts are summed with a warp reduction.
 __global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ scores,
                                                      const uint8_t *__restrict__ kept,
                                                      uint32_t n, uint32_t need, int tie_high,
                                                      uint8_t *__restrict__ sel) {
-    __shared__ double ss[kSelChunk];
-    __shared__ uint8_t sk[kSelChunk];
-    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool valid = b < n;
-    const bool cand = valid && !kept[b];
-    const double sb = valid ? scores[b] : 0.0;
-    uint32_t rank = 0;
-    for (uint32_t c0 = 0; c0 < n; c0 += kSelChunk) {
-        const uint32_t m = min(static_cast<uint32_t>(kSelChunk), n - c0);
-        for (uint32_t i = threadIdx.x; i < m; i += blockDim.x) {
-            ss[i] = scores[c0 + i];
-            sk[i] = kept[c0 + i];
-        }
-        __syncthreads();
-        if (cand) {
-            for (uint32_t i = 0; i < m; ++i) {
-                if (sk[i]) continue;
-                const double sc = ss[i];
-                const uint32_t c = c0 + i;
-                const bool better = sc > sb || (sc == sb && (tie_high ? c > b : c < b));
-                rank += better ? 1u : 0u;
-            }
-        }
-        __syncthreads();
+    const uint32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (b >= n) return;
+    if (kept[b]) {
+        if (lane == 0) sel[b] = 1;
+        return;
     }
-    if (valid) sel[b] = kept[b] ? 1 : (rank < need ? 1 : 0);
+    const double sb = scores[b];
+    uint32_t rank = 0;
+    for (uint32_t c = lane; c < n; c += 32) {
+        if (kept[c]) continue;
+        const double sc = scores[c];
+        rank += (sc > sb || (sc == sb && (tie_high ? c > b : c < b))) ? 1u : 0u;
+    }
+    rank = __reduce_add_sync(0xffffffffu, rank);
+    if (lane == 0) sel[b] = rank < need ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -525,8 +507,8 @@ cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint
 cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
                          uint8_t *active, uint32_t n_layer, uint32_t n_head, uint32_t n_head_kv,
                          uint32_t d_head, cudaStream_t st) {
-    qprep_kernel<<<n_layer, 256, 0, st>>>(q_sum, q_count, qv, nq, active, n_head, n_head_kv,
-                                          d_head);
+    qprep_kernel<<<dim3(n_layer, n_head_kv), d_head, d_head * sizeof(float), st>>>(
+        q_sum, q_count, qv, nq, active, n_head, n_head_kv, d_head);
     return cudaGetLastError();
 }
 
@@ -558,16 +540,16 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    reduce_kernel<<<(n_blocks + 255) / 256, 256, 0, st>>>(contrib, active, n_layer, stride,
-                                                          has_block, n_blocks, scores);
+    reduce_kernel<<<(n_blocks + 63) / 64, 64, 0, st>>>(contrib, active, n_layer, stride,
+                                                       has_block, n_blocks, scores);
     return cudaGetLastError();
 }
 
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    select_kernel<<<(n_blocks + 255) / 256, 256, 0, st>>>(scores, kept, n_blocks, need,
-                                                          tie_higher_id, sel);
+    select_kernel<<<(n_blocks + 7) / 8, 256, 0, st>>>(scores, kept, n_blocks, need,
+                                                      tie_higher_id, sel);
     return cudaGetLastError();
 }
 

@@ -79,6 +79,7 @@ class Prof(ctypes.Structure):
         ("asm_new_ms", ctypes.c_double), ("h2d_ms", ctypes.c_double),
         ("score_bytes", ctypes.c_uint64), ("asm_moved_bytes", ctypes.c_uint64),
         ("asm_new_bytes", ctypes.c_uint64), ("h2d_bytes", ctypes.c_uint64),
+        ("n_gap", ctypes.c_uint32), ("gap_ms", ctypes.c_double),
     ]
 
     def as_dict(self):
