@@ -254,6 +254,33 @@ int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
 int kvmret_d2d_batched(kvmret_ctx *ctx, const void *const *src, void *const *dst,
                        const uint64_t *nbytes, int n);
 
+/* ---- allocation-free scoring. No counterpart in the reference: this entry
+ *      point exists for callers that cannot allocate device memory (code that
+ *      runs inside an allocator hook, under a memory manager that owns the whole
+ *      device, or on a serving path where cudaMalloc is forbidden). ----
+ *
+ * Same scores as kvmret_score, from caller-owned inputs and output:
+ *   summ_dev      [n_layer][n_head_kv][d_head][summ_stride] f32 block summaries
+ *                 (the context's own layout), 16-byte aligned, summ_stride a
+ *                 multiple of 64 and >= n_blocks
+ *   q_sum_dev     [n_layer][n_head * d_head] f32 query sums
+ *   q_count_dev   [n_layer] u32 query row counts
+ *   has_block_dev [n_blocks] u8, nonzero where the block holds data
+ *   scores_dev    [n_blocks] f64 output
+ * It calls no allocator. Its scratch is one file-scope device array of
+ * KVMRET_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * exit; a call needing more (n_layer * summ_stride * 8 bytes plus the query
+ * scratch) is rejected with KVMRET_ERR_ARG. The first call on each device,
+ * with that device current, looks up the array's device address: make it
+ * before any stream capture. Calls share the array (each call writes every
+ * scratch byte it reads, so nothing needs clearing); calls that overlap on the
+ * GPU race. `stream` is a cudaStream_t (NULL = legacy default stream). */
+#define KVMRET_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int kvmret_score_noalloc(const float *summ_dev, uint32_t summ_stride, const float *q_sum_dev,
+                         const uint32_t *q_count_dev, const uint8_t *has_block_dev,
+                         uint32_t n_blocks, uint32_t n_layer, uint32_t n_head,
+                         uint32_t n_head_kv, uint32_t d_head, double *scores_dev, void *stream);
+
 /* ---- host block table: the selection / plan logic alone, no GPU needed
  *      (KvMemStore, kvmem/include/kvmem/kvmem_store.hpp:329-491). ---- */
 int kvmret_table_create(const kvmret_config *cfg, kvmret_table **out);

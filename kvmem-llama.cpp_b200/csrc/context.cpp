@@ -67,6 +67,10 @@ uint32_t hadamard_nrot_k(uint32_t d_head) {
 
 }  // namespace
 
+namespace kvmret {
+int set_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace kvmret
+
 struct kvmret_ctx {
     kvmret_config cfg{};
     // geometry

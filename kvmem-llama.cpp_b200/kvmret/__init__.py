@@ -143,6 +143,8 @@ SIGNATURES = {
                                         ctypes.c_float, _U32, _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
                                           ctypes.POINTER(_U64), ctypes.c_int]),
+    "kvmret_score_noalloc": (ctypes.c_int, [_P, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _U32,
+                                            _P, _P]),
     "kvmret_table_create": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.POINTER(_P)]),
     "kvmret_table_destroy": (None, [_P]),
     "kvmret_table_append": (ctypes.c_int, [_P, _U32]),
