@@ -190,6 +190,65 @@ ORC_API void orc_score(const float *mean, const uint8_t *has, const float *q_sum
     }
 }
 
+// S3 split for layer sharding: the per-(layer, block) term layer / n_head_kv of
+// score_retrieval (:4186-4188) for a contiguous range of layers, and the
+// layer-ordered reduction acc / nlay (:4189-4193). Composing the two over all
+// layers in order is orc_score.
+// terms: [n_layer][n_blocks] f64 (0 for inactive layers); active: [n_layer].
+ORC_API void orc_score_terms(const float *mean, const float *q_sum, const uint32_t *q_count,
+                             uint32_t n_blocks, uint32_t n_layer, uint32_t n_head,
+                             uint32_t n_head_kv, uint32_t d_head, double *terms,
+                             uint8_t *active) {
+    const uint32_t n_embd_k = n_head_kv * d_head;
+    const uint32_t g = n_head_kv == 0 ? 1 : n_head / n_head_kv;
+    std::vector<float> qh(d_head);
+    for (uint32_t il = 0; il < n_layer; ++il) {
+        active[il] = q_count[il] != 0;
+        for (uint32_t b = 0; b < n_blocks; ++b) {
+            double &out = terms[static_cast<size_t>(il) * n_blocks + b];
+            out = 0.0;
+            if (q_count[il] == 0) continue;
+            const float *mk = mean + (static_cast<size_t>(b) * n_layer + il) * n_embd_k;
+            double layer = 0;
+            const float invq = 1.0f / static_cast<float>(q_count[il] * std::max(1u, g));
+            for (uint32_t h = 0; h < n_head_kv; ++h) {
+                std::fill(qh.begin(), qh.end(), 0.0f);
+                for (uint32_t gi = 0; gi < g; ++gi) {
+                    const uint32_t qh_i = h * g + gi;
+                    if (qh_i >= n_head) break;
+                    const float *q = q_sum + static_cast<size_t>(il) * n_head * d_head +
+                                     static_cast<size_t>(qh_i) * d_head;
+                    for (uint32_t d = 0; d < d_head; ++d) qh[d] += q[d];
+                }
+                const float *kh = mk + static_cast<size_t>(h) * d_head;
+                float dot = 0, nq = 0, nk = 0;
+                for (uint32_t d = 0; d < d_head; ++d) {
+                    const float qv = qh[d] * invq;
+                    dot += qv * kh[d];
+                    nq += qv * qv;
+                    nk += kh[d] * kh[d];
+                }
+                layer += dot / (std::sqrt(nq) * std::sqrt(nk) + 1e-6f);
+            }
+            out = layer / static_cast<double>(std::max(1u, n_head_kv));
+        }
+    }
+}
+
+ORC_API void orc_score_reduce(const double *terms, const uint8_t *active, const uint8_t *has,
+                              uint32_t n_blocks, uint32_t n_layer, double *scores) {
+    for (uint32_t b = 0; b < n_blocks; ++b) {
+        double acc = 0;
+        uint32_t nlay = 0;
+        for (uint32_t il = 0; il < n_layer; ++il) {
+            if (!active[il]) continue;
+            acc += terms[static_cast<size_t>(il) * n_blocks + b];
+            nlay++;
+        }
+        scores[b] = (has[b] && nlay) ? acc / nlay : 0;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // S6 — top-k block selection, TopK policy.
 // kvmem/src/host/kvmem_store.cpp:357-359 (pick_topk_blocks -> constrain_media,

@@ -40,6 +40,8 @@ def _load_orc():
         "orc_mean_k_f16_batch": (None, [_PU16, ctypes.c_uint64, _U32, _U32, _PF]),
         "orc_query_add": (None, [_PF, _PU32, _PF, _U32, _U32]),
         "orc_score": (None, [_PF, _PU8, _PF, _PU32, _U32, _U32, _U32, _U32, _U32, _PD]),
+        "orc_score_terms": (None, [_PF, _PF, _PU32, _U32, _U32, _U32, _U32, _U32, _PD, _PU8]),
+        "orc_score_reduce": (None, [_PD, _PU8, _PU8, _U32, _U32, _PD]),
         "orc_pick_topk": (_U32, [_PD, _U32, _U32, _U32, _U32, _PU32, _U32, ctypes.c_int, _PU32]),
         "orc_store_create": (_P, [_U32, ctypes.c_int]),
         "orc_store_free": (None, [_P]),
@@ -134,6 +136,30 @@ def score(mean: np.ndarray, has: np.ndarray, q_sum: np.ndarray, q_count: np.ndar
     out = np.zeros(N, np.float64)
     orc.orc_score(_ptr(mean, _PF), _ptr(has, _PU8), _ptr(q_sum, _PF), _ptr(q_count, _PU32), N, L,
                   n_head, n_head_kv, d_head, _ptr(out, _PD))
+    return out
+
+
+def score_terms(mean, q_sum, q_count, n_head, n_head_kv, d_head):
+    """Per-(layer, block) terms of the layers in `mean` [N][L][E] -> ([L][N] f64, [L] u8)."""
+    mean = np.ascontiguousarray(mean, np.float32)
+    N, L, _ = mean.shape
+    q_sum = np.ascontiguousarray(q_sum, np.float32)
+    q_count = np.ascontiguousarray(q_count, np.uint32)
+    terms = np.zeros((L, N), np.float64)
+    active = np.zeros(L, np.uint8)
+    orc.orc_score_terms(_ptr(mean, _PF), _ptr(q_sum, _PF), _ptr(q_count, _PU32), N, L, n_head,
+                        n_head_kv, d_head, _ptr(terms, _PD), _ptr(active, _PU8))
+    return terms, active
+
+
+def score_reduce(terms, active, has):
+    terms = np.ascontiguousarray(terms, np.float64)
+    L, N = terms.shape
+    active = np.ascontiguousarray(active, np.uint8)
+    has = np.ascontiguousarray(has, np.uint8)
+    out = np.zeros(N, np.float64)
+    orc.orc_score_reduce(_ptr(terms, _PD), _ptr(active, _PU8), _ptr(has, _PU8), N, L,
+                         _ptr(out, _PD))
     return out
 
 

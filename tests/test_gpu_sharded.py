@@ -1,0 +1,107 @@
+"""Layer-sharded retrieval on 2 GPUs: each rank's context owns half of the
+layers; the per-(layer, block) score terms and per-layer query flags are
+all-gathered over NCCL and reduced in global layer order, so every rank
+selects the same blocks as the single-context oracle, bit for bit, and
+assembles its own layers' windows. Skipped with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, out):
+    import sys
+    from datetime import timedelta
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, os.path.join(root, "kvmem-llama.cpp_b200"), os.path.join(root, "oracle")):
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+    import kvmret
+    from kvm_helpers import config_for
+    from kvmret import synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    w = synth.scaled(synth.CONFIGS[1], n_layer=4, n_blocks=96, budget_blocks=12, n_planted=4)
+    hist = synth.NumpyHistory(w)
+    Ll = w.n_layer // world
+    sl = slice(rank * Ll, (rank + 1) * Ll)
+    r = kvmret.Retriever(config_for(w, n_layer=Ll, device=rank))
+    n = w.n_tokens
+    k = np.ascontiguousarray(hist.k.reshape(w.n_layer, n, w.E)[sl])
+    v = np.ascontiguousarray(hist.v.reshape(w.n_layer, n, w.E)[sl])
+    r.append(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    stride = r.contrib_stride
+    c_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
+    a_loc = torch.zeros(Ll, dtype=torch.uint8, device="cuda")
+    c_all = torch.zeros(w.n_layer * stride, dtype=torch.float64, device="cuda")
+    a_all = torch.zeros(w.n_layer, dtype=torch.uint8, device="cuda")
+    q = hist.queries(3)
+    res = []
+    for s in range(3):
+        r.query_reset()
+        r.query_add(torch.from_numpy(np.ascontiguousarray(
+            q[s].reshape(w.n_layer, 1, -1)[sl])).cuda())
+        r.score_layers(c_loc, a_loc)
+        r.sync()
+        dist.all_gather_into_tensor(c_all, c_loc)
+        dist.all_gather_into_tensor(a_all, a_loc)
+        torch.cuda.synchronize()
+        r.score_reduce(c_all, a_all, w.n_layer)
+        ids = r.select()
+        r.apply(ids)
+        lay, bases = r.window_layout()
+        res.append((ids.tobytes(), lay.tobytes(), bases.tobytes()))
+    out[rank] = res
+    r.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_layer_sharded_selection_matches_oracle():
+    import pyoracle as po
+    from kvm_helpers import oracle_scores
+    from kvmret import synth
+    w = synth.scaled(synth.CONFIGS[1], n_layer=4, n_blocks=96, budget_blocks=12, n_planted=4)
+    hist = synth.NumpyHistory(w)
+    q = hist.queries(3)
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    store = po.Store(w.block_tokens)
+    store.append(w.n_tokens)
+    for s in range(3):
+        want, _ = oracle_scores(hist, q[s].reshape(w.n_layer, -1).astype(np.float32),
+                                np.ones(w.n_layer, np.uint32))
+        want_ids = po.pick_topk(want, w.budget_blocks, w.sink_blocks)
+        _, _, rm, _ = store.set_selection(want_ids)
+        for rank in range(2):
+            ids, lay, bases = (np.frombuffer(b, t) for b, t in
+                               zip(out[rank][s], (np.uint32, np.uint32, np.int32)))
+            assert np.array_equal(ids, want_ids)
+            assert np.array_equal(lay, rm[:, 0].astype(np.uint32))
+            assert np.array_equal(bases, rm[:, 3])
