@@ -11,8 +11,9 @@ its window position, V copied).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
 
 N > 1 runs under torchrun, one rank per GPU, each owning n_layer / N layers;
-the only cross-rank traffic is an NCCL all-gather of the per-(layer, block)
-score terms (f64) and per-layer query flags, 1 MiB total at 64 layers.
+the only cross-rank traffic is one NCCL all-gather per step of the
+per-(layer, block) score terms (f64) with each layer's query flag packed in
+its row, ~1 MiB in total at 64 layers.
 """
 from __future__ import annotations
 
@@ -262,28 +263,24 @@ def run_ours(args, w):
 
     stride = r.contrib_stride
     contrib_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
-    active_loc = torch.zeros(Ll, dtype=torch.uint8, device="cuda")
     contrib_all = contrib_loc if world == 1 else torch.zeros(w.n_layer * stride,
                                                               dtype=torch.float64, device="cuda")
-    active_all = active_loc if world == 1 else torch.zeros(w.n_layer, dtype=torch.uint8,
-                                                           device="cuda")
     ext = torch.cuda.ExternalStream(r.stream_ptr)
     cur = torch.cuda.current_stream()
 
     def step(q_dev):
         r.query_reset()
         r.query_add(q_dev)
-        r.score_layers(contrib_loc, active_loc)
+        r.score_layers(contrib_loc)
         if world > 1:
             ev = torch.cuda.Event()
             ev.record(ext)
             cur.wait_event(ev)
             dist.all_gather_into_tensor(contrib_all, contrib_loc)
-            dist.all_gather_into_tensor(active_all, active_loc)
             ev2 = torch.cuda.Event()
             ev2.record(cur)
             ext.wait_event(ev2)
-        r.score_reduce(contrib_all, active_all, w.n_layer)
+        r.score_reduce(contrib_all, w.n_layer)
         ids = r.select()
         return r.apply(ids)
 

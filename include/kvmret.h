@@ -150,20 +150,18 @@ int kvmret_query_get(kvmret_ctx *ctx, float *q_sum_host, uint32_t *q_count_host)
  *      src/adapter/llama-memory-kvmem.cpp:4149-4196 ---- */
 /* Score every block; if scores_host != NULL copy the n_blocks f64 scores out. */
 int kvmret_score(kvmret_ctx *ctx, double *scores_host);
-/* Layer-sharded form: per-(layer, block) terms layer_sum / n_head_kv (f64) of
- * this context's layers, without the reduction. contrib_out_dev (NULL = the
- * context's own buffer) receives [n_layer][contrib_stride] f64 and
- * active_out_dev (may be NULL) the per-layer "has query" flags [n_layer] u8. */
-int kvmret_score_layers(kvmret_ctx *ctx, double *contrib_out_dev, uint8_t *active_out_dev);
-/* Device pointer to the contribution buffer [n_layer][contrib_stride] f64 and
- * the per-layer "has query" flags [n_layer] u8. */
+/* Layer-sharded form: the per-(layer, block) terms layer_sum / n_head_kv (f64)
+ * of this context's layers, without the reduction, as exchange rows of
+ * kvmret_contrib_stride(ctx) doubles: row l holds the terms of blocks
+ * [0, n_blocks) and, in its LAST column, 1.0 if layer l has query rows else
+ * 0.0 — so one all-gather of [n_layer][stride] per shard carries everything.
+ * contrib_out_dev == NULL writes the context's own buffer (kvmret_contrib_dev). */
+int kvmret_score_layers(kvmret_ctx *ctx, double *contrib_out_dev);
 const double *kvmret_contrib_dev(kvmret_ctx *ctx);
-const uint8_t *kvmret_layer_active_dev(kvmret_ctx *ctx);
 uint32_t kvmret_contrib_stride(kvmret_ctx *ctx);
-/* Reduce gathered contributions of ALL layers of the model, in layer order:
- *   contrib_all_dev [n_layer_all][stride] f64, active_all_dev [n_layer_all] u8. */
-int kvmret_score_reduce(kvmret_ctx *ctx, const double *contrib_all_dev,
-                        const uint8_t *active_all_dev, uint32_t n_layer_all, uint32_t stride);
+/* Reduce the gathered rows of ALL layers of the model, in layer order
+ * (contrib_all_dev [n_layer_all][stride], shards concatenated by layer). */
+int kvmret_score_reduce(kvmret_ctx *ctx, const double *contrib_all_dev, uint32_t n_layer_all);
 
 /* ---- selection (S5/S6): llama_memory_kvmem::preview_retrieval
  *      (src/adapter/llama-memory-kvmem.cpp:4327-4347) -> KvMemRuntime::

@@ -75,6 +75,7 @@ struct kvmret_ctx {
     kvmret_config cfg{};
     // geometry
     uint32_t E = 0, qdim = 0, ncap = 0, win_slots = 0, pool_slots = 0;
+    uint32_t cstride = 0;  // exchange row: ncap score terms, padding, query flag last
     uint64_t k_row = 0, v_row = 0, unit_k = 0, unit = 0, slot_bytes = 0;
     uint64_t win_k_layer = 0, win_v_layer = 0;
     kvmret::AssembleGeom geom{};
@@ -89,7 +90,7 @@ struct kvmret_ctx {
     kvmret::CopyOp *ops_dev = nullptr;
     float2 *rope_tab = nullptr;  // cos/sin of every window position [pos][n_rot/2]
     // host
-    uint8_t *repo_host = nullptr, *repo_dev = nullptr, *pin_sel = nullptr;
+    uint8_t *repo_host = nullptr, *repo_dev = nullptr, *pin_sel = nullptr, *pin_kept = nullptr;
     std::vector<uint32_t> q_count;
     bool q_dirty = true;
     kvmret::BlockTable table;
@@ -170,17 +171,6 @@ int validate(const kvmret_config &c) {
     return KVMRET_OK;
 }
 
-int ensure_qprep(kvmret_ctx *c) {
-    if (!c->q_dirty) return KVMRET_OK;
-    CK(cudaMemcpyAsync(c->q_count_dev, c->q_count.data(), c->q_count.size() * sizeof(uint32_t),
-                       cudaMemcpyHostToDevice, c->st));
-    CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, c->cfg.n_layer,
-                            c->cfg.n_head, c->cfg.n_head_kv, c->cfg.d_head, c->st));
-    c->prof.launches += 1;
-    c->q_dirty = false;
-    return KVMRET_OK;
-}
-
 enum { PR_SCORE = 0, PR_ASM_MOVED, PR_ASM_NEW, PR_H2D, PR_GAP };
 constexpr size_t kEventPool = 8192;
 
@@ -213,6 +203,7 @@ void free_all(kvmret_ctx *c) {
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
     if (c->pin_sel) cudaFreeHost(c->pin_sel);
+    if (c->pin_kept) cudaFreeHost(c->pin_kept);
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     for (cudaEvent_t e : c->ev_grp)
         if (e) cudaEventDestroy(e);
@@ -247,6 +238,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     c->E = k.n_head_kv * k.d_head;
     c->qdim = k.n_head * k.d_head;
     c->ncap = static_cast<uint32_t>(align_up(k.max_blocks, 128));
+    c->cstride = c->ncap + 64;
     c->k_row = kvmret_row_bytes(k.k_type, c->E);
     c->v_row = kvmret_row_bytes(k.v_type, c->E);
     c->unit_k = align_up(static_cast<uint64_t>(k.block_tokens) * c->k_row, 256);
@@ -292,7 +284,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     TRY(dmalloc(&c->active, L));
     TRY(dmalloc(&c->kept_dev, c->ncap));
     TRY(dmalloc(&c->sel_dev, c->ncap));
-    TRY(dmalloc(&c->contrib, L * c->ncap * sizeof(double)));
+    TRY(dmalloc(&c->contrib, L * c->cstride * sizeof(double)));
     TRY(dmalloc(&c->scores, c->ncap * sizeof(double)));
     TRY(dmalloc(&c->pool, static_cast<size_t>(c->pool_slots) * c->slot_bytes));
     TRY(dmalloc(&c->win_k, L * c->win_k_layer));
@@ -306,7 +298,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     CK(cudaMemsetAsync(c->tail_sum, 0, 2 * L * c->E * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->q_sum, 0, L * c->qdim * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->has_block, 0, c->ncap, c->st));
-    CK(cudaMemsetAsync(c->contrib, 0, L * c->ncap * sizeof(double), c->st));
+    CK(cudaMemsetAsync(c->contrib, 0, L * c->cstride * sizeof(double), c->st));
     CK(cudaMemsetAsync(c->scores, 0, c->ncap * sizeof(double), c->st));
 
     const size_t repo_bytes = static_cast<size_t>(k.max_blocks) * c->slot_bytes;
@@ -321,6 +313,11 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     e = cudaHostAlloc(reinterpret_cast<void **>(&c->pin_sel), c->ncap, cudaHostAllocDefault);
     if (e != cudaSuccess) {
         c->pin_sel = nullptr;
+        return fail(KVMRET_ERR_NOMEM, "pinned staging: %s", cudaGetErrorString(e));
+    }
+    e = cudaHostAlloc(reinterpret_cast<void **>(&c->pin_kept), c->ncap, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        c->pin_kept = nullptr;
         return fail(KVMRET_ERR_NOMEM, "pinned staging: %s", cudaGetErrorString(e));
     }
     c->q_count.assign(L, 0);
@@ -507,7 +504,9 @@ int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
     const uint32_t n = c->table.n_blocks();
     const uint8_t *sel = kept.data();
     if (need > 0) {
-        CK(cudaMemcpyAsync(c->kept_dev, kept.data(), n, cudaMemcpyHostToDevice, c->st));
+        // select() ends in a stream synchronisation, so the staging buffer is free here
+        std::copy(kept.begin(), kept.begin() + n, c->pin_kept);
+        CK(cudaMemcpyAsync(c->kept_dev, c->pin_kept, n, cudaMemcpyHostToDevice, c->st));
         CK(kvmret::launch_select(c->scores, c->kept_dev, n, need, c->cfg.tie_higher_id,
                                  c->sel_dev, c->st));
         c->prof.launches += 1;
@@ -526,25 +525,35 @@ int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
     return KVMRET_OK;
 }
 
-int score_layers_impl(kvmret_ctx *c, double *contrib_out, uint8_t *active_out) {
-    TRY(ensure_qprep(c));
+// Per-(layer, block) terms into rows of cstride doubles (out == nullptr: the
+// context's buffer); the layer's query flag goes to the last column of its row.
+int score_layers_impl(kvmret_ctx *c, double *out) {
+    double *dst = out ? out : c->contrib;
+    if (out) c->q_dirty = true;  // the flag column of a caller buffer is written by qprep
+    if (c->q_dirty) {
+        CK(cudaMemcpyAsync(c->q_count_dev, c->q_count.data(), c->q_count.size() * sizeof(uint32_t),
+                           cudaMemcpyHostToDevice, c->st));
+        CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active,
+                                c->cfg.n_layer, c->cfg.n_head, c->cfg.n_head_kv, c->cfg.d_head,
+                                c->st, dst, c->cstride));
+        c->prof.launches += 1;
+        c->q_dirty = false;
+    }
     const uint32_t n = c->table.n_blocks();
     const uint64_t bytes = static_cast<uint64_t>(c->cfg.n_layer) * c->E *
-                           ((n + 127) / 128 * 128) * sizeof(float);
+                           ((n + 63) / 64 * 64) * sizeof(float);
     const int pr = prof_begin(c, c->st, PR_SCORE, bytes);
-    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, contrib_out ? contrib_out : c->contrib,
-                            c->cfg.n_layer, c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st));
+    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, dst, c->cfg.n_layer,
+                            c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st, c->cstride));
     prof_end(c, c->st, pr);
     c->prof.launches += n ? 1 : 0;
-    if (active_out)
-        CK(cudaMemcpyAsync(active_out, c->active, c->cfg.n_layer, cudaMemcpyDeviceToDevice, c->st));
     return KVMRET_OK;
 }
 
 int score_impl(kvmret_ctx *c, double *scores_host) {
-    TRY(score_layers_impl(c, nullptr, nullptr));
+    TRY(score_layers_impl(c, nullptr));
     const uint32_t n = c->table.n_blocks();
-    CK(kvmret::launch_reduce(c->contrib, c->active, c->cfg.n_layer, c->ncap, c->has_block, n,
+    CK(kvmret::launch_reduce(c->contrib, c->active, c->cfg.n_layer, c->cstride, c->has_block, n,
                              c->scores, c->st));
     c->prof.launches += n ? 1 : 0;
     if (scores_host) {
@@ -774,21 +783,18 @@ int kvmret_score(kvmret_ctx *c, double *scores_host) {
     return score_impl(c, scores_host);
 }
 
-int kvmret_score_layers(kvmret_ctx *c, double *contrib_out, uint8_t *active_out) {
+int kvmret_score_layers(kvmret_ctx *c, double *contrib_out) {
     NEED_CTX(c);
-    return score_layers_impl(c, contrib_out, active_out);
+    return score_layers_impl(c, contrib_out);
 }
 
 const double *kvmret_contrib_dev(kvmret_ctx *c) { return c ? c->contrib : nullptr; }
-const uint8_t *kvmret_layer_active_dev(kvmret_ctx *c) { return c ? c->active : nullptr; }
-uint32_t kvmret_contrib_stride(kvmret_ctx *c) { return c ? c->ncap : 0; }
+uint32_t kvmret_contrib_stride(kvmret_ctx *c) { return c ? c->cstride : 0; }
 
-int kvmret_score_reduce(kvmret_ctx *c, const double *contrib_all, const uint8_t *active_all,
-                        uint32_t n_layer_all, uint32_t stride) {
+int kvmret_score_reduce(kvmret_ctx *c, const double *contrib_all, uint32_t n_layer_all) {
     NEED_CTX(c);
-    if (!contrib_all || !active_all || stride < c->table.n_blocks())
-        return fail(KVMRET_ERR_ARG, "bad contribution buffer");
-    CK(kvmret::launch_reduce(contrib_all, active_all, n_layer_all, stride, c->has_block,
+    if (!contrib_all || n_layer_all == 0) return fail(KVMRET_ERR_ARG, "bad contribution buffer");
+    CK(kvmret::launch_reduce(contrib_all, nullptr, n_layer_all, c->cstride, c->has_block,
                              c->table.n_blocks(), c->scores, c->st));
     c->prof.launches += 1;
     return KVMRET_OK;

@@ -47,7 +47,7 @@ __global__ void query_add_kernel(float *__restrict__ q_sum, const T *__restrict_
 __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__restrict__ q_count,
                              float *__restrict__ qv, float *__restrict__ nq,
                              uint8_t *__restrict__ active, uint32_t n_head, uint32_t n_head_kv,
-                             uint32_t d_head) {
+                             uint32_t d_head, double *__restrict__ flag_col, uint32_t cstride) {
     extern __shared__ float sv[];
     const uint32_t l = blockIdx.x, h = blockIdx.y;
     const uint32_t g = n_head_kv == 0 ? 1 : n_head / n_head_kv;
@@ -70,7 +70,11 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
         float a = 0.0f;
         for (uint32_t d = 0; d < d_head; ++d) a = __fadd_rn(a, __fmul_rn(sv[d], sv[d]));
         nq[static_cast<size_t>(l) * n_head_kv + h] = a;
-        if (h == 0) active[l] = cnt != 0;
+        if (h == 0) {
+            active[l] = cnt != 0;
+            // packed exchange form: the layer's query flag in the last column of its row
+            if (flag_col) flag_col[static_cast<size_t>(l) * cstride + cstride - 1] = cnt ? 1.0 : 0.0;
+        }
     }
 }
 
@@ -87,11 +91,12 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                                                     const float *__restrict__ nq,
                                                     const uint8_t *__restrict__ active,
                                                     double *__restrict__ contrib,
-                                                    uint32_t n_head_kv, uint32_t ncap) {
+                                                    uint32_t n_head_kv, uint32_t ncap,
+                                                    uint32_t cstride) {
     extern __shared__ float smem[];
     const uint32_t l = blockIdx.y;
     const uint32_t b0 = blockIdx.x * kTile;
-    double *out = contrib + static_cast<size_t>(l) * ncap + b0;
+    double *out = contrib + static_cast<size_t>(l) * cstride + b0;
     if (!active[l]) {
         for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) out[t] = 0.0;
         return;
@@ -152,8 +157,9 @@ __global__ void reduce_kernel(const double *__restrict__ contrib, const uint8_t 
     double acc = 0.0;
     uint32_t nlay = 0;
     for (uint32_t l = 0; l < n_layer; ++l) {
-        if (!active[l]) continue;
-        acc = __dadd_rn(acc, contrib[static_cast<size_t>(l) * stride + b]);
+        const double *row = contrib + static_cast<size_t>(l) * stride;
+        if (active ? !active[l] : row[stride - 1] == 0.0) continue;
+        acc = __dadd_rn(acc, row[b]);
         ++nlay;
     }
     scores[b] = nlay ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
@@ -506,29 +512,33 @@ cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint
 
 cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
                          uint8_t *active, uint32_t n_layer, uint32_t n_head, uint32_t n_head_kv,
-                         uint32_t d_head, cudaStream_t st) {
+                         uint32_t d_head, cudaStream_t st, double *flag_col, uint32_t cstride) {
     qprep_kernel<<<dim3(n_layer, n_head_kv), d_head, d_head * sizeof(float), st>>>(
-        q_sum, q_count, qv, nq, active, n_head, n_head_kv, d_head);
+        q_sum, q_count, qv, nq, active, n_head, n_head_kv, d_head, flag_col, cstride);
     return cudaGetLastError();
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
-                         cudaStream_t st) {
+                         cudaStream_t st, uint32_t cstride) {
+    if (cstride == 0) cstride = ncap;
     const uint32_t tiles = (n_blocks + kTile - 1) / kTile;
     if (tiles == 0) return cudaSuccess;
     const dim3 grid(tiles, n_layer);
     const size_t smem = static_cast<size_t>(n_head_kv) * (d_head + kTile) * sizeof(float);
     switch (d_head) {
     case 64:
-        score_kernel<64><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        score_kernel<64><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
+                                                   cstride);
         break;
     case 128:
-        score_kernel<128><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        score_kernel<128><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
+                                                   cstride);
         break;
     case 256:
-        score_kernel<256><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap);
+        score_kernel<256><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
+                                                   cstride);
         break;
     default:
         return cudaErrorInvalidValue;

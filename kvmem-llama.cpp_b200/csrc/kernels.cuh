@@ -45,17 +45,22 @@ cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint
                              uint32_t n_rows, uint32_t qdim, cudaStream_t st);
 
 // S3 prologue: per (layer, kv head) the scaled group query and its squared norm.
+// With flag_col set, each layer's query flag (1.0 / 0.0) is also written to
+// flag_col[l * cstride + cstride - 1] (the packed exchange row).
 cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
                          uint8_t *active, uint32_t n_layer, uint32_t n_head,
-                         uint32_t n_head_kv, uint32_t d_head, cudaStream_t st);
+                         uint32_t n_head_kv, uint32_t d_head, cudaStream_t st,
+                         double *flag_col = nullptr, uint32_t cstride = 0);
 
-// S3: per (layer, block) term layer_sum / n_head_kv.
+// S3: per (layer, block) term layer_sum / n_head_kv into contrib rows of
+// cstride doubles (0 = ncap).
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap,
-                         uint32_t n_blocks, cudaStream_t st);
+                         uint32_t n_blocks, cudaStream_t st, uint32_t cstride = 0);
 
-// S3 epilogue: layer-ordered sum, / number of layers with a query.
+// S3 epilogue: layer-ordered sum, / number of layers with a query. With
+// active == nullptr the flags are read from each row's last column.
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st);

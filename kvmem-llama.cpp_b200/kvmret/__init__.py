@@ -119,13 +119,12 @@ SIGNATURES = {
     "kvmret_query_set": (ctypes.c_int, [_P, _PF, _PU32]),
     "kvmret_query_get": (ctypes.c_int, [_P, _PF, _PU32]),
     "kvmret_score": (ctypes.c_int, [_P, _PD]),
-    "kvmret_score_layers": (ctypes.c_int, [_P, _P, _P]),
+    "kvmret_score_layers": (ctypes.c_int, [_P, _P]),
     "kvmret_prof_enable": (ctypes.c_int, [_P, ctypes.c_int]),
     "kvmret_prof_read": (ctypes.c_int, [_P, ctypes.POINTER(Prof)]),
     "kvmret_contrib_dev": (_P, [_P]),
-    "kvmret_layer_active_dev": (_P, [_P]),
     "kvmret_contrib_stride": (_U32, [_P]),
-    "kvmret_score_reduce": (ctypes.c_int, [_P, _P, _P, _U32, _U32]),
+    "kvmret_score_reduce": (ctypes.c_int, [_P, _P, _U32]),
     "kvmret_select": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32]),
     "kvmret_preview": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32]),
     "kvmret_apply_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.POINTER(StepStats)]),
@@ -294,19 +293,18 @@ class Retriever:
         _check(lib.kvmret_select(self.h, mp, len(m), ids.ctypes.data_as(_PU32), ctypes.byref(n)))
         return ids[: n.value].copy()
 
-    def score_layers(self, contrib_out=None, active_out=None):
-        """Per-(layer, block) terms into torch CUDA buffers (or the internal one)."""
+    def score_layers(self, contrib_out=None):
+        """Exchange rows [n_layer][contrib_stride] f64 (terms + query flag in the last
+        column) into a torch CUDA buffer, or the context's own buffer."""
         _check(lib.kvmret_score_layers(self.h, None if contrib_out is None else
-                                       contrib_out.data_ptr(),
-                                       None if active_out is None else active_out.data_ptr()))
+                                       contrib_out.data_ptr()))
 
     @property
     def contrib_stride(self) -> int:
         return int(lib.kvmret_contrib_stride(self.h))
 
-    def score_reduce(self, contrib_all, active_all, n_layer_all: int):
-        _check(lib.kvmret_score_reduce(self.h, contrib_all.data_ptr(), active_all.data_ptr(),
-                                       n_layer_all, self.contrib_stride))
+    def score_reduce(self, contrib_all, n_layer_all: int):
+        _check(lib.kvmret_score_reduce(self.h, contrib_all.data_ptr(), n_layer_all))
 
     def prof_enable(self, on=True):
         _check(lib.kvmret_prof_enable(self.h, int(on)))

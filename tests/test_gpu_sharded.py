@@ -1,6 +1,6 @@
 """Layer-sharded retrieval on 2 GPUs: each rank's context owns half of the
-layers; the per-(layer, block) score terms and per-layer query flags are
-all-gathered over NCCL and reduced in global layer order, so every rank
+layers; the per-(layer, block) score terms, with each layer's query flag in
+the last column of its row, are all-gathered over NCCL and reduced in global layer order, so every rank
 selects the same blocks as the single-context oracle, bit for bit, and
 assembles its own layers' windows. Skipped with fewer than 2 GPUs.
 """
@@ -50,21 +50,18 @@ def _rank(rank, world, port, out):
     r.append(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
     stride = r.contrib_stride
     c_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
-    a_loc = torch.zeros(Ll, dtype=torch.uint8, device="cuda")
     c_all = torch.zeros(w.n_layer * stride, dtype=torch.float64, device="cuda")
-    a_all = torch.zeros(w.n_layer, dtype=torch.uint8, device="cuda")
     q = hist.queries(3)
     res = []
     for s in range(3):
         r.query_reset()
         r.query_add(torch.from_numpy(np.ascontiguousarray(
             q[s].reshape(w.n_layer, 1, -1)[sl])).cuda())
-        r.score_layers(c_loc, a_loc)
+        r.score_layers(c_loc)
         r.sync()
         dist.all_gather_into_tensor(c_all, c_loc)
-        dist.all_gather_into_tensor(a_all, a_loc)
         torch.cuda.synchronize()
-        r.score_reduce(c_all, a_all, w.n_layer)
+        r.score_reduce(c_all, w.n_layer)
         ids = r.select()
         r.apply(ids)
         lay, bases = r.window_layout()
