@@ -254,7 +254,13 @@ def run_ours(args, w):
     for t0 in range(0, w.n_tokens, chunk):
         m = min(chunk, w.n_tokens - t0)
         kc, vc = hist.chunk(t0, m)
-        r.append(kc, vc, pos0=t0)
+        if w.k_type == kvmret.TYPE_F16:
+            r.append(kc, vc, pos0=t0)
+        else:  # config 3: q8_0 K rows, q4_0 V rows, summaries from the f16 capture
+            kq = kvmret.quantize_f16(kc, w.k_type)
+            vq = kvmret.quantize_f16(vc, w.v_type)
+            r.append(kc, vq, k_rows=kq, pos0=t0)
+            del kq, vq
         r.sync()
         del kc, vc
     torch.cuda.synchronize()
@@ -268,10 +274,21 @@ def run_ours(args, w):
     ext = torch.cuda.ExternalStream(r.stream_ptr)
     cur = torch.cuda.current_stream()
 
+    marks = []  # (label, event) on the library stream, --timeline only
+
+    def mark(label):
+        if args.timeline:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(ext)
+            marks.append((label, e))
+
     def step(q_dev):
+        mark("start")
         r.query_reset()
         r.query_add(q_dev)
+        mark("query")
         r.score_layers(contrib_loc)
+        mark("score")
         if world > 1:
             ev = torch.cuda.Event()
             ev.record(ext)
@@ -280,9 +297,13 @@ def run_ours(args, w):
             ev2 = torch.cuda.Event()
             ev2.record(cur)
             ext.wait_event(ev2)
+        mark("exchange")
         r.score_reduce(contrib_all, w.n_layer)
         ids = r.select()
-        return r.apply(ids)
+        mark("select")
+        st = r.apply(ids)
+        mark("apply_enqueued")
+        return st
 
     def queries(n):
         out = []
@@ -312,6 +333,7 @@ def run_ours(args, w):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stats = []
+    marks.clear()
     e0.record(ext)
     for q in qs:
         stats.append(step(q))
@@ -321,6 +343,15 @@ def run_ours(args, w):
     barrier()
     prof = r.prof_read()
     r.prof_enable(False)
+    timeline = None
+    if args.timeline and marks:
+        acc, cnt = {}, {}
+        for (la, ea), (lb, eb) in zip(marks, marks[1:]):
+            key = f"{la}->{lb}"
+            acc[key] = acc.get(key, 0.0) + ea.elapsed_time(eb)
+            cnt[key] = cnt.get(key, 0) + 1
+        timeline = {k: round(acc[k] / cnt[k] * 1e3, 1) for k in acc}
+        marks.clear()
     ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -420,6 +451,7 @@ def run_ours(args, w):
                     "h2d_bytes_per_step": int(qs[0].numel() * 2 + h2d_step),
                     "d2h_bytes_per_step": int(w.n_blocks)},
             "gpu_launches": int(prof["launches"]),
+            "timeline_us": timeline,
             "clocks": clk,
             "setup_s": round(t_setup, 1),
         }
@@ -452,6 +484,8 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="record device events between the phases of each timed step (diagnostic)")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (dev only)")
     ap.add_argument("--budget", type=int, default=0, help="override budget blocks (dev only)")
     ap.add_argument("--reserve", type=int, default=-1, help="override reserve slots (dev only)")

@@ -246,6 +246,11 @@ int kvmret_rope_f16(const uint16_t *k_dev, uint16_t *out_dev, uint32_t n_tok, ui
 int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* f16 values -> q8_0 / q4_0 blocks (n_elems a multiple of 32): the quantisers
+ * of kvmem_stagein_quantize (src/adapter/llama-kvmem-stagein.cu:181-234,
+ * 616-642), used to build quantised cache rows and repository bytes. */
+int kvmret_quantize_f16(const uint16_t *src_dev, void *dst_dev, int32_t type, uint64_t n_elems,
+                        void *stream);
 /* Batched byte copies on the context stream, at most 8192 per call
  * (kvmem_d2d_batched, src/adapter/llama-kvmem-stagein.cu:1002-1035, which uses
  * its execution state's preallocated op buffer the same way). */

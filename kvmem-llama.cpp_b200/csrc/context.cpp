@@ -989,6 +989,18 @@ int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_k
     return KVMRET_OK;
 }
 
+int kvmret_quantize_f16(const uint16_t *src, void *dst, int32_t type, uint64_t n_elems,
+                        void *stream) {
+    if (!src || !dst) return fail(KVMRET_ERR_ARG, "null buffer");
+    if (type != KVMRET_TYPE_Q8_0 && type != KVMRET_TYPE_Q4_0)
+        return fail(KVMRET_ERR_ARG, "type must be q8_0 or q4_0");
+    if (n_elems % 32 || (reinterpret_cast<uintptr_t>(src) & 15))
+        return fail(KVMRET_ERR_ARG, "n_elems must be a multiple of 32 and src 16-byte aligned");
+    CK(kvmret::launch_quantize(src, static_cast<uint8_t *>(dst), n_elems / 32,
+                               type == KVMRET_TYPE_Q8_0, static_cast<cudaStream_t>(stream)));
+    return KVMRET_OK;
+}
+
 int kvmret_d2d_batched(kvmret_ctx *c, const void *const *src, void *const *dst,
                        const uint64_t *nbytes, int n) {
     NEED_CTX(c);

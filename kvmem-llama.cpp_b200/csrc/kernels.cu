@@ -460,6 +460,55 @@ __global__ void append_repo_kernel(AppendArgs a) {
     for (uint64_t w = lane; w < a.v_row / 16; w += 32) vd[w] = __ldg(vs + w);
 }
 
+// f16 rows -> q8_0 / q4_0 rows, one thread per 32-element block
+// (quant_q8_0 / quant_q4_0, llama-kvmem-stagein.cu:181-234).
+__global__ void quantize_kernel(const uint16_t *__restrict__ x, uint8_t *__restrict__ y,
+                                uint64_t n_blocks, int q8) {
+    const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+    if (i >= n_blocks) return;
+    float v[32];
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + i * 32);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 w = __ldg(src + c);
+        const uint16_t *h = reinterpret_cast<const uint16_t *>(&w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[c * 8 + e] = h2f(h[e]);
+    }
+    if (q8) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint8_t *b = y + i * 34;
+        *reinterpret_cast<uint16_t *>(b) = f2h(d);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            b[2 + j] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(v[j], id))));
+    } else {
+        float amax = 0.0f, vmax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (amax < fabsf(v[j])) {
+                amax = fabsf(v[j]);
+                vmax = v[j];
+            }
+        const float d = __fdiv_rn(vmax, -8.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint8_t *b = y + i * 18;
+        *reinterpret_cast<uint16_t *>(b) = f2h(d);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            int x0 = static_cast<int>(__fadd_rn(__fmul_rn(v[j], id), 8.5f));
+            int x1 = static_cast<int>(__fadd_rn(__fmul_rn(v[j + 16], id), 8.5f));
+            x0 = x0 > 15 ? 15 : x0;
+            x1 = x1 > 15 ? 15 : x1;
+            b[2 + j] = static_cast<uint8_t>((x0 & 15) | ((x1 & 15) << 4));
+        }
+    }
+}
+
 __global__ void copy_ops_kernel(const CopyOp *__restrict__ ops, int n) {
     const int i = blockIdx.x;
     if (i >= n) return;
@@ -602,6 +651,14 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {
     const uint32_t warps_per_cta = 8;
     append_repo_kernel<<<dim3((a.n_tok + warps_per_cta - 1) / warps_per_cta, a.n_layer),
                          warps_per_cta * 32, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bool q8,
+                            cudaStream_t st) {
+    if (n_blocks == 0) return cudaSuccess;
+    quantize_kernel<<<static_cast<unsigned>((n_blocks + 255) / 256), 256, 0, st>>>(x, y, n_blocks,
+                                                                                   q8 ? 1 : 0);
     return cudaGetLastError();
 }
 

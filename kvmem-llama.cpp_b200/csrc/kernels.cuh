@@ -108,6 +108,10 @@ struct AppendArgs {
 };
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t st);
 
+// f16 rows -> q8_0 (q8 = true) or q4_0 blocks of 32 elements.
+cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bool q8,
+                            cudaStream_t st);
+
 struct CopyOp {
     const uint8_t *src;
     uint8_t *dst;

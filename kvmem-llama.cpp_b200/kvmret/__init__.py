@@ -140,6 +140,7 @@ SIGNATURES = {
                                        ctypes.c_float, _P]),
     "kvmret_rope_q8_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
                                         ctypes.c_float, _U32, _P]),
+    "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
                                           ctypes.POINTER(_U64), ctypes.c_int]),
     "kvmret_score_noalloc": (ctypes.c_int, [_P, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _U32,
@@ -413,6 +414,17 @@ def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, str
     _torch_sync()
     _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
                                d_head, pos0, freq_base, freq_scale, stream or None))
+
+
+def quantize_f16(x, type_id, stream=0):
+    """f16 CUDA tensor (numel % 32 == 0) -> uint8 CUDA tensor of q8_0 / q4_0 blocks."""
+    import torch
+    n = x.numel()
+    per = 34 if type_id == TYPE_Q8_0 else 18
+    out = torch.empty(n // 32 * per, dtype=torch.uint8, device=x.device)
+    _torch_sync()
+    _check(lib.kvmret_quantize_f16(x.data_ptr(), out.data_ptr(), type_id, n, stream or None))
+    return out
 
 
 def rope_q8_0(k, out, n_tok, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, fwht_n=0,

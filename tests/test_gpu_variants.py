@@ -147,6 +147,17 @@ def test_stateless_rope_f16_and_q8():
     assert dq <= 1 and dd <= 1
 
 
+def test_gpu_quantiser_matches_oracle_bit_exact():
+    rng = np.random.default_rng(12)
+    x = (rng.standard_normal(32 * 1000) * 3).astype(np.float16)
+    x[:32] = 0  # an all-zero block (d = 0)
+    xd = torch.from_numpy(x).cuda()
+    q8 = kvmret.quantize_f16(xd, kvmret.TYPE_Q8_0).cpu().numpy()
+    q4 = kvmret.quantize_f16(xd, kvmret.TYPE_Q4_0).cpu().numpy()
+    assert np.array_equal(q8, po.quant_q8_0(x.astype(np.float32)))
+    assert np.array_equal(q4, po.quant_q4_0(x.astype(np.float32)))
+
+
 def test_d2d_batched():
     w = synth.CONFIGS[1]
     r = kvmret.Retriever(config_for(synth.scaled(w, n_blocks=8, budget_blocks=4)))
