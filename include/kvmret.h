@@ -82,11 +82,11 @@ typedef struct kvmret_step_stats {
     uint32_t n_stage_in;      /* plan.stage_in (newly in the working set) */
     uint32_t n_stage_out;     /* plan.stage_out */
     uint32_t n_skip;          /* plan remaps with skip set */
-    uint32_t n_h2d_blocks;    /* blocks copied host -> HBM pool this step */
+    uint32_t n_h2d_blocks;    /* blocks read from the host repository this step */
     uint32_t n_assembled;     /* window slots rewritten (new + moved) */
     uint32_t n_moved;         /* window slots rewritten from a resident block */
     uint32_t total_window_tokens;
-    uint64_t h2d_bytes;       /* host -> device bytes of the stage-in */
+    uint64_t h2d_bytes;       /* host -> device bytes of the stage-in (host link) */
     uint64_t assemble_bytes;  /* HBM bytes read + written by window assembly */
 } kvmret_step_stats;
 
@@ -186,6 +186,15 @@ int kvmret_preview(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandat
  *      stream reaches this point. ---- */
 int kvmret_apply_selection(kvmret_ctx *ctx, const uint32_t *ids, uint32_t n_ids,
                            kvmret_step_stats *stats);
+/* Asynchronous step: top-k over the current scores (after kvmret_score or
+ * kvmret_score_reduce), device plan and window assembly, all enqueued on the
+ * context stream with no host synchronisation; fresh blocks are read from the
+ * mapped pinned repository by the assembly itself. Up to 4 steps may be in
+ * flight; kvmret_step_collect returns the oldest one's selection and stats
+ * (waiting for its readback) and replays it in the host block table. */
+int kvmret_select_apply_async(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory);
+int kvmret_step_collect(kvmret_ctx *ctx, uint32_t *ids_out, uint32_t *n_out,
+                        kvmret_step_stats *stats);
 /* llama_kvmem_apply_retrieval (src/adapter/llama-memory-kvmem.cpp:4778-4782,
  * apply_retrieval :4419-4422): preview + apply. ids_out may be NULL. */
 int kvmret_apply_retrieval(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
@@ -218,15 +227,13 @@ int kvmret_window_read(kvmret_ctx *ctx, uint32_t layer, int is_v, uint32_t slot0
  *      the stream each kernel or copy runs on. ---- */
 typedef struct kvmret_prof {
     uint64_t launches;        /* kernels launched by the context since reset */
-    uint32_t n_score, n_asm_moved, n_asm_new, n_h2d;   /* timed regions */
+    uint32_t n_score, n_asm;  /* timed scoring / assembly launches */
     uint32_t dropped;         /* regions not timed (event pool exhausted) */
     double score_ms;          /* scoring kernel */
-    double asm_moved_ms;      /* window assembly of resident (moved) blocks */
-    double asm_new_ms;        /* window assembly of freshly staged blocks */
-    double h2d_ms;            /* host -> HBM pool copies (copy stream) */
-    uint64_t score_bytes, asm_moved_bytes, asm_new_bytes, h2d_bytes;
-    uint32_t n_gap;           /* select -> apply hand-overs timed */
-    double gap_ms;            /* device idle while the host plans (select end -> apply enqueue) */
+    double asm_ms;            /* window assembly (moved and fresh slots in one launch) */
+    uint64_t score_bytes;     /* summary bytes the scoring read */
+    uint64_t asm_hbm_bytes;   /* HBM bytes the assemblies read + wrote (collected steps) */
+    uint64_t asm_link_bytes;  /* host-link bytes fresh slots read (collected steps) */
 } kvmret_prof;
 /* Reset the counters and turn event timing on (1) or off (0). */
 int kvmret_prof_enable(kvmret_ctx *ctx, int on);

@@ -1,6 +1,15 @@
 // Retrieval context: device state of one shard (layers) of one session and
 // the host orchestration of a retrieval step. Implements the C ABI of
 // include/kvmret.h; no C++ exception leaves this file.
+//
+// A step runs entirely on the device once it is enqueued: query accumulation,
+// scoring, the exact top-k, the device plan (window diff, HBM pool slots, job
+// lists) and the window assembly, which reads fresh blocks straight from the
+// mapped pinned repository. The selected ids and the plan counts come back
+// through a pinned readback ring; the host block table replays each selection
+// when it is collected, which keeps the reference's plan metadata (stage-in /
+// stage-out lists, remap rows) without the host ever sitting between the
+// selection and the assembly.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -39,6 +48,12 @@ int fail(int code, const char *fmt, ...) {
             return fail(KVMRET_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_));            \
     } while (0)
 
+#define TRY(x)                                                                                \
+    do {                                                                                      \
+        const int r_ = (x);                                                                   \
+        if (r_ != KVMRET_OK) return r_;                                                       \
+    } while (0)
+
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
 bool type_ok(int32_t t) {
@@ -65,6 +80,10 @@ uint32_t hadamard_nrot_k(uint32_t d_head) {
     return nrot / 2;
 }
 
+constexpr int kRing = 4;          // readback slots (steps in flight before a collect)
+constexpr size_t kEventPool = 8192;
+enum { PR_SCORE = 0, PR_ASM };
+
 }  // namespace
 
 namespace kvmret {
@@ -80,49 +99,48 @@ struct kvmret_ctx {
     uint64_t win_k_layer = 0, win_v_layer = 0;
     kvmret::AssembleGeom geom{};
     kvmret::Theta theta{};
-    // device
+    // device: scoring
     float *summ = nullptr, *tail_sum = nullptr, *q_sum = nullptr, *qv = nullptr, *nq = nullptr;
     uint32_t *q_count_dev = nullptr;
     uint8_t *has_block = nullptr, *active = nullptr, *kept_dev = nullptr, *sel_dev = nullptr;
     double *contrib = nullptr, *scores = nullptr;
+    // device: window, pool and plan state
     uint8_t *pool = nullptr, *win_k = nullptr, *win_v = nullptr;
+    float2 *rope_tab = nullptr;  // cos/sin of every window position [pos][n_rot/2]
+    int32_t *d_win_id = nullptr, *d_win_base = nullptr, *d_blk_slot = nullptr,
+            *d_slot_blk = nullptr;
+    uint32_t *d_win_ntok = nullptr, *d_blk_ntok = nullptr, *d_slot_ntok = nullptr,
+             *d_slot_used = nullptr, *d_counts = nullptr, *d_ids = nullptr;
     Job *jobs_dev = nullptr;
     kvmret::CopyOp *ops_dev = nullptr;
-    float2 *rope_tab = nullptr;  // cos/sin of every window position [pos][n_rot/2]
     // host
-    uint8_t *repo_host = nullptr, *repo_dev = nullptr, *pin_sel = nullptr, *pin_kept = nullptr;
+    uint8_t *repo_host = nullptr, *repo_dev = nullptr;
+    uint8_t *pin_flags = nullptr;  // kept / selection flags staging
+    uint32_t *pin_rb = nullptr;    // readback ring: kRing x (8 counts + win_slots ids)
+    cudaEvent_t ev_rb[kRing] = {};
+    int rb_head = 0, rb_pending = 0;
+    uint32_t step = 0;
     std::vector<uint32_t> q_count;
     bool q_dirty = true;
+    std::vector<uint8_t> kept_cached;  // last kept flags uploaded
+    bool kept_valid = false;
     kvmret::BlockTable table;
     kvmret::Plan last_plan;
-    // HBM pool: which block each slot holds and with how many tokens staged
-    std::vector<int32_t> block_slot;   // [ncap] pool slot or -1
-    std::vector<int32_t> slot_block;   // [pool_slots] block or -1
-    std::vector<uint32_t> slot_ntok;   // tokens staged in the slot
-    std::vector<uint64_t> slot_used;   // step of last use (cache eviction order)
-    std::vector<uint32_t> free_slots;  // LIFO
-    uint64_t step = 0;
-    // window: block, RoPE base and tokens of each slot
-    std::vector<int32_t> win_id, win_base;
-    std::vector<uint32_t> win_ntok;
-    cudaStream_t st = nullptr, st_copy = nullptr;
-    cudaEvent_t ev_prev = nullptr, ev_h2d = nullptr;
-    static constexpr int kGroups = 8;  // fresh-block copy/assembly pipeline depth
-    cudaEvent_t ev_grp[kGroups] = {};
-    // timing (kvmret_prof_*): event pool and pending (begin, end, kind, bytes)
+    kvmret_step_stats last_stats{};
+    cudaStream_t st = nullptr;
+    // timing (kvmret_prof_*): event pool and pending (begin, end, kind)
     struct Region {
         cudaEvent_t a, b;
         int kind;
-        uint64_t bytes;
     };
     bool prof_on = false;
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_next = 0;
     std::vector<Region> pending;
     kvmret_prof prof{};
-    int gap_open = -1;  // region opened at the end of select, closed by apply
 
     explicit kvmret_ctx(const kvmret::TableConfig &tc) : table(tc) {}
+    uint32_t *rb(int slot) { return pin_rb + static_cast<size_t>(slot) * (8 + win_slots); }
 };
 
 struct kvmret_table {
@@ -164,24 +182,25 @@ int validate(const kvmret_config &c) {
     if (kr % 16 || vr % 16)
         return fail(KVMRET_ERR_ARG, "row bytes %llu / %llu not multiples of 16",
                     (unsigned long long)kr, (unsigned long long)vr);
-    const uint32_t pool = c.pool_blocks ? c.pool_blocks : c.budget_blocks + c.reserve_blocks;
+    const uint32_t win = c.budget_blocks + c.reserve_blocks;
+    const uint32_t pool = c.pool_blocks ? c.pool_blocks : win;
     if (pool < c.budget_blocks)
         return fail(KVMRET_ERR_ARG, "pool_blocks %u < budget_blocks %u", pool, c.budget_blocks);
+    if (win > 4096 || pool > 8192)
+        return fail(KVMRET_ERR_ARG, "window of %u slots / pool of %u slots exceeds 4096 / 8192",
+                    win, pool);
     if (c.freq_base <= 0.0f) return fail(KVMRET_ERR_ARG, "freq_base must be > 0");
     return KVMRET_OK;
 }
 
-enum { PR_SCORE = 0, PR_ASM_MOVED, PR_ASM_NEW, PR_H2D, PR_GAP };
-constexpr size_t kEventPool = 8192;
-
 // Begin a timed region on stream `s`; returns the region index or -1.
-int prof_begin(kvmret_ctx *c, cudaStream_t s, int kind, uint64_t bytes) {
+int prof_begin(kvmret_ctx *c, cudaStream_t s, int kind) {
     if (!c->prof_on) return -1;
     if (c->ev_next + 2 > c->ev_pool.size()) {
         ++c->prof.dropped;
         return -1;
     }
-    kvmret_ctx::Region r{c->ev_pool[c->ev_next], c->ev_pool[c->ev_next + 1], kind, bytes};
+    kvmret_ctx::Region r{c->ev_pool[c->ev_next], c->ev_pool[c->ev_next + 1], kind};
     c->ev_next += 2;
     if (cudaEventRecord(r.a, s) != cudaSuccess) return -1;
     c->pending.push_back(r);
@@ -195,22 +214,20 @@ void prof_end(kvmret_ctx *c, cudaStream_t s, int idx) {
 void free_all(kvmret_ctx *c) {
     if (c->cfg.device >= 0) cudaSetDevice(c->cfg.device);
     if (c->st) cudaStreamSynchronize(c->st);
-    if (c->st_copy) cudaStreamSynchronize(c->st_copy);
     void *dev[] = {c->summ, c->tail_sum, c->q_sum, c->qv, c->nq, c->q_count_dev, c->has_block,
                    c->active, c->kept_dev, c->sel_dev, c->contrib, c->scores, c->pool,
-                   c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab};
+                   c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab, c->d_win_id,
+                   c->d_win_base, c->d_blk_slot, c->d_slot_blk, c->d_win_ntok, c->d_blk_ntok,
+                   c->d_slot_ntok, c->d_slot_used, c->d_counts, c->d_ids};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
-    if (c->pin_sel) cudaFreeHost(c->pin_sel);
-    if (c->pin_kept) cudaFreeHost(c->pin_kept);
+    if (c->pin_flags) cudaFreeHost(c->pin_flags);
+    if (c->pin_rb) cudaFreeHost(c->pin_rb);
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
-    for (cudaEvent_t e : c->ev_grp)
+    for (cudaEvent_t e : c->ev_rb)
         if (e) cudaEventDestroy(e);
-    if (c->ev_prev) cudaEventDestroy(c->ev_prev);
-    if (c->ev_h2d) cudaEventDestroy(c->ev_h2d);
     if (c->st) cudaStreamDestroy(c->st);
-    if (c->st_copy) cudaStreamDestroy(c->st_copy);
 }
 
 template <typename T>
@@ -225,11 +242,16 @@ int dmalloc(T **p, size_t bytes) {
     return KVMRET_OK;
 }
 
-#define TRY(x)                                                                                \
-    do {                                                                                      \
-        const int r_ = (x);                                                                   \
-        if (r_ != KVMRET_OK) return r_;                                                       \
-    } while (0)
+template <typename T>
+int hmalloc(T **p, size_t bytes, unsigned flags) {
+    const cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(p), bytes, flags);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        return fail(KVMRET_ERR_NOMEM, "pinned host allocation of %zu bytes: %s", bytes,
+                    cudaGetErrorString(e));
+    }
+    return KVMRET_OK;
+}
 
 int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     c->cfg = cfg;
@@ -268,12 +290,9 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     g.fwht_scale = fwht_n ? 1.0f / std::sqrt(static_cast<float>(fwht_n)) : 0.0f;
 
     CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
-    CK(cudaStreamCreateWithFlags(&c->st_copy, cudaStreamNonBlocking));
-    CK(cudaEventCreateWithFlags(&c->ev_prev, cudaEventDisableTiming));
-    CK(cudaEventCreateWithFlags(&c->ev_h2d, cudaEventDisableTiming));
-    for (auto &e : c->ev_grp) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto &e : c->ev_rb) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
 
-    const size_t L = k.n_layer;
+    const size_t L = k.n_layer, W = c->win_slots, P = c->pool_slots;
     TRY(dmalloc(&c->summ, L * c->E * c->ncap * sizeof(float)));
     TRY(dmalloc(&c->tail_sum, 2 * L * c->E * sizeof(float)));
     TRY(dmalloc(&c->q_sum, L * c->qdim * sizeof(float)));
@@ -286,174 +305,123 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     TRY(dmalloc(&c->sel_dev, c->ncap));
     TRY(dmalloc(&c->contrib, L * c->cstride * sizeof(double)));
     TRY(dmalloc(&c->scores, c->ncap * sizeof(double)));
-    TRY(dmalloc(&c->pool, static_cast<size_t>(c->pool_slots) * c->slot_bytes));
+    TRY(dmalloc(&c->pool, P * c->slot_bytes));
     TRY(dmalloc(&c->win_k, L * c->win_k_layer));
     TRY(dmalloc(&c->win_v, L * c->win_v_layer));
-    TRY(dmalloc(&c->jobs_dev, 2ull * c->win_slots * sizeof(Job)));
+    TRY(dmalloc(&c->jobs_dev, 2 * W * sizeof(Job)));
     TRY(dmalloc(&c->ops_dev, 8192 * sizeof(kvmret::CopyOp)));
     const uint32_t n_pos = c->win_slots * k.block_tokens;
     TRY(dmalloc(&c->rope_tab, static_cast<size_t>(n_pos) * (k.n_rot / 2) * sizeof(float2)));
-    CK(kvmret::launch_rope_table(c->rope_tab, n_pos, k.n_rot / 2, c->theta, c->st));
+    TRY(dmalloc(&c->d_win_id, W * sizeof(int32_t)));
+    TRY(dmalloc(&c->d_win_base, W * sizeof(int32_t)));
+    TRY(dmalloc(&c->d_win_ntok, W * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_blk_slot, c->ncap * sizeof(int32_t)));
+    TRY(dmalloc(&c->d_blk_ntok, c->ncap * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_slot_blk, P * sizeof(int32_t)));
+    TRY(dmalloc(&c->d_slot_ntok, P * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_slot_used, P * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_counts, 8 * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_ids, W * sizeof(uint32_t)));
     CK(cudaMemsetAsync(c->summ, 0, L * c->E * c->ncap * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->tail_sum, 0, 2 * L * c->E * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->q_sum, 0, L * c->qdim * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->has_block, 0, c->ncap, c->st));
     CK(cudaMemsetAsync(c->contrib, 0, L * c->cstride * sizeof(double), c->st));
     CK(cudaMemsetAsync(c->scores, 0, c->ncap * sizeof(double), c->st));
+    CK(cudaMemsetAsync(c->d_win_id, 0xff, W * sizeof(int32_t), c->st));  // -1: empty
+    CK(cudaMemsetAsync(c->d_win_base, 0, W * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_win_ntok, 0, W * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_blk_slot, 0xff, c->ncap * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_blk_ntok, 0, c->ncap * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_blk, 0xff, P * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_ntok, 0, P * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_used, 0, P * sizeof(uint32_t), c->st));
+    CK(kvmret::launch_rope_table(c->rope_tab, n_pos, k.n_rot / 2, c->theta, c->st));
 
     const size_t repo_bytes = static_cast<size_t>(k.max_blocks) * c->slot_bytes;
-    cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&c->repo_host), repo_bytes,
-                                  cudaHostAllocMapped | cudaHostAllocPortable);
-    if (e != cudaSuccess) {
-        c->repo_host = nullptr;
-        return fail(KVMRET_ERR_NOMEM, "pinned repository of %zu bytes: %s", repo_bytes,
-                    cudaGetErrorString(e));
-    }
+    TRY(hmalloc(&c->repo_host, repo_bytes, cudaHostAllocMapped | cudaHostAllocPortable));
     CK(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->repo_dev), c->repo_host, 0));
-    e = cudaHostAlloc(reinterpret_cast<void **>(&c->pin_sel), c->ncap, cudaHostAllocDefault);
-    if (e != cudaSuccess) {
-        c->pin_sel = nullptr;
-        return fail(KVMRET_ERR_NOMEM, "pinned staging: %s", cudaGetErrorString(e));
-    }
-    e = cudaHostAlloc(reinterpret_cast<void **>(&c->pin_kept), c->ncap, cudaHostAllocDefault);
-    if (e != cudaSuccess) {
-        c->pin_kept = nullptr;
-        return fail(KVMRET_ERR_NOMEM, "pinned staging: %s", cudaGetErrorString(e));
-    }
+    TRY(hmalloc(&c->pin_flags, c->ncap, cudaHostAllocDefault));
+    TRY(hmalloc(&c->pin_rb, kRing * (8 + W) * sizeof(uint32_t), cudaHostAllocDefault));
     c->q_count.assign(L, 0);
-    c->block_slot.assign(c->ncap, -1);
-    c->slot_block.assign(c->pool_slots, -1);
-    c->slot_ntok.assign(c->pool_slots, 0);
-    c->slot_used.assign(c->pool_slots, 0);
-    c->free_slots.clear();
-    for (uint32_t s = c->pool_slots; s > 0; --s) c->free_slots.push_back(s - 1);
-    c->win_id.assign(c->win_slots, -1);
-    c->win_base.assign(c->win_slots, 0);
-    c->win_ntok.assign(c->win_slots, 0);
     CK(cudaStreamSynchronize(c->st));
     return KVMRET_OK;
 }
 
-// Pool slot for a block entering the window: a free slot (LIFO), else (cache
-// mode) the least recently used slot whose block is not in the new window.
-int32_t take_slot(kvmret_ctx *c, const std::vector<uint8_t> &in_new) {
-    if (!c->free_slots.empty()) {
-        const uint32_t s = c->free_slots.back();
-        c->free_slots.pop_back();
-        return static_cast<int32_t>(s);
-    }
-    int32_t best = -1;
-    for (uint32_t s = 0; s < c->pool_slots; ++s) {
-        const int32_t b = c->slot_block[s];
-        if (b >= 0 && in_new[b]) continue;
-        if (best < 0 || c->slot_used[s] < c->slot_used[best]) best = static_cast<int32_t>(s);
-    }
-    if (best >= 0 && c->slot_block[best] >= 0) c->block_slot[c->slot_block[best]] = -1;
-    return best;
+// Readback of the oldest uncollected step: wait for it, replay its selection
+// in the host block table (the plan metadata) and fill the stats.
+int collect_one(kvmret_ctx *c, uint32_t *ids_out, uint32_t *n_out) {
+    const int slot = (c->rb_head - c->rb_pending + kRing) % kRing;
+    CK(cudaEventSynchronize(c->ev_rb[slot]));
+    const uint32_t *r = c->rb(slot);
+    const uint32_t n_moved = r[0], n_fresh = r[1], n_sel = r[2], err = r[4];
+    --c->rb_pending;
+    if (err) return fail(KVMRET_ERR_STATE, "device plan error 0x%x (window or pool too small)", err);
+    const uint32_t *ids = r + 8;
+    c->last_plan = c->table.set_selection(ids, n_sel, false);
+    kvmret_step_stats &s = c->last_stats;
+    std::memset(&s, 0, sizeof(s));
+    s.n_selected = n_sel;
+    s.n_stage_in = static_cast<uint32_t>(c->last_plan.stage_in.size());
+    s.n_stage_out = static_cast<uint32_t>(c->last_plan.stage_out.size());
+    for (const auto &rm : c->last_plan.remaps) s.n_skip += rm.skip ? 1u : 0u;
+    s.n_h2d_blocks = n_fresh;
+    s.n_assembled = n_moved + n_fresh;
+    s.n_moved = n_moved;
+    s.total_window_tokens = r[3];
+    const uint64_t row = c->k_row + c->v_row, L = c->cfg.n_layer;
+    s.h2d_bytes = static_cast<uint64_t>(r[6]) * row * L;
+    s.assemble_bytes = 2ull * (static_cast<uint64_t>(r[5]) + r[6]) * row * L;
+    c->prof.asm_hbm_bytes += s.assemble_bytes;
+    c->prof.asm_link_bytes += s.h2d_bytes;
+    if (ids_out) std::copy(ids, ids + n_sel, ids_out);
+    if (n_out) *n_out = n_sel;
+    return KVMRET_OK;
 }
 
-int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_stats *stats) {
-    const uint32_t nb = c->table.n_blocks();
-    const int gap = c->gap_open;
-    c->gap_open = -1;
-    {  // bound the window before touching any state
-        std::vector<uint8_t> seen(nb, 0);
-        uint32_t uniq = 0;
-        for (uint32_t i = 0; i < n_ids; ++i)
-            if (ids[i] < nb && !seen[ids[i]]) {
-                seen[ids[i]] = 1;
-                ++uniq;
-            }
-        if (uniq > c->win_slots)
-            return fail(KVMRET_ERR_ARG, "selection of %u blocks exceeds %u window slots", uniq,
-                        c->win_slots);
-    }
-    c->last_plan = c->table.set_selection(ids, n_ids, false);
-    const kvmret::Plan &p = c->last_plan;
+int drain(kvmret_ctx *c) {
+    while (c->rb_pending > 0) TRY(collect_one(c, nullptr, nullptr));
+    return KVMRET_OK;
+}
+
+// Device plan + assembly from the selection flags in sel_dev, then an
+// asynchronous readback of the ids and counts.
+int plan_and_assemble(kvmret_ctx *c) {
+    if (c->rb_pending == kRing) TRY(collect_one(c, nullptr, nullptr));
     ++c->step;
-    std::vector<uint8_t> in_new(c->ncap, 0);
-    for (const auto &r : p.remaps) in_new[r.id] = 1;
-    // Release pool slots of blocks that left the window (kept as cache if asked).
-    if (!c->cfg.pool_cache) {
-        for (uint32_t s = 0; s < c->pool_slots; ++s) {
-            const int32_t b = c->slot_block[s];
-            if (b >= 0 && !in_new[b]) {
-                c->block_slot[b] = -1;
-                c->slot_block[s] = -1;
-                c->free_slots.push_back(s);
-            }
-        }
-    }
-    // Blocks without a current pool copy are staged from the host repository.
-    std::vector<std::pair<uint32_t, uint32_t>> h2d;  // (block, slot)
-    std::vector<uint8_t> fresh(c->ncap, 0);
-    const auto &blocks = c->table.blocks();
-    for (const auto &r : p.remaps) {
-        int32_t s = c->block_slot[r.id];
-        if (s < 0 || c->slot_ntok[s] != blocks[r.id].n_tok) {
-            if (s < 0) {
-                s = take_slot(c, in_new);
-                if (s < 0) return fail(KVMRET_ERR_STATE, "HBM pool exhausted");
-                c->slot_block[s] = static_cast<int32_t>(r.id);
-                c->block_slot[r.id] = s;
-            }
-            c->slot_ntok[s] = blocks[r.id].n_tok;
-            h2d.emplace_back(r.id, static_cast<uint32_t>(s));
-            fresh[r.id] = 1;
-        }
-        c->slot_used[s] = c->step;
-    }
-    // Window slots whose content changes: moved residents first, then fresh blocks.
-    std::vector<Job> moved, added;
-    uint32_t w = 0;
-    for (const auto &r : p.remaps) {
-        const bool same = c->win_id[w] == static_cast<int32_t>(r.id) && c->win_base[w] == r.to &&
-                          c->win_ntok[w] == r.n_tok && !fresh[r.id];
-        if (!same) {
-            Job j{static_cast<uint32_t>(c->block_slot[r.id]), w, r.to, r.n_tok};
-            (fresh[r.id] ? added : moved).push_back(j);
-        }
-        c->win_id[w] = static_cast<int32_t>(r.id);
-        c->win_base[w] = r.to;
-        c->win_ntok[w] = r.n_tok;
-        ++w;
-    }
-    for (; w < c->win_slots; ++w) {
-        c->win_id[w] = -1;
-        c->win_ntok[w] = 0;
-    }
-    // Enqueue. Host->pool copies go on the copy stream after the previous
-    // step's readers of the pool, in up to kGroups groups; resident moves start
-    // at once on the compute stream; each group of fresh blocks is assembled as
-    // soon as its own copies have landed.
-    std::vector<Job> all(moved);
-    all.insert(all.end(), added.begin(), added.end());
-    prof_end(c, c->st, gap);
-    if (!all.empty())
-        CK(cudaMemcpyAsync(c->jobs_dev, all.data(), all.size() * sizeof(Job),
-                           cudaMemcpyHostToDevice, c->st));
-    const size_t n_new = h2d.size();  // == added.size(), same order
-    const size_t groups = std::min<size_t>(n_new, kvmret_ctx::kGroups);
-    auto grp_begin = [&](size_t g) { return n_new * g / groups; };
-    if (n_new) {
-        CK(cudaEventRecord(c->ev_prev, c->st));
-        CK(cudaStreamWaitEvent(c->st_copy, c->ev_prev, 0));
-        const int pr = prof_begin(c, c->st_copy, PR_H2D, n_new * c->slot_bytes);
-        for (size_t g = 0; g < groups; ++g) {
-            for (size_t i = grp_begin(g); i < grp_begin(g + 1); ++i)
-                CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(h2d[i].second) * c->slot_bytes,
-                                   c->repo_host + static_cast<uint64_t>(h2d[i].first) * c->slot_bytes,
-                                   c->slot_bytes, cudaMemcpyHostToDevice, c->st_copy));
-            CK(cudaEventRecord(c->ev_grp[g], c->st_copy));
-        }
-        prof_end(c, c->st_copy, pr);
-    }
-    auto job_bytes = [&](const Job *v, size_t n) {
-        uint64_t tok = 0;
-        for (size_t i = 0; i < n; ++i) tok += v[i].n_tok;
-        return 2ull * tok * (c->k_row + c->v_row) * c->cfg.n_layer;
-    };
+    kvmret::PlanArgs pa{};
+    pa.sel = c->sel_dev;
+    pa.blk_ntok = c->d_blk_ntok;
+    pa.n_blocks = c->table.n_blocks();
+    pa.win_slots = c->win_slots;
+    pa.pool_slots = c->pool_slots;
+    pa.step = c->step;
+    pa.pool_cache = c->cfg.pool_cache;
+    pa.win_id = c->d_win_id;
+    pa.win_base = c->d_win_base;
+    pa.win_ntok = c->d_win_ntok;
+    pa.blk_slot = c->d_blk_slot;
+    pa.slot_blk = c->d_slot_blk;
+    pa.slot_ntok = c->d_slot_ntok;
+    pa.slot_used = c->d_slot_used;
+    pa.jobs = c->jobs_dev;
+    pa.counts = c->d_counts;
+    pa.ids = c->d_ids;
+    CK(kvmret::launch_plan(pa, c->st));
+    const int slot = c->rb_head;
+    uint32_t *r = c->rb(slot);
+    CK(cudaMemcpyAsync(r, c->d_counts, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(r + 8, c->d_ids, c->win_slots * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                       c->st));
+    CK(cudaEventRecord(c->ev_rb[slot], c->st));
+    c->rb_head = (c->rb_head + 1) % kRing;
+    ++c->rb_pending;
     kvmret::AsmLaunch al{};
+    al.jobs = c->jobs_dev;
+    al.counts = c->d_counts;
+    al.fresh_offset = c->win_slots;
+    al.repo = c->repo_dev;
+    al.pool_w = c->pool;
     al.pool = c->pool;
     al.slot_bytes = c->slot_bytes;
     al.win_k = c->win_k;
@@ -461,67 +429,41 @@ int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_s
     al.gtab = c->rope_tab;
     al.theta = c->theta;
     al.g = c->geom;
-    if (!moved.empty()) {
-        const int pr = prof_begin(c, c->st, PR_ASM_MOVED, job_bytes(moved.data(), moved.size()));
-        al.jobs = c->jobs_dev;
-        CK(kvmret::launch_assemble(al, static_cast<uint32_t>(moved.size()), c->st));
-        prof_end(c, c->st, pr);
-        c->prof.launches += 1;
-    }
-    for (size_t g = 0; g < groups; ++g) {
-        const size_t b = grp_begin(g), e = grp_begin(g + 1);
-        CK(cudaStreamWaitEvent(c->st, c->ev_grp[g], 0));
-        const int pr = prof_begin(c, c->st, PR_ASM_NEW, job_bytes(added.data() + b, e - b));
-        al.jobs = c->jobs_dev + moved.size() + b;
-        CK(kvmret::launch_assemble(al, static_cast<uint32_t>(e - b), c->st));
-        prof_end(c, c->st, pr);
-        c->prof.launches += 1;
-    }
-    if (stats) {
-        std::memset(stats, 0, sizeof(*stats));
-        stats->n_selected = static_cast<uint32_t>(p.remaps.size());
-        stats->n_stage_in = static_cast<uint32_t>(p.stage_in.size());
-        stats->n_stage_out = static_cast<uint32_t>(p.stage_out.size());
-        for (const auto &r : p.remaps) stats->n_skip += r.skip ? 1u : 0u;
-        stats->n_h2d_blocks = static_cast<uint32_t>(h2d.size());
-        stats->n_assembled = static_cast<uint32_t>(all.size());
-        stats->n_moved = static_cast<uint32_t>(moved.size());
-        stats->total_window_tokens = p.window_tokens;
-        stats->h2d_bytes = static_cast<uint64_t>(h2d.size()) * c->slot_bytes;
-        uint64_t tok = 0;
-        for (const Job &j : all) tok += j.n_tok;
-        stats->assemble_bytes = 2ull * tok * (c->k_row + c->v_row) * c->cfg.n_layer;
+    const int pr = prof_begin(c, c->st, PR_ASM);
+    CK(kvmret::launch_assemble(al, 2 * c->win_slots, c->st));
+    prof_end(c, c->st, pr);
+    c->prof.launches += 2;
+    return KVMRET_OK;
+}
+
+// Upload the kept flags of the top-k (sink, mandatory newest-first, recent)
+// when they changed; returns `need` through *need.
+int upload_kept(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *need) {
+    std::vector<uint8_t> kept;
+    uint32_t kept_count = 0;
+    *need = c->table.keep(mandatory, n_mand, kept, kept_count);
+    if (!c->kept_valid || kept != c->kept_cached) {
+        const uint32_t n = c->table.n_blocks();
+        CK(cudaStreamSynchronize(c->st));  // the staging buffer may still feed an earlier copy
+        std::copy(kept.begin(), kept.begin() + n, c->pin_flags);
+        CK(cudaMemcpyAsync(c->kept_dev, c->pin_flags, n, cudaMemcpyHostToDevice, c->st));
+        c->kept_cached.swap(kept);
+        c->kept_valid = true;
     }
     return KVMRET_OK;
 }
 
-int select_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
-                uint32_t *n_out) {
-    if (!n_out) return fail(KVMRET_ERR_ARG, "n_out is NULL");
-    std::vector<uint8_t> kept;
-    uint32_t kept_count = 0;
-    const uint32_t need = c->table.keep(mandatory, n_mand, kept, kept_count);
+int select_device(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
+    uint32_t need = 0;
+    TRY(upload_kept(c, mandatory, n_mand, &need));
     const uint32_t n = c->table.n_blocks();
-    const uint8_t *sel = kept.data();
     if (need > 0) {
-        // select() ends in a stream synchronisation, so the staging buffer is free here
-        std::copy(kept.begin(), kept.begin() + n, c->pin_kept);
-        CK(cudaMemcpyAsync(c->kept_dev, c->pin_kept, n, cudaMemcpyHostToDevice, c->st));
         CK(kvmret::launch_select(c->scores, c->kept_dev, n, need, c->cfg.tie_higher_id,
                                  c->sel_dev, c->st));
         c->prof.launches += 1;
-        CK(cudaMemcpyAsync(c->pin_sel, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
-        c->gap_open = prof_begin(c, c->st, PR_GAP, 0);
-        CK(cudaStreamSynchronize(c->st));
-        sel = c->pin_sel;
+    } else if (n) {
+        CK(cudaMemcpyAsync(c->sel_dev, c->kept_dev, n, cudaMemcpyDeviceToDevice, c->st));
     }
-    uint32_t m = 0;
-    for (uint32_t i = 0; i < n; ++i)
-        if (sel[i]) {
-            if (ids_out) ids_out[m] = i;
-            ++m;
-        }
-    *n_out = m;
     return KVMRET_OK;
 }
 
@@ -540,27 +482,20 @@ int score_layers_impl(kvmret_ctx *c, double *out) {
         c->q_dirty = false;
     }
     const uint32_t n = c->table.n_blocks();
-    const uint64_t bytes = static_cast<uint64_t>(c->cfg.n_layer) * c->E *
-                           ((n + 63) / 64 * 64) * sizeof(float);
-    const int pr = prof_begin(c, c->st, PR_SCORE, bytes);
+    const int pr = prof_begin(c, c->st, PR_SCORE);
     CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, dst, c->cfg.n_layer,
                             c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st, c->cstride));
     prof_end(c, c->st, pr);
+    c->prof.score_bytes += static_cast<uint64_t>(c->cfg.n_layer) * c->E * ((n + 63) / 64 * 64) *
+                           sizeof(float);
     c->prof.launches += n ? 1 : 0;
     return KVMRET_OK;
 }
 
-int score_impl(kvmret_ctx *c, double *scores_host) {
-    TRY(score_layers_impl(c, nullptr));
-    const uint32_t n = c->table.n_blocks();
-    CK(kvmret::launch_reduce(c->contrib, c->active, c->cfg.n_layer, c->cstride, c->has_block, n,
-                             c->scores, c->st));
-    c->prof.launches += n ? 1 : 0;
-    if (scores_host) {
-        CK(cudaMemcpyAsync(scores_host, c->scores, n * sizeof(double), cudaMemcpyDeviceToHost,
-                           c->st));
-        CK(cudaStreamSynchronize(c->st));
-    }
+int reduce_impl(kvmret_ctx *c, const double *rows, uint32_t n_layer_all, const uint8_t *active) {
+    CK(kvmret::launch_reduce(rows, active, n_layer_all, c->cstride, c->has_block,
+                             c->table.n_blocks(), c->scores, c->st));
+    c->prof.launches += 1;
     return KVMRET_OK;
 }
 
@@ -580,6 +515,47 @@ int score_impl(kvmret_ctx *c, double *scores_host) {
         if (de_ != cudaSuccess)                                                               \
             return fail(KVMRET_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(de_));        \
     } while (0)
+
+int preview_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
+                 uint32_t *n_out) {
+    if (!n_out) return fail(KVMRET_ERR_ARG, "n_out is NULL");
+    TRY(select_device(c, mandatory, n_mand));
+    const uint32_t n = c->table.n_blocks();
+    CK(cudaMemcpyAsync(c->pin_flags, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    c->kept_valid = false;  // the staging buffer now holds the selection
+    uint32_t m = 0;
+    for (uint32_t i = 0; i < n; ++i)
+        if (c->pin_flags[i]) {
+            if (ids_out) ids_out[m] = i;
+            ++m;
+        }
+    *n_out = m;
+    return KVMRET_OK;
+}
+
+int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_stats *stats) {
+    TRY(drain(c));
+    const uint32_t nb = c->table.n_blocks();
+    std::vector<uint8_t> flags(c->ncap, 0);
+    uint32_t uniq = 0;
+    for (uint32_t i = 0; i < n_ids; ++i)
+        if (ids[i] < nb && !flags[ids[i]]) {
+            flags[ids[i]] = 1;
+            ++uniq;
+        }
+    if (uniq > c->win_slots)
+        return fail(KVMRET_ERR_ARG, "selection of %u blocks exceeds %u window slots", uniq,
+                    c->win_slots);
+    CK(cudaStreamSynchronize(c->st));
+    std::copy(flags.begin(), flags.begin() + nb, c->pin_flags);
+    c->kept_valid = false;
+    if (nb) CK(cudaMemcpyAsync(c->sel_dev, c->pin_flags, nb, cudaMemcpyHostToDevice, c->st));
+    TRY(plan_and_assemble(c));
+    TRY(collect_one(c, nullptr, nullptr));
+    if (stats) *stats = c->last_stats;
+    return KVMRET_OK;
+}
 
 }  // namespace
 
@@ -621,7 +597,7 @@ uint64_t kvmret_row_bytes(int32_t type, uint32_t n) {
 }
 
 const char *kvmret_last_error(void) { return g_err.c_str(); }
-const char *kvmret_version(void) { return "kvmret 0.1 sm_100a"; }
+const char *kvmret_version(void) { return "kvmret 0.2 sm_100a"; }
 
 int kvmret_create(const kvmret_config *cfg, kvmret_ctx **out) {
     if (!cfg || !out) return fail(KVMRET_ERR_ARG, "null argument");
@@ -657,8 +633,7 @@ void *kvmret_stream(kvmret_ctx *c) { return c ? static_cast<void *>(c->st) : nul
 int kvmret_sync(kvmret_ctx *c) {
     NEED_CTX(c);
     CK(cudaStreamSynchronize(c->st));
-    CK(cudaStreamSynchronize(c->st_copy));
-    return KVMRET_OK;
+    GUARD(return drain(c));
 }
 
 void *kvmret_repo_host(kvmret_ctx *c) { return c ? c->repo_host : nullptr; }
@@ -700,12 +675,14 @@ int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *
     a.unit_k = c->unit_k;
     a.unit = c->unit;
     a.summ = c->summ;
+    a.blk_ntok = c->d_blk_ntok;
     a.tail_sum = c->tail_sum;
     a.has_block = c->has_block;
     a.repo_dev = c->repo_dev;
     CK(kvmret::launch_append(a, c->st));
     c->prof.launches += 2;
     GUARD(c->table.append(n_tok));
+    c->kept_valid = false;
     return KVMRET_OK;
 }
 
@@ -780,7 +757,14 @@ int kvmret_query_get(kvmret_ctx *c, float *q_sum, uint32_t *q_count) {
 
 int kvmret_score(kvmret_ctx *c, double *scores_host) {
     NEED_CTX(c);
-    return score_impl(c, scores_host);
+    TRY(score_layers_impl(c, nullptr));
+    TRY(reduce_impl(c, c->contrib, c->cfg.n_layer, c->active));
+    if (scores_host) {
+        CK(cudaMemcpyAsync(scores_host, c->scores, c->table.n_blocks() * sizeof(double),
+                           cudaMemcpyDeviceToHost, c->st));
+        CK(cudaStreamSynchronize(c->st));
+    }
+    return KVMRET_OK;
 }
 
 int kvmret_score_layers(kvmret_ctx *c, double *contrib_out) {
@@ -794,16 +778,13 @@ uint32_t kvmret_contrib_stride(kvmret_ctx *c) { return c ? c->cstride : 0; }
 int kvmret_score_reduce(kvmret_ctx *c, const double *contrib_all, uint32_t n_layer_all) {
     NEED_CTX(c);
     if (!contrib_all || n_layer_all == 0) return fail(KVMRET_ERR_ARG, "bad contribution buffer");
-    CK(kvmret::launch_reduce(contrib_all, nullptr, n_layer_all, c->cstride, c->has_block,
-                             c->table.n_blocks(), c->scores, c->st));
-    c->prof.launches += 1;
-    return KVMRET_OK;
+    return reduce_impl(c, contrib_all, n_layer_all, nullptr);
 }
 
 int kvmret_prof_enable(kvmret_ctx *c, int on) {
     NEED_CTX(c);
     CK(cudaStreamSynchronize(c->st));
-    CK(cudaStreamSynchronize(c->st_copy));
+    GUARD(TRY(drain(c)));
     if (on && c->ev_pool.empty()) {
         GUARD(c->ev_pool.resize(kEventPool, nullptr));
         for (auto &e : c->ev_pool) CK(cudaEventCreate(&e));
@@ -819,17 +800,16 @@ int kvmret_prof_read(kvmret_ctx *c, kvmret_prof *out) {
     NEED_CTX(c);
     if (!out) return fail(KVMRET_ERR_ARG, "null output");
     CK(cudaStreamSynchronize(c->st));
-    CK(cudaStreamSynchronize(c->st_copy));
+    GUARD(TRY(drain(c)));
     for (const auto &r : c->pending) {
         float ms = 0.0f;
-        if (r.kind == PR_GAP && cudaEventQuery(r.b) != cudaSuccess) continue;  // never closed
         CK(cudaEventElapsedTime(&ms, r.a, r.b));
-        switch (r.kind) {
-        case PR_SCORE: c->prof.score_ms += ms; ++c->prof.n_score; c->prof.score_bytes += r.bytes; break;
-        case PR_ASM_MOVED: c->prof.asm_moved_ms += ms; ++c->prof.n_asm_moved; c->prof.asm_moved_bytes += r.bytes; break;
-        case PR_ASM_NEW: c->prof.asm_new_ms += ms; ++c->prof.n_asm_new; c->prof.asm_new_bytes += r.bytes; break;
-        case PR_GAP: c->prof.gap_ms += ms; ++c->prof.n_gap; break;
-        default: c->prof.h2d_ms += ms; ++c->prof.n_h2d; c->prof.h2d_bytes += r.bytes; break;
+        if (r.kind == PR_SCORE) {
+            c->prof.score_ms += ms;
+            ++c->prof.n_score;
+        } else {
+            c->prof.asm_ms += ms;
+            ++c->prof.n_asm;
         }
     }
     c->pending.clear();
@@ -842,13 +822,13 @@ int kvmret_select(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uin
                   uint32_t *n_out) {
     NEED_CTX(c);
     if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");
-    GUARD(return select_impl(c, mandatory, n_mand, ids_out, n_out));
+    GUARD(return preview_impl(c, mandatory, n_mand, ids_out, n_out));
 }
 
 int kvmret_preview(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
                    uint32_t *n_out) {
     NEED_CTX(c);
-    TRY(score_impl(c, nullptr));
+    TRY(kvmret_score(c, nullptr));
     return kvmret_select(c, mandatory, n_mand, ids_out, n_out);
 }
 
@@ -859,22 +839,35 @@ int kvmret_apply_selection(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids,
     GUARD(return apply_impl(c, ids, n_ids, stats));
 }
 
+int kvmret_select_apply_async(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
+    NEED_CTX(c);
+    if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");
+    GUARD(TRY(select_device(c, mandatory, n_mand)));
+    GUARD(return plan_and_assemble(c));
+}
+
+int kvmret_step_collect(kvmret_ctx *c, uint32_t *ids_out, uint32_t *n_out,
+                        kvmret_step_stats *stats) {
+    NEED_CTX(c);
+    if (c->rb_pending == 0) return fail(KVMRET_ERR_STATE, "no step to collect");
+    GUARD(TRY(collect_one(c, ids_out, n_out)));
+    if (stats) *stats = c->last_stats;
+    return KVMRET_OK;
+}
+
 int kvmret_apply_retrieval(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand,
                            uint32_t *ids_out, uint32_t *n_out, kvmret_step_stats *stats) {
     NEED_CTX(c);
-    std::vector<uint32_t> ids;
-    GUARD(ids.resize(c->cfg.budget_blocks > c->table.n_blocks() ? c->table.n_blocks()
-                                                                : c->cfg.budget_blocks));
-    uint32_t n = 0;
-    TRY(kvmret_preview(c, mandatory, n_mand, ids.data(), &n));
-    if (ids_out) std::copy(ids.begin(), ids.begin() + n, ids_out);
-    if (n_out) *n_out = n;
-    return kvmret_apply_selection(c, ids.data(), n, stats);
+    TRY(kvmret_score(c, nullptr));
+    GUARD(TRY(drain(c)));
+    TRY(kvmret_select_apply_async(c, mandatory, n_mand));
+    return kvmret_step_collect(c, ids_out, n_out, stats);
 }
 
 int kvmret_last_plan(kvmret_ctx *c, int32_t *remaps, uint32_t *n_remaps, uint32_t *stage_in,
                      uint32_t *n_stage_in, uint32_t *stage_out, uint32_t *n_stage_out) {
-    if (!c) return fail(KVMRET_ERR_ARG, "null context");
+    NEED_CTX(c);
+    GUARD(TRY(drain(c)));
     const kvmret::Plan &p = c->last_plan;
     if (n_remaps) *n_remaps = static_cast<uint32_t>(p.remaps.size());
     if (remaps)
@@ -905,11 +898,20 @@ void *kvmret_window_v(kvmret_ctx *c, uint32_t layer) {
 uint32_t kvmret_window_slots(kvmret_ctx *c) { return c ? c->win_slots : 0; }
 
 int kvmret_window_layout(kvmret_ctx *c, uint32_t *ids, int32_t *bases, uint32_t *n_out) {
-    if (!c || !n_out) return fail(KVMRET_ERR_ARG, "null argument");
+    NEED_CTX(c);
+    if (!n_out) return fail(KVMRET_ERR_ARG, "null argument");
+    std::vector<int32_t> wid, wb;
+    GUARD(wid.resize(c->win_slots));
+    GUARD(wb.resize(c->win_slots));
+    CK(cudaMemcpyAsync(wid.data(), c->d_win_id, c->win_slots * sizeof(int32_t),
+                       cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(wb.data(), c->d_win_base, c->win_slots * sizeof(int32_t),
+                       cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
     uint32_t n = 0;
-    while (n < c->win_slots && c->win_id[n] >= 0) {
-        if (ids) ids[n] = static_cast<uint32_t>(c->win_id[n]);
-        if (bases) bases[n] = c->win_base[n];
+    while (n < c->win_slots && wid[n] >= 0) {
+        if (ids) ids[n] = static_cast<uint32_t>(wid[n]);
+        if (bases) bases[n] = wb[n];
         ++n;
     }
     *n_out = n;

@@ -6,6 +6,8 @@
 
 #include <cuda_fp16.h>
 
+#include <cub/block/block_scan.cuh>
+
 #include "kvmret.h"
 
 namespace kvmret {
@@ -235,16 +237,29 @@ __global__ void rope_table_kernel(float2 *__restrict__ cs, uint32_t n_pos, uint3
 }
 
 // f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves.
-template <int D>
+// raw_dst (fresh blocks) also receives the unrotated rows; src is then host
+// memory read with plain loads.
+template <int D, bool FRESH>
 __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
                                               uint8_t *__restrict__ dst, const float2 *tab,
-                                              uint32_t n_tok, uint32_t n_head_kv) {
+                                              uint32_t n_tok, uint32_t n_head_kv,
+                                              uint8_t *__restrict__ raw_dst) {
     constexpr int HALF = D / 2, CPR = HALF / 8;
     const uint32_t n_items = n_tok * n_head_kv * CPR;
     for (uint32_t w = threadIdx.x; w < n_items; w += blockDim.x) {
         const uint32_t row = w / CPR, j = w % CPR, t = row / n_head_kv;
         const uint4 *sp = reinterpret_cast<const uint4 *>(src + static_cast<size_t>(row) * D * 2);
-        const uint4 lo = __ldg(sp + j), hi = __ldg(sp + CPR + j);
+        uint4 lo, hi;
+        if constexpr (FRESH) {
+            lo = sp[j];
+            hi = sp[CPR + j];
+            uint4 *rp = reinterpret_cast<uint4 *>(raw_dst + static_cast<size_t>(row) * D * 2);
+            rp[j] = lo;
+            rp[CPR + j] = hi;
+        } else {
+            lo = __ldg(sp + j);
+            hi = __ldg(sp + CPR + j);
+        }
         const uint16_t *a = reinterpret_cast<const uint16_t *>(&lo);
         const uint16_t *b = reinterpret_cast<const uint16_t *>(&hi);
         uint4 olo, ohi;
@@ -344,6 +359,19 @@ __device__ __forceinline__ void copy16_from_smem(const uint8_t *src, uint8_t *__
     const uint64_t n = nbytes / 16;
     for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = s[w];
 }
+// Host-memory source (plain loads), written to one or two destinations.
+__device__ __forceinline__ void copy16_host(const uint8_t *src, uint8_t *__restrict__ dst,
+                                            uint8_t *__restrict__ dst2, uint64_t nbytes) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    uint4 *d2 = reinterpret_cast<uint4 *>(dst2);
+    const uint64_t n = nbytes / 16;
+    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) {
+        const uint4 v = s[w];
+        d[w] = v;
+        if (d2) d2[w] = v;
+    }
+}
 
 constexpr int kAsmThreads = 512;
 constexpr int kQ8ChunkTok = 16;
@@ -365,35 +393,71 @@ __global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_cons
     constexpr int HALF = D / 2;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     float2 *tab = reinterpret_cast<float2 *>(smem_raw);
-    Job job;
+    uint32_t pool_slot, win_slot, n_tok, block = 0;
+    int32_t pos0;
+    bool fresh = false;
+    uint32_t group = blockIdx.y;
     if (jobs) {
-        job = jobs[blockIdx.x];
+        uint32_t j = blockIdx.x;
+        if (a.counts) {
+            // 1-D grid: every (fresh job, layer group) CTA first, so the host-link
+            // reads start at once and overlap the moves; then the moved jobs.
+            const uint32_t G = gridDim.y == 1 ? a.n_groups : 1;
+            const uint32_t half = a.fresh_offset * G;
+            const uint32_t idx = blockIdx.x;
+            if (idx < half) {
+                j = idx / G;
+                group = idx % G;
+                if (j >= a.counts[1]) return;
+                j += a.fresh_offset;
+                fresh = true;
+            } else {
+                j = (idx - half) / G;
+                group = (idx - half) % G;
+                if (j >= a.counts[0]) return;
+            }
+        }
+        const Job *jp = jobs + j;
+        pool_slot = jp->pool_slot;
+        win_slot = jp->win_slot;
+        pos0 = jp->pos0;
+        n_tok = jp->n_tok;
+        block = jp->block;
     } else {  // stateless form: chunk i of a contiguous run of rows
-        job.pool_slot = blockIdx.x;
-        job.win_slot = blockIdx.x;
-        job.pos0 = synth_pos0 + static_cast<int32_t>(blockIdx.x * g.block_tokens);
-        job.n_tok = min(g.block_tokens, synth_ntok - blockIdx.x * g.block_tokens);
+        pool_slot = blockIdx.x;
+        win_slot = blockIdx.x;
+        pos0 = synth_pos0 + static_cast<int32_t>(blockIdx.x * g.block_tokens);
+        n_tok = min(g.block_tokens, synth_ntok - blockIdx.x * g.block_tokens);
     }
-    build_rope_table<HALF>(tab, job.pos0, job.n_tok, theta, a.gtab);
+    build_rope_table<HALF>(tab, pos0, n_tok, theta, a.gtab);
     __syncthreads();
-    const uint32_t l0 = blockIdx.y * layers_per_cta;
+    const uint32_t l0 = group * layers_per_cta;
     const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
-    const uint8_t *slot = pool + static_cast<uint64_t>(job.pool_slot) * slot_bytes;
-    const uint64_t wk = static_cast<uint64_t>(job.win_slot) * g.block_tokens * g.k_row;
-    const uint64_t wv = static_cast<uint64_t>(job.win_slot) * g.block_tokens * g.v_row;
+    const uint8_t *slot = fresh ? a.repo + static_cast<uint64_t>(block) * slot_bytes
+                                : pool + static_cast<uint64_t>(pool_slot) * slot_bytes;
+    uint8_t *raw_slot = fresh ? a.pool_w + static_cast<uint64_t>(pool_slot) * slot_bytes : nullptr;
+    const uint64_t wk = static_cast<uint64_t>(win_slot) * g.block_tokens * g.k_row;
+    const uint64_t wv = static_cast<uint64_t>(win_slot) * g.block_tokens * g.v_row;
     for (uint32_t l = l0; l < l1; ++l) {
         const uint8_t *src = slot + static_cast<uint64_t>(l) * g.unit;
+        uint8_t *raw = raw_slot ? raw_slot + static_cast<uint64_t>(l) * g.unit : nullptr;
         uint8_t *dk = win_k + static_cast<uint64_t>(l) * g.win_k_layer + wk;
         if constexpr (!Q8) {
-            rope_rows_f16<D>(src, dk, tab, job.n_tok, g.n_head_kv);
+            if (raw)
+                rope_rows_f16<D, true>(src, dk, tab, n_tok, g.n_head_kv, raw);
+            else
+                rope_rows_f16<D, false>(src, dk, tab, n_tok, g.n_head_kv, nullptr);
         } else {
             uint8_t *stage = smem_raw + static_cast<size_t>(g.block_tokens) * HALF * sizeof(float2);
             const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
             const uint32_t nwarp = blockDim.x >> 5;
             const uint64_t head_bytes = (D / 32) * 34;
-            for (uint32_t t0 = 0; t0 < job.n_tok; t0 += kQ8ChunkTok) {
-                const uint32_t nt = min(static_cast<uint32_t>(kQ8ChunkTok), job.n_tok - t0);
-                copy16(src + t0 * g.k_row, stage, nt * g.k_row);
+            for (uint32_t t0 = 0; t0 < n_tok; t0 += kQ8ChunkTok) {
+                const uint32_t nt = min(static_cast<uint32_t>(kQ8ChunkTok), n_tok - t0);
+                if (raw)
+                    copy16_host(src + t0 * g.k_row, stage, raw + t0 * g.k_row, nt * g.k_row);
+                else
+                    copy16(src + t0 * g.k_row, stage, nt * g.k_row);
                 __syncthreads();
                 for (uint32_t r = warp; r < nt * g.n_head_kv; r += nwarp) {
                     const uint32_t tt = r / g.n_head_kv, h = r % g.n_head_kv;
@@ -405,9 +469,14 @@ __global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_cons
                 __syncthreads();
             }
         }
-        if (g.v_row)
-            copy16(src + g.unit_k, win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv,
-                   static_cast<uint64_t>(job.n_tok) * g.v_row);
+        if (g.v_row) {
+            uint8_t *dv = win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv;
+            const uint64_t vb = static_cast<uint64_t>(n_tok) * g.v_row;
+            if (raw)
+                copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb);
+            else
+                copy16(src + g.unit_k, dv, vb);
+        }
     }
 }
 
@@ -437,7 +506,10 @@ __global__ void append_summary_kernel(AppendArgs a, const float *__restrict__ ta
             __fmul_rn(s, inv);
         if (cnt < T) tail_out[static_cast<size_t>(l) * E + e] = s;
     }
-    if (l == 0 && threadIdx.x == 0) a.has_block[b] = 1;
+    if (l == 0 && threadIdx.x == 0) {
+        a.has_block[b] = 1;
+        if (a.blk_ntok) a.blk_ntok[b] = cnt;
+    }
 }
 
 // Repository rows: each (layer, token) K and V row goes to
@@ -509,6 +581,194 @@ __global__ void quantize_kernel(const uint16_t *__restrict__ x, uint8_t *__restr
     }
 }
 
+// ---------------------------------------------------------------------------
+// Device plan (one CTA). Every array index below derives from n_blocks,
+// win_slots and pool_slots, whose sizes the host checked against the buffers.
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
+    using Scan = cub::BlockScan<uint32_t, kPlanThreads>;
+    __shared__ typename Scan::TempStorage ts;
+    __shared__ uint32_t s_err, s_mtok, s_ftok;
+    extern __shared__ __align__(16) uint32_t psm[];
+    const uint32_t W = a.win_slots, P = a.pool_slots, tid = threadIdx.x;
+    uint32_t *s_ids = psm;
+    int32_t *s_base = reinterpret_cast<int32_t *>(psm + W);
+    uint32_t *s_ntok = psm + 2 * W;
+    int32_t *s_slot = reinterpret_cast<int32_t *>(psm + 3 * W);
+    uint32_t *s_flag = psm + 4 * W;  // bit 0: stage from the host, bit 1: needs a slot
+    uint32_t *s_free = psm + 5 * W;  // [P]
+    uint32_t *s_cu = psm + 5 * W + P;  // [P] eviction key: slot_used, ~0u if not a candidate
+    if (tid == 0) s_err = 0, s_mtok = 0, s_ftok = 0;
+
+    // 1. selected ids ascending with their chronological bases
+    const uint32_t n = a.n_blocks;
+    const uint32_t C = (n + kPlanThreads - 1) / kPlanThreads;
+    const uint32_t b0 = min(n, tid * C), b1 = min(n, b0 + C);
+    uint32_t cnt = 0, tok = 0;
+    for (uint32_t b = b0; b < b1; ++b)
+        if (a.sel[b]) ++cnt, tok += a.blk_ntok[b];
+    uint32_t pos, total, tpos, ttotal;
+    Scan(ts).ExclusiveSum(cnt, pos, total);
+    __syncthreads();
+    Scan(ts).ExclusiveSum(tok, tpos, ttotal);
+    __syncthreads();
+    for (uint32_t b = b0; b < b1; ++b)
+        if (a.sel[b]) {
+            if (pos < W) {
+                s_ids[pos] = b;
+                s_base[pos] = static_cast<int32_t>(tpos);
+                s_ntok[pos] = a.blk_ntok[b];
+            }
+            ++pos;
+            tpos += a.blk_ntok[b];
+        }
+    if (tid == 0 && total > W) s_err = 1;
+    const uint32_t n_sel = min(total, W);
+    __syncthreads();
+
+    // 2. without caching, blocks that left the selection give their slot back
+    if (!a.pool_cache)
+        for (uint32_t s = tid; s < P; s += kPlanThreads) {
+            const int32_t b = a.slot_blk[s];
+            if (b >= 0 && !a.sel[b]) {
+                a.slot_blk[s] = -1;
+                a.blk_slot[b] = -1;
+            }
+        }
+    __syncthreads();
+
+    // 3. which window blocks need their pool copy (re)staged, and a slot
+    const uint32_t Cw = (n_sel + kPlanThreads - 1) / kPlanThreads;
+    const uint32_t i0 = min(n_sel, tid * Cw), i1 = min(n_sel, i0 + Cw);
+    uint32_t need = 0;
+    for (uint32_t i = i0; i < i1; ++i) {
+        const int32_t sl = a.blk_slot[s_ids[i]];
+        uint32_t f = 0;
+        if (sl < 0) f = 3, ++need;
+        else if (a.slot_ntok[sl] != s_ntok[i]) f = 1;
+        s_slot[i] = sl;
+        s_flag[i] = f;
+    }
+    uint32_t need_rank, n_need;
+    Scan(ts).ExclusiveSum(need, need_rank, n_need);
+    __syncthreads();
+    const uint32_t Cp = (P + kPlanThreads - 1) / kPlanThreads;
+    const uint32_t p0 = min(P, tid * Cp), p1 = min(P, p0 + Cp);
+    uint32_t fc = 0;
+    for (uint32_t s = p0; s < p1; ++s) fc += a.slot_blk[s] < 0 ? 1u : 0u;
+    uint32_t frank, n_free;
+    Scan(ts).ExclusiveSum(fc, frank, n_free);
+    __syncthreads();
+    for (uint32_t s = p0; s < p1; ++s)
+        if (a.slot_blk[s] < 0) s_free[frank++] = s;
+    __syncthreads();
+    if (n_need > n_free) {  // cache mode: evict least recently used blocks outside the window
+        const uint32_t deficit = n_need - n_free;
+        // Candidates are pooled blocks outside the new window; their LRU key is
+        // staged in shared memory (~0u marks a non-candidate; slot_used never
+        // reaches it) so the exact rank below reads no global memory.
+        for (uint32_t s = tid; s < P; s += kPlanThreads) {
+            const int32_t b = a.slot_blk[s];
+            s_cu[s] = (b < 0 || a.sel[b]) ? 0xffffffffu : a.slot_used[s];
+        }
+        __syncthreads();
+        uint32_t n_cand_local = 0;
+        for (uint32_t s = tid; s < P; s += kPlanThreads) {
+            const uint32_t u = s_cu[s];
+            if (u == 0xffffffffu) continue;
+            ++n_cand_local;
+            uint32_t r = 0;
+            for (uint32_t s2 = 0; s2 < P; ++s2) {
+                const uint32_t u2 = s_cu[s2];
+                r += (u2 < u || (u2 == u && s2 < s)) ? 1u : 0u;
+            }
+            if (r < deficit) {
+                s_free[n_free + r] = s;
+                a.blk_slot[a.slot_blk[s]] = -1;
+            }
+        }
+        uint32_t n_cand;
+        uint32_t dummy;
+        Scan(ts).ExclusiveSum(n_cand_local, dummy, n_cand);
+        __syncthreads();
+        const uint32_t n_ev = min(deficit, n_cand);
+        for (uint32_t k = tid; k < n_ev; k += kPlanThreads) a.slot_blk[s_free[n_free + k]] = -1;
+        if (tid == 0 && n_cand < deficit) s_err |= 2;
+        n_free += n_ev;
+        __syncthreads();
+    }
+    for (uint32_t i = i0; i < i1; ++i)
+        if (s_flag[i] & 2) {
+            const uint32_t k = need_rank++;
+            if (k < n_free) {
+                const uint32_t s = s_free[k];
+                s_slot[i] = static_cast<int32_t>(s);
+                a.blk_slot[s_ids[i]] = static_cast<int32_t>(s);
+                a.slot_blk[s] = static_cast<int32_t>(s_ids[i]);
+            } else {
+                atomicOr(&s_err, 4u);
+            }
+        }
+    __syncthreads();
+
+    // 4. job lists and the new window
+    uint32_t mv = 0, fr = 0;
+    for (uint32_t i = i0; i < i1; ++i) {
+        const bool stage = s_flag[i] & 1;
+        const bool changed = a.win_id[i] != static_cast<int32_t>(s_ids[i]) ||
+                             a.win_base[i] != s_base[i] || a.win_ntok[i] != s_ntok[i];
+        fr += stage ? 1u : 0u;
+        mv += (!stage && changed) ? 1u : 0u;
+    }
+    uint32_t mrank, n_moved, frk, n_fresh;
+    Scan(ts).ExclusiveSum(mv, mrank, n_moved);
+    __syncthreads();
+    Scan(ts).ExclusiveSum(fr, frk, n_fresh);
+    __syncthreads();
+    for (uint32_t i = i0; i < i1; ++i) {
+        const bool stage = s_flag[i] & 1;
+        const bool changed = a.win_id[i] != static_cast<int32_t>(s_ids[i]) ||
+                             a.win_base[i] != s_base[i] || a.win_ntok[i] != s_ntok[i];
+        const int32_t sl = s_slot[i];
+        if (sl >= 0 && (stage || changed)) {
+            Job j{};
+            j.pool_slot = static_cast<uint32_t>(sl);
+            j.win_slot = i;
+            j.pos0 = s_base[i];
+            j.n_tok = s_ntok[i];
+            j.block = s_ids[i];
+            if (stage) {
+                a.jobs[W + frk++] = j;
+                a.slot_ntok[sl] = s_ntok[i];
+                atomicAdd(&s_ftok, s_ntok[i]);
+            } else {
+                a.jobs[mrank++] = j;
+                atomicAdd(&s_mtok, s_ntok[i]);
+            }
+        }
+        if (sl >= 0) a.slot_used[sl] = a.step;
+        a.win_id[i] = static_cast<int32_t>(s_ids[i]);
+        a.win_base[i] = s_base[i];
+        a.win_ntok[i] = s_ntok[i];
+        a.ids[i] = s_ids[i];
+    }
+    for (uint32_t i = n_sel + tid; i < W; i += kPlanThreads) {
+        a.win_id[i] = -1;
+        a.win_ntok[i] = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        a.counts[0] = n_moved;
+        a.counts[1] = n_fresh;
+        a.counts[2] = n_sel;
+        a.counts[3] = ttotal;
+        a.counts[4] = s_err;
+        a.counts[5] = s_mtok;
+        a.counts[6] = s_ftok;
+    }
+}
+
 __global__ void copy_ops_kernel(const CopyOp *__restrict__ ops, int n) {
     const int i = blockIdx.x;
     if (i >= n) return;
@@ -533,15 +793,22 @@ uint32_t layers_per_cta(uint32_t n_jobs, uint32_t n_layer) {
 
 template <int D, bool Q8>
 cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
-    const uint32_t lpc = layers_per_cta(n_jobs, a.g.n_layer);
-    const dim3 grid(n_jobs, (a.g.n_layer + lpc - 1) / lpc);
+    // With device counts the job total is unknown here; n_jobs is then the
+    // grid's upper bound and the layer split follows the layer count alone.
+    const uint32_t lpc = a.counts ? (a.g.n_layer <= 8 ? 1u : a.g.n_layer <= 16 ? 2u
+                                                      : a.g.n_layer <= 32 ? 4u : 8u)
+                                  : layers_per_cta(n_jobs, a.g.n_layer);
+    const uint32_t groups = (a.g.n_layer + lpc - 1) / lpc;
+    AsmLaunch al = a;
+    al.n_groups = groups;
+    const dim3 grid = a.counts ? dim3(n_jobs * groups, 1) : dim3(n_jobs, groups);
     size_t smem = static_cast<size_t>(a.g.block_tokens) * (D / 2) * sizeof(float2);
     if (Q8) smem += static_cast<size_t>(kQ8ChunkTok) * a.g.k_row;
     auto kfn = assemble_kernel<D, Q8>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kfn<<<grid, kAsmThreads, smem, st>>>(a, lpc);
+    kfn<<<grid, kAsmThreads, smem, st>>>(al, lpc);
     return cudaGetLastError();
 }
 
@@ -659,6 +926,19 @@ cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bo
     if (n_blocks == 0) return cudaSuccess;
     quantize_kernel<<<static_cast<unsigned>((n_blocks + 255) / 256), 256, 0, st>>>(x, y, n_blocks,
                                                                                    q8 ? 1 : 0);
+    return cudaGetLastError();
+}
+
+size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots) {
+    return (5ull * win_slots + 2ull * pool_slots) * sizeof(uint32_t);
+}
+
+cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st) {
+    const size_t smem = plan_smem_bytes(a.win_slots, a.pool_slots);
+    cudaError_t e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    plan_kernel<<<1, kPlanThreads, smem, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -7,16 +7,19 @@
 
 namespace kvmret {
 
-// One window-assembly job: rebuild window slot `win_slot` of every layer in
-// [layer_begin, layer_end) from HBM pool slot `pool_slot`, K rotated at
-// positions pos0 .. pos0 + n_tok - 1.
+// One window-assembly job: rebuild window slot `win_slot` of every layer from
+// HBM pool slot `pool_slot` (or, for a fresh block, from block `block` of the
+// mapped host repository, also filling the pool slot), K rotated at positions
+// pos0 .. pos0 + n_tok - 1.
 struct Job {
     uint32_t pool_slot;
     uint32_t win_slot;
     int32_t pos0;
     uint32_t n_tok;
+    uint32_t block;
+    uint32_t pad[3];
 };
-static_assert(sizeof(Job) == 16, "Job is 16 bytes");
+static_assert(sizeof(Job) == 32, "Job is 32 bytes");
 
 // RoPE frequencies theta_i = freq_base^(-2i/n_rot) * freq_scale, computed on
 // the host exactly as the reference's host RoPE does; passed by value.
@@ -77,6 +80,14 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
 // covering every window position.
 struct AsmLaunch {
     const Job *jobs;
+    // Device job counts {moved, fresh} written by the plan kernel (nullptr: the
+    // launch's n_jobs jobs are all moved jobs). Moved jobs sit at jobs[0..),
+    // fresh jobs at jobs[fresh_offset..); CTAs beyond the counts exit at once.
+    const uint32_t *counts;
+    uint32_t fresh_offset;
+    uint32_t n_groups;      // layer groups per job (set by the launcher)
+    const uint8_t *repo;    // device alias of the mapped pinned repository (fresh jobs)
+    uint8_t *pool_w;        // writable pool base (fresh jobs fill their slot)
     const uint8_t *pool;
     uint64_t slot_bytes;
     uint8_t *win_k;
@@ -88,6 +99,31 @@ struct AsmLaunch {
     AssembleGeom g;
 };
 cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st);
+
+// Device plan of one step (S7/S9-S11 physical part): from the selection flags,
+// the chronological window (ids ascending, bases = running token sums), the
+// HBM pool slots (release of blocks that left unless caching, LRU eviction,
+// allocation in slot order), the moved / fresh job lists, the window update,
+// and counts {n_moved, n_fresh, n_sel, window_tokens, error, moved_tokens,
+// fresh_tokens} plus the selected ids for the host.
+struct PlanArgs {
+    const uint8_t *sel;
+    const uint32_t *blk_ntok;
+    uint32_t n_blocks, win_slots, pool_slots, step;
+    int pool_cache;
+    int32_t *win_id;
+    int32_t *win_base;
+    uint32_t *win_ntok;
+    int32_t *blk_slot;
+    int32_t *slot_blk;
+    uint32_t *slot_ntok;
+    uint32_t *slot_used;
+    Job *jobs;          // [2 * win_slots]: moved, then fresh at + win_slots
+    uint32_t *counts;   // [8]
+    uint32_t *ids;      // [win_slots]
+};
+cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st);
+size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots);
 
 // cos/sin table of positions [0, n_pos) for the window (see AsmLaunch::gtab).
 cudaError_t launch_rope_table(float2 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
@@ -102,6 +138,7 @@ struct AppendArgs {
     uint32_t n_layer, n_head_kv, d_head, block_tokens, ncap;
     uint64_t k_row, v_row, unit_k, unit;
     float *summ;             // [L][Hkv][D][ncap]
+    uint32_t *blk_ntok;      // [ncap] tokens per block (kept current for the device plan)
     float *tail_sum;         // [L][E] running sum of the trailing partial block
     uint8_t *has_block;      // [ncap]
     uint8_t *repo_dev;       // device alias of the mapped pinned repository

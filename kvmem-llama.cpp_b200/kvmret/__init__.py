@@ -5,9 +5,13 @@ in libkvmret.so. There is no CPU fallback: importing this module raises if the
 library has not been built (``make -C kvmem-llama.cpp_b200/csrc``).
 
 Device buffers are passed as torch CUDA tensors (their data_ptr()). The
-library runs on its own CUDA stream; the wrapper synchronises torch's current
-stream before handing tensors over and the library stream before results are
-read back, so callers can mix both freely.
+library runs on its own CUDA stream. Around each call that reads or writes
+torch tensors the wrapper orders the two streams with events, no host
+synchronisation: the library stream first waits for torch's current stream
+(the inputs are ready), and afterwards torch's current stream waits for the
+library stream, so torch's caching allocator cannot hand a freed tensor's
+memory to later torch work before the library is done with it. Results read
+back through the C ABI wait for the library stream.
 """
 from __future__ import annotations
 
@@ -73,13 +77,10 @@ class StepStats(ctypes.Structure):
 class Prof(ctypes.Structure):
     _fields_ = [
         ("launches", ctypes.c_uint64), ("n_score", ctypes.c_uint32),
-        ("n_asm_moved", ctypes.c_uint32), ("n_asm_new", ctypes.c_uint32),
-        ("n_h2d", ctypes.c_uint32), ("dropped", ctypes.c_uint32),
-        ("score_ms", ctypes.c_double), ("asm_moved_ms", ctypes.c_double),
-        ("asm_new_ms", ctypes.c_double), ("h2d_ms", ctypes.c_double),
-        ("score_bytes", ctypes.c_uint64), ("asm_moved_bytes", ctypes.c_uint64),
-        ("asm_new_bytes", ctypes.c_uint64), ("h2d_bytes", ctypes.c_uint64),
-        ("n_gap", ctypes.c_uint32), ("gap_ms", ctypes.c_double),
+        ("n_asm", ctypes.c_uint32), ("dropped", ctypes.c_uint32),
+        ("score_ms", ctypes.c_double), ("asm_ms", ctypes.c_double),
+        ("score_bytes", ctypes.c_uint64), ("asm_hbm_bytes", ctypes.c_uint64),
+        ("asm_link_bytes", ctypes.c_uint64),
     ]
 
     def as_dict(self):
@@ -130,6 +131,8 @@ SIGNATURES = {
     "kvmret_apply_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.POINTER(StepStats)]),
     "kvmret_apply_retrieval": (ctypes.c_int, [_P, _PU32, _U32, _PU32, _PU32,
                                               ctypes.POINTER(StepStats)]),
+    "kvmret_select_apply_async": (ctypes.c_int, [_P, _PU32, _U32]),
+    "kvmret_step_collect": (ctypes.c_int, [_P, _PU32, _PU32, ctypes.POINTER(StepStats)]),
     "kvmret_last_plan": (ctypes.c_int, [_P, _PI32, _PU32, _PU32, _PU32, _PU32, _PU32]),
     "kvmret_window_k": (_P, [_P, _U32]),
     "kvmret_window_v": (_P, [_P, _U32]),
@@ -191,10 +194,36 @@ class Plan:
     stage_out: np.ndarray
 
 
-def _torch_sync():
+def _torch_stream(stream):
+    """The caller's stream, or torch's current stream when none is given."""
+    if stream:
+        return stream
     import torch
-    if torch.cuda.is_available():
-        torch.cuda.current_stream().synchronize()
+    return torch.cuda.current_stream().cuda_stream
+
+
+class _Ordered:
+    """Context manager: library stream after torch's current stream on entry,
+    torch's current stream after the library stream on exit."""
+
+    def __init__(self, stream_ptr: int):
+        self.ptr = stream_ptr
+
+    def __enter__(self):
+        import torch
+        self.ext = torch.cuda.ExternalStream(self.ptr)
+        self.cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(self.cur)
+        self.ext.wait_event(ev)
+        return self
+
+    def __exit__(self, *exc):
+        import torch
+        ev = torch.cuda.Event()
+        ev.record(self.ext)
+        self.cur.wait_event(ev)
+        return False
 
 
 class Retriever:
@@ -242,10 +271,10 @@ class Retriever:
         """k_cap: [L][n][E] f16 CUDA tensor; k_rows / v_rows: [L][n][row bytes] CUDA tensors."""
         n = int(k_cap.shape[1])
         pos0 = self.n_tokens if pos0 is None else pos0
-        _torch_sync()
-        _check(lib.kvmret_append(self.h, pos0, n, k_cap.data_ptr(),
-                                 None if k_rows is None else k_rows.data_ptr(),
-                                 v_rows.data_ptr()))
+        with _Ordered(self.stream_ptr):
+            _check(lib.kvmret_append(self.h, pos0, n, k_cap.data_ptr(),
+                                     None if k_rows is None else k_rows.data_ptr(),
+                                     v_rows.data_ptr()))
 
     def summaries(self) -> np.ndarray:
         out = np.zeros((self.n_blocks, self.cfg.n_layer, self.E), np.float32)
@@ -266,9 +295,9 @@ class Retriever:
     def query_add(self, q):
         """q: [L][n_rows][n_head*d_head] f16 or f32 CUDA tensor."""
         import torch
-        _torch_sync()
         fn = lib.kvmret_query_add_f16 if q.dtype == torch.float16 else lib.kvmret_query_add_f32
-        _check(fn(self.h, q.data_ptr(), int(q.shape[1])))
+        with _Ordered(self.stream_ptr):
+            _check(fn(self.h, q.data_ptr(), int(q.shape[1])))
 
     def query_set(self, q_sum: np.ndarray, q_count: np.ndarray):
         q_sum = np.ascontiguousarray(q_sum, np.float32)
@@ -297,15 +326,19 @@ class Retriever:
     def score_layers(self, contrib_out=None):
         """Exchange rows [n_layer][contrib_stride] f64 (terms + query flag in the last
         column) into a torch CUDA buffer, or the context's own buffer."""
-        _check(lib.kvmret_score_layers(self.h, None if contrib_out is None else
-                                       contrib_out.data_ptr()))
+        if contrib_out is None:
+            _check(lib.kvmret_score_layers(self.h, None))
+            return
+        with _Ordered(self.stream_ptr):
+            _check(lib.kvmret_score_layers(self.h, contrib_out.data_ptr()))
 
     @property
     def contrib_stride(self) -> int:
         return int(lib.kvmret_contrib_stride(self.h))
 
     def score_reduce(self, contrib_all, n_layer_all: int):
-        _check(lib.kvmret_score_reduce(self.h, contrib_all.data_ptr(), n_layer_all))
+        with _Ordered(self.stream_ptr):
+            _check(lib.kvmret_score_reduce(self.h, contrib_all.data_ptr(), n_layer_all))
 
     def prof_enable(self, on=True):
         _check(lib.kvmret_prof_enable(self.h, int(on)))
@@ -327,6 +360,20 @@ class Retriever:
         st = StepStats()
         _check(lib.kvmret_apply_selection(self.h, ap, len(a), ctypes.byref(st)))
         return st.as_dict()
+
+    def select_apply_async(self, mandatory=()):
+        """Top-k + device plan + assembly, enqueued without host synchronisation."""
+        m, mp = _u32(list(mandatory))
+        _check(lib.kvmret_select_apply_async(self.h, mp, len(m)))
+
+    def step_collect(self):
+        """Selection and stats of the oldest uncollected asynchronous step."""
+        ids = np.zeros(max(1, self.cfg.budget_blocks + self.cfg.reserve_blocks), np.uint32)
+        n = _U32(0)
+        st = StepStats()
+        _check(lib.kvmret_step_collect(self.h, ids.ctypes.data_as(_PU32), ctypes.byref(n),
+                                       ctypes.byref(st)))
+        return ids[: n.value].copy(), st.as_dict()
 
     def apply_retrieval(self, mandatory=()):
         m, mp = _u32(list(mandatory))
@@ -410,10 +457,9 @@ class Table:
 
 
 def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, stream=0):
-    """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors."""
-    _torch_sync()
+    """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors (torch's current stream)."""
     _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
-                               d_head, pos0, freq_base, freq_scale, stream or None))
+                               d_head, pos0, freq_base, freq_scale, _torch_stream(stream)))
 
 
 def quantize_f16(x, type_id, stream=0):
@@ -422,14 +468,13 @@ def quantize_f16(x, type_id, stream=0):
     n = x.numel()
     per = 34 if type_id == TYPE_Q8_0 else 18
     out = torch.empty(n // 32 * per, dtype=torch.uint8, device=x.device)
-    _torch_sync()
-    _check(lib.kvmret_quantize_f16(x.data_ptr(), out.data_ptr(), type_id, n, stream or None))
+    _check(lib.kvmret_quantize_f16(x.data_ptr(), out.data_ptr(), type_id, n,
+                                   _torch_stream(stream)))
     return out
 
 
 def rope_q8_0(k, out, n_tok, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, fwht_n=0,
               stream=0):
     """k, out: q8_0 rows [n_tok][n_head_kv*d_head/32*34] uint8 CUDA tensors."""
-    _torch_sync()
     _check(lib.kvmret_rope_q8_0(k.data_ptr(), out.data_ptr(), n_tok, n_head_kv, d_head, d_head,
-                                pos0, freq_base, freq_scale, fwht_n, stream or None))
+                                pos0, freq_base, freq_scale, fwht_n, _torch_stream(stream)))

@@ -137,3 +137,47 @@ def test_apply_retrieval_entry_point(hist1):
         assert len(ids) == w.budget_blocks
     _check_window(r, hist1, layers=[1])
     r.close()
+
+
+@pytest.mark.parametrize("pool_cache", [0, 1])
+def test_async_step_matches_preview_apply(hist1, pool_cache):
+    """score -> select_apply_async with the collect lagging one step behind (the
+    bench's loop) gives the same selections and byte-identical windows as
+    preview -> apply_selection."""
+    w = W1
+    a = kvmret.Retriever(config_for(w, pool_cache=pool_cache))
+    b = kvmret.Retriever(config_for(w, pool_cache=pool_cache))
+    append_history(a, hist1, cuts=[3000])
+    append_history(b, hist1, cuts=[])
+    qs = hist1.queries(8)
+    got_b = []
+    for s in range(len(qs)):
+        q = torch.from_numpy(qs[s].reshape(w.n_layer, 1, -1)).cuda()
+        a.query_reset()
+        a.query_add(q)
+        ids_a = a.preview()
+        a.apply(ids_a)
+        b.query_reset()
+        b.query_add(q)
+        b.score_layers()
+        kvmret._check(kvmret.lib.kvmret_score_reduce(b.h, kvmret.lib.kvmret_contrib_dev(b.h),
+                                                      w.n_layer))
+        b.select_apply_async()
+        if s > 0:
+            got_b.append(b.step_collect()[0])
+        got_a = ids_a
+        if s > 0:
+            assert list(got_b[-1]) == list(prev_a)
+        prev_a = got_a
+    got_b.append(b.step_collect()[0])
+    assert list(got_b[-1]) == list(prev_a)
+    la, ba = a.window_layout()
+    lb, bb = b.window_layout()
+    assert np.array_equal(la, lb) and np.array_equal(ba, bb)
+    for l in range(w.n_layer):
+        for is_v in (False, True):
+            assert np.array_equal(a.window_read(l, is_v, 0, len(la)),
+                                  b.window_read(l, is_v, 0, len(lb)))
+    assert np.array_equal(a.last_plan().remaps, b.last_plan().remaps)
+    a.close()
+    b.close()
