@@ -253,6 +253,11 @@ int kvmret_rope_f16(const uint16_t *k_dev, uint16_t *out_dev, uint32_t n_tok, ui
 int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* The same for q4_0 K rows (dequant_q4_0 / quant_q4_0,
+ * src/adapter/llama-kvmem-stagein.cu:145-158, 201-234). */
+int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
+                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                     float freq_scale, uint32_t fwht_n, void *stream);
 /* f16 values -> q8_0 / q4_0 blocks (n_elems a multiple of 32): the quantisers
  * of kvmem_stagein_quantize (src/adapter/llama-kvmem-stagein.cu:181-234,
  * 616-642), used to build quantised cache rows and repository bytes. */

@@ -106,7 +106,8 @@ struct kvmret_ctx {
     double *contrib = nullptr, *scores = nullptr;
     // device: window, pool and plan state
     uint8_t *pool = nullptr, *win_k = nullptr, *win_v = nullptr;
-    float2 *rope_tab = nullptr;  // cos/sin of every window position [pos][n_rot/2]
+    // cos/sin of every window position, [pos][n_rot/4] x {c_2j, c_2j+1, s_2j, s_2j+1}
+    float4 *rope_tab = nullptr;
     int32_t *d_win_id = nullptr, *d_win_base = nullptr, *d_blk_slot = nullptr,
             *d_slot_blk = nullptr;
     uint32_t *d_win_ntok = nullptr, *d_blk_ntok = nullptr, *d_slot_ntok = nullptr,
@@ -174,8 +175,9 @@ int validate(const kvmret_config &c) {
                     c.d_head);
     if (c.max_blocks == 0 || c.budget_blocks == 0)
         return fail(KVMRET_ERR_ARG, "max_blocks and budget_blocks must be > 0");
-    if (c.k_type != KVMRET_TYPE_F16 && c.k_type != KVMRET_TYPE_Q8_0)
-        return fail(KVMRET_ERR_ARG, "k_type %d unsupported (f16 or q8_0)", c.k_type);
+    if (c.k_type != KVMRET_TYPE_F16 && c.k_type != KVMRET_TYPE_Q8_0 &&
+        c.k_type != KVMRET_TYPE_Q4_0)
+        return fail(KVMRET_ERR_ARG, "k_type %d unsupported (f16, q8_0 or q4_0)", c.k_type);
     if (!type_ok(c.v_type)) return fail(KVMRET_ERR_ARG, "v_type %d unsupported", c.v_type);
     const uint64_t kr = kvmret_row_bytes(c.k_type, c.n_head_kv * c.d_head);
     const uint64_t vr = kvmret_row_bytes(c.v_type, c.n_head_kv * c.d_head);
@@ -311,7 +313,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     TRY(dmalloc(&c->jobs_dev, 2 * W * sizeof(Job)));
     TRY(dmalloc(&c->ops_dev, 8192 * sizeof(kvmret::CopyOp)));
     const uint32_t n_pos = c->win_slots * k.block_tokens;
-    TRY(dmalloc(&c->rope_tab, static_cast<size_t>(n_pos) * (k.n_rot / 2) * sizeof(float2)));
+    TRY(dmalloc(&c->rope_tab, static_cast<size_t>(n_pos) * (k.n_rot / 4) * sizeof(float4)));
     TRY(dmalloc(&c->d_win_id, W * sizeof(int32_t)));
     TRY(dmalloc(&c->d_win_base, W * sizeof(int32_t)));
     TRY(dmalloc(&c->d_win_ntok, W * sizeof(uint32_t)));
@@ -958,16 +960,17 @@ int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n
     return KVMRET_OK;
 }
 
-int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
-                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
-                     float freq_scale, uint32_t fwht_n, void *stream) {
+namespace {
+int rope_quant(int32_t type, const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
+               uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base, float freq_scale,
+               uint32_t fwht_n, void *stream) {
     if (!k || !out || n_head_kv == 0) return fail(KVMRET_ERR_ARG, "bad rope arguments");
     if ((d_head != 64 && d_head != 128 && d_head != 256) || n_rot != d_head)
         return fail(KVMRET_ERR_ARG, "rope needs d_head in {64,128,256} and n_rot == d_head");
     if (fwht_n != 0 && fwht_n != d_head)
         return fail(KVMRET_ERR_ARG, "fwht_n must be 0 or d_head");
-    const uint64_t row = kvmret_row_bytes(KVMRET_TYPE_Q8_0, n_head_kv * d_head);
-    if (row % 16) return fail(KVMRET_ERR_ARG, "q8_0 row of %llu bytes not 16-aligned",
+    const uint64_t row = kvmret_row_bytes(type, n_head_kv * d_head);
+    if (row % 16) return fail(KVMRET_ERR_ARG, "quantised K row of %llu bytes not 16-aligned",
                               (unsigned long long)row);
     if (n_tok == 0) return KVMRET_OK;
     kvmret::AssembleGeom g{};
@@ -976,19 +979,44 @@ int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_k
     g.d_head = d_head;
     g.block_tokens = 128;
     g.k_row = row;
-    g.k_type = KVMRET_TYPE_Q8_0;
+    g.k_type = type;
     g.fwht_n = fwht_n;
     g.fwht_scale = fwht_n ? 1.0f / std::sqrt(static_cast<float>(fwht_n)) : 0.0f;
     kvmret::AsmLaunch al{};
     al.pool = static_cast<const uint8_t *>(k);
     al.slot_bytes = 128 * row;
     al.win_k = static_cast<uint8_t *>(out);
-    al.synth_pos0 = pos0;
     al.synth_ntok = n_tok;
     al.theta = make_theta(n_rot, freq_base, freq_scale);
     al.g = g;
-    CK(kvmret::launch_assemble(al, (n_tok + 127) / 128, static_cast<cudaStream_t>(stream)));
+    // cos/sin of positions pos0 .. pos0 + n_tok - 1, indexed from 0
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float4 *tab = nullptr;
+    const size_t tab_bytes = static_cast<size_t>(n_tok) * (n_rot / 4) * sizeof(float4);
+    CK(cudaMallocAsync(reinterpret_cast<void **>(&tab), tab_bytes, st));
+    al.synth_pos0 = 0;
+    al.gtab = tab;
+    cudaError_t e = kvmret::launch_rope_table(tab, n_tok, n_rot / 2, al.theta, st, pos0);
+    if (e == cudaSuccess) e = kvmret::launch_assemble(al, (n_tok + 127) / 128, st);
+    const cudaError_t ef = cudaFreeAsync(tab, st);
+    CK(e);
+    CK(ef);
     return KVMRET_OK;
+}
+}  // namespace
+
+int kvmret_rope_q8_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
+                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                     float freq_scale, uint32_t fwht_n, void *stream) {
+    return rope_quant(KVMRET_TYPE_Q8_0, k, out, n_tok, n_head_kv, d_head, n_rot, pos0, freq_base,
+                      freq_scale, fwht_n, stream);
+}
+
+int kvmret_rope_q4_0(const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
+                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
+                     float freq_scale, uint32_t fwht_n, void *stream) {
+    return rope_quant(KVMRET_TYPE_Q4_0, k, out, n_tok, n_head_kv, d_head, n_rot, pos0, freq_base,
+                      freq_scale, fwht_n, stream);
 }
 
 int kvmret_quantize_f16(const uint16_t *src, void *dst, int32_t type, uint64_t n_elems,

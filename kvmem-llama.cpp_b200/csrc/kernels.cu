@@ -218,22 +218,33 @@ __device__ __forceinline__ float2 rope_cs(int32_t pos, float theta) {
 template <int HALF>
 __device__ __forceinline__ void build_rope_table(float2 *tab, int32_t pos0, uint32_t n_tok,
                                                  const float *__restrict__ theta,
-                                                 const float2 *__restrict__ gtab) {
+                                                 const float4 *__restrict__ gtab) {
     for (uint32_t idx = threadIdx.x; idx < n_tok * HALF; idx += blockDim.x) {
         const uint32_t t = idx / HALF, i = idx % HALF;
-        tab[t * HALF + tab_swz(i)] =
-            gtab ? gtab[static_cast<size_t>(pos0) * HALF + idx]
-                 : rope_cs(pos0 + static_cast<int32_t>(t), theta[i]);
+        float2 cs;
+        if (gtab) {
+            const float4 v = gtab[(static_cast<size_t>(pos0) + t) * (HALF / 2) + i / 2];
+            cs = (i & 1) ? make_float2(v.y, v.w) : make_float2(v.x, v.z);
+        } else {
+            cs = rope_cs(pos0 + static_cast<int32_t>(t), theta[i]);
+        }
+        tab[t * HALF + tab_swz(i)] = cs;
     }
 }
 
-// Context table: cs[pos][i] for pos in [0, n_pos).
-__global__ void rope_table_kernel(float2 *__restrict__ cs, uint32_t n_pos, uint32_t half,
-                                  const __grid_constant__ Theta th) {
-    const size_t n = static_cast<size_t>(n_pos) * half;
+// Position table: cs[p][j] = {c_2j, c_2j+1, s_2j, s_2j+1} of position
+// pos_base + p, for p in [0, n_pos).
+__global__ void rope_table_kernel(float4 *__restrict__ cs, uint32_t n_pos, uint32_t half,
+                                  int32_t pos_base, const __grid_constant__ Theta th) {
+    const uint32_t hp = half / 2;
+    const size_t n = static_cast<size_t>(n_pos) * hp;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < n;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x)
-        cs[idx] = rope_cs(static_cast<int32_t>(idx / half), th.v[idx % half]);
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int32_t pos = pos_base + static_cast<int32_t>(idx / hp);
+        const uint32_t j = static_cast<uint32_t>(idx % hp);
+        const float2 u = rope_cs(pos, th.v[2 * j]), v = rope_cs(pos, th.v[2 * j + 1]);
+        cs[idx] = make_float4(u.x, v.x, u.y, v.y);
+    }
 }
 
 // f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves.
@@ -279,125 +290,66 @@ __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
     }
 }
 
-// q8_0 K, one warp per (token, head) row held in shared memory, in place:
-// dequant (llama-kvmem-stagein.cu:133-143) -> RoPE -> FWHT (:105-131) ->
-// q8_0 (:181-199). Lane j holds elements EPL*j .. EPL*j + EPL - 1.
-template <int D>
-__device__ __forceinline__ void rope_row_q8(uint8_t *row, const float2 *tr, uint32_t lane,
-                                            uint32_t fwht_n, float fwht_scale) {
-    constexpr int EPL = D / 32, HALF = D / 2, LPB = 32 / EPL;  // lanes per q8 block
-    const uint32_t i0 = lane * EPL;
-    uint8_t *blk = row + (i0 / 32) * 34;
-    const uint32_t in_blk = i0 % 32;
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk));
-    float x[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e)
-        x[e] = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + in_blk + e])), d);
-    // RoPE: pair (i, i + D/2) sits in lanes (j, j ^ 16).
-    const bool low = lane < 16;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const uint32_t ii = (low ? i0 : i0 - HALF) + e;
-        const float2 cs = tr[tab_swz(ii)];
-        x[e] = low ? __fsub_rn(__fmul_rn(x[e], cs.x), __fmul_rn(other, cs.y))
-                   : __fadd_rn(__fmul_rn(other, cs.y), __fmul_rn(x[e], cs.x));
-    }
-    if (fwht_n) {
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) x[e] = __fmul_rn(x[e], fwht_scale);
-#pragma unroll
-        for (int h = 1; h < EPL; h *= 2) {
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                if (e & h) continue;
-                const float a = x[e], b = x[e + h];
-                x[e] = __fadd_rn(a, b);
-                x[e + h] = __fsub_rn(a, b);
-            }
-        }
-#pragma unroll
-        for (int hl = 1; hl < 32; hl *= 2) {  // element stride hl * EPL
-            const bool upper = lane & hl;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                const float p = __shfl_xor_sync(0xffffffffu, x[e], hl);
-                x[e] = upper ? __fsub_rn(p, x[e]) : __fadd_rn(x[e], p);
-            }
-        }
-    }
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(x[e]));
-#pragma unroll
-    for (int m = 1; m < LPB; m *= 2) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    const float dq = __fdiv_rn(amax, 127.0f);
-    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < EPL; ++e)
-        blk[2 + in_blk + e] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
-    if (in_blk == 0) *reinterpret_cast<uint16_t *>(blk) = f2h(dq);
-    __syncwarp();
-}
-
 // 16-byte vector copies by the whole CTA. copy16 reads through the read-only
-// global path (__ldg), so its source must be global memory; copy16_from_smem
-// is the shared-memory-source form.
+// global path (__ldg), so its source must be global memory; copy16_host
+// reads host memory (mapped pinned) with plain loads and writes one or two
+// destinations. Four loads are in flight per thread.
 __device__ __forceinline__ void copy16(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
                                        uint64_t nbytes) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
-    const uint64_t n = nbytes / 16;
-    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = __ldg(s + w);
+    const uint64_t n = nbytes / 16, step = blockDim.x;
+    uint64_t w = threadIdx.x;
+    for (; w + 3 * step < n; w += 4 * step) {
+        const uint4 v0 = __ldg(s + w), v1 = __ldg(s + w + step);
+        const uint4 v2 = __ldg(s + w + 2 * step), v3 = __ldg(s + w + 3 * step);
+        d[w] = v0;
+        d[w + step] = v1;
+        d[w + 2 * step] = v2;
+        d[w + 3 * step] = v3;
+    }
+    for (; w < n; w += step) d[w] = __ldg(s + w);
 }
-__device__ __forceinline__ void copy16_from_smem(const uint8_t *src, uint8_t *__restrict__ dst,
-                                                 uint64_t nbytes) {
-    const uint4 *s = reinterpret_cast<const uint4 *>(src);
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-    const uint64_t n = nbytes / 16;
-    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) d[w] = s[w];
-}
-// Host-memory source (plain loads), written to one or two destinations.
 __device__ __forceinline__ void copy16_host(const uint8_t *src, uint8_t *__restrict__ dst,
                                             uint8_t *__restrict__ dst2, uint64_t nbytes) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
     uint4 *d2 = reinterpret_cast<uint4 *>(dst2);
-    const uint64_t n = nbytes / 16;
-    for (uint64_t w = threadIdx.x; w < n; w += blockDim.x) {
+    const uint64_t n = nbytes / 16, step = blockDim.x;
+    uint64_t w = threadIdx.x;
+    for (; w + 3 * step < n; w += 4 * step) {
+        const uint4 v0 = s[w], v1 = s[w + step], v2 = s[w + 2 * step], v3 = s[w + 3 * step];
+        d[w] = v0;
+        d[w + step] = v1;
+        d[w + 2 * step] = v2;
+        d[w + 3 * step] = v3;
+        if (d2) {
+            d2[w] = v0;
+            d2[w + step] = v1;
+            d2[w + 2 * step] = v2;
+            d2[w + 3 * step] = v3;
+        }
+    }
+    for (; w < n; w += step) {
         const uint4 v = s[w];
         d[w] = v;
         if (d2) d2[w] = v;
     }
 }
 
-constexpr int kAsmThreads = 512;
-constexpr int kQ8ChunkTok = 16;
-
-// S10-S13: CTA = one job x a range of layers. K re-roped from the pool's
-// unrotated copy at the job's window base; V copied.
-template <int D, bool Q8>
-__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_constant__ AsmLaunch a,
-                                                               uint32_t layers_per_cta) {
-    const AssembleGeom &g = a.g;
-    const Job *__restrict__ jobs = a.jobs;
-    const uint8_t *__restrict__ pool = a.pool;
-    const uint64_t slot_bytes = a.slot_bytes;
-    uint8_t *__restrict__ win_k = a.win_k;
-    uint8_t *__restrict__ win_v = a.win_v;
-    const float *theta = a.theta.v;
-    const int32_t synth_pos0 = a.synth_pos0;
-    const uint32_t synth_ntok = a.synth_ntok;
-    constexpr int HALF = D / 2;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    float2 *tab = reinterpret_cast<float2 *>(smem_raw);
-    uint32_t pool_slot, win_slot, n_tok, block = 0;
+// One CTA's share of an assembly launch: which job, which layer group.
+struct JobView {
+    uint32_t pool_slot, win_slot, n_tok, block, group;
     int32_t pos0;
-    bool fresh = false;
-    uint32_t group = blockIdx.y;
-    if (jobs) {
+    bool fresh;
+};
+
+// Returns false when the CTA has no job (beyond the device counts).
+__device__ __forceinline__ bool decode_job(const AsmLaunch &a, JobView &v) {
+    v.group = blockIdx.y;
+    v.fresh = false;
+    v.block = 0;
+    if (a.jobs) {
         uint32_t j = blockIdx.x;
         if (a.counts) {
             // 1-D grid: every (fresh job, layer group) CTA first, so the host-link
@@ -407,77 +359,553 @@ __global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_cons
             const uint32_t idx = blockIdx.x;
             if (idx < half) {
                 j = idx / G;
-                group = idx % G;
-                if (j >= a.counts[1]) return;
+                v.group = idx % G;
+                if (j >= a.counts[1]) return false;
                 j += a.fresh_offset;
-                fresh = true;
+                v.fresh = true;
             } else {
                 j = (idx - half) / G;
-                group = (idx - half) % G;
-                if (j >= a.counts[0]) return;
+                v.group = (idx - half) % G;
+                if (j >= a.counts[0]) return false;
             }
         }
-        const Job *jp = jobs + j;
-        pool_slot = jp->pool_slot;
-        win_slot = jp->win_slot;
-        pos0 = jp->pos0;
-        n_tok = jp->n_tok;
-        block = jp->block;
+        const Job *jp = a.jobs + j;
+        v.pool_slot = jp->pool_slot;
+        v.win_slot = jp->win_slot;
+        v.pos0 = jp->pos0;
+        v.n_tok = jp->n_tok;
+        v.block = jp->block;
     } else {  // stateless form: chunk i of a contiguous run of rows
-        pool_slot = blockIdx.x;
-        win_slot = blockIdx.x;
-        pos0 = synth_pos0 + static_cast<int32_t>(blockIdx.x * g.block_tokens);
-        n_tok = min(g.block_tokens, synth_ntok - blockIdx.x * g.block_tokens);
+        v.pool_slot = blockIdx.x;
+        v.win_slot = blockIdx.x;
+        v.pos0 = a.synth_pos0 + static_cast<int32_t>(blockIdx.x * a.g.block_tokens);
+        v.n_tok = min(a.g.block_tokens, a.synth_ntok - blockIdx.x * a.g.block_tokens);
     }
-    build_rope_table<HALF>(tab, pos0, n_tok, theta, a.gtab);
+    return true;
+}
+
+constexpr int kAsmThreads = 512;
+
+// S10-S12, f16 K: CTA = one job x a range of layers. K re-roped from the
+// pool's unrotated copy at the job's window base; V copied.
+template <int D>
+__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_constant__ AsmLaunch a,
+                                                               uint32_t layers_per_cta) {
+    const AssembleGeom &g = a.g;
+    constexpr int HALF = D / 2;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    float2 *tab = reinterpret_cast<float2 *>(smem_raw);
+    JobView jv;
+    if (!decode_job(a, jv)) return;
+    build_rope_table<HALF>(tab, jv.pos0, jv.n_tok, a.theta.v, a.gtab);
     __syncthreads();
-    const uint32_t l0 = group * layers_per_cta;
+    const uint32_t l0 = jv.group * layers_per_cta;
     const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
-    const uint8_t *slot = fresh ? a.repo + static_cast<uint64_t>(block) * slot_bytes
-                                : pool + static_cast<uint64_t>(pool_slot) * slot_bytes;
-    uint8_t *raw_slot = fresh ? a.pool_w + static_cast<uint64_t>(pool_slot) * slot_bytes : nullptr;
-    const uint64_t wk = static_cast<uint64_t>(win_slot) * g.block_tokens * g.k_row;
-    const uint64_t wv = static_cast<uint64_t>(win_slot) * g.block_tokens * g.v_row;
+    const uint8_t *slot = jv.fresh ? a.repo + static_cast<uint64_t>(jv.block) * a.slot_bytes
+                                   : a.pool + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes;
+    uint8_t *raw_slot =
+        jv.fresh ? a.pool_w + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes : nullptr;
+    const uint64_t wk = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.k_row;
+    const uint64_t wv = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.v_row;
     for (uint32_t l = l0; l < l1; ++l) {
         const uint8_t *src = slot + static_cast<uint64_t>(l) * g.unit;
         uint8_t *raw = raw_slot ? raw_slot + static_cast<uint64_t>(l) * g.unit : nullptr;
-        uint8_t *dk = win_k + static_cast<uint64_t>(l) * g.win_k_layer + wk;
-        if constexpr (!Q8) {
-            if (raw)
-                rope_rows_f16<D, true>(src, dk, tab, n_tok, g.n_head_kv, raw);
-            else
-                rope_rows_f16<D, false>(src, dk, tab, n_tok, g.n_head_kv, nullptr);
-        } else {
-            uint8_t *stage = smem_raw + static_cast<size_t>(g.block_tokens) * HALF * sizeof(float2);
-            const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            const uint32_t nwarp = blockDim.x >> 5;
-            const uint64_t head_bytes = (D / 32) * 34;
-            for (uint32_t t0 = 0; t0 < n_tok; t0 += kQ8ChunkTok) {
-                const uint32_t nt = min(static_cast<uint32_t>(kQ8ChunkTok), n_tok - t0);
-                if (raw)
-                    copy16_host(src + t0 * g.k_row, stage, raw + t0 * g.k_row, nt * g.k_row);
-                else
-                    copy16(src + t0 * g.k_row, stage, nt * g.k_row);
-                __syncthreads();
-                for (uint32_t r = warp; r < nt * g.n_head_kv; r += nwarp) {
-                    const uint32_t tt = r / g.n_head_kv, h = r % g.n_head_kv;
-                    rope_row_q8<D>(stage + tt * g.k_row + h * head_bytes,
-                                   tab + (t0 + tt) * HALF, lane, g.fwht_n, g.fwht_scale);
-                }
-                __syncthreads();
-                copy16_from_smem(stage, dk + t0 * g.k_row, nt * g.k_row);
-                __syncthreads();
-            }
-        }
+        uint8_t *dk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer + wk;
+        if (raw)
+            rope_rows_f16<D, true>(src, dk, tab, jv.n_tok, g.n_head_kv, raw);
+        else
+            rope_rows_f16<D, false>(src, dk, tab, jv.n_tok, g.n_head_kv, nullptr);
         if (g.v_row) {
-            uint8_t *dv = win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv;
-            const uint64_t vb = static_cast<uint64_t>(n_tok) * g.v_row;
+            uint8_t *dv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv;
+            const uint64_t vb = static_cast<uint64_t>(jv.n_tok) * g.v_row;
             if (raw)
                 copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb);
             else
                 copy16(src + g.unit_k, dv, vb);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// S13, quantised K: dequant (llama-kvmem-stagein.cu:133-158) -> RoPE ->
+// FWHT (:105-131) -> requant (:181-234), per K head row of D elements.
+//
+// Register layout. A row is held by LPR = D/64 lanes; sub-lane q holds quant
+// block q (elements 32q .. 32q+31) in xl[] and block LPR+q (elements
+// D/2+32q ..) in xh[]. Every RoPE pair (i, i+D/2) and every quant block is
+// then inside one lane; of the FWHT's strides 1 .. D/2, the strides 1-16 and
+// D/2 run in registers and only 32 .. D/4 cross lanes (log2(LPR) shuffle
+// stages, none for D = 64). A warp holds 32/LPR rows, which is always 64
+// quant blocks: 2176 bytes of q8_0 or 1152 of q4_0 (one "segment").
+//
+// Data movement. Segments are contiguous in the pool and in the window. Each
+// warp streams its segments, and the V rows in segment-sized pieces, through
+// kQStages shared-memory stages with 16-byte cp.async copies (fresh jobs:
+// plain loads from the mapped host repository, also written to the pool
+// slot), converts K in place, and writes each piece back with 16-byte
+// stores. A K stage also receives the cos/sin rows of the tokens the
+// segment spans when they fit kQTabBytes.
+//
+// Byte access. Quant blocks (34 or 18 bytes) start at offsets that are 0 or 2
+// mod 4 (rows are 4-byte multiples); a block is read as whole 32-bit words
+// from the enclosing aligned word and realigned with byte permutes, and
+// written as whole words plus one 16-bit store at the unaligned end, so no
+// two lanes write the same byte.
+//
+// Arithmetic. Pairs of elements go through packed f32x2 operations, each of
+// which rounds both halves exactly like the scalar operation.
+template <int KT> struct QBlk;
+template <> struct QBlk<0> {  // q8_0 {f16 d; int8 q[32]}
+    static constexpr int bytes = 34, words = 8;
+};
+template <> struct QBlk<1> {  // q4_0 {f16 d; u8 q[16]: lo nibble j, hi nibble j+16}
+    static constexpr int bytes = 18, words = 4;
+};
+
+// Launch shape (tunable at build time): threads per CTA, pipeline stages per
+// warp, resident CTAs per SM the register allocation is sized for.
+#ifndef KVMRET_Q_THREADS
+#define KVMRET_Q_THREADS 256
+#endif
+#ifndef KVMRET_Q_STAGES
+#define KVMRET_Q_STAGES 4
+#endif
+#ifndef KVMRET_Q_MINB
+#define KVMRET_Q_MINB 2
+#endif
+constexpr int kQThreads = KVMRET_Q_THREADS;
+constexpr int kQStages = KVMRET_Q_STAGES;
+constexpr int kQSegBlocks = 64;   // quant blocks per warp segment
+constexpr int kQTabBytes = 1024;  // staged cos/sin bytes per K segment
+
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float a, float b) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(f32x2 r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// a * b + c with one rounding; used only with b = +-1, where it equals the
+// correctly rounded c + a or c - a.
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// round-half-away-from-zero (C roundf) for |y| < 2^23: truncate y + s, s =
+// copysign(0.5 - 2^-25, y) (the float just below one half). Exactness: for
+// |y| >= 1 the sum is exact or rounds only across the binade edge, where
+// truncation already gives the rounded value; for |y| < 1 the only
+// candidates for a wrong carry are the ties y = +-0.5 (sum 1 - 2^-25 rounds
+// to 1, as wanted) and y = +-(0.5 - 2^-25) (sum 1 - 2^-24, exact, truncates
+// to 0). Checked against the host roundf on every float of magnitude < 256.
+__device__ __forceinline__ float round_away(float y) {
+    return truncf(__fadd_rn(y, copysignf(0.49999997f, y)));
+}
+
+// Reads the quant block at byte offset o of a shared-memory segment: scale
+// bits and the payload as words (payload byte 4j+k = byte k of p[j]).
+template <int KT>
+__device__ __forceinline__ void load_qblock(const uint8_t *seg, uint32_t o, uint32_t &d16,
+                                            uint32_t (&p)[QBlk<KT>::words]) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(seg + (o & ~3u));
+    const bool odd = o & 2u;
+    uint32_t prev = w[0];
+    d16 = odd ? (prev >> 16) : (prev & 0xffffu);
+    const uint32_t sel = odd ? 0x7654u : 0x5432u;
+#pragma unroll
+    for (int j = 0; j < QBlk<KT>::words; ++j) {
+        const uint32_t nx = w[j + 1];
+        p[j] = __byte_perm(prev, nx, sel);
+        prev = nx;
+    }
+}
+
+template <int KT>
+__device__ __forceinline__ void store_qblock(uint8_t *seg, uint32_t o, uint32_t d16,
+                                             const uint32_t (&p)[QBlk<KT>::words]) {
+    constexpr int NW = QBlk<KT>::words;
+    const bool odd = o & 2u;
+    uint32_t *w = reinterpret_cast<uint32_t *>(seg + (odd ? o + 2 : o));
+    const uint32_t sel = odd ? 0x7654u : 0x5432u;
+    uint32_t prev = d16 << 16;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        w[k] = __byte_perm(prev, p[k], sel);
+        prev = p[k];
+    }
+    *reinterpret_cast<uint16_t *>(seg + (odd ? o : o + 4 * NW)) =
+        static_cast<uint16_t>(odd ? d16 : (p[NW - 1] >> 16));
+}
+
+// Float of a small integer from the low byte of a magic-biased word:
+// bits 0x4B0000xx are the float 2^23 + xx, exact.
+__device__ __forceinline__ float byte_float(uint32_t word, uint32_t k) {
+    return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u | k));
+}
+
+template <int KT>
+__device__ __forceinline__ void dequant_qblock(uint32_t d16, const uint32_t (&p)[QBlk<KT>::words],
+                                               float (&x)[32]) {
+    const float d = h2f(static_cast<uint16_t>(d16));
+    const f32x2 D2 = pk2(d, d);
+    if constexpr (KT == 0) {  // x = float(int8) * d
+        const f32x2 M2 = pk2(8388736.0f, 8388736.0f);  // 2^23 + 128
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t u = p[j] ^ 0x80808080u;  // int8 s -> s + 128
+#pragma unroll
+            for (int k = 0; k < 4; k += 2)
+                upk2(mul2(sub2(pk2(byte_float(u, k), byte_float(u, k + 1)), M2), D2),
+                     x[4 * j + k], x[4 * j + k + 1]);
+        }
+    } else {  // x = (nibble - 8) * d
+        const f32x2 M2 = pk2(8388616.0f, 8388616.0f);  // 2^23 + 8
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = p[j] & 0x0F0F0F0Fu, hi = (p[j] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                upk2(mul2(sub2(pk2(byte_float(lo, k), byte_float(lo, k + 1)), M2), D2),
+                     x[4 * j + k], x[4 * j + k + 1]);
+                upk2(mul2(sub2(pk2(byte_float(hi, k), byte_float(hi, k + 1)), M2), D2),
+                     x[16 + 4 * j + k], x[16 + 4 * j + k + 1]);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
+                                                   uint32_t b3) {
+    return __byte_perm(__byte_perm(b0, b1, 0x0040u), __byte_perm(b2, b3, 0x0040u), 0x5410u);
+}
+
+template <int KT>
+__device__ __forceinline__ void requant_qblock(const float (&x)[32], uint32_t &d16,
+                                               uint32_t (&p)[QBlk<KT>::words]) {
+    if constexpr (KT == 0) {  // quant_q8_0: d = amax / 127, q = round(x / d)
+        // max |x| by a tree (max is exact, so the order is free); the initial
+        // 0 of the sequential form is the last operand.
+        float m[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) m[e] = fmaxf(fabsf(x[e]), fabsf(x[e + 16]));
+#pragma unroll
+        for (int w = 8; w >= 1; w /= 2)
+#pragma unroll
+            for (int e = 0; e < w; ++e) m[e] = fmaxf(m[e], m[e + w]);
+        const float amax = fmaxf(0.0f, m[0]);
+        const float dq = __fdiv_rn(amax, 127.0f);
+        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        d16 = f2h(dq);
+        const f32x2 ID2 = pk2(id, id), M2 = pk2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint32_t b[4];
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                float y0, y1;
+                upk2(mul2(pk2(x[4 * j + k], x[4 * j + k + 1]), ID2), y0, y1);
+                // |round| <= 127: + 1.5 * 2^23 leaves it in the low byte
+                float z0, z1;
+                upk2(add2(pk2(round_away(y0), round_away(y1)), M2), z0, z1);
+                b[k] = __float_as_uint(z0);
+                b[k + 1] = __float_as_uint(z1);
+            }
+            p[j] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+        }
+    } else {  // quant_q4_0: d = vmax / -8 (vmax: first element of largest |x|)
+        float amax = 0.0f, vmax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const float a = fabsf(x[e]);
+            if (amax < a) {
+                amax = a;
+                vmax = x[e];
+            }
+        }
+        const float dq = __fdiv_rn(vmax, -8.0f);
+        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        d16 = f2h(dq);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t b[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = 4 * j + k;
+                const int x0 = min(__float2int_rz(__fadd_rn(__fmul_rn(x[i], id), 8.5f)), 15);
+                const int x1 = min(__float2int_rz(__fadd_rn(__fmul_rn(x[i + 16], id), 8.5f)), 15);
+                b[k] = static_cast<uint32_t>((x0 & 15) | ((x1 & 15) << 4));
+            }
+            p[j] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+        }
+    }
+}
+
+// In-lane butterflies of stride h (2 <= h <= 16) over one 32-element block,
+// two pairs per packed operation.
+template <int H>
+__device__ __forceinline__ void fwht_stage2(float (&x)[32]) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        if (e & H) continue;
+        const f32x2 a = pk2(x[e], x[e + 1]), b = pk2(x[e + H], x[e + H + 1]);
+        upk2(add2(a, b), x[e], x[e + 1]);
+        upk2(sub2(a, b), x[e + H], x[e + H + 1]);
+    }
+}
+
+// RoPE of a lane's 32 pairs from cos/sin pairs t4[0..15] = {c, c', s, s'}.
+__device__ __forceinline__ void rope_pairs(float (&xl)[32], float (&xh)[32], const float4 *t4) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        const float4 cs = t4[e / 2];
+        const f32x2 X0 = pk2(xl[e], xl[e + 1]), X1 = pk2(xh[e], xh[e + 1]);
+        const f32x2 C = pk2(cs.x, cs.y), S = pk2(cs.z, cs.w);
+        upk2(sub2(mul2(X0, C), mul2(X1, S)), xl[e], xl[e + 1]);
+        upk2(add2(mul2(X0, S), mul2(X1, C)), xh[e], xh[e + 1]);
+    }
+}
+
+// n / d for n * d < 2^32 (m = ceil(2^32 / d)).
+struct FastDiv {
+    uint64_t m;
+    __device__ explicit FastDiv(uint32_t d) : m((0x100000000ull + d - 1) / d) {}
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return static_cast<uint32_t>((static_cast<uint64_t>(n) * m) >> 32);
+    }
+};
+
+// Converts the rows of one K segment in place. The row of lane pair r is job
+// row row_base + r (token (row_base + r) / n_head_kv); its cos/sin pairs are
+// tab[(token - tab_tok0) * D/4 + j] (a staged shared-memory slice or the
+// position table).
+template <int D, int KT>
+__device__ __forceinline__ void convert_row(uint8_t *seg, uint32_t lane, uint32_t n_rows_seg,
+                                            uint32_t row_base, const FastDiv &hkv,
+                                            uint32_t n_rows, const float4 *tab,
+                                            uint32_t tab_tok0, uint32_t fwht_n,
+                                            float fwht_scale) {
+    constexpr int LPR = D / 64, BB = QBlk<KT>::bytes, NW = QBlk<KT>::words;
+    constexpr uint32_t HEAD_BYTES = (D / 32) * BB;
+    const uint32_t r = lane / LPR, q = lane % LPR;
+    const uint32_t R = min(row_base + r, n_rows - 1);  // idle lanes recompute a valid row
+    const uint32_t tok = hkv.div(R);
+    const uint32_t o_lo = r * HEAD_BYTES + BB * q;
+    const uint32_t o_hi = r * HEAD_BYTES + BB * (LPR + q);
+    float xl[32], xh[32];
+    {
+        uint32_t d16, p[NW];
+        load_qblock<KT>(seg, o_lo, d16, p);
+        dequant_qblock<KT>(d16, p, xl);
+        load_qblock<KT>(seg, o_hi, d16, p);
+        dequant_qblock<KT>(d16, p, xh);
+    }
+    // RoPE, pair (i, i + D/2) with i = 32q + e: (x0 c - x1 s, x0 s + x1 c).
+    rope_pairs(xl, xh, tab + (tok - tab_tok0) * (D / 4) + 16 * q);
+    if (fwht_n) {  // fwht_n == D: scale on input, then strides 1, 2, ..., D/2
+        const f32x2 sc = pk2(fwht_scale, fwht_scale);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+            upk2(mul2(pk2(xl[e], xl[e + 1]), sc), xl[e], xl[e + 1]);
+            upk2(mul2(pk2(xh[e], xh[e + 1]), sc), xh[e], xh[e + 1]);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+            float u = xl[e], v = xl[e + 1];
+            xl[e] = __fadd_rn(u, v);
+            xl[e + 1] = __fsub_rn(u, v);
+            u = xh[e];
+            v = xh[e + 1];
+            xh[e] = __fadd_rn(u, v);
+            xh[e + 1] = __fsub_rn(u, v);
+        }
+        fwht_stage2<2>(xl); fwht_stage2<2>(xh);
+        fwht_stage2<4>(xl); fwht_stage2<4>(xh);
+        fwht_stage2<8>(xl); fwht_stage2<8>(xh);
+        fwht_stage2<16>(xl); fwht_stage2<16>(xh);
+#pragma unroll
+        for (int m = 1; m < LPR; m *= 2) {  // stride 32m: partner sub-lane q ^ m
+            const float sg = (q & m) ? -1.0f : 1.0f;
+            const f32x2 S2 = pk2(sg, sg);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                const float pl0 = __shfl_xor_sync(0xffffffffu, xl[e], m);
+                const float pl1 = __shfl_xor_sync(0xffffffffu, xl[e + 1], m);
+                const float ph0 = __shfl_xor_sync(0xffffffffu, xh[e], m);
+                const float ph1 = __shfl_xor_sync(0xffffffffu, xh[e + 1], m);
+                upk2(fma2(pk2(xl[e], xl[e + 1]), S2, pk2(pl0, pl1)), xl[e], xl[e + 1]);
+                upk2(fma2(pk2(xh[e], xh[e + 1]), S2, pk2(ph0, ph1)), xh[e], xh[e + 1]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {  // stride D/2
+            const f32x2 u = pk2(xl[e], xl[e + 1]), v = pk2(xh[e], xh[e + 1]);
+            upk2(add2(u, v), xl[e], xl[e + 1]);
+            upk2(sub2(u, v), xh[e], xh[e + 1]);
+        }
+    }
+    uint32_t dl, dh, pl[NW], ph[NW];
+    requant_qblock<KT>(xl, dl, pl);
+    requant_qblock<KT>(xh, dh, ph);
+    __syncwarp();
+    if (r < n_rows_seg) {
+        store_qblock<KT>(seg, o_lo, dl, pl);
+        store_qblock<KT>(seg, o_hi, dh, ph);
+    }
+    __syncwarp();
+}
+
+__device__ __forceinline__ void cp_async16(uint8_t *smem_dst, const uint8_t *gsrc) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// A warp's walk over the CTA's work items: for each of its layers, the K
+// segments then the V pieces of the job's (block, layer) unit, dealt to the
+// warps round-robin. Advancing costs no division.
+struct ItemIter {
+    uint32_t l, s;  // layer, index within the layer's items
+    __device__ __forceinline__ void advance(uint32_t step, uint32_t per_layer) {
+        s += step;
+        while (s >= per_layer) {
+            s -= per_layer;
+            ++l;
+        }
+    }
+};
+
+template <int D, int KT>
+__global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
+    assemble_quant_kernel(const __grid_constant__ AsmLaunch a, uint32_t layers_per_cta) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
+    constexpr uint32_t STAGE = SEG + kQTabBytes;
+    constexpr uint32_t PAIRS = D / 4, TAB_TOK = kQTabBytes / (PAIRS * sizeof(float4));
+    constexpr uint32_t HEAD_BYTES = (D / 32) * QBlk<KT>::bytes;
+    constexpr uint32_t RPW = SEG / HEAD_BYTES;
+    const AssembleGeom &g = a.g;
+    JobView jv;
+    if (!decode_job(a, jv)) return;
+    const uint32_t l0 = jv.group * layers_per_cta;
+    const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
+    const bool fresh = jv.fresh;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    uint8_t *wbuf = smem_raw + static_cast<size_t>(warp) * kQStages * STAGE;
+    const uint8_t *slot = fresh ? a.repo + static_cast<uint64_t>(jv.block) * a.slot_bytes
+                                : a.pool + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes;
+    uint8_t *raw_slot =
+        fresh ? a.pool_w + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes : nullptr;
+    const uint32_t kbytes = jv.n_tok * static_cast<uint32_t>(g.k_row);
+    const uint32_t vbytes = jv.n_tok * static_cast<uint32_t>(g.v_row);
+    const uint32_t nseg_k = (kbytes + SEG - 1) / SEG;
+    const uint32_t per_layer = nseg_k + (vbytes + SEG - 1) / SEG;
+    const uint32_t n_rows = jv.n_tok * g.n_head_kv;
+    const FastDiv hkv(g.n_head_kv);
+    const uint64_t wk = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.k_row;
+    const uint64_t wv = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.v_row;
+    // the launcher always supplies a table for quantised K
+    const float4 *gtab_job = a.gtab + static_cast<size_t>(jv.pos0) * PAIRS;
+
+    // item fields: source, destination, byte count, rows and spanned tokens
+    auto src_of = [&](const ItemIter &x, uint32_t &off, uint32_t &bytes, bool &is_v) {
+        is_v = x.s >= nseg_k;
+        off = (is_v ? x.s - nseg_k : x.s) * SEG;
+        bytes = min(SEG, (is_v ? vbytes : kbytes) - off);
+        return slot + static_cast<uint64_t>(x.l) * g.unit + (is_v ? g.unit_k : 0) + off;
+    };
+    auto tokens = [&](uint32_t off, uint32_t &t0, uint32_t &nt) {
+        const uint32_t row_base = off / HEAD_BYTES;
+        t0 = hkv.div(row_base);
+        nt = hkv.div(min(row_base + RPW, n_rows) - 1) - t0 + 1;
+    };
+    if (per_layer == 0) return;
+    ItemIter cur{l0, 0}, pre{l0, 0};
+    cur.advance(warp, per_layer);
+    pre.advance(warp, per_layer);
+    auto issue = [&](uint32_t k) {  // prefetch this warp's k-th item into stage k % kQStages
+        if (pre.l < l1) {
+            uint32_t off, bytes, t0, nt;
+            bool is_v;
+            const uint8_t *src = src_of(pre, off, bytes, is_v);
+            uint8_t *dst = wbuf + (k % kQStages) * STAGE;
+            for (uint32_t c = lane; c < bytes / 16; c += 32) cp_async16(dst + 16 * c, src + 16 * c);
+            if (!is_v) {
+                tokens(off, t0, nt);
+                if (nt <= TAB_TOK) {
+                    const uint8_t *ts = reinterpret_cast<const uint8_t *>(gtab_job + t0 * PAIRS);
+                    for (uint32_t c = lane; c < nt * PAIRS; c += 32)
+                        cp_async16(dst + SEG + 16 * c, ts + 16 * c);
+                }
+            }
+            pre.advance(nwarp, per_layer);
+        }
+        cp_async_commit();
+    };
+    if (!fresh) {
+#pragma unroll
+        for (int k = 0; k < kQStages - 1; ++k) issue(k);
+    }
+    for (uint32_t k = 0; cur.l < l1; ++k, cur.advance(nwarp, per_layer)) {
+        uint32_t off, bytes, t0 = 0, nt = 0;
+        bool is_v;
+        const uint8_t *src = src_of(cur, off, bytes, is_v);
+        uint8_t *buf = wbuf + (k % kQStages) * STAGE;
+        if (fresh) {
+            const uint4 *sp = reinterpret_cast<const uint4 *>(src);
+            uint4 *rp = reinterpret_cast<uint4 *>(raw_slot + (src - slot));
+            uint4 *bp = reinterpret_cast<uint4 *>(buf);
+            for (uint32_t c = lane; c < bytes / 16; c += 32) {
+                const uint4 v = sp[c];
+                bp[c] = v;
+                rp[c] = v;
+            }
+            __syncwarp();
+        } else {
+            issue(k + kQStages - 1);
+            cp_async_wait<kQStages - 1>();
+            __syncwarp();
+        }
+        uint8_t *dst = is_v ? a.win_v + static_cast<uint64_t>(cur.l) * g.win_v_layer + wv + off
+                            : a.win_k + static_cast<uint64_t>(cur.l) * g.win_k_layer + wk + off;
+        if (!is_v) {
+            tokens(off, t0, nt);
+            const bool staged = !fresh && nt <= TAB_TOK;
+            const uint32_t row_base = off / HEAD_BYTES;
+            convert_row<D, KT>(buf, lane, min(RPW, n_rows - row_base), row_base, hkv, n_rows,
+                               staged ? reinterpret_cast<const float4 *>(buf + SEG) : gtab_job,
+                               staged ? t0 : 0u, g.fwht_n, g.fwht_scale);
+        }
+        uint4 *dp = reinterpret_cast<uint4 *>(dst);
+        const uint4 *bp = reinterpret_cast<const uint4 *>(buf);
+        for (uint32_t c = lane; c < bytes / 16; c += 32) dp[c] = bp[c];
+        __syncwarp();
+    }
+    if (!fresh) cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -791,24 +1219,44 @@ uint32_t layers_per_cta(uint32_t n_jobs, uint32_t n_layer) {
     return static_cast<uint32_t>(lpc < n_layer ? lpc : n_layer);
 }
 
-template <int D, bool Q8>
-cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
+uint32_t layers_per_cta_for(const AsmLaunch &a, uint32_t n_jobs) {
     // With device counts the job total is unknown here; n_jobs is then the
     // grid's upper bound and the layer split follows the layer count alone.
-    const uint32_t lpc = a.counts ? (a.g.n_layer <= 8 ? 1u : a.g.n_layer <= 16 ? 2u
-                                                      : a.g.n_layer <= 32 ? 4u : 8u)
-                                  : layers_per_cta(n_jobs, a.g.n_layer);
+    return a.counts ? (a.g.n_layer <= 8 ? 1u : a.g.n_layer <= 16 ? 2u
+                                             : a.g.n_layer <= 32 ? 4u : 8u)
+                    : layers_per_cta(n_jobs, a.g.n_layer);
+}
+
+template <int D>
+cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
+    const uint32_t lpc = layers_per_cta_for(a, n_jobs);
     const uint32_t groups = (a.g.n_layer + lpc - 1) / lpc;
     AsmLaunch al = a;
     al.n_groups = groups;
     const dim3 grid = a.counts ? dim3(n_jobs * groups, 1) : dim3(n_jobs, groups);
-    size_t smem = static_cast<size_t>(a.g.block_tokens) * (D / 2) * sizeof(float2);
-    if (Q8) smem += static_cast<size_t>(kQ8ChunkTok) * a.g.k_row;
-    auto kfn = assemble_kernel<D, Q8>;
+    const size_t smem = static_cast<size_t>(a.g.block_tokens) * (D / 2) * sizeof(float2);
+    auto kfn = assemble_kernel<D>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kfn<<<grid, kAsmThreads, smem, st>>>(al, lpc);
+    return cudaGetLastError();
+}
+
+template <int D, int KT>
+cudaError_t launch_assemble_quant_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
+    const uint32_t lpc = layers_per_cta_for(a, n_jobs);
+    const uint32_t groups = (a.g.n_layer + lpc - 1) / lpc;
+    AsmLaunch al = a;
+    al.n_groups = groups;
+    const dim3 grid = a.counts ? dim3(n_jobs * groups, 1) : dim3(n_jobs, groups);
+    const size_t smem = static_cast<size_t>(kQThreads / 32) * kQStages *
+                        (kQSegBlocks * QBlk<KT>::bytes + kQTabBytes);
+    auto kfn = assemble_quant_kernel<D, KT>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kfn<<<grid, kQThreads, smem, st>>>(al, lpc);
     return cudaGetLastError();
 }
 
@@ -881,22 +1329,25 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
 
 cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
     if (n_jobs == 0) return cudaSuccess;
-    const bool q8 = a.g.k_type == KVMRET_TYPE_Q8_0;
+    const bool q8 = a.g.k_type == KVMRET_TYPE_Q8_0, q4 = a.g.k_type == KVMRET_TYPE_Q4_0;
     switch (a.g.d_head) {
-    case 64: return q8 ? launch_assemble_t<64, true>(a, n_jobs, st)
-                       : launch_assemble_t<64, false>(a, n_jobs, st);
-    case 128: return q8 ? launch_assemble_t<128, true>(a, n_jobs, st)
-                        : launch_assemble_t<128, false>(a, n_jobs, st);
-    case 256: return q8 ? launch_assemble_t<256, true>(a, n_jobs, st)
-                        : launch_assemble_t<256, false>(a, n_jobs, st);
+    case 64: return q8 ? launch_assemble_quant_t<64, 0>(a, n_jobs, st)
+                  : q4 ? launch_assemble_quant_t<64, 1>(a, n_jobs, st)
+                       : launch_assemble_t<64>(a, n_jobs, st);
+    case 128: return q8 ? launch_assemble_quant_t<128, 0>(a, n_jobs, st)
+                   : q4 ? launch_assemble_quant_t<128, 1>(a, n_jobs, st)
+                        : launch_assemble_t<128>(a, n_jobs, st);
+    case 256: return q8 ? launch_assemble_quant_t<256, 0>(a, n_jobs, st)
+                   : q4 ? launch_assemble_quant_t<256, 1>(a, n_jobs, st)
+                        : launch_assemble_t<256>(a, n_jobs, st);
     default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_rope_table(float2 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
-                              cudaStream_t st) {
+cudaError_t launch_rope_table(float4 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
+                              cudaStream_t st, int32_t pos_base) {
     if (n_pos == 0) return cudaSuccess;
-    rope_table_kernel<<<1184, 256, 0, st>>>(cs, n_pos, half, th);
+    rope_table_kernel<<<1184, 256, 0, st>>>(cs, n_pos, half, pos_base, th);
     return cudaGetLastError();
 }
 

@@ -75,9 +75,10 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
 // S10-S13: window assembly from the HBM pool. One launch rebuilds n_jobs
 // window slots on every layer. With jobs == nullptr the jobs are synthesised:
 // job i covers tokens [i*T, min((i+1)*T, synth_ntok)) of a contiguous run,
-// pool slot i -> window slot i, positions from synth_pos0. gtab (may be null:
-// evaluate on the fly) is the context's cos/sin table [position][n_rot/2],
-// covering every window position.
+// pool slot i -> window slot i, positions from synth_pos0. gtab is the cos/sin
+// table, [position][n_rot/4] x {c_2j, c_2j+1, s_2j, s_2j+1}, covering every
+// position the launch uses (the f16 form may pass null: evaluate on the fly;
+// quantised K requires it).
 struct AsmLaunch {
     const Job *jobs;
     // Device job counts {moved, fresh} written by the plan kernel (nullptr: the
@@ -92,7 +93,7 @@ struct AsmLaunch {
     uint64_t slot_bytes;
     uint8_t *win_k;
     uint8_t *win_v;
-    const float2 *gtab;
+    const float4 *gtab;
     int32_t synth_pos0;
     uint32_t synth_ntok;
     Theta theta;
@@ -126,8 +127,8 @@ cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st);
 size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots);
 
 // cos/sin table of positions [0, n_pos) for the window (see AsmLaunch::gtab).
-cudaError_t launch_rope_table(float2 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
-                              cudaStream_t st);
+cudaError_t launch_rope_table(float4 *cs, uint32_t n_pos, uint32_t half, const Theta &th,
+                              cudaStream_t st, int32_t pos_base = 0);
 
 // S2 + S14: summaries of the appended tokens and the repository rows.
 struct AppendArgs {

@@ -143,6 +143,8 @@ SIGNATURES = {
                                        ctypes.c_float, _P]),
     "kvmret_rope_q8_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
                                         ctypes.c_float, _U32, _P]),
+    "kvmret_rope_q4_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
+                                        ctypes.c_float, _U32, _P]),
     "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
                                           ctypes.POINTER(_U64), ctypes.c_int]),
@@ -477,4 +479,11 @@ def rope_q8_0(k, out, n_tok, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=
               stream=0):
     """k, out: q8_0 rows [n_tok][n_head_kv*d_head/32*34] uint8 CUDA tensors."""
     _check(lib.kvmret_rope_q8_0(k.data_ptr(), out.data_ptr(), n_tok, n_head_kv, d_head, d_head,
+                                pos0, freq_base, freq_scale, fwht_n, _torch_stream(stream)))
+
+
+def rope_q4_0(k, out, n_tok, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, fwht_n=0,
+              stream=0):
+    """k, out: q4_0 rows [n_tok][n_head_kv*d_head/32*18] uint8 CUDA tensors."""
+    _check(lib.kvmret_rope_q4_0(k.data_ptr(), out.data_ptr(), n_tok, n_head_kv, d_head, d_head,
                                 pos0, freq_base, freq_scale, fwht_n, _torch_stream(stream)))

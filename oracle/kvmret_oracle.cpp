@@ -635,3 +635,18 @@ ORC_API void orc_rope_block_q8_0(const uint8_t *k_q8, uint32_t n_tok, uint32_t n
     if (fwht_n) orc_fwht(b.data(), n / fwht_n, fwht_n);
     orc_quant_q8_0(b.data(), out, n / 32);
 }
+
+// The same item path for q4_0 K (dequant_q4_0 / quant_q4_0, stagein.cu:145-158,
+// :201-234). k_q4: [n_tok][n_head*n_embd_head/32] q4_0 blocks.
+ORC_API void orc_rope_block_q4_0(const uint8_t *k_q4, uint32_t n_tok, uint32_t n_head,
+                                 uint32_t n_embd_head, uint32_t n_rot, int32_t pos0,
+                                 float freq_base, float freq_scale, uint32_t fwht_n,
+                                 uint8_t *out) {
+    const size_t n = static_cast<size_t>(n_tok) * n_head * n_embd_head;
+    std::vector<float> a(n), b(n);
+    orc_dequant_q4_0(k_q4, a.data(), n / 32);
+    orc_rope_neox(a.data(), n_tok, n_head, n_embd_head, n_rot, pos0, freq_base, freq_scale,
+                  b.data());
+    if (fwht_n) orc_fwht(b.data(), n / fwht_n, fwht_n);
+    orc_quant_q4_0(b.data(), out, n / 32);
+}

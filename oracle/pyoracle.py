@@ -62,6 +62,8 @@ def _load_orc():
         "orc_hadamard_rows": (None, [_PF, ctypes.c_uint64, _U32, _U32, _U32]),
         "orc_rope_block_q8_0": (None, [_PU8, _U32, _U32, _U32, _U32, ctypes.c_int32,
                                        ctypes.c_float, ctypes.c_float, _U32, _PU8]),
+        "orc_rope_block_q4_0": (None, [_PU8, _U32, _U32, _U32, _U32, ctypes.c_int32,
+                                       ctypes.c_float, ctypes.c_float, _U32, _PU8]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -281,6 +283,14 @@ def rope_block_q8_0(k_q8, n_tok, n_head, d_head, pos0, freq_base, freq_scale=1.0
     k = np.ascontiguousarray(k_q8, np.uint8)
     out = np.zeros_like(k)
     orc.orc_rope_block_q8_0(_ptr(k, _PU8), n_tok, n_head, d_head, d_head, pos0, freq_base,
+                            freq_scale, fwht_n, _ptr(out, _PU8))
+    return out
+
+
+def rope_block_q4_0(k_q4, n_tok, n_head, d_head, pos0, freq_base, freq_scale=1.0, fwht_n=0):
+    k = np.ascontiguousarray(k_q4, np.uint8)
+    out = np.zeros_like(k)
+    orc.orc_rope_block_q4_0(_ptr(k, _PU8), n_tok, n_head, d_head, d_head, pos0, freq_base,
                             freq_scale, fwht_n, _ptr(out, _PU8))
     return out
 

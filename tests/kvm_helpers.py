@@ -34,6 +34,17 @@ def q8_blocks_diff(a, b):
     return int(np.abs(qa - qb).max(initial=0)), int(f16_ulp_diff(da, db).max(initial=0))
 
 
+def q4_blocks_diff(a, b):
+    """(max nibble difference, max scale ulp difference) between q4_0 byte arrays."""
+    a = np.asarray(a, np.uint8).reshape(-1, 18)
+    b = np.asarray(b, np.uint8).reshape(-1, 18)
+    da = a[:, :2].copy().view(np.uint16).reshape(-1)
+    db = b[:, :2].copy().view(np.uint16).reshape(-1)
+    qa = np.concatenate([a[:, 2:] & 15, a[:, 2:] >> 4], 1).astype(np.int32)
+    qb = np.concatenate([b[:, 2:] & 15, b[:, 2:] >> 4], 1).astype(np.int32)
+    return int(np.abs(qa - qb).max(initial=0)), int(f16_ulp_diff(da, db).max(initial=0))
+
+
 def history_units(hist):
     """K/V of a NumpyHistory as [N][L][T][E] f16 (block, layer) units."""
     w = hist.w

@@ -1,5 +1,5 @@
-"""GPU parity beyond config 1: q8_0 K / q4_0 V windows (dequant -> RoPE ->
-FWHT -> requant within 1 LSB), other head geometries (d_head 64 / 256, no
+"""GPU parity beyond config 1: quantised K windows (q8_0 / q4_0 K, dequant ->
+RoPE -> FWHT -> requant within 1 LSB), other head geometries (d_head 64 / 256, no
 GQA, odd group sizes), layers without a query, ties under both tie rules,
 mandatory pinning, the stateless RoPE entry points and batched copies."""
 import ctypes
@@ -11,7 +11,7 @@ import torch
 import kvmret
 import pyoracle as po
 from kvm_helpers import (append_history, config_for, f16_ulp_diff, history_units,
-                         oracle_scores, q8_blocks_diff)
+                         oracle_scores, q4_blocks_diff, q8_blocks_diff)
 from kvmret import synth
 
 pytestmark = pytest.mark.gpu
@@ -24,17 +24,38 @@ def _quant_rows(fn, row_bytes):
     return f
 
 
-def test_q8_k_q4_v_window():
+_QROW = {kvmret.TYPE_Q8_0: (po.quant_q8_0, 34), kvmret.TYPE_Q4_0: (po.quant_q4_0, 18),
+         kvmret.TYPE_F16: (None, 64)}
+
+
+def _rows_fn(t, E):
+    fn, per = _QROW[t]
+    if fn is None:
+        return None, E * 2
+    return _quant_rows(fn, E // 32 * per), E // 32 * per
+
+
+@pytest.mark.parametrize("kt,vt", [(kvmret.TYPE_Q8_0, kvmret.TYPE_Q4_0),
+                                   (kvmret.TYPE_Q4_0, kvmret.TYPE_Q8_0),
+                                   (kvmret.TYPE_Q8_0, kvmret.TYPE_F16)])
+def test_quant_k_window(kt, vt):
+    """Window K for quantised K (dequant -> RoPE -> FWHT -> requant) within
+    1 LSB of the oracle, V bytes exact, over fresh and moved blocks."""
     w = synth.scaled(synth.CONFIGS[3], n_layer=2, n_blocks=48, budget_blocks=12,
-                     reserve_blocks=4, n_planted=4, n_head=16)
+                     reserve_blocks=4, n_planted=4, n_head=16, k_type=kt, v_type=vt)
     hist = synth.NumpyHistory(w)
     r = kvmret.Retriever(config_for(w))
-    kq = _quant_rows(po.quant_q8_0, 1088)
-    vq = _quant_rows(po.quant_q4_0, 576)
-    append_history(r, hist, cuts=[130, 3000], k_rows_fn=kq, v_rows_fn=vq)
     L, n, E = w.n_layer, w.n_tokens, w.E
-    k_q8 = kq(hist.k.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * 1088)
-    v_q4 = vq(hist.v.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * 576)
+    kq, krow = _rows_fn(kt, E)
+    vq, vrow = _rows_fn(vt, E)
+    append_history(r, hist, cuts=[130, 3000], k_rows_fn=kq, v_rows_fn=vq)
+    k_q = kq(hist.k.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * krow)
+    if vq is None:
+        v_b = hist.v.reshape(L, w.n_blocks, -1).view(np.uint8)
+    else:
+        v_b = vq(hist.v.reshape(L, n, E)).reshape(L, w.n_blocks, w.block_tokens * vrow)
+    rope = po.rope_block_q8_0 if kt == kvmret.TYPE_Q8_0 else po.rope_block_q4_0
+    diff = q8_blocks_diff if kt == kvmret.TYPE_Q8_0 else q4_blocks_diff
     q = hist.queries(3)
     worst_q, worst_d = 0, 0
     for s in range(3):
@@ -52,11 +73,11 @@ def test_q8_k_q4_v_window():
             wk = r.window_read(l, False, 0, len(lay_ids)).reshape(len(lay_ids), -1)
             wv = r.window_read(l, True, 0, len(lay_ids)).reshape(len(lay_ids), -1)
             for i, (b, base) in enumerate(zip(lay_ids, bases)):
-                want_k = po.rope_block_q8_0(k_q8[l, b], w.block_tokens, w.n_head_kv, w.d_head,
-                                            int(base), w.freq_base, fwht_n=128)
-                dq, dd = q8_blocks_diff(wk[i], want_k)
+                want_k = rope(k_q[l, b], w.block_tokens, w.n_head_kv, w.d_head, int(base),
+                              w.freq_base, fwht_n=128)
+                dq, dd = diff(wk[i], want_k)
                 worst_q, worst_d = max(worst_q, dq), max(worst_d, dd)
-                assert np.array_equal(wv[i], v_q4[l, b])
+                assert np.array_equal(wv[i], v_b[l, b])
     assert worst_q <= 1 and worst_d <= 1
     r.close()
 
@@ -127,7 +148,7 @@ def test_ties_follow_tie_rule(tie_higher):
     r.close()
 
 
-def test_stateless_rope_f16_and_q8():
+def test_stateless_rope_f16():
     rng = np.random.default_rng(3)
     n, hkv, d = 300, 8, 128
     x = rng.standard_normal((n, hkv, d)).astype(np.float16)
@@ -137,13 +158,28 @@ def test_stateless_rope_f16_and_q8():
     torch.cuda.synchronize()
     want = po.rope_block_f16(x.view(np.uint16), 12345, 1e6)
     assert f16_ulp_diff(out.cpu().numpy().view(np.uint16), want).max() <= 2
-    q8 = po.quant_q8_0(x.astype(np.float32)).reshape(n, -1)
-    kq = torch.from_numpy(q8).cuda()
-    oq = torch.empty_like(kq)
-    kvmret.rope_q8_0(kq, oq, n, 777, hkv, d, 1e6, fwht_n=128)
+
+
+# ragged token counts (partial warp segments, a partial last 128-token chunk),
+# every head size, FWHT on and off
+@pytest.mark.parametrize("qt", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("n,hkv,d,fwht", [(300, 8, 128, 128), (37, 2, 128, 0), (129, 4, 64, 64),
+                                          (70, 2, 256, 256), (5, 6, 256, 0)])
+def test_stateless_rope_quant(qt, n, hkv, d, fwht):
+    rng = np.random.default_rng(n + d)
+    x = (rng.standard_normal((n, hkv, d)) * 3).astype(np.float16)
+    if qt == "q8_0":
+        q = po.quant_q8_0(x.astype(np.float32)).reshape(n, -1)
+        fn, want_fn, diff = kvmret.rope_q8_0, po.rope_block_q8_0, q8_blocks_diff
+    else:
+        q = po.quant_q4_0(x.astype(np.float32)).reshape(n, -1)
+        fn, want_fn, diff = kvmret.rope_q4_0, po.rope_block_q4_0, q4_blocks_diff
+    kq = torch.from_numpy(q).cuda()
+    oq = torch.full_like(kq, 0xAB)
+    fn(kq, oq, n, 777, hkv, d, 1e6, fwht_n=fwht)
     torch.cuda.synchronize()
-    want8 = po.rope_block_q8_0(q8, n, hkv, d, 777, 1e6, fwht_n=128)
-    dq, dd = q8_blocks_diff(oq.cpu().numpy(), want8)
+    want = want_fn(q, n, hkv, d, 777, 1e6, fwht_n=fwht)
+    dq, dd = diff(oq.cpu().numpy(), want)
     assert dq <= 1 and dd <= 1
 
 
