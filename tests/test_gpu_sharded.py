@@ -53,17 +53,23 @@ def _rank(rank, world, port, out):
     c_all = torch.zeros(w.n_layer * stride, dtype=torch.float64, device="cuda")
     q = hist.queries(3)
     res = []
-    for s in range(3):
+    # the same three queries twice: through select + apply, then through the
+    # GPU-resident step (select_apply_async + step_collect)
+    for s in range(6):
         r.query_reset()
         r.query_add(torch.from_numpy(np.ascontiguousarray(
-            q[s].reshape(w.n_layer, 1, -1)[sl])).cuda())
+            q[s % 3].reshape(w.n_layer, 1, -1)[sl])).cuda())
         r.score_layers(c_loc)
         r.sync()
         dist.all_gather_into_tensor(c_all, c_loc)
         torch.cuda.synchronize()
         r.score_reduce(c_all, w.n_layer)
-        ids = r.select()
-        r.apply(ids)
+        if s < 3:
+            ids = r.select()
+            r.apply(ids)
+        else:
+            r.select_apply_async()
+            ids = r.step_collect()[0]
         lay, bases = r.window_layout()
         res.append((ids.tobytes(), lay.tobytes(), bases.tobytes()))
     out[rank] = res
@@ -91,8 +97,8 @@ def test_two_gpu_layer_sharded_selection_matches_oracle():
         assert p.exitcode == 0
     store = po.Store(w.block_tokens)
     store.append(w.n_tokens)
-    for s in range(3):
-        want, _ = oracle_scores(hist, q[s].reshape(w.n_layer, -1).astype(np.float32),
+    for s in range(6):
+        want, _ = oracle_scores(hist, q[s % 3].reshape(w.n_layer, -1).astype(np.float32),
                                 np.ones(w.n_layer, np.uint32))
         want_ids = po.pick_topk(want, w.budget_blocks, w.sink_blocks)
         _, _, rm, _ = store.set_selection(want_ids)
