@@ -347,6 +347,13 @@ def run_ours(args, w):
     r.sync()
     torch.cuda.synchronize()
     barrier()
+    if args.print_steps and rank == 0:
+        # per timed step: what the window assembly of that step moved (the
+        # algorithmic bytes of a launch a profiler captured)
+        for i, st in enumerate(stats):
+            print(f"step {i}: n_moved {st['n_moved']} n_h2d {st['n_h2d_blocks']} "
+                  f"assemble_bytes {st['assemble_bytes']} h2d_bytes {st['h2d_bytes']}",
+                  file=sys.stderr)
     prof = r.prof_read()
     r.prof_enable(False)
     timeline = None
@@ -422,6 +429,13 @@ def run_ours(args, w):
     t_roof = score_step / (hbm * 1e9) + max(h2d_step / (link * 1e9),
                                              (h2d_step + asm_step) / (hbm * 1e9))
     kv_bytes = score_step + h2d_step + asm_step
+    # DRAM traffic of one assembly launch: the ratio of ncu's dram read + write
+    # bytes to the launch's algorithmic bytes, measured on an 8-layer cut of
+    # the same workload (profiles/step_kernels_cfg2_l8.md: 1564.6 / 1585.4 MB;
+    # profiles/assemble_quant_kernel_cfg3_l8.md: 793.3 / 824.7 MB), scaled to
+    # this launch's algorithmic bytes (the traffic grows with the blocks moved).
+    traffic_ratio = (1564.6 / 1585.4) if w.k_type == kvmret.TYPE_F16 else (793.3 / 824.7)
+    asm_traffic = traffic_ratio * asm_hbm
 
     line = None
     if rank == 0:
@@ -441,11 +455,15 @@ def run_ours(args, w):
                 "l2": "inputs larger than L2 (summaries "
                       f"{score_step / 2**20:.0f} MiB/step, window/pool GiB-scale)",
                 "pool_cache": bool(args.pool_cache)},
-            "roofline": {"kernel": "assemble_kernel (window assembly: moved slots from the "
-                                   "HBM pool, fresh slots from the host repository)",
+            "roofline": {"kernel": ("assemble_kernel" if w.k_type == kvmret.TYPE_F16
+                                    else "assemble_quant_kernel")
+                                   + " (window assembly: moved slots from the HBM pool, "
+                                     "fresh slots from the host repository)",
                          "bound": "hbm" if asm_hbm / hbm >= asm_link / link else "host link",
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(asm_frac, 4), "traffic": None,
+                         "frac": round(asm_frac, 4), "traffic": int(asm_traffic),
+                         "traffic_source": "ncu dram bytes / algorithmic bytes of an 8-layer "
+                                           "capture, scaled to this launch",
                          "peak_source": peak_src,
                          "avg_launch_ms": round(asm_ms, 4),
                          "alg_hbm_bytes_per_launch": int(asm_hbm),
@@ -500,6 +518,8 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--print-steps", action="store_true",
+                    help="print each timed step's window-assembly counts to stderr (diagnostic)")
     ap.add_argument("--timeline", action="store_true",
                     help="record device events between the phases of each timed step (diagnostic)")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (dev only)")
