@@ -258,6 +258,25 @@ int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
 int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* ---- prefill scoring (an extension: the reference scores the MEAN query of a
+ *      span, src/adapter/llama-memory-kvmem.cpp:4149-4196; here every token of
+ *      a prefill chunk is scored) ----
+ * q_dev: [n_layer][n_tok][n_head * d_head] f16 pre-RoPE queries of the chunk.
+ * score(t, b) = mean over layers l and KV heads g of the cosine between the
+ * token's group query sum_{h in g} q[l][t][h] and block b's summary, computed
+ * from unit-length f16 operands on the tensor cores with f32 accumulation.
+ * sel_dev[max_blocks] receives 1 for every block in some token's top_k (by
+ * score, ties by the config's tie rule), else 0. scores_dev (optional):
+ * [n_tok][n_blocks] f32. n_sel_out (optional, host): number of selected blocks;
+ * passing it makes the call synchronous and reports a GEMM pipeline timeout. */
+int kvmret_prefill_score(kvmret_ctx *ctx, const uint16_t *q_dev, uint32_t n_tok, uint32_t top_k,
+                         uint8_t *sel_dev, float *scores_dev, uint32_t *n_sel_out);
+/* C = alpha * A * B^T on the tensor cores: A [m][k], B [n][k] f16 row-major,
+ * C [m][n] f32; m % 128 == 0, n % 256 == 0, k % 64 == 0, 16-byte aligned
+ * operands. err_dev (optional device word) is set to 1 if the kernel's
+ * pipeline gave up waiting. The prefill scorer's contraction. */
+int kvmret_gemm_f16_nt(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
+                       uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, void *stream);
 /* f16 values -> q8_0 / q4_0 blocks (n_elems a multiple of 32): the quantisers
  * of kvmem_stagein_quantize (src/adapter/llama-kvmem-stagein.cu:181-234,
  * 616-642), used to build quantised cache rows and repository bytes. */

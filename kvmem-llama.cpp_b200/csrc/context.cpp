@@ -23,6 +23,7 @@
 
 #include "kernels.cuh"
 #include "kvmret.h"
+#include "prefill.cuh"
 #include "table.hpp"
 
 using kvmret::Job;
@@ -114,6 +115,13 @@ struct kvmret_ctx {
              *d_slot_used = nullptr, *d_counts = nullptr, *d_ids = nullptr;
     Job *jobs_dev = nullptr;
     kvmret::CopyOp *ops_dev = nullptr;
+    // device: prefill scorer (allocated on first use). pf_a: unit group
+    // queries [pf_rows][K] f16; pf_b: unit summaries [pf_nrows][K] f16, rows
+    // below mhat_valid current; pf_s: scores [pf_rows][pf_nrows] f32.
+    uint16_t *pf_a = nullptr, *pf_b = nullptr;
+    float *pf_s = nullptr;
+    uint32_t *pf_err = nullptr;
+    uint32_t pf_rows = 0, pf_nrows = 0, mhat_valid = 0;
     // host
     uint8_t *repo_host = nullptr, *repo_dev = nullptr;
     uint8_t *pin_flags = nullptr;  // kept / selection flags staging
@@ -220,7 +228,8 @@ void free_all(kvmret_ctx *c) {
                    c->active, c->kept_dev, c->sel_dev, c->contrib, c->scores, c->pool,
                    c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab, c->d_win_id,
                    c->d_win_base, c->d_blk_slot, c->d_slot_blk, c->d_win_ntok, c->d_blk_ntok,
-                   c->d_slot_ntok, c->d_slot_used, c->d_counts, c->d_ids};
+                   c->d_slot_ntok, c->d_slot_used, c->d_counts, c->d_ids, c->pf_a, c->pf_b,
+                   c->pf_s, c->pf_err};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
@@ -683,6 +692,8 @@ int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *
     a.repo_dev = c->repo_dev;
     CK(kvmret::launch_append(a, c->st));
     c->prof.launches += 2;
+    // the prefill scorer's unit summaries of the touched blocks are stale now
+    c->mhat_valid = std::min(c->mhat_valid, pos0 / c->cfg.block_tokens);
     GUARD(c->table.append(n_tok));
     c->kept_valid = false;
     return KVMRET_OK;
@@ -1104,3 +1115,86 @@ int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Prefill scoring (an extension of score_retrieval, which scores the mean
+// query of a span, llama-memory-kvmem.cpp:4149-4196): every token of a chunk
+// against every block, per-token top-k, union.
+
+int kvmret_gemm_f16_nt(const uint16_t *a, const uint16_t *b, float *c, uint32_t m, uint32_t n,
+                       uint32_t k, float alpha, uint32_t *err, void *stream) {
+    if (!a || !b || !c) return fail(KVMRET_ERR_ARG, "null operand");
+    if (m % 128 || n % 256 || k % 64 || k == 0)
+        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
+    CUtensorMap ma, mb;
+    CK(kvmret::make_gemm_maps(a, b, m, n, k, &ma, &mb));
+    CK(kvmret::launch_gemm_f16_nt(ma, mb, c, m, n, k, alpha, err,
+                                  static_cast<cudaStream_t>(stream)));
+    return KVMRET_OK;
+}
+
+int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint32_t top_k,
+                         uint8_t *sel, float *scores, uint32_t *n_sel_out) {
+    NEED_CTX(c);
+    if (!q || !sel || n_tok == 0 || top_k == 0)
+        return fail(KVMRET_ERR_ARG, "prefill scoring needs q, sel, n_tok > 0, top_k > 0");
+    const uint32_t L = c->cfg.n_layer, Hkv = c->cfg.n_head_kv, D = c->cfg.d_head;
+    const uint32_t nb = c->table.n_blocks();
+    CK(cudaMemsetAsync(sel, 0, c->cfg.max_blocks, c->st));
+    if (nb == 0) {
+        if (n_sel_out) *n_sel_out = 0;
+        return KVMRET_OK;
+    }
+    const uint64_t K = static_cast<uint64_t>(L) * Hkv * D;
+    if (K % 64 || K > (1ull << 31)) return fail(KVMRET_ERR_ARG, "prefill K = %llu unsupported",
+                                               (unsigned long long)K);
+    const uint32_t rows = (n_tok + 127) / 128 * 128;
+    const uint32_t nrows = (c->ncap + 255) / 256 * 256;
+    if (!c->pf_b) {
+        TRY(dmalloc(&c->pf_b, static_cast<size_t>(nrows) * K * 2));
+        CK(cudaMemsetAsync(c->pf_b, 0, static_cast<size_t>(nrows) * K * 2, c->st));
+        TRY(dmalloc(&c->pf_err, 16));
+        CK(cudaMemsetAsync(c->pf_err, 0, 16, c->st));
+        c->pf_nrows = nrows;
+        c->mhat_valid = 0;
+    }
+    if (c->pf_rows < rows) {
+        if (c->pf_a) cudaFree(c->pf_a);
+        if (c->pf_s) cudaFree(c->pf_s);
+        c->pf_a = nullptr;
+        c->pf_s = nullptr;
+        c->pf_rows = 0;
+        TRY(dmalloc(&c->pf_a, static_cast<size_t>(rows) * K * 2));
+        TRY(dmalloc(&c->pf_s, static_cast<size_t>(rows) * nrows * sizeof(float)));
+        CK(cudaMemsetAsync(c->pf_a, 0, static_cast<size_t>(rows) * K * 2, c->st));
+        c->pf_rows = rows;
+    }
+    const uint32_t n_used = (nb + 255) / 256 * 256;
+    CK(kvmret::launch_mhat(c->summ, c->pf_b, L, Hkv, D, c->ncap, c->mhat_valid, nb, K, c->st));
+    c->mhat_valid = nb;
+    CK(kvmret::launch_qhat(q, c->pf_a, L, n_tok, c->cfg.n_head, Hkv, D, K, c->st));
+    CUtensorMap ma, mb;
+    CK(kvmret::make_gemm_maps(c->pf_a, c->pf_b, rows, n_used, static_cast<uint32_t>(K), &ma,
+                              &mb));
+    CK(kvmret::launch_gemm_f16_nt(ma, mb, c->pf_s, rows, n_used, static_cast<uint32_t>(K),
+                                  1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st));
+    CK(kvmret::launch_topk_union(c->pf_s, n_used, n_tok, nb, top_k, c->cfg.tie_higher_id, sel,
+                                 c->st));
+    c->prof.launches += 4;
+    if (scores)
+        CK(cudaMemcpy2DAsync(scores, static_cast<size_t>(nb) * sizeof(float), c->pf_s,
+                             static_cast<size_t>(n_used) * sizeof(float), nb * sizeof(float),
+                             n_tok, cudaMemcpyDeviceToDevice, c->st));
+    if (n_sel_out) {
+        std::vector<uint8_t> h(nb);
+        uint32_t err = 0;
+        CK(cudaMemcpyAsync(h.data(), sel, nb, cudaMemcpyDeviceToHost, c->st));
+        CK(cudaMemcpyAsync(&err, c->pf_err, sizeof(err), cudaMemcpyDeviceToHost, c->st));
+        CK(cudaStreamSynchronize(c->st));
+        if (err) return fail(KVMRET_ERR_CUDA, "tensor-core GEMM gave up waiting (pipeline stall)");
+        uint32_t n = 0;
+        for (uint8_t f : h) n += f != 0;
+        *n_sel_out = n;
+    }
+    return KVMRET_OK;
+}

@@ -1,0 +1,308 @@
+// Dense f16 GEMM on the sm_100a tensor cores (tcgen05), C = alpha * A * B^T
+// with A [M][K] and B [N][K] f16 row-major (both K-major) and C [M][N] f32.
+// It is the contraction of the prefill scorer (a chunk's normalised group
+// queries against every block's normalised summary, all layers and KV heads
+// stacked along K) and is exported on its own as kvmret_gemm_f16_nt.
+//
+// One CTA computes a 128 x 256 tile of C with the accumulator in tensor memory
+// (256 of the SM's 512 TMEM columns, f32). Warp roles:
+//   warp 0      TMA producer: 2-D tiled loads of A (128 x 64) and B (256 x 64)
+//               into a 4-stage shared-memory ring, 128-byte swizzle, no
+//               multicast; completion by mbarrier transaction counts;
+//   warp 1      allocates TMEM; one elected lane issues tcgen05.mma
+//               (kind::f16, M = 128, N = 256, K = 16; four per 64-wide stage)
+//               and commits each stage back to the producer, and the finished
+//               accumulator to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time (warp w
+//               reads TMEM lanes 32 * (w % 4) ..), scale, 16-byte stores.
+// Every mbarrier wait is bounded; on a timeout the CTA records an error in
+// *err, stops issuing, drains what it issued (bounded), frees its TMEM and
+// returns.
+#include "gemm_tc.cuh"
+
+#include <cuda_fp16.h>
+
+namespace kvmret {
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
+constexpr uint32_t kStageA = kTileM * kTileK * 2;  // 16 KiB
+constexpr uint32_t kStageB = kTileN * kTileK * 2;  // 32 KiB
+constexpr uint32_t kStageBytes = kStageA + kStageB;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint64_t kWaitNs = 2000000000ull;  // a pipeline wait gives up after 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase with the given parity to complete; gives up (false)
+// after kWaitNs of wall time.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (i == 0) {
+            t0 = global_ns();
+        } else if ((i & 63) == 0 && global_ns() - t0 > kWaitNs) {
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x,
+                                            int32_t y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle:
+// 8-row x 128-byte atoms stacked every 1024 bytes (stride byte offset), the
+// leading byte offset unused (1), descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: D f32, A and B f16, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
+                            (static_cast<uint32_t>(kTileM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_c, uint64_t da, uint64_t db,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            tmem_c),
+        "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+        " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+        " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31},"
+        " [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_f16_nt_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, float *__restrict__ c,
+                       uint32_t ldc, uint32_t n_ktiles, float alpha, uint32_t *err) {
+    extern __shared__ uint8_t smem_raw[];
+    // stages must start on 1024-byte boundaries (the swizzle atom)
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *const smem = smem_raw + (base - raw);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    // bars[0..S): stage full, bars[S..2S): stage empty, bars[2S]: accumulator ready
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 1);
+    __shared__ uint32_t s_fail;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t m0 = blockIdx.y * kTileM, n0 = blockIdx.x * kTileN;
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (kStages + s); };
+    const uint32_t acc_bar = bar0 + 8u * (2 * kStages);
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int s = 0; s < 2 * kStages + 1; ++s) mbar_init(bar0 + 8u * s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a))
+                     : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b))
+                     : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // producer
+            uint32_t k = 0;
+            for (; k < n_ktiles; ++k) {
+                const uint32_t s = k % kStages, round = k / kStages;
+                if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1u)) break;
+                if (*static_cast<volatile uint32_t *>(&s_fail)) break;
+                const uint32_t sa = base + s * kStageBytes;
+                mbar_expect_tx(full_bar(s), kStageBytes);
+                tma_load_2d(sa, &map_a, static_cast<int32_t>(k * kTileK),
+                            static_cast<int32_t>(m0), full_bar(s));
+                tma_load_2d(sa + kStageA, &map_b, static_cast<int32_t>(k * kTileK),
+                            static_cast<int32_t>(n0), full_bar(s));
+            }
+            if (k < n_ktiles) {  // gave up: drain the loads already issued (bounded)
+                atomicExch(&s_fail, 1u);
+                for (uint32_t j = (k > kStages ? k - kStages : 0); j < k; ++j)
+                    mbar_wait(full_bar(j % kStages), (j / kStages) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            uint32_t k = 0;
+            for (; k < n_ktiles; ++k) {
+                const uint32_t s = k % kStages;
+                if (!mbar_wait(full_bar(s), (k / kStages) & 1u)) break;
+                if (*static_cast<volatile uint32_t *>(&s_fail)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t sa = base + s * kStageBytes;
+                const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kStageA);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kTileK / 16; ++kk)  // +32 bytes per K = 16 slice
+                    mma_f16(tmem, da + 2 * kk, db + 2 * kk, (k | kk) != 0);
+                mma_commit(empty_bar(s));
+            }
+            if (k < n_ktiles) atomicExch(&s_fail, 1u);
+            mma_commit(acc_bar);  // arrives once every MMA issued above has completed
+        }
+    } else {  // epilogue, warps 2..5
+        const uint32_t q = warp & 3u;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0));
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok && !*static_cast<volatile uint32_t *>(&s_fail)) {
+            const uint32_t row = m0 + 32 * q + lane;
+            float *crow = c + static_cast<size_t>(row) * ldc + n0;
+#pragma unroll 1
+            for (uint32_t col = 0; col < kTileN; col += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((32 * q) << 16) + col, v);
+                float4 *dst = reinterpret_cast<float4 *>(crow + col);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    dst[j] = make_float4(alpha * __uint_as_float(v[4 * j]),
+                                         alpha * __uint_as_float(v[4 * j + 1]),
+                                         alpha * __uint_as_float(v[4 * j + 2]),
+                                         alpha * __uint_as_float(v[4 * j + 3]));
+            }
+        } else if (lane == 0) {
+            atomicExch(&s_fail, 1u);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && s_fail && err) atomicExch(err, 1u);
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 2-D f16 tensor {k, rows}, row stride k * 2 bytes, box {64, box_rows}, 128-byte swizzle.
+cudaError_t encode_kmajor(CUtensorMap *map, const void *base, uint32_t rows, uint32_t k,
+                          uint32_t box_rows) {
+    const EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {k, rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t make_gemm_maps(const void *a, const void *b, uint32_t m, uint32_t n, uint32_t k,
+                           CUtensorMap *map_a, CUtensorMap *map_b) {
+    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15)
+        return cudaErrorInvalidValue;
+    cudaError_t e = encode_kmajor(map_a, a, m, k, kTileM);
+    if (e == cudaSuccess) e = encode_kmajor(map_b, b, n, k, kTileN);
+    return e;
+}
+
+size_t gemm_smem_bytes() {
+    return kStages * static_cast<size_t>(kStageBytes) + 1024 /* alignment */ +
+           (2 * kStages + 1) * 8 + 16;
+}
+
+cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
+                               uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
+                               cudaStream_t st) {
+    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return cudaErrorInvalidValue;
+    const size_t smem = gemm_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(gemm_f16_nt_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    const dim3 grid(n / kTileN, m / kTileM);
+    gemm_f16_nt_kernel<<<grid, kGemmThreads, smem, st>>>(map_a, map_b, c, n, k / kTileK, alpha,
+                                                          err);
+    return cudaGetLastError();
+}
+
+}  // namespace kvmret

@@ -146,6 +146,9 @@ SIGNATURES = {
     "kvmret_rope_q4_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
                                         ctypes.c_float, _U32, _P]),
     "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
+    "kvmret_prefill_score": (ctypes.c_int, [_P, _P, _U32, _U32, _P, _P, _PU32]),
+    "kvmret_gemm_f16_nt": (ctypes.c_int, [_P, _P, _P, _U32, _U32, _U32, ctypes.c_float, _P,
+                                          _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
                                           ctypes.POINTER(_U64), ctypes.c_int]),
     "kvmret_score_noalloc": (ctypes.c_int, [_P, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _U32,
@@ -363,6 +366,26 @@ class Retriever:
         _check(lib.kvmret_apply_selection(self.h, ap, len(a), ctypes.byref(st)))
         return st.as_dict()
 
+    def prefill_score(self, q, top_k, scores=False):
+        """Per-token scores of a prefill chunk and the union of the per-token top_k.
+
+        q: [L][n_tok][n_head*d_head] f16 CUDA tensor. Returns (sel flags as a
+        uint8 numpy array over the blocks, number selected, scores [n_tok][n_blocks]
+        f32 numpy array or None)."""
+        import torch
+        n_tok = int(q.shape[1])
+        sel = torch.zeros(self.cfg.max_blocks, dtype=torch.uint8, device=q.device)
+        nb = int(lib.kvmret_n_blocks(self.h))
+        sc = torch.empty((n_tok, max(1, nb)), dtype=torch.float32, device=q.device) if scores \
+            else None
+        n = _U32(0)
+        with _Ordered(self.stream_ptr):
+            _check(lib.kvmret_prefill_score(self.h, q.data_ptr(), n_tok, top_k, sel.data_ptr(),
+                                            sc.data_ptr() if sc is not None else None,
+                                            ctypes.byref(n)))
+        return (sel.cpu().numpy()[:nb], n.value,
+                sc.cpu().numpy()[:, :nb] if sc is not None else None)
+
     def select_apply_async(self, mandatory=()):
         """Top-k + device plan + assembly, enqueued without host synchronisation."""
         m, mp = _u32(list(mandatory))
@@ -462,6 +485,19 @@ def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, str
     """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors (torch's current stream)."""
     _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
                                d_head, pos0, freq_base, freq_scale, _torch_stream(stream)))
+
+
+def gemm_f16_nt(a, b, alpha=1.0, stream=0):
+    """C = alpha * a @ b.T on the tensor cores; a [m][k], b [n][k] f16 CUDA tensors
+    (m % 128 == 0, n % 256 == 0, k % 64 == 0). Returns (C f32 CUDA tensor, error flag)."""
+    import torch
+    m, k = a.shape
+    n = b.shape[0]
+    c = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    err = torch.zeros(4, dtype=torch.int32, device=a.device)
+    _check(lib.kvmret_gemm_f16_nt(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, alpha,
+                                  err.data_ptr(), _torch_stream(stream)))
+    return c, err
 
 
 def quantize_f16(x, type_id, stream=0):

@@ -54,15 +54,17 @@ def history_units(hist):
     return k, v
 
 
-def append_history(r, hist, cuts, k_rows_fn=None, v_rows_fn=None):
-    """Append the history to a Retriever in chunks ending at token offsets `cuts`."""
+def append_history(r, hist, cuts, k_rows_fn=None, v_rows_fn=None, start=0, stop=None):
+    """Append tokens [start, stop) of the history (default: all) to a Retriever in
+    chunks ending at token offsets `cuts`."""
     import torch
     w = hist.w
     L, n, E = w.n_layer, w.n_tokens, w.E
     k = hist.k.reshape(L, n, E)
     v = hist.v.reshape(L, n, E)
-    t0 = 0
-    for t1 in list(cuts) + [n]:
+    t0 = start
+    stop = n if stop is None else stop
+    for t1 in [c for c in cuts if c < stop] + [stop]:
         if t1 <= t0:
             continue
         kc = torch.from_numpy(np.ascontiguousarray(k[:, t0:t1])).cuda()
