@@ -506,6 +506,139 @@ def run_ours(args, w):
         print(json.dumps(line), flush=True)
 
 
+def run_prefill(args, w):
+    """Config 4: one step = score a prefill chunk (every token against every block
+    summary on the tensor cores, per-token top-k, union), then append the
+    chunk's K/V (its completed blocks go to the pinned host repository, their
+    summaries are recomputed). 1 GPU."""
+    import numpy as np
+    import torch
+
+    import kvmret
+    from kvmret import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0 or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("config 4 runs on one GPU")
+    torch.cuda.set_device(0)
+    T, P, K = w.block_tokens, w.prefill_tokens, w.prefill_topk
+    n_steps = args.warmup + args.steps
+    blocks_cap = w.n_blocks + (n_steps + 6) * ((P + T - 1) // T)  # + the e2e steps
+    cfg = kvmret.default_config(
+        n_layer=w.n_layer, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head,
+        block_tokens=T, max_blocks=blocks_cap, budget_blocks=w.budget_blocks,
+        reserve_blocks=w.reserve_blocks, sink_blocks=w.sink_blocks, n_rot=w.d_head,
+        freq_base=w.freq_base, device=0)
+    t_setup = time.perf_counter()
+    r = kvmret.Retriever(cfg)
+    hist = synth.TorchHistory(w, 0)
+    for t0 in range(0, w.n_tokens, 64 * T):
+        kc, vc = hist.chunk(t0, min(64 * T, w.n_tokens - t0))
+        r.append(kc, vc, pos0=t0)
+        r.sync()
+        del kc, vc
+    # two prefill chunks resident in HBM: queries [L][P][Hq*D] (N(0,1) plus a
+    # share of the planted direction) and the chunk's K / V rows
+    g = torch.Generator(device="cuda").manual_seed(w.seed + 11)
+    qs, kvs = [], []
+    for i in range(2):
+        q = torch.randn((w.n_layer, P, w.n_head * w.d_head), generator=g, device="cuda")
+        q.add_(0.3 * hist.q0.float().reshape(w.n_layer, 1, -1))
+        qs.append(q.half())
+        kvs.append(hist.chunk(w.n_tokens + i * P, P))
+        del q
+    sel = torch.zeros(blocks_cap, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    t_setup = time.perf_counter() - t_setup
+    lib, h = kvmret.lib, r.h
+    ext = torch.cuda.ExternalStream(r.stream_ptr)
+    pos = [w.n_tokens]
+
+    def step(i, q_dev=None, k_dev=None, v_dev=None):
+        q_dev = qs[i % 2] if q_dev is None else q_dev
+        kc, vc = kvs[i % 2] if k_dev is None else (k_dev, v_dev)
+        kvmret._check(lib.kvmret_prefill_score(h, q_dev.data_ptr(), P, K, sel.data_ptr(), None,
+                                                None))
+        kvmret._check(lib.kvmret_append(h, pos[0], P, kc.data_ptr(), None, vc.data_ptr()))
+        pos[0] += P
+
+    clocks = Clocks(0)
+    time.sleep(0.6)
+    for i in range(args.warmup):
+        step(i)
+    r.sync()
+    r.prof_enable(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for i in range(args.steps):
+        step(i)
+    e1.record(ext)
+    r.sync()
+    torch.cuda.synchronize()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    prof = r.prof_read()
+    r.prof_enable(False)
+    n_union = int(sel[: int(lib.kvmret_n_blocks(h))].sum().item())
+    # e2e: the chunk's queries and K / V copied from pinned host memory each
+    # step, the union flags read back
+    qh = qs[0].cpu().pin_memory()
+    kh, vh = (x.cpu().pin_memory() for x in kvs[0])
+    qd, kd, vd = torch.empty_like(qs[0]), torch.empty_like(kvs[0][0]), torch.empty_like(kvs[0][1])
+    sel_h = torch.empty_like(sel, device="cpu").pin_memory()
+    e2e_steps = max(1, min(args.steps, 5))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        with kvmret._Ordered(r.stream_ptr):
+            step(i, qd, kd, vd)
+        torch.cuda.current_stream().wait_stream(ext)
+        sel_h.copy_(sel, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_us = (time.perf_counter() - t0) / e2e_steps * 1e6
+    clk = clocks.stop()
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    gemm_ms = prof["gemm_ms"] / max(1, prof["n_gemm"])
+    gemm_tf = prof["gemm_flops"] / max(1, prof["n_gemm"]) / (gemm_ms / 1e3) / 1e12 \
+        if gemm_ms > 0 else 0.0
+    link = link_gbps()
+    append_bytes = w.n_layer * P * 2 * w.E * 2  # K and V rows of the chunk into the repository
+    line = {
+        "metric": "prefill scoring + harvest us/step (config 4: 2048-token chunk x 2048 block "
+                  "summaries x 64 layers, per-token top-256 union, append of 16 blocks x 64 "
+                  "layers)",
+        "value": round(ms_step * 1e3, 1), "unit": "us/step", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
+        "data": "synthetic: seeded N(0,1) x LogNormal channel scale history with "
+                f"{w.n_planted} planted blocks; N(0,1) + 0.3 q0 chunk queries",
+        "config": {"workload": f"{w.name}: {w.n_layer} layers, {w.n_head}q/{w.n_head_kv}kv, "
+                               f"d{w.d_head}, {w.n_blocks} blocks + {P}-token chunks, top-{K}",
+                   "l2": "inputs larger than L2 (2 GiB of chunk queries per step)"},
+        "roofline": {"kernel": "gemm_f16_nt_kernel (tcgen05, TMEM accumulator)",
+                     "bound": "tensor", "achieved": round(gemm_tf, 1), "peak": tc_peak,
+                     "unit": "TFLOP/s", "frac": round(gemm_tf / tc_peak, 4), "traffic": None,
+                     "peak_source": "measured bf16_tflops (burst)" if peaks else "fallback",
+                     "avg_launch_ms": round(gemm_ms, 4),
+                     "alg_flops_per_launch": prof["gemm_flops"] / max(1, prof["n_gemm"])},
+        "step_roofline": {"append_bytes": append_bytes, "link_gbs_measured": round(link, 2),
+                          "t_append_link_us": round(append_bytes / (link * 1e9) * 1e6, 1),
+                          "frac": round(append_bytes / (link * 1e9) / (ms_step / 1e3), 4)},
+        "union_blocks_last_step": n_union,
+        "e2e": {"value": round(e2e_us, 1), "unit": "us/step",
+                "h2d_bytes_per_step": int(qs[0].numel() * 2 + 2 * kvs[0][0].numel() * 2),
+                "d2h_bytes_per_step": int(sel.numel())},
+        "gpu_launches": int(prof["launches"]), "clocks": clk,
+        "setup_s": round(t_setup, 1),
+    }
+    r.close()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -541,6 +674,8 @@ def main():
         w = synth.scaled(w, reserve_blocks=args.reserve)
     if args.impl == "reference":
         run_reference(args, w)
+    elif w.prefill_tokens:
+        run_prefill(args, w)
     else:
         run_ours(args, w)
 

@@ -234,6 +234,9 @@ typedef struct kvmret_prof {
     uint64_t score_bytes;     /* summary bytes the scoring read */
     uint64_t asm_hbm_bytes;   /* HBM bytes the assemblies read + wrote (collected steps) */
     uint64_t asm_link_bytes;  /* host-link bytes fresh slots read (collected steps) */
+    uint32_t n_gemm, pad_;    /* timed prefill-scorer GEMM launches */
+    double gemm_ms;           /* prefill-scorer tensor-core GEMM */
+    double gemm_flops;        /* its algorithmic FLOPs (2 * tokens * blocks * K) */
 } kvmret_prof;
 /* Reset the counters and turn event timing on (1) or off (0). */
 int kvmret_prof_enable(kvmret_ctx *ctx, int on);

@@ -83,7 +83,7 @@ uint32_t hadamard_nrot_k(uint32_t d_head) {
 
 constexpr int kRing = 4;          // readback slots (steps in flight before a collect)
 constexpr size_t kEventPool = 8192;
-enum { PR_SCORE = 0, PR_ASM };
+enum { PR_SCORE = 0, PR_ASM, PR_GEMM };
 
 }  // namespace
 
@@ -820,6 +820,9 @@ int kvmret_prof_read(kvmret_ctx *c, kvmret_prof *out) {
         if (r.kind == PR_SCORE) {
             c->prof.score_ms += ms;
             ++c->prof.n_score;
+        } else if (r.kind == PR_GEMM) {
+            c->prof.gemm_ms += ms;
+            ++c->prof.n_gemm;
         } else {
             c->prof.asm_ms += ms;
             ++c->prof.n_asm;
@@ -1176,8 +1179,11 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     CUtensorMap ma, mb;
     CK(kvmret::make_gemm_maps(c->pf_a, c->pf_b, rows, n_used, static_cast<uint32_t>(K), &ma,
                               &mb));
+    const int pr = prof_begin(c, c->st, PR_GEMM);
     CK(kvmret::launch_gemm_f16_nt(ma, mb, c->pf_s, rows, n_used, static_cast<uint32_t>(K),
                                   1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st));
+    prof_end(c, c->st, pr);
+    if (c->prof_on) c->prof.gemm_flops += 2.0 * n_tok * nb * static_cast<double>(K);
     CK(kvmret::launch_topk_union(c->pf_s, n_used, n_tok, nb, top_k, c->cfg.tie_higher_id, sel,
                                  c->st));
     c->prof.launches += 4;

@@ -80,7 +80,9 @@ class Prof(ctypes.Structure):
         ("n_asm", ctypes.c_uint32), ("dropped", ctypes.c_uint32),
         ("score_ms", ctypes.c_double), ("asm_ms", ctypes.c_double),
         ("score_bytes", ctypes.c_uint64), ("asm_hbm_bytes", ctypes.c_uint64),
-        ("asm_link_bytes", ctypes.c_uint64),
+        ("asm_link_bytes", ctypes.c_uint64), ("n_gemm", ctypes.c_uint32),
+        ("pad_", ctypes.c_uint32), ("gemm_ms", ctypes.c_double),
+        ("gemm_flops", ctypes.c_double),
     ]
 
     def as_dict(self):

@@ -37,6 +37,8 @@ class Workload:
     steps: int = 100
     drift: float = 0.05
     seed: int = 1234
+    prefill_tokens: int = 0   # config 4: tokens per prefill chunk
+    prefill_topk: int = 0     # config 4: per-token top-k of the union
 
     @property
     def n_tokens(self):
@@ -64,6 +66,12 @@ CONFIGS = {
     3: Workload("cfg3", n_layer=64, n_head=64, n_head_kv=8, d_head=128, block_tokens=128,
                 n_blocks=2048, budget_blocks=256, sink_blocks=1, reserve_blocks=128,
                 n_planted=32, k_type=TYPE_Q8_0, v_type=TYPE_Q4_0, seed=1237),
+    # 4: prefill/harvest: a 2048-token chunk scored against the 2048 block
+    # summaries (tensor cores), per-token top-256 union, then the chunk's 16
+    # completed blocks per layer appended with their summaries.
+    4: Workload("cfg4", n_layer=64, n_head=64, n_head_kv=8, d_head=128, block_tokens=128,
+                n_blocks=2048, budget_blocks=256, sink_blocks=1, reserve_blocks=128,
+                n_planted=32, seed=1238, prefill_tokens=2048, prefill_topk=256),
 }
 
 
@@ -123,7 +131,12 @@ def torch_history_chunk(w: Workload, gen, scale, u, planted_mask, tok0: int, n_t
     k = torch.randn((L, n_tok, Hkv, D), generator=gen, device="cuda", dtype=torch.float32)
     k.mul_(scale[:, None])
     blk = (torch.arange(tok0, tok0 + n_tok, device="cuda") // T)
-    m = planted_mask[blk].to(torch.float32)[None, :, None, None]
+    # tokens past the planted mask's blocks (a prefill chunk beyond the
+    # history) are never planted
+    inb = blk < planted_mask.numel()
+    m = torch.zeros(n_tok, device="cuda", dtype=torch.float32)
+    m[inb] = planted_mask[blk[inb]].to(torch.float32)
+    m = m[None, :, None, None]
     k.add_(0.5 * m * u[:, None])
     v = torch.randn((L, n_tok, Hkv, D), generator=gen, device="cuda", dtype=torch.float32)
     return k.to(torch.float16).reshape(L, n_tok, Hkv * D), v.to(torch.float16).reshape(
