@@ -261,6 +261,27 @@ int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
 int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* ---- session lanes (config 5: several conversations per GPU, stepped
+ *      together; the reference keeps one KvMemStore per lane,
+ *      src/adapter/llama-memory-kvmem.cpp:1624-1714) ----
+ * A group of contexts on one device (same layer count and block capacity).
+ * Each lane's kernels run on the lane's own stream, forked from and joined to
+ * `stream`, so the lanes overlap on the GPU. The lanes' score terms share one
+ * exchange buffer, lane-major: rows_out [n_lanes][n_layer][kvmret_contrib_stride]. */
+typedef struct kvmret_lanes kvmret_lanes;
+int kvmret_lanes_create(kvmret_ctx *const *lanes, uint32_t n_lanes, kvmret_lanes **out);
+void kvmret_lanes_destroy(kvmret_lanes *g);
+/* Per-layer score terms of every lane's accumulated query (kvmret_score_layers per lane). */
+int kvmret_lanes_score_layers(kvmret_lanes *g, double *rows_out, void *stream);
+/* rows_all: [n_ranks][n_lanes][n_layer][stride], the all-gather of every rank's
+ * rows_out in layer order (n_ranks = 1: rows_out itself). Per lane: reduce over
+ * all n_ranks * n_layer layers, top-k (mandatory[i], n_mandatory[i]; both may be
+ * null), plan and window assembly, enqueued without host synchronisation;
+ * collect each lane with kvmret_step_collect. */
+int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uint32_t n_ranks,
+                                    const uint32_t *const *mandatory,
+                                    const uint32_t *n_mandatory, void *stream);
+
 /* ---- prefill scoring (an extension: the reference scores the MEAN query of a
  *      span, src/adapter/llama-memory-kvmem.cpp:4149-4196; here every token of
  *      a prefill chunk is scored) ----

@@ -1204,3 +1204,127 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     }
     return KVMRET_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Session lanes (config 5): one context per lane on the same device, stepped
+// together. Each lane's kernels run on its own stream, forked from and joined
+// to the caller's stream, so the lanes' scoring and window assembly overlap
+// on the GPU; the lanes' score terms share one exchange buffer, so a
+// layer-sharded group needs one collective per step for all lanes.
+
+struct kvmret_lanes {
+    std::vector<kvmret_ctx *> ctx;
+    uint32_t L_local = 0, cstride = 0;
+    cudaEvent_t fork = nullptr;
+    std::vector<cudaEvent_t> join;
+    double *scratch = nullptr;  // per lane [n_ranks * L_local][cstride], gathered rows
+    uint64_t scratch_rows = 0;
+};
+
+namespace {
+
+void lanes_free(kvmret_lanes *g) {
+    if (!g) return;
+    if (!g->ctx.empty() && g->ctx[0]->cfg.device >= 0) cudaSetDevice(g->ctx[0]->cfg.device);
+    for (kvmret_ctx *c : g->ctx) cudaStreamSynchronize(c->st);
+    if (g->scratch) cudaFree(g->scratch);
+    if (g->fork) cudaEventDestroy(g->fork);
+    for (cudaEvent_t e : g->join)
+        if (e) cudaEventDestroy(e);
+    delete g;
+}
+
+// fork: every lane stream waits for the caller's stream
+int lanes_fork(kvmret_lanes *g, cudaStream_t caller) {
+    CK(cudaEventRecord(g->fork, caller));
+    for (kvmret_ctx *c : g->ctx) CK(cudaStreamWaitEvent(c->st, g->fork, 0));
+    return KVMRET_OK;
+}
+// join: the caller's stream waits for every lane stream
+int lanes_join(kvmret_lanes *g, cudaStream_t caller) {
+    for (size_t i = 0; i < g->ctx.size(); ++i) {
+        CK(cudaEventRecord(g->join[i], g->ctx[i]->st));
+        CK(cudaStreamWaitEvent(caller, g->join[i], 0));
+    }
+    return KVMRET_OK;
+}
+
+}  // namespace
+
+int kvmret_lanes_create(kvmret_ctx *const *lanes, uint32_t n, kvmret_lanes **out) {
+    if (!lanes || n == 0 || !out) return fail(KVMRET_ERR_ARG, "need lanes and an output");
+    *out = nullptr;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!lanes[i]) return fail(KVMRET_ERR_ARG, "lane %u is null", i);
+        const kvmret_config &a = lanes[0]->cfg, &b = lanes[i]->cfg;
+        if (a.device != b.device || a.n_layer != b.n_layer || lanes[i]->cstride != lanes[0]->cstride)
+            return fail(KVMRET_ERR_ARG, "lane %u: device, layer count and block capacity must match",
+                        i);
+        for (uint32_t j = 0; j < i; ++j)
+            if (lanes[j] == lanes[i]) return fail(KVMRET_ERR_ARG, "lane %u repeated", i);
+    }
+    kvmret_lanes *g = new (std::nothrow) kvmret_lanes;
+    if (!g) return fail(KVMRET_ERR_NOMEM, "out of host memory");
+    g->ctx.assign(lanes, lanes + n);
+    g->L_local = lanes[0]->cfg.n_layer;
+    g->cstride = lanes[0]->cstride;
+    if (lanes[0]->cfg.device >= 0) cudaSetDevice(lanes[0]->cfg.device);
+    g->join.assign(n, nullptr);
+    cudaError_t e = cudaEventCreateWithFlags(&g->fork, cudaEventDisableTiming);
+    for (uint32_t i = 0; i < n && e == cudaSuccess; ++i)
+        e = cudaEventCreateWithFlags(&g->join[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        lanes_free(g);
+        return fail(KVMRET_ERR_CUDA, "event creation failed: %s", cudaGetErrorString(e));
+    }
+    *out = g;
+    return KVMRET_OK;
+}
+
+void kvmret_lanes_destroy(kvmret_lanes *g) { lanes_free(g); }
+
+int kvmret_lanes_score_layers(kvmret_lanes *g, double *rows_out, void *stream) {
+    if (!g || !rows_out) return fail(KVMRET_ERR_ARG, "bad lanes call");
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    TRY(lanes_fork(g, caller));
+    const uint64_t lane_rows = static_cast<uint64_t>(g->L_local) * g->cstride;
+    for (size_t i = 0; i < g->ctx.size(); ++i)
+        TRY(kvmret_score_layers(g->ctx[i], rows_out + i * lane_rows));
+    return lanes_join(g, caller);
+}
+
+int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uint32_t n_ranks,
+                                    const uint32_t *const *mandatory,
+                                    const uint32_t *n_mandatory, void *stream) {
+    if (!g || !rows_all || n_ranks == 0) return fail(KVMRET_ERR_ARG, "bad lanes call");
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    const uint32_t n = static_cast<uint32_t>(g->ctx.size());
+    const uint64_t lane_rows = static_cast<uint64_t>(g->L_local) * g->cstride;
+    const uint64_t need = static_cast<uint64_t>(n) * n_ranks * lane_rows;
+    if (n_ranks > 1 && g->scratch_rows < need) {
+        if (g->scratch) cudaFree(g->scratch);
+        g->scratch = nullptr;
+        g->scratch_rows = 0;
+        TRY(dmalloc(&g->scratch, need * sizeof(double)));
+        g->scratch_rows = need;
+    }
+    TRY(lanes_fork(g, caller));
+    for (uint32_t i = 0; i < n; ++i) {
+        kvmret_ctx *c = g->ctx[i];
+        const double *rows = rows_all + i * lane_rows;
+        if (n_ranks > 1) {
+            // rows_all is [rank][lane][L_local][cstride]: gather this lane's rows
+            // of every rank into [rank * L_local][cstride] (global layer order)
+            double *dst = g->scratch + static_cast<uint64_t>(i) * n_ranks * lane_rows;
+            CK(cudaMemcpy2DAsync(dst, lane_rows * sizeof(double), rows,
+                                 static_cast<size_t>(n) * lane_rows * sizeof(double),
+                                 lane_rows * sizeof(double), n_ranks, cudaMemcpyDeviceToDevice,
+                                 c->st));
+            rows = dst;
+        }
+        TRY(kvmret_score_reduce(c, rows, n_ranks * g->L_local));
+        const uint32_t nm = n_mandatory ? n_mandatory[i] : 0;
+        TRY(kvmret_select_apply_async(c, nm && mandatory ? mandatory[i] : nullptr, nm));
+    }
+    return lanes_join(g, caller);
+}

@@ -149,6 +149,11 @@ SIGNATURES = {
                                         ctypes.c_float, _U32, _P]),
     "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
     "kvmret_prefill_score": (ctypes.c_int, [_P, _P, _U32, _U32, _P, _P, _PU32]),
+    "kvmret_lanes_create": (ctypes.c_int, [ctypes.POINTER(_P), _U32, ctypes.POINTER(_P)]),
+    "kvmret_lanes_destroy": (None, [_P]),
+    "kvmret_lanes_score_layers": (ctypes.c_int, [_P, _P, _P]),
+    "kvmret_lanes_select_apply_async": (ctypes.c_int, [_P, _P, _U32, ctypes.POINTER(_PU32),
+                                                       _PU32, _P]),
     "kvmret_gemm_f16_nt": (ctypes.c_int, [_P, _P, _P, _U32, _U32, _U32, ctypes.c_float, _P,
                                           _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
@@ -487,6 +492,52 @@ def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, str
     """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors (torch's current stream)."""
     _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
                                d_head, pos0, freq_base, freq_scale, _torch_stream(stream)))
+
+
+class Lanes:
+    """Session lanes (one Retriever per lane, same device), stepped together.
+
+    rows buffers are lane-major f64 CUDA tensors: [n_lanes][n_layer][contrib_stride]
+    locally, [n_ranks][n_lanes][n_layer][contrib_stride] after an all-gather."""
+
+    def __init__(self, retrievers):
+        self.lanes = list(retrievers)
+        arr = (_P * len(self.lanes))(*[r.h for r in self.lanes])
+        h = _P()
+        _check(lib.kvmret_lanes_create(arr, len(self.lanes), ctypes.byref(h)))
+        self.h = h
+
+    @property
+    def rows_per_rank(self):
+        r = self.lanes[0]
+        return len(self.lanes) * r.cfg.n_layer * r.contrib_stride
+
+    def score_layers(self, rows_out, stream=0):
+        _check(lib.kvmret_lanes_score_layers(self.h, rows_out.data_ptr(), _torch_stream(stream)))
+
+    def select_apply_async(self, rows_all, n_ranks=1, mandatory=None, stream=0):
+        n = len(self.lanes)
+        keep = []
+        mp = nm = None
+        if mandatory is not None:
+            ptrs = (_PU32 * n)()
+            counts = (ctypes.c_uint32 * n)()
+            for i, m in enumerate(mandatory):
+                a, ap = _u32(list(m))
+                keep.append(a)
+                ptrs[i] = ap
+                counts[i] = len(a)
+            mp, nm = ptrs, counts
+        _check(lib.kvmret_lanes_select_apply_async(self.h, rows_all.data_ptr(), n_ranks, mp, nm,
+                                                    _torch_stream(stream)))
+
+    def collect(self):
+        return [r.step_collect() for r in self.lanes]
+
+    def close(self):
+        if self.h:
+            lib.kvmret_lanes_destroy(self.h)
+            self.h = None
 
 
 def gemm_f16_nt(a, b, alpha=1.0, stream=0):
