@@ -639,6 +639,206 @@ def run_prefill(args, w):
     print(json.dumps(line), flush=True)
 
 
+def host_mem_available():
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def run_lanes(args, w):
+    """Config 5: `w.lanes` session lanes per GPU, each its own history and
+    queries, layers split over the ranks; one step = every lane's query scored,
+    one exchange for all lanes (N > 1), then every lane's top-k, plan and window
+    assembly. The pinned host repositories of all lanes must fit the box's host
+    memory; the per-lane history is shortened to fit when it does not, and the
+    JSON line says so."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import kvmret
+    from kvmret import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    if w.n_layer % world:
+        raise SystemExit(f"{w.n_layer} layers do not split over {world} GPUs")
+    Ll = w.n_layer // world
+    layer0 = rank * Ll
+    T, NL = w.block_tokens, w.lanes
+    E = w.E
+    row = kvmret.row_bytes(w.k_type, E) + kvmret.row_bytes(w.v_type, E)
+    per_block = Ll * T * row
+    avail = host_mem_available() // max(1, local_world)
+    fit_blocks = int(0.75 * avail / (NL * per_block)) if avail else w.n_blocks
+    n_blocks = max(w.budget_blocks + w.reserve_blocks + 64, min(w.n_blocks, fit_blocks))
+    if world > 1:  # every rank must hold the same history length
+        t = torch.tensor([n_blocks], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        n_blocks = int(t.item())
+    wl = synth.scaled(w, n_blocks=n_blocks)
+    t_setup = time.perf_counter()
+    rs, hists = [], []
+    for lane in range(NL):
+        lw = synth.scaled(wl, seed=w.seed + 101 * lane)
+        cfg = kvmret.default_config(
+            n_layer=Ll, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head,
+            block_tokens=T, max_blocks=n_blocks, budget_blocks=w.budget_blocks,
+            reserve_blocks=w.reserve_blocks, sink_blocks=w.sink_blocks, k_type=w.k_type,
+            v_type=w.v_type, n_rot=w.d_head, freq_base=w.freq_base,
+            pool_cache=int(args.pool_cache), device=local)
+        r = kvmret.Retriever(cfg)
+        h = synth.TorchHistory(lw, local, layer0=layer0, n_layer=Ll)
+        for t0 in range(0, lw.n_tokens, 64 * T):
+            m = min(64 * T, lw.n_tokens - t0)
+            kc, vc = h.chunk(t0, m)
+            r.append(kc, kvmret.quantize_f16(vc, w.v_type), k_rows=kvmret.quantize_f16(
+                kc, w.k_type), pos0=t0)
+            r.sync()
+            del kc, vc
+        rs.append(r)
+        hists.append(h)
+    lanes = kvmret.Lanes(rs)
+    torch.cuda.synchronize()
+    t_setup = time.perf_counter() - t_setup
+    rows = torch.zeros(lanes.rows_per_rank, dtype=torch.float64, device="cuda")
+    rows_all = rows if world == 1 else torch.zeros(world * lanes.rows_per_rank,
+                                                  dtype=torch.float64, device="cuda")
+    cur = torch.cuda.current_stream()
+
+    def queries(n):
+        return [[h.next_query()[layer0:layer0 + Ll].contiguous() for h in hists]
+                for _ in range(n)]
+
+    def step(qs):
+        for r, q in zip(rs, qs):
+            r.query_reset()
+            r.query_add(q)
+        lanes.score_layers(rows, stream=cur.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(rows_all, rows)
+        lanes.select_apply_async(rows_all, world, stream=cur.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    clocks = Clocks(local)
+    time.sleep(0.6)
+    for qs in queries(args.warmup):
+        step(qs)
+        lanes.collect()
+    torch.cuda.synchronize()
+    qs_all = queries(args.steps)
+    for r in rs:
+        r.prof_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stats = []
+    e0.record(cur)
+    for i, qs in enumerate(qs_all):
+        step(qs)
+        if i > 0:
+            stats.append([st for _, st in lanes.collect()])
+    e1.record(cur)
+    stats.append([st for _, st in lanes.collect()])
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    profs = [r.prof_read() for r in rs]
+    # e2e: every lane's query copied from pinned host memory each step, the ids
+    # of the previous step read back on the host
+    qh = [[q.cpu().pin_memory() for q in qs] for qs in queries(args.steps)]
+    qd = [torch.empty_like(q) for q in qs_all[0]]
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i, qs in enumerate(qh):
+        for d, q in zip(qd, qs):
+            d.copy_(q, non_blocking=True)
+        step(qd)
+        if i > 0:
+            lanes.collect()
+    lanes.collect()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    hbm, peak_src = load_peaks()
+    link = link_gbps()
+    n_asm = sum(p["n_asm"] for p in profs)
+    asm_ms = sum(p["asm_ms"] for p in profs)
+    asm_hbm = sum(p["asm_hbm_bytes"] for p in profs)
+    asm_link = sum(p["asm_link_bytes"] for p in profs)
+    score_bytes = sum(p["score_bytes"] for p in profs) / max(1, args.steps)
+    asm_step = asm_hbm / max(1, args.steps)
+    link_step = asm_link / max(1, args.steps)
+    t_roof = score_bytes / (hbm * 1e9) + max(link_step / (link * 1e9),
+                                             (link_step + asm_step) / (hbm * 1e9))
+    line = None
+    if rank == 0:
+        line = {
+            "metric": "multi-lane retrieval+stage-in us/step (config 5: all lanes per step)",
+            "value": round(ms_step * 1e3, 1), "unit": "us/step", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q8_0/q4_0", "data": "synthetic: per-lane seeded histories and drifting "
+                                          "queries (config 2's distributions)",
+            "config": {"workload": f"{w.name}: {NL} lanes x {w.n_layer} layers, "
+                                   f"{w.n_head}q/{w.n_head_kv}kv, d{w.d_head}, budget "
+                                   f"{w.budget_blocks}, reserve {w.reserve_blocks}",
+                       "history_tokens_per_lane": n_blocks * T,
+                       "history_note": None if n_blocks >= w.n_blocks else
+                       f"shortened from {w.n_tokens} to fit the pinned repositories of "
+                       f"{NL} lanes into this box's host memory",
+                       "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}, "
+                                                            f"{NL} lanes per GPU"},
+            "roofline": {"kernel": "assemble_quant_kernel, all lanes", "bound": "hbm",
+                         "achieved": round(asm_hbm / (asm_ms / 1e3) / 1e9, 1) if asm_ms else 0,
+                         "peak": hbm, "unit": "GB/s",
+                         "frac": round(asm_hbm / (asm_ms / 1e3) / 1e9 / hbm, 4) if asm_ms
+                         else 0, "traffic": None, "peak_source": peak_src,
+                         "note": "per-lane launches overlap, so the summed launch time "
+                                 "exceeds the step's device time"},
+            "step_roofline": {"t_roof_us": round(t_roof * 1e6, 1),
+                              "frac": round(t_roof * 1e3 / ms_step, 4),
+                              "B_sum": int(score_bytes), "B_link": int(link_step),
+                              "B_asm": int(asm_step), "link_gbs_measured": round(link, 2)},
+            "e2e": {"value": round(e2e_s / args.steps * 1e6, 1), "unit": "us/step",
+                    "h2d_bytes_per_step": int(sum(q.numel() * 2 for q in qd)),
+                    "d2h_bytes_per_step": int(NL * 4 * (w.budget_blocks + w.reserve_blocks))},
+            "gpu_launches": int(sum(p["launches"] for p in profs)),
+            "clocks": clk, "setup_s": round(t_setup, 1),
+        }
+    lanes.close()
+    for r in rs:
+        r.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -676,6 +876,8 @@ def main():
         run_reference(args, w)
     elif w.prefill_tokens:
         run_prefill(args, w)
+    elif w.lanes:
+        run_lanes(args, w)
     else:
         run_ours(args, w)
 

@@ -39,6 +39,7 @@ class Workload:
     seed: int = 1234
     prefill_tokens: int = 0   # config 4: tokens per prefill chunk
     prefill_topk: int = 0     # config 4: per-token top-k of the union
+    lanes: int = 0            # config 5: concurrent session lanes
 
     @property
     def n_tokens(self):
@@ -72,6 +73,11 @@ CONFIGS = {
     4: Workload("cfg4", n_layer=64, n_head=64, n_head_kv=8, d_head=128, block_tokens=128,
                 n_blocks=2048, budget_blocks=256, sink_blocks=1, reserve_blocks=128,
                 n_planted=32, seed=1238, prefill_tokens=2048, prefill_topk=256),
+    # 5: 8 session lanes, each its own 256K-token q8_0 K / q4_0 V history and
+    # seeded queries, layer-sharded, stepped together.
+    5: Workload("cfg5", n_layer=64, n_head=64, n_head_kv=8, d_head=128, block_tokens=128,
+                n_blocks=2048, budget_blocks=256, sink_blocks=1, reserve_blocks=128,
+                n_planted=32, k_type=TYPE_Q8_0, v_type=TYPE_Q4_0, seed=1239, lanes=8),
 }
 
 
