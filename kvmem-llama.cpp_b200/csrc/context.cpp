@@ -430,6 +430,7 @@ int plan_and_assemble(kvmret_ctx *c) {
     kvmret::AsmLaunch al{};
     al.jobs = c->jobs_dev;
     al.counts = c->d_counts;
+    al.work = c->d_counts + 7;
     al.fresh_offset = c->win_slots;
     al.repo = c->repo_dev;
     al.pool_w = c->pool;
@@ -948,6 +949,27 @@ int kvmret_window_read(kvmret_ctx *c, uint32_t layer, int is_v, uint32_t slot0, 
     return KVMRET_OK;
 }
 
+namespace {
+// Stateless RoPE over a contiguous run of n_tok rows at positions pos0 ..:
+// a temporary cos/sin table of those positions (indexed from 0), then the
+// assembly kernel's stateless form, chunks of 128 rows.
+int rope_stateless(kvmret::AsmLaunch &al, uint32_t n_tok, uint32_t n_rot, int32_t pos0,
+                   cudaStream_t st) {
+    float4 *tab = nullptr;
+    const size_t tab_bytes = static_cast<size_t>(n_tok) * (n_rot / 4) * sizeof(float4);
+    CK(cudaMallocAsync(reinterpret_cast<void **>(&tab), tab_bytes, st));
+    al.synth_pos0 = 0;
+    al.synth_ntok = n_tok;
+    al.gtab = tab;
+    cudaError_t e = kvmret::launch_rope_table(tab, n_tok, n_rot / 2, al.theta, st, pos0);
+    if (e == cudaSuccess) e = kvmret::launch_assemble(al, (n_tok + 127) / 128, st);
+    const cudaError_t ef = cudaFreeAsync(tab, st);
+    CK(e);
+    CK(ef);
+    return KVMRET_OK;
+}
+}  // namespace
+
 int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n_head_kv,
                     uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                     float freq_scale, void *stream) {
@@ -966,12 +988,9 @@ int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n
     al.pool = reinterpret_cast<const uint8_t *>(k);
     al.slot_bytes = 128 * g.k_row;
     al.win_k = reinterpret_cast<uint8_t *>(out);
-    al.synth_pos0 = pos0;
-    al.synth_ntok = n_tok;
     al.theta = make_theta(n_rot, freq_base, freq_scale);
     al.g = g;
-    CK(kvmret::launch_assemble(al, (n_tok + 127) / 128, static_cast<cudaStream_t>(stream)));
-    return KVMRET_OK;
+    return rope_stateless(al, n_tok, n_rot, pos0, static_cast<cudaStream_t>(stream));
 }
 
 namespace {
@@ -1000,22 +1019,9 @@ int rope_quant(int32_t type, const void *k, void *out, uint32_t n_tok, uint32_t 
     al.pool = static_cast<const uint8_t *>(k);
     al.slot_bytes = 128 * row;
     al.win_k = static_cast<uint8_t *>(out);
-    al.synth_ntok = n_tok;
     al.theta = make_theta(n_rot, freq_base, freq_scale);
     al.g = g;
-    // cos/sin of positions pos0 .. pos0 + n_tok - 1, indexed from 0
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    float4 *tab = nullptr;
-    const size_t tab_bytes = static_cast<size_t>(n_tok) * (n_rot / 4) * sizeof(float4);
-    CK(cudaMallocAsync(reinterpret_cast<void **>(&tab), tab_bytes, st));
-    al.synth_pos0 = 0;
-    al.gtab = tab;
-    cudaError_t e = kvmret::launch_rope_table(tab, n_tok, n_rot / 2, al.theta, st, pos0);
-    if (e == cudaSuccess) e = kvmret::launch_assemble(al, (n_tok + 127) / 128, st);
-    const cudaError_t ef = cudaFreeAsync(tab, st);
-    CK(e);
-    CK(ef);
-    return KVMRET_OK;
+    return rope_stateless(al, n_tok, n_rot, pos0, static_cast<cudaStream_t>(stream));
 }
 }  // namespace
 

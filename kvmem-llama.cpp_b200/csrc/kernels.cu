@@ -196,40 +196,17 @@ __global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ 
 }
 
 // ---------------------------------------------------------------------------
-// RoPE table: cos / sin of the float angle (pos0 + t) * theta[i]
-// (rope.cpp:27-33). The angle is the reference's float product; cos and sin
-// are evaluated in double and rounded once to float, i.e. correctly rounded,
-// so the table does not add the few-ulp error of a float sincos. Window
-// positions come from a per-context table built once at creation; the
-// stateless entry points evaluate the same expression on the fly. Entries of
-// each 8-wide group are rotated by the group index so the 8 threads of a head
-// row hit distinct shared-memory banks.
-__device__ __forceinline__ uint32_t tab_swz(uint32_t i) {
-    return (i & ~7u) | (((i & 7u) - (i >> 3)) & 7u);
-}
-
+// RoPE table: cos / sin of the float angle pos * theta[i] (rope.cpp:27-33).
+// The angle is the reference's float product; cos and sin are evaluated in
+// double and rounded once to float, i.e. correctly rounded, so the table does
+// not add the few-ulp error of a float sincos. Window positions come from a
+// per-context table built once at creation; the stateless entry points build a
+// temporary table for their positions.
 __device__ __forceinline__ float2 rope_cs(int32_t pos, float theta) {
     const float ang = __fmul_rn(static_cast<float>(pos), theta);
     double s, c;
     sincos(static_cast<double>(ang), &s, &c);
     return make_float2(__double2float_rn(c), __double2float_rn(s));
-}
-
-template <int HALF>
-__device__ __forceinline__ void build_rope_table(float2 *tab, int32_t pos0, uint32_t n_tok,
-                                                 const float *__restrict__ theta,
-                                                 const float4 *__restrict__ gtab) {
-    for (uint32_t idx = threadIdx.x; idx < n_tok * HALF; idx += blockDim.x) {
-        const uint32_t t = idx / HALF, i = idx % HALF;
-        float2 cs;
-        if (gtab) {
-            const float4 v = gtab[(static_cast<size_t>(pos0) + t) * (HALF / 2) + i / 2];
-            cs = (i & 1) ? make_float2(v.y, v.w) : make_float2(v.x, v.z);
-        } else {
-            cs = rope_cs(pos0 + static_cast<int32_t>(t), theta[i]);
-        }
-        tab[t * HALF + tab_swz(i)] = cs;
-    }
 }
 
 // Position table: cs[p][j] = {c_2j, c_2j+1, s_2j, s_2j+1} of position
@@ -247,46 +224,72 @@ __global__ void rope_table_kernel(float4 *__restrict__ cs, uint32_t n_pos, uint3
     }
 }
 
-// f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves.
-// raw_dst (fresh blocks) also receives the unrotated rows; src is then host
-// memory read with plain loads.
+// Items per thread whose loads are issued together (tunable at build time).
+#ifndef KVMRET_F16_UNROLL
+#define KVMRET_F16_UNROLL 2
+#endif
+
+template <int D>
+__device__ __forceinline__ void rope_chunk_f16(const uint4 &lo, const uint4 &hi, uint4 &olo,
+                                               uint4 &ohi, const float4 *__restrict__ cs) {
+    const uint16_t *a = reinterpret_cast<const uint16_t *>(&lo);
+    const uint16_t *b = reinterpret_cast<const uint16_t *>(&hi);
+    uint16_t *oa = reinterpret_cast<uint16_t *>(&olo);
+    uint16_t *ob = reinterpret_cast<uint16_t *>(&ohi);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        const float4 t = __ldg(cs + e / 2);
+        float x0 = h2f(a[e]), x1 = h2f(b[e]);
+        oa[e] = f2h(__fsub_rn(__fmul_rn(x0, t.x), __fmul_rn(x1, t.z)));
+        ob[e] = f2h(__fadd_rn(__fmul_rn(x0, t.z), __fmul_rn(x1, t.x)));
+        x0 = h2f(a[e + 1]);
+        x1 = h2f(b[e + 1]);
+        oa[e + 1] = f2h(__fsub_rn(__fmul_rn(x0, t.y), __fmul_rn(x1, t.w)));
+        ob[e + 1] = f2h(__fadd_rn(__fmul_rn(x0, t.w), __fmul_rn(x1, t.y)));
+    }
+}
+
+// f16 K: rows [n_tok][Hkv][D] f16, 16-byte chunks of the low and high halves;
+// row r is token r / n_head_kv at table row tab + token * D/4. raw_dst (fresh
+// blocks) also receives the unrotated rows; src is then host memory read with
+// plain loads.
 template <int D, bool FRESH>
 __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
-                                              uint8_t *__restrict__ dst, const float2 *tab,
-                                              uint32_t n_tok, uint32_t n_head_kv,
-                                              uint8_t *__restrict__ raw_dst) {
-    constexpr int HALF = D / 2, CPR = HALF / 8;
+                                              uint8_t *__restrict__ dst,
+                                              const float4 *__restrict__ tab, uint32_t n_tok,
+                                              uint32_t n_head_kv, uint8_t *__restrict__ raw_dst) {
+    constexpr int HALF = D / 2, CPR = HALF / 8, U = KVMRET_F16_UNROLL;
     const uint32_t n_items = n_tok * n_head_kv * CPR;
-    for (uint32_t w = threadIdx.x; w < n_items; w += blockDim.x) {
-        const uint32_t row = w / CPR, j = w % CPR, t = row / n_head_kv;
-        const uint4 *sp = reinterpret_cast<const uint4 *>(src + static_cast<size_t>(row) * D * 2);
-        uint4 lo, hi;
-        if constexpr (FRESH) {
-            lo = sp[j];
-            hi = sp[CPR + j];
-            uint4 *rp = reinterpret_cast<uint4 *>(raw_dst + static_cast<size_t>(row) * D * 2);
-            rp[j] = lo;
-            rp[CPR + j] = hi;
-        } else {
-            lo = __ldg(sp + j);
-            hi = __ldg(sp + CPR + j);
-        }
-        const uint16_t *a = reinterpret_cast<const uint16_t *>(&lo);
-        const uint16_t *b = reinterpret_cast<const uint16_t *>(&hi);
-        uint4 olo, ohi;
-        uint16_t *oa = reinterpret_cast<uint16_t *>(&olo);
-        uint16_t *ob = reinterpret_cast<uint16_t *>(&ohi);
-        const float2 *tr = tab + t * HALF;
+    for (uint32_t w0 = threadIdx.x; w0 < n_items; w0 += U * blockDim.x) {
+        uint4 lo[U], hi[U];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float2 cs = tr[tab_swz(j * 8 + e)];
-            const float x0 = h2f(a[e]), x1 = h2f(b[e]);
-            oa[e] = f2h(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
-            ob[e] = f2h(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
+        for (int u = 0; u < U; ++u) {  // all loads first
+            const uint32_t w = w0 + u * blockDim.x;
+            if (w >= n_items) break;
+            const uint32_t row = w / CPR, j = w % CPR;
+            const uint4 *sp = reinterpret_cast<const uint4 *>(src + static_cast<size_t>(row) * D * 2);
+            if constexpr (FRESH) {
+                lo[u] = sp[j];
+                hi[u] = sp[CPR + j];
+                uint4 *rp = reinterpret_cast<uint4 *>(raw_dst + static_cast<size_t>(row) * D * 2);
+                rp[j] = lo[u];
+                rp[CPR + j] = hi[u];
+            } else {
+                lo[u] = __ldg(sp + j);
+                hi[u] = __ldg(sp + CPR + j);
+            }
         }
-        uint4 *dp = reinterpret_cast<uint4 *>(dst + static_cast<size_t>(row) * D * 2);
-        dp[j] = olo;
-        dp[CPR + j] = ohi;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint32_t w = w0 + u * blockDim.x;
+            if (w >= n_items) break;
+            const uint32_t row = w / CPR, j = w % CPR, t = row / n_head_kv;
+            uint4 olo, ohi;
+            rope_chunk_f16<D>(lo[u], hi[u], olo, ohi, tab + static_cast<size_t>(t) * (D / 4) + 4 * j);
+            uint4 *dp = reinterpret_cast<uint4 *>(dst + static_cast<size_t>(row) * D * 2);
+            dp[j] = olo;
+            dp[CPR + j] = ohi;
+        }
     }
 }
 
@@ -386,43 +389,86 @@ __device__ __forceinline__ bool decode_job(const AsmLaunch &a, JobView &v) {
 
 constexpr int kAsmThreads = 512;
 
-// S10-S12, f16 K: CTA = one job x a range of layers. K re-roped from the
-// pool's unrotated copy at the job's window base; V copied.
+// One (job, layer) unit of the f16 assembly: K re-roped from the unrotated
+// copy (pool, or host repository for a fresh job, which is also copied into
+// its pool slot) at the job's window base; V copied.
 template <int D>
-__global__ void __launch_bounds__(kAsmThreads) assemble_kernel(const __grid_constant__ AsmLaunch a,
-                                                               uint32_t layers_per_cta) {
+__device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobView &jv,
+                                                  uint32_t l, const float4 *tab) {
     const AssembleGeom &g = a.g;
-    constexpr int HALF = D / 2;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    float2 *tab = reinterpret_cast<float2 *>(smem_raw);
-    JobView jv;
-    if (!decode_job(a, jv)) return;
-    build_rope_table<HALF>(tab, jv.pos0, jv.n_tok, a.theta.v, a.gtab);
-    __syncthreads();
-    const uint32_t l0 = jv.group * layers_per_cta;
-    const uint32_t l1 = min(g.n_layer, l0 + layers_per_cta);
     const uint8_t *slot = jv.fresh ? a.repo + static_cast<uint64_t>(jv.block) * a.slot_bytes
                                    : a.pool + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes;
-    uint8_t *raw_slot =
-        jv.fresh ? a.pool_w + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes : nullptr;
-    const uint64_t wk = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.k_row;
-    const uint64_t wv = static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.v_row;
-    for (uint32_t l = l0; l < l1; ++l) {
-        const uint8_t *src = slot + static_cast<uint64_t>(l) * g.unit;
-        uint8_t *raw = raw_slot ? raw_slot + static_cast<uint64_t>(l) * g.unit : nullptr;
-        uint8_t *dk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer + wk;
+    const uint8_t *src = slot + static_cast<uint64_t>(l) * g.unit;
+    uint8_t *raw = jv.fresh ? a.pool_w + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes +
+                                  static_cast<uint64_t>(l) * g.unit
+                            : nullptr;
+    uint8_t *dk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer +
+                  static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.k_row;
+    if (raw)
+        rope_rows_f16<D, true>(src, dk, tab, jv.n_tok, g.n_head_kv, raw);
+    else
+        rope_rows_f16<D, false>(src, dk, tab, jv.n_tok, g.n_head_kv, nullptr);
+    if (g.v_row) {
+        uint8_t *dv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
+                      static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.v_row;
+        const uint64_t vb = static_cast<uint64_t>(jv.n_tok) * g.v_row;
         if (raw)
-            rope_rows_f16<D, true>(src, dk, tab, jv.n_tok, g.n_head_kv, raw);
+            copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb);
         else
-            rope_rows_f16<D, false>(src, dk, tab, jv.n_tok, g.n_head_kv, nullptr);
-        if (g.v_row) {
-            uint8_t *dv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer + wv;
-            const uint64_t vb = static_cast<uint64_t>(jv.n_tok) * g.v_row;
-            if (raw)
-                copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb);
-            else
-                copy16(src + g.unit_k, dv, vb);
+            copy16(src + g.unit_k, dv, vb);
+    }
+}
+
+#ifndef KVMRET_F16_MINB
+#define KVMRET_F16_MINB 2
+#endif
+// S10-S12, f16 K. With device counts (the GPU-resident step) the grid is
+// persistent (one wave) and CTAs take work units from a device counter: first
+// the fresh jobs in groups of up to 8 layers (host-link bound, started at
+// once), then the moved jobs one layer at a time, so the CTAs finish together
+// (no partial last wave). cos/sin come from the position table through L1.
+// Without counts (stateless form): CTA = one chunk, layer 0.
+template <int D>
+__global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
+    assemble_kernel(const __grid_constant__ AsmLaunch a) {
+    constexpr uint32_t PAIRS = D / 4;
+    JobView jv;
+    if (!a.counts) {
+        if (!decode_job(a, jv)) return;
+        assemble_unit_f16<D>(a, jv, 0, a.gtab + static_cast<size_t>(jv.pos0) * PAIRS);
+        return;
+    }
+    __shared__ uint32_t s_unit;
+    const uint32_t L = a.g.n_layer, LF = min(L, 8u), gf = (L + LF - 1) / LF;
+    const uint32_t n_fu = a.counts[1] * gf;
+    const uint32_t n_units = n_fu + a.counts[0] * L;
+    for (;;) {
+        if (threadIdx.x == 0) s_unit = atomicAdd(a.work, 1u);
+        __syncthreads();
+        const uint32_t u = s_unit;
+        __syncthreads();  // every thread has read s_unit before it is overwritten
+        if (u >= n_units) break;
+        uint32_t j, l0, l1;
+        if (u < n_fu) {
+            j = a.fresh_offset + u / gf;
+            l0 = (u % gf) * LF;
+            l1 = min(L, l0 + LF);
+            jv.fresh = true;
+        } else {
+            const uint32_t v = u - n_fu;
+            j = v / L;
+            l0 = v % L;
+            l1 = l0 + 1;
+            jv.fresh = false;
         }
+        const Job *jp = a.jobs + j;
+        jv.pool_slot = jp->pool_slot;
+        jv.win_slot = jp->win_slot;
+        jv.pos0 = jp->pos0;
+        jv.n_tok = jp->n_tok;
+        jv.block = jp->block;
+        const float4 *tab = a.gtab + static_cast<size_t>(jv.pos0) * PAIRS;
+        for (uint32_t l = l0; l < l1; ++l) assemble_unit_f16<D>(a, jv, l, tab);
     }
 }
 
@@ -1194,6 +1240,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
         a.counts[4] = s_err;
         a.counts[5] = s_mtok;
         a.counts[6] = s_ftok;
+        a.counts[7] = 0;  // the assembly's work-unit counter
     }
 }
 
@@ -1229,17 +1276,24 @@ uint32_t layers_per_cta_for(const AsmLaunch &a, uint32_t n_jobs) {
 
 template <int D>
 cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
-    const uint32_t lpc = layers_per_cta_for(a, n_jobs);
-    const uint32_t groups = (a.g.n_layer + lpc - 1) / lpc;
-    AsmLaunch al = a;
-    al.n_groups = groups;
-    const dim3 grid = a.counts ? dim3(n_jobs * groups, 1) : dim3(n_jobs, groups);
-    const size_t smem = static_cast<size_t>(a.g.block_tokens) * (D / 2) * sizeof(float2);
     auto kfn = assemble_kernel<D>;
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    kfn<<<grid, kAsmThreads, smem, st>>>(al, lpc);
+    if (!a.counts) {
+        kfn<<<n_jobs, kAsmThreads, 0, st>>>(a);
+        return cudaGetLastError();
+    }
+    // persistent: as many CTAs as fit on the device at once
+    static int per_sm = 0, n_sm = 0;
+    if (per_sm == 0) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess)
+            e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kAsmThreads, 0);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) per_sm = 1;
+    }
+    kfn<<<static_cast<uint32_t>(per_sm * n_sm), kAsmThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -85,6 +85,7 @@ struct AsmLaunch {
     // launch's n_jobs jobs are all moved jobs). Moved jobs sit at jobs[0..),
     // fresh jobs at jobs[fresh_offset..); CTAs beyond the counts exit at once.
     const uint32_t *counts;
+    uint32_t *work;         // f16 form with counts: unit counter (zeroed by the plan kernel)
     uint32_t fresh_offset;
     uint32_t n_groups;      // layer groups per job (set by the launcher)
     const uint8_t *repo;    // device alias of the mapped pinned repository (fresh jobs)
