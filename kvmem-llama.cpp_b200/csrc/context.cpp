@@ -419,14 +419,6 @@ int plan_and_assemble(kvmret_ctx *c) {
     pa.counts = c->d_counts;
     pa.ids = c->d_ids;
     CK(kvmret::launch_plan(pa, c->st));
-    const int slot = c->rb_head;
-    uint32_t *r = c->rb(slot);
-    CK(cudaMemcpyAsync(r, c->d_counts, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->st));
-    CK(cudaMemcpyAsync(r + 8, c->d_ids, c->win_slots * sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                       c->st));
-    CK(cudaEventRecord(c->ev_rb[slot], c->st));
-    c->rb_head = (c->rb_head + 1) % kRing;
-    ++c->rb_pending;
     kvmret::AsmLaunch al{};
     al.jobs = c->jobs_dev;
     al.counts = c->d_counts;
@@ -445,6 +437,16 @@ int plan_and_assemble(kvmret_ctx *c) {
     CK(kvmret::launch_assemble(al, 2 * c->win_slots, c->st));
     prof_end(c, c->st, pr);
     c->prof.launches += 2;
+    // the plan's counts and ids go back to the host after the assembly, so the
+    // two small copies do not sit between the plan and the assembly
+    const int slot = c->rb_head;
+    uint32_t *r = c->rb(slot);
+    CK(cudaMemcpyAsync(r, c->d_counts, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(r + 8, c->d_ids, c->win_slots * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                       c->st));
+    CK(cudaEventRecord(c->ev_rb[slot], c->st));
+    c->rb_head = (c->rb_head + 1) % kRing;
+    ++c->rb_pending;
     return KVMRET_OK;
 }
 

@@ -146,10 +146,16 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
 }
 
 // S3 epilogue (:4189-4193): acc over layers in order, score = acc / nlay.
-__global__ void reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
-                              uint32_t n_layer, uint32_t stride,
-                              const uint8_t *__restrict__ has_block, uint32_t n_blocks,
-                              double *__restrict__ scores) {
+__global__ void __launch_bounds__(128)
+    reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
+                  uint32_t n_layer, uint32_t stride, const uint8_t *__restrict__ has_block,
+                  uint32_t n_blocks, double *__restrict__ scores) {
+    // the layers that carry a query, once per CTA
+    extern __shared__ uint8_t s_act[];
+    for (uint32_t l = threadIdx.x; l < n_layer; l += blockDim.x)
+        s_act[l] = active ? active[l]
+                          : (contrib[static_cast<size_t>(l) * stride + stride - 1] != 0.0);
+    __syncthreads();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n_blocks) return;
     if (!has_block[b]) {
@@ -158,11 +164,22 @@ __global__ void reduce_kernel(const double *__restrict__ contrib, const uint8_t 
     }
     double acc = 0.0;
     uint32_t nlay = 0;
-    for (uint32_t l = 0; l < n_layer; ++l) {
-        const double *row = contrib + static_cast<size_t>(l) * stride;
-        if (active ? !active[l] : row[stride - 1] == 0.0) continue;
-        acc = __dadd_rn(acc, row[b]);
-        ++nlay;
+    for (uint32_t l0 = 0; l0 < n_layer; l0 += 16) {
+        double v[16];
+#pragma unroll
+        for (uint32_t u = 0; u < 16; ++u) {  // 16 independent loads in flight
+            const uint32_t l = l0 + u;
+            v[u] = (l < n_layer && s_act[l]) ? __ldg(contrib + static_cast<size_t>(l) * stride + b)
+                                             : 0.0;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 16; ++u) {  // summed strictly in layer order
+            const uint32_t l = l0 + u;
+            if (l < n_layer && s_act[l]) {
+                acc = __dadd_rn(acc, v[u]);
+                ++nlay;
+            }
+        }
     }
     scores[b] = nlay ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
 }
@@ -193,6 +210,36 @@ __global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ 
     }
     rank = __reduce_add_sync(0xffffffffu, rank);
     if (lane == 0) sel[b] = rank < need ? 1 : 0;
+}
+
+// The same with every score and kept flag staged in shared memory first (one
+// load of the whole array per CTA of 32 warps, then ranks from shared memory).
+__global__ void __launch_bounds__(1024) select_smem_kernel(const double *__restrict__ scores,
+                                                           const uint8_t *__restrict__ kept,
+                                                           uint32_t n, uint32_t need,
+                                                           int tie_high, uint8_t *__restrict__ sel) {
+    extern __shared__ double s_sc[];
+    uint8_t *s_kept = reinterpret_cast<uint8_t *>(s_sc + n);
+    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
+        s_sc[c] = scores[c];
+        s_kept[c] = kept[c];
+    }
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+    for (uint32_t b = blockIdx.x * nwarp + (threadIdx.x >> 5); b < n; b += gridDim.x * nwarp) {
+        if (s_kept[b]) {
+            if (lane == 0) sel[b] = 1;
+            continue;
+        }
+        const double sb = s_sc[b];
+        uint32_t rank = 0;
+        for (uint32_t c = lane; c < n; c += 32) {
+            const double sc = s_sc[c];
+            rank += (!s_kept[c] && (sc > sb || (sc == sb && (tie_high ? c > b : c < b)))) ? 1u : 0u;
+        }
+        rank = __reduce_add_sync(0xffffffffu, rank);
+        if (lane == 0) sel[b] = rank < need ? 1 : 0;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1368,16 +1415,26 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    reduce_kernel<<<(n_blocks + 63) / 64, 64, 0, st>>>(contrib, active, n_layer, stride,
-                                                       has_block, n_blocks, scores);
+    reduce_kernel<<<(n_blocks + 127) / 128, 128, n_layer, st>>>(contrib, active, n_layer, stride,
+                                                               has_block, n_blocks, scores);
     return cudaGetLastError();
 }
 
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    select_kernel<<<(n_blocks + 7) / 8, 256, 0, st>>>(scores, kept, n_blocks, need,
-                                                      tie_higher_id, sel);
+    const size_t smem = static_cast<size_t>(n_blocks) * (sizeof(double) + 1);
+    if (smem <= 160 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(select_smem_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        select_smem_kernel<<<(n_blocks + 31) / 32, 1024, smem, st>>>(scores, kept, n_blocks, need,
+                                                                    tie_higher_id, sel);
+    } else {
+        select_kernel<<<(n_blocks + 7) / 8, 256, 0, st>>>(scores, kept, n_blocks, need,
+                                                          tie_higher_id, sel);
+    }
     return cudaGetLastError();
 }
 
