@@ -6,6 +6,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include <cub/block/block_scan.cuh>
 
 #include "kvmret.h"
@@ -94,54 +96,65 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                                                     const uint8_t *__restrict__ active,
                                                     double *__restrict__ contrib,
                                                     uint32_t n_head_kv, uint32_t ncap,
-                                                    uint32_t cstride) {
+                                                    uint32_t cstride, uint32_t tiles,
+                                                    uint32_t n_units, uint32_t per_cta) {
     extern __shared__ float smem[];
-    const uint32_t l = blockIdx.y;
-    const uint32_t b0 = blockIdx.x * kTile;
-    double *out = contrib + static_cast<size_t>(l) * cstride + b0;
-    if (!active[l]) {
-        for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) out[t] = 0.0;
-        return;
-    }
     float *sq = smem;                       // [Hkv][D]
     float *cosb = smem + n_head_kv * D;     // [Hkv][kTile]
-    for (uint32_t i = threadIdx.x; i < n_head_kv * D; i += blockDim.x)
-        sq[i] = qv[static_cast<size_t>(l) * n_head_kv * D + i];
-    __syncthreads();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
     const size_t dstep = ncap / 2;  // float2 stride between d rows
-    for (uint32_t h = warp; h < n_head_kv; h += nwarp) {
-        const float2 *p = reinterpret_cast<const float2 *>(
-                              summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
-                          lane;
-        const float *qh = sq + h * D;
-        float d0 = 0.f, d1 = 0.f, n0 = 0.f, n1 = 0.f;
-#pragma unroll 2
-        for (int dd = 0; dd < D; dd += 16) {
-            float2 k[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) k[u] = __ldg(p + static_cast<size_t>(dd + u) * dstep);
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const float q = qh[dd + u];
-                d0 = __fadd_rn(d0, __fmul_rn(q, k[u].x));
-                d1 = __fadd_rn(d1, __fmul_rn(q, k[u].y));
-                n0 = __fadd_rn(n0, __fmul_rn(k[u].x, k[u].x));
-                n1 = __fadd_rn(n1, __fmul_rn(k[u].y, k[u].y));
-            }
+    // units (layer, tile of kTile blocks), layer-major; this CTA's contiguous
+    // share, so every CTA carries the same number of units
+    const uint32_t u0 = blockIdx.x * per_cta, u1 = min(n_units, u0 + per_cta);
+    uint32_t l_loaded = ~0u;
+    for (uint32_t u = u0; u < u1; ++u) {
+        const uint32_t l = u / tiles;
+        const uint32_t b0 = (u % tiles) * kTile;
+        double *out = contrib + static_cast<size_t>(l) * cstride + b0;
+        if (!active[l]) {
+            for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) out[t] = 0.0;
+            continue;
         }
-        const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
-        float *cb = cosb + h * kTile + lane * 2;
-        cb[0] = __fdiv_rn(d0, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n0)), 1e-6f));
-        cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
-    }
-    __syncthreads();
-    // layer += cos (double, head order); term = layer / n_head_kv (:4186-4188).
-    for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) {
-        double layer = 0.0;
-        for (uint32_t h = 0; h < n_head_kv; ++h)
-            layer = __dadd_rn(layer, static_cast<double>(cosb[h * kTile + t]));
-        out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
+        if (l != l_loaded) {
+            __syncthreads();  // the previous unit's readers of sq are done
+            for (uint32_t i = threadIdx.x; i < n_head_kv * D; i += blockDim.x)
+                sq[i] = qv[static_cast<size_t>(l) * n_head_kv * D + i];
+            l_loaded = l;
+        }
+        __syncthreads();
+        for (uint32_t h = warp; h < n_head_kv; h += nwarp) {
+            const float2 *p = reinterpret_cast<const float2 *>(
+                                  summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
+                              lane;
+            const float *qh = sq + h * D;
+            float d0 = 0.f, d1 = 0.f, n0 = 0.f, n1 = 0.f;
+#pragma unroll 2
+            for (int dd = 0; dd < D; dd += 16) {
+                float2 k[16];
+#pragma unroll
+                for (int v = 0; v < 16; ++v) k[v] = __ldg(p + static_cast<size_t>(dd + v) * dstep);
+#pragma unroll
+                for (int v = 0; v < 16; ++v) {
+                    const float q = qh[dd + v];
+                    d0 = __fadd_rn(d0, __fmul_rn(q, k[v].x));
+                    d1 = __fadd_rn(d1, __fmul_rn(q, k[v].y));
+                    n0 = __fadd_rn(n0, __fmul_rn(k[v].x, k[v].x));
+                    n1 = __fadd_rn(n1, __fmul_rn(k[v].y, k[v].y));
+                }
+            }
+            const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
+            float *cb = cosb + h * kTile + lane * 2;
+            cb[0] = __fdiv_rn(d0, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n0)), 1e-6f));
+            cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
+        }
+        __syncthreads();
+        // layer += cos (double, head order); term = layer / n_head_kv (:4186-4188).
+        for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) {
+            double layer = 0.0;
+            for (uint32_t h = 0; h < n_head_kv; ++h)
+                layer = __dadd_rn(layer, static_cast<double>(cosb[h * kTile + t]));
+            out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
+        }
     }
 }
 
@@ -1383,6 +1396,30 @@ cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv,
     return cudaGetLastError();
 }
 
+template <int D>
+cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
+                           const uint8_t *active, double *contrib, uint32_t n_layer,
+                           uint32_t n_head_kv, uint32_t ncap, uint32_t tiles, cudaStream_t st,
+                           uint32_t cstride) {
+    const size_t smem = static_cast<size_t>(n_head_kv) * (D + kTile) * sizeof(float);
+    auto kfn = score_kernel<D>;
+    // as many units per CTA as it takes for one wave of resident CTAs, then as
+    // few CTAs as carry them all: every CTA gets the same share
+    int per_sm = 0, n_sm = 0, dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, 256, smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
+    const uint32_t n_units = tiles * n_layer;
+    const uint32_t per_cta = (n_units + slots - 1) / slots;
+    const uint32_t grid = (n_units + per_cta - 1) / per_cta;
+    kfn<<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap, cstride, tiles,
+                                  n_units, per_cta);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
@@ -1390,25 +1427,19 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
     if (cstride == 0) cstride = ncap;
     const uint32_t tiles = (n_blocks + kTile - 1) / kTile;
     if (tiles == 0) return cudaSuccess;
-    const dim3 grid(tiles, n_layer);
-    const size_t smem = static_cast<size_t>(n_head_kv) * (d_head + kTile) * sizeof(float);
     switch (d_head) {
     case 64:
-        score_kernel<64><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
-                                                   cstride);
-        break;
+        return launch_score_t<64>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
+                                  st, cstride);
     case 128:
-        score_kernel<128><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
-                                                   cstride);
-        break;
+        return launch_score_t<128>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
+                                   st, cstride);
     case 256:
-        score_kernel<256><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
-                                                   cstride);
-        break;
+        return launch_score_t<256>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
+                                   st, cstride);
     default:
         return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
