@@ -129,8 +129,9 @@ struct kvmret_ctx {
     cudaEvent_t ev_rb[kRing] = {};
     int rb_head = 0, rb_pending = 0;
     uint32_t step = 0;
-    std::vector<uint32_t> q_count;
-    bool q_dirty = true;
+    std::vector<uint32_t> q_count;  // host mirror of q_count_dev
+    bool q_dirty = true;            // qv / nq / active must be recomputed
+    bool q_reset_pending = true;    // q_sum / q_count_dev hold a stale query
     std::vector<uint8_t> kept_cached;  // last kept flags uploaded
     bool kept_valid = false;
     kvmret::BlockTable table;
@@ -483,12 +484,22 @@ int select_device(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
 
 // Per-(layer, block) terms into rows of cstride doubles (out == nullptr: the
 // context's buffer); the layer's query flag goes to the last column of its row.
+// A reset is folded into the next query_add; anything that reads the query
+// state before such an add clears it here instead.
+int settle_query(kvmret_ctx *c) {
+    if (!c->q_reset_pending) return KVMRET_OK;
+    CK(cudaMemsetAsync(c->q_sum, 0, static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
+                       c->st));
+    CK(cudaMemsetAsync(c->q_count_dev, 0, c->cfg.n_layer * sizeof(uint32_t), c->st));
+    c->q_reset_pending = false;
+    return KVMRET_OK;
+}
+
 int score_layers_impl(kvmret_ctx *c, double *out) {
     double *dst = out ? out : c->contrib;
     if (out) c->q_dirty = true;  // the flag column of a caller buffer is written by qprep
+    TRY(settle_query(c));
     if (c->q_dirty) {
-        CK(cudaMemcpyAsync(c->q_count_dev, c->q_count.data(), c->q_count.size() * sizeof(uint32_t),
-                           cudaMemcpyHostToDevice, c->st));
         CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active,
                                 c->cfg.n_layer, c->cfg.n_head, c->cfg.n_head_kv, c->cfg.d_head,
                                 c->st, dst, c->cstride));
@@ -721,9 +732,8 @@ int kvmret_get_summaries(kvmret_ctx *c, float *out) {
 
 int kvmret_query_reset(kvmret_ctx *c) {
     NEED_CTX(c);
-    CK(cudaMemsetAsync(c->q_sum, 0, static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
-                       c->st));
     std::fill(c->q_count.begin(), c->q_count.end(), 0u);
+    c->q_reset_pending = true;  // the next add assigns instead of adding
     c->q_dirty = true;
     return KVMRET_OK;
 }
@@ -732,7 +742,9 @@ static int query_add(kvmret_ctx *c, const void *q, bool f16, uint32_t n_rows) {
     NEED_CTX(c);
     if (!q) return fail(KVMRET_ERR_ARG, "null query");
     if (n_rows == 0) return KVMRET_OK;
-    CK(kvmret::launch_query_add(c->q_sum, q, f16, c->cfg.n_layer, n_rows, c->qdim, c->st));
+    CK(kvmret::launch_query_add(c->q_sum, q, f16, c->cfg.n_layer, n_rows, c->qdim, c->st,
+                                c->q_count_dev, c->q_reset_pending));
+    c->q_reset_pending = false;
     c->prof.launches += 1;
     for (auto &x : c->q_count) x += n_rows;
     c->q_dirty = true;
@@ -753,6 +765,9 @@ int kvmret_query_set(kvmret_ctx *c, const float *q_sum, const uint32_t *q_count)
                        static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),
                        cudaMemcpyHostToDevice, c->st));
     for (uint32_t l = 0; l < c->cfg.n_layer; ++l) c->q_count[l] = q_count[l];
+    CK(cudaMemcpyAsync(c->q_count_dev, c->q_count.data(), c->cfg.n_layer * sizeof(uint32_t),
+                       cudaMemcpyHostToDevice, c->st));
+    c->q_reset_pending = false;
     c->q_dirty = true;
     CK(cudaStreamSynchronize(c->st));
     return KVMRET_OK;
@@ -760,6 +775,7 @@ int kvmret_query_set(kvmret_ctx *c, const float *q_sum, const uint32_t *q_count)
 
 int kvmret_query_get(kvmret_ctx *c, float *q_sum, uint32_t *q_count) {
     NEED_CTX(c);
+    TRY(settle_query(c));
     if (q_sum) {
         CK(cudaMemcpyAsync(q_sum, c->q_sum,
                            static_cast<size_t>(c->cfg.n_layer) * c->qdim * sizeof(float),

@@ -25,14 +25,19 @@ __device__ __forceinline__ uint16_t f2h(float f) {
 }
 
 // ---------------------------------------------------------------------------
-// S1: q_sum += rows, row order (llama-memory-kvmem.cpp:3417-3432).
+// S1: q_sum += rows, row order (llama-memory-kvmem.cpp:3417-3432); with
+// assign, q_sum = the rows' sum (a reset folded into the first add).
 template <typename T>
 __global__ void query_add_kernel(float *__restrict__ q_sum, const T *__restrict__ rows,
-                                 uint32_t n_rows, uint32_t qdim) {
+                                 uint32_t n_rows, uint32_t qdim, uint32_t *__restrict__ q_count,
+                                 int assign) {
     const uint32_t l = blockIdx.y;
     const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+    // the row count lives on the device; assign = the first add after a reset
+    if (q_count && blockIdx.x == 0 && threadIdx.x == 0)
+        q_count[l] = assign ? n_rows : q_count[l] + n_rows;
     if (e >= qdim) return;
-    float s = q_sum[static_cast<size_t>(l) * qdim + e];
+    float s = assign ? 0.0f : q_sum[static_cast<size_t>(l) * qdim + e];
     const T *src = rows + static_cast<size_t>(l) * n_rows * qdim + e;
     for (uint32_t r = 0; r < n_rows; ++r) {
         float v;
@@ -1377,14 +1382,15 @@ cudaError_t launch_assemble_quant_t(const AsmLaunch &a, uint32_t n_jobs, cudaStr
 }  // namespace
 
 cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint32_t n_layer,
-                             uint32_t n_rows, uint32_t qdim, cudaStream_t st) {
+                             uint32_t n_rows, uint32_t qdim, cudaStream_t st, uint32_t *q_count,
+                             bool assign) {
     const dim3 grid((qdim + 255) / 256, n_layer);
     if (rows_f16)
-        query_add_kernel<uint16_t><<<grid, 256, 0, st>>>(q_sum, static_cast<const uint16_t *>(rows),
-                                                         n_rows, qdim);
+        query_add_kernel<uint16_t><<<grid, 256, 0, st>>>(
+            q_sum, static_cast<const uint16_t *>(rows), n_rows, qdim, q_count, assign);
     else
         query_add_kernel<float><<<grid, 256, 0, st>>>(q_sum, static_cast<const float *>(rows),
-                                                      n_rows, qdim);
+                                                      n_rows, qdim, q_count, assign);
     return cudaGetLastError();
 }
 

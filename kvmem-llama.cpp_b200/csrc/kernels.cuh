@@ -43,9 +43,11 @@ struct AssembleGeom {
     float fwht_scale;       // 1 / sqrt(fwht_n), computed on the host
 };
 
-// S1: q_sum[l][e] += sum over rows (row order), f16 or f32 rows [L][n_rows][qdim].
+// S1: q_sum[l][e] += sum over rows (row order), f16 or f32 rows [L][n_rows][qdim];
+// q_count (optional, device) += n_rows per layer; assign: start from zero.
 cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint32_t n_layer,
-                             uint32_t n_rows, uint32_t qdim, cudaStream_t st);
+                             uint32_t n_rows, uint32_t qdim, cudaStream_t st,
+                             uint32_t *q_count = nullptr, bool assign = false);
 
 // S3 prologue: per (layer, kv head) the scaled group query and its squared norm.
 // With flag_col set, each layer's query flag (1.0 / 0.0) is also written to
