@@ -211,3 +211,34 @@ def test_d2d_batched():
     for o, z in zip(offs, sizes):
         assert np.array_equal(d_[o + 7:o + 7 + z], s[o:o + z])
     r.close()
+
+
+def test_quant_k_partial_newest_block():
+    """A q8_0 K history ending mid-block: the partial newest block, pinned by the
+    mandatory list, is requantised row for row (the rows past its end stay
+    untouched work items)."""
+    w = synth.scaled(synth.CONFIGS[3], n_layer=2, n_blocks=24, budget_blocks=6,
+                     reserve_blocks=2, n_planted=2, n_head=16)
+    hist = synth.NumpyHistory(w)
+    r = kvmret.Retriever(config_for(w))
+    T, L, E = w.block_tokens, w.n_layer, w.E
+    n_app = 20 * T + 37
+    kq, vq = _quant_rows(po.quant_q8_0, 1088), _quant_rows(po.quant_q4_0, 576)
+    append_history(r, hist, cuts=[], k_rows_fn=kq, v_rows_fn=vq, stop=n_app)
+    newest = n_app // T
+    k_all = kq(hist.k.reshape(L, -1, E)[:, :n_app])
+    for s in range(2):
+        r.query_reset()
+        r.query_add(torch.from_numpy(hist.queries(2)[s].reshape(L, 1, -1)).cuda())
+        ids, _ = r.apply_retrieval(mandatory=[newest])
+        assert newest in ids.tolist()
+    lay, bases = r.window_layout()
+    i = list(lay).index(newest)
+    n_b = n_app - newest * T
+    for l in range(L):
+        wk = r.window_read(l, False, i, 1).reshape(T, -1)[:n_b]
+        want = po.rope_block_q8_0(k_all[l, newest * T:n_app], n_b, w.n_head_kv, w.d_head,
+                                  int(bases[i]), w.freq_base, fwht_n=128)
+        dq, dd = q8_blocks_diff(wk, want)
+        assert dq <= 1 and dd <= 1
+    r.close()
