@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include <cub/block/block_scan.cuh>
 
@@ -15,7 +16,6 @@
 namespace kvmret {
 namespace {
 
-constexpr int kTile = 64;  // blocks per scoring CTA (32 lanes x float2)
 
 __device__ __forceinline__ float h2f(uint16_t h) {
     return __half2float(__ushort_as_half(h));
@@ -88,13 +88,13 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
 }
 
 // ---------------------------------------------------------------------------
-// S3: one CTA = one layer x kTile (64) blocks. Summaries are block-minor
-// [L][Hkv][D][ncap], so lane j of a warp walks blocks 2j, 2j+1 with float2
-// loads: each d step of a warp reads 256 contiguous bytes, and each block's
-// dot / norm is accumulated strictly in d order (score_retrieval :4179-4185).
-// Warp w handles heads w, w + 8, ...; the per-layer head sum is taken in head
-// order from shared memory.
-template <int D>
+// S3: a unit = one layer x TILE blocks (64: lane j walks blocks 2j, 2j+1 with
+// float2 loads; 32: one block per lane). Summaries are block-minor
+// [L][Hkv][D][ncap], so each d step of a warp reads 256 (128) contiguous
+// bytes, and each block's dot / norm is accumulated strictly in d order
+// (score_retrieval :4179-4185). Warp w handles heads w, w + 8, ...; the
+// per-layer head sum is taken in head order from shared memory.
+template <int D, int V>
 __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ summ,
                                                     const float *__restrict__ qv,
                                                     const float *__restrict__ nq,
@@ -103,21 +103,23 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                                                     uint32_t n_head_kv, uint32_t ncap,
                                                     uint32_t cstride, uint32_t tiles,
                                                     uint32_t n_units, uint32_t per_cta) {
+    constexpr uint32_t TILE = 32 * V;  // blocks per unit: V per lane
+    using VecT = typename std::conditional<V == 2, float2, float>::type;
     extern __shared__ float smem[];
     float *sq = smem;                       // [Hkv][D]
-    float *cosb = smem + n_head_kv * D;     // [Hkv][kTile]
+    float *cosb = smem + n_head_kv * D;     // [Hkv][TILE]
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
-    const size_t dstep = ncap / 2;  // float2 stride between d rows
-    // units (layer, tile of kTile blocks), layer-major; this CTA's contiguous
+    const size_t dstep = ncap / V;  // vector stride between d rows
+    // units (layer, tile of TILE blocks), layer-major; this CTA's contiguous
     // share, so every CTA carries the same number of units
     const uint32_t u0 = blockIdx.x * per_cta, u1 = min(n_units, u0 + per_cta);
     uint32_t l_loaded = ~0u;
     for (uint32_t u = u0; u < u1; ++u) {
         const uint32_t l = u / tiles;
-        const uint32_t b0 = (u % tiles) * kTile;
+        const uint32_t b0 = (u % tiles) * TILE;
         double *out = contrib + static_cast<size_t>(l) * cstride + b0;
         if (!active[l]) {
-            for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) out[t] = 0.0;
+            for (uint32_t t = threadIdx.x; t < TILE; t += blockDim.x) out[t] = 0.0;
             continue;
         }
         if (l != l_loaded) {
@@ -128,36 +130,42 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
         }
         __syncthreads();
         for (uint32_t h = warp; h < n_head_kv; h += nwarp) {
-            const float2 *p = reinterpret_cast<const float2 *>(
-                                  summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
-                              lane;
+            const VecT *p = reinterpret_cast<const VecT *>(
+                                summ + (static_cast<size_t>(l) * n_head_kv + h) * D * ncap + b0) +
+                            lane;
             const float *qh = sq + h * D;
             float d0 = 0.f, d1 = 0.f, n0 = 0.f, n1 = 0.f;
 #pragma unroll 2
             for (int dd = 0; dd < D; dd += 16) {
-                float2 k[16];
+                VecT k[16];
 #pragma unroll
                 for (int v = 0; v < 16; ++v) k[v] = __ldg(p + static_cast<size_t>(dd + v) * dstep);
 #pragma unroll
                 for (int v = 0; v < 16; ++v) {
                     const float q = qh[dd + v];
-                    d0 = __fadd_rn(d0, __fmul_rn(q, k[v].x));
-                    d1 = __fadd_rn(d1, __fmul_rn(q, k[v].y));
-                    n0 = __fadd_rn(n0, __fmul_rn(k[v].x, k[v].x));
-                    n1 = __fadd_rn(n1, __fmul_rn(k[v].y, k[v].y));
+                    if constexpr (V == 2) {
+                        d0 = __fadd_rn(d0, __fmul_rn(q, k[v].x));
+                        d1 = __fadd_rn(d1, __fmul_rn(q, k[v].y));
+                        n0 = __fadd_rn(n0, __fmul_rn(k[v].x, k[v].x));
+                        n1 = __fadd_rn(n1, __fmul_rn(k[v].y, k[v].y));
+                    } else {
+                        d0 = __fadd_rn(d0, __fmul_rn(q, k[v]));
+                        n0 = __fadd_rn(n0, __fmul_rn(k[v], k[v]));
+                    }
                 }
             }
             const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
-            float *cb = cosb + h * kTile + lane * 2;
+            float *cb = cosb + h * TILE + lane * V;
             cb[0] = __fdiv_rn(d0, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n0)), 1e-6f));
-            cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
+            if constexpr (V == 2)
+                cb[1] = __fdiv_rn(d1, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(n1)), 1e-6f));
         }
         __syncthreads();
         // layer += cos (double, head order); term = layer / n_head_kv (:4186-4188).
-        for (uint32_t t = threadIdx.x; t < kTile; t += blockDim.x) {
+        for (uint32_t t = threadIdx.x; t < TILE; t += blockDim.x) {
             double layer = 0.0;
             for (uint32_t h = 0; h < n_head_kv; ++h)
-                layer = __dadd_rn(layer, static_cast<double>(cosb[h * kTile + t]));
+                layer = __dadd_rn(layer, static_cast<double>(cosb[h * TILE + t]));
             out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
         }
     }
@@ -489,9 +497,9 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
 #endif
 // S10-S12, f16 K. With device counts (the GPU-resident step) the grid is
 // persistent (one wave) and CTAs take work units from a device counter: first
-// the fresh jobs in groups of up to 8 layers (host-link bound, started at
-// once), then the moved jobs one layer at a time, so the CTAs finish together
-// (no partial last wave). cos/sin come from the position table through L1.
+// the fresh jobs (host-link bound, started at once), then the moved jobs, one
+// (job, layer) unit at a time, so the CTAs finish together (no partial last
+// wave). cos/sin come from the position table through L1.
 // Without counts (stateless form): CTA = one chunk, layer 0.
 template <int D>
 __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
@@ -504,7 +512,11 @@ __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
         return;
     }
     __shared__ uint32_t s_unit;
-    const uint32_t L = a.g.n_layer, LF = min(L, 8u), gf = (L + LF - 1) / LF;
+    // fresh jobs are host-link bound for most of the launch: about 16 fresh
+    // units (each CTA keeps ~32 KB of host loads in flight) saturate the link
+    // without taking more CTAs away from the HBM-bound moved units
+    const uint32_t L = a.g.n_layer;
+    const uint32_t LF = min(L, max(1u, (a.counts[1] * L + 15) / 16)), gf = (L + LF - 1) / LF;
     const uint32_t n_fu = a.counts[1] * gf;
     const uint32_t n_units = n_fu + a.counts[0] * L;
     for (;;) {
@@ -1402,28 +1414,43 @@ cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv,
     return cudaGetLastError();
 }
 
-template <int D>
-cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
-                           const uint8_t *active, double *contrib, uint32_t n_layer,
-                           uint32_t n_head_kv, uint32_t ncap, uint32_t tiles, cudaStream_t st,
-                           uint32_t cstride) {
-    const size_t smem = static_cast<size_t>(n_head_kv) * (D + kTile) * sizeof(float);
-    auto kfn = score_kernel<D>;
-    // as many units per CTA as it takes for one wave of resident CTAs, then as
-    // few CTAs as carry them all: every CTA gets the same share
-    int per_sm = 0, n_sm = 0, dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, 256, smem);
-    if (e != cudaSuccess) return e;
-    const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
+template <int D, int V>
+cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
+                            const uint8_t *active, double *contrib, uint32_t n_layer,
+                            uint32_t n_head_kv, uint32_t ncap, uint32_t tiles, uint32_t slots,
+                            size_t smem, cudaStream_t st, uint32_t cstride) {
     const uint32_t n_units = tiles * n_layer;
     const uint32_t per_cta = (n_units + slots - 1) / slots;
     const uint32_t grid = (n_units + per_cta - 1) / per_cta;
-    kfn<<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap, cstride, tiles,
-                                  n_units, per_cta);
+    score_kernel<D, V><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
+                                                 cstride, tiles, n_units, per_cta);
     return cudaGetLastError();
+}
+
+// As many units per CTA as it takes for one wave of resident CTAs, then as few
+// CTAs as carry them all: every CTA gets the same share. With fewer units
+// than resident CTAs (few layers per GPU) the tile shrinks to 32 blocks so
+// more CTAs keep loads in flight.
+template <int D>
+cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
+                           const uint8_t *active, double *contrib, uint32_t n_layer,
+                           uint32_t n_head_kv, uint32_t ncap, uint32_t n_blocks, cudaStream_t st,
+                           uint32_t cstride) {
+    int per_sm = 0, n_sm = 0, dev = 0;
+    const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 2>, 256, smem64);
+    if (e != cudaSuccess) return e;
+    const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
+    const uint32_t tiles64 = (n_blocks + 63) / 64;
+    if (tiles64 * n_layer >= slots)
+        return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                     tiles64, slots, smem64, st, cstride);
+    const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
+    return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                 (n_blocks + 31) / 32, slots, smem32, st, cstride);
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
@@ -1431,18 +1458,17 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
                          cudaStream_t st, uint32_t cstride) {
     if (cstride == 0) cstride = ncap;
-    const uint32_t tiles = (n_blocks + kTile - 1) / kTile;
-    if (tiles == 0) return cudaSuccess;
+    if (n_blocks == 0) return cudaSuccess;
     switch (d_head) {
     case 64:
-        return launch_score_t<64>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
-                                  st, cstride);
+        return launch_score_t<64>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                  n_blocks, st, cstride);
     case 128:
-        return launch_score_t<128>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
-                                   st, cstride);
+        return launch_score_t<128>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                   n_blocks, st, cstride);
     case 256:
-        return launch_score_t<256>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap, tiles,
-                                   st, cstride);
+        return launch_score_t<256>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                   n_blocks, st, cstride);
     default:
         return cudaErrorInvalidValue;
     }

@@ -242,3 +242,25 @@ def test_quant_k_partial_newest_block():
         dq, dd = q8_blocks_diff(wk, want)
         assert dq <= 1 and dd <= 1
     r.close()
+
+
+def test_scores_bit_exact_with_wide_grid():
+    """Enough (layer, 64-block) units for a full wave of scoring CTAs: the
+    float2 two-blocks-per-lane form (the full-size form) against the oracle."""
+    w = synth.Workload("wide", n_layer=16, n_head=4, n_head_kv=2, d_head=64, block_tokens=16,
+                       n_blocks=3584, budget_blocks=40, sink_blocks=1, reserve_blocks=4,
+                       n_planted=8, seed=91)
+    hist = synth.NumpyHistory(w)
+    r = kvmret.Retriever(config_for(w))
+    append_history(r, hist, cuts=[w.n_tokens // 3])
+    q = hist.queries(2)
+    for s in range(2):
+        q_sum = q[s].reshape(w.n_layer, -1).astype(np.float32)
+        q_count = np.ones(w.n_layer, np.uint32)
+        q_count[3] = 0  # a layer without a query
+        r.query_set(q_sum, q_count)
+        got = r.score()
+        want, _ = oracle_scores(hist, q_sum, q_count)
+        assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+        assert list(r.select()) == list(po.pick_topk(want, w.budget_blocks, w.sink_blocks))
+    r.close()
