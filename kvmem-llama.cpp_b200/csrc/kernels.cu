@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <type_traits>
+#include <utility>
 
 #include <cub/block/block_scan.cuh>
 
@@ -15,6 +16,29 @@
 
 namespace kvmret {
 namespace {
+
+// Programmatic dependent launch: the step's kernels are launched so that each
+// may be scheduled while its predecessor on the stream drains; every such
+// kernel calls dep_wait() (griddepcontrol.wait) before it reads anything its
+// predecessors wrote, which returns once they have completed and their writes
+// are visible.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dep(void (*kfn)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...);
+}
+
+__device__ __forceinline__ void dep_wait() { cudaGridDependencySynchronize(); }
 
 
 __device__ __forceinline__ float h2f(uint16_t h) {
@@ -31,6 +55,7 @@ template <typename T>
 __global__ void query_add_kernel(float *__restrict__ q_sum, const T *__restrict__ rows,
                                  uint32_t n_rows, uint32_t qdim, uint32_t *__restrict__ q_count,
                                  int assign) {
+    dep_wait();
     const uint32_t l = blockIdx.y;
     const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
     // the row count lives on the device; assign = the first add after a reset
@@ -57,6 +82,7 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
                              float *__restrict__ qv, float *__restrict__ nq,
                              uint8_t *__restrict__ active, uint32_t n_head, uint32_t n_head_kv,
                              uint32_t d_head, double *__restrict__ flag_col, uint32_t cstride) {
+    dep_wait();
     extern __shared__ float sv[];
     const uint32_t l = blockIdx.x, h = blockIdx.y;
     const uint32_t g = n_head_kv == 0 ? 1 : n_head / n_head_kv;
@@ -103,6 +129,7 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                                                     uint32_t n_head_kv, uint32_t ncap,
                                                     uint32_t cstride, uint32_t tiles,
                                                     uint32_t n_units, uint32_t per_cta) {
+    dep_wait();
     constexpr uint32_t TILE = 32 * V;  // blocks per unit: V per lane
     using VecT = typename std::conditional<V == 2, float2, float>::type;
     extern __shared__ float smem[];
@@ -176,6 +203,7 @@ __global__ void __launch_bounds__(128)
     reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
                   uint32_t n_layer, uint32_t stride, const uint8_t *__restrict__ has_block,
                   uint32_t n_blocks, double *__restrict__ scores) {
+    dep_wait();
     // the layers that carry a query, once per CTA
     extern __shared__ uint8_t s_act[];
     for (uint32_t l = threadIdx.x; l < n_layer; l += blockDim.x)
@@ -220,6 +248,7 @@ __global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ 
                                                      const uint8_t *__restrict__ kept,
                                                      uint32_t n, uint32_t need, int tie_high,
                                                      uint8_t *__restrict__ sel) {
+    dep_wait();
     const uint32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
     if (b >= n) return;
@@ -244,6 +273,7 @@ __global__ void __launch_bounds__(1024) select_smem_kernel(const double *__restr
                                                            const uint8_t *__restrict__ kept,
                                                            uint32_t n, uint32_t need,
                                                            int tie_high, uint8_t *__restrict__ sel) {
+    dep_wait();
     extern __shared__ double s_sc[];
     uint8_t *s_kept = reinterpret_cast<uint8_t *>(s_sc + n);
     for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
@@ -504,6 +534,7 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
 template <int D>
 __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
     assemble_kernel(const __grid_constant__ AsmLaunch a) {
+    dep_wait();
     constexpr uint32_t PAIRS = D / 4;
     JobView jv;
     if (!a.counts) {
@@ -925,6 +956,7 @@ struct ItemIter {
 template <int D, int KT>
 __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
     assemble_quant_kernel(const __grid_constant__ AsmLaunch a, uint32_t layers_per_cta) {
+    dep_wait();
     extern __shared__ __align__(16) uint8_t smem_raw[];
     constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
     constexpr uint32_t STAGE = SEG + kQTabBytes;
@@ -1138,6 +1170,7 @@ __global__ void quantize_kernel(const uint16_t *__restrict__ x, uint8_t *__restr
 constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
+    dep_wait();
     using Scan = cub::BlockScan<uint32_t, kPlanThreads>;
     __shared__ typename Scan::TempStorage ts;
     __shared__ uint32_t s_err, s_mtok, s_ftok;
@@ -1355,8 +1388,7 @@ template <int D>
 cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
     auto kfn = assemble_kernel<D>;
     if (!a.counts) {
-        kfn<<<n_jobs, kAsmThreads, 0, st>>>(a);
-        return cudaGetLastError();
+        return launch_dep(kfn, dim3(n_jobs), dim3(kAsmThreads), 0, st, a);
     }
     // persistent: as many CTAs as fit on the device at once
     static int per_sm = 0, n_sm = 0;
@@ -1370,8 +1402,8 @@ cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t 
         if (e != cudaSuccess) return e;
         if (per_sm < 1) per_sm = 1;
     }
-    kfn<<<static_cast<uint32_t>(per_sm * n_sm), kAsmThreads, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_dep(kfn, dim3(static_cast<uint32_t>(per_sm * n_sm)), dim3(kAsmThreads), 0, st,
+                      a);
 }
 
 template <int D, int KT>
@@ -1387,8 +1419,7 @@ cudaError_t launch_assemble_quant_t(const AsmLaunch &a, uint32_t n_jobs, cudaStr
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kfn<<<grid, kQThreads, smem, st>>>(al, lpc);
-    return cudaGetLastError();
+    return launch_dep(kfn, grid, dim3(kQThreads), smem, st, al, lpc);
 }
 
 }  // namespace
@@ -1397,21 +1428,21 @@ cudaError_t launch_query_add(float *q_sum, const void *rows, bool rows_f16, uint
                              uint32_t n_rows, uint32_t qdim, cudaStream_t st, uint32_t *q_count,
                              bool assign) {
     const dim3 grid((qdim + 255) / 256, n_layer);
+    const int as = assign ? 1 : 0;
     if (rows_f16)
-        query_add_kernel<uint16_t><<<grid, 256, 0, st>>>(
-            q_sum, static_cast<const uint16_t *>(rows), n_rows, qdim, q_count, assign);
-    else
-        query_add_kernel<float><<<grid, 256, 0, st>>>(q_sum, static_cast<const float *>(rows),
-                                                      n_rows, qdim, q_count, assign);
-    return cudaGetLastError();
+        return launch_dep(query_add_kernel<uint16_t>, grid, dim3(256), 0, st, q_sum,
+                          static_cast<const uint16_t *>(rows), n_rows, qdim, q_count, as);
+    return launch_dep(query_add_kernel<float>, grid, dim3(256), 0, st, q_sum,
+                      static_cast<const float *>(rows), n_rows, qdim, q_count, as);
 }
 
 cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv, float *nq,
                          uint8_t *active, uint32_t n_layer, uint32_t n_head, uint32_t n_head_kv,
                          uint32_t d_head, cudaStream_t st, double *flag_col, uint32_t cstride) {
-    qprep_kernel<<<dim3(n_layer, n_head_kv), d_head, d_head * sizeof(float), st>>>(
+    return launch_dep(qprep_kernel, dim3(n_layer, n_head_kv), dim3(d_head), d_head * sizeof(float), st,
+                      
         q_sum, q_count, qv, nq, active, n_head, n_head_kv, d_head, flag_col, cstride);
-    return cudaGetLastError();
+    
 }
 
 template <int D, int V>
@@ -1422,9 +1453,8 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
     const uint32_t n_units = tiles * n_layer;
     const uint32_t per_cta = (n_units + slots - 1) / slots;
     const uint32_t grid = (n_units + per_cta - 1) / per_cta;
-    score_kernel<D, V><<<grid, 256, smem, st>>>(summ, qv, nq, active, contrib, n_head_kv, ncap,
-                                                 cstride, tiles, n_units, per_cta);
-    return cudaGetLastError();
+    return launch_dep(score_kernel<D, V>, dim3(grid), dim3(256), smem, st, summ, qv, nq, active,
+                      contrib, n_head_kv, ncap, cstride, tiles, n_units, per_cta);
 }
 
 // As many units per CTA as it takes for one wave of resident CTAs, then as few
@@ -1478,9 +1508,8 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    reduce_kernel<<<(n_blocks + 127) / 128, 128, n_layer, st>>>(contrib, active, n_layer, stride,
-                                                               has_block, n_blocks, scores);
-    return cudaGetLastError();
+    return launch_dep(reduce_kernel, dim3((n_blocks + 127) / 128), dim3(128), n_layer, st,
+                      contrib, active, n_layer, stride, has_block, n_blocks, scores);
 }
 
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
@@ -1492,13 +1521,11 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        select_smem_kernel<<<(n_blocks + 31) / 32, 1024, smem, st>>>(scores, kept, n_blocks, need,
-                                                                    tie_higher_id, sel);
-    } else {
-        select_kernel<<<(n_blocks + 7) / 8, 256, 0, st>>>(scores, kept, n_blocks, need,
-                                                          tie_higher_id, sel);
+        return launch_dep(select_smem_kernel, dim3((n_blocks + 31) / 32), dim3(1024), smem, st,
+                          scores, kept, n_blocks, need, tie_higher_id, sel);
     }
-    return cudaGetLastError();
+    return launch_dep(select_kernel, dim3((n_blocks + 7) / 8), dim3(256), 0, st, scores, kept,
+                      n_blocks, need, tie_higher_id, sel);
 }
 
 cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
@@ -1563,8 +1590,7 @@ cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    plan_kernel<<<1, kPlanThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_dep(plan_kernel, dim3(1), dim3(kPlanThreads), smem, st, a);
 }
 
 cudaError_t launch_copy_ops(const CopyOp *ops, int n, cudaStream_t st) {
