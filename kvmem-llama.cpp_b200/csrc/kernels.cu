@@ -162,23 +162,46 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                             lane;
             const float *qh = sq + h * D;
             float d0 = 0.f, d1 = 0.f, n0 = 0.f, n1 = 0.f;
+            if constexpr (V == 2) {  // bandwidth-bound form: 2 x 16 rows per batch
 #pragma unroll 2
-            for (int dd = 0; dd < D; dd += 16) {
-                VecT k[16];
+                for (int dd = 0; dd < D; dd += 16) {
+                    float2 k[16];
 #pragma unroll
-                for (int v = 0; v < 16; ++v) k[v] = __ldg(p + static_cast<size_t>(dd + v) * dstep);
+                    for (int v = 0; v < 16; ++v)
+                        k[v] = __ldg(p + static_cast<size_t>(dd + v) * dstep);
 #pragma unroll
-                for (int v = 0; v < 16; ++v) {
-                    const float q = qh[dd + v];
-                    if constexpr (V == 2) {
+                    for (int v = 0; v < 16; ++v) {
+                        const float q = qh[dd + v];
                         d0 = __fadd_rn(d0, __fmul_rn(q, k[v].x));
                         d1 = __fadd_rn(d1, __fmul_rn(q, k[v].y));
                         n0 = __fadd_rn(n0, __fmul_rn(k[v].x, k[v].x));
                         n1 = __fadd_rn(n1, __fmul_rn(k[v].y, k[v].y));
-                    } else {
-                        d0 = __fadd_rn(d0, __fmul_rn(q, k[v]));
-                        n0 = __fadd_rn(n0, __fmul_rn(k[v], k[v]));
                     }
+                }
+            } else {
+                // latency-bound form (few layers): the next 16 d rows are loaded
+                // before the current ones are consumed (the compiler barrier
+                // keeps the loads ahead of the dependent sums)
+                constexpr int RB = 16;
+                float cur[RB], nxt[RB];
+#pragma unroll
+                for (int v = 0; v < RB; ++v) cur[v] = __ldg(p + static_cast<size_t>(v) * dstep);
+#pragma unroll 1
+                for (int dd = 0; dd < D; dd += RB) {
+                    if (dd + RB < D) {
+#pragma unroll
+                        for (int v = 0; v < RB; ++v)
+                            nxt[v] = __ldg(p + static_cast<size_t>(dd + RB + v) * dstep);
+                    }
+                    asm volatile("" ::: "memory");
+#pragma unroll
+                    for (int v = 0; v < RB; ++v) {
+                        const float q = qh[dd + v];
+                        d0 = __fadd_rn(d0, __fmul_rn(q, cur[v]));
+                        n0 = __fadd_rn(n0, __fmul_rn(cur[v], cur[v]));
+                    }
+#pragma unroll
+                    for (int v = 0; v < RB; ++v) cur[v] = nxt[v];
                 }
             }
             const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * n_head_kv + h]);
@@ -1479,8 +1502,11 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
         return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
                                      tiles64, slots, smem64, st, cstride);
     const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 1>, 256, smem32);
+    if (e != cudaSuccess) return e;
+    const uint32_t slots1 = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
     return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                 (n_blocks + 31) / 32, slots, smem32, st, cstride);
+                                 (n_blocks + 31) / 32, slots1, smem32, st, cstride);
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
