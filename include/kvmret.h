@@ -261,6 +261,21 @@ int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
 int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* ---- layer-sharded exchange over NVLink peer memory (no collective
+ *      library). One context per rank, each holding n_layer of
+ *      the world * n_layer layers in rank order. Set-up (once): every rank
+ *      calls kvmret_exchange_export, the 64-byte handles are all-gathered by
+ *      the caller (any host channel), every rank calls kvmret_exchange_import.
+ *      Per step, kvmret_score_exchange replaces kvmret_score_layers + the
+ *      caller's all-gather + kvmret_score_reduce: the scoring kernel writes this
+ *      rank's per-layer terms into every rank's receive buffer and publishes
+ *      the step; the reduction waits (at most 2 s; a timeout is reported by the
+ *      next collect as plan error 0x100) for every rank's step and reduces all
+ *      layers in global order. Then kvmret_select_apply_async as usual. ---- */
+int kvmret_exchange_export(kvmret_ctx *ctx, uint32_t world, void *handle_out);
+int kvmret_exchange_import(kvmret_ctx *ctx, uint32_t rank, uint32_t world, const void *handles);
+int kvmret_score_exchange(kvmret_ctx *ctx);
+
 /* ---- session lanes (config 5: several conversations per GPU, stepped
  *      together; the reference keeps one KvMemStore per lane,
  *      src/adapter/llama-memory-kvmem.cpp:1624-1714) ----

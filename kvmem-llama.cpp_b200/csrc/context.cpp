@@ -122,6 +122,14 @@ struct kvmret_ctx {
     float *pf_s = nullptr;
     uint32_t *pf_err = nullptr;
     uint32_t pf_rows = 0, pf_nrows = 0, mhat_valid = 0;
+    // layer-sharded exchange over peer memory (kvmret_exchange_*): one region
+    // per rank = 2 halves (step parity) of [world * n_layer][cstride] rows,
+    // then flags [kMaxRanks], counter, err; peer regions opened via CUDA IPC
+    uint8_t *ex_region = nullptr;
+    uint8_t *ex_peer[kvmret::kMaxRanks] = {};
+    uint32_t ex_world = 0, ex_rank = 0, ex_step = 0;
+    uint64_t ex_half = 0;  // doubles per half
+    uint64_t ex_tail = 0;  // byte offset of the flags
     // host
     uint8_t *repo_host = nullptr, *repo_dev = nullptr;
     uint8_t *pin_flags = nullptr;  // kept / selection flags staging
@@ -225,6 +233,9 @@ void prof_end(kvmret_ctx *c, cudaStream_t s, int idx) {
 void free_all(kvmret_ctx *c) {
     if (c->cfg.device >= 0) cudaSetDevice(c->cfg.device);
     if (c->st) cudaStreamSynchronize(c->st);
+    for (uint32_t p = 0; p < kvmret::kMaxRanks; ++p)
+        if (c->ex_peer[p] && c->ex_peer[p] != c->ex_region) cudaIpcCloseMemHandle(c->ex_peer[p]);
+    if (c->ex_region) cudaFree(c->ex_region);
     void *dev[] = {c->summ, c->tail_sum, c->q_sum, c->qv, c->nq, c->q_count_dev, c->has_block,
                    c->active, c->kept_dev, c->sel_dev, c->contrib, c->scores, c->pool,
                    c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab, c->d_win_id,
@@ -419,6 +430,9 @@ int plan_and_assemble(kvmret_ctx *c) {
     pa.jobs = c->jobs_dev;
     pa.counts = c->d_counts;
     pa.ids = c->d_ids;
+    pa.ext_err = c->ex_world > 1 ? reinterpret_cast<const uint32_t *>(c->ex_region + c->ex_tail +
+                                                                     4 * (kvmret::kMaxRanks + 1))
+                                 : nullptr;
     CK(kvmret::launch_plan(pa, c->st));
     kvmret::AsmLaunch al{};
     al.jobs = c->jobs_dev;
@@ -1351,4 +1365,90 @@ int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uin
         TRY(kvmret_select_apply_async(c, nm && mandatory ? mandatory[i] : nullptr, nm));
     }
     return lanes_join(g, caller);
+}
+
+// ---------------------------------------------------------------------------
+// Layer-sharded exchange over NVLink peer memory: each rank's scoring kernel
+// writes its rows straight into every rank's receive buffer and publishes a
+// step flag; each rank's reduction waits for all flags (bounded) and reduces
+// all layers in global order. No collective library is involved.
+
+int kvmret_exchange_export(kvmret_ctx *c, uint32_t world, void *handle_out) {
+    NEED_CTX(c);
+    if (world < 2 || world > kvmret::kMaxRanks || !handle_out)
+        return fail(KVMRET_ERR_ARG, "exchange needs 2..%d ranks and a handle buffer",
+                    kvmret::kMaxRanks);
+    if (c->ex_region) return fail(KVMRET_ERR_STATE, "exchange already set up");
+    const uint64_t half = static_cast<uint64_t>(world) * c->cfg.n_layer * c->cstride;
+    const uint64_t tail = align_up(2 * half * sizeof(double), 256);
+    const uint64_t bytes = tail + 256;
+    TRY(dmalloc(&c->ex_region, bytes));
+    CK(cudaMemset(c->ex_region, 0, bytes));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->ex_region));
+    std::memcpy(handle_out, &h, sizeof(h));
+    c->ex_half = half;
+    c->ex_tail = tail;
+    c->ex_world = world;
+    return KVMRET_OK;
+}
+
+int kvmret_exchange_import(kvmret_ctx *c, uint32_t rank, uint32_t world, const void *handles) {
+    NEED_CTX(c);
+    if (!c->ex_region || world != c->ex_world || rank >= world || !handles)
+        return fail(KVMRET_ERR_ARG, "export first, with the same rank count");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    for (uint32_t p = 0; p < world; ++p) {
+        if (p == rank) {
+            c->ex_peer[p] = c->ex_region;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + 64ull * p, sizeof(h));
+        void *ptr = nullptr;
+        CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        c->ex_peer[p] = static_cast<uint8_t *>(ptr);
+    }
+    c->ex_rank = rank;
+    return KVMRET_OK;
+}
+
+int kvmret_score_exchange(kvmret_ctx *c) {
+    NEED_CTX(c);
+    if (!c->ex_region || !c->ex_peer[c->ex_rank])
+        return fail(KVMRET_ERR_STATE, "exchange not set up");
+    const uint32_t W = c->ex_world, L = c->cfg.n_layer;
+    const uint32_t step = ++c->ex_step;
+    const uint64_t half_off = (step & 1u) * c->ex_half;
+    const uint64_t slice = half_off + static_cast<uint64_t>(c->ex_rank) * L * c->cstride;
+    double *local = reinterpret_cast<double *>(c->ex_region) + slice;
+    kvmret::Peers pr{};
+    for (uint32_t p = 0; p < W; ++p) {
+        pr.rows[p] = reinterpret_cast<double *>(c->ex_peer[p]) + slice;
+        pr.flags[p] = reinterpret_cast<uint32_t *>(c->ex_peer[p] + c->ex_tail);
+    }
+    uint32_t *tail = reinterpret_cast<uint32_t *>(c->ex_region + c->ex_tail);
+    pr.counter = tail + kvmret::kMaxRanks;
+    pr.n = W;
+    pr.rank = c->ex_rank;
+    pr.step = step;
+    pr.n_layer = L;
+    // qprep writes the query flags into the local slice; the scoring kernel
+    // pushes the slice to every peer and signals
+    c->q_dirty = true;
+    TRY(settle_query(c));
+    CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, L, c->cfg.n_head,
+                            c->cfg.n_head_kv, c->cfg.d_head, c->st, local, c->cstride));
+    c->q_dirty = false;
+    const uint32_t n = c->table.n_blocks();
+    const int prs = prof_begin(c, c->st, PR_SCORE);
+    CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, local, L, c->cfg.n_head_kv,
+                            c->cfg.d_head, c->ncap, n, c->st, c->cstride, &pr));
+    prof_end(c, c->st, prs);
+    c->prof.score_bytes += static_cast<uint64_t>(L) * c->E * ((n + 63) / 64 * 64) * sizeof(float);
+    CK(kvmret::launch_reduce(reinterpret_cast<double *>(c->ex_region) + half_off, nullptr, W * L,
+                             c->cstride, c->has_block, n, c->scores, c->st, tail, W, step,
+                             tail + kvmret::kMaxRanks + 1));
+    c->prof.launches += 3;
+    return KVMRET_OK;
 }

@@ -114,6 +114,37 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
 }
 
 // ---------------------------------------------------------------------------
+// Exchange signal, run by every CTA of a scoring launch at its end: the CTA's
+// peer stores are fenced at system scope, and the last CTA to finish (device
+// counter) pushes the layer query flags (the rows' last column, written by
+// qprep), fences again and publishes the step number in every rank's flag
+// slot for this rank. The receiver reads rows only after it has seen the flag
+// (acquire), so the rows are complete when read.
+__device__ void exchange_signal(const Peers &peers, const double *local, uint32_t cstride) {
+    __threadfence_system();
+    __syncthreads();
+    __shared__ uint32_t s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(peers.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (uint32_t l = threadIdx.x; l < peers.n_layer; l += blockDim.x) {
+        const double f = local[static_cast<size_t>(l) * cstride + cstride - 1];
+        for (uint32_t p = 0; p < peers.n; ++p)
+            if (p != peers.rank) peers.rows[p][static_cast<size_t>(l) * cstride + cstride - 1] = f;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *peers.counter = 0;
+        for (uint32_t p = 0; p < peers.n; ++p)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flags[p] + peers.rank),
+                         "r"(peers.step)
+                         : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // S3: a unit = one layer x TILE blocks (64: lane j walks blocks 2j, 2j+1 with
 // float2 loads; 32: one block per lane). Summaries are block-minor
 // [L][Hkv][D][ncap], so each d step of a warp reads 256 (128) contiguous
@@ -128,7 +159,8 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                                                     double *__restrict__ contrib,
                                                     uint32_t n_head_kv, uint32_t ncap,
                                                     uint32_t cstride, uint32_t tiles,
-                                                    uint32_t n_units, uint32_t per_cta) {
+                                                    uint32_t n_units, uint32_t per_cta,
+                                                    const __grid_constant__ Peers peers) {
     dep_wait();
     constexpr uint32_t TILE = 32 * V;  // blocks per unit: V per lane
     using VecT = typename std::conditional<V == 2, float2, float>::type;
@@ -216,22 +248,53 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
             double layer = 0.0;
             for (uint32_t h = 0; h < n_head_kv; ++h)
                 layer = __dadd_rn(layer, static_cast<double>(cosb[h * TILE + t]));
-            out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
+            const double term = __ddiv_rn(layer, static_cast<double>(n_head_kv));
+            out[t] = term;
+            // exchange: the same term into this rank's slice of every peer's buffer
+            for (uint32_t p = 0; p < peers.n; ++p)
+                if (p != peers.rank)
+                    peers.rows[p][static_cast<size_t>(l) * cstride + b0 + t] = term;
         }
     }
+    if (peers.n > 1) exchange_signal(peers, contrib, cstride);
 }
 
 // S3 epilogue (:4189-4193): acc over layers in order, score = acc / nlay.
 __global__ void __launch_bounds__(128)
     reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
                   uint32_t n_layer, uint32_t stride, const uint8_t *__restrict__ has_block,
-                  uint32_t n_blocks, double *__restrict__ scores) {
+                  uint32_t n_blocks, double *__restrict__ scores, const uint32_t *wait_flags,
+                  uint32_t wait_n, uint32_t wait_step, uint32_t *err) {
     dep_wait();
+    if (wait_flags) {  // peer-memory exchange: every rank's rows of this step have landed
+        if (threadIdx.x == 0) {
+            uint64_t t0 = 0;
+            for (uint32_t p = 0; p < wait_n; ++p) {
+                for (uint32_t i = 0;; ++i) {
+                    uint32_t v;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];"
+                                 : "=r"(v)
+                                 : "l"(wait_flags + p)
+                                 : "memory");
+                    if (static_cast<int32_t>(v - wait_step) >= 0) break;
+                    uint64_t now;
+                    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
+                    if (i == 0) t0 = now;
+                    if (now - t0 > 2000000000ull) {  // 2 s: a rank is gone
+                        atomicExch(err, 1u);
+                        break;
+                    }
+                    __nanosleep(200);
+                }
+            }
+        }
+        __syncthreads();
+    }
     // the layers that carry a query, once per CTA
     extern __shared__ uint8_t s_act[];
     for (uint32_t l = threadIdx.x; l < n_layer; l += blockDim.x)
         s_act[l] = active ? active[l]
-                          : (contrib[static_cast<size_t>(l) * stride + stride - 1] != 0.0);
+                          : (__ldcg(contrib + static_cast<size_t>(l) * stride + stride - 1) != 0.0);
     __syncthreads();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n_blocks) return;
@@ -246,7 +309,8 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
         for (uint32_t u = 0; u < 16; ++u) {  // 16 independent loads in flight
             const uint32_t l = l0 + u;
-            v[u] = (l < n_layer && s_act[l]) ? __ldg(contrib + static_cast<size_t>(l) * stride + b)
+            // L2-coherent loads: rows may have been written by peer GPUs
+            v[u] = (l < n_layer && s_act[l]) ? __ldcg(contrib + static_cast<size_t>(l) * stride + b)
                                              : 0.0;
         }
 #pragma unroll
@@ -1370,7 +1434,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
         a.counts[1] = n_fresh;
         a.counts[2] = n_sel;
         a.counts[3] = ttotal;
-        a.counts[4] = s_err;
+        a.counts[4] = s_err | ((a.ext_err && *a.ext_err) ? 0x100u : 0u);
         a.counts[5] = s_mtok;
         a.counts[6] = s_ftok;
         a.counts[7] = 0;  // the assembly's work-unit counter
@@ -1472,12 +1536,12 @@ template <int D, int V>
 cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
                             const uint8_t *active, double *contrib, uint32_t n_layer,
                             uint32_t n_head_kv, uint32_t ncap, uint32_t tiles, uint32_t slots,
-                            size_t smem, cudaStream_t st, uint32_t cstride) {
+                            size_t smem, cudaStream_t st, uint32_t cstride, const Peers &peers) {
     const uint32_t n_units = tiles * n_layer;
     const uint32_t per_cta = (n_units + slots - 1) / slots;
     const uint32_t grid = (n_units + per_cta - 1) / per_cta;
     return launch_dep(score_kernel<D, V>, dim3(grid), dim3(256), smem, st, summ, qv, nq, active,
-                      contrib, n_head_kv, ncap, cstride, tiles, n_units, per_cta);
+                      contrib, n_head_kv, ncap, cstride, tiles, n_units, per_cta, peers);
 }
 
 // As many units per CTA as it takes for one wave of resident CTAs, then as few
@@ -1488,7 +1552,7 @@ template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
                            uint32_t n_head_kv, uint32_t ncap, uint32_t n_blocks, cudaStream_t st,
-                           uint32_t cstride) {
+                           uint32_t cstride, const Peers &peers) {
     int per_sm = 0, n_sm = 0, dev = 0;
     const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
     cudaError_t e = cudaGetDevice(&dev);
@@ -1500,31 +1564,33 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
     const uint32_t tiles64 = (n_blocks + 63) / 64;
     if (tiles64 * n_layer >= slots)
         return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                     tiles64, slots, smem64, st, cstride);
+                                     tiles64, slots, smem64, st, cstride, peers);
     const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 1>, 256, smem32);
     if (e != cudaSuccess) return e;
     const uint32_t slots1 = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
     return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                 (n_blocks + 31) / 32, slots1, smem32, st, cstride);
+                                 (n_blocks + 31) / 32, slots1, smem32, st, cstride, peers);
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
-                         cudaStream_t st, uint32_t cstride) {
+                         cudaStream_t st, uint32_t cstride, const Peers *peers_in) {
     if (cstride == 0) cstride = ncap;
     if (n_blocks == 0) return cudaSuccess;
+    Peers none{};
+    const Peers &peers = peers_in ? *peers_in : none;
     switch (d_head) {
     case 64:
         return launch_score_t<64>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                  n_blocks, st, cstride);
+                                   n_blocks, st, cstride, peers);
     case 128:
         return launch_score_t<128>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                   n_blocks, st, cstride);
+                                   n_blocks, st, cstride, peers);
     case 256:
         return launch_score_t<256>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                   n_blocks, st, cstride);
+                                   n_blocks, st, cstride, peers);
     default:
         return cudaErrorInvalidValue;
     }
@@ -1532,10 +1598,12 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
 
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
-                          double *scores, cudaStream_t st) {
+                          double *scores, cudaStream_t st, const uint32_t *wait_flags,
+                          uint32_t wait_n, uint32_t wait_step, uint32_t *err) {
     if (n_blocks == 0) return cudaSuccess;
     return launch_dep(reduce_kernel, dim3((n_blocks + 127) / 128), dim3(128), n_layer, st,
-                      contrib, active, n_layer, stride, has_block, n_blocks, scores);
+                      contrib, active, n_layer, stride, has_block, n_blocks, scores, wait_flags,
+                      wait_n, wait_step, err);
 }
 
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,

@@ -59,16 +59,32 @@ cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv,
 
 // S3: per (layer, block) term layer_sum / n_head_kv into contrib rows of
 // cstride doubles (0 = ncap).
+// Peer-memory exchange of the layer-sharded score rows (NVLink, no
+// collective): rows[p] is this rank's row slice inside rank p's receive
+// buffer, flags[p] rank p's per-rank step flags; counter is a device word the
+// last CTA uses to know every CTA has pushed its rows.
+constexpr int kMaxRanks = 8;
+struct Peers {
+    double *rows[kMaxRanks];
+    uint32_t *flags[kMaxRanks];
+    uint32_t *counter;
+    uint32_t n, rank, step, n_layer;
+};
+
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap,
-                         uint32_t n_blocks, cudaStream_t st, uint32_t cstride = 0);
+                         uint32_t n_blocks, cudaStream_t st, uint32_t cstride = 0,
+                         const Peers *peers = nullptr);
 
 // S3 epilogue: layer-ordered sum, / number of layers with a query. With
 // active == nullptr the flags are read from each row's last column.
+// With wait_flags, each CTA first waits (at most 2 s) until every one of the
+// wait_n ranks' flags has reached wait_step; on a timeout it sets *err.
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
-                          double *scores, cudaStream_t st);
+                          double *scores, cudaStream_t st, const uint32_t *wait_flags = nullptr,
+                          uint32_t wait_n = 0, uint32_t wait_step = 0, uint32_t *err = nullptr);
 
 // S6: sel[b] = kept[b] || (rank of b among non-kept blocks < need).
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
@@ -125,6 +141,7 @@ struct PlanArgs {
     Job *jobs;          // [2 * win_slots]: moved, then fresh at + win_slots
     uint32_t *counts;   // [8]
     uint32_t *ids;      // [win_slots]
+    const uint32_t *ext_err;  // optional: a nonzero word here is reported as error 0x100
 };
 cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st);
 size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots);

@@ -149,6 +149,9 @@ SIGNATURES = {
                                         ctypes.c_float, _U32, _P]),
     "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
     "kvmret_prefill_score": (ctypes.c_int, [_P, _P, _U32, _U32, _P, _P, _PU32]),
+    "kvmret_exchange_export": (ctypes.c_int, [_P, _U32, _P]),
+    "kvmret_exchange_import": (ctypes.c_int, [_P, _U32, _U32, _P]),
+    "kvmret_score_exchange": (ctypes.c_int, [_P]),
     "kvmret_lanes_create": (ctypes.c_int, [ctypes.POINTER(_P), _U32, ctypes.POINTER(_P)]),
     "kvmret_lanes_destroy": (None, [_P]),
     "kvmret_lanes_score_layers": (ctypes.c_int, [_P, _P, _P]),
@@ -392,6 +395,24 @@ class Retriever:
                                             ctypes.byref(n)))
         return (sel.cpu().numpy()[:nb], n.value,
                 sc.cpu().numpy()[:, :nb] if sc is not None else None)
+
+    def exchange_export(self, world) -> bytes:
+        """Peer-memory exchange set-up, step 1: this rank's 64-byte IPC handle."""
+        buf = (ctypes.c_uint8 * 64)()
+        _check(lib.kvmret_exchange_export(self.h, world, buf))
+        return bytes(buf)
+
+    def exchange_import(self, rank, handles):
+        """Step 2: every rank's handle, in rank order."""
+        raw = b"".join(handles)
+        buf = (ctypes.c_uint8 * len(raw)).from_buffer_copy(raw)
+        _check(lib.kvmret_exchange_import(self.h, rank, len(handles), buf))
+
+    def score_exchange(self):
+        """Score this rank's layers, push the rows to every rank, wait for all
+        ranks' rows and reduce (replaces score_layers + all-gather + score_reduce)."""
+        with _Ordered(self.stream_ptr):
+            _check(lib.kvmret_score_exchange(self.h))
 
     def select_apply_async(self, mandatory=()):
         """Top-k + device plan + assembly, enqueued without host synchronisation."""

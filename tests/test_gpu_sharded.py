@@ -1,6 +1,8 @@
 """Layer-sharded retrieval on 2 GPUs: each rank's context owns half of the
 layers; the per-(layer, block) score terms, with each layer's query flag in
-the last column of its row, are all-gathered over NCCL and reduced in global layer order, so every rank
+the last column of its row, are exchanged (an NCCL all-gather, or the
+scoring kernel's own writes into every rank's buffer over NVLink peer memory)
+and reduced in global layer order, so every rank
 selects the same blocks as the single-context oracle, bit for bit, and
 assembles its own layers' windows. Skipped with fewer than 2 GPUs.
 """
@@ -23,7 +25,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, exchange="nccl"):
     import sys
     from datetime import timedelta
     here = os.path.dirname(os.path.abspath(__file__))
@@ -51,6 +53,10 @@ def _rank(rank, world, port, out):
     stride = r.contrib_stride
     c_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
     c_all = torch.zeros(w.n_layer * stride, dtype=torch.float64, device="cuda")
+    if exchange == "p2p":
+        handles = [None] * world
+        dist.all_gather_object(handles, r.exchange_export(world))
+        r.exchange_import(rank, handles)
     q = hist.queries(3)
     res = []
     # the same three queries twice: through select + apply, then through the
@@ -59,11 +65,14 @@ def _rank(rank, world, port, out):
         r.query_reset()
         r.query_add(torch.from_numpy(np.ascontiguousarray(
             q[s % 3].reshape(w.n_layer, 1, -1)[sl])).cuda())
-        r.score_layers(c_loc)
-        r.sync()
-        dist.all_gather_into_tensor(c_all, c_loc)
-        torch.cuda.synchronize()
-        r.score_reduce(c_all, w.n_layer)
+        if exchange == "p2p":
+            r.score_exchange()
+        else:
+            r.score_layers(c_loc)
+            r.sync()
+            dist.all_gather_into_tensor(c_all, c_loc)
+            torch.cuda.synchronize()
+            r.score_reduce(c_all, w.n_layer)
         if s < 3:
             ids = r.select()
             r.apply(ids)
@@ -78,7 +87,8 @@ def _rank(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_layer_sharded_selection_matches_oracle():
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_two_gpu_layer_sharded_selection_matches_oracle(exchange):
     import pyoracle as po
     from kvm_helpers import oracle_scores
     from kvmret import synth
@@ -89,7 +99,7 @@ def test_two_gpu_layer_sharded_selection_matches_oracle():
     mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, out, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
