@@ -11,9 +11,12 @@ its window position, V copied).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
 
 N > 1 runs under torchrun, one rank per GPU, each owning n_layer / N layers;
-the only cross-rank traffic is one NCCL all-gather per step of the
-per-(layer, block) score terms (f64) with each layer's query flag packed in
-its row, ~1 MiB in total at 64 layers.
+the only cross-rank traffic per step is the per-(layer, block) score terms
+(f64, each layer's query flag packed in its row, ~1 MiB in total at 64
+layers): by default the scoring kernel writes them into every rank's buffer
+over NVLink peer memory (CUDA IPC, set up once through the process group) and
+the reduction waits on per-rank step flags; --exchange nccl uses an NCCL
+all-gather instead.
 """
 from __future__ import annotations
 
@@ -282,23 +285,34 @@ def run_ours(args, w):
             e.record(ext)
             marks.append((label, e))
 
+    p2p = world > 1 and args.exchange == "p2p"
+    if p2p:  # peer-memory exchange: IPC handles all-gathered once over the process group
+        handles = [None] * world
+        dist.all_gather_object(handles, r.exchange_export(world))
+        r.exchange_import(rank, handles)
+
     def step(q_dev):
         mark("start")
         r.query_reset()
         r.query_add(q_dev)
         mark("query")
-        r.score_layers(contrib_loc)
-        mark("score")
-        if world > 1:
-            ev = torch.cuda.Event()
-            ev.record(ext)
-            cur.wait_event(ev)
-            dist.all_gather_into_tensor(contrib_all, contrib_loc)
-            ev2 = torch.cuda.Event()
-            ev2.record(cur)
-            ext.wait_event(ev2)
-        mark("exchange")
-        r.score_reduce(contrib_all, w.n_layer)
+        if p2p:  # score + push rows to every rank + wait + reduce, all on the device
+            r.score_exchange()
+            mark("score")
+            mark("exchange")
+        else:
+            r.score_layers(contrib_loc)
+            mark("score")
+            if world > 1:
+                ev = torch.cuda.Event()
+                ev.record(ext)
+                cur.wait_event(ev)
+                dist.all_gather_into_tensor(contrib_all, contrib_loc)
+                ev2 = torch.cuda.Event()
+                ev2.record(cur)
+                ext.wait_event(ev2)
+            mark("exchange")
+            r.score_reduce(contrib_all, w.n_layer)
         r.select_apply_async()
         mark("apply_enqueued")
 
@@ -452,6 +466,7 @@ def run_ours(args, w):
                             f"budget {w.budget_blocks} blocks, sink {w.sink_blocks}, gen-reserve "
                             f"{w.reserve_blocks} slots",
                 "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
+                "exchange": (args.exchange if world > 1 else None),
                 "l2": "inputs larger than L2 (summaries "
                       f"{score_step / 2**20:.0f} MiB/step, window/pool GiB-scale)",
                 "pool_cache": bool(args.pool_cache)},
@@ -851,6 +866,9 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: score-row exchange through NVLink peer memory written by the "
+                         "scoring kernel (default), or an NCCL all-gather")
     ap.add_argument("--print-steps", action="store_true",
                     help="print each timed step's window-assembly counts to stderr (diagnostic)")
     ap.add_argument("--timeline", action="store_true",

@@ -114,14 +114,15 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
 }
 
 // ---------------------------------------------------------------------------
-// Exchange signal, run by every CTA of a scoring launch at its end: the CTA's
-// peer stores are fenced at system scope, and the last CTA to finish (device
-// counter) pushes the layer query flags (the rows' last column, written by
-// qprep), fences again and publishes the step number in every rank's flag
-// slot for this rank. The receiver reads rows only after it has seen the flag
-// (acquire), so the rows are complete when read.
+// Exchange signal, run by every CTA of a scoring launch at its end (its rows
+// were already stored into every peer's buffer by the epilogue). A CTA's
+// stores are ordered before its increment of the device counter (gpu-scope
+// fence); the last CTA, having observed every increment, pushes the layer
+// query flags (the rows' last column, written by qprep), fences at system
+// scope and publishes the step number in every rank's flag slot for this
+// rank with a release store. The receiver acquires the flag before it reads.
 __device__ void exchange_signal(const Peers &peers, const double *local, uint32_t cstride) {
-    __threadfence_system();
+    __threadfence();
     __syncthreads();
     __shared__ uint32_t s_last;
     if (threadIdx.x == 0) s_last = atomicAdd(peers.counter, 1u) == gridDim.x - 1;
@@ -129,7 +130,7 @@ __device__ void exchange_signal(const Peers &peers, const double *local, uint32_
     if (!s_last) return;
     __threadfence();
     for (uint32_t l = threadIdx.x; l < peers.n_layer; l += blockDim.x) {
-        const double f = local[static_cast<size_t>(l) * cstride + cstride - 1];
+        const double f = __ldcg(local + static_cast<size_t>(l) * cstride + cstride - 1);
         for (uint32_t p = 0; p < peers.n; ++p)
             if (p != peers.rank) peers.rows[p][static_cast<size_t>(l) * cstride + cstride - 1] = f;
     }
