@@ -12,7 +12,11 @@
 // selection and the assembly.
 #include <cuda_runtime.h>
 
+#include <sys/syscall.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <cctype>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -276,6 +280,38 @@ int hmalloc(T **p, size_t bytes, unsigned flags) {
     return KVMRET_OK;
 }
 
+// NUMA node of a GPU's PCIe attachment (-1 when unknown).
+int gpu_numa_node(int device) {
+    char bus[32] = {};
+    if (cudaDeviceGetPCIBusId(bus, sizeof(bus), device) != cudaSuccess) return -1;
+    for (char *q = bus; *q; ++q) *q = static_cast<char>(std::tolower(*q));
+    char path[128];
+    std::snprintf(path, sizeof(path), "/sys/bus/pci/devices/%s/numa_node", bus);
+    FILE *f = std::fopen(path, "r");
+    if (!f) return -1;
+    int node = -1;
+    if (std::fscanf(f, "%d", &node) != 1) node = -1;
+    std::fclose(f);
+    return node;
+}
+
+// Pinned allocation whose pages are placed on `node` (preferred policy for
+// the calling thread while the driver pins them), so the GPU reads its
+// repository without crossing the inter-socket link. Falls back silently to
+// the default placement.
+template <typename T>
+int hmalloc_near(T **p, size_t bytes, unsigned flags, int node) {
+    constexpr long kMpolDefault = 0, kMpolPreferred = 1;
+    bool bound = false;
+    if (node >= 0 && node < 64) {
+        unsigned long mask = 1ul << node;
+        bound = syscall(SYS_set_mempolicy, kMpolPreferred, &mask, 64ul) == 0;
+    }
+    const int rc = hmalloc(p, bytes, flags);
+    if (bound) syscall(SYS_set_mempolicy, kMpolDefault, nullptr, 0ul);
+    return rc;
+}
+
 int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     c->cfg = cfg;
     const kvmret_config &k = c->cfg;
@@ -362,7 +398,8 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
     CK(kvmret::launch_rope_table(c->rope_tab, n_pos, k.n_rot / 2, c->theta, c->st));
 
     const size_t repo_bytes = static_cast<size_t>(k.max_blocks) * c->slot_bytes;
-    TRY(hmalloc(&c->repo_host, repo_bytes, cudaHostAllocMapped | cudaHostAllocPortable));
+    TRY(hmalloc_near(&c->repo_host, repo_bytes, cudaHostAllocMapped | cudaHostAllocPortable,
+                     gpu_numa_node(k.device)));
     CK(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->repo_dev), c->repo_host, 0));
     TRY(hmalloc(&c->pin_flags, c->ncap, cudaHostAllocDefault));
     TRY(hmalloc(&c->pin_rb, kRing * (8 + W) * sizeof(uint32_t), cudaHostAllocDefault));
