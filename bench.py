@@ -28,6 +28,8 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "kvmem-llama.cpp_b200")
 sys.path.insert(0, PKG)
@@ -331,13 +333,28 @@ def run_ours(args, w):
     clocks = Clocks(local)
     time.sleep(0.6)
     # warm-up (the first step stages the whole window from the host)
-    for q in queries(args.warmup):
-        step(q)
-        r.step_collect()
-    r.sync()
+    warm_q = queries(args.warmup)
+    step(warm_q[0])
+    ids0 = r.step_collect()[0]
+
+    def restart():
+        """Untimed: the start state both measured loops begin from. An empty
+        working set and pool (kvmret_clear_working_set), the first warm-up
+        step's selection staged again, then the other warm-up steps; the state
+        (window, pool contents and LRU order) is then a function of these
+        queries alone, so the e2e loop repeats the timed loop's work exactly."""
+        r.clear_working_set(drop_pool=True)
+        r.apply(ids0)
+        for q in warm_q[1:]:
+            step(q)
+            r.step_collect()
+        r.sync()
+
+    restart()
 
     # timed region: device time of exactly K steps on the library stream
     qs = queries(args.steps)
+    qh = [q.cpu().pin_memory() for q in qs]  # the same K queries for the e2e loop
     torch.cuda.synchronize()
     r.prof_enable(True)
     barrier()
@@ -345,6 +362,7 @@ def run_ours(args, w):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stats = []
+    ids_timed = []
     marks.clear()
     e0.record(ext)
     # the host enqueues step k+1 before collecting step k, so the device never
@@ -354,10 +372,14 @@ def run_ours(args, w):
     for i, q in enumerate(qs):
         step(q)
         if i > 0:
-            stats.append(r.step_collect()[1])
+            ids_k, st_k = r.step_collect()
+            ids_timed.append(ids_k)
+            stats.append(st_k)
     torch.cuda.nvtx.range_pop()
     e1.record(ext)
-    stats.append(r.step_collect()[1])
+    ids_k, st_k = r.step_collect()
+    ids_timed.append(ids_k)
+    stats.append(st_k)
     r.sync()
     torch.cuda.synchronize()
     barrier()
@@ -386,8 +408,10 @@ def run_ours(args, w):
         ms = float(t.item())
     ms_step = ms / args.steps
 
-    # e2e: host query buffer -> device every step, ids back on the host
-    qh = [q.cpu().pin_memory() for q in queries(args.steps)]
+    # e2e: the same K queries from pinned host memory -> device every step, ids
+    # back on the host, from the same start state as the timed loop (its
+    # selections and per-step work are checked against the timed loop's below)
+    restart()
     qd = torch.empty_like(qs[0])
     barrier()
     torch.cuda.synchronize()
@@ -403,6 +427,7 @@ def run_ours(args, w):
             e2e_stats.append(st_k)
     ids_k, st_k = r.step_collect()
     e2e_ids.append(ids_k)
+    e2e_stats.append(st_k)
     r.sync()
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
@@ -415,6 +440,11 @@ def run_ours(args, w):
 
     def avg(key, ss):
         return sum(s[key] for s in ss) / len(ss)
+
+    e2e_same = (len(e2e_ids) == len(ids_timed) and
+                all(np.array_equal(a, b) for a, b in zip(e2e_ids, ids_timed)) and
+                all(a["n_moved"] == b["n_moved"] and a["n_h2d_blocks"] == b["n_h2d_blocks"]
+                    for a, b in zip(e2e_stats, stats)))
 
     n_h2d = avg("n_h2d_blocks", stats)
     n_moved = avg("n_moved", stats)
@@ -445,10 +475,10 @@ def run_ours(args, w):
     kv_bytes = score_step + h2d_step + asm_step
     # DRAM traffic of one assembly launch: the ratio of ncu's dram read + write
     # bytes to the launch's algorithmic bytes, measured on an 8-layer cut of
-    # the same workload (profiles/step_kernels_cfg2_l8.md: 1564.6 / 1585.4 MB;
+    # the same workload (profiles/step_kernels_cfg2_l8.md: 1556.8 / 1585.4 MB;
     # profiles/assemble_quant_kernel_cfg3_l8.md: 793.3 / 824.7 MB), scaled to
     # this launch's algorithmic bytes (the traffic grows with the blocks moved).
-    traffic_ratio = (1564.6 / 1585.4) if w.k_type == kvmret.TYPE_F16 else (793.3 / 824.7)
+    traffic_ratio = (1556.8 / 1585.4) if w.k_type == kvmret.TYPE_F16 else (793.3 / 824.7)
     asm_traffic = traffic_ratio * asm_hbm
 
     line = None
@@ -497,8 +527,11 @@ def run_ours(args, w):
             "churn": {"n_h2d_blocks": round(n_h2d, 2), "n_moved": round(n_moved, 2),
                       "n_assembled": round(n_asm, 2)},
             "e2e": {"value": round(e2e_us, 1), "unit": "us/step",
-                    "h2d_bytes_per_step": int(qs[0].numel() * 2 + h2d_step),
-                    "d2h_bytes_per_step": int(w.n_blocks)},
+                    "h2d_bytes_per_step": int(qs[0].numel() * 2 + avg("h2d_bytes", e2e_stats)),
+                    "d2h_bytes_per_step": int(w.n_blocks),
+                    "same_steps_as_timed": e2e_same,
+                    "churn": {"n_h2d_blocks": round(avg("n_h2d_blocks", e2e_stats), 2),
+                              "n_moved": round(avg("n_moved", e2e_stats), 2)}},
             "gpu_launches": int(prof["launches"]),
             "timeline_us": timeline,
             "clocks": clk,
@@ -751,10 +784,23 @@ def run_lanes(args, w):
 
     clocks = Clocks(local)
     time.sleep(0.6)
-    for qs in queries(args.warmup):
-        step(qs)
-        lanes.collect()
-    torch.cuda.synchronize()
+    warm = queries(args.warmup)
+    step(warm[0])
+    ids0 = [ids for ids, _ in lanes.collect()]
+
+    def restart():
+        """Untimed: every lane's working set and pool emptied, the first
+        warm-up step's selection staged again, then the other warm-up steps;
+        the timed and the e2e loops both start from this state."""
+        for r, ids in zip(rs, ids0):
+            r.clear_working_set(drop_pool=True)
+            r.apply(ids)
+        for qs in warm[1:]:
+            step(qs)
+            lanes.collect()
+        torch.cuda.synchronize()
+
+    restart()
     qs_all = queries(args.steps)
     for r in rs:
         r.prof_enable(True)
@@ -766,9 +812,9 @@ def run_lanes(args, w):
     for i, qs in enumerate(qs_all):
         step(qs)
         if i > 0:
-            stats.append([st for _, st in lanes.collect()])
+            stats.append(lanes.collect())
     e1.record(cur)
-    stats.append([st for _, st in lanes.collect()])
+    stats.append(lanes.collect())
     torch.cuda.synchronize()
     barrier()
     ms = e0.elapsed_time(e1)
@@ -778,22 +824,29 @@ def run_lanes(args, w):
         ms = float(t.item())
     ms_step = ms / args.steps
     profs = [r.prof_read() for r in rs]
-    # e2e: every lane's query copied from pinned host memory each step, the ids
-    # of the previous step read back on the host
-    qh = [[q.cpu().pin_memory() for q in qs] for qs in queries(args.steps)]
+    # e2e: the same queries, every lane's copied from pinned host memory each
+    # step, the ids of the previous step read back on the host, from the same
+    # start state as the timed loop
+    qh = [[q.cpu().pin_memory() for q in qs] for qs in qs_all]
     qd = [torch.empty_like(q) for q in qs_all[0]]
+    restart()
     barrier()
     torch.cuda.synchronize()
+    e2e_res = []
     t0 = time.perf_counter()
     for i, qs in enumerate(qh):
         for d, q in zip(qd, qs):
             d.copy_(q, non_blocking=True)
         step(qd)
         if i > 0:
-            lanes.collect()
-    lanes.collect()
+            e2e_res.append(lanes.collect())
+    e2e_res.append(lanes.collect())
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
+    e2e_same = len(e2e_res) == len(stats) and all(
+        np.array_equal(ia, ib) and sa["n_moved"] == sb["n_moved"] and
+        sa["n_h2d_blocks"] == sb["n_h2d_blocks"]
+        for ra, rb in zip(e2e_res, stats) for (ia, sa), (ib, sb) in zip(ra, rb))
     clk = clocks.stop()
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
@@ -841,7 +894,8 @@ def run_lanes(args, w):
                               "B_asm": int(asm_step), "link_gbs_measured": round(link, 2)},
             "e2e": {"value": round(e2e_s / args.steps * 1e6, 1), "unit": "us/step",
                     "h2d_bytes_per_step": int(sum(q.numel() * 2 for q in qd)),
-                    "d2h_bytes_per_step": int(NL * 4 * (w.budget_blocks + w.reserve_blocks))},
+                    "d2h_bytes_per_step": int(NL * 4 * (w.budget_blocks + w.reserve_blocks)),
+                    "same_steps_as_timed": e2e_same},
             "gpu_launches": int(sum(p["launches"] for p in profs)),
             "clocks": clk, "setup_s": round(t_setup, 1),
         }

@@ -195,6 +195,14 @@ int kvmret_apply_selection(kvmret_ctx *ctx, const uint32_t *ids, uint32_t n_ids,
 int kvmret_select_apply_async(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory);
 int kvmret_step_collect(kvmret_ctx *ctx, uint32_t *ids_out, uint32_t *n_out,
                         kvmret_step_stats *stats);
+/* KvMemStore::clear_working_set (kvmem/include/kvmem/kvmem_store.hpp:470-472,
+ * kvmem/src/host/kvmem_store.cpp:897-901): the working set becomes empty (a
+ * new session over the same history); blocks, summaries and the repository
+ * stay, and blocks still in the HBM pool are rebuilt from it by the next
+ * step. drop_pool != 0 also forgets the pool's contents and LRU history, so
+ * the next step stages its whole selection from the host repository, as
+ * right after kvmret_create. Collects any step still in flight first. */
+int kvmret_clear_working_set(kvmret_ctx *ctx, int drop_pool);
 /* llama_kvmem_apply_retrieval (src/adapter/llama-memory-kvmem.cpp:4778-4782,
  * apply_retrieval :4419-4422): preview + apply. ids_out may be NULL. */
 int kvmret_apply_retrieval(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
@@ -368,6 +376,9 @@ int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_man
 /* set_selection + the runtime's spill/admit tier effect. remaps_out rows as
  * kvmret_last_plan; counts_out[6]: n_stage_in, n_stage_out, n_remaps,
  * total_window_tokens, selection_overlap_blocks, gpu_reused_blocks. */
+/* KvMemStore::clear_working_set (kvmem/src/host/kvmem_store.cpp:897-901);
+ * drop_gpu != 0 also takes every block out of the GPU tier. */
+int kvmret_table_clear_working_set(kvmret_table *t, int drop_gpu);
 int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_ids,
                                int force_raw_refresh, uint32_t *stage_in_out,
                                uint32_t *stage_out_out, int32_t *remaps_out,

@@ -925,6 +925,26 @@ int kvmret_apply_selection(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids,
     GUARD(return apply_impl(c, ids, n_ids, stats));
 }
 
+int kvmret_clear_working_set(kvmret_ctx *c, int drop_pool) {
+    NEED_CTX(c);
+    GUARD(TRY(drain(c)));
+    GUARD(c->table.clear_working_set(drop_pool != 0));
+    // an empty window: every slot of the next selection is rebuilt, from the
+    // pool where the block is still pooled, else from the host repository
+    const size_t W = c->win_slots, P = c->pool_slots;
+    CK(cudaMemsetAsync(c->d_win_id, 0xff, W * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_win_base, 0, W * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_win_ntok, 0, W * sizeof(uint32_t), c->st));
+    if (drop_pool) {  // the pool as created: no block pooled, no LRU history
+        CK(cudaMemsetAsync(c->d_blk_slot, 0xff, c->ncap * sizeof(int32_t), c->st));
+        CK(cudaMemsetAsync(c->d_slot_blk, 0xff, P * sizeof(int32_t), c->st));
+        CK(cudaMemsetAsync(c->d_slot_ntok, 0, P * sizeof(uint32_t), c->st));
+        CK(cudaMemsetAsync(c->d_slot_used, 0, P * sizeof(uint32_t), c->st));
+    }
+    c->last_plan = kvmret::Plan{};
+    return KVMRET_OK;
+}
+
 int kvmret_select_apply_async(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
     NEED_CTX(c);
     if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");
@@ -1158,6 +1178,12 @@ int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_man
     if (kept_out) std::copy(kept.begin(), kept.end(), kept_out);
     if (kept_count) *kept_count = kc;
     if (need) *need = nd;
+    return KVMRET_OK;
+}
+
+int kvmret_table_clear_working_set(kvmret_table *t, int drop_gpu) {
+    if (!t) return fail(KVMRET_ERR_ARG, "null argument");
+    GUARD(t->t.clear_working_set(drop_gpu != 0));
     return KVMRET_OK;
 }
 

@@ -127,4 +127,11 @@ Plan BlockTable::set_selection(const uint32_t *ids, uint32_t n_ids, bool force_r
     return p;
 }
 
+void BlockTable::clear_working_set(bool drop_gpu) {
+    for (Block &b : blocks_) {
+        b.in_ws = false;
+        if (drop_gpu) b.on_gpu = false;
+    }
+}
+
 }  // namespace kvmret

@@ -67,6 +67,13 @@ public:
     // set_selection (+ the runtime's tier effect). ids need not be sorted.
     Plan set_selection(const uint32_t *ids, uint32_t n_ids, bool force_raw_refresh);
 
+    // KvMemStore::clear_working_set (kvmem/include/kvmem/kvmem_store.hpp:470-472,
+    // kvmem/src/host/kvmem_store.cpp:897-901): no block is in the working set
+    // any more; the registry and the baked positions stay. drop_gpu also takes
+    // every block out of the GPU tier (the context's pool reset, which the
+    // reference's store has no counterpart for).
+    void clear_working_set(bool drop_gpu);
+
 private:
     TableConfig cfg_;
     std::vector<Block> blocks_;

@@ -135,6 +135,7 @@ SIGNATURES = {
                                               ctypes.POINTER(StepStats)]),
     "kvmret_select_apply_async": (ctypes.c_int, [_P, _PU32, _U32]),
     "kvmret_step_collect": (ctypes.c_int, [_P, _PU32, _PU32, ctypes.POINTER(StepStats)]),
+    "kvmret_clear_working_set": (ctypes.c_int, [_P, ctypes.c_int]),
     "kvmret_last_plan": (ctypes.c_int, [_P, _PI32, _PU32, _PU32, _PU32, _PU32, _PU32]),
     "kvmret_window_k": (_P, [_P, _U32]),
     "kvmret_window_v": (_P, [_P, _U32]),
@@ -168,6 +169,7 @@ SIGNATURES = {
     "kvmret_table_append": (ctypes.c_int, [_P, _U32]),
     "kvmret_table_n_blocks": (_U32, [_P]),
     "kvmret_table_keep": (ctypes.c_int, [_P, _PU32, _U32, _PU8, _PU32, _PU32]),
+    "kvmret_table_clear_working_set": (ctypes.c_int, [_P, ctypes.c_int]),
     "kvmret_table_set_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32,
                                                   _PI32, _PU32]),
 }
@@ -428,6 +430,11 @@ class Retriever:
                                        ctypes.byref(st)))
         return ids[: n.value].copy(), st.as_dict()
 
+    def clear_working_set(self, drop_pool=False):
+        """Empty the working set (a new session over the same history); with
+        drop_pool the HBM pool is forgotten too, as right after creation."""
+        _check(lib.kvmret_clear_working_set(self.h, int(drop_pool)))
+
     def apply_retrieval(self, mandatory=()):
         m, mp = _u32(list(mandatory))
         ids = np.zeros(max(1, min(self.cfg.budget_blocks, self.n_blocks)), np.uint32)
@@ -493,6 +500,9 @@ class Table:
         _check(lib.kvmret_table_keep(self.h, mp, len(m), kept.ctypes.data_as(_PU8),
                                      ctypes.byref(kc), ctypes.byref(need)))
         return kept[: self.n_blocks].copy(), kc.value, need.value
+
+    def clear_working_set(self, drop_gpu=False):
+        _check(lib.kvmret_table_clear_working_set(self.h, int(drop_gpu)))
 
     def set_selection(self, ids, force_raw_refresh=False):
         a, ap = _u32(ids)

@@ -364,6 +364,16 @@ ORC_API uint32_t orc_store_block_tokens(void *p, uint32_t id) {
     return static_cast<OrcStore *>(p)->blocks[id].n_tokens;
 }
 
+// KvMemStore::clear_working_set (kvmem/src/host/kvmem_store.cpp:897-901): no
+// block stays in the working set; tiers and baked positions are kept.
+// drop_gpu (no reference counterpart) also moves every block off the GPU tier.
+ORC_API void orc_store_clear_working_set(void *p, int drop_gpu) {
+    for (OrcBlock &b : static_cast<OrcStore *>(p)->blocks) {
+        b.in_working_set = false;
+        if (drop_gpu) b.gpu = false;
+    }
+}
+
 // Plan output arrays are caller-sized to block_count entries.
 // remap rows: block_id, n_tokens, from_base, to_base, working_k_resident, skip, raw_refresh.
 // counts[0..5]: n_stage_in, n_stage_out, n_remaps, total_window_tokens,

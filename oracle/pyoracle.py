@@ -47,6 +47,7 @@ def _load_orc():
         "orc_store_free": (None, [_P]),
         "orc_store_append": (None, [_P, _U32]),
         "orc_store_block_count": (_U32, [_P]),
+        "orc_store_clear_working_set": (None, [_P, ctypes.c_int]),
         "orc_store_set_selection": (None, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32, _PI32,
                                            _PU32]),
         "orc_rope_neox": (None, [_PF, _U32, _U32, _U32, _U32, ctypes.c_int32, ctypes.c_float,
@@ -83,6 +84,7 @@ def _load_ref():
         "ref_runtime_create": (_P, [_U32, _U32, _U32, ctypes.c_int]),
         "ref_runtime_free": (None, [_P]),
         "ref_runtime_append": (None, [_P, _U32]),
+        "ref_runtime_clear_working_set": (None, [_P]),
         "ref_runtime_select": (None, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32, _PI32,
                                       _PU32]),
         "ref_mean_k_f32": (None, [_PF, _U32, _U32, _U32, _PF]),
@@ -199,6 +201,9 @@ class Store:
     def append(self, n_tokens):
         orc.orc_store_append(self.h, n_tokens)
 
+    def clear_working_set(self, drop_gpu=False):
+        orc.orc_store_clear_working_set(self.h, int(drop_gpu))
+
     def set_selection(self, ids, force_raw_refresh=False):
         n = orc.orc_store_block_count(self.h)
         a = np.ascontiguousarray(ids, np.uint32)
@@ -230,6 +235,9 @@ class RefRuntime:
     def append(self, n_tokens):
         ref.ref_runtime_append(self.h, n_tokens)
         self.n += n_tokens
+
+    def clear_working_set(self):
+        ref.ref_runtime_clear_working_set(self.h)
 
     def set_selection(self, ids, force_raw_refresh=False):
         nb = (self.n + self.bt - 1) // self.bt

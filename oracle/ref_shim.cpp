@@ -51,6 +51,11 @@ REF_API void ref_runtime_append(void *p, uint32_t n_tokens) {
     static_cast<RefRuntime *>(p)->rt.register_append(n_tokens);
 }
 
+// The store's clear_working_set, reached through the runtime's store().
+REF_API void ref_runtime_clear_working_set(void *p) {
+    static_cast<RefRuntime *>(p)->rt.store().clear_working_set();
+}
+
 // prepare_selection (set_selection) + finish_reselect (spill then admit).
 REF_API void ref_runtime_select(void *p, const uint32_t *ids, uint32_t n_ids,
                                 int force_raw_refresh, uint32_t *stage_in,

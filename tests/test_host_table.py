@@ -86,3 +86,48 @@ def test_keep_all_fit_and_empty():
     t.append(128 * 3)
     kept, kc, need = t.keep()
     assert list(kept) == [1, 1, 1] and need == 0
+
+
+@pytest.mark.parametrize("immutable", [False, True])
+@pytest.mark.parametrize("seed", range(4))
+def test_clear_working_set_equals_oracle(seed, immutable):
+    """clear_working_set between selections (with and without dropping the GPU
+    tier): the next plans stay identical to the oracle's."""
+    rng = np.random.default_rng(400 + seed)
+    bt = 16
+    t = _table(bt, 1 << 20, immutable=immutable)
+    o = po.Store(bt, immutable)
+    t.append(bt * 60)
+    o.append(bt * 60)
+    for step in range(12):
+        if step % 3 == 2:
+            drop = bool(rng.random() < 0.5)
+            t.clear_working_set(drop)
+            o.clear_working_set(drop)
+        ids = rng.choice(60, size=int(rng.integers(1, 40)), replace=False)
+        for x, y in zip(t.set_selection(ids), o.set_selection(ids)):
+            assert np.array_equal(x, y)
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", range(4))
+def test_clear_working_set_equals_reference_runtime(seed):
+    """The reference store's clear_working_set (kvmem_store.cpp:897-901): after
+    it every selected block is staged in again, resident ones as resident."""
+    rng = np.random.default_rng(500 + seed)
+    bt = 128
+    t = _table(bt, 1 << 20)
+    r = po.RefRuntime(bt, 1 << 20, 1, False)
+    t.append(bt * 200)
+    r.append(bt * 200)
+    for step in range(9):
+        if step % 3 == 1:
+            t.clear_working_set()
+            r.clear_working_set()
+        ids = rng.choice(200, size=int(rng.integers(1, 48)), replace=False)
+        a = t.set_selection(ids)
+        b = r.set_selection(ids)
+        for x, y in zip(a, b):
+            assert np.array_equal(x, y)
+        if step % 3 == 1:  # right after the clear: every selected block stages in
+            assert a[3][0] == len(set(ids.tolist()))
