@@ -467,8 +467,8 @@ int plan_and_assemble(kvmret_ctx *c) {
     pa.jobs = c->jobs_dev;
     pa.counts = c->d_counts;
     pa.ids = c->d_ids;
-    pa.ext_err = c->ex_world > 1 ? reinterpret_cast<const uint32_t *>(c->ex_region + c->ex_tail +
-                                                                     4 * (kvmret::kMaxRanks + 1))
+    pa.ext_err = c->ex_world > 1 ? reinterpret_cast<uint32_t *>(c->ex_region + c->ex_tail +
+                                                               4 * (kvmret::kMaxRanks + 1))
                                  : nullptr;
     CK(kvmret::launch_plan(pa, c->st));
     kvmret::AsmLaunch al{};

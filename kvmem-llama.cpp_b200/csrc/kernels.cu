@@ -1271,7 +1271,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     uint32_t *s_flag = psm + 4 * W;  // bit 0: stage from the host, bit 1: needs a slot
     uint32_t *s_free = psm + 5 * W;  // [P]
     uint32_t *s_cu = psm + 5 * W + P;  // [P] eviction key: slot_used, ~0u if not a candidate
-    if (tid == 0) s_err = 0, s_mtok = 0, s_ftok = 0;
+    if (tid == 0) s_err = a.ext_err ? atomicExch(a.ext_err, 0u) : 0u;  // consumed once
+    __syncthreads();
+    if (s_err) {  // a rank's score rows never arrived: keep the window, pool and plan as they are
+        if (tid == 0) {
+            for (int i = 0; i < 8; ++i) a.counts[i] = 0;
+            a.counts[4] = 0x100u;
+        }
+        return;
+    }
+    if (tid == 0) s_mtok = 0, s_ftok = 0;
 
     // 1. selected ids ascending with their chronological bases
     const uint32_t n = a.n_blocks;
@@ -1435,7 +1444,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
         a.counts[1] = n_fresh;
         a.counts[2] = n_sel;
         a.counts[3] = ttotal;
-        a.counts[4] = s_err | ((a.ext_err && *a.ext_err) ? 0x100u : 0u);
+        a.counts[4] = s_err;
         a.counts[5] = s_mtok;
         a.counts[6] = s_ftok;
         a.counts[7] = 0;  // the assembly's work-unit counter

@@ -141,7 +141,7 @@ struct PlanArgs {
     Job *jobs;          // [2 * win_slots]: moved, then fresh at + win_slots
     uint32_t *counts;   // [8]
     uint32_t *ids;      // [win_slots]
-    const uint32_t *ext_err;  // optional: a nonzero word here is reported as error 0x100
+    uint32_t *ext_err;  // optional: a nonzero word here (read and cleared) fails the step as 0x100
 };
 cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st);
 size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots);

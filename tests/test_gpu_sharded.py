@@ -4,7 +4,8 @@ the last column of its row, are exchanged (an NCCL all-gather, or the
 scoring kernel's own writes into every rank's buffer over NVLink peer memory)
 and reduced in global layer order, so every rank
 selects the same blocks as the single-context oracle, bit for bit, and
-assembles its own layers' windows. Skipped with fewer than 2 GPUs.
+assembles its own layers' windows (skipped with fewer than 2 GPUs). On one
+GPU: the peer-memory exchange's bounded wait when a rank never writes.
 """
 import os
 import socket
@@ -118,3 +119,72 @@ def test_two_gpu_layer_sharded_selection_matches_oracle(exchange):
             assert np.array_equal(ids, want_ids)
             assert np.array_equal(lay, rm[:, 0].astype(np.uint32))
             assert np.array_equal(bases, rm[:, 3])
+
+
+def _silent_rank(w_kwargs, q_handle, q_done):
+    """Rank 1 of a 2-rank exchange that exports its region (same geometry as
+    rank 0's) and then never scores: its flag is never set."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, os.path.join(root, "kvmem-llama.cpp_b200")):
+        sys.path.insert(0, p)
+    import kvmret
+    from kvm_helpers import config_for
+    from kvmret import synth
+    r = kvmret.Retriever(config_for(synth.Workload(**w_kwargs)))
+    q_handle.put(r.exchange_export(2))
+    q_done.get(timeout=300)
+    r.close()
+
+
+def test_exchange_wait_gives_up_when_a_rank_never_writes():
+    """The reduce's wait on a peer's flag is bounded (2 s): the step then fails
+    with plan error 0x100, the window stays as it was, and the context keeps
+    working. One GPU: the silent rank is a second process that only exports."""
+    import time
+    import kvmret
+    import pyoracle as po
+    from kvm_helpers import append_history, config_for, oracle_scores
+    from kvmret import synth
+    wk = dict(name="ex", n_layer=2, n_head=8, n_head_kv=2, d_head=128, block_tokens=64,
+              n_blocks=32, budget_blocks=6, sink_blocks=1, reserve_blocks=0, n_planted=2,
+              seed=61)
+    ctx = mp.get_context("spawn")
+    q_handle, q_done = ctx.Queue(), ctx.Queue()
+    p = ctx.Process(target=_silent_rank, args=(wk, q_handle, q_done))
+    p.start()
+    try:
+        w = synth.Workload(**wk)
+        hist = synth.NumpyHistory(w)
+        r = kvmret.Retriever(config_for(w))
+        append_history(r, hist, cuts=[])
+        before = r.apply([0, 5, 9])
+        assert before["n_selected"] == 3
+        h0 = r.exchange_export(2)
+        h1 = q_handle.get(timeout=300)
+        r.exchange_import(0, [h0, h1])
+        q = hist.queries(1)[0]
+        r.query_reset()
+        r.query_add(torch.from_numpy(q.reshape(w.n_layer, 1, -1)).cuda())
+        t0 = time.monotonic()
+        r.score_exchange()
+        r.select_apply_async()
+        with pytest.raises(kvmret.KvmretError, match="0x100"):
+            r.step_collect()
+        assert 1.5 < time.monotonic() - t0 < 60
+        assert list(r.window_layout()[0]) == [0, 5, 9]  # the failed step changed nothing
+        # a local step on the same context afterwards selects the oracle's blocks
+        got = r.score()
+        want, _ = oracle_scores(hist, q.reshape(w.n_layer, -1).astype(np.float32),
+                                np.ones(w.n_layer, np.uint32))
+        assert np.array_equal(got.view(np.uint64), want.view(np.uint64))
+        ids = r.select()
+        assert list(ids) == list(po.pick_topk(want, w.budget_blocks, w.sink_blocks))
+        st = r.apply(ids)
+        assert list(r.window_layout()[0]) == sorted(ids.tolist()) and st["n_selected"] == len(ids)
+        r.close()
+    finally:
+        q_done.put(1)
+        p.join(timeout=120)
+    assert p.exitcode == 0
