@@ -118,3 +118,28 @@ def test_clear_with_steps_in_flight_collects_them_first():
     assert st["n_h2d_blocks"] == 3
     _check_window(r, hist)
     r.close()
+
+
+@pytest.mark.parametrize("pool_cache", [0, 1])
+def test_full_pool_frees_before_it_allocates(pool_cache):
+    """Every release precedes the new allocations (the ordering invariant of
+    kvmem/tests/kvmem_runtime_test.cpp:51-80): with a pool exactly as large as
+    the selection, a disjoint selection fits only if the departing blocks'
+    slots are released first."""
+    w = synth.Workload("fp", n_layer=2, n_head=8, n_head_kv=2, d_head=128, block_tokens=64,
+                       n_blocks=24, budget_blocks=6, sink_blocks=1, reserve_blocks=0,
+                       n_planted=1, seed=13)
+    hist = synth.NumpyHistory(w)
+    r = kvmret.Retriever(config_for(w, pool_cache=pool_cache, pool_blocks=6))
+    append_history(r, hist, cuts=[])
+    a, b = [1, 3, 5, 7, 9, 11], [0, 2, 4, 6, 8, 10]
+    assert r.apply(a)["n_h2d_blocks"] == 6
+    st = r.apply(b)
+    assert st["n_h2d_blocks"] == 6 and st["n_stage_out"] == 6
+    assert list(r.window_layout()[0]) == b
+    _check_window(r, hist)
+    st = r.apply(a)  # b's blocks took every slot: a is staged again from the host
+    assert st["n_h2d_blocks"] == 6
+    assert list(r.window_layout()[0]) == a
+    _check_window(r, hist)
+    r.close()
