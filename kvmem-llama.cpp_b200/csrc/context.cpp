@@ -59,6 +59,30 @@ int fail(int code, const char *fmt, ...) {
         if (r_ != KVMRET_OK) return r_;                                                       \
     } while (0)
 
+// Makes a context's device current for the length of an entry point and gives
+// the caller back its own current device on return.
+class DeviceScope {
+public:
+    DeviceScope() = default;
+    DeviceScope(const DeviceScope &) = delete;
+    DeviceScope &operator=(const DeviceScope &) = delete;
+    cudaError_t enter(int dev) {
+        if (dev < 0) return cudaSuccess;
+        int cur = 0;
+        cudaError_t e = cudaGetDevice(&cur);
+        if (e != cudaSuccess || cur == dev) return e;
+        e = cudaSetDevice(dev);
+        if (e == cudaSuccess) prev_ = cur;
+        return e;
+    }
+    ~DeviceScope() {
+        if (prev_ >= 0) cudaSetDevice(prev_);
+    }
+
+private:
+    int prev_ = -1;
+};
+
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
 bool type_ok(int32_t t) {
@@ -235,7 +259,8 @@ void prof_end(kvmret_ctx *c, cudaStream_t s, int idx) {
 }
 
 void free_all(kvmret_ctx *c) {
-    if (c->cfg.device >= 0) cudaSetDevice(c->cfg.device);
+    DeviceScope ds;
+    ds.enter(c->cfg.device);
     if (c->st) cudaStreamSynchronize(c->st);
     for (uint32_t p = 0; p < kvmret::kMaxRanks; ++p)
         if (c->ex_peer[p] && c->ex_peer[p] != c->ex_region) cudaIpcCloseMemHandle(c->ex_peer[p]);
@@ -312,10 +337,10 @@ int hmalloc_near(T **p, size_t bytes, unsigned flags, int node) {
     return rc;
 }
 
-int create_impl(const kvmret_config &cfg, kvmret_ctx *c) {
+int create_impl(const kvmret_config &cfg, kvmret_ctx *c, DeviceScope &ds) {
     c->cfg = cfg;
     const kvmret_config &k = c->cfg;
-    CK(cudaSetDevice(k.device));
+    CK(ds.enter(k.device));
     c->E = k.n_head_kv * k.d_head;
     c->qdim = k.n_head * k.d_head;
     c->ncap = static_cast<uint32_t>(align_up(k.max_blocks, 128));
@@ -584,13 +609,13 @@ int reduce_impl(kvmret_ctx *c, const double *rows, uint32_t n_layer_all, const u
         return fail(KVMRET_ERR_STATE, "internal error");                                     \
     }
 
+// First statement of an entry point on a context: the context's device is
+// current until the function returns.
 #define NEED_CTX(c)                                                                           \
-    do {                                                                                      \
-        if (!(c)) return fail(KVMRET_ERR_ARG, "null context");                               \
-        const cudaError_t de_ = cudaSetDevice((c)->cfg.device);                               \
-        if (de_ != cudaSuccess)                                                               \
-            return fail(KVMRET_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(de_));        \
-    } while (0)
+    if (!(c)) return fail(KVMRET_ERR_ARG, "null context");                                   \
+    DeviceScope dscope_;                                                                      \
+    if (const cudaError_t de_ = dscope_.enter((c)->cfg.device); de_ != cudaSuccess)           \
+    return fail(KVMRET_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(de_))
 
 int preview_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *ids_out,
                  uint32_t *n_out) {
@@ -681,9 +706,10 @@ int kvmret_create(const kvmret_config *cfg, kvmret_ctx **out) {
     TRY(validate(*cfg));
     kvmret_ctx *c = nullptr;
     GUARD(c = new kvmret_ctx(table_config(*cfg)));
+    DeviceScope ds;  // create_impl makes the context's device current
     int r = KVMRET_ERR_STATE;
     try {
-        r = create_impl(*cfg, c);
+        r = create_impl(*cfg, c, ds);
     } catch (...) {
         r = fail(KVMRET_ERR_NOMEM, "host allocation failed during create");
     }
@@ -1326,7 +1352,8 @@ namespace {
 
 void lanes_free(kvmret_lanes *g) {
     if (!g) return;
-    if (!g->ctx.empty() && g->ctx[0]->cfg.device >= 0) cudaSetDevice(g->ctx[0]->cfg.device);
+    DeviceScope ds;
+    if (!g->ctx.empty()) ds.enter(g->ctx[0]->cfg.device);
     for (kvmret_ctx *c : g->ctx) cudaStreamSynchronize(c->st);
     if (g->scratch) cudaFree(g->scratch);
     if (g->fork) cudaEventDestroy(g->fork);
@@ -1369,7 +1396,8 @@ int kvmret_lanes_create(kvmret_ctx *const *lanes, uint32_t n, kvmret_lanes **out
     g->ctx.assign(lanes, lanes + n);
     g->L_local = lanes[0]->cfg.n_layer;
     g->cstride = lanes[0]->cstride;
-    if (lanes[0]->cfg.device >= 0) cudaSetDevice(lanes[0]->cfg.device);
+    DeviceScope ds;
+    ds.enter(lanes[0]->cfg.device);
     g->join.assign(n, nullptr);
     cudaError_t e = cudaEventCreateWithFlags(&g->fork, cudaEventDisableTiming);
     for (uint32_t i = 0; i < n && e == cudaSuccess; ++i)
@@ -1386,6 +1414,7 @@ void kvmret_lanes_destroy(kvmret_lanes *g) { lanes_free(g); }
 
 int kvmret_lanes_score_layers(kvmret_lanes *g, double *rows_out, void *stream) {
     if (!g || !rows_out) return fail(KVMRET_ERR_ARG, "bad lanes call");
+    NEED_CTX(g->ctx[0]);
     cudaStream_t caller = static_cast<cudaStream_t>(stream);
     TRY(lanes_fork(g, caller));
     const uint64_t lane_rows = static_cast<uint64_t>(g->L_local) * g->cstride;
@@ -1398,6 +1427,7 @@ int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uin
                                     const uint32_t *const *mandatory,
                                     const uint32_t *n_mandatory, void *stream) {
     if (!g || !rows_all || n_ranks == 0) return fail(KVMRET_ERR_ARG, "bad lanes call");
+    NEED_CTX(g->ctx[0]);
     cudaStream_t caller = static_cast<cudaStream_t>(stream);
     const uint32_t n = static_cast<uint32_t>(g->ctx.size());
     const uint64_t lane_rows = static_cast<uint64_t>(g->L_local) * g->cstride;
