@@ -91,7 +91,9 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def link_gbps(nbytes=1 << 30, reps=3):
+def link_gbps(nbytes=1 << 30, reps=3, d2h=False):
+    """Host link bandwidth: best of `reps` 1 GiB copies between pinned host
+    memory and the device (host to device unless d2h), CUDA events."""
     import torch
     h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
@@ -101,7 +103,10 @@ def link_gbps(nbytes=1 << 30, reps=3):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(s):
             e0.record(s)
-            d.copy_(h, non_blocking=True)
+            if d2h:
+                h.copy_(d, non_blocking=True)
+            else:
+                d.copy_(h, non_blocking=True)
             e1.record(s)
         torch.cuda.synchronize()
         best = min(best, e0.elapsed_time(e1) / 1e3)
@@ -271,6 +276,7 @@ def run_ours(args, w):
     torch.cuda.synchronize()
     t_setup = time.perf_counter() - t_setup
     link = link_gbps()
+    link_d2h = link_gbps(d2h=True)
 
     stride = r.contrib_stride
     contrib_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
@@ -520,7 +526,8 @@ def run_ours(args, w):
             "step_roofline": {"t_roof_us": round(t_roof * 1e6, 1),
                               "t_meas_us": round(ms_step * 1e3, 1),
                               "frac": round(t_roof * 1e3 / ms_step, 4),
-                              "link_gbs_measured": round(link, 2), "hbm_gbs": hbm,
+                              "link_gbs_measured": round(link, 2),
+                              "link_d2h_gbs_measured": round(link_d2h, 2), "hbm_gbs": hbm,
                               "B_sum": int(score_step), "B_link": int(h2d_step),
                               "B_asm": int(asm_step)},
             "kv_gbps": round(kv_bytes / (ms_step / 1e3) / 1e9, 1),
