@@ -38,6 +38,30 @@ METRIC = "retrieval+stage-in µs/decode step (64 layers, 256K); KV GB/s vs HBM/l
 FALLBACK_HBM_GBS = 6650.0
 
 
+def workloads():
+    """The workload definitions (kvmret/workloads.py), loaded by path: plain
+    data, so the reference arm never imports the kvmret package or loads its
+    native library."""
+    import importlib.util
+    name = "kvmret_bench_workloads"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(
+            name, os.path.join(PKG, "kvmret", "workloads.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod  # dataclasses resolve the module while building the class
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+def decode_workload(w):
+    """config.workload and dtype of a decode-step line (both arms print these)."""
+    TYPE_F16 = workloads().TYPE_F16
+    desc = (f"{w.name}: {w.n_layer} layers, {w.n_head}q/{w.n_head_kv}kv heads, d{w.d_head}, "
+            f"{w.n_blocks} blocks x {w.block_tokens} tok ({w.n_tokens // 1024}K), budget "
+            f"{w.budget_blocks} blocks, sink {w.sink_blocks}, gen-reserve {w.reserve_blocks} slots")
+    return desc, ("f16" if w.k_type == TYPE_F16 else "q8_0/q4_0")
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -219,8 +243,8 @@ def run_reference(args, w):
     line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/step",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": w.name, "threads": threads},
+            "vs_baseline": None, "dtype": decode_workload(w)[1], "data": "synthetic",
+            "config": {"workload": decode_workload(w)[0], "threads": threads},
             "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads,
                              "kind": kind, "sample": sample,
                              "parts_ms": {k: round(v * 1e3, 3) for k, v in parts.items()}},
@@ -493,14 +517,11 @@ def run_ours(args, w):
             "metric": METRIC, "value": round(ms_step * 1e3, 1), "unit": "us/step",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16" if w.k_type == kvmret.TYPE_F16 else "q8_0/q4_0",
+            "vs_baseline": None, "dtype": decode_workload(w)[1],
             "data": "synthetic: seeded N(0,1) x LogNormal(0,0.5) channel scale, "
                     f"{w.n_planted} planted blocks, query drift {w.drift}/step",
             "config": {
-                "workload": f"{w.name}: {w.n_layer} layers, {w.n_head}q/{w.n_head_kv}kv heads, "
-                            f"d{w.d_head}, {w.n_blocks} blocks x {T} tok ({w.n_tokens // 1024}K), "
-                            f"budget {w.budget_blocks} blocks, sink {w.sink_blocks}, gen-reserve "
-                            f"{w.reserve_blocks} slots",
+                "workload": decode_workload(w)[0],
                 "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
                 "exchange": (args.exchange if world > 1 else None),
                 "l2": "inputs larger than L2 (summaries "
@@ -943,14 +964,14 @@ def main():
     ap.add_argument("--churn-asm", type=int, default=168,
                     help="reference arm: window slots rewritten per step (measured: 167.6)")
     args = ap.parse_args()
-    from kvmret import synth
-    w = synth.CONFIGS[args.config]
+    wl = workloads()
+    w = wl.CONFIGS[args.config]
     if args.layers:
-        w = synth.scaled(w, n_layer=args.layers)
+        w = wl.scaled(w, n_layer=args.layers)
     if args.budget:
-        w = synth.scaled(w, budget_blocks=args.budget)
+        w = wl.scaled(w, budget_blocks=args.budget)
     if args.reserve >= 0:
-        w = synth.scaled(w, reserve_blocks=args.reserve)
+        w = wl.scaled(w, reserve_blocks=args.reserve)
     if args.impl == "reference":
         run_reference(args, w)
     elif w.prefill_tokens:
