@@ -131,3 +131,52 @@ def test_clear_working_set_equals_reference_runtime(seed):
             assert np.array_equal(x, y)
         if step % 3 == 1:  # right after the clear: every selected block stages in
             assert a[3][0] == len(set(ids.tolist()))
+
+
+try:
+    from hypothesis import given, settings, strategies as hs
+except ImportError:  # pragma: no cover - hypothesis is part of the test image
+    hs = None
+
+if hs is not None:
+    _op = hs.one_of(
+        hs.tuples(hs.just("append"), hs.integers(1, 80)),
+        hs.tuples(hs.just("clear"), hs.booleans()),
+        hs.tuples(hs.just("select"), hs.lists(hs.integers(0, 70), max_size=40), hs.booleans()),
+    )
+
+    @needs_ref
+    @settings(max_examples=60, deadline=None, derandomize=True)
+    @given(first=hs.integers(1, 600), ops=hs.lists(_op, min_size=1, max_size=14),
+           immutable=hs.booleans())
+    def test_random_op_sequences_match_oracle_and_reference(first, ops, immutable):
+        """Any sequence of appends, working-set clears (keeping the GPU tier,
+        the reference's form; or dropping it) and selections, with forced
+        refreshes: the host table, the oracle and the reference runtime give
+        the same plans (the reference only for clears that keep the tier)."""
+        bt = 16
+        t = _table(bt, 1 << 20, immutable=immutable)
+        o = po.Store(bt, immutable)
+        r = po.RefRuntime(bt, 1 << 20, 1, immutable)
+        ref_ok = True
+        for x in (t, o, r):
+            x.append(first)
+        for op in ops:
+            if op[0] == "append":
+                for x in (t, o, r):
+                    x.append(op[1])
+            elif op[0] == "clear":
+                t.clear_working_set(op[1])
+                o.clear_working_set(op[1])
+                if op[1]:
+                    ref_ok = False  # the reference store has no tier drop
+                else:
+                    r.clear_working_set()
+            else:
+                ids = np.asarray(op[1], np.uint32)
+                a, b = t.set_selection(ids, op[2]), o.set_selection(ids, op[2])
+                for x, y in zip(a, b):
+                    assert np.array_equal(x, y)
+                if ref_ok:
+                    for x, y in zip(a, r.set_selection(ids, op[2])):
+                        assert np.array_equal(x, y)
