@@ -139,82 +139,211 @@ def link_gbps(nbytes=1 << 30, reps=3, d2h=False):
 
 
 # ---------------------------------------------------------------------------
-def cpu_sample(w, n_h2d, n_asm, threads, use_ref, budget_s=10.0):
-    """CPU time of one step of the same workload, from timed samples of each
-    component (restated score_retrieval; pick_topk / set_selection /
-    rope_neox_apply from the reference's libkvmem when built, else the
-    oracle's restatement; memcpy staging of the stage-in bytes into a pinned
-    slab), scaled by the step's unit counts."""
-    import concurrent.futures as cf
-
-    import numpy as np
+def load_oracle():
+    """The CPU oracle and, when built, the reference's own libkvmem (the
+    checker of the parity pass and the CPU arms; never on the timed GPU path)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle as po
-    use_ref = use_ref and po.ref is not None
-    rng = np.random.default_rng(0)
-    L, N, E, T = w.n_layer, w.n_blocks, w.E, w.block_tokens
-    ls = 2  # layers scored per sample
-    mean = rng.standard_normal((N, ls, E)).astype(np.float32)
-    has = np.ones(N, np.uint8)
-    q_sum = rng.standard_normal((ls, w.qdim)).astype(np.float32)
-    q_count = np.ones(ls, np.uint32)
-    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    return po
 
-    def timed(fn, reps):
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            fn()
-        return (time.perf_counter() - t0) / reps
 
-    # S3: score N blocks x ls layers; threads split the blocks
-    parts = np.array_split(np.arange(N), threads)
+def workload_config(w):
+    """`config` of a decode-step line: the same keys and values in both arms."""
+    sum_mib = w.n_layer * w.n_blocks * w.E * 4 / 2**20
+    return {"workload": decode_workload(w)[0],
+            "l2": f"inputs larger than L2: {sum_mib:.0f} MiB of block summaries read per step, "
+                  "GiB-scale window and block repository"}
 
-    def score_all():
-        list(pool.map(lambda ix: po.score(mean[ix], has[ix], q_sum, q_count, w.n_head,
-                                          w.n_head_kv, w.d_head), parts))
-    t_score = timed(score_all, 2) * (L / ls)
-    scores = po.score(mean, has, q_sum, q_count, w.n_head, w.n_head_kv, w.d_head)
-    # S6 + S7
-    if use_ref:
-        t_topk = timed(lambda: po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks), 5)
-        rt = po.RefRuntime(T, w.budget_blocks, w.sink_blocks)
-        rt.append(N * T)
-        ids = po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks)
-        t_plan = timed(lambda: rt.set_selection(ids), 5)
-    else:
-        t_topk = timed(lambda: po.pick_topk(scores, w.budget_blocks, w.sink_blocks), 5)
-        st = po.Store(T)
-        st.append(N * T)
-        ids = po.pick_topk(scores, w.budget_blocks, w.sink_blocks)
-        t_plan = timed(lambda: st.set_selection(ids), 5)
-    # S11: staging memcpy of one block's units (all layers) into a host slab
-    unit = T * E * 2 * 2
-    s_np = np.ones(L * unit, np.uint8)
-    d_np = np.zeros(L * unit, np.uint8)
-    chunks = np.array_split(np.arange(L * unit // 4096), threads)
 
-    def stage():
-        list(pool.map(lambda ix: np.copyto(d_np[ix[0] * 4096:(ix[-1] + 1) * 4096],
-                                           s_np[ix[0] * 4096:(ix[-1] + 1) * 4096]), chunks))
-    t_stage = timed(stage, 3) * n_h2d
-    # S12: RoPE of K block-layer units (f16 -> f32 -> rope -> f16)
-    kb = rng.standard_normal((threads, T, w.n_head_kv, w.d_head)).astype(np.float16)
+def _ptrs(addrs):
+    import ctypes
+    a = np.ascontiguousarray(addrs, np.uint64)
+    return a, a.ctypes.data_as(ctypes.POINTER(ctypes.c_void_p))
 
-    def rope_unit(i):
-        x = kb[i].astype(np.float32)
-        if use_ref:
-            y = po.ref_rope_neox(x, 4096 + i, w.freq_base)
+
+class CpuRetrieval:
+    """One retrieval step of the workload on the host cores: the CPU arms
+    (the `--impl reference` arm and the GPU arm's `cpu_baseline`).
+
+    Per step, in full: the restated score_retrieval of every block on every
+    layer (threads over blocks), the reference's pick_topk_blocks and
+    KvMemRuntime set_selection (libkvmem compiled from the reference's
+    sources; the oracle's restatement when it is not built), the staging
+    memcpy of every stage-in block's K and V rows (all layers) from the host
+    repository into a staging area, and for every block-layer the plan
+    rebuilds (remap rows without skip) its K rotated by rope_neox_apply at
+    the new window base (f16 in and out; q8_0 K: dequant -> RoPE -> FWHT ->
+    requant) and its V rows copied into the window.
+
+    The workload has the distributions of the GPU arm's: block summaries are
+    the block means of N(0,1) x LogNormal(0,0.5) channel-scaled keys (drawn
+    directly as N(0, 1/T) x scale, planted blocks +0.5 along the group query
+    direction), the decode query drifts by 0.05 N(0,1) per step. The host
+    repository holds R distinct blocks (block b reads slot b mod R) and the
+    window holds S slots (slot i writes i mod S): 1 GiB and 2 GiB, well above
+    the host caches, so the copies and RoPE stream from and to DRAM as with
+    the full-size arrays."""
+
+    R, S = 32, 64
+
+    def __init__(self, w, threads, use_ref=True, seed_offset=0):
+        import concurrent.futures as cf
+        po = load_oracle()
+        self.po, self.w = po, w
+        self.use_ref = use_ref and po.ref is not None
+        self.kind = "reference" if self.use_ref else "port"
+        self.threads = threads
+        self.pool = cf.ThreadPoolExecutor(max_workers=threads)
+        TYPE_F16 = workloads().TYPE_F16
+        self.f16 = w.k_type == TYPE_F16
+        L, Hq, Hkv, D, N, T = w.n_layer, w.n_head, w.n_head_kv, w.d_head, w.n_blocks, \
+            w.block_tokens
+        rng = np.random.default_rng(w.seed + seed_offset)
+        scale = np.exp(rng.normal(0.0, 0.5, size=(L, Hkv, D))).astype(np.float32)
+        q0 = rng.standard_normal((L, Hq, D)).astype(np.float16)
+        planted = np.sort(rng.choice(np.arange(w.sink_blocks, N), size=min(w.n_planted,
+                                     N - w.sink_blocks), replace=False))
+        qg = q0.astype(np.float32).reshape(L, Hkv, Hq // Hkv, D).sum(axis=2)
+        u = qg / np.linalg.norm(qg, axis=-1, keepdims=True)
+        mean = rng.standard_normal((N, L, Hkv, D), dtype=np.float32)
+        mean *= scale[None] / np.float32(np.sqrt(T))
+        mean[planted] += np.float32(0.5) * u[None]
+        self.mean = mean.reshape(N, L, Hkv * D)
+        self.has = np.ones(N, np.uint8)
+        self.q = q0.astype(np.float32)
+        self.qrng = np.random.default_rng(w.seed + seed_offset + 7)
+        E = w.E
+        self.k_row = E * 2 if self.f16 else E // 32 * 34
+        self.v_row = E * 2 if w.v_type == TYPE_F16 else (E // 32 * 34 if w.v_type == 8
+                                                          else E // 32 * 18)
+        self.kb, self.vb = T * self.k_row, T * self.v_row
+        unit = self.kb + self.vb
+        self.unit = unit
+        # repository and window contents: N(0,1) f16 rows (quantised for q8_0 K)
+        base = rng.standard_normal(T * E).astype(np.float32)
+        if self.f16:
+            kblk = base.astype(np.float16).view(np.uint8)
         else:
-            y = po.rope_neox(x, 4096 + i, w.freq_base)
-        return y.astype(np.float16)
+            kblk = po.quant_q8_0(base)
+        vblk = (base.astype(np.float16).view(np.uint8) if w.v_type == TYPE_F16
+                else (po.quant_q8_0(base) if w.v_type == 8 else po.quant_q4_0(base)))
+        one = np.concatenate([kblk[:self.kb], vblk[:self.vb]])
+        self.repo = np.empty((self.R, L, unit), np.uint8)
+        self.repo[:] = one
+        self.win = np.zeros((self.S, L, unit), np.uint8)
+        self.slab = np.zeros((self.S, L, unit), np.uint8)  # staging area
+        self.parts = [ix for ix in np.array_split(np.arange(N), threads) if len(ix)]
+        if self.use_ref:
+            self.rt = po.RefRuntime(T, w.budget_blocks, w.sink_blocks)
+        else:
+            self.rt = po.Store(T)
+        self.rt.append(N * T)
+        self.fwht_n = D if not self.f16 else 0
 
-    t_rope = timed(lambda: list(pool.map(rope_unit, range(threads))), 2) / threads
-    t_rope *= n_asm * L
-    pool.shutdown()
-    total = t_score + t_topk + t_plan + t_stage + t_rope
-    parts_s = {"score": t_score, "topk": t_topk, "plan": t_plan, "stage_memcpy": t_stage,
-               "rope": t_rope}
-    return total, parts_s, ("reference" if use_ref else "port")
+    def next_query(self):
+        q16 = self.q.astype(np.float16)
+        self.q = self.q + np.float32(self.w.drift) * self.qrng.standard_normal(
+            self.q.shape).astype(np.float32)
+        return q16.reshape(self.w.n_layer, -1)
+
+    def _score(self, q_sum):
+        w, po = self.w, self.po
+        q_count = np.ones(w.n_layer, np.uint32)
+        out = list(self.pool.map(
+            lambda ix: po.score(self.mean[ix[0]:ix[-1] + 1], self.has[ix[0]:ix[-1] + 1], q_sum,
+                                q_count, w.n_head, w.n_head_kv, w.d_head), self.parts))
+        return np.concatenate(out)
+
+    def _split(self, n):
+        k = max(1, min(self.threads, n))
+        b = np.linspace(0, n, k + 1).astype(np.int64)
+        return [(int(b[i]), int(b[i + 1])) for i in range(k) if b[i + 1] > b[i]]
+
+    def step(self):
+        """One full step; returns its counts."""
+        w, po = self.w, self.po
+        L = w.n_layer
+        q_sum = self.next_query().astype(np.float32)
+        scores = self._score(q_sum)
+        if self.use_ref:
+            ids = po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks)
+        else:
+            ids = po.pick_topk(scores, w.budget_blocks, w.sink_blocks)
+        si, so, rm, cnt = self.rt.set_selection(ids)
+        # staging memcpy: every stage-in block's K and V rows of all layers
+        import ctypes
+        lyr = np.arange(L, dtype=np.uint64)
+        rb, sb, wb = (np.uint64(a.ctypes.data) for a in (self.repo, self.slab, self.win))
+        unit = np.uint64(self.unit)
+        lib = po.ref if self.use_ref else po.orc
+        si64 = np.asarray(si, np.uint64)
+        if len(si64):
+            src = rb + (((si64 % np.uint64(self.R))[:, None] * np.uint64(L) + lyr) * unit)
+            dst = sb + (((np.arange(len(si64), dtype=np.uint64) % np.uint64(self.S))[:, None] *
+                         np.uint64(L) + lyr) * unit)
+            a_s, p_s = _ptrs(src.reshape(-1))
+            a_d, p_d = _ptrs(dst.reshape(-1))
+            a_n = np.full(a_s.size, self.unit, np.uint64)
+            p_n = a_n.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64))
+            copy = lib.ref_copy_list if self.use_ref else lib.orc_copy_list
+            list(self.pool.map(lambda r_: copy(p_s, p_d, p_n, r_[0], r_[1]),
+                               self._split(a_s.size)))
+        # window rebuild: every remapped block-layer (skip == 0)
+        sel = np.nonzero(rm[:, 5] == 0)[0] if len(rm) else np.zeros(0, np.int64)
+        moved = sel
+        if len(sel):
+            blk = rm[sel, 0].astype(np.uint64)
+            o_src = ((blk % np.uint64(self.R))[:, None] * np.uint64(L) + lyr) * unit
+            o_dst = ((sel.astype(np.uint64) % np.uint64(self.S))[:, None] * np.uint64(L) +
+                     lyr) * unit
+            a1, p1 = _ptrs((rb + o_src).reshape(-1))
+            a2, p2 = _ptrs((wb + o_dst).reshape(-1))
+            a3, p3 = _ptrs((rb + o_src + np.uint64(self.kb)).reshape(-1))
+            a4, p4 = _ptrs((wb + o_dst + np.uint64(self.kb)).reshape(-1))
+            pa = np.ascontiguousarray(np.repeat(rm[sel, 3], L), np.int32)
+            pp = pa.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+            T, H, D = w.block_tokens, w.n_head_kv, w.d_head
+            n_units = a1.size
+            if self.f16:
+                fn = lib.ref_rope_units_f16 if self.use_ref else lib.orc_rope_units_f16
+                list(self.pool.map(lambda r_: fn(p1, p2, p3, p4, self.vb, pp, r_[0], r_[1], T, H,
+                                                 D, w.freq_base, 1.0), self._split(n_units)))
+            else:  # quantised K: the restated stage-in kernels (no host code in the reference)
+                fn = po.orc.orc_rope_units_q8_0
+                list(self.pool.map(lambda r_: fn(p1, p2, p3, p4, self.vb, pp, r_[0], r_[1], T, H,
+                                                 D, w.freq_base, 1.0, self.fwht_n),
+                                   self._split(n_units)))
+        return {"n_stage_in": len(si), "n_rebuilt": len(moved), "ids": ids}
+
+    def close(self):
+        self.pool.shutdown()
+
+
+def cpu_steps(w, steps, warmup, threads, use_ref=True):
+    """Mean seconds per full CPU step over `steps` timed steps after `warmup`."""
+    cpu = CpuRetrieval(w, threads, use_ref)
+    for _ in range(warmup):
+        cpu.step()
+    times, stats = [], []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        st = cpu.step()
+        times.append(time.perf_counter() - t0)
+        stats.append(st)
+    cpu.close()
+    churn = {"n_stage_in": round(sum(s["n_stage_in"] for s in stats) / len(stats), 2),
+             "n_rebuilt": round(sum(s["n_rebuilt"] for s in stats) / len(stats), 2)}
+    return sum(times) / len(times), cpu.kind, churn
+
+
+def cpu_sample_text(w, kind, steps, warmup, threads):
+    src = ("libkvmem from the reference's sources (pick_topk_blocks, KvMemRuntime "
+           "set_selection, rope_neox_apply) + restated score_retrieval"
+           if kind == "reference" else "the oracle's restatement of the path")
+    return (f"{steps} timed steps (after {warmup} warm-up) of the full workload on "
+            f"{threads} host threads, each step in full: score all {w.n_layer} layers x "
+            f"{w.n_blocks} blocks, top-k, plan, staging memcpy of every stage-in block, "
+            f"RoPE + V copy of every rebuilt block-layer; {src}")
 
 
 # ---------------------------------------------------------------------------
@@ -222,38 +351,155 @@ def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import pyoracle as po
     threads = os.cpu_count() or 1
-    n_h2d, n_asm = args.churn_h2d, args.churn_asm
-    vals = []
-    for _ in range(args.warmup):
-        cpu_sample(w, n_h2d, n_asm, threads, True)
-    parts = None
-    for _ in range(args.steps):
-        t, parts, kind = cpu_sample(w, n_h2d, n_asm, threads, True)
-        vals.append(t)
-    us = sum(vals) / len(vals) * 1e6
-    sample = (f"per step: restated score_retrieval on 2 of {w.n_layer} layers x {w.n_blocks} "
-              f"blocks (x{w.n_layer // 2}), pick_topk + set_selection on all blocks, memcpy "
-              f"staging of one block's {w.n_layer} layers (x{n_h2d} new blocks/step), "
-              f"rope_neox_apply of {threads} block-layers (x{n_asm} moved blocks x "
-              f"{w.n_layer} layers); "
-              f"{'libkvmem from reference sources' if po.ref is not None else 'oracle port'}")
+    sec, kind, churn = cpu_steps(w, args.steps, args.warmup, threads, True)
+    us = sec * 1e6
     line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/step",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": decode_workload(w)[1], "data": "synthetic",
-            "config": {"workload": decode_workload(w)[0], "threads": threads},
+            "vs_baseline": None, "dtype": decode_workload(w)[1],
+            "data": "synthetic: seeded N(0,1) x LogNormal(0,0.5) channel-scale summaries, "
+                    f"{w.n_planted} planted blocks, query drift {w.drift}/step",
+            "config": workload_config(w),
+            "churn": churn,
             "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads,
-                             "kind": kind, "sample": sample,
-                             "parts_ms": {k: round(v * 1e3, 3) for k, v in parts.items()}},
+                             "kind": kind,
+                             "sample": cpu_sample_text(w, kind, args.steps, args.warmup,
+                                                       threads)},
             "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
+# DRAM traffic of the window-assembly kernels per algorithmic byte: ncu's
+# dram__bytes_read.sum + dram__bytes_write.sum over one captured launch divided
+# by that launch's algorithmic bytes (8-layer cut of the same workload:
+#   ncu --section MemoryWorkloadAnalysis --clock-control none -k regex:assemble
+#       -s 20 -c 1 python bench.py --layers 8 --steps 5 --warmup 3 --config C
+# ). The traffic grows with the blocks a launch moves, so a launch's traffic is
+# this ratio times its algorithmic bytes.
+NCU_TRAFFIC_RATIO = {"assemble_kernel": 1556.8 / 1585.4,
+                     "assemble_quant_kernel": 793.3 / 824.7}
+
+
+class OracleCheck:
+    """The checker of the parity pass (outside every timed region): the
+    oracle's restated score_retrieval over host copies of this rank's block
+    summaries, the per-layer terms of all ranks reduced in global layer order,
+    pick_topk, and the set_selection plan replayed over every host-table
+    operation of the run, plus the oracle RoPE / requantisation of sampled
+    window slots from the pinned repository's bytes."""
+
+    def __init__(self, po, w, r, Ll, world, threads, dist):
+        import concurrent.futures as cf
+        self.po, self.w, self.r, self.Ll, self.world, self.dist = po, w, r, Ll, world, dist
+        self.mean = r.summaries()  # [N][Ll][E]
+        N = self.mean.shape[0]
+        self.N = N
+        self.pool = cf.ThreadPoolExecutor(max_workers=max(1, threads))
+        self.parts = [ix for ix in np.array_split(np.arange(N), max(1, threads)) if len(ix)]
+        self.store = po.Store(w.block_tokens)
+        self.store.append(w.n_tokens)
+        self.tie_high = bool(r.cfg.tie_higher_id)
+
+    def ids(self, q_host):
+        """Oracle selection of one step's query ([Ll][1][qdim] f16, this rank's layers)."""
+        import torch
+        po, w = self.po, self.w
+        q_sum = q_host.numpy().reshape(self.Ll, -1).astype(np.float32)
+        q_count = np.ones(self.Ll, np.uint32)
+        res = list(self.pool.map(
+            lambda ix: po.score_terms(self.mean[ix[0]:ix[-1] + 1], q_sum, q_count, w.n_head,
+                                      w.n_head_kv, w.d_head), self.parts))
+        terms = np.concatenate([t for t, _ in res], axis=1)
+        act = res[0][1]
+        if self.world > 1:
+            t = torch.from_numpy(np.ascontiguousarray(terms)).cuda().reshape(-1)
+            t_all = torch.empty(self.world * t.numel(), dtype=t.dtype, device="cuda")
+            self.dist.all_gather_into_tensor(t_all, t)
+            a = torch.from_numpy(act.astype(np.uint8)).cuda()
+            a_all = torch.empty(self.world * a.numel(), dtype=a.dtype, device="cuda")
+            self.dist.all_gather_into_tensor(a_all, a)
+            terms = t_all.cpu().numpy().reshape(-1, self.N)
+            act = a_all.cpu().numpy()
+        scores = po.score_reduce(terms, act, np.ones(self.N, np.uint8))
+        return po.pick_topk(scores, w.budget_blocks, w.sink_blocks,
+                            tie_higher_id=self.tie_high)
+
+    def replay(self, op):
+        if op[0] == "clear":
+            self.store.clear_working_set(op[1])
+            return None
+        return self.store.set_selection(op[1])
+
+    def summaries_exact(self):
+        """Device summaries of sampled blocks against the oracle's token-order
+        mean of the repository's unrotated f16 K rows (f16 K only)."""
+        po, w, r = self.po, self.w, self.r
+        repo = r.repo_view()
+        unit = int(kvmret_lib().kvmret_repo_unit_bytes(r.h))
+        T, E = w.block_tokens, w.E
+        ok = True
+        for b in sorted({0, self.N // 3, 2 * self.N // 3, self.N - 1}):
+            for l in range(self.Ll):
+                o = (b * self.Ll + l) * unit
+                k = repo[o:o + T * E * 2].view(np.float16).reshape(1, T, E)
+                ok &= bool(np.array_equal(po.mean_k(k)[0].view(np.uint32),
+                                          self.mean[b, l].view(np.uint32)))
+        return ok
+
+    def window_slot(self, layer, slot, block, n_tok, base):
+        """(K difference, V equal) of one window slot of one layer: f16 K in
+        ulps; q8_0 K as (max |q| LSB, max scale ulp)."""
+        po, w, r = self.po, self.w, self.r
+        repo = r.repo_view()
+        unit = int(kvmret_lib().kvmret_repo_unit_bytes(r.h))
+        kbytes = int(kvmret_lib().kvmret_repo_k_bytes(r.h))
+        o = (block * self.Ll + layer) * unit
+        kr, vr = r.k_row, r.v_row
+        src_k = np.array(repo[o:o + n_tok * kr])
+        src_v = np.array(repo[o + kbytes:o + kbytes + n_tok * vr])
+        win_k = r.window_read(layer, False, slot, 1)[:n_tok * kr]
+        win_v = r.window_read(layer, True, slot, 1)[:n_tok * vr]
+        H, D = w.n_head_kv, w.d_head
+        if r.cfg.k_type == 1:
+            want = po.rope_block_f16(src_k.view(np.uint16).reshape(n_tok, H, D), base,
+                                     w.freq_base).reshape(-1)
+            kd = int(f16_ulps(win_k.view(np.uint16), want).max(initial=0))
+            kdiff = (kd, 0)
+        else:
+            want = po.rope_block_q8_0(src_k, n_tok, H, D, base, w.freq_base, fwht_n=D)
+            kdiff = q8_diff(win_k, want)
+        return kdiff, bool(np.array_equal(win_v, src_v))
+
+    def close(self):
+        self.pool.shutdown()
+
+
+def kvmret_lib():
+    import kvmret
+    return kvmret.lib
+
+
+def f16_ulps(a_bits, b_bits):
+    a = np.asarray(a_bits, np.uint16).astype(np.int32)
+    b = np.asarray(b_bits, np.uint16).astype(np.int32)
+    oa = np.where(a & 0x8000, 0x8000 - a, a)
+    ob = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(oa - ob)
+
+
+def q8_diff(a, b):
+    a = np.asarray(a, np.uint8).reshape(-1, 34)
+    b = np.asarray(b, np.uint8).reshape(-1, 34)
+    qa = a[:, 2:].view(np.int8).astype(np.int32)
+    qb = b[:, 2:].view(np.int8).astype(np.int32)
+    da = a[:, :2].copy().view(np.uint16).reshape(-1)
+    db = b[:, :2].copy().view(np.uint16).reshape(-1)
+    return int(np.abs(qa - qb).max(initial=0)), int(f16_ulps(da, db).max(initial=0))
+
+
 def run_ours(args, w):
     import numpy as np
     import torch
@@ -265,6 +511,7 @@ def run_ours(args, w):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
@@ -348,80 +595,122 @@ def run_ours(args, w):
         r.select_apply_async()
         mark("apply_enqueued")
 
+    # every host-table operation of the run, in order (the parity pass replays
+    # them in the oracle's store)
+    table_log = []
+
+    def collect():
+        ids_k, st_k = r.step_collect()
+        table_log.append(("sel", ids_k))
+        return ids_k, st_k
+
     def queries(n):
-        out = []
-        for _ in range(n):
-            q = hist.next_query()[layer0:layer0 + Ll].contiguous()
-            out.append(q)
-        return out
+        return [hist.next_query()[layer0:layer0 + Ll].contiguous() for _ in range(n)]
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # clocks are sampled from before the warm-up until after the e2e loop
+    # clocks are sampled from before the warm-up until after the last timed loop
     clocks = Clocks(local)
     time.sleep(0.6)
     # warm-up (the first step stages the whole window from the host)
     warm_q = queries(args.warmup)
     step(warm_q[0])
-    ids0 = r.step_collect()[0]
+    ids0 = collect()[0]
+    warm_ids = []
 
     def restart():
-        """Untimed: the start state both measured loops begin from. An empty
+        """Untimed: the start state every measured loop begins from. An empty
         working set and pool (kvmret_clear_working_set), the first warm-up
         step's selection staged again, then the other warm-up steps; the state
         (window, pool contents and LRU order) is then a function of these
-        queries alone, so the e2e loop repeats the timed loop's work exactly."""
+        queries alone, so every loop repeats the same work."""
         r.clear_working_set(drop_pool=True)
+        table_log.append(("clear", True))
         r.apply(ids0)
+        table_log.append(("sel", ids0))
+        warm_ids.clear()
         for q in warm_q[1:]:
             step(q)
-            r.step_collect()
+            warm_ids.append(collect()[0])
         r.sync()
 
-    restart()
+    def timed_loop(qs):
+        """Device time of exactly len(qs) steps on the library stream (max over
+        ranks), with each step's ids and stats and the kernel timings."""
+        restart()
+        torch.cuda.synchronize()
+        r.prof_enable(True)
+        barrier()
+        r.sync()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stats, ids_l = [], []
+        marks.clear()
+        e0.record(ext)
+        # the host enqueues step k+1 before collecting step k, so the device never
+        # waits for the host between steps. The NVTX range lets a profiler keep
+        # only these launches (ncu --nvtx --nvtx-include "timed_steps/").
+        torch.cuda.nvtx.range_push("timed_steps")
+        for i, q in enumerate(qs):
+            step(q)
+            if i > 0:
+                ids_k, st_k = collect()
+                ids_l.append(ids_k)
+                stats.append(st_k)
+        torch.cuda.nvtx.range_pop()
+        e1.record(ext)
+        ids_k, st_k = collect()
+        ids_l.append(ids_k)
+        stats.append(st_k)
+        r.sync()
+        torch.cuda.synchronize()
+        barrier()
+        prof = r.prof_read()
+        r.prof_enable(False)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / len(qs), ids_l, stats, prof
 
-    # timed region: device time of exactly K steps on the library stream
+    def avg(key, ss):
+        return sum(s[key] for s in ss) / len(ss)
+
+    hbm, peak_src = load_peaks()
+    asm_name = "assemble_kernel" if w.k_type == kvmret.TYPE_F16 else "assemble_quant_kernel"
+
+    def figures(ms_step, stats, prof):
+        """Per-step byte counts, the assembly kernel's live roofline and the step roofline."""
+        n_launch = max(1, prof["n_asm"])
+        asm_ms = prof["asm_ms"] / n_launch
+        asm_hbm = prof["asm_hbm_bytes"] / n_launch
+        asm_link = prof["asm_link_bytes"] / n_launch
+        achieved = asm_hbm / (asm_ms / 1e3) / 1e9 if asm_ms > 0 else 0.0
+        t_asm_roof = max(asm_hbm / (hbm * 1e9), asm_link / (link * 1e9))
+        h2d_step = avg("h2d_bytes", stats)
+        asm_step = avg("assemble_bytes", stats)
+        score_step = prof["score_bytes"] / max(1, prof["n_score"])
+        score_ms = prof["score_ms"] / max(1, prof["n_score"])
+        t_roof = score_step / (hbm * 1e9) + max(h2d_step / (link * 1e9),
+                                                 (h2d_step + asm_step) / (hbm * 1e9))
+        return {"asm_ms": asm_ms, "asm_hbm": asm_hbm, "asm_link": asm_link,
+                "achieved": achieved,
+                "asm_frac": t_asm_roof / (asm_ms / 1e3) if asm_ms > 0 else 0.0,
+                "h2d_step": h2d_step, "asm_step": asm_step, "score_step": score_step,
+                "score_ms": score_ms,
+                "score_gbs": score_step / (score_ms / 1e3) / 1e9 if score_ms > 0 else 0.0,
+                "t_roof": t_roof, "step_frac": t_roof * 1e3 / ms_step,
+                "churn": {"n_h2d_blocks": round(avg("n_h2d_blocks", stats), 2),
+                          "n_moved": round(avg("n_moved", stats), 2),
+                          "n_assembled": round(avg("n_assembled", stats), 2)}}
+
+    # --- timed region: device time of exactly K steps on the library stream
     qs = queries(args.steps)
     qh = [q.cpu().pin_memory() for q in qs]  # the same K queries for the e2e loop
-    torch.cuda.synchronize()
-    r.prof_enable(True)
-    barrier()
-    r.sync()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stats = []
-    ids_timed = []
-    marks.clear()
-    e0.record(ext)
-    # the host enqueues step k+1 before collecting step k, so the device never
-    # waits for the host between steps. The NVTX range lets a profiler keep
-    # only these launches (ncu --nvtx --nvtx-include "timed_steps/").
-    torch.cuda.nvtx.range_push("timed_steps")
-    for i, q in enumerate(qs):
-        step(q)
-        if i > 0:
-            ids_k, st_k = r.step_collect()
-            ids_timed.append(ids_k)
-            stats.append(st_k)
-    torch.cuda.nvtx.range_pop()
-    e1.record(ext)
-    ids_k, st_k = r.step_collect()
-    ids_timed.append(ids_k)
-    stats.append(st_k)
-    r.sync()
-    torch.cuda.synchronize()
-    barrier()
-    if args.print_steps and rank == 0:
-        # per timed step: what the window assembly of that step moved (the
-        # algorithmic bytes of a launch a profiler captured)
-        for i, st in enumerate(stats):
-            print(f"step {i}: n_moved {st['n_moved']} n_h2d {st['n_h2d_blocks']} "
-                  f"assemble_bytes {st['assemble_bytes']} h2d_bytes {st['h2d_bytes']}",
-                  file=sys.stderr)
-    prof = r.prof_read()
-    r.prof_enable(False)
+    ms_step, ids_timed, stats, prof = timed_loop(qs)
     timeline = None
     if args.timeline and marks:
         acc, cnt = {}, {}
@@ -431,85 +720,152 @@ def run_ours(args, w):
             cnt[key] = cnt.get(key, 0) + 1
         timeline = {k: round(acc[k] / cnt[k] * 1e3, 1) for k in acc}
         marks.clear()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
+    if args.print_steps and rank == 0:
+        # per timed step: what the window assembly of that step moved (the
+        # algorithmic bytes of a launch a profiler captured)
+        for i, st in enumerate(stats):
+            print(f"step {i}: n_moved {st['n_moved']} n_h2d {st['n_h2d_blocks']} "
+                  f"assemble_bytes {st['assemble_bytes']} h2d_bytes {st['h2d_bytes']}",
+                  file=sys.stderr)
 
-    # e2e: the same K queries from pinned host memory -> device every step, ids
-    # back on the host, from the same start state as the timed loop (its
+    # --- e2e: the same K queries from pinned host memory -> device every step,
+    # ids back on the host, from the same start state as the timed loop (its
     # selections and per-step work are checked against the timed loop's below)
     restart()
     qd = torch.empty_like(qs[0])
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    e2e_stats = []
-    e2e_ids = []
+    e2e_stats, e2e_ids = [], []
     for i, q in enumerate(qh):
         qd.copy_(q, non_blocking=True)
         step(qd)
         if i > 0:
-            ids_k, st_k = r.step_collect()  # the previous step's ids, read on the host
+            ids_k, st_k = collect()  # the previous step's ids, read on the host
             e2e_ids.append(ids_k)
             e2e_stats.append(st_k)
-    ids_k, st_k = r.step_collect()
+    ids_k, st_k = collect()
     e2e_ids.append(ids_k)
     e2e_stats.append(st_k)
     r.sync()
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    clk = clocks.stop()
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_us = e2e_s / args.steps * 1e6
-
-    def avg(key, ss):
-        return sum(s[key] for s in ss) / len(ss)
-
     e2e_same = (len(e2e_ids) == len(ids_timed) and
                 all(np.array_equal(a, b) for a, b in zip(e2e_ids, ids_timed)) and
                 all(a["n_moved"] == b["n_moved"] and a["n_h2d_blocks"] == b["n_h2d_blocks"]
                     for a, b in zip(e2e_stats, stats)))
 
-    n_h2d = avg("n_h2d_blocks", stats)
-    n_moved = avg("n_moved", stats)
-    n_asm = avg("n_assembled", stats)
-    h2d_step = avg("h2d_bytes", stats)
-    asm_step = avg("assemble_bytes", stats)
-    score_step = prof["score_bytes"] / max(1, prof["n_score"])
-    if prof["dropped"]:
-        print(f"warning: {prof['dropped']} timing regions dropped", file=sys.stderr)
-    hbm, peak_src = load_peaks()
+    # --- the other residency, same queries and start state (a sub-result)
+    other = None
+    if not args.no_residency_variant:
+        r.set_pool_cache(not args.pool_cache)
+        ms_o, ids_o, stats_o, prof_o = timed_loop(qs)
+        r.set_pool_cache(args.pool_cache)
+        fo = figures(ms_o, stats_o, prof_o)
+        other = {"pool_cache": not args.pool_cache,
+                 "residency": ("HBM pool keeps evicted blocks in idle slots" if not
+                               args.pool_cache else "only the working set on the GPU (the "
+                                                    "reference's residency)"),
+                 "value": round(ms_o * 1e3, 1), "unit": "us/step",
+                 "same_ids_as_timed": all(np.array_equal(a, b) for a, b in zip(ids_o, ids_timed)),
+                 "churn": fo["churn"],
+                 "step_roofline": {"t_roof_us": round(fo["t_roof"] * 1e6, 1),
+                                   "frac": round(fo["step_frac"], 4)},
+                 "assembly": {"avg_launch_ms": round(fo["asm_ms"], 4),
+                              "frac": round(fo["asm_frac"], 4),
+                              "bound": "hbm" if fo["asm_hbm"] / hbm >= fo["asm_link"] / link
+                              else "host link"}}
 
-    # roofline of the dominant kernel (window assembly), live event timing. One
-    # launch rebuilds moved slots from the HBM pool and fresh slots from the host
-    # repository, so its bound is the slower of its HBM bytes at the HBM peak and
-    # its host-link bytes at the measured link bandwidth.
-    n_launch = max(1, prof["n_asm"])
-    asm_ms = prof["asm_ms"] / n_launch
-    asm_hbm = prof["asm_hbm_bytes"] / n_launch
-    asm_link = prof["asm_link_bytes"] / n_launch
-    achieved = asm_hbm / (asm_ms / 1e3) / 1e9 if asm_ms > 0 else 0.0
-    t_asm_roof = max(asm_hbm / (hbm * 1e9), asm_link / (link * 1e9))
-    asm_frac = t_asm_roof / (asm_ms / 1e3) if asm_ms > 0 else 0.0
-    score_ms = prof["score_ms"] / max(1, prof["n_score"])
-    score_gbs = score_step / (score_ms / 1e3) / 1e9 if score_ms > 0 else 0.0
-    # step roofline: T = B_sum/BW_hbm + max(B_link/BW_link, (B_link + B_asm)/BW_hbm)
-    t_roof = score_step / (hbm * 1e9) + max(h2d_step / (link * 1e9),
-                                             (h2d_step + asm_step) / (hbm * 1e9))
-    kv_bytes = score_step + h2d_step + asm_step
-    # DRAM traffic of one assembly launch: the ratio of ncu's dram read + write
-    # bytes to the launch's algorithmic bytes, measured on an 8-layer cut of
-    # the same workload (profiles/step_kernels_cfg2_l8.md: 1556.8 / 1585.4 MB;
-    # profiles/assemble_quant_kernel_cfg3_l8.md: 793.3 / 824.7 MB), scaled to
-    # this launch's algorithmic bytes (the traffic grows with the blocks moved).
-    traffic_ratio = (1556.8 / 1585.4) if w.k_type == kvmret.TYPE_F16 else (793.3 / 824.7)
-    asm_traffic = traffic_ratio * asm_hbm
+    # --- parity pass (untimed): the same steps once more from the same start
+    # state, one at a time, each checked against the oracle
+    parity = None
+    if not args.no_parity:
+        po = load_oracle()
+        threads = max(1, (os.cpu_count() or 1) // max(1, local_world))
+        chk = OracleCheck(po, w, r, Ll, world, threads, dist)
+        restart()
+        for op in table_log:
+            chk.replay(op)
+        n_log = len(table_log)
+        oracle_warm = [chk.ids(q.cpu()) for q in warm_q]
+        ok_ids = np.array_equal(ids0, oracle_warm[0]) and all(
+            np.array_equal(a, b) for a, b in zip(warm_ids, oracle_warm[1:]))
+        ok_plan = ok_layout = ok_v = ok_timed = True
+        k_max, k_scale_max, n_slots = 0, 0, 0
+        pass_ids = []
+        for i, q in enumerate(qs):
+            step(q)
+            ids_d, _ = collect()
+            plan = r.last_plan()
+            lay, bases = r.window_layout()
+            want = chk.ids(qh[i])
+            si, so, rm, _ = chk.store.set_selection(want)
+            pass_ids.append(ids_d)
+            ok_ids &= bool(np.array_equal(ids_d, want))
+            ok_timed &= bool(np.array_equal(ids_d, ids_timed[i]))
+            ok_plan &= bool(np.array_equal(plan.remaps, rm) and np.array_equal(plan.stage_in, si)
+                            and np.array_equal(plan.stage_out, so))
+            ok_layout &= bool(np.array_equal(lay, rm[:, 0].astype(np.uint32)) and
+                              np.array_equal(bases, rm[:, 3]))
+            n = len(rm)
+            rebuilt = np.nonzero(rm[:, 5] == 0)[0]
+            slots = {n - 1, (i * 37) % n}
+            if len(rebuilt):
+                slots.add(int(rebuilt[(i * 13) % len(rebuilt)]))
+            for sl in sorted(slots):
+                for layer in sorted({0, Ll - 1}):
+                    (kd, ksd), v_eq = chk.window_slot(layer, sl, int(rm[sl, 0]), int(rm[sl, 1]),
+                                                      int(rm[sl, 3]))
+                    k_max, k_scale_max = max(k_max, kd), max(k_scale_max, ksd)
+                    ok_v &= v_eq
+                    n_slots += 1
+        summ_ok = chk.summaries_exact() if w.k_type == kvmret.TYPE_F16 else None
+        chk.close()
+        del n_log
+        flags = torch.tensor([ok_ids, ok_plan, ok_layout, ok_v, ok_timed, e2e_same,
+                              summ_ok is not False], dtype=torch.int32, device="cuda")
+        mx = torch.tensor([k_max, k_scale_max], dtype=torch.int32, device="cuda")
+        across = True
+        if world > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            mine = b"".join(a.astype(np.uint32).tobytes() for a in pass_ids)
+            allr = [None] * world
+            dist.all_gather_object(allr, mine)
+            across = all(x == allr[0] for x in allr)
+        f = [bool(x) for x in flags.tolist()]
+        kx = mx.tolist()
+        parity = {
+            "checker": "oracle/kvmret_oracle.cpp: restated score_retrieval (terms reduced over "
+                       "all layers in layer order), pick_topk, set_selection replayed over "
+                       "every host-table operation of the run, RoPE / dequant-RoPE-FWHT-requant "
+                       "of window slots from the pinned repository's bytes",
+            "steps_checked": len(warm_q) + len(qs),
+            "ids_bit_exact": f[0], "timed_ids_equal_checked_ids": f[4],
+            "plan_rows_exact": f[1], "window_layout_exact": f[2],
+            "window_slots_checked": n_slots * (world if world > 1 else 1),
+            "window_v_exact": f[3],
+            "summaries_bit_exact": (f[6] if summ_ok is not None else None),
+        }
+        if w.k_type == kvmret.TYPE_F16:
+            parity["window_k_max_ulp"] = kx[0]
+        else:
+            parity["window_k_max_lsb"] = kx[0]
+            parity["window_k_scale_max_ulp"] = kx[1]
+            parity["summaries_note"] = ("quantised K: the repository holds q8_0 rows, the "
+                                        "summaries come from the f16 capture")
+        if world > 1:
+            parity["ids_equal_across_ranks"] = across
+
+    clk = clocks.stop()
+    fg = figures(ms_step, stats, prof)
+    kv_bytes = fg["score_step"] + fg["h2d_step"] + fg["asm_step"]
+    asm_traffic = NCU_TRAFFIC_RATIO[asm_name] * fg["asm_hbm"]
 
     line = None
     if rank == 0:
@@ -520,43 +876,42 @@ def run_ours(args, w):
             "vs_baseline": None, "dtype": decode_workload(w)[1],
             "data": "synthetic: seeded N(0,1) x LogNormal(0,0.5) channel scale, "
                     f"{w.n_planted} planted blocks, query drift {w.drift}/step",
-            "config": {
-                "workload": decode_workload(w)[0],
-                "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
-                "exchange": (args.exchange if world > 1 else None),
-                "l2": "inputs larger than L2 (summaries "
-                      f"{score_step / 2**20:.0f} MiB/step, window/pool GiB-scale)",
-                "pool_cache": bool(args.pool_cache)},
-            "roofline": {"kernel": ("assemble_kernel" if w.k_type == kvmret.TYPE_F16
-                                    else "assemble_quant_kernel")
-                                   + " (window assembly: moved slots from the HBM pool, "
-                                     "fresh slots from the host repository)",
-                         "bound": "hbm" if asm_hbm / hbm >= asm_link / link else "host link",
-                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(asm_frac, 4), "traffic": int(asm_traffic),
-                         "traffic_source": "ncu dram bytes / algorithmic bytes of an 8-layer "
-                                           "capture, scaled to this launch",
+            "config": workload_config(w),
+            "setup": {"layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
+                      "exchange": (args.exchange if world > 1 else None),
+                      "pool_cache": bool(args.pool_cache)},
+            "roofline": {"kernel": asm_name + " (window assembly: moved slots from the HBM "
+                                              "pool, fresh slots from the host repository)",
+                         "bound": "hbm" if fg["asm_hbm"] / hbm >= fg["asm_link"] / link
+                         else "host link",
+                         "achieved": round(fg["achieved"], 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(fg["asm_frac"], 4), "traffic": int(asm_traffic),
+                         "traffic_source": "ncu dram read + write bytes per algorithmic byte "
+                                           "of an 8-layer capture, times this launch's "
+                                           "algorithmic bytes",
                          "peak_source": peak_src,
-                         "avg_launch_ms": round(asm_ms, 4),
-                         "alg_hbm_bytes_per_launch": int(asm_hbm),
-                         "alg_link_bytes_per_launch": int(asm_link),
+                         "avg_launch_ms": round(fg["asm_ms"], 4),
+                         "alg_hbm_bytes_per_launch": int(fg["asm_hbm"]),
+                         "alg_link_bytes_per_launch": int(fg["asm_link"]),
                          "link_gbs_measured": round(link, 2)},
             "kernels": {
-                "score": {"ms": round(score_ms, 4), "GB/s": round(score_gbs, 1),
-                          "frac_hbm": round(score_gbs / hbm, 4)}},
-            "step_roofline": {"t_roof_us": round(t_roof * 1e6, 1),
+                "score": {"ms": round(fg["score_ms"], 4), "GB/s": round(fg["score_gbs"], 1),
+                          "frac_hbm": round(fg["score_gbs"] / hbm, 4)}},
+            "step_roofline": {"t_roof_us": round(fg["t_roof"] * 1e6, 1),
                               "t_meas_us": round(ms_step * 1e3, 1),
-                              "frac": round(t_roof * 1e3 / ms_step, 4),
+                              "frac": round(fg["step_frac"], 4),
                               "link_gbs_measured": round(link, 2),
                               "link_d2h_gbs_measured": round(link_d2h, 2), "hbm_gbs": hbm,
-                              "B_sum": int(score_step), "B_link": int(h2d_step),
-                              "B_asm": int(asm_step)},
+                              "B_sum": int(fg["score_step"]), "B_link": int(fg["h2d_step"]),
+                              "B_asm": int(fg["asm_step"])},
             "kv_gbps": round(kv_bytes / (ms_step / 1e3) / 1e9, 1),
-            "churn": {"n_h2d_blocks": round(n_h2d, 2), "n_moved": round(n_moved, 2),
-                      "n_assembled": round(n_asm, 2)},
+            "churn": fg["churn"],
+            "other_residency": other,
+            "parity": parity,
             "e2e": {"value": round(e2e_us, 1), "unit": "us/step",
                     "h2d_bytes_per_step": int(qs[0].numel() * 2 + avg("h2d_bytes", e2e_stats)),
-                    "d2h_bytes_per_step": int(w.n_blocks),
+                    # per step the readback ring returns 8 counts and the window's ids
+                    "d2h_bytes_per_step": int(4 * (8 + w.budget_blocks + w.reserve_blocks)),
                     "same_steps_as_timed": e2e_same,
                     "churn": {"n_h2d_blocks": round(avg("n_h2d_blocks", e2e_stats), 2),
                               "n_moved": round(avg("n_moved", e2e_stats), 2)}},
@@ -565,19 +920,16 @@ def run_ours(args, w):
             "clocks": clk,
             "setup_s": round(t_setup, 1),
         }
-        if world == 1 and not args.no_cpu_baseline:
-            total, parts, kind = cpu_sample(w, max(1, round(n_h2d)), max(1, round(n_asm)), 1,
-                                            False)
-            line["cpu_baseline"] = {
-                "value": round(total * 1e6, 1), "unit": "us/step", "cores": 1, "kind": kind,
-                "sample": "restated score_retrieval on 2 layers x all blocks (scaled to "
-                          f"{w.n_layer}), pick_topk + set_selection, memcpy staging of one "
-                          f"block (x{round(n_h2d)}), host RoPE of 1 block-layer (x"
-                          f"{round(n_asm)} x {w.n_layer})",
-                "parts_ms": {k: round(v * 1e3, 3) for k, v in parts.items()}}
     r.close()
     if world > 1:
         dist.destroy_process_group()
+    if line is not None and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sec, kind, churn = cpu_steps(w, 3, 1, threads, True)
+        line["cpu_baseline"] = {"value": round(sec * 1e6, 1), "unit": "us/step",
+                                "cores": threads, "kind": kind,
+                                "sample": cpu_sample_text(w, kind, 3, 1, threads),
+                                "churn": churn}
     if line is not None:
         print(json.dumps(line), flush=True)
 
@@ -948,6 +1300,10 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the untimed parity pass against the CPU oracle")
+    ap.add_argument("--no-residency-variant", action="store_true",
+                    help="skip the timed loop under the other pool residency")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: score-row exchange through NVLink peer memory written by the "
                          "scoring kernel (default), or an NCCL all-gather")
@@ -958,11 +1314,6 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (dev only)")
     ap.add_argument("--budget", type=int, default=0, help="override budget blocks (dev only)")
     ap.add_argument("--reserve", type=int, default=-1, help="override reserve slots (dev only)")
-    ap.add_argument("--churn-h2d", type=int, default=6,
-                    help="reference arm: blocks staged from the host per step (config 2 churn "
-                         "measured by this bench without the pool cache: 6.2)")
-    ap.add_argument("--churn-asm", type=int, default=168,
-                    help="reference arm: window slots rewritten per step (measured: 167.6)")
     args = ap.parse_args()
     wl = workloads()
     w = wl.CONFIGS[args.config]

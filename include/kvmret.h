@@ -203,6 +203,13 @@ int kvmret_step_collect(kvmret_ctx *ctx, uint32_t *ids_out, uint32_t *n_out,
  * the next step stages its whole selection from the host repository, as
  * right after kvmret_create. Collects any step still in flight first. */
 int kvmret_clear_working_set(kvmret_ctx *ctx, int drop_pool);
+/* Residency policy of the HBM block pool for later steps (the config's
+ * pool_cache): 1 keeps blocks that left the window in idle pool slots as a
+ * cache (least recently used evicted first), 0 frees a block's slot as soon
+ * as the block leaves the window, so only the working set stays on the GPU —
+ * the reference's residency (KvMemRuntime::spill_outgoing,
+ * kvmem/src/host/kvmem_runtime.cpp:225-249). Collects any step in flight. */
+int kvmret_set_pool_cache(kvmret_ctx *ctx, int on);
 /* llama_kvmem_apply_retrieval (src/adapter/llama-memory-kvmem.cpp:4778-4782,
  * apply_retrieval :4419-4422): preview + apply. ids_out may be NULL. */
 int kvmret_apply_retrieval(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,
@@ -353,7 +360,9 @@ int kvmret_d2d_batched(kvmret_ctx *ctx, const void *const *src, void *const *dst
  * exit; a call needing more (n_layer * summ_stride * 8 bytes plus the query
  * scratch) is rejected with KVMRET_ERR_ARG. The first call on each device,
  * with that device current, looks up the array's device address: make it
- * before any stream capture. Calls share the array (each call writes every
+ * before any stream capture. The address is cached per CUDA context; after a
+ * cudaDeviceReset the next call looks it up again (again, not while a capture
+ * is under way). Calls share the array (each call writes every
  * scratch byte it reads, so nothing needs clearing); calls that overlap on the
  * GPU race. `stream` is a cudaStream_t (NULL = legacy default stream). */
 #define KVMRET_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)

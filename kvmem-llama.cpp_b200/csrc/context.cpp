@@ -971,6 +971,15 @@ int kvmret_clear_working_set(kvmret_ctx *c, int drop_pool) {
     return KVMRET_OK;
 }
 
+int kvmret_set_pool_cache(kvmret_ctx *c, int on) {
+    NEED_CTX(c);
+    GUARD(TRY(drain(c)));
+    // the next plan frees every pooled block outside its window when caching
+    // is off (its release pass scans all pool slots)
+    c->cfg.pool_cache = on != 0;
+    return KVMRET_OK;
+}
+
 int kvmret_select_apply_async(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
     NEED_CTX(c);
     if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");
@@ -1254,6 +1263,9 @@ int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_
 int kvmret_gemm_f16_nt(const uint16_t *a, const uint16_t *b, float *c, uint32_t m, uint32_t n,
                        uint32_t k, float alpha, uint32_t *err, void *stream) {
     if (!a || !b || !c) return fail(KVMRET_ERR_ARG, "null operand");
+    // the epilogue writes C with 16-byte vector stores
+    if (reinterpret_cast<uintptr_t>(c) & 15)
+        return fail(KVMRET_ERR_ARG, "gemm output must be 16-byte aligned");
     if (m % 128 || n % 256 || k % 64 || k == 0)
         return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
     CUtensorMap ma, mb;
@@ -1306,6 +1318,8 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     CUtensorMap ma, mb;
     CK(kvmret::make_gemm_maps(c->pf_a, c->pf_b, rows, n_used, static_cast<uint32_t>(K), &ma,
                               &mb));
+    // the pipeline-timeout word reports on this launch only
+    CK(cudaMemsetAsync(c->pf_err, 0, sizeof(uint32_t), c->st));
     const int pr = prof_begin(c, c->st, PR_GEMM);
     CK(kvmret::launch_gemm_f16_nt(ma, mb, c->pf_s, rows, n_used, static_cast<uint32_t>(K),
                                   1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st));

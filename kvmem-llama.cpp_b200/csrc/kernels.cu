@@ -145,6 +145,14 @@ __device__ void exchange_signal(const Peers &peers, const double *local, uint32_
     }
 }
 
+// The exchange signal alone, for a rank whose history holds no block yet: its
+// peers still wait for this rank's step flag (and its layers' query flags).
+__global__ void exchange_signal_kernel(const double *local, uint32_t cstride,
+                                       const __grid_constant__ Peers peers) {
+    dep_wait();
+    exchange_signal(peers, local, cstride);
+}
+
 // ---------------------------------------------------------------------------
 // S3: a unit = one layer x TILE blocks (64: lane j walks blocks 2j, 2j+1 with
 // float2 loads; 32: one block per lane). Summaries are block-minor
@@ -1588,7 +1596,12 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
                          cudaStream_t st, uint32_t cstride, const Peers *peers_in) {
     if (cstride == 0) cstride = ncap;
-    if (n_blocks == 0) return cudaSuccess;
+    if (n_blocks == 0) {
+        if (peers_in && peers_in->n > 1)
+            return launch_dep(exchange_signal_kernel, dim3(1), dim3(256), 0, st,
+                              static_cast<const double *>(contrib), cstride, *peers_in);
+        return cudaSuccess;
+    }
     Peers none{};
     const Peers &peers = peers_in ? *peers_in : none;
     switch (d_head) {
@@ -1610,8 +1623,10 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st, const uint32_t *wait_flags,
                           uint32_t wait_n, uint32_t wait_step, uint32_t *err) {
-    if (n_blocks == 0) return cudaSuccess;
-    return launch_dep(reduce_kernel, dim3((n_blocks + 127) / 128), dim3(128), n_layer, st,
+    // with an exchange to wait for, one CTA still takes part in the step
+    // protocol when there is nothing to reduce
+    if (n_blocks == 0 && !wait_flags) return cudaSuccess;
+    return launch_dep(reduce_kernel, dim3(std::max(1u, (n_blocks + 127) / 128)), dim3(128), n_layer, st,
                       contrib, active, n_layer, stride, has_block, n_blocks, scores, wait_flags,
                       wait_n, wait_step, err);
 }

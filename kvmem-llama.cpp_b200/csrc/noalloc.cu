@@ -11,8 +11,10 @@
 //
 // The array is KVMRET_NOALLOC_SCRATCH_BYTES (8 MiB) and every GPU that loads
 // this library holds it until the process exits. Its device address is looked
-// up once per device, with that device current, on the first call made on the
-// device; make that first call before any CUDA stream capture begins. All
+// up once per device and CUDA context, with that device current, on the first
+// call made in that context; make that first call before any CUDA stream
+// capture begins. After cudaDeviceReset the device gets a new context and the
+// next call looks the address up again (the module is loaded anew). All
 // calls on a device share the array and it keeps the previous call's
 // contents: every byte a call reads is written by the same call first, so
 // nothing needs clearing, but two calls whose work overlaps on the GPU (for
@@ -36,7 +38,34 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[KVMRET_NOALLOC_
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void *g_scratch_dev[kMaxDevices] = {};
+// per device: the context the address was looked up in, and the address
+struct ScratchEntry {
+    void *ctx;
+    void *ptr;
+};
+ScratchEntry g_scratch_dev[kMaxDevices] = {};
+
+// cuCtxGetCurrent through the runtime's driver entry-point table (the library
+// does not link the driver library itself).
+typedef int (*CtxGetCurrentFn)(void **);
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<CtxGetCurrentFn>(nullptr);
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    return fn;
+}
+
+void *current_ctx() {
+    void *ctx = nullptr;
+    const CtxGetCurrentFn fn = ctx_get_current();
+    if (!fn || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
 
 int nerr(int code, const std::string &msg) { return kvmret::set_error(code, msg.c_str()); }
 
@@ -49,15 +78,20 @@ int scratch_for_current_device(void **out) {
     if (e != cudaSuccess) return nerr(KVMRET_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return nerr(KVMRET_ERR_ARG, "device ordinal out of range");
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_dev[dev]) {
+    ScratchEntry &ent = g_scratch_dev[dev];
+    void *ctx = ent.ptr ? current_ctx() : nullptr;
+    if (!ent.ptr || !ctx || ctx != ent.ctx) {
+        // first call in this context (or a context we cannot identify): look
+        // the address up, which also makes the device's context current
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p)
             return nerr(KVMRET_ERR_CUDA,
                         std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-        g_scratch_dev[dev] = p;
+        ent.ptr = p;
+        ent.ctx = current_ctx();
     }
-    *out = g_scratch_dev[dev];
+    *out = ent.ptr;
     return KVMRET_OK;
 }
 

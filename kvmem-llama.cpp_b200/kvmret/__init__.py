@@ -136,6 +136,7 @@ SIGNATURES = {
     "kvmret_select_apply_async": (ctypes.c_int, [_P, _PU32, _U32]),
     "kvmret_step_collect": (ctypes.c_int, [_P, _PU32, _PU32, ctypes.POINTER(StepStats)]),
     "kvmret_clear_working_set": (ctypes.c_int, [_P, ctypes.c_int]),
+    "kvmret_set_pool_cache": (ctypes.c_int, [_P, ctypes.c_int]),
     "kvmret_last_plan": (ctypes.c_int, [_P, _PI32, _PU32, _PU32, _PU32, _PU32, _PU32]),
     "kvmret_window_k": (_P, [_P, _U32]),
     "kvmret_window_v": (_P, [_P, _U32]),
@@ -434,6 +435,11 @@ class Retriever:
         """Empty the working set (a new session over the same history); with
         drop_pool the HBM pool is forgotten too, as right after creation."""
         _check(lib.kvmret_clear_working_set(self.h, int(drop_pool)))
+
+    def set_pool_cache(self, on: bool):
+        """Residency of the HBM pool for later steps: cache evicted blocks in
+        idle slots (True) or keep only the working set (False)."""
+        _check(lib.kvmret_set_pool_cache(self.h, int(on)))
 
     def apply_retrieval(self, mandatory=()):
         m, mp = _u32(list(mandatory))

@@ -660,3 +660,38 @@ ORC_API void orc_rope_block_q4_0(const uint8_t *k_q4, uint32_t n_tok, uint32_t n
     if (fwht_n) orc_fwht(b.data(), n / fwht_n, fwht_n);
     orc_quant_q4_0(b.data(), out, n / 32);
 }
+
+// ---------------------------------------------------------------------------
+// Host stage-in of one step for the benchmark's CPU arms when the reference
+// library was not built: units [u0, u1) of (block, layer) K rotated with
+// orc_rope_block_f16 at their window bases, V bytes copied; and a list of
+// byte copies (the staging memcpy).
+ORC_API void orc_rope_units_f16(const uint16_t *const *k_src, uint16_t *const *k_dst,
+                                const uint8_t *const *v_src, uint8_t *const *v_dst,
+                                uint64_t v_bytes, const int32_t *pos0, uint32_t u0, uint32_t u1,
+                                uint32_t n_tok, uint32_t n_head, uint32_t n_embd_head,
+                                float freq_base, float freq_scale) {
+    for (uint32_t u = u0; u < u1; ++u) {
+        orc_rope_block_f16(k_src[u], n_tok, n_head, n_embd_head, n_embd_head, pos0[u], freq_base,
+                           freq_scale, k_dst[u]);
+        if (v_bytes) std::memcpy(v_dst[u], v_src[u], v_bytes);
+    }
+}
+
+// q8_0 K units: dequant -> RoPE -> FWHT -> requant (orc_rope_block_q8_0).
+ORC_API void orc_rope_units_q8_0(const uint8_t *const *k_src, uint8_t *const *k_dst,
+                                 const uint8_t *const *v_src, uint8_t *const *v_dst,
+                                 uint64_t v_bytes, const int32_t *pos0, uint32_t u0, uint32_t u1,
+                                 uint32_t n_tok, uint32_t n_head, uint32_t n_embd_head,
+                                 float freq_base, float freq_scale, uint32_t fwht_n) {
+    for (uint32_t u = u0; u < u1; ++u) {
+        orc_rope_block_q8_0(k_src[u], n_tok, n_head, n_embd_head, n_embd_head, pos0[u], freq_base,
+                            freq_scale, fwht_n, k_dst[u]);
+        if (v_bytes) std::memcpy(v_dst[u], v_src[u], v_bytes);
+    }
+}
+
+ORC_API void orc_copy_list(const uint8_t *const *src, uint8_t *const *dst, const uint64_t *nbytes,
+                           uint32_t i0, uint32_t i1) {
+    for (uint32_t i = i0; i < i1; ++i) std::memcpy(dst[i], src[i], nbytes[i]);
+}

@@ -24,6 +24,7 @@ _PF = ctypes.POINTER(ctypes.c_float)
 _PD = ctypes.POINTER(ctypes.c_double)
 _PU8 = ctypes.POINTER(ctypes.c_uint8)
 _PU16 = ctypes.POINTER(ctypes.c_uint16)
+_PP = ctypes.POINTER(ctypes.c_void_p)
 
 
 def _ptr(a, t):
@@ -65,6 +66,11 @@ def _load_orc():
                                        ctypes.c_float, ctypes.c_float, _U32, _PU8]),
         "orc_rope_block_q4_0": (None, [_PU8, _U32, _U32, _U32, _U32, ctypes.c_int32,
                                        ctypes.c_float, ctypes.c_float, _U32, _PU8]),
+        "orc_rope_units_f16": (None, [_PP, _PP, _PP, _PP, ctypes.c_uint64, _PI32, _U32, _U32,
+                                      _U32, _U32, _U32, ctypes.c_float, ctypes.c_float]),
+        "orc_rope_units_q8_0": (None, [_PP, _PP, _PP, _PP, ctypes.c_uint64, _PI32, _U32, _U32,
+                                       _U32, _U32, _U32, ctypes.c_float, ctypes.c_float, _U32]),
+        "orc_copy_list": (None, [_PP, _PP, ctypes.POINTER(ctypes.c_uint64), _U32, _U32]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -90,6 +96,9 @@ def _load_ref():
         "ref_mean_k_f32": (None, [_PF, _U32, _U32, _U32, _PF]),
         "ref_rope_neox": (None, [_PF, _U32, _U32, _U32, _U32, ctypes.c_int32, ctypes.c_float,
                                  ctypes.c_float, _PF]),
+        "ref_rope_units_f16": (None, [_PP, _PP, _PP, _PP, ctypes.c_uint64, _PI32, _U32, _U32,
+                                      _U32, _U32, _U32, ctypes.c_float, ctypes.c_float]),
+        "ref_copy_list": (None, [_PP, _PP, ctypes.POINTER(ctypes.c_uint64), _U32, _U32]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)

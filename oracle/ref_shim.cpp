@@ -109,3 +109,39 @@ REF_API void ref_rope_neox(const float *k, uint32_t n_tok, uint32_t n_head,
     c.freq_scale = freq_scale;
     kvmem::rope_neox_apply(c, k, n_tok, pos0, out);
 }
+
+// The stage-in work of one retrieval step on the host cores, for the CPU
+// reference arm of the benchmark: every unit is one (block, layer) of the
+// window. Its K (n_tok rows of n_head x n_embd_head f16) is converted to f32,
+// rotated by the reference's rope_neox_apply at the unit's window base, and
+// rounded back to f16 (F16C conversions, round to nearest even); its V bytes
+// are copied. Units [u0, u1) of the arrays; a caller splits the units over
+// its threads.
+REF_API void ref_rope_units_f16(const uint16_t *const *k_src, uint16_t *const *k_dst,
+                                const uint8_t *const *v_src, uint8_t *const *v_dst,
+                                uint64_t v_bytes, const int32_t *pos0, uint32_t u0, uint32_t u1,
+                                uint32_t n_tok, uint32_t n_head, uint32_t n_embd_head,
+                                float freq_base, float freq_scale) {
+    kvmem::RopeConfig c;
+    c.n_rot = n_embd_head;
+    c.n_embd_head = n_embd_head;
+    c.n_head_kv = n_head;
+    c.freq_base = freq_base;
+    c.freq_scale = freq_scale;
+    const size_t n = static_cast<size_t>(n_tok) * n_head * n_embd_head;
+    std::vector<float> x(n), y(n);
+    for (uint32_t u = u0; u < u1; ++u) {
+        const _Float16 *src = reinterpret_cast<const _Float16 *>(k_src[u]);
+        _Float16 *dst = reinterpret_cast<_Float16 *>(k_dst[u]);
+        for (size_t i = 0; i < n; ++i) x[i] = static_cast<float>(src[i]);
+        kvmem::rope_neox_apply(c, x.data(), n_tok, pos0[u], y.data());
+        for (size_t i = 0; i < n; ++i) dst[i] = static_cast<_Float16>(y[i]);
+        if (v_bytes) std::memcpy(v_dst[u], v_src[u], v_bytes);
+    }
+}
+
+// Byte copies [i0, i1) of a list (the staging memcpy of stage-in blocks).
+REF_API void ref_copy_list(const uint8_t *const *src, uint8_t *const *dst, const uint64_t *nbytes,
+                           uint32_t i0, uint32_t i1) {
+    for (uint32_t i = i0; i < i1; ++i) std::memcpy(dst[i], src[i], nbytes[i]);
+}

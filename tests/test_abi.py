@@ -47,3 +47,11 @@ def test_bad_config_is_rejected_with_message():
     rc = kvmret.lib.kvmret_create(ctypes.byref(c), ctypes.byref(h))
     assert rc == -1 and not h
     assert b"d_head" in kvmret.lib.kvmret_last_error()
+
+
+def test_gemm_rejects_misaligned_output_before_any_launch():
+    # fake, never dereferenced device addresses: the output's 16-byte
+    # alignment is checked on the host before any CUDA call
+    rc = kvmret.lib.kvmret_gemm_f16_nt(16, 16, 17, 128, 256, 64, 1.0, None, None)
+    assert rc == -1
+    assert b"aligned" in kvmret.lib.kvmret_last_error()

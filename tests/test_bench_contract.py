@@ -1,6 +1,6 @@
 """bench.py's JSON contract, on the CPU: the reference arm's line (config 1,
-one step) carries the keys the driver reads and the same workload description
-as this library's arm; other ranks of a multi-rank launch print nothing; the
+one step, run in full) carries the keys the driver reads and the same config
+object as this library's arm; other ranks of a multi-rank launch print nothing; the
 reference arm never loads this library's native code."""
 import json
 import os
@@ -36,7 +36,11 @@ def test_reference_arm_line_and_isolation():
     import bench
     wl = bench.workloads()
     assert d["config"]["workload"] == bench.decode_workload(wl.CONFIGS[1])[0]
+    # the same `config` object the library's arm prints for this workload
+    assert d["config"] == bench.workload_config(wl.CONFIGS[1])
     assert d["dtype"] == "f16"
+    # every step ran in full: its selection churn is reported, not assumed
+    assert d["churn"]["n_rebuilt"] >= 0 and "every" in d["cpu_baseline"]["sample"]
 
 
 def test_reference_arm_other_ranks_print_nothing():

@@ -188,3 +188,81 @@ def test_exchange_wait_gives_up_when_a_rank_never_writes():
         q_done.put(1)
         p.join(timeout=120)
     assert p.exitcode == 0
+
+
+def _empty_rank(w_kwargs, q_handle, q_peer, q_done):
+    """Rank 1 of a 2-rank exchange whose history holds no block: it scores
+    once (no query rows), which must still publish its step flag to rank 0;
+    its own wait for rank 0 (which has not scored yet) gives up after 2 s."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (here, os.path.join(root, "kvmem-llama.cpp_b200")):
+        sys.path.insert(0, p)
+    import kvmret
+    from kvm_helpers import config_for
+    from kvmret import synth
+    r = kvmret.Retriever(config_for(synth.Workload(**w_kwargs)))
+    h1 = r.exchange_export(2)
+    q_handle.put(h1)
+    h0 = q_peer.get(timeout=300)
+    r.exchange_import(1, [h0, h1])
+    r.query_reset()
+    r.score_exchange()
+    r.select_apply_async()
+    try:
+        r.step_collect()
+        status = "ok"
+    except kvmret.KvmretError as e:
+        status = str(e)
+    r.sync()
+    q_done.put(status)
+    q_peer.get(timeout=300)  # rank 0 finished with this rank's region
+    r.close()
+
+
+def test_exchange_rank_with_empty_history_still_signals():
+    """A rank with no blocks yet takes part in the step protocol: rank 0 (with
+    a history) completes its exchange step at once, with the oracle's
+    selection over its own layers (rank 1 contributes no query rows), instead
+    of timing out. The ranks' steps run one after the other, never as two
+    waiting kernels at the same time."""
+    import time
+    import kvmret
+    import pyoracle as po
+    from kvm_helpers import append_history, config_for, oracle_scores
+    from kvmret import synth
+    wk = dict(name="ex0", n_layer=2, n_head=8, n_head_kv=2, d_head=128, block_tokens=64,
+              n_blocks=32, budget_blocks=6, sink_blocks=1, reserve_blocks=0, n_planted=2,
+              seed=62)
+    ctx = mp.get_context("spawn")
+    q_handle, q_peer, q_done = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    p = ctx.Process(target=_empty_rank, args=(wk, q_handle, q_peer, q_done))
+    p.start()
+    try:
+        w = synth.Workload(**wk)
+        hist = synth.NumpyHistory(w)
+        r = kvmret.Retriever(config_for(w))
+        append_history(r, hist, cuts=[])
+        h0 = r.exchange_export(2)
+        h1 = q_handle.get(timeout=300)
+        q_peer.put(h0)
+        r.exchange_import(0, [h0, h1])
+        # rank 1 scores first and gives up waiting for rank 0 (bounded, 2 s)
+        assert "0x100" in q_done.get(timeout=300)
+        q = hist.queries(1)[0]
+        r.query_reset()
+        r.query_add(torch.from_numpy(q.reshape(w.n_layer, 1, -1)).cuda())
+        t0 = time.monotonic()
+        r.score_exchange()
+        r.select_apply_async()
+        ids, _ = r.step_collect()
+        assert time.monotonic() - t0 < 1.5  # rank 1's flag was already there
+        want, _ = oracle_scores(hist, q.reshape(w.n_layer, -1).astype(np.float32),
+                                np.ones(w.n_layer, np.uint32))
+        assert list(ids) == list(po.pick_topk(want, w.budget_blocks, w.sink_blocks))
+        r.close()
+    finally:
+        q_peer.put(1)
+        p.join(timeout=120)
+    assert p.exitcode == 0
