@@ -175,18 +175,27 @@ class CpuRetrieval:
     the new window base (f16 in and out; q8_0 K: dequant -> RoPE -> FWHT ->
     requant) and its V rows copied into the window.
 
-    The workload has the distributions of the GPU arm's: block summaries are
-    the block means of N(0,1) x LogNormal(0,0.5) channel-scaled keys (drawn
-    directly as N(0, 1/T) x scale, planted blocks +0.5 along the group query
-    direction), the decode query drifts by 0.05 N(0,1) per step. The host
-    repository holds R distinct blocks (block b reads slot b mod R) and the
-    window holds S slots (slot i writes i mod S): 1 GiB and 2 GiB, well above
-    the host caches, so the copies and RoPE stream from and to DRAM as with
-    the full-size arrays."""
+    Workload: the library arm's own history (TorchHistory, generated with
+    torch on the GPU when one is present) with its block summaries computed by
+    the library's arithmetic (token-order f32 sum x 1/T), and the same drifting
+    query sequence, so both arms select the same blocks step by step; without
+    a GPU, summaries drawn from the same distributions (N(0, 1/T) x channel
+    scale, planted blocks +0.5 along the group query direction). With a decode
+    tail the newest tail_blocks are this turn's decode blocks: each step
+    appends one decode token and the top-k runs over the blocks before them
+    (they stay in the window beyond the budget, as the library's gen mode
+    keeps them). The host repository holds R distinct blocks (block b reads
+    slot b mod R) and the window holds S slots (slot i writes i mod S): 1 GiB
+    and 2 GiB, well above the host caches, so the copies and RoPE stream from
+    and to DRAM as with the full-size arrays."""
 
     R, S = 32, 64
 
-    def __init__(self, w, threads, use_ref=True, seed_offset=0):
+    def __init__(self, w, threads, use_ref=True, tail_blocks=0, source=None, decode=True):
+        """source: (summaries [N][L][E] f32, next_query() -> [L][Hq*D] f16
+        numpy); None: generate the workload here. decode: one decode token
+        appended per step, the decode blocks (the newest tail_blocks and the
+        token's block) kept beyond the budget."""
         import concurrent.futures as cf
         po = load_oracle()
         self.po, self.w = po, w
@@ -198,20 +207,13 @@ class CpuRetrieval:
         self.f16 = w.k_type == TYPE_F16
         L, Hq, Hkv, D, N, T = w.n_layer, w.n_head, w.n_head_kv, w.d_head, w.n_blocks, \
             w.block_tokens
-        rng = np.random.default_rng(w.seed + seed_offset)
-        scale = np.exp(rng.normal(0.0, 0.5, size=(L, Hkv, D))).astype(np.float32)
-        q0 = rng.standard_normal((L, Hq, D)).astype(np.float16)
-        planted = np.sort(rng.choice(np.arange(w.sink_blocks, N), size=min(w.n_planted,
-                                     N - w.sink_blocks), replace=False))
-        qg = q0.astype(np.float32).reshape(L, Hkv, Hq // Hkv, D).sum(axis=2)
-        u = qg / np.linalg.norm(qg, axis=-1, keepdims=True)
-        mean = rng.standard_normal((N, L, Hkv, D), dtype=np.float32)
-        mean *= scale[None] / np.float32(np.sqrt(T))
-        mean[planted] += np.float32(0.5) * u[None]
-        self.mean = mean.reshape(N, L, Hkv * D)
+        rng = np.random.default_rng(w.seed)
+        if source is None:
+            source = cpu_workload(w, rng)
+        self.mean, self._next_query = source
         self.has = np.ones(N, np.uint8)
-        self.q = q0.astype(np.float32)
-        self.qrng = np.random.default_rng(w.seed + seed_offset + 7)
+        self.decode = decode
+        self.gen_first = N - tail_blocks if decode else N
         E = w.E
         self.k_row = E * 2 if self.f16 else E // 32 * 34
         self.v_row = E * 2 if w.v_type == TYPE_F16 else (E // 32 * 34 if w.v_type == 8
@@ -238,13 +240,11 @@ class CpuRetrieval:
         else:
             self.rt = po.Store(T)
         self.rt.append(N * T)
+        self.n_tok = N * T
         self.fwht_n = D if not self.f16 else 0
 
     def next_query(self):
-        q16 = self.q.astype(np.float16)
-        self.q = self.q + np.float32(self.w.drift) * self.qrng.standard_normal(
-            self.q.shape).astype(np.float32)
-        return q16.reshape(self.w.n_layer, -1)
+        return self._next_query()
 
     def _score(self, q_sum):
         w, po = self.w, self.po
@@ -265,10 +265,17 @@ class CpuRetrieval:
         L = w.n_layer
         q_sum = self.next_query().astype(np.float32)
         scores = self._score(q_sum)
+        g0 = self.gen_first
+        if self.decode:  # one decode token per step
+            self.rt.append(1)
+            self.n_tok += 1
+        nb = (self.n_tok + w.block_tokens - 1) // w.block_tokens
         if self.use_ref:
-            ids = po.ref_pick_topk(scores, w.budget_blocks, w.sink_blocks)
+            ids = po.ref_pick_topk(scores[:g0], w.budget_blocks, w.sink_blocks)
         else:
-            ids = po.pick_topk(scores, w.budget_blocks, w.sink_blocks)
+            ids = po.pick_topk(scores[:g0], w.budget_blocks, w.sink_blocks)
+        if g0 < nb:  # the decode blocks stay in the window beyond the budget
+            ids = np.concatenate([ids, np.arange(g0, nb, dtype=ids.dtype)])
         si, so, rm, cnt = self.rt.set_selection(ids)
         # staging memcpy: every stage-in block's K and V rows of all layers
         import ctypes
@@ -319,9 +326,42 @@ class CpuRetrieval:
         self.pool.shutdown()
 
 
-def cpu_steps(w, steps, warmup, threads, use_ref=True):
+def cpu_workload(w, rng):
+    """(summaries [N][L][E] f32, next_query) of the workload: the library arm's
+    own TorchHistory and query sequence when a GPU is present, else draws from
+    the same distributions."""
+    try:
+        import torch
+        gpu = torch.cuda.is_available()
+    except ImportError:
+        gpu = False
+    if gpu:
+        mean, h = workloads().torch_block_summaries(w, 0)
+        return mean, lambda: h.next_query().reshape(w.n_layer, -1).cpu().numpy()
+    L, Hq, Hkv, D, N, T = w.n_layer, w.n_head, w.n_head_kv, w.d_head, w.n_blocks, \
+        w.block_tokens
+    scale = np.exp(rng.normal(0.0, 0.5, size=(L, Hkv, D))).astype(np.float32)
+    q0 = rng.standard_normal((L, Hq, D)).astype(np.float16)
+    planted = workloads().planted_ids(w, rng)
+    qg = q0.astype(np.float32).reshape(L, Hkv, Hq // Hkv, D).sum(axis=2)
+    u = qg / np.linalg.norm(qg, axis=-1, keepdims=True)
+    mean = rng.standard_normal((N, L, Hkv, D), dtype=np.float32)
+    mean *= scale[None] / np.float32(np.sqrt(T))
+    mean[planted] += np.float32(0.5) * u[None]
+    state = {"q": q0.astype(np.float32), "rng": np.random.default_rng(w.seed + 7)}
+
+    def next_query():
+        q16 = state["q"].astype(np.float16)
+        state["q"] = state["q"] + np.float32(w.drift) * state["rng"].standard_normal(
+            q0.shape).astype(np.float32)
+        return q16.reshape(L, -1)
+    return mean.reshape(N, L, Hkv * D), next_query
+
+
+def cpu_steps(w, steps, warmup, threads, use_ref=True, tail_blocks=0, source=None,
+              decode=True):
     """Mean seconds per full CPU step over `steps` timed steps after `warmup`."""
-    cpu = CpuRetrieval(w, threads, use_ref)
+    cpu = CpuRetrieval(w, threads, use_ref, tail_blocks, source, decode)
     for _ in range(warmup):
         cpu.step()
     times, stats = [], []
@@ -352,7 +392,8 @@ def run_reference(args, w):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    sec, kind, churn = cpu_steps(w, args.steps, args.warmup, threads, True)
+    sec, kind, churn = cpu_steps(w, args.steps, args.warmup, threads, True,
+                                 decode_tail(args, w), decode=not args.no_decode)
     us = sec * 1e6
     line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/step",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -391,20 +432,23 @@ class OracleCheck:
     operation of the run, plus the oracle RoPE / requantisation of sampled
     window slots from the pinned repository's bytes."""
 
-    def __init__(self, po, w, r, Ll, world, threads, dist):
+    def __init__(self, po, w, r, Ll, world, threads, dist, gen_first):
         import concurrent.futures as cf
         self.po, self.w, self.r, self.Ll, self.world, self.dist = po, w, r, Ll, world, dist
-        self.mean = r.summaries()  # [N][Ll][E]
+        # the top-k candidates: the blocks before the decode blocks
+        self.g0 = gen_first
+        self.mean = np.ascontiguousarray(r.summaries()[:gen_first])  # [g0][Ll][E]
         N = self.mean.shape[0]
         self.N = N
         self.pool = cf.ThreadPoolExecutor(max_workers=max(1, threads))
         self.parts = [ix for ix in np.array_split(np.arange(N), max(1, threads)) if len(ix)]
-        self.store = po.Store(w.block_tokens)
-        self.store.append(w.n_tokens)
+        self.store = po.Store(w.block_tokens)  # replays the run's table log from empty
         self.tie_high = bool(r.cfg.tie_higher_id)
 
-    def ids(self, q_host):
-        """Oracle selection of one step's query ([Ll][1][qdim] f16, this rank's layers)."""
+    def ids(self, q_host, n_blocks):
+        """Oracle selection of one step's query ([Ll][1][qdim] f16, this rank's
+        layers) over a store of n_blocks blocks: the top-k of the blocks before
+        the decode blocks, plus the decode blocks."""
         import torch
         po, w = self.po, self.w
         q_sum = q_host.numpy().reshape(self.Ll, -1).astype(np.float32)
@@ -424,14 +468,23 @@ class OracleCheck:
             terms = t_all.cpu().numpy().reshape(-1, self.N)
             act = a_all.cpu().numpy()
         scores = po.score_reduce(terms, act, np.ones(self.N, np.uint8))
-        return po.pick_topk(scores, w.budget_blocks, w.sink_blocks,
-                            tie_higher_id=self.tie_high)
+        ids = po.pick_topk(scores, w.budget_blocks, w.sink_blocks, tie_higher_id=self.tie_high)
+        if n_blocks > self.g0:
+            ids = np.concatenate([ids, np.arange(self.g0, n_blocks, dtype=ids.dtype)])
+        return ids
 
     def replay(self, op):
-        if op[0] == "clear":
+        """One host-table operation of the run, in the oracle's store."""
+        kind = op[0]
+        if kind == "clear":
             self.store.clear_working_set(op[1])
-            return None
-        return self.store.set_selection(op[1])
+        elif kind == "append":
+            self.store.append(op[1])
+        elif kind == "truncate":
+            self.store.truncate(op[1])
+        else:
+            return self.store.set_selection(op[1])
+        return None
 
     def summaries_exact(self):
         """Device summaries of sampled blocks against the oracle's token-order
@@ -500,6 +553,16 @@ def q8_diff(a, b):
     return int(np.abs(qa - qb).max(initial=0)), int(f16_ulps(da, db).max(initial=0))
 
 
+def decode_tail(args, w):
+    """Decode blocks at the end of the history: at most what the gen reserve
+    holds next to the loop's own decode block."""
+    if args.no_decode:
+        return 0
+    spare = w.reserve_blocks - 1 - (args.warmup + args.steps + w.block_tokens - 1) // \
+        w.block_tokens
+    return max(0, min(args.decode_tail, spare, w.n_blocks - w.budget_blocks - 1))
+
+
 def run_ours(args, w):
     import numpy as np
     import torch
@@ -522,28 +585,62 @@ def run_ours(args, w):
     Ll = w.n_layer // world
     layer0 = rank * Ll
     T = w.block_tokens
+    # decode: the newest `tail` blocks of the history are this turn's decode
+    # blocks (appended in gen mode, pinned in reserve slots), and every step
+    # appends one more decode token before its retrieval
+    decoding = not args.no_decode
+    tail = decode_tail(args, w)
+    n_dec = args.warmup + args.steps  # decode tokens of one loop
+    H0 = w.n_tokens                   # the history every loop starts from
+    quant = w.k_type != kvmret.TYPE_F16
 
     cfg = kvmret.default_config(
         n_layer=Ll, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head, block_tokens=T,
-        max_blocks=w.n_blocks, budget_blocks=w.budget_blocks, reserve_blocks=w.reserve_blocks,
-        sink_blocks=w.sink_blocks, k_type=w.k_type, v_type=w.v_type, n_rot=w.d_head,
-        freq_base=w.freq_base, pool_cache=int(args.pool_cache), device=local)
+        max_blocks=w.n_blocks + (n_dec + T - 1) // T + 1, budget_blocks=w.budget_blocks,
+        reserve_blocks=w.reserve_blocks, sink_blocks=w.sink_blocks, k_type=w.k_type,
+        v_type=w.v_type, n_rot=w.d_head, freq_base=w.freq_base,
+        pool_cache=int(args.pool_cache), device=local)
     t_setup = time.perf_counter()
     r = kvmret.Retriever(cfg)
     hist = synth.TorchHistory(w, local, layer0=layer0, n_layer=Ll)
-    chunk = 64 * T
+    table_log = []  # every host-table operation of the run, in order
+
+    def append(kc, vc, t0):
+        if quant:  # config 3: q8_0 K rows, q4_0 V rows, summaries from the f16 capture
+            r.append(kc, kvmret.quantize_f16(vc, w.v_type).view(Ll, kc.shape[1], -1),
+                     k_rows=kvmret.quantize_f16(kc, w.k_type).view(Ll, kc.shape[1], -1), pos0=t0)
+        else:
+            r.append(kc, vc, pos0=t0)
+        table_log.append(("append", int(kc.shape[1])))
+
+    g0_tok = (w.n_blocks - tail) * T
+    chunk = 64 * T  # the chunks torch_block_summaries generates, same random stream
     for t0 in range(0, w.n_tokens, chunk):
         m = min(chunk, w.n_tokens - t0)
         kc, vc = hist.chunk(t0, m)
-        if w.k_type == kvmret.TYPE_F16:
-            r.append(kc, vc, pos0=t0)
-        else:  # config 3: q8_0 K rows, q4_0 V rows, summaries from the f16 capture
-            kq = kvmret.quantize_f16(kc, w.k_type)
-            vq = kvmret.quantize_f16(vc, w.v_type)
-            r.append(kc, vq, k_rows=kq, pos0=t0)
-            del kq, vq
+        cut = min(max(g0_tok - t0, 0), m)  # tokens before the decode tail
+        if cut:
+            append(kc[:, :cut].contiguous(), vc[:, :cut].contiguous(), t0)
+        if cut < m:
+            if r.gen_first_block is None:
+                r.gen_begin()
+            append(kc[:, cut:].contiguous(), vc[:, cut:].contiguous(), t0 + cut)
         r.sync()
         del kc, vc
+    if decoding and r.gen_first_block is None:
+        r.gen_begin()
+    # the decode tokens of one loop, one [Ll][1][row] tensor set per token
+    dk, dv = hist.chunk(H0, n_dec)
+    dec = []
+    for i in range(n_dec):
+        kc = dk[:, i:i + 1].contiguous()
+        vc = dv[:, i:i + 1].contiguous()
+        if quant:
+            dec.append((kc, kvmret.quantize_f16(kc, w.k_type).view(Ll, 1, -1),
+                        kvmret.quantize_f16(vc, w.v_type).view(Ll, 1, -1)))
+        else:
+            dec.append((kc, None, vc))
+    del dk, dv
     torch.cuda.synchronize()
     t_setup = time.perf_counter() - t_setup
     link = link_gbps()
@@ -570,8 +667,11 @@ def run_ours(args, w):
         dist.all_gather_object(handles, r.exchange_export(world))
         r.exchange_import(rank, handles)
 
-    def step(q_dev):
+    def step(q_dev, d=None):
         mark("start")
+        if d is not None:  # the decode token of this step (gen mode: into its reserve slot)
+            r.append(d[0], d[2], k_rows=d[1])
+            table_log.append(("append", 1))
         r.query_reset()
         r.query_add(q_dev)
         mark("query")
@@ -595,10 +695,6 @@ def run_ours(args, w):
         r.select_apply_async()
         mark("apply_enqueued")
 
-    # every host-table operation of the run, in order (the parity pass replays
-    # them in the oracle's store)
-    table_log = []
-
     def collect():
         ids_k, st_k = r.step_collect()
         table_log.append(("sel", ids_k))
@@ -614,25 +710,24 @@ def run_ours(args, w):
     # clocks are sampled from before the warm-up until after the last timed loop
     clocks = Clocks(local)
     time.sleep(0.6)
-    # warm-up (the first step stages the whole window from the host)
     warm_q = queries(args.warmup)
-    step(warm_q[0])
-    ids0 = collect()[0]
     warm_ids = []
 
     def restart():
-        """Untimed: the start state every measured loop begins from. An empty
-        working set and pool (kvmret_clear_working_set), the first warm-up
-        step's selection staged again, then the other warm-up steps; the state
-        (window, pool contents and LRU order) is then a function of these
-        queries alone, so every loop repeats the same work."""
+        """Untimed: the start state every measured loop begins from. The
+        history cut back to its H0 tokens (the previous loop's decode tokens
+        leave), an empty working set and pool (kvmret_clear_working_set), then
+        the warm-up steps, each with its decode token (the first one stages
+        the whole window from the host); the state (history, window, pool
+        contents and LRU order) is then a function of these inputs alone, so
+        every loop repeats the same work."""
+        r.truncate(H0)
+        table_log.append(("truncate", H0))
         r.clear_working_set(drop_pool=True)
         table_log.append(("clear", True))
-        r.apply(ids0)
-        table_log.append(("sel", ids0))
         warm_ids.clear()
-        for q in warm_q[1:]:
-            step(q)
+        for j, q in enumerate(warm_q):
+            step(q, dec[j] if decoding else None)
             warm_ids.append(collect()[0])
         r.sync()
 
@@ -653,8 +748,9 @@ def run_ours(args, w):
         # waits for the host between steps. The NVTX range lets a profiler keep
         # only these launches (ncu --nvtx --nvtx-include "timed_steps/").
         torch.cuda.nvtx.range_push("timed_steps")
+        W = len(warm_q)
         for i, q in enumerate(qs):
-            step(q)
+            step(q, dec[W + i] if decoding else None)
             if i > 0:
                 ids_k, st_k = collect()
                 ids_l.append(ids_k)
@@ -733,13 +829,25 @@ def run_ours(args, w):
     # selections and per-step work are checked against the timed loop's below)
     restart()
     qd = torch.empty_like(qs[0])
+    W = len(warm_q)
+    # this loop's decode rows in pinned host memory, and their device staging
+    dec_h = [tuple(x.cpu().pin_memory() if x is not None else None for x in d)
+             for d in dec[W:]] if decoding else []
+    dec_d = tuple(torch.empty_like(x) if x is not None else None for x in dec[0]) if decoding \
+        else None
+    dec_bytes = sum(x.numel() * x.element_size() for x in dec[0] if x is not None) if decoding \
+        else 0
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e2e_stats, e2e_ids = [], []
     for i, q in enumerate(qh):
         qd.copy_(q, non_blocking=True)
-        step(qd)
+        if decoding:
+            for dst, src in zip(dec_d, dec_h[i]):
+                if dst is not None:
+                    dst.copy_(src, non_blocking=True)
+        step(qd, dec_d)
         if i > 0:
             ids_k, st_k = collect()  # the previous step's ids, read on the host
             e2e_ids.append(ids_k)
@@ -787,23 +895,24 @@ def run_ours(args, w):
     if not args.no_parity:
         po = load_oracle()
         threads = max(1, (os.cpu_count() or 1) // max(1, local_world))
-        chk = OracleCheck(po, w, r, Ll, world, threads, dist)
+        chk = OracleCheck(po, w, r, Ll, world, threads, dist, w.n_blocks - tail)
         restart()
         for op in table_log:
             chk.replay(op)
-        n_log = len(table_log)
-        oracle_warm = [chk.ids(q.cpu()) for q in warm_q]
-        ok_ids = np.array_equal(ids0, oracle_warm[0]) and all(
-            np.array_equal(a, b) for a, b in zip(warm_ids, oracle_warm[1:]))
+        nb_at = lambda j: (H0 + (j + 1 if decoding else 0) + T - 1) // T  # noqa: E731
+        oracle_warm = [chk.ids(q.cpu(), nb_at(j)) for j, q in enumerate(warm_q)]
+        ok_ids = all(np.array_equal(a, b) for a, b in zip(warm_ids, oracle_warm))
         ok_plan = ok_layout = ok_v = ok_timed = True
         k_max, k_scale_max, n_slots = 0, 0, 0
         pass_ids = []
         for i, q in enumerate(qs):
-            step(q)
+            step(q, dec[W + i] if decoding else None)
+            if decoding:
+                chk.replay(("append", 1))
             ids_d, _ = collect()
             plan = r.last_plan()
             lay, bases = r.window_layout()
-            want = chk.ids(qh[i])
+            want = chk.ids(qh[i], nb_at(W + i))
             si, so, rm, _ = chk.store.set_selection(want)
             pass_ids.append(ids_d)
             ok_ids &= bool(np.array_equal(ids_d, want))
@@ -826,7 +935,6 @@ def run_ours(args, w):
                     n_slots += 1
         summ_ok = chk.summaries_exact() if w.k_type == kvmret.TYPE_F16 else None
         chk.close()
-        del n_log
         flags = torch.tensor([ok_ids, ok_plan, ok_layout, ok_v, ok_timed, e2e_same,
                               summ_ok is not False], dtype=torch.int32, device="cuda")
         mx = torch.tensor([k_max, k_scale_max], dtype=torch.int32, device="cuda")
@@ -879,7 +987,13 @@ def run_ours(args, w):
             "config": workload_config(w),
             "setup": {"layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
                       "exchange": (args.exchange if world > 1 else None),
-                      "pool_cache": bool(args.pool_cache)},
+                      "pool_cache": bool(args.pool_cache),
+                      "decode": ({"tail_blocks": tail, "tokens_per_step": 1,
+                                  "note": "the newest tail blocks are this turn's decode "
+                                          "blocks, pinned in gen-reserve window slots "
+                                          "(kvmret_gen_begin); every step first appends "
+                                          "one decode token into its reserve slot"}
+                                 if decoding else None)},
             "roofline": {"kernel": asm_name + " (window assembly: moved slots from the HBM "
                                               "pool, fresh slots from the host repository)",
                          "bound": "hbm" if fg["asm_hbm"] / hbm >= fg["asm_link"] / link
@@ -909,7 +1023,8 @@ def run_ours(args, w):
             "other_residency": other,
             "parity": parity,
             "e2e": {"value": round(e2e_us, 1), "unit": "us/step",
-                    "h2d_bytes_per_step": int(qs[0].numel() * 2 + avg("h2d_bytes", e2e_stats)),
+                    "h2d_bytes_per_step": int(qs[0].numel() * 2 + dec_bytes +
+                                              avg("h2d_bytes", e2e_stats)),
                     # per step the readback ring returns 8 counts and the window's ids
                     "d2h_bytes_per_step": int(4 * (8 + w.budget_blocks + w.reserve_blocks)),
                     "same_steps_as_timed": e2e_same,
@@ -920,12 +1035,17 @@ def run_ours(args, w):
             "clocks": clk,
             "setup_s": round(t_setup, 1),
         }
+    summ_host = r.summaries()[:w.n_blocks] if line is not None and world == 1 else None
     r.close()
     if world > 1:
         dist.destroy_process_group()
     if line is not None and world == 1 and not args.no_cpu_baseline:
+        # the same workload on the host cores: this run's summaries and the
+        # same query sequence (a fresh generator of it)
         threads = os.cpu_count() or 1
-        sec, kind, churn = cpu_steps(w, 3, 1, threads, True)
+        qgen = synth.TorchHistory(w, local)
+        src = (summ_host, lambda: qgen.next_query().reshape(w.n_layer, -1).cpu().numpy())
+        sec, kind, churn = cpu_steps(w, 3, 1, threads, True, tail, src, decoding)
         line["cpu_baseline"] = {"value": round(sec * 1e6, 1), "unit": "us/step",
                                 "cores": threads, "kind": kind,
                                 "sample": cpu_sample_text(w, kind, 3, 1, threads),
@@ -1300,6 +1420,12 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-tail", type=int, default=64,
+                    help="blocks at the end of the history generated in this turn (decode "
+                         "blocks pinned in gen-reserve slots)")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="retrieval steps only: no decode token per step, no gen-reserve "
+                         "placement")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the untimed parity pass against the CPU oracle")
     ap.add_argument("--no-residency-variant", action="store_true",

@@ -131,6 +131,45 @@ int kvmret_append(kvmret_ctx *ctx, uint32_t pos0, uint32_t n_tok, const uint16_t
                   const void *k_rows_dev, const void *v_rows_dev);
 uint32_t kvmret_n_blocks(kvmret_ctx *ctx);
 uint32_t kvmret_n_tokens(kvmret_ctx *ctx);
+/* KvMemRuntime::truncate_to (kvmem/src/host/kvmem_runtime.cpp:94-112,
+ * KvMemStore::truncate_to kvmem/src/host/kvmem_store.cpp:207-227,
+ * RawKvStore::truncate_to kvmem/src/host/raw_kv_store.cpp:1096-1126): keep
+ * the first n_tokens tokens. Blocks past them leave the store, the HBM pool
+ * and the window; a partial last block keeps its first tokens, its f16
+ * summary rebuilt from the repository's K rows (quantised K: block
+ * boundaries only, since the repository holds no f16 K). Collects steps in
+ * flight first. */
+int kvmret_truncate(kvmret_ctx *ctx, uint32_t n_tokens);
+
+/* ---- gen-reserve placement (S15): the adapter's prepare_working_set after
+ *      a retrieval (src/adapter/llama-memory-kvmem.cpp:2314-2365: "pin the
+ *      working set and place decode tokens into gen_reserve slots"), its
+ *      alloc_slot (:1720-1741) and the cell mapping of kvmem_fill_slot_info
+ *      (src/adapter/llama-kvmem-batch.cpp:5-58). ----
+ * kvmret_gen_begin: from now on every block that kvmret_append touches (the
+ * decode blocks: the block holding the next token and those after it) gets a
+ * window slot of its own when it has none (the first free slot: it is the
+ * newest block, so that is its chronological place, RoPE base = the window's
+ * token count), plus an HBM pool slot, and each append writes its tokens into
+ * that window slot (K rotated at base + offset; quantised K dequantised,
+ * rotated, Hadamard-transformed and requantised) and into the pool slot, so
+ * attention sees them at once. These blocks stay in every later window beyond
+ * the budget (the top-k of later steps runs over the blocks before them),
+ * using the reserve_blocks slots. An append that finds no free window or pool
+ * slot fails with KVMRET_ERR_STATE ("no free GPU slot for block N") and
+ * changes nothing. An append may touch at most 64 blocks in this mode.
+ * kvmret_gen_end: the decode blocks become ordinary blocks for the next
+ * selection; reports KVMRET_ERR_STATE if a bound block was ever missing from
+ * the window when its tokens were written. */
+int kvmret_gen_begin(kvmret_ctx *ctx);
+int kvmret_gen_end(kvmret_ctx *ctx);
+/* First decode block of gen mode (0xffffffff when gen mode is off). */
+uint32_t kvmret_gen_first_block(kvmret_ctx *ctx);
+/* Cache cell of each token position [pos0, pos0 + n_tok): window slot of its
+ * block * block_tokens + offset in the block, -1 when the block is not in the
+ * window (kvmem_fill_slot_info, src/adapter/llama-kvmem-batch.cpp:5-58).
+ * Waits for the context stream. */
+int kvmret_cells(kvmret_ctx *ctx, uint32_t pos0, uint32_t n_tok, int32_t *cells_out);
 /* Summaries in the order the reference's mean_k returns them:
  * out [n_blocks][n_layer][n_head_kv * d_head] f32 (host). */
 int kvmret_get_summaries(kvmret_ctx *ctx, float *out_host);
@@ -388,6 +427,11 @@ int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_man
 /* KvMemStore::clear_working_set (kvmem/src/host/kvmem_store.cpp:897-901);
  * drop_gpu != 0 also takes every block out of the GPU tier. */
 int kvmret_table_clear_working_set(kvmret_table *t, int drop_gpu);
+/* KvMemStore::truncate_to (kvmem/src/host/kvmem_store.cpp:207-227). */
+int kvmret_table_truncate(kvmret_table *t, uint32_t n_tokens);
+/* set_block_tier(id, KvTier::GPU) (kvmem/src/host/kvmem_store.cpp:250-277):
+ * the tier change of a decode block given a reserve slot. */
+int kvmret_table_set_on_gpu(kvmret_table *t, uint32_t block_id);
 int kvmret_table_set_selection(kvmret_table *t, const uint32_t *ids, uint32_t n_ids,
                                int force_raw_refresh, uint32_t *stage_in_out,
                                uint32_t *stage_out_out, int32_t *remaps_out,

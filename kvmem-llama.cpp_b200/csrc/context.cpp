@@ -21,6 +21,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <new>
 #include <string>
 #include <vector>
@@ -112,6 +113,7 @@ uint32_t hadamard_nrot_k(uint32_t d_head) {
 constexpr int kRing = 4;          // readback slots (steps in flight before a collect)
 constexpr size_t kEventPool = 8192;
 enum { PR_SCORE = 0, PR_ASM, PR_GEMM };
+enum { OP_APPEND = 0, OP_TRUNCATE, OP_ON_GPU };  // deferred block-table operations
 
 }  // namespace
 
@@ -171,6 +173,26 @@ struct kvmret_ctx {
     std::vector<uint8_t> kept_cached;  // last kept flags uploaded
     bool kept_valid = false;
     kvmret::BlockTable table;
+    // Tokens appended so far, in call (= stream) order; launches size their
+    // block loops from it. The block table above lags: it replays each step's
+    // selection when the step is collected, so appends, truncations and tier
+    // changes made while steps are in flight reach it after the steps that
+    // were enqueued before them (deferred table operations).
+    uint32_t live_tokens = 0;
+    struct TableOp {
+        uint32_t after_step;
+        int kind;
+        uint32_t arg;
+    };
+    std::deque<TableOp> deferred;
+    uint32_t rb_step[kRing] = {};  // step number of each readback slot
+    // gen-reserve placement (kvmret_gen_begin / kvmret_gen_end): blocks from
+    // gen_first on receive their decode tokens in the window and stay in every
+    // window beyond the budget; gen_bound marks those holding a window slot
+    bool gen_on = false;
+    uint32_t gen_first = 0;
+    std::vector<uint8_t> gen_bound;
+    uint32_t *d_gen_err = nullptr;
     kvmret::Plan last_plan;
     kvmret_step_stats last_stats{};
     cudaStream_t st = nullptr;
@@ -187,6 +209,9 @@ struct kvmret_ctx {
 
     explicit kvmret_ctx(const kvmret::TableConfig &tc) : table(tc) {}
     uint32_t *rb(int slot) { return pin_rb + static_cast<size_t>(slot) * (8 + win_slots); }
+    uint32_t live_blocks() const {
+        return (live_tokens + cfg.block_tokens - 1) / cfg.block_tokens;
+    }
 };
 
 struct kvmret_table {
@@ -270,7 +295,7 @@ void free_all(kvmret_ctx *c) {
                    c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab, c->d_win_id,
                    c->d_win_base, c->d_blk_slot, c->d_slot_blk, c->d_win_ntok, c->d_blk_ntok,
                    c->d_slot_ntok, c->d_slot_used, c->d_counts, c->d_ids, c->pf_a, c->pf_b,
-                   c->pf_s, c->pf_err};
+                   c->pf_s, c->pf_err, c->d_gen_err};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
@@ -406,6 +431,8 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c, DeviceScope &ds) {
     TRY(dmalloc(&c->d_slot_used, P * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_counts, 8 * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_ids, W * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_gen_err, 16));
+    CK(cudaMemsetAsync(c->d_gen_err, 0, 16, c->st));
     CK(cudaMemsetAsync(c->summ, 0, L * c->E * c->ncap * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->tail_sum, 0, 2 * L * c->E * sizeof(float), c->st));
     CK(cudaMemsetAsync(c->q_sum, 0, L * c->qdim * sizeof(float), c->st));
@@ -429,8 +456,31 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c, DeviceScope &ds) {
     TRY(hmalloc(&c->pin_flags, c->ncap, cudaHostAllocDefault));
     TRY(hmalloc(&c->pin_rb, kRing * (8 + W) * sizeof(uint32_t), cudaHostAllocDefault));
     c->q_count.assign(L, 0);
+    c->gen_bound.assign(c->ncap, 0);
     CK(cudaStreamSynchronize(c->st));
     return KVMRET_OK;
+}
+
+void apply_table_op(kvmret_ctx *c, int kind, uint32_t arg) {
+    if (kind == OP_APPEND) c->table.append(arg);
+    else if (kind == OP_TRUNCATE) c->table.truncate(arg);
+    else c->table.set_on_gpu(arg);
+}
+
+// A block-table operation in stream order: applied now when no step is in
+// flight, else after the newest enqueued step has been collected.
+void table_op(kvmret_ctx *c, int kind, uint32_t arg) {
+    if (c->rb_pending == 0) apply_table_op(c, kind, arg);
+    else c->deferred.push_back({c->step, kind, arg});
+}
+
+void apply_deferred(kvmret_ctx *c, uint32_t upto_step) {
+    while (!c->deferred.empty() &&
+           static_cast<int32_t>(c->deferred.front().after_step - upto_step) <= 0) {
+        const auto op = c->deferred.front();
+        c->deferred.pop_front();
+        apply_table_op(c, op.kind, op.arg);
+    }
 }
 
 // Readback of the oldest uncollected step: wait for it, replay its selection
@@ -441,9 +491,13 @@ int collect_one(kvmret_ctx *c, uint32_t *ids_out, uint32_t *n_out) {
     const uint32_t *r = c->rb(slot);
     const uint32_t n_moved = r[0], n_fresh = r[1], n_sel = r[2], err = r[4];
     --c->rb_pending;
-    if (err) return fail(KVMRET_ERR_STATE, "device plan error 0x%x (window or pool too small)", err);
+    if (err) {
+        apply_deferred(c, c->rb_step[slot]);
+        return fail(KVMRET_ERR_STATE, "device plan error 0x%x (window or pool too small)", err);
+    }
     const uint32_t *ids = r + 8;
     c->last_plan = c->table.set_selection(ids, n_sel, false);
+    apply_deferred(c, c->rb_step[slot]);
     kvmret_step_stats &s = c->last_stats;
     std::memset(&s, 0, sizeof(s));
     s.n_selected = n_sel;
@@ -477,7 +531,7 @@ int plan_and_assemble(kvmret_ctx *c) {
     kvmret::PlanArgs pa{};
     pa.sel = c->sel_dev;
     pa.blk_ntok = c->d_blk_ntok;
-    pa.n_blocks = c->table.n_blocks();
+    pa.n_blocks = c->live_blocks();
     pa.win_slots = c->win_slots;
     pa.pool_slots = c->pool_slots;
     pa.step = c->step;
@@ -517,6 +571,7 @@ int plan_and_assemble(kvmret_ctx *c) {
     // the plan's counts and ids go back to the host after the assembly, so the
     // two small copies do not sit between the plan and the assembly
     const int slot = c->rb_head;
+    c->rb_step[slot] = c->step;
     uint32_t *r = c->rb(slot);
     CK(cudaMemcpyAsync(r, c->d_counts, 8 * sizeof(uint32_t), cudaMemcpyDeviceToHost, c->st));
     CK(cudaMemcpyAsync(r + 8, c->d_ids, c->win_slots * sizeof(uint32_t), cudaMemcpyDeviceToHost,
@@ -532,9 +587,13 @@ int plan_and_assemble(kvmret_ctx *c) {
 int upload_kept(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint32_t *need) {
     std::vector<uint8_t> kept;
     uint32_t kept_count = 0;
-    *need = c->table.keep(mandatory, n_mand, kept, kept_count);
+    const uint32_t n = c->live_blocks();
+    // in gen mode the decode blocks from gen_first on are kept beyond the
+    // budget; the top-k runs over the blocks before them
+    const uint32_t g0 = (c->gen_on && c->gen_first < n) ? c->gen_first : n;
+    *need = c->table.keep(g0, mandatory, n_mand, kept, kept_count);
+    kept.resize(n, 1);
     if (!c->kept_valid || kept != c->kept_cached) {
-        const uint32_t n = c->table.n_blocks();
         CK(cudaStreamSynchronize(c->st));  // the staging buffer may still feed an earlier copy
         std::copy(kept.begin(), kept.begin() + n, c->pin_flags);
         CK(cudaMemcpyAsync(c->kept_dev, c->pin_flags, n, cudaMemcpyHostToDevice, c->st));
@@ -547,7 +606,7 @@ int upload_kept(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint3
 int select_device(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
     uint32_t need = 0;
     TRY(upload_kept(c, mandatory, n_mand, &need));
-    const uint32_t n = c->table.n_blocks();
+    const uint32_t n = c->live_blocks();
     if (need > 0) {
         CK(kvmret::launch_select(c->scores, c->kept_dev, n, need, c->cfg.tie_higher_id,
                                  c->sel_dev, c->st));
@@ -582,7 +641,7 @@ int score_layers_impl(kvmret_ctx *c, double *out) {
         c->prof.launches += 1;
         c->q_dirty = false;
     }
-    const uint32_t n = c->table.n_blocks();
+    const uint32_t n = c->live_blocks();
     const int pr = prof_begin(c, c->st, PR_SCORE);
     CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, dst, c->cfg.n_layer,
                             c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st, c->cstride));
@@ -595,7 +654,7 @@ int score_layers_impl(kvmret_ctx *c, double *out) {
 
 int reduce_impl(kvmret_ctx *c, const double *rows, uint32_t n_layer_all, const uint8_t *active) {
     CK(kvmret::launch_reduce(rows, active, n_layer_all, c->cstride, c->has_block,
-                             c->table.n_blocks(), c->scores, c->st));
+                             c->live_blocks(), c->scores, c->st));
     c->prof.launches += 1;
     return KVMRET_OK;
 }
@@ -621,7 +680,7 @@ int preview_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint
                  uint32_t *n_out) {
     if (!n_out) return fail(KVMRET_ERR_ARG, "n_out is NULL");
     TRY(select_device(c, mandatory, n_mand));
-    const uint32_t n = c->table.n_blocks();
+    const uint32_t n = c->live_blocks();
     CK(cudaMemcpyAsync(c->pin_flags, c->sel_dev, n, cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
     c->kept_valid = false;  // the staging buffer now holds the selection
@@ -637,7 +696,7 @@ int preview_impl(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand, uint
 
 int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_stats *stats) {
     TRY(drain(c));
-    const uint32_t nb = c->table.n_blocks();
+    const uint32_t nb = c->live_blocks();
     std::vector<uint8_t> flags(c->ncap, 0);
     uint32_t uniq = 0;
     for (uint32_t i = 0; i < n_ids; ++i)
@@ -645,6 +704,13 @@ int apply_impl(kvmret_ctx *c, const uint32_t *ids, uint32_t n_ids, kvmret_step_s
             flags[ids[i]] = 1;
             ++uniq;
         }
+    // in gen mode the decode blocks stay in every window
+    if (c->gen_on)
+        for (uint32_t b = c->gen_first; b < nb; ++b)
+            if (!flags[b]) {
+                flags[b] = 1;
+                ++uniq;
+            }
     if (uniq > c->win_slots)
         return fail(KVMRET_ERR_ARG, "selection of %u blocks exceeds %u window slots", uniq,
                     c->win_slots);
@@ -741,32 +807,13 @@ int kvmret_sync(kvmret_ctx *c) {
 void *kvmret_repo_host(kvmret_ctx *c) { return c ? c->repo_host : nullptr; }
 uint64_t kvmret_repo_unit_bytes(kvmret_ctx *c) { return c ? c->unit : 0; }
 uint64_t kvmret_repo_k_bytes(kvmret_ctx *c) { return c ? c->unit_k : 0; }
-uint32_t kvmret_n_blocks(kvmret_ctx *c) { return c ? c->table.n_blocks() : 0; }
-uint32_t kvmret_n_tokens(kvmret_ctx *c) { return c ? c->table.n_tokens() : 0; }
+uint32_t kvmret_n_blocks(kvmret_ctx *c) { return c ? c->live_blocks() : 0; }
+uint32_t kvmret_n_tokens(kvmret_ctx *c) { return c ? c->live_tokens : 0; }
 
-int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *k_cap,
-                  const void *k_rows, const void *v_rows) {
-    NEED_CTX(c);
-    if (pos0 != c->table.n_tokens())
-        return fail(KVMRET_ERR_ARG, "append at %u, store holds %u tokens", pos0,
-                    c->table.n_tokens());
-    if (n_tok == 0) return KVMRET_OK;
-    const uint64_t cap = static_cast<uint64_t>(c->cfg.max_blocks) * c->cfg.block_tokens;
-    if (static_cast<uint64_t>(pos0) + n_tok > cap)
-        return fail(KVMRET_ERR_ARG, "append of %u tokens exceeds capacity %llu", n_tok,
-                    (unsigned long long)cap);
-    if (!k_cap || !v_rows) return fail(KVMRET_ERR_ARG, "k_cap and v_rows are required");
-    if (!k_rows) {
-        if (c->cfg.k_type != KVMRET_TYPE_F16)
-            return fail(KVMRET_ERR_ARG, "k_rows required for quantised K");
-        k_rows = k_cap;
-    }
+namespace {
+
+kvmret::AppendArgs append_args(kvmret_ctx *c) {
     kvmret::AppendArgs a{};
-    a.k_cap = k_cap;
-    a.k_rows = static_cast<const uint8_t *>(k_rows);
-    a.v_rows = static_cast<const uint8_t *>(v_rows);
-    a.pos0 = pos0;
-    a.n_tok = n_tok;
     a.n_layer = c->cfg.n_layer;
     a.n_head_kv = c->cfg.n_head_kv;
     a.d_head = c->cfg.d_head;
@@ -781,19 +828,284 @@ int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *
     a.tail_sum = c->tail_sum;
     a.has_block = c->has_block;
     a.repo_dev = c->repo_dev;
+    return a;
+}
+
+// Gen mode, before an append of tokens [pos0, pos0 + n_tok): every touched
+// block without a window slot gets one (prepare_working_set's alloc_slot for
+// incoming blocks, llama-memory-kvmem.cpp:2349-2365). The reference's pool
+// of GPU slots is budget + gen_reserve; here a bound block takes the first
+// free window slot (it is the newest block, so that is its chronological
+// place; its RoPE base is the window's token count) and an HBM pool slot (a
+// free one, else the least recently used pooled block outside the window).
+// With no free window or pool slot the append fails before anything is
+// enqueued ("no free GPU slot", as the reference reports and then truncates
+// the store back). Fills the write list of the touched blocks.
+int gen_prepare(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, kvmret::GenWrite &gw) {
+    const uint32_t T = c->cfg.block_tokens;
+    const uint32_t b_lo = pos0 / T, b_hi = (pos0 + n_tok - 1) / T;
+    if (b_hi - b_lo + 1 > static_cast<uint32_t>(kvmret::kMaxGenSegs))
+        return fail(KVMRET_ERR_ARG, "gen mode: an append may touch at most %d blocks (%u tokens)",
+                    kvmret::kMaxGenSegs, (kvmret::kMaxGenSegs - 1) * T);
+    std::vector<uint32_t> rebuild_lo(b_hi - b_lo + 1, ~0u);
+    bool need = false;
+    for (uint32_t b = b_lo; b <= b_hi; ++b) need |= !c->gen_bound[b];
+    if (need) {
+        const uint32_t W = c->win_slots, P = c->pool_slots;
+        std::vector<int32_t> win_id(W), win_base(W), slot_blk(P), blk_slot(b_hi - b_lo + 1);
+        std::vector<uint32_t> win_ntok(W), slot_used(P);
+        CK(cudaStreamSynchronize(c->st));
+        CK(cudaMemcpy(win_id.data(), c->d_win_id, W * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(win_base.data(), c->d_win_base, W * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(win_ntok.data(), c->d_win_ntok, W * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(slot_blk.data(), c->d_slot_blk, P * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(slot_used.data(), c->d_slot_used, P * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(blk_slot.data(), c->d_blk_slot + b_lo, blk_slot.size() * 4,
+                      cudaMemcpyDeviceToHost));
+        std::vector<uint8_t> in_win(c->ncap, 0);
+        for (int32_t id : win_id)
+            if (id >= 0 && static_cast<uint32_t>(id) < c->ncap) in_win[id] = 1;
+        kvmret::GenBinds gb{};
+        gb.step = c->step;
+        for (uint32_t b = b_lo; b <= b_hi; ++b) {
+            if (c->gen_bound[b]) continue;
+            const uint32_t n_exist = pos0 > b * T ? std::min(T, pos0 - b * T) : 0;
+            uint32_t ws = 0;
+            int32_t base = 0;
+            if (in_win[b]) {
+                while (win_id[ws] != static_cast<int32_t>(b)) ++ws;
+                // a window slot holding all the block's rows needs nothing;
+                // one left behind by appends made outside gen mode is
+                // rebuilt in place from the repository's rows
+                if (win_ntok[ws] == n_exist) continue;
+                base = win_base[ws];
+            } else {
+                while (ws < W && win_id[ws] >= 0) ++ws;
+                if (ws == W)
+                    return fail(KVMRET_ERR_STATE,
+                                "no free GPU slot for block %u (all %u window slots hold blocks)",
+                                b, W);
+                for (uint32_t i = 0; i < ws; ++i) base += static_cast<int32_t>(win_ntok[i]);
+            }
+            int32_t ps = blk_slot[b - b_lo], evict = -1;
+            if (ps < 0) {
+                for (uint32_t k = 0; k < P && ps < 0; ++k)
+                    if (slot_blk[k] < 0) ps = static_cast<int32_t>(k);
+            }
+            if (ps < 0) {  // least recently used pooled block outside the window
+                for (uint32_t k = 0; k < P; ++k) {
+                    const int32_t o = slot_blk[k];
+                    if (o < 0 || in_win[o]) continue;
+                    if (ps < 0 || slot_used[k] < slot_used[ps]) ps = static_cast<int32_t>(k);
+                }
+                if (ps < 0)
+                    return fail(KVMRET_ERR_STATE,
+                                "no free GPU slot for block %u (all %u pool slots hold window "
+                                "blocks)", b, P);
+                evict = slot_blk[ps];
+            }
+            kvmret::GenBind &gbi = gb.b[gb.n++];
+            gbi.block = b;
+            gbi.win_slot = ws;
+            gbi.pool_slot = static_cast<uint32_t>(ps);
+            gbi.n_exist = n_exist;
+            gbi.base = base;
+            gbi.evict_block = evict;
+            // host mirrors for the next binding of this append: the block
+            // fills up to its final token count before the next one starts
+            win_id[ws] = static_cast<int32_t>(b);
+            win_ntok[ws] = std::min(T, pos0 + n_tok - b * T);
+            slot_blk[ps] = static_cast<int32_t>(b);
+            in_win[b] = 1;
+            rebuild_lo[b - b_lo] = 0;
+        }
+        // enqueue: the existing rows of partial blocks into their pool slots,
+        // then the bindings
+        for (uint32_t i = 0; i < gb.n; ++i)
+            if (gb.b[i].n_exist)
+                CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(gb.b[i].pool_slot) * c->slot_bytes,
+                                   c->repo_host + static_cast<uint64_t>(gb.b[i].block) * c->slot_bytes,
+                                   c->slot_bytes, cudaMemcpyHostToDevice, c->st));
+        gb.win_id = c->d_win_id;
+        gb.win_base = c->d_win_base;
+        gb.win_ntok = c->d_win_ntok;
+        gb.blk_slot = c->d_blk_slot;
+        gb.slot_blk = c->d_slot_blk;
+        gb.slot_ntok = c->d_slot_ntok;
+        gb.slot_used = c->d_slot_used;
+        CK(kvmret::launch_gen_bind(gb, c->st));
+        c->prof.launches += gb.n ? 1 : 0;
+        for (uint32_t i = 0; i < gb.n; ++i) table_op(c, OP_ON_GPU, gb.b[i].block);
+        for (uint32_t b = b_lo; b <= b_hi; ++b) c->gen_bound[b] = 1;
+    }
+    gw.n_seg = 0;
+    for (uint32_t b = b_lo; b <= b_hi; ++b) {
+        kvmret::GenSeg &sg = gw.seg[gw.n_seg++];
+        sg.block = b;
+        sg.new_lo = std::max(pos0, b * T) - b * T;
+        sg.new_hi = std::min(pos0 + n_tok, (b + 1) * T) - b * T;
+        sg.rebuild_lo = rebuild_lo[b - b_lo] == 0 ? 0 : sg.new_lo;
+        sg.tok0 = b * T + sg.new_lo - pos0;
+    }
+    return KVMRET_OK;
+}
+
+}  // namespace
+
+int kvmret_append(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, const uint16_t *k_cap,
+                  const void *k_rows, const void *v_rows) {
+    NEED_CTX(c);
+    if (pos0 != c->live_tokens)
+        return fail(KVMRET_ERR_ARG, "append at %u, store holds %u tokens", pos0, c->live_tokens);
+    if (n_tok == 0) return KVMRET_OK;
+    const uint64_t cap = static_cast<uint64_t>(c->cfg.max_blocks) * c->cfg.block_tokens;
+    if (static_cast<uint64_t>(pos0) + n_tok > cap)
+        return fail(KVMRET_ERR_ARG, "append of %u tokens exceeds capacity %llu", n_tok,
+                    (unsigned long long)cap);
+    if (!k_cap || !v_rows) return fail(KVMRET_ERR_ARG, "k_cap and v_rows are required");
+    if (!k_rows) {
+        if (c->cfg.k_type != KVMRET_TYPE_F16)
+            return fail(KVMRET_ERR_ARG, "k_rows required for quantised K");
+        k_rows = k_cap;
+    }
+    kvmret::GenWrite gw{};
+    if (c->gen_on) GUARD(TRY(gen_prepare(c, pos0, n_tok, gw)));
+    kvmret::AppendArgs a = append_args(c);
+    a.k_cap = k_cap;
+    a.k_rows = static_cast<const uint8_t *>(k_rows);
+    a.v_rows = static_cast<const uint8_t *>(v_rows);
+    a.pos0 = pos0;
+    a.n_tok = n_tok;
     CK(kvmret::launch_append(a, c->st));
     c->prof.launches += 2;
+    if (c->gen_on) {  // the decode tokens into the window and the pool
+        gw.n_tok_append = n_tok;
+        gw.win_slots = c->win_slots;
+        gw.k_rows = a.k_rows;
+        gw.v_rows = a.v_rows;
+        gw.pool = c->pool;
+        gw.slot_bytes = c->slot_bytes;
+        gw.win_k = c->win_k;
+        gw.win_v = c->win_v;
+        gw.gtab = c->rope_tab;
+        gw.win_id = c->d_win_id;
+        gw.win_base = c->d_win_base;
+        gw.blk_slot = c->d_blk_slot;
+        gw.win_ntok = c->d_win_ntok;
+        gw.slot_ntok = c->d_slot_ntok;
+        gw.err = c->d_gen_err;
+        gw.g = c->geom;
+        CK(kvmret::launch_gen_write(gw, c->st));
+        c->prof.launches += 1;
+    }
     // the prefill scorer's unit summaries of the touched blocks are stale now
     c->mhat_valid = std::min(c->mhat_valid, pos0 / c->cfg.block_tokens);
-    GUARD(c->table.append(n_tok));
+    c->live_tokens += n_tok;
+    GUARD(table_op(c, OP_APPEND, n_tok));
     c->kept_valid = false;
     return KVMRET_OK;
+}
+
+int kvmret_truncate(kvmret_ctx *c, uint32_t n_tokens) {
+    NEED_CTX(c);
+    if (n_tokens > c->live_tokens)
+        return fail(KVMRET_ERR_ARG, "truncate to %u tokens, store holds %u", n_tokens,
+                    c->live_tokens);
+    if (n_tokens == c->live_tokens) return KVMRET_OK;
+    const uint32_t T = c->cfg.block_tokens;
+    const uint32_t tail = n_tokens % T;
+    if (tail && c->cfg.k_type != KVMRET_TYPE_F16)
+        return fail(KVMRET_ERR_ARG,
+                    "quantised K: truncate to a block boundary (the repository holds no f16 K "
+                    "to rebuild a partial block's summary from)");
+    GUARD(TRY(drain(c)));
+    const uint32_t nb_old = c->live_blocks();
+    const uint32_t nb_new = (n_tokens + T - 1) / T;
+    kvmret::TruncArgs ta{};
+    ta.nb_new = nb_new;
+    ta.nb_old = nb_old;
+    ta.tail_ntok = tail;
+    ta.pool_slots = c->pool_slots;
+    ta.win_slots = c->win_slots;
+    ta.has_block = c->has_block;
+    ta.blk_ntok = c->d_blk_ntok;
+    ta.blk_slot = c->d_blk_slot;
+    ta.slot_blk = c->d_slot_blk;
+    ta.slot_ntok = c->d_slot_ntok;
+    ta.win_id = c->d_win_id;
+    ta.win_ntok = c->d_win_ntok;
+    CK(kvmret::launch_truncate(ta, c->st));
+    if (tail) CK(kvmret::launch_resum(append_args(c), nb_new - 1, tail, c->st));
+    c->prof.launches += tail ? 2 : 1;
+    GUARD(c->table.truncate(n_tokens));
+    c->live_tokens = n_tokens;
+    for (uint32_t b = nb_new; b < nb_old && b < c->ncap; ++b) c->gen_bound[b] = 0;
+    if (c->gen_on) c->gen_first = std::min(c->gen_first, n_tokens / T);
+    c->mhat_valid = std::min(c->mhat_valid, n_tokens / T);
+    c->kept_valid = false;
+    CK(cudaStreamSynchronize(c->st));
+    return KVMRET_OK;
+}
+
+int kvmret_gen_begin(kvmret_ctx *c) {
+    NEED_CTX(c);
+    if (c->gen_on) return fail(KVMRET_ERR_STATE, "gen mode is already on");
+    c->gen_on = true;
+    c->gen_first = c->live_tokens / c->cfg.block_tokens;
+    std::fill(c->gen_bound.begin(), c->gen_bound.end(), 0);
+    c->kept_valid = false;
+    return KVMRET_OK;
+}
+
+int kvmret_gen_end(kvmret_ctx *c) {
+    NEED_CTX(c);
+    if (!c->gen_on) return KVMRET_OK;
+    uint32_t err = 0;
+    CK(cudaMemcpyAsync(&err, c->d_gen_err, sizeof(err), cudaMemcpyDeviceToHost, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    c->gen_on = false;
+    c->kept_valid = false;
+    if (err) {
+        CK(cudaMemset(c->d_gen_err, 0, sizeof(err)));
+        return fail(KVMRET_ERR_STATE, "a decode block bound to the window was missing from it "
+                                      "when its tokens were written");
+    }
+    return KVMRET_OK;
+}
+
+int kvmret_cells(kvmret_ctx *c, uint32_t pos0, uint32_t n_tok, int32_t *cells_out) {
+    NEED_CTX(c);
+    if (n_tok && !cells_out) return fail(KVMRET_ERR_ARG, "null output");
+    if (static_cast<uint64_t>(pos0) + n_tok > c->live_tokens)
+        return fail(KVMRET_ERR_ARG, "positions [%u, %u) beyond the %u stored tokens", pos0,
+                    pos0 + n_tok, c->live_tokens);
+    std::vector<int32_t> win_id;
+    GUARD(win_id.resize(c->win_slots));
+    CK(cudaStreamSynchronize(c->st));
+    CK(cudaMemcpy(win_id.data(), c->d_win_id, c->win_slots * 4, cudaMemcpyDeviceToHost));
+    const uint32_t T = c->cfg.block_tokens;
+    int32_t cur_b = -1, cur_s = -1;
+    for (uint32_t i = 0; i < n_tok; ++i) {
+        const uint32_t p = pos0 + i, b = p / T;
+        if (static_cast<int32_t>(b) != cur_b) {
+            cur_b = static_cast<int32_t>(b);
+            cur_s = -1;
+            for (uint32_t k = 0; k < c->win_slots; ++k)
+                if (win_id[k] == cur_b) cur_s = static_cast<int32_t>(k);
+        }
+        cells_out[i] = cur_s < 0 ? -1 : cur_s * static_cast<int32_t>(T) + static_cast<int32_t>(p - b * T);
+    }
+    return KVMRET_OK;
+}
+
+uint32_t kvmret_gen_first_block(kvmret_ctx *c) {
+    return (c && c->gen_on) ? c->gen_first : 0xffffffffu;
 }
 
 int kvmret_get_summaries(kvmret_ctx *c, float *out) {
     NEED_CTX(c);
     if (!out) return fail(KVMRET_ERR_ARG, "null output");
-    const uint32_t n = c->table.n_blocks(), L = c->cfg.n_layer, E = c->E;
+    const uint32_t n = c->live_blocks(), L = c->cfg.n_layer, E = c->E;
     std::vector<float> tmp;
     GUARD(tmp.resize(static_cast<size_t>(L) * E * c->ncap));
     CK(cudaMemcpyAsync(tmp.data(), c->summ, tmp.size() * sizeof(float), cudaMemcpyDeviceToHost,
@@ -869,7 +1181,7 @@ int kvmret_score(kvmret_ctx *c, double *scores_host) {
     TRY(score_layers_impl(c, nullptr));
     TRY(reduce_impl(c, c->contrib, c->cfg.n_layer, c->active));
     if (scores_host) {
-        CK(cudaMemcpyAsync(scores_host, c->scores, c->table.n_blocks() * sizeof(double),
+        CK(cudaMemcpyAsync(scores_host, c->scores, c->live_blocks() * sizeof(double),
                            cudaMemcpyDeviceToHost, c->st));
         CK(cudaStreamSynchronize(c->st));
     }
@@ -955,6 +1267,8 @@ int kvmret_clear_working_set(kvmret_ctx *c, int drop_pool) {
     NEED_CTX(c);
     GUARD(TRY(drain(c)));
     GUARD(c->table.clear_working_set(drop_pool != 0));
+    // the window loses every block, decode blocks bound to it included
+    std::fill(c->gen_bound.begin(), c->gen_bound.end(), 0);
     // an empty window: every slot of the next selection is rebuilt, from the
     // pool where the block is still pooled, else from the host repository
     const size_t W = c->win_slots, P = c->pool_slots;
@@ -1216,6 +1530,18 @@ int kvmret_table_keep(kvmret_table *t, const uint32_t *mandatory, uint32_t n_man
     return KVMRET_OK;
 }
 
+int kvmret_table_truncate(kvmret_table *t, uint32_t n_tokens) {
+    if (!t) return fail(KVMRET_ERR_ARG, "null argument");
+    GUARD(t->t.truncate(n_tokens));
+    return KVMRET_OK;
+}
+
+int kvmret_table_set_on_gpu(kvmret_table *t, uint32_t block_id) {
+    if (!t) return fail(KVMRET_ERR_ARG, "null argument");
+    t->t.set_on_gpu(block_id);
+    return KVMRET_OK;
+}
+
 int kvmret_table_clear_working_set(kvmret_table *t, int drop_gpu) {
     if (!t) return fail(KVMRET_ERR_ARG, "null argument");
     GUARD(t->t.clear_working_set(drop_gpu != 0));
@@ -1281,7 +1607,7 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     if (!q || !sel || n_tok == 0 || top_k == 0)
         return fail(KVMRET_ERR_ARG, "prefill scoring needs q, sel, n_tok > 0, top_k > 0");
     const uint32_t L = c->cfg.n_layer, Hkv = c->cfg.n_head_kv, D = c->cfg.d_head;
-    const uint32_t nb = c->table.n_blocks();
+    const uint32_t nb = c->live_blocks();
     CK(cudaMemsetAsync(sel, 0, c->cfg.max_blocks, c->st));
     if (nb == 0) {
         if (n_sel_out) *n_sel_out = 0;
@@ -1547,7 +1873,7 @@ int kvmret_score_exchange(kvmret_ctx *c) {
     CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, L, c->cfg.n_head,
                             c->cfg.n_head_kv, c->cfg.d_head, c->st, local, c->cstride));
     c->q_dirty = false;
-    const uint32_t n = c->table.n_blocks();
+    const uint32_t n = c->live_blocks();
     const int prs = prof_begin(c, c->st, PR_SCORE);
     CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, local, L, c->cfg.n_head_kv,
                             c->cfg.d_head, c->ncap, n, c->st, c->cstride, &pr));

@@ -1160,6 +1160,195 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 }
 
 // ---------------------------------------------------------------------------
+// S15, gen-reserve placement (llama-memory-kvmem.cpp:2314-2365, alloc_slot
+// :1720-1741). The host chose the slots; one thread records every binding in
+// order (a binding may evict the block an earlier one displaced).
+__global__ void gen_bind_kernel(const __grid_constant__ GenBinds g) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    for (uint32_t i = 0; i < g.n; ++i) {
+        const GenBind &b = g.b[i];
+        if (b.evict_block >= 0) g.blk_slot[b.evict_block] = -1;
+        g.win_id[b.win_slot] = static_cast<int32_t>(b.block);
+        g.win_base[b.win_slot] = b.base;
+        g.win_ntok[b.win_slot] = b.n_exist;
+        g.blk_slot[b.block] = static_cast<int32_t>(b.pool_slot);
+        g.slot_blk[b.pool_slot] = static_cast<int32_t>(b.block);
+        g.slot_ntok[b.pool_slot] = b.n_exist;
+        g.slot_used[b.pool_slot] = g.step;
+    }
+}
+
+// The window and pool slots of a bound block, looked up on the device (a step
+// may have moved the block to another window slot since it was bound).
+__device__ __forceinline__ bool gen_slots(const GenWrite &a, uint32_t block, uint32_t &ws,
+                                          uint32_t &ps, int32_t &base) {
+    __shared__ int32_t s_ws;
+    if (threadIdx.x == 0) s_ws = -1;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < a.win_slots; i += blockDim.x)
+        if (a.win_id[i] == static_cast<int32_t>(block)) s_ws = static_cast<int32_t>(i);
+    __syncthreads();
+    const int32_t w = s_ws, p = a.blk_slot[block];
+    if (w < 0 || p < 0) {
+        if (threadIdx.x == 0) atomicExch(a.err, 1u);
+        return false;
+    }
+    ws = static_cast<uint32_t>(w);
+    ps = static_cast<uint32_t>(p);
+    base = a.win_base[w];
+    return true;
+}
+
+// f16 K: CTA = (layer, bound block).
+template <int D>
+__global__ void __launch_bounds__(256) gen_write_f16_kernel(const __grid_constant__ GenWrite a) {
+    constexpr uint32_t PAIRS = D / 4;
+    const AssembleGeom &g = a.g;
+    const uint32_t l = blockIdx.x;
+    const GenSeg sg = a.seg[blockIdx.y];
+    uint32_t ws, ps;
+    int32_t base;
+    if (!gen_slots(a, sg.block, ws, ps, base)) return;
+    uint8_t *pk = a.pool + static_cast<uint64_t>(ps) * a.slot_bytes + static_cast<uint64_t>(l) * g.unit;
+    uint8_t *pv = pk + g.unit_k;
+    uint8_t *wk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer +
+                  static_cast<uint64_t>(ws) * g.block_tokens * g.k_row;
+    uint8_t *wv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
+                  static_cast<uint64_t>(ws) * g.block_tokens * g.v_row;
+    if (sg.new_lo > sg.rebuild_lo) {  // rows already in the pool slot
+        const uint32_t n = sg.new_lo - sg.rebuild_lo;
+        rope_rows_f16<D, false>(pk + sg.rebuild_lo * g.k_row, wk + sg.rebuild_lo * g.k_row,
+                                a.gtab + static_cast<size_t>(base + sg.rebuild_lo) * PAIRS, n,
+                                g.n_head_kv, nullptr);
+        copy16(pv + sg.rebuild_lo * g.v_row, wv + sg.rebuild_lo * g.v_row,
+               static_cast<uint64_t>(n) * g.v_row);
+    }
+    const uint32_t n = sg.new_hi - sg.new_lo;
+    const uint64_t row0 = static_cast<uint64_t>(l) * a.n_tok_append + sg.tok0;
+    rope_rows_f16<D, true>(a.k_rows + row0 * g.k_row, wk + sg.new_lo * g.k_row,
+                           a.gtab + static_cast<size_t>(base + sg.new_lo) * PAIRS, n,
+                           g.n_head_kv, pk + sg.new_lo * g.k_row);
+    copy16_host(a.v_rows + row0 * g.v_row, wv + sg.new_lo * g.v_row, pv + sg.new_lo * g.v_row,
+                static_cast<uint64_t>(n) * g.v_row);
+    if (l == 0 && threadIdx.x == 0) {
+        a.win_ntok[ws] = sg.new_hi;
+        a.slot_ntok[ps] = sg.new_hi;
+    }
+}
+
+// Quantised K: CTA = (layer, bound block), each warp converts 16-row
+// segments in shared memory (rows from the pool below new_lo, from the caller
+// above it, the latter also stored unrotated into the pool slot).
+constexpr int kGenQWarps = 4;
+template <int D, int KT>
+__global__ void __launch_bounds__(32 * kGenQWarps) gen_write_quant_kernel(const __grid_constant__ GenWrite a) {
+    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
+    constexpr uint32_t HEAD_BYTES = (D / 32) * QBlk<KT>::bytes;
+    constexpr uint32_t RPW = SEG / HEAD_BYTES;
+    constexpr uint32_t PAIRS = D / 4;
+    __shared__ __align__(16) uint8_t sm[kGenQWarps][SEG];
+    const AssembleGeom &g = a.g;
+    const uint32_t l = blockIdx.x;
+    const GenSeg sg = a.seg[blockIdx.y];
+    uint32_t ws, ps;
+    int32_t base;
+    if (!gen_slots(a, sg.block, ws, ps, base)) return;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t kr = static_cast<uint32_t>(g.k_row), vr = static_cast<uint32_t>(g.v_row);
+    uint8_t *pk = a.pool + static_cast<uint64_t>(ps) * a.slot_bytes + static_cast<uint64_t>(l) * g.unit;
+    uint8_t *pv = pk + g.unit_k;
+    uint8_t *wk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer +
+                  static_cast<uint64_t>(ws) * g.block_tokens * g.k_row;
+    uint8_t *wv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
+                  static_cast<uint64_t>(ws) * g.block_tokens * g.v_row;
+    const uint64_t row0 = static_cast<uint64_t>(l) * a.n_tok_append + sg.tok0;
+    const uint8_t *ck = a.k_rows + row0 * kr;  // caller row of token new_lo
+    const uint32_t n_rows = (sg.new_hi - sg.rebuild_lo) * g.n_head_kv;
+    const uint32_t kbytes = (sg.new_hi - sg.rebuild_lo) * kr;
+    const uint32_t lo_bytes = (sg.new_lo - sg.rebuild_lo) * kr;  // bytes served by the pool
+    const FastDiv hkv(g.n_head_kv);
+    const float4 *tab = a.gtab + static_cast<size_t>(base + sg.rebuild_lo) * PAIRS;
+    uint8_t *buf = sm[warp];
+    for (uint32_t off = warp * SEG; off < kbytes; off += kGenQWarps * SEG) {
+        const uint32_t bytes = min(SEG, kbytes - off);
+        for (uint32_t c = lane; c < bytes / 16; c += 32) {
+            const uint32_t o = off + 16 * c;
+            uint4 v;
+            if (o < lo_bytes) {
+                v = *reinterpret_cast<const uint4 *>(pk + sg.rebuild_lo * kr + o);
+            } else {
+                v = *reinterpret_cast<const uint4 *>(ck + (o - lo_bytes));
+                *reinterpret_cast<uint4 *>(pk + sg.rebuild_lo * kr + o) = v;  // unrotated
+            }
+            *reinterpret_cast<uint4 *>(buf + 16 * c) = v;
+        }
+        __syncwarp();
+        const uint32_t row_base = off / HEAD_BYTES;
+        convert_row<D, KT>(buf, lane, min(RPW, n_rows - row_base), row_base, hkv, n_rows, tab, 0u,
+                           g.fwht_n, g.fwht_scale);
+        uint4 *dp = reinterpret_cast<uint4 *>(wk + sg.rebuild_lo * kr + off);
+        for (uint32_t c = lane; c < bytes / 16; c += 32) dp[c] = reinterpret_cast<const uint4 *>(buf)[c];
+        __syncwarp();
+    }
+    // V rows: pool part, then the caller's part (also into the pool)
+    if (sg.new_lo > sg.rebuild_lo)
+        copy16(pv + sg.rebuild_lo * vr, wv + sg.rebuild_lo * vr,
+               static_cast<uint64_t>(sg.new_lo - sg.rebuild_lo) * vr);
+    copy16_host(a.v_rows + row0 * vr, wv + sg.new_lo * vr, pv + sg.new_lo * vr,
+                static_cast<uint64_t>(sg.new_hi - sg.new_lo) * vr);
+    if (l == 0 && threadIdx.x == 0) {
+        a.win_ntok[ws] = sg.new_hi;
+        a.slot_ntok[ps] = sg.new_hi;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Truncation: the dropped blocks leave the block set, the HBM pool and the
+// window (they are the newest blocks, so they sit at the window's end).
+__global__ void __launch_bounds__(1024) truncate_kernel(const __grid_constant__ TruncArgs a) {
+    for (uint32_t b = a.nb_new + threadIdx.x; b < a.nb_old; b += blockDim.x) {
+        a.has_block[b] = 0;
+        a.blk_ntok[b] = 0;
+        a.blk_slot[b] = -1;
+    }
+    // the kept partial block: its window and pool copies hold valid rows only
+    // up to tail_ntok (later appends may bring other tokens)
+    const int32_t part = a.tail_ntok ? static_cast<int32_t>(a.nb_new) - 1 : -1;
+    for (uint32_t s = threadIdx.x; s < a.pool_slots; s += blockDim.x) {
+        if (a.slot_blk[s] >= static_cast<int32_t>(a.nb_new)) a.slot_blk[s] = -1;
+        else if (a.slot_blk[s] == part) a.slot_ntok[s] = min(a.slot_ntok[s], a.tail_ntok);
+    }
+    for (uint32_t i = threadIdx.x; i < a.win_slots; i += blockDim.x) {
+        if (a.win_id[i] >= static_cast<int32_t>(a.nb_new)) {
+            a.win_id[i] = -1;
+            a.win_ntok[i] = 0;
+        } else if (a.win_id[i] == part) {
+            a.win_ntok[i] = min(a.win_ntok[i], a.tail_ntok);
+        }
+    }
+    if (threadIdx.x == 0 && a.tail_ntok && a.nb_new) a.blk_ntok[a.nb_new - 1] = a.tail_ntok;
+}
+
+// The summary of a truncated partial f16 block from the repository's K rows
+// (the same token-order sum as append_summary_kernel; RawKvStore::truncate_to
+// recomputes it from the stored K, raw_kv_store.cpp:1096-1126). CTA = layer.
+__global__ void resum_kernel(AppendArgs a, uint32_t block, uint32_t n_tok) {
+    const uint32_t l = blockIdx.x;
+    const uint32_t E = a.n_head_kv * a.d_head;
+    const float inv = __fdiv_rn(1.0f, static_cast<float>(n_tok));
+    const uint16_t *k = reinterpret_cast<const uint16_t *>(
+        a.repo_dev + (static_cast<uint64_t>(block) * a.n_layer + l) * a.unit);
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
+        float s = 0.0f;
+        for (uint32_t t = 0; t < n_tok; ++t) s = __fadd_rn(s, h2f(k[static_cast<size_t>(t) * E + e]));
+        const uint32_t h = e / a.d_head, d = e % a.d_head;
+        a.summ[((static_cast<size_t>(l) * a.n_head_kv + h) * a.d_head + d) * a.ncap + block] =
+            __fmul_rn(s, inv);
+        a.tail_sum[static_cast<size_t>(l) * E + e] = s;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // S2 + S14: summaries of the appended tokens. CTA = (layer, touched block);
 // thread e sums its channel over the block's new tokens in token order,
 // continuing the trailing partial block's running sum
@@ -1710,6 +1899,49 @@ cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st) {
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     return launch_dep(plan_kernel, dim3(1), dim3(kPlanThreads), smem, st, a);
+}
+
+cudaError_t launch_gen_bind(const GenBinds &g, cudaStream_t st) {
+    if (g.n == 0) return cudaSuccess;
+    gen_bind_kernel<<<1, 32, 0, st>>>(g);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gen_write(const GenWrite &a, cudaStream_t st) {
+    if (a.n_seg == 0) return cudaSuccess;
+    const dim3 grid(a.g.n_layer, a.n_seg);
+    const bool q8 = a.g.k_type == KVMRET_TYPE_Q8_0, q4 = a.g.k_type == KVMRET_TYPE_Q4_0;
+    const dim3 qb(32 * kGenQWarps);
+    switch (a.g.d_head) {
+    case 64:
+        if (q8) gen_write_quant_kernel<64, 0><<<grid, qb, 0, st>>>(a);
+        else if (q4) gen_write_quant_kernel<64, 1><<<grid, qb, 0, st>>>(a);
+        else gen_write_f16_kernel<64><<<grid, 256, 0, st>>>(a);
+        break;
+    case 128:
+        if (q8) gen_write_quant_kernel<128, 0><<<grid, qb, 0, st>>>(a);
+        else if (q4) gen_write_quant_kernel<128, 1><<<grid, qb, 0, st>>>(a);
+        else gen_write_f16_kernel<128><<<grid, 256, 0, st>>>(a);
+        break;
+    case 256:
+        if (q8) gen_write_quant_kernel<256, 0><<<grid, qb, 0, st>>>(a);
+        else if (q4) gen_write_quant_kernel<256, 1><<<grid, qb, 0, st>>>(a);
+        else gen_write_f16_kernel<256><<<grid, 256, 0, st>>>(a);
+        break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_truncate(const TruncArgs &a, cudaStream_t st) {
+    truncate_kernel<<<1, 1024, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_resum(const AppendArgs &a, uint32_t block, uint32_t n_tok, cudaStream_t st) {
+    if (n_tok == 0) return cudaSuccess;
+    resum_kernel<<<a.n_layer, 256, 0, st>>>(a, block, n_tok);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_copy_ops(const CopyOp *ops, int n, cudaStream_t st) {

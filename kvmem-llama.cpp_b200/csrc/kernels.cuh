@@ -170,6 +170,75 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t st);
 cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bool q8,
                             cudaStream_t st);
 
+// ---- gen-reserve placement: decode blocks bound to reserve window slots ----
+// One binding: window slot `win_slot` (RoPE base `base`) and pool slot
+// `pool_slot` now hold `block`, whose first `n_exist` rows are already in the
+// pool slot; `evict_block` (>= 0) loses its pool slot.
+struct GenBind {
+    uint32_t block, win_slot, pool_slot, n_exist;
+    int32_t base, evict_block;
+};
+constexpr int kMaxGenBinds = 64;  // = kMaxGenSegs: every touched block may bind
+struct GenBinds {
+    GenBind b[kMaxGenBinds];
+    uint32_t n, step;
+    int32_t *win_id;
+    int32_t *win_base;
+    uint32_t *win_ntok;
+    int32_t *blk_slot;
+    int32_t *slot_blk;
+    uint32_t *slot_ntok;
+    uint32_t *slot_used;
+};
+cudaError_t launch_gen_bind(const GenBinds &g, cudaStream_t st);
+
+// Rows of one bound block written into its window slot (K rotated at the
+// slot's base + row, V copied) and its pool slot (unrotated): rows
+// [rebuild_lo, new_lo) from the pool slot, rows [new_lo, new_hi) from the
+// caller's append rows starting at append token tok0.
+struct GenSeg {
+    uint32_t block, rebuild_lo, new_lo, new_hi, tok0;
+};
+constexpr int kMaxGenSegs = 64;
+struct GenWrite {
+    GenSeg seg[kMaxGenSegs];
+    uint32_t n_seg, n_tok_append, win_slots;
+    const uint8_t *k_rows;  // [n_layer][n_tok_append][k_row] unrotated K
+    const uint8_t *v_rows;  // [n_layer][n_tok_append][v_row]
+    uint8_t *pool;
+    uint64_t slot_bytes;
+    uint8_t *win_k;
+    uint8_t *win_v;
+    const float4 *gtab;     // the window's position table
+    const int32_t *win_id;
+    const int32_t *win_base;
+    const int32_t *blk_slot;
+    uint32_t *win_ntok;
+    uint32_t *slot_ntok;
+    uint32_t *err;          // set to 1 when a bound block is not in the window
+    AssembleGeom g;
+};
+static_assert(kMaxGenBinds >= kMaxGenSegs, "every block an append touches may need a binding");
+cudaError_t launch_gen_write(const GenWrite &a, cudaStream_t st);
+
+// Truncation (KvMemStore::truncate_to + RawKvStore::truncate_to): blocks
+// [nb_new, nb_old) leave the block set, the pool and the window; with
+// tail_ntok > 0 block nb_new - 1 keeps tail_ntok tokens.
+struct TruncArgs {
+    uint32_t nb_new, nb_old, tail_ntok, pool_slots, win_slots;
+    uint8_t *has_block;
+    uint32_t *blk_ntok;
+    int32_t *blk_slot;
+    int32_t *slot_blk;
+    uint32_t *slot_ntok;
+    int32_t *win_id;
+    uint32_t *win_ntok;
+};
+cudaError_t launch_truncate(const TruncArgs &a, cudaStream_t st);
+// The summary and running tail sum of a partial f16 block recomputed from the
+// repository's first n_tok unrotated K rows (token-order f32 sum, * 1/n_tok).
+cudaError_t launch_resum(const AppendArgs &a, uint32_t block, uint32_t n_tok, cudaStream_t st);
+
 struct CopyOp {
     const uint8_t *src;
     uint8_t *dst;

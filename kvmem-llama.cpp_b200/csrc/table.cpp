@@ -27,9 +27,8 @@ void BlockTable::append(uint32_t n_tok) {
 
 // pick_topk_ungrouped up to the score fill, kvmem/src/host/kvmem_store.cpp:482-534:
 // sink prefix, mandatory newest-first while budget lasts, recent suffix.
-uint32_t BlockTable::keep(const uint32_t *mandatory, uint32_t n_mandatory,
+uint32_t BlockTable::keep(uint32_t n, const uint32_t *mandatory, uint32_t n_mandatory,
                           std::vector<uint8_t> &kept, uint32_t &kept_count) const {
-    const uint32_t n = n_blocks();
     kept.assign(n, 0);
     kept_count = 0;
     if (n == 0) return 0;
@@ -125,6 +124,22 @@ Plan BlockTable::set_selection(const uint32_t *ids, uint32_t n_ids, bool force_r
     for (uint32_t id : p.stage_out) blocks_[id].on_gpu = false;
     for (uint32_t id : p.stage_in) blocks_[id].on_gpu = true;
     return p;
+}
+
+void BlockTable::truncate(uint32_t n_tokens) {
+    if (n_tokens >= total_) return;
+    while (!blocks_.empty() && blocks_.back().pos0 >= n_tokens) {
+        total_ -= blocks_.back().n_tok;
+        blocks_.pop_back();
+    }
+    if (!blocks_.empty()) {
+        Block &last = blocks_.back();
+        if (last.pos0 + last.n_tok > n_tokens) {
+            const uint32_t keep_tok = n_tokens - last.pos0;
+            total_ -= last.n_tok - keep_tok;
+            last.n_tok = keep_tok;
+        }
+    }
 }
 
 void BlockTable::clear_working_set(bool drop_gpu) {

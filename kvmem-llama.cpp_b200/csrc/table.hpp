@@ -58,11 +58,26 @@ public:
     // register_append: extend the partial tail block, then open new blocks.
     void append(uint32_t n_tok);
 
-    // Always-kept ids of a top-k selection. kept[] is resized to n_blocks.
-    // Returns the count still to be filled by score (0 if everything fits, in
-    // which case kept[] marks every block).
+    // Always-kept ids of a top-k selection over the first n blocks. kept[] is
+    // resized to n. Returns the count still to be filled by score (0 if
+    // everything fits, in which case kept[] marks every block).
+    uint32_t keep(uint32_t n, const uint32_t *mandatory, uint32_t n_mandatory,
+                  std::vector<uint8_t> &kept, uint32_t &kept_count) const;
     uint32_t keep(const uint32_t *mandatory, uint32_t n_mandatory, std::vector<uint8_t> &kept,
-                  uint32_t &kept_count) const;
+                  uint32_t &kept_count) const {
+        return keep(n_blocks(), mandatory, n_mandatory, kept, kept_count);
+    }
+
+    // KvMemStore::truncate_to (kvmem/src/host/kvmem_store.cpp:207-227): drop
+    // the blocks that start at or after n_tokens, shrink the trailing one.
+    void truncate(uint32_t n_tokens);
+
+    // set_block_tier(id, KvTier::GPU) (kvmem/src/host/kvmem_store.cpp:250-277):
+    // a block placed on the GPU outside a selection (a decode block bound to a
+    // reserve slot, src/adapter/llama-memory-kvmem.cpp:2349-2362).
+    void set_on_gpu(uint32_t id) {
+        if (id < blocks_.size()) blocks_[id].on_gpu = true;
+    }
 
     // set_selection (+ the runtime's tier effect). ids need not be sorted.
     Plan set_selection(const uint32_t *ids, uint32_t n_ids, bool force_raw_refresh);

@@ -115,6 +115,11 @@ SIGNATURES = {
     "kvmret_append": (ctypes.c_int, [_P, _U32, _U32, _P, _P, _P]),
     "kvmret_n_blocks": (_U32, [_P]),
     "kvmret_n_tokens": (_U32, [_P]),
+    "kvmret_truncate": (ctypes.c_int, [_P, _U32]),
+    "kvmret_gen_begin": (ctypes.c_int, [_P]),
+    "kvmret_gen_end": (ctypes.c_int, [_P]),
+    "kvmret_gen_first_block": (_U32, [_P]),
+    "kvmret_cells": (ctypes.c_int, [_P, _U32, _U32, _PI32]),
     "kvmret_get_summaries": (ctypes.c_int, [_P, _PF]),
     "kvmret_query_reset": (ctypes.c_int, [_P]),
     "kvmret_query_add_f16": (ctypes.c_int, [_P, _P, _U32]),
@@ -171,6 +176,8 @@ SIGNATURES = {
     "kvmret_table_n_blocks": (_U32, [_P]),
     "kvmret_table_keep": (ctypes.c_int, [_P, _PU32, _U32, _PU8, _PU32, _PU32]),
     "kvmret_table_clear_working_set": (ctypes.c_int, [_P, ctypes.c_int]),
+    "kvmret_table_truncate": (ctypes.c_int, [_P, _U32]),
+    "kvmret_table_set_on_gpu": (ctypes.c_int, [_P, _U32]),
     "kvmret_table_set_selection": (ctypes.c_int, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32,
                                                   _PI32, _PU32]),
 }
@@ -293,6 +300,29 @@ class Retriever:
             _check(lib.kvmret_append(self.h, pos0, n, k_cap.data_ptr(),
                                      None if k_rows is None else k_rows.data_ptr(),
                                      v_rows.data_ptr()))
+
+    def truncate(self, n_tokens: int):
+        """Keep the first n_tokens tokens (KvMemRuntime::truncate_to)."""
+        _check(lib.kvmret_truncate(self.h, n_tokens))
+
+    def gen_begin(self):
+        """Decode blocks from here on take reserve window slots, get their
+        tokens written into the window at append, and stay pinned."""
+        _check(lib.kvmret_gen_begin(self.h))
+
+    def gen_end(self):
+        _check(lib.kvmret_gen_end(self.h))
+
+    @property
+    def gen_first_block(self):
+        v = int(lib.kvmret_gen_first_block(self.h))
+        return None if v == 0xffffffff else v
+
+    def cells(self, pos0: int, n_tok: int) -> np.ndarray:
+        """Cache cell (window slot * block_tokens + offset, -1 if absent) per position."""
+        out = np.zeros(max(1, n_tok), np.int32)
+        _check(lib.kvmret_cells(self.h, pos0, n_tok, out.ctypes.data_as(_PI32)))
+        return out[:n_tok].copy()
 
     def summaries(self) -> np.ndarray:
         out = np.zeros((self.n_blocks, self.cfg.n_layer, self.E), np.float32)
@@ -509,6 +539,12 @@ class Table:
 
     def clear_working_set(self, drop_gpu=False):
         _check(lib.kvmret_table_clear_working_set(self.h, int(drop_gpu)))
+
+    def truncate(self, n_tokens: int):
+        _check(lib.kvmret_table_truncate(self.h, n_tokens))
+
+    def set_tier_gpu(self, block_id: int):
+        _check(lib.kvmret_table_set_on_gpu(self.h, block_id))
 
     def set_selection(self, ids, force_raw_refresh=False):
         a, ap = _u32(ids)

@@ -364,6 +364,33 @@ ORC_API uint32_t orc_store_block_tokens(void *p, uint32_t id) {
     return static_cast<OrcStore *>(p)->blocks[id].n_tokens;
 }
 
+// KvMemStore::truncate_to (kvmem/src/host/kvmem_store.cpp:207-227): pop the
+// blocks that start at or past token_pos, shrink the trailing one.
+ORC_API void orc_store_truncate(void *p, uint32_t token_pos) {
+    auto &s = *static_cast<OrcStore *>(p);
+    if (token_pos >= s.total_tokens) return;
+    while (!s.blocks.empty() && s.blocks.back().orig_pos_start >= token_pos) {
+        s.total_tokens -= s.blocks.back().n_tokens;
+        s.blocks.pop_back();
+    }
+    if (!s.blocks.empty()) {
+        OrcBlock &last = s.blocks.back();
+        if (last.orig_pos_start + last.n_tokens > token_pos) {
+            const uint32_t keep = token_pos - last.orig_pos_start;
+            s.total_tokens -= last.n_tokens - keep;
+            last.n_tokens = keep;
+        }
+    }
+}
+
+// set_block_tier(id, KvTier::GPU) (kvmem/src/host/kvmem_store.cpp:250-277),
+// as the adapter does for a decode block it gives a reserve slot
+// (src/adapter/llama-memory-kvmem.cpp:2349-2362).
+ORC_API void orc_store_set_tier_gpu(void *p, uint32_t id) {
+    auto &s = *static_cast<OrcStore *>(p);
+    if (id < s.blocks.size()) s.blocks[id].gpu = true;
+}
+
 // KvMemStore::clear_working_set (kvmem/src/host/kvmem_store.cpp:897-901): no
 // block stays in the working set; tiers and baked positions are kept.
 // drop_gpu (no reference counterpart) also moves every block off the GPU tier.

@@ -49,6 +49,8 @@ def _load_orc():
         "orc_store_append": (None, [_P, _U32]),
         "orc_store_block_count": (_U32, [_P]),
         "orc_store_clear_working_set": (None, [_P, ctypes.c_int]),
+        "orc_store_truncate": (None, [_P, _U32]),
+        "orc_store_set_tier_gpu": (None, [_P, _U32]),
         "orc_store_set_selection": (None, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32, _PI32,
                                            _PU32]),
         "orc_rope_neox": (None, [_PF, _U32, _U32, _U32, _U32, ctypes.c_int32, ctypes.c_float,
@@ -91,6 +93,8 @@ def _load_ref():
         "ref_runtime_free": (None, [_P]),
         "ref_runtime_append": (None, [_P, _U32]),
         "ref_runtime_clear_working_set": (None, [_P]),
+        "ref_runtime_truncate": (None, [_P, _U32]),
+        "ref_runtime_set_tier_gpu": (None, [_P, _U32]),
         "ref_runtime_select": (None, [_P, _PU32, _U32, ctypes.c_int, _PU32, _PU32, _PI32,
                                       _PU32]),
         "ref_mean_k_f32": (None, [_PF, _U32, _U32, _U32, _PF]),
@@ -213,6 +217,12 @@ class Store:
     def clear_working_set(self, drop_gpu=False):
         orc.orc_store_clear_working_set(self.h, int(drop_gpu))
 
+    def truncate(self, n_tokens):
+        orc.orc_store_truncate(self.h, n_tokens)
+
+    def set_tier_gpu(self, block_id):
+        orc.orc_store_set_tier_gpu(self.h, block_id)
+
     def set_selection(self, ids, force_raw_refresh=False):
         n = orc.orc_store_block_count(self.h)
         a = np.ascontiguousarray(ids, np.uint32)
@@ -247,6 +257,13 @@ class RefRuntime:
 
     def clear_working_set(self):
         ref.ref_runtime_clear_working_set(self.h)
+
+    def truncate(self, n_tokens):
+        ref.ref_runtime_truncate(self.h, n_tokens)
+        self.n = min(self.n, n_tokens)
+
+    def set_tier_gpu(self, block_id):
+        ref.ref_runtime_set_tier_gpu(self.h, block_id)
 
     def set_selection(self, ids, force_raw_refresh=False):
         nb = (self.n + self.bt - 1) // self.bt

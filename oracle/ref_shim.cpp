@@ -145,3 +145,12 @@ REF_API void ref_copy_list(const uint8_t *const *src, uint8_t *const *dst, const
                            uint32_t i0, uint32_t i1) {
     for (uint32_t i = i0; i < i1; ++i) std::memcpy(dst[i], src[i], nbytes[i]);
 }
+
+// KvMemRuntime::truncate_to and the store's set_block_tier(id, GPU), for the
+// host-table tests of truncation and decode-block placement.
+REF_API void ref_runtime_truncate(void *p, uint32_t token_pos) {
+    static_cast<RefRuntime *>(p)->rt.truncate_to(token_pos);
+}
+REF_API void ref_runtime_set_tier_gpu(void *p, uint32_t block_id) {
+    static_cast<RefRuntime *>(p)->rt.store().set_block_tier(block_id, kvmem::KvTier::GPU, -1, -1);
+}

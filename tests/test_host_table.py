@@ -143,6 +143,8 @@ if hs is not None:
         hs.tuples(hs.just("append"), hs.integers(1, 80)),
         hs.tuples(hs.just("clear"), hs.booleans()),
         hs.tuples(hs.just("select"), hs.lists(hs.integers(0, 70), max_size=40), hs.booleans()),
+        hs.tuples(hs.just("truncate"), hs.floats(0.0, 1.0)),
+        hs.tuples(hs.just("tier_gpu"), hs.integers(0, 70)),
     )
 
     @needs_ref
@@ -150,9 +152,10 @@ if hs is not None:
     @given(first=hs.integers(1, 600), ops=hs.lists(_op, min_size=1, max_size=14),
            immutable=hs.booleans())
     def test_random_op_sequences_match_oracle_and_reference(first, ops, immutable):
-        """Any sequence of appends, working-set clears (keeping the GPU tier,
-        the reference's form; or dropping it) and selections, with forced
-        refreshes: the host table, the oracle and the reference runtime give
+        """Any sequence of appends, truncations, tier changes to GPU, working-set
+        clears (keeping the GPU tier, the reference's form; or dropping it) and
+        selections, with forced refreshes: the host table, the oracle and the
+        reference runtime give
         the same plans (the reference only for clears that keep the tier)."""
         bt = 16
         t = _table(bt, 1 << 20, immutable=immutable)
@@ -161,10 +164,19 @@ if hs is not None:
         ref_ok = True
         for x in (t, o, r):
             x.append(first)
+        n_tok = first
         for op in ops:
             if op[0] == "append":
                 for x in (t, o, r):
                     x.append(op[1])
+                n_tok += op[1]
+            elif op[0] == "truncate":  # KvMemStore::truncate_to
+                n_tok = int(op[1] * n_tok)
+                for x in (t, o, r):
+                    x.truncate(n_tok)
+            elif op[0] == "tier_gpu":  # a decode block given a reserve slot
+                for x in (t, o, r):
+                    x.set_tier_gpu(op[1])
             elif op[0] == "clear":
                 t.clear_working_set(op[1])
                 o.clear_working_set(op[1])
