@@ -322,10 +322,12 @@ int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
  *      the caller (any host channel), every rank calls kvmret_exchange_import.
  *      Per step, kvmret_score_exchange replaces kvmret_score_layers + the
  *      caller's all-gather + kvmret_score_reduce: the scoring kernel writes this
- *      rank's per-layer terms into every rank's receive buffer and publishes
- *      the step; the reduction waits (at most 2 s; a timeout is reported by the
- *      next collect as plan error 0x100) for every rank's step and reduces all
- *      layers in global order. Then kvmret_select_apply_async as usual. ---- */
+ *      rank's per-layer terms into its own exchange region (two halves,
+ *      alternating by step) and publishes the step in every rank's flag array;
+ *      the reduction waits (at most 2 s; a timeout is reported by the next
+ *      collect as plan error 0x100) for every rank's step, then reads every
+ *      rank's rows from its region over NVLink and reduces all layers in global
+ *      order. Then kvmret_select_apply_async as usual. ---- */
 int kvmret_exchange_export(kvmret_ctx *ctx, uint32_t world, void *handle_out);
 int kvmret_exchange_import(kvmret_ctx *ctx, uint32_t rank, uint32_t world, const void *handles);
 int kvmret_score_exchange(kvmret_ctx *ctx);

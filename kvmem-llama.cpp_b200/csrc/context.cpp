@@ -153,8 +153,9 @@ struct kvmret_ctx {
     uint32_t *pf_err = nullptr;
     uint32_t pf_rows = 0, pf_nrows = 0, mhat_valid = 0;
     // layer-sharded exchange over peer memory (kvmret_exchange_*): one region
-    // per rank = 2 halves (step parity) of [world * n_layer][cstride] rows,
-    // then flags [kMaxRanks], counter, err; peer regions opened via CUDA IPC
+    // per rank = 2 halves (step parity) of this rank's [n_layer][cstride]
+    // rows, then flags [kMaxRanks], counter, err; peer regions opened via
+    // CUDA IPC and read by the reduction
     uint8_t *ex_region = nullptr;
     uint8_t *ex_peer[kvmret::kMaxRanks] = {};
     uint32_t ex_world = 0, ex_rank = 0, ex_step = 0;
@@ -429,7 +430,7 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c, DeviceScope &ds) {
     TRY(dmalloc(&c->d_slot_blk, P * sizeof(int32_t)));
     TRY(dmalloc(&c->d_slot_ntok, P * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_slot_used, P * sizeof(uint32_t)));
-    TRY(dmalloc(&c->d_counts, 8 * sizeof(uint32_t)));
+    TRY(dmalloc(&c->d_counts, 16 * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_ids, W * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_gen_err, 16));
     CK(cudaMemsetAsync(c->d_gen_err, 0, 16, c->st));
@@ -554,6 +555,7 @@ int plan_and_assemble(kvmret_ctx *c) {
     al.jobs = c->jobs_dev;
     al.counts = c->d_counts;
     al.work = c->d_counts + 7;
+    al.work_moved = c->d_counts + 8;
     al.fresh_offset = c->win_slots;
     al.repo = c->repo_dev;
     al.pool_w = c->pool;
@@ -1812,7 +1814,7 @@ int kvmret_exchange_export(kvmret_ctx *c, uint32_t world, void *handle_out) {
         return fail(KVMRET_ERR_ARG, "exchange needs 2..%d ranks and a handle buffer",
                     kvmret::kMaxRanks);
     if (c->ex_region) return fail(KVMRET_ERR_STATE, "exchange already set up");
-    const uint64_t half = static_cast<uint64_t>(world) * c->cfg.n_layer * c->cstride;
+    const uint64_t half = static_cast<uint64_t>(c->cfg.n_layer) * c->cstride;
     const uint64_t tail = align_up(2 * half * sizeof(double), 256);
     const uint64_t bytes = tail + 256;
     TRY(dmalloc(&c->ex_region, bytes));
@@ -1853,21 +1855,23 @@ int kvmret_score_exchange(kvmret_ctx *c) {
     const uint32_t W = c->ex_world, L = c->cfg.n_layer;
     const uint32_t step = ++c->ex_step;
     const uint64_t half_off = (step & 1u) * c->ex_half;
-    const uint64_t slice = half_off + static_cast<uint64_t>(c->ex_rank) * L * c->cstride;
-    double *local = reinterpret_cast<double *>(c->ex_region) + slice;
+    double *local = reinterpret_cast<double *>(c->ex_region) + half_off;
     kvmret::Peers pr{};
+    kvmret::RowSource rs{};
     for (uint32_t p = 0; p < W; ++p) {
-        pr.rows[p] = reinterpret_cast<double *>(c->ex_peer[p]) + slice;
         pr.flags[p] = reinterpret_cast<uint32_t *>(c->ex_peer[p] + c->ex_tail);
+        rs.base[p] = reinterpret_cast<const double *>(c->ex_peer[p]) + half_off;
     }
+    rs.l_local = L;
+    rs.n_ranks = W;
     uint32_t *tail = reinterpret_cast<uint32_t *>(c->ex_region + c->ex_tail);
     pr.counter = tail + kvmret::kMaxRanks;
     pr.n = W;
     pr.rank = c->ex_rank;
     pr.step = step;
     pr.n_layer = L;
-    // qprep writes the query flags into the local slice; the scoring kernel
-    // pushes the slice to every peer and signals
+    // qprep writes the query flags into the local rows' last column; the
+    // scoring kernel writes the terms beside them and signals every rank
     c->q_dirty = true;
     TRY(settle_query(c));
     CK(kvmret::launch_qprep(c->q_sum, c->q_count_dev, c->qv, c->nq, c->active, L, c->cfg.n_head,
@@ -1879,9 +1883,8 @@ int kvmret_score_exchange(kvmret_ctx *c) {
                             c->cfg.d_head, c->ncap, n, c->st, c->cstride, &pr));
     prof_end(c, c->st, prs);
     c->prof.score_bytes += static_cast<uint64_t>(L) * c->E * ((n + 63) / 64 * 64) * sizeof(float);
-    CK(kvmret::launch_reduce(reinterpret_cast<double *>(c->ex_region) + half_off, nullptr, W * L,
-                             c->cstride, c->has_block, n, c->scores, c->st, tail, W, step,
-                             tail + kvmret::kMaxRanks + 1));
+    CK(kvmret::launch_reduce(nullptr, nullptr, W * L, c->cstride, c->has_block, n, c->scores,
+                             c->st, tail, W, step, tail + kvmret::kMaxRanks + 1, &rs));
     c->prof.launches += 3;
     return KVMRET_OK;
 }

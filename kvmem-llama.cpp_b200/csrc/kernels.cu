@@ -114,26 +114,20 @@ __global__ void qprep_kernel(const float *__restrict__ q_sum, const uint32_t *__
 }
 
 // ---------------------------------------------------------------------------
-// Exchange signal, run by every CTA of a scoring launch at its end (its rows
-// were already stored into every peer's buffer by the epilogue). A CTA's
-// stores are ordered before its increment of the device counter (gpu-scope
-// fence); the last CTA, having observed every increment, pushes the layer
-// query flags (the rows' last column, written by qprep), fences at system
-// scope and publishes the step number in every rank's flag slot for this
-// rank with a release store. The receiver acquires the flag before it reads.
-__device__ void exchange_signal(const Peers &peers, const double *local, uint32_t cstride) {
+// Exchange signal, run by every CTA of a scoring launch at its end (its rows,
+// and the layer query flags qprep wrote in the rows' last column, are in this
+// rank's own exchange region). A CTA's stores are ordered before its increment
+// of the device counter (gpu-scope fence); the last CTA, having observed every
+// increment, fences at system scope and publishes the step number in every
+// rank's flag slot for this rank with a release store. A reader acquires the
+// flag before it reads the rows over NVLink.
+__device__ void exchange_signal(const Peers &peers) {
     __threadfence();
     __syncthreads();
     __shared__ uint32_t s_last;
     if (threadIdx.x == 0) s_last = atomicAdd(peers.counter, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
-    for (uint32_t l = threadIdx.x; l < peers.n_layer; l += blockDim.x) {
-        const double f = __ldcg(local + static_cast<size_t>(l) * cstride + cstride - 1);
-        for (uint32_t p = 0; p < peers.n; ++p)
-            if (p != peers.rank) peers.rows[p][static_cast<size_t>(l) * cstride + cstride - 1] = f;
-    }
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -147,10 +141,9 @@ __device__ void exchange_signal(const Peers &peers, const double *local, uint32_
 
 // The exchange signal alone, for a rank whose history holds no block yet: its
 // peers still wait for this rank's step flag (and its layers' query flags).
-__global__ void exchange_signal_kernel(const double *local, uint32_t cstride,
-                                       const __grid_constant__ Peers peers) {
+__global__ void exchange_signal_kernel(const __grid_constant__ Peers peers) {
     dep_wait();
-    exchange_signal(peers, local, cstride);
+    exchange_signal(peers);
 }
 
 // ---------------------------------------------------------------------------
@@ -257,23 +250,32 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
             double layer = 0.0;
             for (uint32_t h = 0; h < n_head_kv; ++h)
                 layer = __dadd_rn(layer, static_cast<double>(cosb[h * TILE + t]));
-            const double term = __ddiv_rn(layer, static_cast<double>(n_head_kv));
-            out[t] = term;
-            // exchange: the same term into this rank's slice of every peer's buffer
-            for (uint32_t p = 0; p < peers.n; ++p)
-                if (p != peers.rank)
-                    peers.rows[p][static_cast<size_t>(l) * cstride + b0 + t] = term;
+            out[t] = __ddiv_rn(layer, static_cast<double>(n_head_kv));
         }
     }
-    if (peers.n > 1) exchange_signal(peers, contrib, cstride);
+    if (peers.n > 1) exchange_signal(peers);
 }
 
 // S3 epilogue (:4189-4193): acc over layers in order, score = acc / nlay.
+// Row of global layer g: local rows (L2-coherent loads), or a rank's row in
+// its exchange region, read over NVLink with system-scope relaxed loads (after
+// the acquire of that rank's step flag).
+__device__ __forceinline__ double row_load(const double *contrib, const RowSource &rs,
+                                           uint32_t g, uint32_t stride, uint32_t col) {
+    if (rs.n_ranks == 0) return __ldcg(contrib + static_cast<size_t>(g) * stride + col);
+    const uint32_t p = g / rs.l_local;
+    const double *ptr = rs.base[p] + static_cast<size_t>(g - p * rs.l_local) * stride + col;
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
 __global__ void __launch_bounds__(128)
     reduce_kernel(const double *__restrict__ contrib, const uint8_t *__restrict__ active,
                   uint32_t n_layer, uint32_t stride, const uint8_t *__restrict__ has_block,
                   uint32_t n_blocks, double *__restrict__ scores, const uint32_t *wait_flags,
-                  uint32_t wait_n, uint32_t wait_step, uint32_t *err) {
+                  uint32_t wait_n, uint32_t wait_step, uint32_t *err,
+                  const __grid_constant__ RowSource rs) {
     dep_wait();
     if (wait_flags) {  // peer-memory exchange: every rank's rows of this step have landed
         if (threadIdx.x == 0) {
@@ -302,8 +304,7 @@ __global__ void __launch_bounds__(128)
     // the layers that carry a query, once per CTA
     extern __shared__ uint8_t s_act[];
     for (uint32_t l = threadIdx.x; l < n_layer; l += blockDim.x)
-        s_act[l] = active ? active[l]
-                          : (__ldcg(contrib + static_cast<size_t>(l) * stride + stride - 1) != 0.0);
+        s_act[l] = active ? active[l] : (row_load(contrib, rs, l, stride, stride - 1) != 0.0);
     __syncthreads();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= n_blocks) return;
@@ -318,9 +319,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
         for (uint32_t u = 0; u < 16; ++u) {  // 16 independent loads in flight
             const uint32_t l = l0 + u;
-            // L2-coherent loads: rows may have been written by peer GPUs
-            v[u] = (l < n_layer && s_act[l]) ? __ldcg(contrib + static_cast<size_t>(l) * stride + b)
-                                             : 0.0;
+            v[u] = (l < n_layer && s_act[l]) ? row_load(contrib, rs, l, stride, b) : 0.0;
         }
 #pragma unroll
         for (uint32_t u = 0; u < 16; ++u) {  // summed strictly in layer order
@@ -1160,6 +1159,306 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 }
 
 // ---------------------------------------------------------------------------
+// S13, the GPU-resident step's quantised-K assembly: persistent warps fed by
+// TMA bulk copies.
+//
+// Work: the flat sequence of items (job, layer, segment) over all fresh jobs,
+// then all moved jobs; a segment is a 16-row K segment (converted) or a
+// same-sized piece of V (copied). Warps take chunks of kQChunk items from two
+// counters the plan zeroes, so all warps finish together: the first warp of
+// every CTA takes fresh chunks (host-link reads) until none is left and then
+// moved ones, the other warps take moved chunks only, so the host-link reads
+// and the HBM moves overlap. A warp streams its
+// items through a ring of kQStages shared-memory stages: one lane resolves the
+// next item into the stage's descriptor and issues a 1-D bulk copy
+// (cp.async.bulk, no multicast, this GPU's memory only) of its bytes
+// (optionally also the cos/sin rows of the tokens a K segment spans, else
+// those come from the position table through L1), completing on the stage's
+// mbarrier, kQStages - 2 items ahead of the item being converted; the
+// converted stage goes back to the window with a bulk store. The conversion
+// (about 1,500 warp instructions per 16-row segment) bounds the kernel, not
+// the copies: the cp.async form above runs at the same speed. Fresh items (host repository, read over the host link) are read
+// with plain loads by the lanes, which also write them to their pool slot.
+// Every mbarrier wait is bounded (2 s); on a timeout the warp records error
+// 0x200 in the plan's error word, waits (bounded) for the copies it issued,
+// and stops.
+#ifndef KVMRET_Q_CHUNK
+#define KVMRET_Q_CHUNK 8
+#endif
+// 1: a K stage also receives the cos/sin rows of its tokens (else they are
+// read from the position table through L1)
+#ifndef KVMRET_Q_TAB
+#define KVMRET_Q_TAB 0
+#endif
+// 1: the GPU-resident step's quantised assembly runs the TMA-fed persistent
+// kernel below; 0: the per-job kernel above (cp.async)
+#ifndef KVMRET_Q_TMA
+#define KVMRET_Q_TMA 1
+#endif
+constexpr uint32_t kQChunk = KVMRET_Q_CHUNK;
+constexpr uint32_t kQTmaTab = KVMRET_Q_TAB ? kQTabBytes : 0;
+constexpr uint32_t kQNone = 0xffffffffu;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (i == 0) t0 = globaltimer_ns();
+        else if ((i & 63) == 0 && globaltimer_ns() - t0 > 2000000000ull) return false;
+    }
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(src), "r"(bytes)
+                 : "memory");
+}
+
+// One item of the sequence, resolved: where its bytes come from and go to.
+struct QItem {
+    const uint8_t *src;   // pool (moved) or host repository (fresh)
+    uint8_t *raw;         // fresh: its pool slot bytes, else null
+    uint8_t *dst;         // window bytes
+    const float4 *tab;    // K: cos/sin rows of the job's first token
+    uint32_t bytes, off, n_rows, is_v;
+};
+
+template <int D, int KT>
+__device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_t n_fresh,
+                                       uint32_t per_job, uint32_t nk, uint32_t n_items_job,
+                                       QItem &it) {
+    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
+    const AssembleGeom &g = a.g;
+    const bool fresh = idx < n_fresh * per_job;
+    const uint32_t rel = fresh ? idx : idx - n_fresh * per_job;
+    const uint32_t j = rel / per_job, rem = rel - j * per_job;
+    const uint32_t l = rem / n_items_job, si = rem - l * n_items_job;
+    const Job *jp = a.jobs + (fresh ? a.fresh_offset + j : j);
+    const uint32_t n_tok = jp->n_tok;
+    it.is_v = si >= nk;
+    it.off = (it.is_v ? si - nk : si) * SEG;
+    const uint32_t total = n_tok * static_cast<uint32_t>(it.is_v ? g.v_row : g.k_row);
+    if (it.off >= total) return false;  // past a partial block's rows
+    it.bytes = min(SEG, total - it.off);
+    const uint64_t part = static_cast<uint64_t>(l) * g.unit + (it.is_v ? g.unit_k : 0) + it.off;
+    const uint32_t ws = jp->win_slot;
+    it.dst = it.is_v ? a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
+                           static_cast<uint64_t>(ws) * g.block_tokens * g.v_row + it.off
+                     : a.win_k + static_cast<uint64_t>(l) * g.win_k_layer +
+                           static_cast<uint64_t>(ws) * g.block_tokens * g.k_row + it.off;
+    if (fresh) {
+        it.src = a.repo + static_cast<uint64_t>(jp->block) * a.slot_bytes + part;
+        it.raw = a.pool_w + static_cast<uint64_t>(jp->pool_slot) * a.slot_bytes + part;
+    } else {
+        it.src = a.pool + static_cast<uint64_t>(jp->pool_slot) * a.slot_bytes + part;
+        it.raw = nullptr;
+    }
+    it.tab = a.gtab + static_cast<size_t>(jp->pos0) * (D / 4);
+    it.n_rows = n_tok * g.n_head_kv;
+    return true;
+}
+
+// A stage's item, resolved once at issue time by the issuing lane.
+struct QDesc {
+    QItem it;
+    uint32_t idx;    // item index, kQNone: the sequence has ended
+    uint32_t kind;   // 0 nothing to do, 1 moved (bulk-loaded), 2 fresh (plain loads)
+    uint32_t t0;     // first token of a K segment
+    uint32_t staged; // its cos/sin rows are in the stage
+};
+
+template <int D, int KT>
+__global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
+    assemble_quant_tma_kernel(const __grid_constant__ AsmLaunch a) {
+    dep_wait();
+    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
+    constexpr uint32_t STAGE = SEG + kQTmaTab;
+    constexpr uint32_t PAIRS = D / 4, TAB_TOK = kQTmaTab / (PAIRS * sizeof(float4));
+    constexpr uint32_t HEAD_BYTES = (D / 32) * QBlk<KT>::bytes;
+    constexpr uint32_t RPW = SEG / HEAD_BYTES;
+    constexpr uint32_t S = kQStages, P = kQStages - 2;
+    static_assert(kQStages >= 3, "the ring needs a stage for the store in flight");
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const AssembleGeom &g = a.g;
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    uint8_t *wbuf = smem_raw + warp * S * STAGE;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + nwarp * S * STAGE) + warp * S;
+    QDesc *desc = reinterpret_cast<QDesc *>(smem_raw + nwarp * S * (STAGE + 8)) + warp * S;
+    const uint32_t T = g.block_tokens;
+    const uint32_t nk = (T * static_cast<uint32_t>(g.k_row) + SEG - 1) / SEG;
+    const uint32_t nv = (T * static_cast<uint32_t>(g.v_row) + SEG - 1) / SEG;
+    const uint32_t n_items_job = nk + nv, per_job = g.n_layer * n_items_job;
+    const uint32_t n_moved = a.counts[0], n_fresh = a.counts[1];
+    const uint32_t n_fi = n_fresh * per_job, n_mi = n_moved * per_job;  // items per kind
+    const FastDiv hkv(g.n_head_kv);
+    if (lane == 0) {
+        for (uint32_t s = 0; s < S; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bars + s))
+                         : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+
+    // the warp's item sequence: chunks from a work counter, one grabbed ahead;
+    // kind 0 = fresh items (counter a.work), 1 = moved items (a.work_moved)
+    uint32_t kind = warp == 0 ? 0u : 1u;
+    auto grab = [&]() {
+        uint32_t c = 0;
+        if (lane == 0) c = atomicAdd(kind == 0 ? a.work : a.work_moved, 1u);
+        return __shfl_sync(0xffffffffu, c, 0);
+    };
+    auto n_of = [&]() { return kind == 0 ? n_fi : n_mi; };
+    auto chunks = [&]() { return (n_of() + kQChunk - 1) / kQChunk; };
+    uint32_t cur_chunk = grab(), next_chunk = 0, pos = 0;
+    if (cur_chunk < chunks()) next_chunk = grab();
+    auto next_item = [&]() -> uint32_t {
+        for (;;) {
+            if (cur_chunk >= chunks()) {
+                if (kind == 1) return kQNone;
+                kind = 1;  // fresh work done: join the moves
+                cur_chunk = grab();
+                pos = 0;
+                if (cur_chunk < chunks()) next_chunk = grab();
+                continue;
+            }
+            const uint32_t idx = cur_chunk * kQChunk + pos;
+            if (pos < kQChunk && idx < n_of()) {
+                ++pos;
+                return kind == 0 ? idx : n_fi + idx;
+            }
+            cur_chunk = next_chunk;
+            pos = 0;
+            if (cur_chunk < chunks()) next_chunk = grab();
+        }
+    };
+    // issue (lane 0): resolve the next item into the stage's descriptor, arm
+    // the stage's barrier and start its bulk copies (moved items)
+    auto issue = [&](uint32_t k) {
+        const uint32_t s = k % S;
+        const uint32_t idx = next_item();
+        if (lane != 0) return;
+        QDesc &d = desc[s];
+        d.idx = idx;
+        d.kind = 0;
+        d.staged = 0;
+        d.t0 = 0;
+        if (idx == kQNone || !q_item<D, KT>(a, idx, n_fresh, per_job, nk, n_items_job, d.it))
+            return;
+        uint32_t tab_bytes = 0;
+        if (!d.it.is_v) {
+            const uint32_t row_base = d.it.off / HEAD_BYTES;
+            d.t0 = hkv.div(row_base);
+            const uint32_t nt = hkv.div(min(row_base + RPW, d.it.n_rows) - 1) - d.t0 + 1;
+            if (!d.it.raw && nt <= TAB_TOK) {
+                tab_bytes = nt * PAIRS * static_cast<uint32_t>(sizeof(float4));
+                d.staged = 1;
+            }
+        }
+        if (d.it.raw) {
+            d.kind = 2;
+            return;
+        }
+        d.kind = 1;
+        const uint32_t bar = smem_addr(bars + s);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                     "r"(d.it.bytes + tab_bytes)
+                     : "memory");
+        const uint32_t buf = smem_addr(wbuf + s * STAGE);
+        bulk_load(buf, d.it.src, d.it.bytes, bar);
+        if (tab_bytes) bulk_load(buf + SEG, d.it.tab + d.t0 * PAIRS, tab_bytes, bar);
+    };
+
+    uint32_t phase = 0;  // bit s: parity of stage s's next completion
+    uint32_t issued = 0;
+    for (; issued < P; ++issued) issue(issued);
+    __syncwarp();
+    bool failed = false;
+    uint32_t c = 0;
+    for (;; ++c) {
+        const uint32_t s = c % S;
+        const QDesc &d = desc[s];
+        if (d.idx == kQNone) break;
+        // the stage of item c + P last served item c + P - S, whose store
+        // must have read its bytes; the store of item c - 1 may still run
+        if (lane == 0)
+            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kQStages - (kQStages - 2) - 1)
+                         : "memory");
+        __syncwarp();
+        issue(issued++);
+        __syncwarp();
+        const uint32_t dk = d.kind;
+        if (dk != 0) {
+            uint8_t *buf = wbuf + s * STAGE;
+            const QItem &it = d.it;
+            if (dk == 2) {  // fresh: plain loads over the host link, also into the pool
+                const uint4 *sp = reinterpret_cast<const uint4 *>(it.src);
+                uint4 *rp = reinterpret_cast<uint4 *>(it.raw);
+                uint4 *bp = reinterpret_cast<uint4 *>(buf);
+                for (uint32_t q = lane; q < it.bytes / 16; q += 32) {
+                    const uint4 v = sp[q];
+                    bp[q] = v;
+                    rp[q] = v;
+                }
+                __syncwarp();
+            } else {
+                if (!mbar_wait_bounded(smem_addr(bars + s), (phase >> s) & 1u)) {
+                    failed = true;
+                    break;
+                }
+                phase ^= 1u << s;
+            }
+            if (!it.is_v) {
+                const uint32_t row_base = it.off / HEAD_BYTES;
+                convert_row<D, KT>(buf, lane, min(RPW, it.n_rows - row_base), row_base, hkv,
+                                   it.n_rows,
+                                   d.staged ? reinterpret_cast<const float4 *>(buf + SEG) : it.tab,
+                                   d.staged ? d.t0 : 0u, g.fwht_n, g.fwht_scale);
+            }
+            // the lanes' writes to the stage before the bulk store reads it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) bulk_store(it.dst, smem_addr(buf), it.bytes);
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    if (failed) {
+        atomicOr(const_cast<uint32_t *>(a.counts) + 4, 0x200u);
+        // wait (bounded) for the bulk loads this warp issued and has not
+        // consumed: items c .. issued - 1
+        for (uint32_t k = c; k < issued; ++k) {
+            const uint32_t s = k % S;
+            if (desc[s].kind != 1) continue;
+            mbar_wait_bounded(smem_addr(bars + s), (phase >> s) & 1u);
+            phase ^= 1u << s;
+        }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
 // S15, gen-reserve placement (llama-memory-kvmem.cpp:2314-2365, alloc_slot
 // :1720-1741). The host chose the slots; one thread records every binding in
 // order (a binding may evict the block an earlier one displaced).
@@ -1472,7 +1771,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     __syncthreads();
     if (s_err) {  // a rank's score rows never arrived: keep the window, pool and plan as they are
         if (tid == 0) {
-            for (int i = 0; i < 8; ++i) a.counts[i] = 0;
+            for (int i = 0; i < 9; ++i) a.counts[i] = 0;
             a.counts[4] = 0x100u;
         }
         return;
@@ -1644,7 +1943,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
         a.counts[4] = s_err;
         a.counts[5] = s_mtok;
         a.counts[6] = s_ftok;
-        a.counts[7] = 0;  // the assembly's work-unit counter
+        a.counts[7] = 0;  // the assembly's work counters
+        a.counts[8] = 0;
     }
 }
 
@@ -1702,6 +2002,27 @@ cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t 
 
 template <int D, int KT>
 cudaError_t launch_assemble_quant_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
+    if (a.counts && KVMRET_Q_TMA) {  // the GPU-resident step: persistent TMA-fed warps
+        constexpr uint32_t STAGE = kQSegBlocks * QBlk<KT>::bytes + kQTmaTab;
+        const size_t smem =
+            static_cast<size_t>(kQThreads / 32) * kQStages * (STAGE + 8 + sizeof(QDesc));
+        auto kfn = assemble_quant_tma_kernel<D, KT>;
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        static int per_sm = 0, n_sm = 0;
+        if (e == cudaSuccess && per_sm == 0) {
+            int dev = 0;
+            e = cudaGetDevice(&dev);
+            if (e == cudaSuccess)
+                e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kQThreads, smem);
+            if (per_sm < 1) per_sm = 1;
+        }
+        if (e != cudaSuccess) return e;
+        return launch_dep(kfn, dim3(static_cast<uint32_t>(per_sm * n_sm)), dim3(kQThreads), smem,
+                          st, a);
+    }
     const uint32_t lpc = layers_per_cta_for(a, n_jobs);
     const uint32_t groups = (a.g.n_layer + lpc - 1) / lpc;
     AsmLaunch al = a;
@@ -1787,8 +2108,7 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
     if (cstride == 0) cstride = ncap;
     if (n_blocks == 0) {
         if (peers_in && peers_in->n > 1)
-            return launch_dep(exchange_signal_kernel, dim3(1), dim3(256), 0, st,
-                              static_cast<const double *>(contrib), cstride, *peers_in);
+            return launch_dep(exchange_signal_kernel, dim3(1), dim3(256), 0, st, *peers_in);
         return cudaSuccess;
     }
     Peers none{};
@@ -1811,13 +2131,15 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st, const uint32_t *wait_flags,
-                          uint32_t wait_n, uint32_t wait_step, uint32_t *err) {
+                          uint32_t wait_n, uint32_t wait_step, uint32_t *err,
+                          const RowSource *rows) {
     // with an exchange to wait for, one CTA still takes part in the step
     // protocol when there is nothing to reduce
     if (n_blocks == 0 && !wait_flags) return cudaSuccess;
+    RowSource none{};
     return launch_dep(reduce_kernel, dim3(std::max(1u, (n_blocks + 127) / 128)), dim3(128), n_layer, st,
                       contrib, active, n_layer, stride, has_block, n_blocks, scores, wait_flags,
-                      wait_n, wait_step, err);
+                      wait_n, wait_step, err, rows ? *rows : none);
 }
 
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,

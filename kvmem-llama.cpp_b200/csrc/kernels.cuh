@@ -60,15 +60,23 @@ cudaError_t launch_qprep(const float *q_sum, const uint32_t *q_count, float *qv,
 // S3: per (layer, block) term layer_sum / n_head_kv into contrib rows of
 // cstride doubles (0 = ncap).
 // Peer-memory exchange of the layer-sharded score rows (NVLink, no
-// collective): rows[p] is this rank's row slice inside rank p's receive
-// buffer, flags[p] rank p's per-rank step flags; counter is a device word the
-// last CTA uses to know every CTA has pushed its rows.
+// collective), pull form: every rank's scoring writes its rows into its own
+// exchange region; the last CTA then publishes the step in every rank's flag
+// array (flags[p] is rank p's array, one word per rank); counter is a device
+// word the last CTA uses to know every CTA has finished. The reductions read
+// the peers' rows from their regions (RowSource).
 constexpr int kMaxRanks = 8;
 struct Peers {
-    double *rows[kMaxRanks];
     uint32_t *flags[kMaxRanks];
     uint32_t *counter;
     uint32_t n, rank, step, n_layer;
+};
+// Where the reduction finds the rows of the global layers: layer g of rank
+// g / l_local at base[g / l_local] + (g % l_local) * stride (n_ranks = 0: the
+// rows are contiguous at `contrib`).
+struct RowSource {
+    const double *base[kMaxRanks];
+    uint32_t l_local, n_ranks;
 };
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
@@ -84,7 +92,8 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
 cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t n_layer,
                           uint32_t stride, const uint8_t *has_block, uint32_t n_blocks,
                           double *scores, cudaStream_t st, const uint32_t *wait_flags = nullptr,
-                          uint32_t wait_n = 0, uint32_t wait_step = 0, uint32_t *err = nullptr);
+                          uint32_t wait_n = 0, uint32_t wait_step = 0, uint32_t *err = nullptr,
+                          const RowSource *rows = nullptr);
 
 // S6: sel[b] = kept[b] || (rank of b among non-kept blocks < need).
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
@@ -103,7 +112,9 @@ struct AsmLaunch {
     // launch's n_jobs jobs are all moved jobs). Moved jobs sit at jobs[0..),
     // fresh jobs at jobs[fresh_offset..); CTAs beyond the counts exit at once.
     const uint32_t *counts;
-    uint32_t *work;         // f16 form with counts: unit counter (zeroed by the plan kernel)
+    uint32_t *work;         // with counts: work counter (zeroed by the plan kernel); the
+                            // quantised form's fresh-item counter
+    uint32_t *work_moved;   // the quantised form's moved-item counter (zeroed by the plan)
     uint32_t fresh_offset;
     uint32_t n_groups;      // layer groups per job (set by the launcher)
     const uint8_t *repo;    // device alias of the mapped pinned repository (fresh jobs)
@@ -139,7 +150,7 @@ struct PlanArgs {
     uint32_t *slot_ntok;
     uint32_t *slot_used;
     Job *jobs;          // [2 * win_slots]: moved, then fresh at + win_slots
-    uint32_t *counts;   // [8]
+    uint32_t *counts;   // [9]: 8 read back per step, [7] and [8] work counters
     uint32_t *ids;      // [win_slots]
     uint32_t *ext_err;  // optional: a nonzero word here (read and cleared) fails the step as 0x100
 };
