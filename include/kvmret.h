@@ -332,6 +332,126 @@ int kvmret_exchange_export(kvmret_ctx *ctx, uint32_t world, void *handle_out);
 int kvmret_exchange_import(kvmret_ctx *ctx, uint32_t rank, uint32_t world, const void *handles);
 int kvmret_score_exchange(kvmret_ctx *ctx);
 
+/* ---- conversation stores: several conversations time-multiplexed on one
+ *      context's window and HBM pool (llama_kvmem_store_create / _switch /
+ *      _rows / _bytes / _destroy, src/adapter/llama-kvmem-hooks.h:107-151;
+ *      swap_conv / detach_conv / attach_conv,
+ *      src/adapter/llama-memory-kvmem.cpp:1217-1714). ----
+ * A store holds one conversation: its pinned host repository, block table,
+ * block summaries (kept in HBM while parked), running tail sum and query
+ * accumulator. kvmret_store_create makes a new empty store with the context's
+ * geometry. kvmret_store_swap collects every step in flight, then exchanges
+ * the context's active conversation with the one in `store` (by pointer:
+ * nothing is copied; on return `store` holds the outgoing conversation),
+ * empties the window and the HBM pool, and stages the incoming
+ * conversation's working set back into the window from its repository.
+ * *restaged (optional) = 1 when the incoming conversation has a working set
+ * in the window, 0 when it has none (an empty or never-selected store). A
+ * store belongs to the context's device; it may be swapped into any context
+ * made with the same configuration. */
+typedef struct kvmret_store kvmret_store;
+int kvmret_store_create(kvmret_ctx *ctx, kvmret_store **out);
+int kvmret_store_swap(kvmret_ctx *ctx, kvmret_store *store, int *restaged);
+/* Tokens held by a (parked) store, and its host repository bytes. */
+uint32_t kvmret_store_rows(const kvmret_store *store);
+uint64_t kvmret_store_bytes(const kvmret_store *store);
+void kvmret_store_destroy(kvmret_store *store);
+
+/* ---- NVMe raw tier (NvmeKvTier, kvmem/include/kvmem/nvme_kv_tier.hpp:113-430):
+ *      a file arena of fixed-size slots, each holding one block's bytes,
+ *      with positional I/O (several host threads may transfer at once). ----
+ * slot_count = total_bytes / slot_bytes (0 disables the tier). A block takes
+ * the lowest free slot; kvmret_nvme_place with evict != 0 gives a full arena's
+ * least recently used block (by write, read or touch order) up, reported in
+ * *evicted. Slot-range transfers must stay inside their slot. Span batches
+ * (one caller buffer) merge runs of full-slot spans whose file offsets and
+ * buffer ranges are both contiguous into one system call. direct_read opens a
+ * second O_DIRECT descriptor used for reads whose buffer, file offset and
+ * size are 4096-byte aligned (others read buffered); drop_page_cache advises
+ * the kernel to drop each transferred range; the backing file loses its
+ * directory entry at once unless durable. Errors: KVMRET_ERR_ARG for bad
+ * arguments, KVMRET_ERR_STATE for a failed or out-of-range transfer, a full
+ * arena or a block that is not resident. */
+typedef struct kvmret_nvme kvmret_nvme;
+typedef struct kvmret_nvme_config {
+    const char *dir;
+    const char *file_name;     /* NULL: "kvmret_nvme.bin" */
+    uint64_t total_bytes;
+    uint64_t slot_bytes;
+    int32_t durable;
+    int32_t direct_read;
+    int32_t drop_page_cache;
+    int32_t pad_;
+} kvmret_nvme_config;
+typedef struct kvmret_nvme_span {
+    int32_t slot;
+    uint32_t pad_;
+    uint64_t buffer_offset;
+    uint64_t bytes;
+} kvmret_nvme_span;
+typedef struct kvmret_nvme_stats {
+    uint64_t bytes, syscalls, direct_bytes, cache_drop_bytes, cache_drop_failures;
+} kvmret_nvme_stats;
+int kvmret_nvme_create(const kvmret_nvme_config *cfg, kvmret_nvme **out);
+void kvmret_nvme_destroy(kvmret_nvme *t);
+uint32_t kvmret_nvme_slot_count(kvmret_nvme *t);
+uint32_t kvmret_nvme_free_slots(kvmret_nvme *t);
+int kvmret_nvme_direct_reads(kvmret_nvme *t);
+int kvmret_nvme_path(kvmret_nvme *t, char *out, uint32_t cap);
+int32_t kvmret_nvme_block_slot(kvmret_nvme *t, uint32_t block);
+int32_t kvmret_nvme_lru_victim(kvmret_nvme *t);
+/* The block's slot (placing it: lowest free slot, else the LRU block's with
+ * evict != 0), -1 when the arena is full or disabled. */
+int32_t kvmret_nvme_place(kvmret_nvme *t, uint32_t block, int evict, int32_t *evicted);
+int kvmret_nvme_release(kvmret_nvme *t, uint32_t block);
+int kvmret_nvme_touch(kvmret_nvme *t, uint32_t block);
+int kvmret_nvme_write_block(kvmret_nvme *t, uint32_t block, const void *data, uint64_t bytes);
+int kvmret_nvme_read_block(kvmret_nvme *t, uint32_t block, void *data, uint64_t bytes);
+int kvmret_nvme_write_range(kvmret_nvme *t, int32_t slot, uint64_t offset, const void *data,
+                            uint64_t bytes);
+int kvmret_nvme_read_range(kvmret_nvme *t, int32_t slot, uint64_t offset, void *data,
+                           uint64_t bytes);
+int kvmret_nvme_write_spans(kvmret_nvme *t, const kvmret_nvme_span *spans, uint32_t n,
+                            const void *buffer, uint64_t buffer_bytes, kvmret_nvme_stats *stats);
+int kvmret_nvme_read_spans(kvmret_nvme *t, const kvmret_nvme_span *spans, uint32_t n,
+                           void *buffer, uint64_t buffer_bytes, kvmret_nvme_stats *stats);
+/* The context's pinned repository and a tier whose slot_bytes hold at least
+ * one repository block (all the context's layers, kvmret_repo_unit_bytes *
+ * n_layer): kvmret_repo_spill writes the blocks' repository bytes to the tier
+ * (placing them, evicting least recently used blocks of a full arena);
+ * kvmret_repo_fill reads resident blocks back into the repository (O_DIRECT
+ * when the tier has direct reads and the sizes are 4096-aligned), after every
+ * step in flight has been collected, so later steps stage them from there —
+ * the reference's NVMe -> pinned staging path
+ * (kvmem/src/host/raw_kv_store.cpp load_k_nvme / load_v_gpu_nvme). */
+int kvmret_repo_spill(kvmret_ctx *ctx, kvmret_nvme *t, const uint32_t *blocks, uint32_t n,
+                      kvmret_nvme_stats *stats);
+int kvmret_repo_fill(kvmret_ctx *ctx, kvmret_nvme *t, const uint32_t *blocks, uint32_t n,
+                     kvmret_nvme_stats *stats);
+
+/* ---- snapshot archive of a context's conversation: the reference's
+ *      RawKvStore stream (RawKvStore::snapshot_write / snapshot_read,
+ *      kvmem/src/host/raw_kv_store.cpp:1225-1287; framing and hash of
+ *      SnapshotWriter / SnapshotReader, kvmem/include/kvmem/snapshot.hpp). ----
+ * Layout (little-endian): u32 magic 0x31564b52; u32 n_layer, n_embd_k,
+ * n_embd_v, block_tokens; u64 k_row_bytes (0 = f16 K), k_gpu_row_bytes (0),
+ * v_gpu_row_bytes (the V row); u64 block count; per block a u64 section size
+ * and per layer: u32 n_tokens, k_gpu_tokens (0), v_gpu_tokens, mean_tokens;
+ * u8 k_gpu_fmt (0), v_gpu_fmt (1); then five vectors, each a u64 element count
+ * and the elements: k (block_tokens unrotated K rows, zero past n_tokens), v
+ * (empty), k_gpu (empty), v_gpu (block_tokens V rows, zero past n_tokens),
+ * k_sum (n_embd_k f32: the token-order sum of the block's K; for quantised K,
+ * whose f16 rows are not kept, a full block's summary with mean_tokens 1).
+ * The hash is 64-bit FNV-1a over every byte. kvmret_snapshot_write with
+ * buf == NULL reports the size only; it collects steps in flight first.
+ * kvmret_snapshot_read fills an empty context (no tokens) made with the same
+ * geometry: repository, summaries, running tail sum and block table; its
+ * working set starts empty. A mismatched or malformed archive is rejected
+ * with KVMRET_ERR_ARG and leaves the context empty. */
+int kvmret_snapshot_write(kvmret_ctx *ctx, void *buf, uint64_t cap, uint64_t *len,
+                          uint64_t *hash);
+int kvmret_snapshot_read(kvmret_ctx *ctx, const void *buf, uint64_t len, uint64_t *hash);
+
 /* ---- session lanes (config 5: several conversations per GPU, stepped
  *      together; the reference keeps one KvMemStore per lane,
  *      src/adapter/llama-memory-kvmem.cpp:1624-1714) ----

@@ -10,6 +10,7 @@
 // when it is collected, which keeps the reference's plan metadata (stage-in /
 // stage-out lists, remap rows) without the host ever sitting between the
 // selection and the assembly.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <sys/syscall.h>
@@ -1800,6 +1801,461 @@ int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uin
         TRY(kvmret_select_apply_async(c, nm && mandatory ? mandatory[i] : nullptr, nm));
     }
     return lanes_join(g, caller);
+}
+
+// ---------------------------------------------------------------------------
+// Conversation stores (the reference's per-conversation host bundle, swapped
+// under one GPU working set: llama_memory_kvmem::swap_conv / detach_conv /
+// attach_conv, src/adapter/llama-memory-kvmem.cpp:1217-1714; C API
+// llama_kvmem_store_create / _switch / _rows / _bytes / _destroy,
+// src/adapter/llama-kvmem-hooks.h:107-151). A store owns one conversation's
+// state: its pinned host repository, block table, block summaries (kept in
+// HBM while parked, so the scorer never waits for them), running tail sum,
+// per-block token counts and data flags, and query accumulator. The window
+// and the HBM pool belong to the context and are shared by every store.
+
+struct kvmret_store {
+    int device = 0;
+    float *summ = nullptr, *tail_sum = nullptr, *q_sum = nullptr;
+    uint32_t *q_count_dev = nullptr, *d_blk_ntok = nullptr;
+    uint8_t *has_block = nullptr;
+    int32_t *d_blk_slot = nullptr;
+    uint8_t *repo_host = nullptr, *repo_dev = nullptr;
+    uint64_t repo_bytes = 0;
+    kvmret::BlockTable table;
+    kvmret::Plan last_plan;
+    uint32_t live_tokens = 0;
+    std::vector<uint32_t> q_count;
+    bool q_reset_pending = true;
+    bool gen_on = false;
+    uint32_t gen_first = 0;
+    std::vector<uint8_t> gen_bound;
+    explicit kvmret_store(const kvmret::TableConfig &tc) : table(tc) {}
+};
+
+namespace {
+
+void store_free(kvmret_store *s) {
+    if (!s) return;
+    DeviceScope ds;
+    ds.enter(s->device);
+    void *dev[] = {s->summ, s->tail_sum, s->q_sum, s->q_count_dev, s->d_blk_ntok,
+                   s->has_block, s->d_blk_slot};
+    for (void *p : dev)
+        if (p) cudaFree(p);
+    if (s->repo_host) cudaFreeHost(s->repo_host);
+    delete s;
+}
+
+// The per-conversation members of a context and of a store change places.
+void exchange_conversation(kvmret_ctx *c, kvmret_store *s) {
+    std::swap(c->summ, s->summ);
+    std::swap(c->tail_sum, s->tail_sum);
+    std::swap(c->q_sum, s->q_sum);
+    std::swap(c->q_count_dev, s->q_count_dev);
+    std::swap(c->d_blk_ntok, s->d_blk_ntok);
+    std::swap(c->has_block, s->has_block);
+    std::swap(c->d_blk_slot, s->d_blk_slot);
+    std::swap(c->repo_host, s->repo_host);
+    std::swap(c->repo_dev, s->repo_dev);
+    std::swap(c->table, s->table);
+    std::swap(c->last_plan, s->last_plan);
+    std::swap(c->live_tokens, s->live_tokens);
+    std::swap(c->q_count, s->q_count);
+    std::swap(c->q_reset_pending, s->q_reset_pending);
+    std::swap(c->gen_on, s->gen_on);
+    std::swap(c->gen_first, s->gen_first);
+    std::swap(c->gen_bound, s->gen_bound);
+}
+
+}  // namespace
+
+int kvmret_store_create(kvmret_ctx *c, kvmret_store **out) {
+    NEED_CTX(c);
+    if (!out) return fail(KVMRET_ERR_ARG, "null output");
+    *out = nullptr;
+    kvmret_store *s = new (std::nothrow) kvmret_store(table_config(c->cfg));
+    if (!s) return fail(KVMRET_ERR_NOMEM, "out of host memory");
+    s->device = c->cfg.device;
+    const size_t L = c->cfg.n_layer, E = c->E;
+    int rc = KVMRET_OK;
+    auto run = [&]() -> int {
+        TRY(dmalloc(&s->summ, L * E * c->ncap * sizeof(float)));
+        TRY(dmalloc(&s->tail_sum, 2 * L * E * sizeof(float)));
+        TRY(dmalloc(&s->q_sum, L * c->qdim * sizeof(float)));
+        TRY(dmalloc(&s->q_count_dev, L * sizeof(uint32_t)));
+        TRY(dmalloc(&s->d_blk_ntok, c->ncap * sizeof(uint32_t)));
+        TRY(dmalloc(&s->has_block, c->ncap));
+        TRY(dmalloc(&s->d_blk_slot, c->ncap * sizeof(int32_t)));
+        CK(cudaMemsetAsync(s->summ, 0, L * E * c->ncap * sizeof(float), c->st));
+        CK(cudaMemsetAsync(s->tail_sum, 0, 2 * L * E * sizeof(float), c->st));
+        CK(cudaMemsetAsync(s->q_sum, 0, L * c->qdim * sizeof(float), c->st));
+        CK(cudaMemsetAsync(s->q_count_dev, 0, L * sizeof(uint32_t), c->st));
+        CK(cudaMemsetAsync(s->d_blk_ntok, 0, c->ncap * sizeof(uint32_t), c->st));
+        CK(cudaMemsetAsync(s->has_block, 0, c->ncap, c->st));
+        CK(cudaMemsetAsync(s->d_blk_slot, 0xff, c->ncap * sizeof(int32_t), c->st));
+        s->repo_bytes = static_cast<uint64_t>(c->cfg.max_blocks) * c->slot_bytes;
+        TRY(hmalloc_near(&s->repo_host, s->repo_bytes, cudaHostAllocMapped | cudaHostAllocPortable,
+                         gpu_numa_node(c->cfg.device)));
+        CK(cudaHostGetDevicePointer(reinterpret_cast<void **>(&s->repo_dev), s->repo_host, 0));
+        s->q_count.assign(L, 0);
+        s->gen_bound.assign(c->ncap, 0);
+        CK(cudaStreamSynchronize(c->st));
+        return KVMRET_OK;
+    };
+    try {
+        rc = run();
+    } catch (...) {
+        rc = fail(KVMRET_ERR_NOMEM, "host allocation failed");
+    }
+    if (rc != KVMRET_OK) {
+        const std::string keep = g_err;
+        store_free(s);
+        g_err = keep;
+        return rc;
+    }
+    *out = s;
+    return KVMRET_OK;
+}
+
+int kvmret_store_swap(kvmret_ctx *c, kvmret_store *s, int *restaged) {
+    NEED_CTX(c);
+    if (!s || s->device != c->cfg.device)
+        return fail(KVMRET_ERR_ARG, "store made for another device or null");
+    // quiesce: every step in flight collected, its selection replayed in the
+    // outgoing store's table, and the stream drained
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));
+    GUARD(exchange_conversation(c, s));
+    // the window and the pool held the outgoing conversation's blocks (its K
+    // and V are already in its repository, written at append): empty both
+    const size_t W = c->win_slots, P = c->pool_slots;
+    CK(cudaMemsetAsync(c->d_win_id, 0xff, W * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_win_base, 0, W * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_win_ntok, 0, W * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_blk, 0xff, P * sizeof(int32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_ntok, 0, P * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_slot_used, 0, P * sizeof(uint32_t), c->st));
+    CK(cudaMemsetAsync(c->d_blk_slot, 0xff, c->ncap * sizeof(int32_t), c->st));
+    c->kept_valid = false;
+    c->q_dirty = true;
+    c->mhat_valid = 0;
+    c->deferred.clear();
+    GUARD(std::fill(c->gen_bound.begin(), c->gen_bound.end(), 0));
+    // the incoming store's working set is staged back into the window from its
+    // repository (the reference's attach rebuilds it from host RAM)
+    std::vector<uint32_t> ws;
+    GUARD(for (uint32_t b = 0; b < c->table.n_blocks(); ++b) if (c->table.blocks()[b].in_ws)
+              ws.push_back(b));
+    if (!ws.empty()) {
+        kvmret_step_stats st{};
+        GUARD(TRY(apply_impl(c, ws.data(), static_cast<uint32_t>(ws.size()), &st)));
+    }
+    if (restaged) *restaged = ws.empty() ? 0 : 1;
+    return KVMRET_OK;
+}
+
+uint32_t kvmret_store_rows(const kvmret_store *s) { return s ? s->live_tokens : 0; }
+
+uint64_t kvmret_store_bytes(const kvmret_store *s) {
+    return s ? s->repo_bytes : 0;
+}
+
+void kvmret_store_destroy(kvmret_store *s) { store_free(s); }
+
+// ---------------------------------------------------------------------------
+// Repository blocks to and from the NVMe raw tier.
+
+int kvmret_repo_spill(kvmret_ctx *c, kvmret_nvme *t, const uint32_t *blocks, uint32_t n,
+                      kvmret_nvme_stats *stats) {
+    NEED_CTX(c);
+    if (!t || (n && !blocks)) return fail(KVMRET_ERR_ARG, "null argument");
+    if (stats) std::memset(stats, 0, sizeof(*stats));
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));  // appends write the repository from the GPU
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t b = blocks[i];
+        if (b >= c->live_blocks()) return fail(KVMRET_ERR_ARG, "block %u is not stored", b);
+        int32_t evicted = -1;
+        const int32_t slot = kvmret_nvme_place(t, b, 1, &evicted);
+        if (slot < 0) return fail(KVMRET_ERR_STATE, "NVMe tier has no slot for block %u", b);
+        kvmret_nvme_span sp{slot, 0, 0, c->slot_bytes};
+        kvmret_nvme_stats st{};
+        // one span at the block's own offset in the repository
+        sp.buffer_offset = static_cast<uint64_t>(b) * c->slot_bytes;
+        TRY(kvmret_nvme_write_spans(t, &sp, 1, c->repo_host,
+                                    static_cast<uint64_t>(c->cfg.max_blocks) * c->slot_bytes, &st));
+        if (stats) {
+            stats->bytes += st.bytes;
+            stats->syscalls += st.syscalls;
+            stats->direct_bytes += st.direct_bytes;
+            stats->cache_drop_bytes += st.cache_drop_bytes;
+            stats->cache_drop_failures += st.cache_drop_failures;
+        }
+    }
+    return KVMRET_OK;
+}
+
+int kvmret_repo_fill(kvmret_ctx *c, kvmret_nvme *t, const uint32_t *blocks, uint32_t n,
+                     kvmret_nvme_stats *stats) {
+    NEED_CTX(c);
+    if (!t || (n && !blocks)) return fail(KVMRET_ERR_ARG, "null argument");
+    if (stats) std::memset(stats, 0, sizeof(*stats));
+    // no step in flight may be reading the repository while it is rewritten
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));
+    std::vector<kvmret_nvme_span> spans;
+    GUARD(spans.reserve(n));
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t b = blocks[i];
+        if (b >= c->live_blocks()) return fail(KVMRET_ERR_ARG, "block %u is not stored", b);
+        const int32_t slot = kvmret_nvme_block_slot(t, b);
+        if (slot < 0) return fail(KVMRET_ERR_STATE, "block %u is not on the NVMe tier", b);
+        GUARD(spans.push_back({slot, 0, static_cast<uint64_t>(b) * c->slot_bytes, c->slot_bytes}));
+        kvmret_nvme_touch(t, b);
+    }
+    return kvmret_nvme_read_spans(t, spans.data(), n, c->repo_host,
+                                  static_cast<uint64_t>(c->cfg.max_blocks) * c->slot_bytes, stats);
+}
+
+// ---------------------------------------------------------------------------
+// Snapshot archive (the reference's RawKvStore stream).
+
+namespace {
+
+constexpr uint32_t kSnapMagic = 0x31564b52u;
+constexpr uint64_t kFnvOffset = 14695981039346656037ull, kFnvPrime = 1099511628211ull;
+
+struct SnapOut {
+    uint8_t *buf;
+    uint64_t cap, len = 0, hash = kFnvOffset;
+    bool hashing, overflow = false;
+    void put(const void *p, uint64_t n) {
+        const uint8_t *b = static_cast<const uint8_t *>(p);
+        if (buf) {
+            if (len + n > cap) overflow = true;
+            else std::memcpy(buf + len, b, n);
+        }
+        if (hashing)
+            for (uint64_t i = 0; i < n; ++i) hash = (hash ^ b[i]) * kFnvPrime;
+        len += n;
+    }
+    void zeros(uint64_t n) {
+        static const uint8_t z[4096] = {};
+        while (n) {
+            const uint64_t k = std::min<uint64_t>(n, sizeof(z));
+            put(z, k);
+            n -= k;
+        }
+    }
+    template <typename T> void scalar(T v) { put(&v, sizeof(v)); }
+};
+
+struct SnapIn {
+    const uint8_t *p;
+    uint64_t left, hash = kFnvOffset;
+    bool hashing;
+    bool read(void *dst, uint64_t n) {
+        if (n > left) return false;
+        if (dst) std::memcpy(dst, p, n);
+        if (hashing)
+            for (uint64_t i = 0; i < n; ++i) hash = (hash ^ p[i]) * kFnvPrime;
+        p += n;
+        left -= n;
+        return true;
+    }
+    template <typename T> bool scalar(T &v) { return read(&v, sizeof(v)); }
+};
+
+}  // namespace
+
+int kvmret_snapshot_write(kvmret_ctx *c, void *buf, uint64_t cap, uint64_t *len,
+                          uint64_t *hash) {
+    NEED_CTX(c);
+    if (!len) return fail(KVMRET_ERR_ARG, "null length");
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));
+    const uint32_t L = c->cfg.n_layer, E = c->E, T = c->cfg.block_tokens;
+    const uint32_t nb = c->live_blocks();
+    const bool f16 = c->cfg.k_type == KVMRET_TYPE_F16;
+    // quantised K keeps no f16 rows: full blocks export their summary (with
+    // mean_tokens 1), the partial newest block its running sum
+    std::vector<float> summ, tail;
+    if (!f16 && buf && nb) {
+        GUARD(summ.resize(static_cast<size_t>(L) * E * c->ncap));
+        GUARD(tail.resize(static_cast<size_t>(L) * E));
+        CK(cudaMemcpy(summ.data(), c->summ, summ.size() * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(tail.data(), c->tail_sum, tail.size() * 4, cudaMemcpyDeviceToHost));
+    }
+    SnapOut o{static_cast<uint8_t *>(buf), cap};
+    o.hashing = hash != nullptr && buf != nullptr;
+    o.scalar(kSnapMagic);
+    o.scalar(L);
+    o.scalar(E);
+    o.scalar(E);
+    o.scalar(T);
+    o.scalar<uint64_t>(f16 ? 0 : c->k_row);
+    o.scalar<uint64_t>(0);
+    o.scalar<uint64_t>(c->v_row);
+    o.scalar<uint64_t>(nb);
+    const uint64_t kb = static_cast<uint64_t>(T) * c->k_row, vb = static_cast<uint64_t>(T) * c->v_row;
+    const uint64_t layer_bytes = 4 * 4 + 2 + 5 * 8 + kb + vb + static_cast<uint64_t>(E) * 4;
+    std::vector<float> sum;
+    GUARD(sum.resize(E));
+    for (uint32_t b = 0; b < nb; ++b) {
+        o.scalar<uint64_t>(layer_bytes * L);
+        const uint32_t n = std::min(T, c->live_tokens - b * T);
+        for (uint32_t l = 0; l < L; ++l) {
+            const uint8_t *unit = c->repo_host + (static_cast<uint64_t>(b) * L + l) * c->unit;
+            const uint32_t mean_tokens = f16 ? n : (n == T ? 1u : n);
+            o.scalar(n);
+            o.scalar<uint32_t>(0);
+            o.scalar(n);
+            o.scalar(mean_tokens);
+            o.scalar<uint8_t>(0);
+            o.scalar<uint8_t>(1);
+            o.scalar<uint64_t>(kb);  // k: block_tokens unrotated rows
+            o.put(unit, static_cast<uint64_t>(n) * c->k_row);
+            o.zeros(kb - static_cast<uint64_t>(n) * c->k_row);
+            o.scalar<uint64_t>(0);   // v
+            o.scalar<uint64_t>(0);   // k_gpu
+            o.scalar<uint64_t>(vb);  // v_gpu
+            o.put(unit + c->unit_k, static_cast<uint64_t>(n) * c->v_row);
+            o.zeros(vb - static_cast<uint64_t>(n) * c->v_row);
+            o.scalar<uint64_t>(E);   // k_sum
+            if (!buf) {
+                o.len += static_cast<uint64_t>(E) * 4;
+                continue;
+            }
+            if (f16) {  // the token-order f32 sum of the stored f16 rows
+                const uint16_t *k = reinterpret_cast<const uint16_t *>(unit);
+                std::fill(sum.begin(), sum.end(), 0.0f);
+                for (uint32_t t = 0; t < n; ++t)
+                    for (uint32_t e = 0; e < E; ++e) {
+                        __half_raw hr;
+                        hr.x = k[static_cast<size_t>(t) * E + e];
+                        sum[e] += __half2float(__half(hr));
+                    }
+            } else {
+                for (uint32_t e = 0; e < E; ++e)
+                    sum[e] = n == T ? summ[(static_cast<size_t>(l) * E + e) * c->ncap + b]
+                                    : tail[static_cast<size_t>(l) * E + e];
+            }
+            o.put(sum.data(), static_cast<uint64_t>(E) * 4);
+        }
+    }
+    *len = o.len;
+    if (buf && o.overflow)
+        return fail(KVMRET_ERR_ARG, "snapshot of %llu bytes exceeds the %llu-byte buffer",
+                    (unsigned long long)o.len, (unsigned long long)cap);
+    if (hash) *hash = o.hash;
+    return KVMRET_OK;
+}
+
+int kvmret_snapshot_read(kvmret_ctx *c, const void *buf, uint64_t len, uint64_t *hash) {
+    NEED_CTX(c);
+    if (!buf) return fail(KVMRET_ERR_ARG, "null buffer");
+    if (c->live_tokens) return fail(KVMRET_ERR_STATE, "snapshot read needs an empty context");
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));
+    const uint32_t L = c->cfg.n_layer, E = c->E, T = c->cfg.block_tokens;
+    const bool f16 = c->cfg.k_type == KVMRET_TYPE_F16;
+    SnapIn in{static_cast<const uint8_t *>(buf), len};
+    in.hashing = hash != nullptr;
+    uint32_t u32[5];
+    uint64_t u64[4];
+    for (uint32_t &x : u32)
+        if (!in.scalar(x)) return fail(KVMRET_ERR_ARG, "truncated snapshot");
+    for (uint64_t &x : u64)
+        if (!in.scalar(x)) return fail(KVMRET_ERR_ARG, "truncated snapshot");
+    if (u32[0] != kSnapMagic || u32[1] != L || u32[2] != E || u32[3] != E || u32[4] != T ||
+        u64[0] != (f16 ? 0 : c->k_row) || u64[1] != 0 || u64[2] != c->v_row)
+        return fail(KVMRET_ERR_ARG, "snapshot made with another geometry");
+    const uint64_t nb = u64[3];
+    if (nb > c->cfg.max_blocks)
+        return fail(KVMRET_ERR_ARG, "snapshot holds %llu blocks, capacity %u",
+                    (unsigned long long)nb, c->cfg.max_blocks);
+    std::vector<float> summ, tail;
+    std::vector<uint32_t> ntok;
+    std::vector<uint8_t> has;
+    GUARD(summ.assign(static_cast<size_t>(L) * E * c->ncap, 0.0f));
+    GUARD(tail.assign(static_cast<size_t>(L) * E, 0.0f));
+    GUARD(ntok.assign(c->ncap, 0));
+    GUARD(has.assign(c->ncap, 0));
+    std::vector<float> ks;
+    GUARD(ks.resize(E));
+    uint32_t total = 0;
+    for (uint64_t b = 0; b < nb; ++b) {
+        uint64_t size = 0;
+        if (!in.scalar(size) || size > in.left) return fail(KVMRET_ERR_ARG, "truncated snapshot");
+        const uint64_t before = in.left;
+        uint32_t n_blk = 0;
+        bool blk_has = true;
+        for (uint32_t l = 0; l < L; ++l) {
+            uint32_t n, kgt, vgt, mt;
+            uint8_t kf, vf;
+            if (!in.scalar(n) || !in.scalar(kgt) || !in.scalar(vgt) || !in.scalar(mt) ||
+                !in.scalar(kf) || !in.scalar(vf))
+                return fail(KVMRET_ERR_ARG, "truncated snapshot");
+            if (std::max({n, kgt, vgt, mt}) > T || kf > 1 || vf > 1 || kgt != 0 || vgt != n ||
+                (l > 0 && n != n_blk) || n == 0)
+                return fail(KVMRET_ERR_ARG, "snapshot block %llu: token counts this store "
+                                            "cannot hold", (unsigned long long)b);
+            n_blk = n;
+            uint8_t *unit = c->repo_host + (b * L + l) * c->unit;
+            uint64_t cnt = 0;
+            // k: at least the block's rows, at most a block
+            if (!in.scalar(cnt) || cnt < static_cast<uint64_t>(n) * c->k_row ||
+                cnt > static_cast<uint64_t>(T) * c->k_row)
+                return fail(KVMRET_ERR_ARG, "snapshot block %llu: bad K rows", (unsigned long long)b);
+            if (!in.read(unit, static_cast<uint64_t>(n) * c->k_row) ||
+                !in.read(nullptr, cnt - static_cast<uint64_t>(n) * c->k_row))
+                return fail(KVMRET_ERR_ARG, "truncated snapshot");
+            if (!in.scalar(cnt) || cnt != 0 || !in.scalar(cnt) || cnt != 0)
+                return fail(KVMRET_ERR_ARG, "snapshot block %llu: host V or packed K rows this "
+                                            "store does not keep", (unsigned long long)b);
+            if (!in.scalar(cnt) || cnt < static_cast<uint64_t>(n) * c->v_row ||
+                cnt > static_cast<uint64_t>(T) * c->v_row)
+                return fail(KVMRET_ERR_ARG, "snapshot block %llu: bad V rows", (unsigned long long)b);
+            if (!in.read(unit + c->unit_k, static_cast<uint64_t>(n) * c->v_row) ||
+                !in.read(nullptr, cnt - static_cast<uint64_t>(n) * c->v_row))
+                return fail(KVMRET_ERR_ARG, "truncated snapshot");
+            if (!in.scalar(cnt) || (mt && cnt != E) || cnt > E)
+                return fail(KVMRET_ERR_ARG, "snapshot block %llu: bad K sum", (unsigned long long)b);
+            if (!in.read(cnt ? ks.data() : nullptr, cnt * 4))
+                return fail(KVMRET_ERR_ARG, "truncated snapshot");
+            if (mt) {  // mean = sum * (1 / mean_tokens), as the append computes it
+                const float inv = 1.0f / static_cast<float>(mt);
+                for (uint32_t e = 0; e < E; ++e)
+                    summ[(static_cast<size_t>(l) * E + e) * c->ncap + b] = ks[e] * inv;
+                if (n < T && mt == n)
+                    std::copy(ks.begin(), ks.end(), tail.begin() + static_cast<size_t>(l) * E);
+            } else {
+                blk_has = false;
+            }
+        }
+        if (before - in.left != size)
+            return fail(KVMRET_ERR_ARG, "snapshot block %llu: section size mismatch",
+                        (unsigned long long)b);
+        if (b + 1 < nb && n_blk != T)
+            return fail(KVMRET_ERR_ARG, "snapshot block %llu is partial but not the last",
+                        (unsigned long long)b);
+        ntok[b] = n_blk;
+        has[b] = blk_has ? 1 : 0;
+        total += n_blk;
+    }
+    if (in.left) return fail(KVMRET_ERR_ARG, "%llu trailing snapshot bytes",
+                             (unsigned long long)in.left);
+    CK(cudaMemcpy(c->summ, summ.data(), summ.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->tail_sum, tail.data(), tail.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->d_blk_ntok, ntok.data(), ntok.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->has_block, has.data(), has.size(), cudaMemcpyHostToDevice));
+    GUARD(c->table.append(total));
+    c->live_tokens = total;
+    c->kept_valid = false;
+    c->mhat_valid = 0;
+    if (hash) *hash = in.hash;
+    return KVMRET_OK;
 }
 
 // ---------------------------------------------------------------------------

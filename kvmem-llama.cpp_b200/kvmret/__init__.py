@@ -74,6 +74,27 @@ class StepStats(ctypes.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class NvmeConfig(ctypes.Structure):
+    _fields_ = [("dir", ctypes.c_char_p), ("file_name", ctypes.c_char_p),
+                ("total_bytes", ctypes.c_uint64), ("slot_bytes", ctypes.c_uint64),
+                ("durable", ctypes.c_int32), ("direct_read", ctypes.c_int32),
+                ("drop_page_cache", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
+class NvmeSpan(ctypes.Structure):
+    _fields_ = [("slot", ctypes.c_int32), ("pad_", ctypes.c_uint32),
+                ("buffer_offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
+
+
+class NvmeStats(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint64), ("syscalls", ctypes.c_uint64),
+                ("direct_bytes", ctypes.c_uint64), ("cache_drop_bytes", ctypes.c_uint64),
+                ("cache_drop_failures", ctypes.c_uint64)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 class Prof(ctypes.Structure):
     _fields_ = [
         ("launches", ctypes.c_uint64), ("n_score", ctypes.c_uint32),
@@ -159,6 +180,35 @@ SIGNATURES = {
     "kvmret_exchange_export": (ctypes.c_int, [_P, _U32, _P]),
     "kvmret_exchange_import": (ctypes.c_int, [_P, _U32, _U32, _P]),
     "kvmret_score_exchange": (ctypes.c_int, [_P]),
+    "kvmret_store_create": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
+    "kvmret_store_swap": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
+    "kvmret_store_rows": (_U32, [_P]),
+    "kvmret_store_bytes": (_U64, [_P]),
+    "kvmret_store_destroy": (None, [_P]),
+    "kvmret_nvme_create": (ctypes.c_int, [ctypes.POINTER(NvmeConfig), ctypes.POINTER(_P)]),
+    "kvmret_nvme_destroy": (None, [_P]),
+    "kvmret_nvme_slot_count": (_U32, [_P]),
+    "kvmret_nvme_free_slots": (_U32, [_P]),
+    "kvmret_nvme_direct_reads": (ctypes.c_int, [_P]),
+    "kvmret_nvme_path": (ctypes.c_int, [_P, ctypes.c_char_p, _U32]),
+    "kvmret_nvme_block_slot": (_I32, [_P, _U32]),
+    "kvmret_nvme_lru_victim": (_I32, [_P]),
+    "kvmret_nvme_place": (_I32, [_P, _U32, ctypes.c_int, _PI32]),
+    "kvmret_nvme_release": (ctypes.c_int, [_P, _U32]),
+    "kvmret_nvme_touch": (ctypes.c_int, [_P, _U32]),
+    "kvmret_nvme_write_block": (ctypes.c_int, [_P, _U32, _P, _U64]),
+    "kvmret_nvme_read_block": (ctypes.c_int, [_P, _U32, _P, _U64]),
+    "kvmret_nvme_write_range": (ctypes.c_int, [_P, _I32, _U64, _P, _U64]),
+    "kvmret_nvme_read_range": (ctypes.c_int, [_P, _I32, _U64, _P, _U64]),
+    "kvmret_nvme_write_spans": (ctypes.c_int, [_P, ctypes.POINTER(NvmeSpan), _U32, _P, _U64,
+                                               ctypes.POINTER(NvmeStats)]),
+    "kvmret_nvme_read_spans": (ctypes.c_int, [_P, ctypes.POINTER(NvmeSpan), _U32, _P, _U64,
+                                              ctypes.POINTER(NvmeStats)]),
+    "kvmret_repo_spill": (ctypes.c_int, [_P, _P, _PU32, _U32, ctypes.POINTER(NvmeStats)]),
+    "kvmret_repo_fill": (ctypes.c_int, [_P, _P, _PU32, _U32, ctypes.POINTER(NvmeStats)]),
+    "kvmret_snapshot_write": (ctypes.c_int, [_P, _P, _U64, ctypes.POINTER(_U64),
+                                             ctypes.POINTER(_U64)]),
+    "kvmret_snapshot_read": (ctypes.c_int, [_P, _P, _U64, ctypes.POINTER(_U64)]),
     "kvmret_lanes_create": (ctypes.c_int, [ctypes.POINTER(_P), _U32, ctypes.POINTER(_P)]),
     "kvmret_lanes_destroy": (None, [_P]),
     "kvmret_lanes_score_layers": (ctypes.c_int, [_P, _P, _P]),
@@ -471,6 +521,48 @@ class Retriever:
         idle slots (True) or keep only the working set (False)."""
         _check(lib.kvmret_set_pool_cache(self.h, int(on)))
 
+    def snapshot(self, hashed=True):
+        """The conversation as a snapshot archive: (uint8 array, FNV-1a hash)."""
+        n = _U64(0)
+        _check(lib.kvmret_snapshot_write(self.h, None, 0, ctypes.byref(n), None))
+        out = np.zeros(n.value, np.uint8)
+        h = _U64(0)
+        _check(lib.kvmret_snapshot_write(self.h, out.ctypes.data_as(_P), n.value, ctypes.byref(n),
+                                         ctypes.byref(h) if hashed else None))
+        return out, h.value
+
+    def restore(self, archive) -> int:
+        """Fill this (empty) context from a snapshot archive; returns its hash."""
+        a = np.ascontiguousarray(archive, np.uint8)
+        h = _U64(0)
+        _check(lib.kvmret_snapshot_read(self.h, a.ctypes.data_as(_P), a.size, ctypes.byref(h)))
+        return h.value
+
+    def repo_spill(self, tier: "Nvme", blocks) -> dict:
+        b, bp = _u32(blocks)
+        st = NvmeStats()
+        _check(lib.kvmret_repo_spill(self.h, tier.h, bp, len(b), ctypes.byref(st)))
+        return st.as_dict()
+
+    def repo_fill(self, tier: "Nvme", blocks) -> dict:
+        b, bp = _u32(blocks)
+        st = NvmeStats()
+        _check(lib.kvmret_repo_fill(self.h, tier.h, bp, len(b), ctypes.byref(st)))
+        return st.as_dict()
+
+    def store_create(self) -> "Store":
+        """A new empty conversation store with this context's geometry."""
+        h = _P()
+        _check(lib.kvmret_store_create(self.h, ctypes.byref(h)))
+        return Store(h)
+
+    def store_swap(self, store: "Store") -> bool:
+        """Exchange the active conversation with `store`'s; True when the
+        incoming conversation's working set was staged back into the window."""
+        r = ctypes.c_int(0)
+        _check(lib.kvmret_store_swap(self.h, store.h, ctypes.byref(r)))
+        return bool(r.value)
+
     def apply_retrieval(self, mandatory=()):
         m, mp = _u32(list(mandatory))
         ids = np.zeros(max(1, min(self.cfg.budget_blocks, self.n_blocks)), np.uint32)
@@ -507,6 +599,133 @@ class Retriever:
         _check(lib.kvmret_window_read(self.h, layer, int(is_v), slot0, n_slots,
                                       out.ctypes.data_as(_P)))
         return out
+
+
+class Nvme:
+    """NVMe raw tier (kvmret_nvme): a file arena of fixed-size slots."""
+
+    def __init__(self, dir, total_bytes, slot_bytes, file_name=None, durable=False,
+                 direct_read=False, drop_page_cache=False):
+        c = NvmeConfig(dir.encode(), file_name.encode() if file_name else None, total_bytes,
+                       slot_bytes, int(durable), int(direct_read), int(drop_page_cache), 0)
+        h = _P()
+        _check(lib.kvmret_nvme_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib.kvmret_nvme_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def enabled(self):
+        return self.slot_count > 0
+
+    @property
+    def slot_count(self):
+        return int(lib.kvmret_nvme_slot_count(self.h))
+
+    @property
+    def free_slots(self):
+        return int(lib.kvmret_nvme_free_slots(self.h))
+
+    @property
+    def direct_reads(self):
+        return bool(lib.kvmret_nvme_direct_reads(self.h))
+
+    @property
+    def path(self):
+        buf = ctypes.create_string_buffer(4096)
+        _check(lib.kvmret_nvme_path(self.h, buf, 4096))
+        return buf.value.decode()
+
+    def block_slot(self, block):
+        return int(lib.kvmret_nvme_block_slot(self.h, block))
+
+    def lru_victim(self):
+        return int(lib.kvmret_nvme_lru_victim(self.h))
+
+    def place(self, block, evict=False):
+        ev = _I32(-1)
+        slot = int(lib.kvmret_nvme_place(self.h, block, int(evict), ctypes.byref(ev)))
+        return slot, ev.value
+
+    def release(self, block):
+        _check(lib.kvmret_nvme_release(self.h, block))
+
+    def touch(self, block):
+        _check(lib.kvmret_nvme_touch(self.h, block))
+
+    def write_block(self, block, data: np.ndarray):
+        d = np.ascontiguousarray(data, np.uint8)
+        _check(lib.kvmret_nvme_write_block(self.h, block, d.ctypes.data_as(_P), d.size))
+
+    def read_block(self, block, n) -> np.ndarray:
+        out = np.zeros(n, np.uint8)
+        _check(lib.kvmret_nvme_read_block(self.h, block, out.ctypes.data_as(_P), n))
+        return out
+
+    def write_range(self, slot, offset, data: np.ndarray):
+        d = np.ascontiguousarray(data, np.uint8)
+        _check(lib.kvmret_nvme_write_range(self.h, slot, offset, d.ctypes.data_as(_P), d.size))
+
+    def read_range(self, slot, offset, n) -> np.ndarray:
+        out = np.zeros(n, np.uint8)
+        _check(lib.kvmret_nvme_read_range(self.h, slot, offset, out.ctypes.data_as(_P), n))
+        return out
+
+    def _spans(self, spans):
+        arr = (NvmeSpan * max(1, len(spans)))()
+        for i, (slot, off, n) in enumerate(spans):
+            arr[i] = NvmeSpan(slot, 0, off, n)
+        return arr
+
+    def write_spans(self, spans, buffer: np.ndarray) -> dict:
+        st = NvmeStats()
+        b = np.ascontiguousarray(buffer, np.uint8)
+        _check(lib.kvmret_nvme_write_spans(self.h, self._spans(spans), len(spans),
+                                           b.ctypes.data_as(_P), b.size, ctypes.byref(st)))
+        return st.as_dict()
+
+    def read_spans(self, spans, buffer: np.ndarray) -> dict:
+        st = NvmeStats()
+        _check(lib.kvmret_nvme_read_spans(self.h, self._spans(spans), len(spans),
+                                          buffer.ctypes.data_as(_P), buffer.size,
+                                          ctypes.byref(st)))
+        return st.as_dict()
+
+
+class Store:
+    """A parked conversation (kvmret_store): made by Retriever.store_create,
+    exchanged with the active one by Retriever.store_swap."""
+
+    def __init__(self, h):
+        self.h = h
+
+    @property
+    def rows(self) -> int:
+        return int(lib.kvmret_store_rows(self.h))
+
+    @property
+    def host_bytes(self) -> int:
+        return int(lib.kvmret_store_bytes(self.h))
+
+    def close(self):
+        if self.h:
+            lib.kvmret_store_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Table:

@@ -103,6 +103,10 @@ def _load_ref():
         "ref_rope_units_f16": (None, [_PP, _PP, _PP, _PP, ctypes.c_uint64, _PI32, _U32, _U32,
                                       _U32, _U32, _U32, ctypes.c_float, ctypes.c_float]),
         "ref_copy_list": (None, [_PP, _PP, ctypes.POINTER(ctypes.c_uint64), _U32, _U32]),
+        "ref_snapshot_rows": (ctypes.c_uint64, [_U32, _U32, _U32, ctypes.c_uint64,
+                                                ctypes.c_uint64, _U32, _PU8, _PF, _PU8, _PU8,
+                                                ctypes.c_uint64,
+                                                ctypes.POINTER(ctypes.c_uint64)]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -368,3 +372,24 @@ def hadamard_rows(x, n_head, d_head, nrot):
     rows = x.size // (n_head * d_head)
     orc.orc_hadamard_rows(_ptr(x, _PF), rows, n_head, d_head, nrot)
     return x
+
+
+# --- snapshot archive -------------------------------------------------------
+def ref_snapshot_rows(n_layer, n_embd, block_tokens, k_row_bytes, v_row_bytes, k_rows, k_f32,
+                      v_rows):
+    """The reference's RawKvStore snapshot of k_rows [L][n][krow] u8 (with
+    their f32 values k_f32 [L][n][E] or None) and v_rows [L][n][vrow] u8:
+    (archive bytes, FNV-1a hash)."""
+    k = np.ascontiguousarray(k_rows, np.uint8)
+    v = np.ascontiguousarray(v_rows, np.uint8)
+    n_tok = k.shape[1]
+    kf = None if k_f32 is None else np.ascontiguousarray(k_f32, np.float32)
+    h = ctypes.c_uint64(0)
+    size = ref.ref_snapshot_rows(n_layer, n_embd, block_tokens, k_row_bytes, v_row_bytes, n_tok,
+                                 _ptr(k, _PU8), None if kf is None else _ptr(kf, _PF),
+                                 _ptr(v, _PU8), None, 0, None)
+    out = np.zeros(size, np.uint8)
+    ref.ref_snapshot_rows(n_layer, n_embd, block_tokens, k_row_bytes, v_row_bytes, n_tok,
+                          _ptr(k, _PU8), None if kf is None else _ptr(kf, _PF), _ptr(v, _PU8),
+                          _ptr(out, _PU8), size, ctypes.byref(h))
+    return out, h.value

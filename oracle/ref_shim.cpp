@@ -154,3 +154,39 @@ REF_API void ref_runtime_truncate(void *p, uint32_t token_pos) {
 REF_API void ref_runtime_set_tier_gpu(void *p, uint32_t block_id) {
     static_cast<RefRuntime *>(p)->rt.store().set_block_tier(block_id, kvmem::KvTier::GPU, -1, -1);
 }
+
+// The reference's own snapshot archive of n_tok tokens per layer, stored the
+// way this library stores them: unrotated K rows (k_row_bytes 0 = f16) with
+// their f32 values for the running sum, and V as packed rows. The bytes of
+// RawKvStore::snapshot_write through a SnapshotWriter into `out`; returns the
+// archive size (also when it exceeds cap, without writing past it).
+#include "kvmem/snapshot.hpp"
+
+REF_API uint64_t ref_snapshot_rows(uint32_t n_layer, uint32_t n_embd, uint32_t block_tokens,
+                                   uint64_t k_row_bytes, uint64_t v_row_bytes, uint32_t n_tok,
+                                   const uint8_t *k_rows, const float *k_f32,
+                                   const uint8_t *v_rows, uint8_t *out, uint64_t cap,
+                                   uint64_t *hash) {
+    kvmem::RawKvStoreConfig c;
+    c.n_layer = n_layer;
+    c.n_embd_k = n_embd;
+    c.n_embd_v = n_embd;
+    c.block_tokens = block_tokens;
+    c.k_row_bytes = k_row_bytes;
+    c.v_gpu_row_bytes = v_row_bytes;
+    kvmem::RawKvStore s(c);
+    const uint64_t krow = k_row_bytes ? k_row_bytes : 2ull * n_embd;
+    for (uint32_t l = 0; l < n_layer; ++l) {
+        s.write_layer_k_rows(0, n_tok, l, k_rows + static_cast<size_t>(l) * n_tok * krow,
+                             k_f32 ? k_f32 + static_cast<size_t>(l) * n_tok * n_embd : nullptr);
+        s.write_layer_v_gpu(0, n_tok, l, v_rows + static_cast<size_t>(l) * n_tok * v_row_bytes);
+    }
+    uint64_t pos = 0;
+    kvmem::SnapshotWriter w([&](const void *p, size_t n) {
+        if (pos + n <= cap) std::memcpy(out + pos, p, n);
+        pos += n;
+    });
+    s.snapshot_write(w);
+    if (hash) *hash = w.hash();
+    return w.bytes();
+}

@@ -21,7 +21,8 @@ import torch
 
 import kvmret
 import pyoracle as po
-from kvm_helpers import append_history, config_for, f16_ulp_diff, history_units, q8_blocks_diff
+from kvm_helpers import append_history, check_window as _check_window, config_for
+from kvm_helpers import oracle_ids_tokens as _oracle_ids, oracle_mean_tokens as _oracle_mean
 from kvmret import synth
 
 pytestmark = pytest.mark.gpu
@@ -35,31 +36,6 @@ def _w(**kw):
     return synth.Workload(**base)
 
 
-def _oracle_mean(hist, n_tok):
-    """Summaries [N][L][E] of the first n_tok tokens (a partial last block)."""
-    w = hist.w
-    T, L, E = w.block_tokens, w.n_layer, w.E
-    k = hist.k.reshape(L, w.n_tokens, E)[:, :n_tok]
-    nb = (n_tok + T - 1) // T
-    out = np.zeros((nb, L, E), np.float32)
-    for b in range(nb):
-        t1 = min(n_tok, (b + 1) * T)
-        out[b] = po.mean_k(np.ascontiguousarray(k[:, b * T:t1]))
-    return out
-
-
-def _oracle_ids(hist, n_tok, q, gen_first=None):
-    """Top-k over the blocks before the decode blocks, plus the decode blocks."""
-    w = hist.w
-    mean = _oracle_mean(hist, n_tok)
-    nb = mean.shape[0]
-    scores = po.score(mean, np.ones(nb, np.uint8), q.reshape(w.n_layer, -1).astype(np.float32),
-                      np.ones(w.n_layer, np.uint32), w.n_head, w.n_head_kv, w.d_head)
-    g0 = nb if gen_first is None else min(gen_first, nb)
-    ids = po.pick_topk(scores[:g0], w.budget_blocks, w.sink_blocks)
-    return sorted(set(ids.tolist()) | set(range(g0, nb)))
-
-
 def _append_tokens(r, hist, t0, t1, quant=False):
     w = hist.w
     L, E = w.n_layer, w.E
@@ -70,37 +46,6 @@ def _append_tokens(r, hist, t0, t1, quant=False):
                  pos0=t0)
     else:
         r.append(k, v, pos0=t0)
-
-
-def _check_window(r, hist, n_tok, want_ids, quant=False):
-    """Layout chronological with running-sum bases; every slot's K and V
-    against the oracle from the stored rows."""
-    w = hist.w
-    T, L = w.block_tokens, w.n_layer
-    ids, bases = r.window_layout()
-    assert list(ids) == list(want_ids)
-    ntok = [min(T, n_tok - b * T) for b in want_ids]
-    assert list(bases) == [int(x) for x in np.concatenate([[0], np.cumsum(ntok)[:-1]])]
-    repo = r.repo_view()
-    unit = int(kvmret.lib.kvmret_repo_unit_bytes(r.h))
-    kb = int(kvmret.lib.kvmret_repo_k_bytes(r.h))
-    for i, (b, base, n) in enumerate(zip(ids, bases, ntok)):
-        for l in range(L):
-            o = (int(b) * L + l) * unit
-            src_k = np.array(repo[o:o + n * r.k_row])
-            src_v = np.array(repo[o + kb:o + kb + n * r.v_row])
-            wk = r.window_read(l, False, i, 1)[:n * r.k_row]
-            wv = r.window_read(l, True, i, 1)[:n * r.v_row]
-            assert np.array_equal(wv, src_v), (i, int(b), l)
-            if quant:
-                want = po.rope_block_q8_0(src_k, n, w.n_head_kv, w.d_head, int(base),
-                                          w.freq_base, fwht_n=w.d_head)
-                assert q8_blocks_diff(wk, want) <= (1, 1), (i, int(b), l)
-            else:
-                want = po.rope_block_f16(src_k.view(np.uint16).reshape(n, w.n_head_kv, w.d_head),
-                                         int(base), w.freq_base)
-                assert f16_ulp_diff(wk.view(np.uint16), want.reshape(-1)).max() <= 2, (i, int(b))
-    return ids
 
 
 @pytest.mark.parametrize("selected_before", [True, False])
