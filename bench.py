@@ -643,7 +643,11 @@ def run_ours(args, w):
     del dk, dv
     torch.cuda.synchronize()
     t_setup = time.perf_counter() - t_setup
+    if world > 1:  # every rank copies at once, as every rank's step reads the host at once
+        dist.barrier()
     link = link_gbps()
+    if world > 1:
+        dist.barrier()
     link_d2h = link_gbps(d2h=True)
 
     stride = r.contrib_stride
@@ -1353,6 +1357,8 @@ def run_lanes(args, w):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     hbm, peak_src = load_peaks()
+    if world > 1:  # every rank copies at once, as in the step
+        dist.barrier()
     link = link_gbps()
     n_asm = sum(p["n_asm"] for p in profs)
     asm_ms = sum(p["asm_ms"] for p in profs)

@@ -93,15 +93,21 @@ def planted_ids(w: Workload, rng: np.random.Generator) -> np.ndarray:
     return np.sort(rng.choice(pool, size=min(w.n_planted, len(pool)), replace=False))
 
 
-def torch_history_chunk(w: Workload, gen, scale, u, planted_mask, tok0: int, n_tok: int):
+def torch_history_chunk(w: Workload, gens, scale, u, planted_mask, tok0: int, n_tok: int):
     """GPU chunk of the history: K, V f16 [L][n_tok][E] for tokens [tok0, tok0+n_tok).
 
-    scale: [L][Hkv][D] f32, u: [L][Hkv][D] unit group query directions,
-    planted_mask: bool [n_blocks] CUDA tensor.
+    gens: one CUDA generator per layer (each layer's keys and values come from
+    its own random stream, so a layer's history does not depend on which
+    other layers a shard holds), scale: [L][Hkv][D] f32, u: [L][Hkv][D] unit
+    group query directions, planted_mask: bool [n_blocks] CUDA tensor.
     """
     import torch
     L, Hkv, D, T = w.n_layer, w.n_head_kv, w.d_head, w.block_tokens
-    k = torch.randn((L, n_tok, Hkv, D), generator=gen, device="cuda", dtype=torch.float32)
+    k = torch.empty((L, n_tok, Hkv, D), device="cuda", dtype=torch.float32)
+    v = torch.empty((L, n_tok, Hkv, D), device="cuda", dtype=torch.float32)
+    for i in range(L):
+        k[i].normal_(generator=gens[i])
+        v[i].normal_(generator=gens[i])
     k.mul_(scale[:, None])
     blk = (torch.arange(tok0, tok0 + n_tok, device="cuda") // T)
     # tokens past the planted mask's blocks (a prefill chunk beyond the
@@ -111,7 +117,6 @@ def torch_history_chunk(w: Workload, gen, scale, u, planted_mask, tok0: int, n_t
     m[inb] = planted_mask[blk[inb]].to(torch.float32)
     m = m[None, :, None, None]
     k.add_(0.5 * m * u[:, None])
-    v = torch.randn((L, n_tok, Hkv, D), generator=gen, device="cuda", dtype=torch.float32)
     return k.to(torch.float16).reshape(L, n_tok, Hkv * D), v.to(torch.float16).reshape(
         L, n_tok, Hkv * D)
 
@@ -138,15 +143,18 @@ class TorchHistory:
         sl = slice(layer0, layer0 + self.n_layer)
         self.scale, self.u, self.mask = scale[sl].contiguous(), u[sl].contiguous(), mask
         self.q0 = q0
-        self.gen = torch.Generator(device="cuda")
-        self.gen.manual_seed(w.seed * 1000 + layer0 + 1)
+        self.gens = []
+        for layer in range(layer0, layer0 + self.n_layer):
+            g = torch.Generator(device="cuda")
+            g.manual_seed(w.seed * 1000 + layer + 1)
+            self.gens.append(g)
         self.qgen = torch.Generator(device="cuda")
         self.qgen.manual_seed(w.seed + 7)
         self.q = q0.float()
 
     def chunk(self, tok0, n_tok):
         w = replace(self.w, n_layer=self.n_layer)
-        return torch_history_chunk(w, self.gen, self.scale, self.u, self.mask, tok0, n_tok)
+        return torch_history_chunk(w, self.gens, self.scale, self.u, self.mask, tok0, n_tok)
 
     def next_query(self):
         """Full-depth f16 query [L][1][Hq*D] for this step, then drift."""
