@@ -315,6 +315,13 @@ int kvmret_rope_q8_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t 
 int kvmret_rope_q4_0(const void *k_dev, void *out_dev, uint32_t n_tok, uint32_t n_head_kv,
                      uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base,
                      float freq_scale, uint32_t fwht_n, void *stream);
+/* Block top-k on caller buffers (KvMemStore::pick_topk_ungrouped,
+ * kvmem/src/host/kvmem_store.cpp:594-616, the score fill after its keep set): sel_dev[b] = 1
+ * for every kept block (kept_dev[b] != 0) and for the `need` best of the
+ * others under (score desc, id: higher wins when tie_higher_id, else lower);
+ * 0 elsewhere. -0.0 and +0.0 tie. One CTA, radix selection, O(n) per pass. */
+int kvmret_topk_select(const double *scores_dev, const uint8_t *kept_dev, uint32_t n,
+                       uint32_t need, int tie_higher_id, uint8_t *sel_dev, void *stream);
 /* ---- layer-sharded exchange over NVLink peer memory (no collective
  *      library). One context per rank, each holding n_layer of
  *      the world * n_layer layers in rank order. Set-up (once): every rank

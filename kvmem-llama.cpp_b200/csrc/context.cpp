@@ -1434,6 +1434,15 @@ int kvmret_rope_f16(const uint16_t *k, uint16_t *out, uint32_t n_tok, uint32_t n
     return rope_stateless(al, n_tok, n_rot, pos0, static_cast<cudaStream_t>(stream));
 }
 
+int kvmret_topk_select(const double *scores, const uint8_t *kept, uint32_t n, uint32_t need,
+                       int tie_higher_id, uint8_t *sel, void *stream) {
+    if (n == 0) return KVMRET_OK;
+    if (!scores || !kept || !sel) return fail(KVMRET_ERR_ARG, "null buffer");
+    CK(kvmret::launch_select(scores, kept, n, need, tie_higher_id ? 1 : 0, sel,
+                             static_cast<cudaStream_t>(stream)));
+    return KVMRET_OK;
+}
+
 namespace {
 int rope_quant(int32_t type, const void *k, void *out, uint32_t n_tok, uint32_t n_head_kv,
                uint32_t d_head, uint32_t n_rot, int32_t pos0, float freq_base, float freq_scale,

@@ -334,62 +334,204 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
-// S6: exact rank selection. Block b (not kept) is chosen iff fewer than
-// `need` other candidates beat it under (score desc, id by tie rule) — the
-// same set nth_element returns for a strict total order
-// (kvmem_store.cpp:600-616). One warp per block: the lanes split the
-// candidates and the counts are summed with a warp reduction.
-__global__ void __launch_bounds__(256) select_kernel(const double *__restrict__ scores,
-                                                     const uint8_t *__restrict__ kept,
-                                                     uint32_t n, uint32_t need, int tie_high,
-                                                     uint8_t *__restrict__ sel) {
-    dep_wait();
-    const uint32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint32_t lane = threadIdx.x & 31;
-    if (b >= n) return;
-    if (kept[b]) {
-        if (lane == 0) sel[b] = 1;
-        return;
-    }
-    const double sb = scores[b];
-    uint32_t rank = 0;
-    for (uint32_t c = lane; c < n; c += 32) {
-        if (kept[c]) continue;
-        const double sc = scores[c];
-        rank += (sc > sb || (sc == sb && (tie_high ? c > b : c < b))) ? 1u : 0u;
-    }
-    rank = __reduce_add_sync(0xffffffffu, rank);
-    if (lane == 0) sel[b] = rank < need ? 1 : 0;
+// Block-wide radix selection over 128-bit keys that are distinct among the
+// valid ones. The common prefix of all valid keys is skipped first (a min/max
+// reduction), then 8-bit digits are resolved from the top: each pass counts
+// the keys that share the resolved prefix into a shared histogram
+// (warp-aggregated atomics) and one warp finds the digit that holds the k-th
+// smallest key. It stops as soon as every key of that digit is among the k
+// smallest, so a handful of passes settle a few thousand keys. Work is
+// O(n) per pass; the result is a threshold with exactly k valid keys <= it.
+using u128 = unsigned __int128;
+
+struct RadixSmem {
+    u128 wmin[32], wmax[32];
+    u128 prefix, thr;
+    uint32_t hist[256];
+    uint32_t wcnt[32];
+    uint32_t k, top, done, mode, n_valid;
+};
+
+enum : uint32_t { kSelNone = 0, kSelAll = 1, kSelThr = 2 };
+
+__device__ __forceinline__ u128 shfl_xor128(u128 x, int o) {
+    const uint64_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint64_t>(x), o);
+    const uint64_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint64_t>(x >> 64), o);
+    return (static_cast<u128>(hi) << 64) | lo;
 }
 
-// The same with every score and kept flag staged in shared memory first (one
-// load of the whole array per CTA of 32 warps, then ranks from shared memory).
-__global__ void __launch_bounds__(1024) select_smem_kernel(const double *__restrict__ scores,
-                                                           const uint8_t *__restrict__ kept,
-                                                           uint32_t n, uint32_t need,
-                                                           int tie_high, uint8_t *__restrict__ sel) {
-    dep_wait();
-    extern __shared__ double s_sc[];
-    uint8_t *s_kept = reinterpret_cast<uint8_t *>(s_sc + n);
-    for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
-        s_sc[c] = scores[c];
-        s_kept[c] = kept[c];
+__device__ __forceinline__ uint32_t clz128(u128 x) {
+    const uint64_t hi = static_cast<uint64_t>(x >> 64);
+    return hi ? static_cast<uint32_t>(__clzll(static_cast<long long>(hi)))
+              : 64u + static_cast<uint32_t>(__clzll(static_cast<long long>(static_cast<uint64_t>(x))));
+}
+
+// key_of(i, key) -> bool: false for an invalid i. Every thread of the block
+// calls this; on return rs.mode is kSelNone (k == 0 or no valid key), kSelAll
+// (k >= the valid count) or kSelThr (select valid keys <= rs.thr), and
+// rs.n_valid is the valid count. blockDim.x is a multiple of 32.
+template <class KeyFn>
+__device__ void block_select_smallest(uint32_t n, uint32_t k, KeyFn key_of, RadixSmem &rs) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    u128 mn = ~static_cast<u128>(0), mx = 0;
+    uint32_t cnt = 0;
+    for (uint32_t i = tid; i < n; i += blockDim.x) {
+        u128 key;
+        if (!key_of(i, key)) continue;
+        mn = key < mn ? key : mn;
+        mx = key > mx ? key : mx;
+        ++cnt;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const u128 a = shfl_xor128(mn, o), b = shfl_xor128(mx, o);
+        mn = a < mn ? a : mn;
+        mx = b > mx ? b : mx;
+        cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    }
+    if (lane == 0) {
+        rs.wmin[warp] = mn;
+        rs.wmax[warp] = mx;
+        rs.wcnt[warp] = cnt;
     }
     __syncthreads();
-    const uint32_t lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
-    for (uint32_t b = blockIdx.x * nwarp + (threadIdx.x >> 5); b < n; b += gridDim.x * nwarp) {
-        if (s_kept[b]) {
-            if (lane == 0) sel[b] = 1;
-            continue;
+    if (tid == 0) {
+        for (uint32_t w = 1; w < nw; ++w) {
+            mn = rs.wmin[w] < mn ? rs.wmin[w] : mn;
+            mx = rs.wmax[w] > mx ? rs.wmax[w] : mx;
+            cnt += rs.wcnt[w];
         }
-        const double sb = s_sc[b];
-        uint32_t rank = 0;
-        for (uint32_t c = lane; c < n; c += 32) {
-            const double sc = s_sc[c];
-            rank += (!s_kept[c] && (sc > sb || (sc == sb && (tie_high ? c > b : c < b)))) ? 1u : 0u;
+        rs.n_valid = cnt;
+        rs.done = 1;
+        if (k == 0 || cnt == 0) {
+            rs.mode = kSelNone;
+        } else if (k >= cnt) {
+            rs.mode = kSelAll;
+        } else {  // at least two distinct keys: mn != mx
+            rs.mode = kSelThr;
+            const uint32_t top = 127u - clz128(mn ^ mx);
+            rs.top = top;
+            rs.prefix = top == 127 ? static_cast<u128>(0) : (mn >> (top + 1)) << (top + 1);
+            rs.k = k;
+            rs.done = 0;
         }
-        rank = __reduce_add_sync(0xffffffffu, rank);
-        if (lane == 0) sel[b] = rank < need ? 1 : 0;
+    }
+    __syncthreads();
+    while (!rs.done) {
+        const uint32_t top = rs.top, shift = top >= 7 ? top - 7 : 0;
+        const uint32_t nb = 1u << (top - shift + 1);
+        const u128 pre = rs.prefix;
+        for (uint32_t b = tid; b < nb; b += blockDim.x) rs.hist[b] = 0;
+        __syncthreads();
+        for (uint32_t base = 0; base < n; base += blockDim.x) {  // warp-uniform trip count
+            const uint32_t i = base + tid;
+            u128 key = 0;
+            bool act = i < n && key_of(i, key);
+            if (act && top < 127) act = (key >> (top + 1)) == (pre >> (top + 1));
+            const uint32_t dg = act ? static_cast<uint32_t>(key >> shift) & (nb - 1) : 0xffffffffu;
+            const uint32_t peers = __match_any_sync(0xffffffffu, dg);
+            if (act && lane == static_cast<uint32_t>(__ffs(peers) - 1))
+                atomicAdd(&rs.hist[dg], static_cast<uint32_t>(__popc(peers)));
+        }
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t c[8], sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t b = lane * 8 + j;
+                c[j] = b < nb ? rs.hist[b] : 0u;
+                sum += c[j];
+            }
+            uint32_t incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += t;
+            }
+            const uint32_t kk = rs.k, excl = incl - sum;
+            const bool mine = excl < kk && kk <= incl;
+            const uint32_t who = static_cast<uint32_t>(__ffs(__ballot_sync(0xffffffffu, mine)) - 1);
+            if (who >= 32 && lane == 0) {  // unreachable for fixed keys; ends the loop regardless
+                rs.mode = kSelAll;
+                rs.done = 1;
+            }
+            if (lane == who) {
+                uint32_t cum = excl, d = lane * 8, cd = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (cd == 0 && cum + c[j] >= kk) {
+                        d = lane * 8 + j;
+                        cd = c[j];
+                    } else if (cd == 0) {
+                        cum += c[j];
+                    }
+                }
+                const uint32_t rem = kk - cum;
+                const u128 p = pre | (static_cast<u128>(d) << shift);
+                if (rem == cd || shift == 0) {  // the whole digit is in (shift 0: one key)
+                    rs.thr = p | ((static_cast<u128>(1) << shift) - 1);
+                    rs.done = 1;
+                } else {
+                    rs.prefix = p;
+                    rs.k = rem;
+                    rs.top = shift - 1;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Order-preserving map of a double onto u64 (-0.0 taken as +0.0, since the
+// reference's comparisons do not separate them).
+__device__ __forceinline__ uint64_t score_key(double x) {
+    if (x == 0.0) x = 0.0;
+    const uint64_t u = static_cast<uint64_t>(__double_as_longlong(x));
+    return (u >> 63) ? ~u : (u | (1ull << 63));
+}
+
+// ---------------------------------------------------------------------------
+// S6: block top-k. Block b (not kept) is chosen iff fewer than `need` other
+// candidates beat it under (score desc, id by tie rule) — the set nth_element
+// returns for that strict total order (kvmem_store.cpp:600-616). One CTA runs
+// a radix selection over the 96-bit keys (score, id): the `need` best
+// candidates are the `need` smallest complemented keys. STAGED keeps the
+// score keys and kept flags in shared memory (n <= kSelectStagedMax).
+constexpr uint32_t kSelectStagedMax = 16384;
+
+template <bool STAGED>
+__global__ void __launch_bounds__(1024) select_radix_kernel(const double *__restrict__ scores,
+                                                            const uint8_t *__restrict__ kept,
+                                                            uint32_t n, uint32_t need, int tie_high,
+                                                            uint8_t *__restrict__ sel) {
+    dep_wait();
+    extern __shared__ __align__(16) uint8_t sel_sm[];
+    __shared__ RadixSmem rs;
+    uint64_t *s_key = reinterpret_cast<uint64_t *>(sel_sm);
+    uint8_t *s_kept = sel_sm + static_cast<size_t>(n) * 8;
+    if (STAGED) {
+        for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
+            s_key[c] = score_key(scores[c]);
+            s_kept[c] = kept[c];
+        }
+        __syncthreads();
+    }
+    auto key_of = [&](uint32_t i, u128 &key) -> bool {
+        if (STAGED ? s_kept[i] : kept[i]) return false;
+        const uint64_t sk = STAGED ? s_key[i] : score_key(scores[i]);
+        const uint32_t idk = tie_high ? i : ~i;
+        key = ~((static_cast<u128>(sk) << 32) | idk);
+        return true;
+    };
+    block_select_smallest(n, need, key_of, rs);
+    const uint32_t mode = rs.mode;
+    const u128 thr = rs.thr;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        u128 key;
+        uint8_t v;
+        if (!key_of(i, key)) v = 1;  // kept
+        else v = mode == kSelAll ? 1 : mode == kSelNone ? 0 : (key <= thr ? 1 : 0);
+        sel[i] = v;
     }
 }
 
@@ -1758,6 +1900,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     using Scan = cub::BlockScan<uint32_t, kPlanThreads>;
     __shared__ typename Scan::TempStorage ts;
     __shared__ uint32_t s_err, s_mtok, s_ftok;
+    __shared__ RadixSmem rsm;
     extern __shared__ __align__(16) uint32_t psm[];
     const uint32_t W = a.win_slots, P = a.pool_slots, tid = threadIdx.x;
     uint32_t *s_ids = psm;
@@ -1767,6 +1910,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     uint32_t *s_flag = psm + 4 * W;  // bit 0: stage from the host, bit 1: needs a slot
     uint32_t *s_free = psm + 5 * W;  // [P]
     uint32_t *s_cu = psm + 5 * W + P;  // [P] eviction key: slot_used, ~0u if not a candidate
+    uint32_t *s_ev = psm + 5 * W + 2 * P;  // [P] evicted slots in slot order
     if (tid == 0) s_err = a.ext_err ? atomicExch(a.ext_err, 0u) : 0u;  // consumed once
     __syncthreads();
     if (s_err) {  // a rank's score rows never arrived: keep the window, pool and plan as they are
@@ -1842,34 +1986,53 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     __syncthreads();
     if (n_need > n_free) {  // cache mode: evict least recently used blocks outside the window
         const uint32_t deficit = n_need - n_free;
-        // Candidates are pooled blocks outside the new window; their LRU key is
-        // staged in shared memory (~0u marks a non-candidate; slot_used never
-        // reaches it) so the exact rank below reads no global memory.
+        // Candidates are pooled blocks outside the new window, ordered by
+        // (slot_used, slot). Their key is staged in shared memory (~0u marks a
+        // non-candidate; slot_used never reaches it); a radix selection finds
+        // the `deficit` least recently used, which are then ranked among
+        // themselves so that the k-th victim takes free-list position k.
         for (uint32_t s = tid; s < P; s += kPlanThreads) {
             const int32_t b = a.slot_blk[s];
             s_cu[s] = (b < 0 || a.sel[b]) ? 0xffffffffu : a.slot_used[s];
         }
         __syncthreads();
-        uint32_t n_cand_local = 0;
-        for (uint32_t s = tid; s < P; s += kPlanThreads) {
+        auto lru_key = [&](uint32_t s, u128 &key) -> bool {
             const uint32_t u = s_cu[s];
-            if (u == 0xffffffffu) continue;
-            ++n_cand_local;
-            uint32_t r = 0;
-            for (uint32_t s2 = 0; s2 < P; ++s2) {
-                const uint32_t u2 = s_cu[s2];
-                r += (u2 < u || (u2 == u && s2 < s)) ? 1u : 0u;
-            }
-            if (r < deficit) {
-                s_free[n_free + r] = s;
-                a.blk_slot[a.slot_blk[s]] = -1;
-            }
+            if (u == 0xffffffffu) return false;
+            key = (static_cast<u128>(u) << 32) | s;
+            return true;
+        };
+        block_select_smallest(P, deficit, lru_key, rsm);
+        const uint32_t mode = rsm.mode, n_cand = rsm.n_valid;
+        const u128 thr = rsm.thr;
+        uint32_t ec = 0;
+        for (uint32_t s = p0; s < p1; ++s) {
+            u128 key;
+            if (lru_key(s, key) && (mode == kSelAll || (mode == kSelThr && key <= thr))) ++ec;
         }
-        uint32_t n_cand;
-        uint32_t dummy;
-        Scan(ts).ExclusiveSum(n_cand_local, dummy, n_cand);
+        uint32_t erank, n_ev;
+        Scan(ts).ExclusiveSum(ec, erank, n_ev);
         __syncthreads();
-        const uint32_t n_ev = min(deficit, n_cand);
+        for (uint32_t s = p0; s < p1; ++s) {
+            u128 key;
+            if (lru_key(s, key) && (mode == kSelAll || (mode == kSelThr && key <= thr)))
+                s_ev[erank++] = s;
+        }
+        __syncthreads();
+        // n_ev <= deficit <= the window's stage-ins: the quadratic rank below
+        // is bounded by the blocks this step copies from the host
+        for (uint32_t k = tid; k < n_ev; k += kPlanThreads) {
+            const uint32_t s = s_ev[k];
+            const uint64_t key = (static_cast<uint64_t>(s_cu[s]) << 32) | s;
+            uint32_t r = 0;
+            for (uint32_t j = 0; j < n_ev; ++j) {
+                const uint32_t s2 = s_ev[j];
+                r += ((static_cast<uint64_t>(s_cu[s2]) << 32) | s2) < key ? 1u : 0u;
+            }
+            s_free[n_free + r] = s;
+            a.blk_slot[a.slot_blk[s]] = -1;
+        }
+        __syncthreads();
         for (uint32_t k = tid; k < n_ev; k += kPlanThreads) a.slot_blk[s_free[n_free + k]] = -1;
         if (tid == 0 && n_cand < deficit) s_err |= 2;
         n_free += n_ev;
@@ -2145,16 +2308,16 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    const size_t smem = static_cast<size_t>(n_blocks) * (sizeof(double) + 1);
-    if (smem <= 160 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(select_smem_kernel,
+    if (n_blocks <= kSelectStagedMax) {
+        const size_t smem = (static_cast<size_t>(n_blocks) * (sizeof(uint64_t) + 1) + 15) & ~15ull;
+        cudaError_t e = cudaFuncSetAttribute(select_radix_kernel<true>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        return launch_dep(select_smem_kernel, dim3((n_blocks + 31) / 32), dim3(1024), smem, st,
-                          scores, kept, n_blocks, need, tie_higher_id, sel);
+        return launch_dep(select_radix_kernel<true>, dim3(1), dim3(1024), smem, st, scores, kept,
+                          n_blocks, need, tie_higher_id, sel);
     }
-    return launch_dep(select_kernel, dim3((n_blocks + 7) / 8), dim3(256), 0, st, scores, kept,
+    return launch_dep(select_radix_kernel<false>, dim3(1), dim3(1024), 0, st, scores, kept,
                       n_blocks, need, tie_higher_id, sel);
 }
 
@@ -2212,7 +2375,7 @@ cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bo
 }
 
 size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots) {
-    return (5ull * win_slots + 2ull * pool_slots) * sizeof(uint32_t);
+    return (5ull * win_slots + 3ull * pool_slots) * sizeof(uint32_t);
 }
 
 cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st) {

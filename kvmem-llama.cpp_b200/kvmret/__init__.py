@@ -176,6 +176,7 @@ SIGNATURES = {
     "kvmret_rope_q4_0": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, _U32, _I32, ctypes.c_float,
                                         ctypes.c_float, _U32, _P]),
     "kvmret_quantize_f16": (ctypes.c_int, [_P, _P, _I32, _U64, _P]),
+    "kvmret_topk_select": (ctypes.c_int, [_P, _P, _U32, _U32, ctypes.c_int, _P, _P]),
     "kvmret_prefill_score": (ctypes.c_int, [_P, _P, _U32, _U32, _P, _P, _PU32]),
     "kvmret_exchange_export": (ctypes.c_int, [_P, _U32, _P]),
     "kvmret_exchange_import": (ctypes.c_int, [_P, _U32, _U32, _P]),
@@ -784,6 +785,17 @@ def rope_f16(k, out, pos0, n_head_kv, d_head, freq_base=1e6, freq_scale=1.0, str
     """k, out: [n_tok][n_head_kv][d_head] f16 CUDA tensors (torch's current stream)."""
     _check(lib.kvmret_rope_f16(k.data_ptr(), out.data_ptr(), int(k.shape[0]), n_head_kv, d_head,
                                d_head, pos0, freq_base, freq_scale, _torch_stream(stream)))
+
+
+def topk_select(scores, kept, need, tie_higher_id=True, stream=0):
+    """scores: f64 [n], kept: u8 [n] CUDA tensors -> u8 [n] selection flags:
+    every kept block plus the `need` best others (score desc, id by tie rule)."""
+    import torch
+    sel = torch.empty(scores.shape[0], dtype=torch.uint8, device=scores.device)
+    _check(lib.kvmret_topk_select(scores.data_ptr(), kept.data_ptr(), int(scores.shape[0]),
+                                  int(need), int(bool(tie_higher_id)), sel.data_ptr(),
+                                  _torch_stream(stream)))
+    return sel
 
 
 class Lanes:

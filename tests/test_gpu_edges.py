@@ -6,8 +6,9 @@ GPU context:
   empty;
 - fewer blocks than the budget: every block is selected, in order, and the
   window holds them at consecutive bases;
-- more blocks than the shared-memory selector holds (n x 9 bytes > 160 KB):
-  the warp-per-block selector picks exactly the oracle's top-k.
+- more blocks than the selector stages in shared memory (16,384): the radix
+  selection reading the scores from global memory picks exactly the oracle's
+  top-k.
 """
 import numpy as np
 import pytest
@@ -73,7 +74,7 @@ def test_fewer_blocks_than_budget_selects_all():
 
 
 def test_block_count_beyond_the_shared_memory_selector():
-    n_blocks = 20000  # 20000 x 9 bytes > 160 KB: the warp-per-block selector runs
+    n_blocks = 20000  # beyond the 16,384 blocks staged in shared memory
     w = synth.Workload("e2", n_layer=1, n_head=2, n_head_kv=1, d_head=64, block_tokens=16,
                        n_blocks=n_blocks, budget_blocks=64, sink_blocks=1, reserve_blocks=0,
                        n_planted=6, seed=9)
