@@ -334,113 +334,150 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
-// Block-wide radix selection over 128-bit keys that are distinct among the
-// valid ones. The common prefix of all valid keys is skipped first (a min/max
-// reduction), then 8-bit digits are resolved from the top: each pass counts
-// the keys that share the resolved prefix into a shared histogram
-// (warp-aggregated atomics) and one warp finds the digit that holds the k-th
-// smallest key. It stops as soon as every key of that digit is among the k
-// smallest, so a handful of passes settle a few thousand keys. Work is
-// O(n) per pass; the result is a threshold with exactly k valid keys <= it.
-using u128 = unsigned __int128;
-
-struct RadixSmem {
-    u128 wmin[32], wmax[32];
-    u128 prefix, thr;
-    uint32_t hist[256];
+// Block-wide radix selection of the k smallest of a set of u64 keys.
+// Each pass takes the keys still in doubt, skips the bits they all share (a
+// min / max reduction), histograms the next 11 bits (2048 bins in shared
+// memory, warp-aggregated atomics) and keeps only the bin holding the k-th
+// key; keys below it are in, keys above it out. Once the keys in doubt fit
+// the candidate list they are compacted into it, so later passes touch only
+// those (a few after the first pass on spread-out data). Work is O(n) for
+// the first pass; the loop ends when the whole bin is in (exact threshold) or
+// when every key left in doubt is equal (a tie group, for the caller to
+// split by a second key).
+struct SelSmem {
+    uint32_t hist[2048];
+    uint64_t wmin[32], wmax[32];
     uint32_t wcnt[32];
-    uint32_t k, top, done, mode, n_valid;
+    uint64_t mn, mx, thr;
+    uint32_t k, m, listed, mode, n_valid, cnt_new, done;
 };
 
-enum : uint32_t { kSelNone = 0, kSelAll = 1, kSelThr = 2 };
+enum : uint32_t { kSelNone = 0, kSelAll = 1, kSelExact = 2, kSelTie = 3 };
 
-__device__ __forceinline__ u128 shfl_xor128(u128 x, int o) {
-    const uint64_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint64_t>(x), o);
-    const uint64_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint64_t>(x >> 64), o);
-    return (static_cast<u128>(hi) << 64) | lo;
-}
-
-__device__ __forceinline__ uint32_t clz128(u128 x) {
-    const uint64_t hi = static_cast<uint64_t>(x >> 64);
-    return hi ? static_cast<uint32_t>(__clzll(static_cast<long long>(hi)))
-              : 64u + static_cast<uint32_t>(__clzll(static_cast<long long>(static_cast<uint64_t>(x))));
-}
-
-// key_of(i, key) -> bool: false for an invalid i. Every thread of the block
-// calls this; on return rs.mode is kSelNone (k == 0 or no valid key), kSelAll
-// (k >= the valid count) or kSelThr (select valid keys <= rs.thr), and
-// rs.n_valid is the valid count. blockDim.x is a multiple of 32.
-template <class KeyFn>
-__device__ void block_select_smallest(uint32_t n, uint32_t k, KeyFn key_of, RadixSmem &rs) {
-    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    u128 mn = ~static_cast<u128>(0), mx = 0;
-    uint32_t cnt = 0;
-    for (uint32_t i = tid; i < n; i += blockDim.x) {
-        u128 key;
-        if (!key_of(i, key)) continue;
-        mn = key < mn ? key : mn;
-        mx = key > mx ? key : mx;
-        ++cnt;
-    }
+// Block min / max / count of (mn, mx, cnt) into s.mn, s.mx and the return value.
+__device__ __forceinline__ uint32_t block_minmax(uint64_t mn, uint64_t mx, uint32_t cnt,
+                                                 SelSmem &s) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
-        const u128 a = shfl_xor128(mn, o), b = shfl_xor128(mx, o);
+        const uint64_t a = __shfl_xor_sync(0xffffffffu, mn, o);
+        const uint64_t b = __shfl_xor_sync(0xffffffffu, mx, o);
         mn = a < mn ? a : mn;
         mx = b > mx ? b : mx;
         cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
     }
     if (lane == 0) {
-        rs.wmin[warp] = mn;
-        rs.wmax[warp] = mx;
-        rs.wcnt[warp] = cnt;
+        s.wmin[warp] = mn;
+        s.wmax[warp] = mx;
+        s.wcnt[warp] = cnt;
     }
     __syncthreads();
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         for (uint32_t w = 1; w < nw; ++w) {
-            mn = rs.wmin[w] < mn ? rs.wmin[w] : mn;
-            mx = rs.wmax[w] > mx ? rs.wmax[w] : mx;
-            cnt += rs.wcnt[w];
+            mn = s.wmin[w] < mn ? s.wmin[w] : mn;
+            mx = s.wmax[w] > mx ? s.wmax[w] : mx;
+            cnt += s.wcnt[w];
         }
-        rs.n_valid = cnt;
-        rs.done = 1;
-        if (k == 0 || cnt == 0) {
-            rs.mode = kSelNone;
-        } else if (k >= cnt) {
-            rs.mode = kSelAll;
-        } else {  // at least two distinct keys: mn != mx
-            rs.mode = kSelThr;
-            const uint32_t top = 127u - clz128(mn ^ mx);
-            rs.top = top;
-            rs.prefix = top == 127 ? static_cast<u128>(0) : (mn >> (top + 1)) << (top + 1);
-            rs.k = k;
-            rs.done = 0;
-        }
+        s.mn = mn;
+        s.mx = mx;
+        s.wcnt[0] = cnt;
     }
     __syncthreads();
-    while (!rs.done) {
-        const uint32_t top = rs.top, shift = top >= 7 ? top - 7 : 0;
+    const uint32_t total = s.wcnt[0];
+    __syncthreads();  // s.wcnt is reused by the next reduction
+    return total;
+}
+
+// Appends index i to `list` (warp-aggregated slot claim). Every lane of the
+// warp calls it; `take` says whether this lane appends.
+template <class IdxT>
+__device__ __forceinline__ void list_push(bool take, uint32_t i, IdxT *list, uint32_t *count) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t m = __ballot_sync(0xffffffffu, take);
+    if (!m) return;
+    uint32_t base = 0;
+    const uint32_t leader = static_cast<uint32_t>(__ffs(m) - 1);
+    if (lane == leader) base = atomicAdd(count, static_cast<uint32_t>(__popc(m)));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (take) list[base + __popc(m & ((1u << lane) - 1))] = static_cast<IdxT>(i);
+}
+
+// key_of(i, key) -> bool (false: i is not a candidate), i < n. Every thread of
+// the block calls this; blockDim.x is a multiple of 32. `la` / `lb` are two
+// candidate lists of `cap` entries each (cap may be 0). On return s.mode is
+//   kSelNone  (k == 0 or no candidate),
+//   kSelAll   (k >= the candidate count),
+//   kSelExact (exactly k candidates have key <= s.thr), or
+//   kSelTie   (fewer than k have key < s.thr, and the s.k still missing are
+//              to be taken from the keys equal to s.thr),
+// and s.n_valid is the candidate count.
+template <class IdxT, class KeyFn>
+__device__ void block_select_u64(uint32_t n, uint32_t k, KeyFn key_of, IdxT *la, IdxT *lb,
+                                 uint32_t cap, SelSmem &s) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) s.cnt_new = 0;
+    __syncthreads();
+    // pass 0: count, range, and the list when everything fits
+    uint64_t mn = ~0ull, mx = 0;
+    uint32_t cnt = 0;
+    const bool fits_all = n <= cap;
+    for (uint32_t base = 0; base < n; base += blockDim.x) {
+        const uint32_t i = base + tid;
+        uint64_t key = 0;
+        const bool v = i < n && key_of(i, key);
+        if (v) {
+            mn = key < mn ? key : mn;
+            mx = key > mx ? key : mx;
+            ++cnt;
+        }
+        if (fits_all) list_push(v, i, la, &s.cnt_new);
+    }
+    const uint32_t total = block_minmax(mn, mx, cnt, s);
+    if (tid == 0) {
+        s.n_valid = total;
+        s.k = k;
+        s.m = total;
+        s.listed = fits_all ? 1u : 0u;
+        s.done = 1;
+        if (k == 0 || total == 0) s.mode = kSelNone;
+        else if (k >= total) s.mode = kSelAll;
+        else if (s.mn == s.mx) s.mode = kSelTie, s.thr = s.mn;
+        else s.done = 0;
+    }
+    __syncthreads();
+    IdxT *cur = la, *nxt = lb;
+    while (!s.done) {
+        const uint64_t lo = s.mn, hi_k = s.mx;
+        const uint32_t top = 63u - static_cast<uint32_t>(__clzll(static_cast<long long>(lo ^ hi_k)));
+        const uint32_t shift = top >= 10 ? top - 10 : 0;
         const uint32_t nb = 1u << (top - shift + 1);
-        const u128 pre = rs.prefix;
-        for (uint32_t b = tid; b < nb; b += blockDim.x) rs.hist[b] = 0;
+        const uint64_t above = top == 63 ? 0ull : (lo >> (top + 1));  // bits all keys in doubt share
+        const bool listed = s.listed;
+        const uint32_t kk = s.k, m = s.m;
+        for (uint32_t b = tid; b < nb; b += blockDim.x) s.hist[b] = 0;
         __syncthreads();
-        for (uint32_t base = 0; base < n; base += blockDim.x) {  // warp-uniform trip count
-            const uint32_t i = base + tid;
-            u128 key = 0;
-            bool act = i < n && key_of(i, key);
-            if (act && top < 127) act = (key >> (top + 1)) == (pre >> (top + 1));
+        const uint32_t span = listed ? m : n;
+        for (uint32_t base = 0; base < span; base += blockDim.x) {  // warp-uniform trip count
+            const uint32_t j = base + tid;
+            uint64_t key = 0;
+            bool act = false;
+            if (j < span) {
+                act = key_of(listed ? static_cast<uint32_t>(cur[j]) : j, key);
+                if (act && !listed && top < 63) act = (key >> (top + 1)) == above;
+                if (act && !listed) act = key >= lo && key <= hi_k;
+            }
             const uint32_t dg = act ? static_cast<uint32_t>(key >> shift) & (nb - 1) : 0xffffffffu;
             const uint32_t peers = __match_any_sync(0xffffffffu, dg);
             if (act && lane == static_cast<uint32_t>(__ffs(peers) - 1))
-                atomicAdd(&rs.hist[dg], static_cast<uint32_t>(__popc(peers)));
+                atomicAdd(&s.hist[dg], static_cast<uint32_t>(__popc(peers)));
         }
         __syncthreads();
-        if (warp == 0) {
-            uint32_t c[8], sum = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t b = lane * 8 + j;
-                c[j] = b < nb ? rs.hist[b] : 0u;
-                sum += c[j];
+        if (warp == 0) {  // lane L owns bins [L * per, (L + 1) * per)
+            const uint32_t per = (nb + 31) / 32;
+            uint32_t sum = 0;
+            for (uint32_t j = 0; j < per; ++j) {
+                const uint32_t b = lane * per + j;
+                sum += b < nb ? s.hist[b] : 0u;
             }
             uint32_t incl = sum;
 #pragma unroll
@@ -448,38 +485,87 @@ __device__ void block_select_smallest(uint32_t n, uint32_t k, KeyFn key_of, Radi
                 const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= static_cast<uint32_t>(o)) incl += t;
             }
-            const uint32_t kk = rs.k, excl = incl - sum;
+            const uint32_t excl = incl - sum;
             const bool mine = excl < kk && kk <= incl;
             const uint32_t who = static_cast<uint32_t>(__ffs(__ballot_sync(0xffffffffu, mine)) - 1);
             if (who >= 32 && lane == 0) {  // unreachable for fixed keys; ends the loop regardless
-                rs.mode = kSelAll;
-                rs.done = 1;
+                s.mode = kSelAll;
+                s.done = 1;
             }
             if (lane == who) {
-                uint32_t cum = excl, d = lane * 8, cd = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    if (cd == 0 && cum + c[j] >= kk) {
-                        d = lane * 8 + j;
-                        cd = c[j];
-                    } else if (cd == 0) {
-                        cum += c[j];
+                uint32_t cum = excl, d = lane * per, cd = 0;
+                for (uint32_t j = 0; j < per; ++j) {
+                    const uint32_t b = lane * per + j;
+                    const uint32_t c = b < nb ? s.hist[b] : 0u;
+                    if (cum + c >= kk) {
+                        d = b;
+                        cd = c;
+                        break;
                     }
+                    cum += c;
                 }
                 const uint32_t rem = kk - cum;
-                const u128 p = pre | (static_cast<u128>(d) << shift);
-                if (rem == cd || shift == 0) {  // the whole digit is in (shift 0: one key)
-                    rs.thr = p | ((static_cast<u128>(1) << shift) - 1);
-                    rs.done = 1;
-                } else {
-                    rs.prefix = p;
-                    rs.k = rem;
-                    rs.top = shift - 1;
+                const uint64_t pre = (top == 63 ? 0ull : (above << (top + 1))) |
+                                     (static_cast<uint64_t>(d) << shift);
+                if (rem == cd) {  // the whole bin is in
+                    s.mode = kSelExact;
+                    s.thr = pre | ((1ull << shift) - 1);
+                    s.done = 1;
+                } else if (shift == 0) {  // one key value, more copies than needed
+                    s.mode = kSelTie;
+                    s.thr = pre;
+                    s.k = rem;
+                    s.done = 1;
+                } else {  // keep the bin: keys in [pre, pre + 2^shift)
+                    s.k = rem;
+                    s.m = cd;
+                    s.mn = pre;
+                    s.mx = pre | ((1ull << shift) - 1);
                 }
+                s.cnt_new = 0;
             }
         }
         __syncthreads();
+        if (s.done) break;
+        // narrow to the kept bin: its exact range, and the list when it fits
+        const uint64_t blo = s.mn, bhi = s.mx;
+        const bool to_list = s.m <= cap;
+        mn = ~0ull;
+        mx = 0;
+        cnt = 0;
+        for (uint32_t base = 0; base < span; base += blockDim.x) {
+            const uint32_t j = base + tid;
+            uint64_t key = 0;
+            bool act = false;
+            uint32_t i = j;
+            if (j < span) {
+                i = listed ? static_cast<uint32_t>(cur[j]) : j;
+                act = key_of(i, key) && key >= blo && key <= bhi;
+            }
+            if (act) {
+                mn = key < mn ? key : mn;
+                mx = key > mx ? key : mx;
+                ++cnt;
+            }
+            if (to_list) list_push(act, i, nxt, &s.cnt_new);
+        }
+        block_minmax(mn, mx, cnt, s);
+        if (tid == 0) {
+            s.listed = to_list ? 1u : 0u;
+            if (s.mn == s.mx) {  // every key left in doubt is equal
+                s.mode = kSelTie;
+                s.thr = s.mn;
+                s.done = 1;
+            }
+        }
+        if (to_list) {
+            IdxT *t = cur;
+            cur = nxt;
+            nxt = t;
+        }
+        __syncthreads();
     }
+    __syncthreads();
 }
 
 // Order-preserving map of a double onto u64 (-0.0 taken as +0.0, since the
@@ -493,44 +579,64 @@ __device__ __forceinline__ uint64_t score_key(double x) {
 // ---------------------------------------------------------------------------
 // S6: block top-k. Block b (not kept) is chosen iff fewer than `need` other
 // candidates beat it under (score desc, id by tie rule) — the set nth_element
-// returns for that strict total order (kvmem_store.cpp:600-616). One CTA runs
-// a radix selection over the 96-bit keys (score, id): the `need` best
-// candidates are the `need` smallest complemented keys. STAGED keeps the
-// score keys and kept flags in shared memory (n <= kSelectStagedMax).
-constexpr uint32_t kSelectStagedMax = 16384;
+// returns for that strict total order (kvmem_store.cpp:600-616). One CTA: a
+// radix selection of the `need` best scores (smallest complemented keys);
+// when the boundary falls inside a group of equal scores, a second selection
+// over the ids of that group settles it by the tie rule.
+constexpr uint32_t kSelectListCap = 16384;
 
-template <bool STAGED>
 __global__ void __launch_bounds__(1024) select_radix_kernel(const double *__restrict__ scores,
                                                             const uint8_t *__restrict__ kept,
                                                             uint32_t n, uint32_t need, int tie_high,
-                                                            uint8_t *__restrict__ sel) {
+                                                            uint8_t *__restrict__ sel,
+                                                            uint32_t cap) {
     dep_wait();
-    extern __shared__ __align__(16) uint8_t sel_sm[];
-    __shared__ RadixSmem rs;
-    uint64_t *s_key = reinterpret_cast<uint64_t *>(sel_sm);
-    uint8_t *s_kept = sel_sm + static_cast<size_t>(n) * 8;
-    if (STAGED) {
-        for (uint32_t c = threadIdx.x; c < n; c += blockDim.x) {
-            s_key[c] = score_key(scores[c]);
-            s_kept[c] = kept[c];
-        }
-        __syncthreads();
-    }
-    auto key_of = [&](uint32_t i, u128 &key) -> bool {
-        if (STAGED ? s_kept[i] : kept[i]) return false;
-        const uint64_t sk = STAGED ? s_key[i] : score_key(scores[i]);
-        const uint32_t idk = tie_high ? i : ~i;
-        key = ~((static_cast<u128>(sk) << 32) | idk);
+    extern __shared__ __align__(16) uint32_t sel_lists[];
+    __shared__ SelSmem ss;
+    uint32_t *la = sel_lists, *lb = sel_lists + cap;
+    auto skey = [&](uint32_t i) -> uint64_t { return ~score_key(scores[i]); };
+    auto key1 = [&](uint32_t i, uint64_t &key) -> bool {
+        if (kept[i]) return false;
+        key = skey(i);
         return true;
     };
-    block_select_smallest(n, need, key_of, rs);
-    const uint32_t mode = rs.mode;
-    const u128 thr = rs.thr;
+    block_select_u64(n, need, key1, la, lb, cap, ss);
+    const uint32_t mode1 = ss.mode;
+    const uint64_t t1 = ss.thr;
+    const uint32_t k2 = ss.k;
+    uint32_t mode2 = kSelNone;
+    uint64_t t2 = 0;
+    if (mode1 == kSelTie) {  // the boundary group: equal scores, split by id
+        auto key2 = [&](uint32_t i, uint64_t &key) -> bool {
+            if (kept[i] || skey(i) != t1) return false;
+            key = tie_high ? static_cast<uint64_t>(~i) : static_cast<uint64_t>(i);
+            return true;
+        };
+        // the keys below the group are in; the group's k2 best by id join them
+        __syncthreads();
+        block_select_u64(n, k2, key2, la, lb, cap, ss);
+        mode2 = ss.mode;
+        t2 = ss.thr;
+    }
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-        u128 key;
         uint8_t v;
-        if (!key_of(i, key)) v = 1;  // kept
-        else v = mode == kSelAll ? 1 : mode == kSelNone ? 0 : (key <= thr ? 1 : 0);
+        if (kept[i]) {
+            v = 1;
+        } else if (mode1 == kSelAll) {
+            v = 1;
+        } else if (mode1 == kSelNone) {
+            v = 0;
+        } else {
+            const uint64_t key = skey(i);
+            if (mode1 == kSelExact) {
+                v = key <= t1;
+            } else if (key != t1) {
+                v = key < t1;
+            } else {
+                const uint64_t ik = tie_high ? static_cast<uint64_t>(~i) : static_cast<uint64_t>(i);
+                v = mode2 == kSelAll || (mode2 == kSelExact && ik <= t2);
+            }
+        }
         sel[i] = v;
     }
 }
@@ -1900,7 +2006,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     using Scan = cub::BlockScan<uint32_t, kPlanThreads>;
     __shared__ typename Scan::TempStorage ts;
     __shared__ uint32_t s_err, s_mtok, s_ftok;
-    __shared__ RadixSmem rsm;
+    __shared__ SelSmem rsm;
     extern __shared__ __align__(16) uint32_t psm[];
     const uint32_t W = a.win_slots, P = a.pool_slots, tid = threadIdx.x;
     uint32_t *s_ids = psm;
@@ -1996,26 +2102,29 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
             s_cu[s] = (b < 0 || a.sel[b]) ? 0xffffffffu : a.slot_used[s];
         }
         __syncthreads();
-        auto lru_key = [&](uint32_t s, u128 &key) -> bool {
+        auto lru_key = [&](uint32_t s, uint64_t &key) -> bool {
             const uint32_t u = s_cu[s];
             if (u == 0xffffffffu) return false;
-            key = (static_cast<u128>(u) << 32) | s;
+            key = (static_cast<uint64_t>(u) << 32) | s;
             return true;
         };
-        block_select_smallest(P, deficit, lru_key, rsm);
+        // the two candidate lists of the selection (u16 slots) live in s_ev
+        // until the victims are known
+        uint16_t *la = reinterpret_cast<uint16_t *>(s_ev);
+        block_select_u64(P, deficit, lru_key, la, la + P, P, rsm);
         const uint32_t mode = rsm.mode, n_cand = rsm.n_valid;
-        const u128 thr = rsm.thr;
+        const uint64_t thr = rsm.thr;  // keys are distinct: never a tie
         uint32_t ec = 0;
         for (uint32_t s = p0; s < p1; ++s) {
-            u128 key;
-            if (lru_key(s, key) && (mode == kSelAll || (mode == kSelThr && key <= thr))) ++ec;
+            uint64_t key;
+            if (lru_key(s, key) && (mode == kSelAll || (mode >= kSelExact && key <= thr))) ++ec;
         }
         uint32_t erank, n_ev;
         Scan(ts).ExclusiveSum(ec, erank, n_ev);
         __syncthreads();
         for (uint32_t s = p0; s < p1; ++s) {
-            u128 key;
-            if (lru_key(s, key) && (mode == kSelAll || (mode == kSelThr && key <= thr)))
+            uint64_t key;
+            if (lru_key(s, key) && (mode == kSelAll || (mode >= kSelExact && key <= thr)))
                 s_ev[erank++] = s;
         }
         __syncthreads();
@@ -2308,17 +2417,14 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    if (n_blocks <= kSelectStagedMax) {
-        const size_t smem = (static_cast<size_t>(n_blocks) * (sizeof(uint64_t) + 1) + 15) & ~15ull;
-        cudaError_t e = cudaFuncSetAttribute(select_radix_kernel<true>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-        return launch_dep(select_radix_kernel<true>, dim3(1), dim3(1024), smem, st, scores, kept,
-                          n_blocks, need, tie_higher_id, sel);
-    }
-    return launch_dep(select_radix_kernel<false>, dim3(1), dim3(1024), 0, st, scores, kept,
-                      n_blocks, need, tie_higher_id, sel);
+    const uint32_t cap = std::min(n_blocks, kSelectListCap);
+    const size_t smem = 2ull * cap * sizeof(uint32_t);
+    cudaError_t e = cudaFuncSetAttribute(select_radix_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    return launch_dep(select_radix_kernel, dim3(1), dim3(1024), smem, st, scores, kept, n_blocks,
+                      need, tie_higher_id, sel, cap);
 }
 
 cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
