@@ -582,23 +582,54 @@ __device__ __forceinline__ uint64_t score_key(double x) {
 // returns for that strict total order (kvmem_store.cpp:600-616). One CTA: a
 // radix selection of the `need` best scores (smallest complemented keys);
 // when the boundary falls inside a group of equal scores, a second selection
-// over the ids of that group settles it by the tie rule.
+// over the ids of that group settles it by the tie rule. STAGED (n up to
+// kSelectStagedMax): every key is loaded once, all loads in flight, into
+// shared memory (a kept block's key is ~0, which no score maps to), and the
+// passes run from there; beyond it the passes read the scores from global
+// memory.
+constexpr uint32_t kSelectStagedMax = 16384;
 constexpr uint32_t kSelectListCap = 16384;
 
+template <bool STAGED>
 __global__ void __launch_bounds__(1024) select_radix_kernel(const double *__restrict__ scores,
                                                             const uint8_t *__restrict__ kept,
                                                             uint32_t n, uint32_t need, int tie_high,
                                                             uint8_t *__restrict__ sel,
                                                             uint32_t cap) {
     dep_wait();
-    extern __shared__ __align__(16) uint32_t sel_lists[];
+    extern __shared__ __align__(16) uint8_t sel_sm[];
     __shared__ SelSmem ss;
-    uint32_t *la = sel_lists, *lb = sel_lists + cap;
-    auto skey = [&](uint32_t i) -> uint64_t { return ~score_key(scores[i]); };
+    using IdxT = typename std::conditional<STAGED, uint16_t, uint32_t>::type;
+    uint64_t *s_key = reinterpret_cast<uint64_t *>(sel_sm);
+    IdxT *la = reinterpret_cast<IdxT *>(sel_sm + (STAGED ? static_cast<size_t>(n) * 8 : 0));
+    IdxT *lb = la + cap;
+    constexpr uint64_t kKept = ~0ull;
+    if (STAGED) {
+        constexpr uint32_t U = 8;
+        for (uint32_t base = 0; base < n; base += U * blockDim.x) {
+            double v[U];
+            uint8_t kp[U];
+#pragma unroll
+            for (uint32_t u = 0; u < U; ++u) {
+                const uint32_t i = base + u * blockDim.x + threadIdx.x;
+                v[u] = i < n ? scores[i] : 0.0;
+                kp[u] = i < n ? kept[i] : 1;
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < U; ++u) {
+                const uint32_t i = base + u * blockDim.x + threadIdx.x;
+                if (i < n) s_key[i] = kp[u] ? kKept : ~score_key(v[u]);
+            }
+        }
+        __syncthreads();
+    }
+    auto skey = [&](uint32_t i) -> uint64_t {
+        if (STAGED) return s_key[i];
+        return kept[i] ? kKept : ~score_key(scores[i]);
+    };
     auto key1 = [&](uint32_t i, uint64_t &key) -> bool {
-        if (kept[i]) return false;
         key = skey(i);
-        return true;
+        return key != kKept;
     };
     block_select_u64(n, need, key1, la, lb, cap, ss);
     const uint32_t mode1 = ss.mode;
@@ -608,7 +639,7 @@ __global__ void __launch_bounds__(1024) select_radix_kernel(const double *__rest
     uint64_t t2 = 0;
     if (mode1 == kSelTie) {  // the boundary group: equal scores, split by id
         auto key2 = [&](uint32_t i, uint64_t &key) -> bool {
-            if (kept[i] || skey(i) != t1) return false;
+            if (skey(i) != t1) return false;
             key = tie_high ? static_cast<uint64_t>(~i) : static_cast<uint64_t>(i);
             return true;
         };
@@ -619,23 +650,19 @@ __global__ void __launch_bounds__(1024) select_radix_kernel(const double *__rest
         t2 = ss.thr;
     }
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint64_t key = skey(i);
         uint8_t v;
-        if (kept[i]) {
-            v = 1;
-        } else if (mode1 == kSelAll) {
+        if (key == kKept || mode1 == kSelAll) {
             v = 1;
         } else if (mode1 == kSelNone) {
             v = 0;
+        } else if (mode1 == kSelExact) {
+            v = key <= t1;
+        } else if (key != t1) {
+            v = key < t1;
         } else {
-            const uint64_t key = skey(i);
-            if (mode1 == kSelExact) {
-                v = key <= t1;
-            } else if (key != t1) {
-                v = key < t1;
-            } else {
-                const uint64_t ik = tie_high ? static_cast<uint64_t>(~i) : static_cast<uint64_t>(i);
-                v = mode2 == kSelAll || (mode2 == kSelExact && ik <= t2);
-            }
+            const uint64_t ik = tie_high ? static_cast<uint64_t>(~i) : static_cast<uint64_t>(i);
+            v = mode2 == kSelAll || (mode2 == kSelExact && ik <= t2);
         }
         sel[i] = v;
     }
@@ -1190,6 +1217,23 @@ struct FastDiv {
     }
 };
 
+// n / d for every 32-bit n: division by an invariant integer with a
+// multiply-high and a shift (Granlund and Montgomery, 1994): l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, t = mulhi(m, n),
+// n / d = (t + ((n - t) >> 1)) >> (l - 1).
+struct DivU32 {
+    uint32_t m, l;
+    __host__ __device__ explicit DivU32(uint32_t d)
+        : m(0), l(d > 1 ? 32u - static_cast<uint32_t>(__builtin_clz(d - 1)) : 0u) {
+        if (l) m = static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        if (l == 0) return n;
+        const uint32_t t = __umulhi(m, n);
+        return (t + ((n - t) >> 1)) >> (l - 1);
+    }
+};
+
 // Converts the rows of one K segment in place. The row of lane pair r is job
 // row row_base + r (token (row_base + r) / n_head_kv); its cos/sin pairs are
 // tab[(token - tab_tok0) * D/4 + j] (a staged shared-memory slice or the
@@ -1411,8 +1455,10 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 // TMA bulk copies.
 //
 // Work: the flat sequence of items (job, layer, segment) over all fresh jobs,
-// then all moved jobs; a segment is a 16-row K segment (converted) or a
-// same-sized piece of V (copied). Warps take chunks of kQChunk items from two
+// then all moved jobs; a segment is a 16-row K segment (converted) or the
+// layer's whole V part (copied global to global by the warp's lanes, with no
+// stage: V needs no conversion, and one item per V part keeps the per-item
+// bookkeeping off the issue slots). Warps take chunks of kQChunk items from two
 // counters the plan zeroes, so all warps finish together: the first warp of
 // every CTA takes fresh chunks (host-link reads) until none is left and then
 // moved ones, the other warps take moved chunks only, so the host-link reads
@@ -1493,23 +1539,25 @@ struct QItem {
     uint32_t bytes, off, n_rows, is_v;
 };
 
+// Item idx of the sequence: per job, per layer, the nk K segments of SEG
+// bytes, then the layer's whole V part as one item (copied directly).
 template <int D, int KT>
 __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_t n_fresh,
-                                       uint32_t per_job, uint32_t nk, uint32_t n_items_job,
-                                       QItem &it) {
+                                       uint32_t per_job, const DivU32 &div_job, uint32_t nk,
+                                       const DivU32 &div_items, QItem &it) {
     constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
     const AssembleGeom &g = a.g;
     const bool fresh = idx < n_fresh * per_job;
     const uint32_t rel = fresh ? idx : idx - n_fresh * per_job;
-    const uint32_t j = rel / per_job, rem = rel - j * per_job;
-    const uint32_t l = rem / n_items_job, si = rem - l * n_items_job;
+    const uint32_t j = div_job.div(rel), rem = rel - j * per_job;
+    const uint32_t l = div_items.div(rem), si = rem - l * (nk + 1);
     const Job *jp = a.jobs + (fresh ? a.fresh_offset + j : j);
     const uint32_t n_tok = jp->n_tok;
     it.is_v = si >= nk;
-    it.off = (it.is_v ? si - nk : si) * SEG;
+    it.off = it.is_v ? 0u : si * SEG;
     const uint32_t total = n_tok * static_cast<uint32_t>(it.is_v ? g.v_row : g.k_row);
     if (it.off >= total) return false;  // past a partial block's rows
-    it.bytes = min(SEG, total - it.off);
+    it.bytes = it.is_v ? total : min(SEG, total - it.off);
     const uint64_t part = static_cast<uint64_t>(l) * g.unit + (it.is_v ? g.unit_k : 0) + it.off;
     const uint32_t ws = jp->win_slot;
     it.dst = it.is_v ? a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
@@ -1532,7 +1580,8 @@ __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_
 struct QDesc {
     QItem it;
     uint32_t idx;    // item index, kQNone: the sequence has ended
-    uint32_t kind;   // 0 nothing to do, 1 moved (bulk-loaded), 2 fresh (plain loads)
+    uint32_t kind;   // 0 nothing to do, 1 moved K (bulk-loaded), 2 fresh K (plain loads),
+                     // 3 V (copied directly by the warp)
     uint32_t t0;     // first token of a K segment
     uint32_t staged; // its cos/sin rows are in the stage
 };
@@ -1556,8 +1605,8 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
     QDesc *desc = reinterpret_cast<QDesc *>(smem_raw + nwarp * S * (STAGE + 8)) + warp * S;
     const uint32_t T = g.block_tokens;
     const uint32_t nk = (T * static_cast<uint32_t>(g.k_row) + SEG - 1) / SEG;
-    const uint32_t nv = (T * static_cast<uint32_t>(g.v_row) + SEG - 1) / SEG;
-    const uint32_t n_items_job = nk + nv, per_job = g.n_layer * n_items_job;
+    const uint32_t n_items_job = nk + 1, per_job = g.n_layer * n_items_job;
+    const DivU32 div_job(per_job), div_items(n_items_job);
     const uint32_t n_moved = a.counts[0], n_fresh = a.counts[1];
     const uint32_t n_fi = n_fresh * per_job, n_mi = n_moved * per_job;  // items per kind
     const FastDiv hkv(g.n_head_kv);
@@ -1612,10 +1661,15 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         d.kind = 0;
         d.staged = 0;
         d.t0 = 0;
-        if (idx == kQNone || !q_item<D, KT>(a, idx, n_fresh, per_job, nk, n_items_job, d.it))
+        if (idx == kQNone ||
+            !q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items, d.it))
             return;
+        if (d.it.is_v) {
+            d.kind = 3;
+            return;
+        }
         uint32_t tab_bytes = 0;
-        if (!d.it.is_v) {
+        {
             const uint32_t row_base = d.it.off / HEAD_BYTES;
             d.t0 = hkv.div(row_base);
             const uint32_t nt = hkv.div(min(row_base + RPW, d.it.n_rows) - 1) - d.t0 + 1;
@@ -1657,7 +1711,30 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         issue(issued++);
         __syncwarp();
         const uint32_t dk = d.kind;
-        if (dk != 0) {
+        if (dk == 3) {  // V: global to global, 8 x 16 bytes in flight per lane
+            const QItem &it = d.it;
+            const uint4 *sp = reinterpret_cast<const uint4 *>(it.src);
+            uint4 *dp = reinterpret_cast<uint4 *>(it.dst);
+            uint4 *rp = reinterpret_cast<uint4 *>(it.raw);
+            const uint32_t nq = it.bytes / 16;
+            constexpr uint32_t U = 8;
+            uint32_t q0 = 0;
+            for (; q0 + 32 * U <= nq; q0 += 32 * U) {
+                uint4 v[U];
+#pragma unroll
+                for (uint32_t u = 0; u < U; ++u) v[u] = sp[q0 + u * 32 + lane];
+#pragma unroll
+                for (uint32_t u = 0; u < U; ++u) {
+                    dp[q0 + u * 32 + lane] = v[u];
+                    if (rp) rp[q0 + u * 32 + lane] = v[u];
+                }
+            }
+            for (uint32_t q = q0 + lane; q < nq; q += 32) {
+                const uint4 v = sp[q];
+                dp[q] = v;
+                if (rp) rp[q] = v;
+            }
+        } else if (dk != 0) {
             uint8_t *buf = wbuf + s * STAGE;
             const QItem &it = d.it;
             if (dk == 2) {  // fresh: plain loads over the host link, also into the pool
@@ -1677,7 +1754,7 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
                 }
                 phase ^= 1u << s;
             }
-            if (!it.is_v) {
+            {
                 const uint32_t row_base = it.off / HEAD_BYTES;
                 convert_row<D, KT>(buf, lane, min(RPW, it.n_rows - row_base), row_base, hkv,
                                    it.n_rows,
@@ -2417,14 +2494,22 @@ cudaError_t launch_reduce(const double *contrib, const uint8_t *active, uint32_t
 cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_blocks,
                           uint32_t need, int tie_higher_id, uint8_t *sel, cudaStream_t st) {
     if (n_blocks == 0) return cudaSuccess;
-    const uint32_t cap = std::min(n_blocks, kSelectListCap);
-    const size_t smem = 2ull * cap * sizeof(uint32_t);
-    cudaError_t e = cudaFuncSetAttribute(select_radix_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (n_blocks <= kSelectStagedMax) {  // keys (8 B) and two u16 lists per block
+        const size_t smem = static_cast<size_t>(n_blocks) * (8 + 2 * 2);
+        auto kfn = select_radix_kernel<true>;
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        return launch_dep(kfn, dim3(1), dim3(1024), smem, st, scores, kept, n_blocks, need,
+                          tie_higher_id, sel, n_blocks);
+    }
+    const size_t smem = 2ull * kSelectListCap * sizeof(uint32_t);
+    auto kfn = select_radix_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    return launch_dep(select_radix_kernel, dim3(1), dim3(1024), smem, st, scores, kept, n_blocks,
-                      need, tie_higher_id, sel, cap);
+    return launch_dep(kfn, dim3(1), dim3(1024), smem, st, scores, kept, n_blocks, need,
+                      tie_higher_id, sel, kSelectListCap);
 }
 
 cudaError_t launch_assemble(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
