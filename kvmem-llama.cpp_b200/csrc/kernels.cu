@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(128)
 // Block-wide radix selection of the k smallest of a set of u64 keys.
 // Each pass takes the keys still in doubt, skips the bits they all share (a
 // min / max reduction), histograms the next 11 bits (2048 bins in shared
-// memory, warp-aggregated atomics) and keeps only the bin holding the k-th
+// memory) and keeps only the bin holding the k-th
 // key; keys below it are in, keys above it out. Once the keys in doubt fit
 // the candidate list they are compacted into it, so later passes touch only
 // those (a few after the first pass on spread-out data). Work is O(n) for
@@ -349,7 +349,7 @@ struct SelSmem {
     uint64_t wmin[32], wmax[32];
     uint32_t wcnt[32];
     uint64_t mn, mx, thr;
-    uint32_t k, m, listed, mode, n_valid, cnt_new, done;
+    uint32_t k, m, listed, mode, n_valid, cnt_new, done, claimed;
 };
 
 enum : uint32_t { kSelNone = 0, kSelAll = 1, kSelExact = 2, kSelTie = 3 };
@@ -467,16 +467,14 @@ __device__ void block_select_u64(uint32_t n, uint32_t k, KeyFn key_of, IdxT *la,
                 if (act && !listed) act = key >= lo && key <= hi_k;
             }
             const uint32_t dg = act ? static_cast<uint32_t>(key >> shift) & (nb - 1) : 0xffffffffu;
-            const uint32_t peers = __match_any_sync(0xffffffffu, dg);
-            if (act && lane == static_cast<uint32_t>(__ffs(peers) - 1))
-                atomicAdd(&s.hist[dg], static_cast<uint32_t>(__popc(peers)));
+            if (act) atomicAdd(&s.hist[dg], 1u);
         }
         __syncthreads();
-        if (warp == 0) {  // lane L owns bins [L * per, (L + 1) * per)
-            const uint32_t per = (nb + 31) / 32;
+        {  // thread t owns bins [t * per, (t + 1) * per); block-wide prefix sum
+            const uint32_t per = (nb + blockDim.x - 1) / blockDim.x;  // <= 2 at 1024 threads
             uint32_t sum = 0;
             for (uint32_t j = 0; j < per; ++j) {
-                const uint32_t b = lane * per + j;
+                const uint32_t b = tid * per + j;
                 sum += b < nb ? s.hist[b] : 0u;
             }
             uint32_t incl = sum;
@@ -485,17 +483,26 @@ __device__ void block_select_u64(uint32_t n, uint32_t k, KeyFn key_of, IdxT *la,
                 const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= static_cast<uint32_t>(o)) incl += t;
             }
-            const uint32_t excl = incl - sum;
-            const bool mine = excl < kk && kk <= incl;
-            const uint32_t who = static_cast<uint32_t>(__ffs(__ballot_sync(0xffffffffu, mine)) - 1);
-            if (who >= 32 && lane == 0) {  // unreachable for fixed keys; ends the loop regardless
-                s.mode = kSelAll;
-                s.done = 1;
+            if (lane == 31) s.wcnt[warp] = incl;
+            __syncthreads();
+            if (warp == 0) {
+                const uint32_t nw = blockDim.x >> 5;
+                const uint32_t v = lane < nw ? s.wcnt[lane] : 0u;
+                uint32_t wi = v;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+                    if (lane >= static_cast<uint32_t>(o)) wi += t;
+                }
+                if (lane < nw) s.wcnt[lane] = wi - v;  // exclusive prefix of the warps
+                if (lane == 0) s.claimed = 0;
             }
-            if (lane == who) {
-                uint32_t cum = excl, d = lane * per, cd = 0;
+            __syncthreads();
+            const uint32_t excl = s.wcnt[warp] + incl - sum;
+            if (excl < kk && kk <= excl + sum) {  // exactly one thread
+                uint32_t cum = excl, d = tid * per, cd = 0;
                 for (uint32_t j = 0; j < per; ++j) {
-                    const uint32_t b = lane * per + j;
+                    const uint32_t b = tid * per + j;
                     const uint32_t c = b < nb ? s.hist[b] : 0u;
                     if (cum + c >= kk) {
                         d = b;
@@ -523,6 +530,12 @@ __device__ void block_select_u64(uint32_t n, uint32_t k, KeyFn key_of, IdxT *la,
                     s.mx = pre | ((1ull << shift) - 1);
                 }
                 s.cnt_new = 0;
+                s.claimed = 1;
+            }
+            __syncthreads();
+            if (tid == 0 && !s.claimed) {  // unreachable for fixed keys; ends the loop regardless
+                s.mode = kSelAll;
+                s.done = 1;
             }
         }
         __syncthreads();
