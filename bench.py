@@ -594,12 +594,16 @@ def run_ours(args, w):
     H0 = w.n_tokens                   # the history every loop starts from
     quant = w.k_type != kvmret.TYPE_F16
 
+    max_blocks = w.n_blocks + (n_dec + T - 1) // T + 1
+    # --hbm-resident: a pool with a slot for every block (the history is
+    # copied into it before every measured loop)
+    pool_blocks = min(8192, max_blocks + w.reserve_blocks) if args.hbm_resident else 0
     cfg = kvmret.default_config(
         n_layer=Ll, n_head=w.n_head, n_head_kv=w.n_head_kv, d_head=w.d_head, block_tokens=T,
-        max_blocks=w.n_blocks + (n_dec + T - 1) // T + 1, budget_blocks=w.budget_blocks,
+        max_blocks=max_blocks, budget_blocks=w.budget_blocks,
         reserve_blocks=w.reserve_blocks, sink_blocks=w.sink_blocks, k_type=w.k_type,
         v_type=w.v_type, n_rot=w.d_head, freq_base=w.freq_base,
-        pool_cache=int(args.pool_cache), device=local)
+        pool_cache=int(args.pool_cache), pool_blocks=pool_blocks, device=local)
     t_setup = time.perf_counter()
     r = kvmret.Retriever(cfg)
     hist = synth.TorchHistory(w, local, layer0=layer0, n_layer=Ll)
@@ -716,6 +720,7 @@ def run_ours(args, w):
     time.sleep(0.6)
     warm_q = queries(args.warmup)
     warm_ids = []
+    r_cache = [bool(args.pool_cache)]  # the pool's caching mode for the next loop
 
     def restart():
         """Untimed: the start state every measured loop begins from. The
@@ -729,6 +734,8 @@ def run_ours(args, w):
         table_log.append(("truncate", H0))
         r.clear_working_set(drop_pool=True)
         table_log.append(("clear", True))
+        if args.hbm_resident and r_cache[0]:
+            r.pool_prefetch(0, (H0 + T - 1) // T)
         warm_ids.clear()
         for j, q in enumerate(warm_q):
             step(q, dec[j] if decoding else None)
@@ -876,8 +883,10 @@ def run_ours(args, w):
     other = None
     if not args.no_residency_variant:
         r.set_pool_cache(not args.pool_cache)
+        r_cache[0] = not args.pool_cache
         ms_o, ids_o, stats_o, prof_o = timed_loop(qs)
         r.set_pool_cache(args.pool_cache)
+        r_cache[0] = args.pool_cache
         fo = figures(ms_o, stats_o, prof_o)
         other = {"pool_cache": not args.pool_cache,
                  "residency": ("HBM pool keeps evicted blocks in idle slots" if not
@@ -992,6 +1001,13 @@ def run_ours(args, w):
             "setup": {"layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}",
                       "exchange": (args.exchange if world > 1 else None),
                       "pool_cache": bool(args.pool_cache),
+                      "pool_slots": int(pool_blocks or (w.budget_blocks + w.reserve_blocks)),
+                      "residency": ("hbm-resident: a pool slot for every block, the whole "
+                                    "history copied into the HBM pool before each measured "
+                                    "loop (kvmret_pool_prefetch)" if args.hbm_resident else
+                                    "pool of the window's size (budget + reserve slots), "
+                                    "caching evicted blocks in idle slots" if args.pool_cache
+                                    else "only the working set on the GPU"),
                       "decode": ({"tail_blocks": tail, "tokens_per_step": 1,
                                   "note": "the newest tail blocks are this turn's decode "
                                           "blocks, pinned in gen-reserve window slots "
@@ -1426,6 +1442,10 @@ def main():
                          "reference's residency model); by default evicted blocks stay cached "
                          "in otherwise idle pool slots")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--hbm-resident", action="store_true",
+                    help="a pool slot for every block, the whole history copied into the HBM "
+                         "pool before each measured loop (kvmret_pool_prefetch); the default "
+                         "keeps the pool at the window's size")
     ap.add_argument("--decode-tail", type=int, default=64,
                     help="blocks at the end of the history generated in this turn (decode "
                          "blocks pinned in gen-reserve slots)")

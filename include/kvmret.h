@@ -249,6 +249,17 @@ int kvmret_clear_working_set(kvmret_ctx *ctx, int drop_pool);
  * the reference's residency (KvMemRuntime::spill_outgoing,
  * kvmem/src/host/kvmem_runtime.cpp:225-249). Collects any step in flight. */
 int kvmret_set_pool_cache(kvmret_ctx *ctx, int on);
+/* HBM-resident history: copies the stored blocks of [first_block,
+ * first_block + n_blocks) that hold no pool slot into free pool slots (lowest
+ * free slot first, no eviction; stops when the pool is full), so that later
+ * steps move them from HBM instead of reading the host repository. The
+ * placed blocks count as least recently used. Needs pool caching on
+ * (KVMRET_ERR_STATE otherwise); size the pool with kvmret_config.pool_blocks.
+ * Drains the context; the copies are done on return. No reference
+ * counterpart: a residency choice of this library (the reference keeps only
+ * the window on the GPU). */
+int kvmret_pool_prefetch(kvmret_ctx *ctx, uint32_t first_block, uint32_t n_blocks,
+                         uint32_t *n_placed);
 /* llama_kvmem_apply_retrieval (src/adapter/llama-memory-kvmem.cpp:4778-4782,
  * apply_retrieval :4419-4422): preview + apply. ids_out may be NULL. */
 int kvmret_apply_retrieval(kvmret_ctx *ctx, const uint32_t *mandatory, uint32_t n_mandatory,

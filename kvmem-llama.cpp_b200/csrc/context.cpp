@@ -1297,6 +1297,61 @@ int kvmret_set_pool_cache(kvmret_ctx *c, int on) {
     return KVMRET_OK;
 }
 
+int kvmret_pool_prefetch(kvmret_ctx *c, uint32_t first_block, uint32_t n_blocks,
+                         uint32_t *n_placed) {
+    NEED_CTX(c);
+    if (n_placed) *n_placed = 0;
+    if (!c->cfg.pool_cache) return fail(KVMRET_ERR_STATE, "pool prefetch needs pool caching on");
+    GUARD(TRY(drain(c)));
+    CK(cudaStreamSynchronize(c->st));
+    const uint32_t nb = c->live_blocks();
+    const uint32_t b0 = std::min(first_block, nb);
+    const uint32_t b1 = static_cast<uint32_t>(
+        std::min<uint64_t>(nb, static_cast<uint64_t>(first_block) + n_blocks));
+    if (b0 >= b1) return KVMRET_OK;
+    const uint32_t P = c->pool_slots, T = c->cfg.block_tokens;
+    std::vector<int32_t> slot_blk(P), blk_slot(b1 - b0);
+    std::vector<uint32_t> slot_ntok(P), slot_used(P);
+    CK(cudaMemcpy(slot_blk.data(), c->d_slot_blk, P * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(slot_ntok.data(), c->d_slot_ntok, P * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(slot_used.data(), c->d_slot_used, P * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(blk_slot.data(), c->d_blk_slot + b0, blk_slot.size() * 4,
+                  cudaMemcpyDeviceToHost));
+    // lowest free slot first; runs of consecutive blocks in consecutive slots
+    // become one copy
+    struct Run { uint32_t b, s, n; };
+    std::vector<Run> runs;
+    uint32_t s = 0, placed = 0;
+    for (uint32_t b = b0; b < b1; ++b) {
+        if (blk_slot[b - b0] >= 0) continue;
+        while (s < P && slot_blk[s] >= 0) ++s;
+        if (s == P) break;
+        slot_blk[s] = static_cast<int32_t>(b);
+        blk_slot[b - b0] = static_cast<int32_t>(s);
+        slot_ntok[s] = std::min(T, c->live_tokens - b * T);
+        slot_used[s] = 0;  // least recently used: the first to go when room is needed
+        if (!runs.empty() && runs.back().b + runs.back().n == b && runs.back().s + runs.back().n == s)
+            ++runs.back().n;
+        else
+            GUARD(runs.push_back({b, s, 1}));
+        ++placed;
+        ++s;
+    }
+    for (const Run &r : runs)
+        CK(cudaMemcpyAsync(c->pool + static_cast<uint64_t>(r.s) * c->slot_bytes,
+                           c->repo_host + static_cast<uint64_t>(r.b) * c->slot_bytes,
+                           static_cast<uint64_t>(r.n) * c->slot_bytes, cudaMemcpyHostToDevice,
+                           c->st));
+    CK(cudaMemcpyAsync(c->d_slot_blk, slot_blk.data(), P * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->d_slot_ntok, slot_ntok.data(), P * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->d_slot_used, slot_used.data(), P * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->d_blk_slot + b0, blk_slot.data(), blk_slot.size() * 4,
+                       cudaMemcpyHostToDevice, c->st));
+    CK(cudaStreamSynchronize(c->st));  // the host vectors are the copies' sources
+    if (n_placed) *n_placed = placed;
+    return KVMRET_OK;
+}
+
 int kvmret_select_apply_async(kvmret_ctx *c, const uint32_t *mandatory, uint32_t n_mand) {
     NEED_CTX(c);
     if (n_mand && !mandatory) return fail(KVMRET_ERR_ARG, "null mandatory list");

@@ -163,6 +163,7 @@ SIGNATURES = {
     "kvmret_step_collect": (ctypes.c_int, [_P, _PU32, _PU32, ctypes.POINTER(StepStats)]),
     "kvmret_clear_working_set": (ctypes.c_int, [_P, ctypes.c_int]),
     "kvmret_set_pool_cache": (ctypes.c_int, [_P, ctypes.c_int]),
+    "kvmret_pool_prefetch": (ctypes.c_int, [_P, _U32, _U32, _PU32]),
     "kvmret_last_plan": (ctypes.c_int, [_P, _PI32, _PU32, _PU32, _PU32, _PU32, _PU32]),
     "kvmret_window_k": (_P, [_P, _U32]),
     "kvmret_window_v": (_P, [_P, _U32]),
@@ -521,6 +522,14 @@ class Retriever:
         """Residency of the HBM pool for later steps: cache evicted blocks in
         idle slots (True) or keep only the working set (False)."""
         _check(lib.kvmret_set_pool_cache(self.h, int(on)))
+
+    def pool_prefetch(self, first_block=0, n_blocks=None) -> int:
+        """Copy stored blocks without a pool slot into free HBM pool slots
+        (HBM-resident history); returns how many were placed."""
+        n = _U32(0)
+        nb = 0xFFFFFFFF if n_blocks is None else int(n_blocks)
+        _check(lib.kvmret_pool_prefetch(self.h, int(first_block), nb, ctypes.byref(n)))
+        return n.value
 
     def snapshot(self, hashed=True):
         """The conversation as a snapshot archive: (uint8 array, FNV-1a hash)."""
