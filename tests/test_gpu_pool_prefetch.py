@@ -44,6 +44,7 @@ def _steps(r, hist, n_tok, qs, quant):
     for q in qs:
         r.query_reset()
         r.query_add(torch.from_numpy(q.reshape(hist.w.n_layer, 1, -1)).cuda())
+        r.score()
         r.select_apply_async()
         ids, st = r.step_collect()
         assert list(ids) == oracle_ids_tokens(hist, n_tok, q)
