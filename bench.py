@@ -421,7 +421,7 @@ def run_reference(args, w):
 # ). The traffic grows with the blocks a launch moves, so a launch's traffic is
 # this ratio times its algorithmic bytes.
 NCU_TRAFFIC_RATIO = {"assemble_kernel": 1556.8 / 1585.4,
-                     "assemble_quant_kernel": 793.3 / 824.7}
+                     "assemble_quant_tma_kernel": 666.9 / 695.2}
 
 
 class OracleCheck:
@@ -787,7 +787,7 @@ def run_ours(args, w):
         return sum(s[key] for s in ss) / len(ss)
 
     hbm, peak_src = load_peaks()
-    asm_name = "assemble_kernel" if w.k_type == kvmret.TYPE_F16 else "assemble_quant_kernel"
+    asm_name = "assemble_kernel" if w.k_type == kvmret.TYPE_F16 else "assemble_quant_tma_kernel"
 
     def figures(ms_step, stats, prof):
         """Per-step byte counts, the assembly kernel's live roofline and the step roofline."""
@@ -1403,7 +1403,7 @@ def run_lanes(args, w):
                        f"{NL} lanes into this box's host memory",
                        "layers_per_gpu": Ll, "parallelism": f"layer-sharded x{world}, "
                                                             f"{NL} lanes per GPU"},
-            "roofline": {"kernel": "assemble_quant_kernel, all lanes", "bound": "hbm",
+            "roofline": {"kernel": "assemble_quant_tma_kernel, all lanes", "bound": "hbm",
                          "achieved": round(asm_hbm / (asm_ms / 1e3) / 1e9, 1) if asm_ms else 0,
                          "peak": hbm, "unit": "GB/s",
                          "frac": round(asm_hbm / (asm_ms / 1e3) / 1e9 / hbm, 4) if asm_ms

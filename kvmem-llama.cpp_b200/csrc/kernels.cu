@@ -602,6 +602,12 @@ __device__ __forceinline__ uint64_t score_key(double x) {
 // memory.
 constexpr uint32_t kSelectStagedMax = 16384;
 constexpr uint32_t kSelectListCap = 16384;
+#ifndef KVMRET_SEL_SMALL_N
+#define KVMRET_SEL_SMALL_N 4096
+#endif
+#ifndef KVMRET_SEL_SMALL_THREADS
+#define KVMRET_SEL_SMALL_THREADS 1024
+#endif
 
 template <bool STAGED>
 __global__ void __launch_bounds__(1024) select_radix_kernel(const double *__restrict__ scores,
@@ -2513,7 +2519,9 @@ cudaError_t launch_select(const double *scores, const uint8_t *kept, uint32_t n_
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        return launch_dep(kfn, dim3(1), dim3(1024), smem, st, scores, kept, n_blocks, need,
+        // small sets: fewer warps make the block-wide barriers of each pass cheaper
+        const uint32_t threads = n_blocks <= KVMRET_SEL_SMALL_N ? KVMRET_SEL_SMALL_THREADS : 1024;
+        return launch_dep(kfn, dim3(1), dim3(threads), smem, st, scores, kept, n_blocks, need,
                           tie_higher_id, sel, n_blocks);
     }
     const size_t smem = 2ull * kSelectListCap * sizeof(uint32_t);
