@@ -510,6 +510,14 @@ int kvmret_prefill_score(kvmret_ctx *ctx, const uint16_t *q_dev, uint32_t n_tok,
  * pipeline gave up waiting. The prefill scorer's contraction. */
 int kvmret_gemm_f16_nt(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
                        uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, void *stream);
+/* The same with a caller workspace (ws_bytes >= kvmret_gemm_ws_bytes()):
+ * when the 128 x 256 tiles would leave SMs idle, one CTA per SM takes an
+ * equal share of all tiles' k-steps and a second launch adds the partial
+ * tiles (summation order fixed, so results repeat run to run). */
+size_t kvmret_gemm_ws_bytes(void);
+int kvmret_gemm_f16_nt_ws(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
+                          uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, float *ws_dev,
+                          size_t ws_bytes, void *stream);
 /* f16 values -> q8_0 / q4_0 blocks (n_elems a multiple of 32): the quantisers
  * of kvmem_stagein_quantize (src/adapter/llama-kvmem-stagein.cu:181-234,
  * 616-642), used to build quantised cache rows and repository bytes. */

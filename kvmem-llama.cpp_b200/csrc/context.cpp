@@ -150,7 +150,8 @@ struct kvmret_ctx {
     // queries [pf_rows][K] f16; pf_b: unit summaries [pf_nrows][K] f16, rows
     // below mhat_valid current; pf_s: scores [pf_rows][pf_nrows] f32.
     uint16_t *pf_a = nullptr, *pf_b = nullptr;
-    float *pf_s = nullptr;
+    float *pf_s = nullptr, *pf_ws = nullptr;  // pf_ws: the GEMM's split partials
+    size_t pf_ws_bytes = 0;
     uint32_t *pf_err = nullptr;
     uint32_t pf_rows = 0, pf_nrows = 0, mhat_valid = 0;
     // layer-sharded exchange over peer memory (kvmret_exchange_*): one region
@@ -297,7 +298,7 @@ void free_all(kvmret_ctx *c) {
                    c->win_k, c->win_v, c->jobs_dev, c->ops_dev, c->rope_tab, c->d_win_id,
                    c->d_win_base, c->d_blk_slot, c->d_slot_blk, c->d_win_ntok, c->d_blk_ntok,
                    c->d_slot_ntok, c->d_slot_used, c->d_counts, c->d_ids, c->pf_a, c->pf_b,
-                   c->pf_s, c->pf_err, c->d_gen_err};
+                   c->pf_s, c->pf_ws, c->pf_err, c->d_gen_err};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->repo_host) cudaFreeHost(c->repo_host);
@@ -1668,6 +1669,32 @@ int kvmret_gemm_f16_nt(const uint16_t *a, const uint16_t *b, float *c, uint32_t 
     return KVMRET_OK;
 }
 
+size_t kvmret_gemm_ws_bytes(void) {
+    int dev = 0, n_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 0;
+    return kvmret::gemm_ws_bytes(static_cast<uint32_t>(n_sm));
+}
+
+int kvmret_gemm_f16_nt_ws(const uint16_t *a, const uint16_t *b, float *c, uint32_t m, uint32_t n,
+                          uint32_t k, float alpha, uint32_t *err, float *ws, size_t ws_bytes,
+                          void *stream) {
+    if (!a || !b || !c || !ws) return fail(KVMRET_ERR_ARG, "null operand");
+    if ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(ws)) & 15)
+        return fail(KVMRET_ERR_ARG, "gemm output and workspace must be 16-byte aligned");
+    if (m % 128 || n % 256 || k % 64 || k == 0)
+        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
+    const size_t need = kvmret_gemm_ws_bytes();
+    if (need == 0 || ws_bytes < need)
+        return fail(KVMRET_ERR_ARG, "gemm workspace of %zu bytes, %zu needed", ws_bytes, need);
+    CUtensorMap ma, mb;
+    CK(kvmret::make_gemm_maps(a, b, m, n, k, &ma, &mb));
+    CK(kvmret::launch_gemm_f16_nt(ma, mb, c, m, n, k, alpha, err,
+                                  static_cast<cudaStream_t>(stream), ws, ws_bytes));
+    return KVMRET_OK;
+}
+
 int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint32_t top_k,
                          uint8_t *sel, float *scores, uint32_t *n_sel_out) {
     NEED_CTX(c);
@@ -1714,8 +1741,16 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     // the pipeline-timeout word reports on this launch only
     CK(cudaMemsetAsync(c->pf_err, 0, sizeof(uint32_t), c->st));
     const int pr = prof_begin(c, c->st, PR_GEMM);
+    if (!c->pf_ws) {  // the split form's partial tiles (two per SM)
+        int dev = 0, n_sm = 0;
+        CK(cudaGetDevice(&dev));
+        CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        c->pf_ws_bytes = kvmret::gemm_ws_bytes(static_cast<uint32_t>(n_sm));
+        TRY(dmalloc(&c->pf_ws, c->pf_ws_bytes));
+    }
     CK(kvmret::launch_gemm_f16_nt(ma, mb, c->pf_s, rows, n_used, static_cast<uint32_t>(K),
-                                  1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st));
+                                  1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st,
+                                  c->pf_ws, c->pf_ws_bytes));
     prof_end(c, c->st, pr);
     if (c->prof_on) c->prof.gemm_flops += 2.0 * n_tok * nb * static_cast<double>(K);
     CK(kvmret::launch_topk_union(c->pf_s, n_used, n_tok, nb, top_k, c->cfg.tie_higher_id, sel,

@@ -4,8 +4,9 @@
 // queries against every block's normalised summary, all layers and KV heads
 // stacked along K) and is exported on its own as kvmret_gemm_f16_nt.
 //
-// One CTA computes a 128 x 256 tile of C with the accumulator in tensor memory
-// (256 of the SM's 512 TMEM columns, f32). Warp roles:
+// A CTA computes 128 x 256 tiles of C (or k-ranges of them, below) with the
+// accumulator in tensor memory (two 256-column f32 buffers of the SM's 512
+// TMEM columns). Warp roles:
 //   warp 0      TMA producer: 2-D tiled loads of A (128 x 64) and B (256 x 64)
 //               into a 4-stage shared-memory ring, 128-byte swizzle, no
 //               multicast; completion by mbarrier transaction counts;
@@ -30,7 +31,7 @@ constexpr int kTileM = 128, kTileN = 256, kTileK = 64, kStages = 4;
 constexpr uint32_t kStageA = kTileM * kTileK * 2;  // 16 KiB
 constexpr uint32_t kStageB = kTileN * kTileK * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kStageA + kStageB;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
 constexpr uint64_t kWaitNs = 2000000000ull;  // a pipeline wait gives up after 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -125,30 +126,58 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Work split (stream-K): the n_tiles x n_ktiles k-steps of the whole product
+// are cut into gridDim.x equal contiguous ranges, one per CTA, so every SM
+// gets the same amount of tensor work whatever the tile count. A range is a
+// run of segments (tile, k0 .. k1): a segment covering the tile's whole K goes
+// to C scaled by alpha; a partial one (the first or the last of a range) goes
+// unscaled to the CTA's workspace slot (0: first, 1: last) and
+// gemm_fixup_kernel adds the tile's partials in CTA order. With one tile per
+// CTA (gridDim.x == n_tiles) every segment is whole and no workspace is used.
+// The accumulator is double-buffered in TMEM (2 x 256 columns), so the MMAs of
+// a CTA's next segment overlap the epilogue of its previous one.
+__device__ __forceinline__ uint64_t range_begin(uint64_t total, uint32_t g, uint32_t n_cta) {
+    return total * g / n_cta;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_nt_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, float *__restrict__ c,
-                       uint32_t ldc, uint32_t n_ktiles, float alpha, uint32_t *err) {
+                       uint32_t ldc, uint32_t n_ktiles, uint32_t tiles_n, uint32_t n_tiles,
+                       float alpha, float *__restrict__ ws, uint32_t *err) {
     extern __shared__ uint8_t smem_raw[];
     // stages must start on 1024-byte boundaries (the swizzle atom)
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *const smem = smem_raw + (base - raw);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-    // bars[0..S): stage full, bars[S..2S): stage empty, bars[2S]: accumulator ready
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 1);
+    // bars[0..S): stage full, [S..2S): stage empty, [2S, 2S+1]: accumulator b
+    // full, [2S+2, 2S+3]: accumulator b drained by the epilogue
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 4);
     __shared__ uint32_t s_fail;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t m0 = blockIdx.y * kTileM, n0 = blockIdx.x * kTileN;
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
     auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (kStages + s); };
-    const uint32_t acc_bar = bar0 + 8u * (2 * kStages);
+    auto acc_full = [&](uint32_t b) { return bar0 + 8u * (2 * kStages + b); };
+    auto acc_empty = [&](uint32_t b) { return bar0 + 8u * (2 * kStages + 2 + b); };
+    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
+    const uint64_t it0 = range_begin(total, blockIdx.x, gridDim.x);
+    const uint64_t it1 = range_begin(total, blockIdx.x + 1, gridDim.x);
+    // segment of iteration `it`: tile, first and end k-step
+    auto segment = [&](uint64_t it, uint32_t &t, uint32_t &k0, uint32_t &k1) {
+        t = static_cast<uint32_t>(it / n_ktiles);
+        k0 = static_cast<uint32_t>(it - static_cast<uint64_t>(t) * n_ktiles);
+        const uint64_t end = k0 + (it1 - it);
+        k1 = end < n_ktiles ? static_cast<uint32_t>(end) : n_ktiles;
+    };
 
     if (threadIdx.x == 0) {
         s_fail = 0;
-        for (int s = 0; s < 2 * kStages + 1; ++s) mbar_init(bar0 + 8u * s, 1);
+        for (int s = 0; s < 2 * kStages + 2; ++s) mbar_init(bar0 + 8u * s, 1);
+        mbar_init(acc_empty(0), 4);  // one arrival per epilogue warp
+        mbar_init(acc_empty(1), 4);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a))
                      : "memory");
@@ -169,63 +198,116 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {  // producer
-            uint32_t k = 0;
-            for (; k < n_ktiles; ++k) {
-                const uint32_t s = k % kStages, round = k / kStages;
-                if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1u)) break;
-                if (*static_cast<volatile uint32_t *>(&s_fail)) break;
-                const uint32_t sa = base + s * kStageBytes;
-                mbar_expect_tx(full_bar(s), kStageBytes);
-                tma_load_2d(sa, &map_a, static_cast<int32_t>(k * kTileK),
-                            static_cast<int32_t>(m0), full_bar(s));
-                tma_load_2d(sa + kStageA, &map_b, static_cast<int32_t>(k * kTileK),
-                            static_cast<int32_t>(n0), full_bar(s));
+            uint32_t q = 0;  // k-steps issued (the stage ring runs across segments)
+            bool stop = false;
+            for (uint64_t it = it0; it < it1 && !stop;) {
+                uint32_t t, k0, k1;
+                segment(it, t, k0, k1);
+                const int32_t m0 = static_cast<int32_t>((t / tiles_n) * kTileM);
+                const int32_t n0 = static_cast<int32_t>((t % tiles_n) * kTileN);
+                for (uint32_t k = k0; k < k1; ++k) {
+                    const uint32_t s = q % kStages, round = q / kStages;
+                    if ((round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1u)) ||
+                        *static_cast<volatile uint32_t *>(&s_fail)) {
+                        stop = true;
+                        break;
+                    }
+                    const uint32_t sa = base + s * kStageBytes;
+                    mbar_expect_tx(full_bar(s), kStageBytes);
+                    tma_load_2d(sa, &map_a, static_cast<int32_t>(k * kTileK), m0, full_bar(s));
+                    tma_load_2d(sa + kStageA, &map_b, static_cast<int32_t>(k * kTileK), n0,
+                                full_bar(s));
+                    ++q;
+                }
+                it += k1 - k0;
             }
-            if (k < n_ktiles) {  // gave up: drain the loads already issued (bounded)
+            if (stop) {  // gave up: drain the loads already issued (bounded)
                 atomicExch(&s_fail, 1u);
-                for (uint32_t j = (k > kStages ? k - kStages : 0); j < k; ++j)
+                for (uint32_t j = (q > kStages ? q - kStages : 0); j < q; ++j)
                     mbar_wait(full_bar(j % kStages), (j / kStages) & 1u);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            uint32_t k = 0;
-            for (; k < n_ktiles; ++k) {
-                const uint32_t s = k % kStages;
-                if (!mbar_wait(full_bar(s), (k / kStages) & 1u)) break;
-                if (*static_cast<volatile uint32_t *>(&s_fail)) break;
+            uint32_t q = 0, j = 0;
+            bool stop = false;
+            for (uint64_t it = it0; it < it1 && !stop; ++j) {
+                uint32_t t, k0, k1;
+                segment(it, t, k0, k1);
+                const uint32_t b = j & 1u;
+                // the epilogue has drained this buffer's previous segment
+                if (j >= 2 && !mbar_wait(acc_empty(b), ((j >> 1) - 1) & 1u)) {
+                    stop = true;
+                    break;
+                }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t sa = base + s * kStageBytes;
-                const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kStageA);
+                const uint32_t acc = tmem + b * kTileN;
+                for (uint32_t k = k0; k < k1; ++k) {
+                    const uint32_t s = q % kStages;
+                    if (!mbar_wait(full_bar(s), (q / kStages) & 1u) ||
+                        *static_cast<volatile uint32_t *>(&s_fail)) {
+                        stop = true;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t sa = base + s * kStageBytes;
+                    const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kStageA);
 #pragma unroll
-                for (uint32_t kk = 0; kk < kTileK / 16; ++kk)  // +32 bytes per K = 16 slice
-                    mma_f16(tmem, da + 2 * kk, db + 2 * kk, (k | kk) != 0);
-                mma_commit(empty_bar(s));
+                    for (uint32_t kk = 0; kk < kTileK / 16; ++kk)  // +32 bytes per K = 16 slice
+                        mma_f16(acc, da + 2 * kk, db + 2 * kk, (k != k0 || kk != 0) ? 1u : 0u);
+                    mma_commit(empty_bar(s));
+                    ++q;
+                }
+                // arrives once every MMA issued above has completed (on a stop
+                // too, so the epilogue wakes and sees the failure)
+                mma_commit(acc_full(b));
+                it += k1 - k0;
             }
-            if (k < n_ktiles) atomicExch(&s_fail, 1u);
-            mma_commit(acc_bar);  // arrives once every MMA issued above has completed
+            if (stop) atomicExch(&s_fail, 1u);
         }
     } else {  // epilogue, warps 2..5
-        const uint32_t q = warp & 3u;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0));
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (ok && !*static_cast<volatile uint32_t *>(&s_fail)) {
-            const uint32_t row = m0 + 32 * q + lane;
-            float *crow = c + static_cast<size_t>(row) * ldc + n0;
+        const uint32_t qd = warp & 3u;
+        uint32_t j = 0;
+        for (uint64_t it = it0; it < it1; ++j) {
+            uint32_t t, k0, k1;
+            segment(it, t, k0, k1);
+            const uint32_t b = j & 1u;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full(b), (j >> 1) & 1u));
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (!ok || *static_cast<volatile uint32_t *>(&s_fail)) {
+                if (lane == 0) atomicExch(&s_fail, 1u);
+                break;
+            }
+            const bool whole = k0 == 0 && k1 == n_ktiles;
+            const uint32_t r = 32 * qd + lane;
+            float *dst_row;
+            float scale = alpha;
+            if (whole) {
+                dst_row = c + static_cast<size_t>((t / tiles_n) * kTileM + r) * ldc +
+                          (t % tiles_n) * kTileN;
+            } else {  // slot 0: the range's first segment, 1: its last
+                const uint32_t slot = 2 * blockIdx.x + (it == it0 ? 0u : 1u);
+                dst_row = ws + (static_cast<size_t>(slot) * kTileM + r) * kTileN;
+                scale = 1.0f;
+            }
 #pragma unroll 1
             for (uint32_t col = 0; col < kTileN; col += 32) {
                 uint32_t v[32];
-                tmem_ld32(tmem + ((32 * q) << 16) + col, v);
-                float4 *dst = reinterpret_cast<float4 *>(crow + col);
+                tmem_ld32(tmem + ((32 * qd) << 16) + b * kTileN + col, v);
+                float4 *dst = reinterpret_cast<float4 *>(dst_row + col);
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    dst[j] = make_float4(alpha * __uint_as_float(v[4 * j]),
-                                         alpha * __uint_as_float(v[4 * j + 1]),
-                                         alpha * __uint_as_float(v[4 * j + 2]),
-                                         alpha * __uint_as_float(v[4 * j + 3]));
+                for (int e = 0; e < 8; ++e)
+                    dst[e] = make_float4(scale * __uint_as_float(v[4 * e]),
+                                         scale * __uint_as_float(v[4 * e + 1]),
+                                         scale * __uint_as_float(v[4 * e + 2]),
+                                         scale * __uint_as_float(v[4 * e + 3]));
             }
-        } else if (lane == 0) {
-            atomicExch(&s_fail, 1u);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acc_empty(b))
+                             : "memory");
+            it += k1 - k0;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -236,6 +318,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(kTmemCols)
                      : "memory");
+    }
+}
+
+// C tile of a tile split over several CTAs: alpha x (the CTAs' partials,
+// added in CTA order). One CTA per tile; tiles held whole by one CTA return.
+__global__ void __launch_bounds__(256)
+    gemm_fixup_kernel(float *__restrict__ c, uint32_t ldc, const float *__restrict__ ws,
+                      uint32_t n_ktiles, uint32_t tiles_n, uint32_t n_tiles, uint32_t n_cta,
+                      float alpha, const uint32_t *err) {
+    if (err && *err) return;  // the product gave up: C is not valid anyway
+    const uint32_t t = blockIdx.x;
+    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
+    const uint64_t a = static_cast<uint64_t>(t) * n_ktiles, z = a + n_ktiles - 1;
+    // the CTAs whose ranges hold k-steps a and z
+    auto owner = [&](uint64_t it) {
+        const uint64_t guess = it * n_cta / total;
+        uint32_t g = guess < n_cta - 1 ? static_cast<uint32_t>(guess) : n_cta - 1;
+        while (g + 1 < n_cta && range_begin(total, g + 1, n_cta) <= it) ++g;
+        while (g > 0 && range_begin(total, g, n_cta) > it) --g;
+        return g;
+    };
+    const uint32_t g0 = owner(a), g1 = owner(z);
+    if (g0 == g1) return;
+    const uint32_t m0 = (t / tiles_n) * kTileM, n0 = (t % tiles_n) * kTileN;
+    for (uint32_t e = threadIdx.x; e < kTileM * kTileN / 4; e += blockDim.x) {
+        const uint32_t r = e / (kTileN / 4), c4 = e % (kTileN / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t g = g0; g <= g1; ++g) {
+            const uint32_t slot = 2 * g + (range_begin(total, g, n_cta) >= a ? 0u : 1u);
+            const float4 p = reinterpret_cast<const float4 *>(
+                ws + (static_cast<size_t>(slot) * kTileM + r) * kTileN)[c4];
+            acc.x += p.x;
+            acc.y += p.y;
+            acc.z += p.z;
+            acc.w += p.w;
+        }
+        reinterpret_cast<float4 *>(c + static_cast<size_t>(m0 + r) * ldc + n0)[c4] =
+            make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
     }
 }
 
@@ -287,21 +407,42 @@ cudaError_t make_gemm_maps(const void *a, const void *b, uint32_t m, uint32_t n,
 
 size_t gemm_smem_bytes() {
     return kStages * static_cast<size_t>(kStageBytes) + 1024 /* alignment */ +
-           (2 * kStages + 1) * 8 + 16;
+           (2 * kStages + 4) * 8 + 16;
+}
+
+size_t gemm_ws_bytes(uint32_t n_cta) {
+    return 2ull * n_cta * kTileM * kTileN * sizeof(float);
 }
 
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
                                uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
-                               cudaStream_t st) {
+                               cudaStream_t st, float *ws, size_t ws_bytes) {
     if (m % kTileM || n % kTileN || k % kTileK || k == 0) return cudaErrorInvalidValue;
     const size_t smem = gemm_smem_bytes();
     cudaError_t e = cudaFuncSetAttribute(gemm_f16_nt_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const dim3 grid(n / kTileN, m / kTileM);
-    gemm_f16_nt_kernel<<<grid, kGemmThreads, smem, st>>>(map_a, map_b, c, n, k / kTileK, alpha,
-                                                          err);
+    const uint32_t tiles_n = n / kTileN, n_tiles = tiles_n * (m / kTileM), n_ktiles = k / kTileK;
+    // one CTA per SM with an equal share of the k-steps when the tiles would
+    // leave SMs idle in the last wave and a workspace is given; else a tile
+    // per CTA
+    int dev = 0, n_sm = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    uint32_t grid = n_tiles;
+    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
+    if (ws && n_sm > 0 && n_tiles % static_cast<uint32_t>(n_sm) != 0 &&
+        n_tiles < 4u * static_cast<uint32_t>(n_sm) && total >= static_cast<uint64_t>(n_sm) &&
+        ws_bytes >= gemm_ws_bytes(static_cast<uint32_t>(n_sm)))
+        grid = static_cast<uint32_t>(n_sm);
+    gemm_f16_nt_kernel<<<grid, kGemmThreads, smem, st>>>(map_a, map_b, c, n, n_ktiles, tiles_n,
+                                                          n_tiles, alpha, ws, err);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || grid == n_tiles) return e;
+    gemm_fixup_kernel<<<n_tiles, 256, 0, st>>>(c, n, ws, n_ktiles, tiles_n, n_tiles, grid, alpha,
+                                               err);
     return cudaGetLastError();
 }
 

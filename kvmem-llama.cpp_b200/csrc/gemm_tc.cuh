@@ -13,9 +13,15 @@
 namespace kvmret {
 
 size_t gemm_smem_bytes();
+// Workspace of the split (stream-K) form for n_cta CTAs: two 128 x 256 f32
+// partial tiles per CTA.
+size_t gemm_ws_bytes(uint32_t n_cta);
+// With a workspace of at least gemm_ws_bytes(SM count), a product whose tiles
+// would leave SMs idle runs as one CTA per SM over equal shares of the
+// k-steps plus a fix-up launch; otherwise one tile per CTA.
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
                                uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
-                               cudaStream_t st);
+                               cudaStream_t st, float *ws = nullptr, size_t ws_bytes = 0);
 // Encodes the two tensor maps (driver entry point looked up once).
 cudaError_t make_gemm_maps(const void *a, const void *b, uint32_t m, uint32_t n, uint32_t k,
                            CUtensorMap *map_a, CUtensorMap *map_b);

@@ -39,6 +39,25 @@ def test_gemm_matches_float64(m, n, k):
     assert torch.all((c.double().cpu() - ref).abs() <= bound)
 
 
+@pytest.mark.parametrize("m,n,k", [(128, 768, 8192), (2048, 2048, 4096), (256, 512, 64)])
+def test_split_gemm_matches_float64(m, n, k):
+    """The workspace form: tiles that leave SMs idle are split over one CTA per
+    SM by k-steps and the partials added by the fix-up launch; same bound, and
+    the same result on a second run."""
+    g = torch.Generator(device="cuda").manual_seed(m * 3 + n + k)
+    a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).half()
+    b = (torch.randn(n, k, device="cuda", generator=g) * 0.5).half()
+    c, err = kvmret.gemm_f16_nt_split(a, b, alpha=0.5)
+    c2, err2 = kvmret.gemm_f16_nt_split(a, b, alpha=0.5)
+    torch.cuda.synchronize()
+    assert int(err[0]) == 0 and int(err2[0]) == 0
+    assert torch.equal(c, c2)
+    a64, b64 = a.double().cpu(), b.double().cpu()
+    ref = 0.5 * (a64 @ b64.T)
+    bound = 0.5 * (a64.abs() @ b64.abs().T) * 2e-6 + 1e-6
+    assert torch.all((c.double().cpu() - ref).abs() <= bound)
+
+
 def _oracle_scores(hist, q, w, n_tokens):
     """float64: mean over (layer, KV head) of cos(group query of token t, summary of b),
     the summary being the mean key of the block's appended tokens."""
