@@ -17,7 +17,7 @@ size_t gemm_smem_bytes();
 // partial tiles per CTA.
 size_t gemm_ws_bytes(uint32_t n_cta);
 // With a workspace of at least gemm_ws_bytes(SM count), a product whose tiles
-// would leave SMs idle runs as one CTA per SM over equal shares of the
+// fill at most half the SMs runs as one CTA per SM over equal shares of the
 // k-steps plus a fix-up launch; otherwise one tile per CTA.
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
                                uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
