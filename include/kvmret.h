@@ -510,12 +510,13 @@ int kvmret_prefill_score(kvmret_ctx *ctx, const uint16_t *q_dev, uint32_t n_tok,
  * pipeline gave up waiting. The prefill scorer's contraction. */
 int kvmret_gemm_f16_nt(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
                        uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, void *stream);
-/* The same with a caller workspace (ws_bytes >= kvmret_gemm_ws_bytes()):
- * when the 128 x 256 tiles fill at most half the SMs, one CTA per SM takes an
- * equal share of all tiles' k-steps and a second launch adds the partial
- * tiles (summation order fixed, so results repeat run to run); larger
- * products run a tile per CTA, whose lockstep k-slices share L2. */
-size_t kvmret_gemm_ws_bytes(void);
+/* The same with a caller workspace of kvmret_gemm_ws_bytes(m, n, k) bytes
+ * (0: none needed, ws_dev may be NULL). When the 128 x 256 tiles would leave
+ * SMs idle, the grid is one CTA per SM: a CTA per tile runs the first k-steps
+ * of its tile in lockstep with the others (the k-slices of A and B shared in
+ * L2), the remaining CTAs split the k tails of all tiles, and a second launch
+ * adds the pieces in a fixed order, so results repeat run to run. */
+size_t kvmret_gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k);
 int kvmret_gemm_f16_nt_ws(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
                           uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, float *ws_dev,
                           size_t ws_bytes, void *stream);

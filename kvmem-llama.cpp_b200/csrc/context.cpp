@@ -1669,24 +1669,20 @@ int kvmret_gemm_f16_nt(const uint16_t *a, const uint16_t *b, float *c, uint32_t 
     return KVMRET_OK;
 }
 
-size_t kvmret_gemm_ws_bytes(void) {
-    int dev = 0, n_sm = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return 0;
-    return kvmret::gemm_ws_bytes(static_cast<uint32_t>(n_sm));
+size_t kvmret_gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k) {
+    return kvmret::gemm_ws_bytes(m, n, k);
 }
 
 int kvmret_gemm_f16_nt_ws(const uint16_t *a, const uint16_t *b, float *c, uint32_t m, uint32_t n,
                           uint32_t k, float alpha, uint32_t *err, float *ws, size_t ws_bytes,
                           void *stream) {
-    if (!a || !b || !c || !ws) return fail(KVMRET_ERR_ARG, "null operand");
+    if (!a || !b || !c) return fail(KVMRET_ERR_ARG, "null operand");
     if ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(ws)) & 15)
         return fail(KVMRET_ERR_ARG, "gemm output and workspace must be 16-byte aligned");
     if (m % 128 || n % 256 || k % 64 || k == 0)
         return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
-    const size_t need = kvmret_gemm_ws_bytes();
-    if (need == 0 || ws_bytes < need)
+    const size_t need = kvmret::gemm_ws_bytes(m, n, k);
+    if (need && (!ws || ws_bytes < need))
         return fail(KVMRET_ERR_ARG, "gemm workspace of %zu bytes, %zu needed", ws_bytes, need);
     CUtensorMap ma, mb;
     CK(kvmret::make_gemm_maps(a, b, m, n, k, &ma, &mb));
@@ -1741,12 +1737,13 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
     // the pipeline-timeout word reports on this launch only
     CK(cudaMemsetAsync(c->pf_err, 0, sizeof(uint32_t), c->st));
     const int pr = prof_begin(c, c->st, PR_GEMM);
-    if (!c->pf_ws) {  // the split form's partial tiles (two per SM)
-        int dev = 0, n_sm = 0;
-        CK(cudaGetDevice(&dev));
-        CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-        c->pf_ws_bytes = kvmret::gemm_ws_bytes(static_cast<uint32_t>(n_sm));
-        TRY(dmalloc(&c->pf_ws, c->pf_ws_bytes));
+    const size_t ws_need = kvmret::gemm_ws_bytes(rows, n_used, static_cast<uint32_t>(K));
+    if (ws_need > c->pf_ws_bytes) {  // the split form's partial tiles
+        if (c->pf_ws) cudaFree(c->pf_ws);
+        c->pf_ws = nullptr;
+        c->pf_ws_bytes = 0;
+        TRY(dmalloc(&c->pf_ws, ws_need));
+        c->pf_ws_bytes = ws_need;
     }
     CK(kvmret::launch_gemm_f16_nt(ma, mb, c->pf_s, rows, n_used, static_cast<uint32_t>(K),
                                   1.0f / static_cast<float>(L * Hkv), c->pf_err, c->st,

@@ -23,6 +23,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace kvmret {
 namespace {
 
@@ -126,25 +128,95 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Work split (stream-K): the n_tiles x n_ktiles k-steps of the whole product
-// are cut into gridDim.x equal contiguous ranges, one per CTA, so every SM
-// gets the same amount of tensor work whatever the tile count. A range is a
-// run of segments (tile, k0 .. k1): a segment covering the tile's whole K goes
-// to C scaled by alpha; a partial one (the first or the last of a range) goes
-// unscaled to the CTA's workspace slot (0: first, 1: last) and
-// gemm_fixup_kernel adds the tile's partials in CTA order. With one tile per
-// CTA (gridDim.x == n_tiles) every segment is whole and no workspace is used.
-// The accumulator is double-buffered in TMEM (2 x 256 columns), so the MMAs of
-// a CTA's next segment overlap the epilogue of its previous one.
-__device__ __forceinline__ uint64_t range_begin(uint64_t total, uint32_t g, uint32_t n_cta) {
-    return total * g / n_cta;
+// Work split. With one tile per CTA (x == n_ktiles, gridDim.x == n_tiles)
+// every CTA runs its tile's whole K and writes C. When the tiles would leave
+// SMs idle (n_tiles < SM count) the grid is one CTA per SM: CTA g < n_tiles
+// (a "main" CTA) runs k-steps [0, x) of tile g, all main CTAs in lockstep so
+// each k-slice of A and B is shared in L2 as in the one-tile form, and writes
+// its raw sums into C; the remaining H CTAs ("helpers") split the tails
+// [x, n_ktiles) of all tiles, in tile order, into equal contiguous ranges and
+// write each piece raw into the workspace slot (tile, piece); then
+// gemm_fixup_kernel sets C = alpha * (C + the tile's pieces in order), so the
+// result does not depend on timing. x = total k-steps / SM count, so every
+// SM gets the same share. The accumulator is double-buffered in TMEM
+// (2 x 256 columns): the MMAs of a helper's next piece overlap the epilogue
+// of its previous one.
+struct GemmSplit {
+    uint32_t n_ktiles, tiles_n, n_tiles;
+    uint32_t x;      // k-steps of a main CTA; n_ktiles: one tile per CTA
+    uint32_t helpers, pieces;  // helper CTAs; workspace slots per tile
+};
+
+__device__ __forceinline__ uint64_t range_begin(uint64_t total, uint32_t g, uint32_t n) {
+    return total * g / n;
 }
+// the helper whose tail range holds tail k-step j
+__device__ __forceinline__ uint32_t tail_owner(uint64_t j, uint64_t total, uint32_t n) {
+    const uint64_t guess = j * n / total;
+    uint32_t h = guess < n - 1 ? static_cast<uint32_t>(guess) : n - 1;
+    while (h + 1 < n && range_begin(total, h + 1, n) <= j) ++h;
+    while (h > 0 && range_begin(total, h, n) > j) --h;
+    return h;
+}
+
+// One CTA's run of segments (tile, k0 .. k1) and where each one goes.
+struct SegWalk {
+    GemmSplit sp;
+    uint32_t role;   // 0: a tile per CTA, 1: main, 2: helper
+    uint64_t it, it1, tail_total;
+    uint32_t h;
+    __device__ SegWalk(const GemmSplit &s, uint32_t g) : sp(s) {
+        if (sp.x == sp.n_ktiles) {
+            role = 0;
+            it = static_cast<uint64_t>(g) * sp.n_ktiles;
+            it1 = it + sp.n_ktiles;
+        } else if (g < sp.n_tiles) {
+            role = 1;
+            it = 0;
+            it1 = sp.x;
+        } else {
+            role = 2;
+            h = g - sp.n_tiles;
+            tail_total = static_cast<uint64_t>(sp.n_tiles) * (sp.n_ktiles - sp.x);
+            it = range_begin(tail_total, h, sp.helpers);
+            it1 = range_begin(tail_total, h + 1, sp.helpers);
+        }
+    }
+    __device__ bool more() const { return it < it1; }
+    // the current segment; kind 0: C scaled, 1: C raw, 2: workspace slot
+    __device__ void get(uint32_t &t, uint32_t &k0, uint32_t &k1, uint32_t &kind,
+                        uint32_t &slot) const {
+        slot = 0;
+        if (role == 0) {
+            t = static_cast<uint32_t>(it / sp.n_ktiles);
+            k0 = 0;
+            k1 = sp.n_ktiles;
+            kind = 0;
+        } else if (role == 1) {
+            t = blockIdx.x;
+            k0 = 0;
+            k1 = sp.x;
+            kind = 1;
+        } else {
+            const uint32_t L = sp.n_ktiles - sp.x;
+            t = static_cast<uint32_t>(it / L);
+            const uint32_t off = static_cast<uint32_t>(it - static_cast<uint64_t>(t) * L);
+            const uint64_t len = it1 - it < L - off ? it1 - it : L - off;
+            k0 = sp.x + off;
+            k1 = k0 + static_cast<uint32_t>(len);
+            kind = 2;
+            slot = t * sp.pieces +
+                   (h - tail_owner(static_cast<uint64_t>(t) * L, tail_total, sp.helpers));
+        }
+    }
+    __device__ void next(uint32_t k0, uint32_t k1) { it += k1 - k0; }
+};
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_nt_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, float *__restrict__ c,
-                       uint32_t ldc, uint32_t n_ktiles, uint32_t tiles_n, uint32_t n_tiles,
-                       float alpha, float *__restrict__ ws, uint32_t *err) {
+                       uint32_t ldc, const __grid_constant__ GemmSplit sp, float alpha,
+                       float *__restrict__ ws, uint32_t *err) {
     extern __shared__ uint8_t smem_raw[];
     // stages must start on 1024-byte boundaries (the swizzle atom)
     const uint32_t raw = smem_u32(smem_raw);
@@ -162,16 +234,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (kStages + s); };
     auto acc_full = [&](uint32_t b) { return bar0 + 8u * (2 * kStages + b); };
     auto acc_empty = [&](uint32_t b) { return bar0 + 8u * (2 * kStages + 2 + b); };
-    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
-    const uint64_t it0 = range_begin(total, blockIdx.x, gridDim.x);
-    const uint64_t it1 = range_begin(total, blockIdx.x + 1, gridDim.x);
-    // segment of iteration `it`: tile, first and end k-step
-    auto segment = [&](uint64_t it, uint32_t &t, uint32_t &k0, uint32_t &k1) {
-        t = static_cast<uint32_t>(it / n_ktiles);
-        k0 = static_cast<uint32_t>(it - static_cast<uint64_t>(t) * n_ktiles);
-        const uint64_t end = k0 + (it1 - it);
-        k1 = end < n_ktiles ? static_cast<uint32_t>(end) : n_ktiles;
-    };
+    const uint32_t tiles_n = sp.tiles_n;
 
     if (threadIdx.x == 0) {
         s_fail = 0;
@@ -200,9 +263,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {  // producer
             uint32_t q = 0;  // k-steps issued (the stage ring runs across segments)
             bool stop = false;
-            for (uint64_t it = it0; it < it1 && !stop;) {
-                uint32_t t, k0, k1;
-                segment(it, t, k0, k1);
+            for (SegWalk sw(sp, blockIdx.x); sw.more() && !stop;) {
+                uint32_t t, k0, k1, kind, slot;
+                sw.get(t, k0, k1, kind, slot);
                 const int32_t m0 = static_cast<int32_t>((t / tiles_n) * kTileM);
                 const int32_t n0 = static_cast<int32_t>((t % tiles_n) * kTileN);
                 for (uint32_t k = k0; k < k1; ++k) {
@@ -219,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 full_bar(s));
                     ++q;
                 }
-                it += k1 - k0;
+                sw.next(k0, k1);
             }
             if (stop) {  // gave up: drain the loads already issued (bounded)
                 atomicExch(&s_fail, 1u);
@@ -231,9 +294,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {  // MMA issuer
             uint32_t q = 0, j = 0;
             bool stop = false;
-            for (uint64_t it = it0; it < it1 && !stop; ++j) {
-                uint32_t t, k0, k1;
-                segment(it, t, k0, k1);
+            for (SegWalk sw(sp, blockIdx.x); sw.more() && !stop; ++j) {
+                uint32_t t, k0, k1, kind, slot;
+                sw.get(t, k0, k1, kind, slot);
                 const uint32_t b = j & 1u;
                 // the epilogue has drained this buffer's previous segment
                 if (j >= 2 && !mbar_wait(acc_empty(b), ((j >> 1) - 1) & 1u)) {
@@ -261,16 +324,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // arrives once every MMA issued above has completed (on a stop
                 // too, so the epilogue wakes and sees the failure)
                 mma_commit(acc_full(b));
-                it += k1 - k0;
+                sw.next(k0, k1);
             }
             if (stop) atomicExch(&s_fail, 1u);
         }
     } else {  // epilogue, warps 2..5
         const uint32_t qd = warp & 3u;
         uint32_t j = 0;
-        for (uint64_t it = it0; it < it1; ++j) {
-            uint32_t t, k0, k1;
-            segment(it, t, k0, k1);
+        for (SegWalk sw(sp, blockIdx.x); sw.more(); ++j) {
+            uint32_t t, k0, k1, kind, slot;
+            sw.get(t, k0, k1, kind, slot);
             const uint32_t b = j & 1u;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full(b), (j >> 1) & 1u));
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -278,18 +341,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (lane == 0) atomicExch(&s_fail, 1u);
                 break;
             }
-            const bool whole = k0 == 0 && k1 == n_ktiles;
             const uint32_t r = 32 * qd + lane;
             float *dst_row;
-            float scale = alpha;
-            if (whole) {
+            const float scale = kind == 0 ? alpha : 1.0f;
+            if (kind < 2)
                 dst_row = c + static_cast<size_t>((t / tiles_n) * kTileM + r) * ldc +
                           (t % tiles_n) * kTileN;
-            } else {  // slot 0: the range's first segment, 1: its last
-                const uint32_t slot = 2 * blockIdx.x + (it == it0 ? 0u : 1u);
+            else
                 dst_row = ws + (static_cast<size_t>(slot) * kTileM + r) * kTileN;
-                scale = 1.0f;
-            }
 #pragma unroll 1
             for (uint32_t col = 0; col < kTileN; col += 32) {
                 uint32_t v[32];
@@ -307,7 +366,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0)
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acc_empty(b))
                              : "memory");
-            it += k1 - k0;
+            sw.next(k0, k1);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -321,41 +380,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 }
 
-// C tile of a tile split over several CTAs: alpha x (the CTAs' partials,
-// added in CTA order). One CTA per tile; tiles held whole by one CTA return.
+// C = alpha * (the main CTA's sums in C + the helpers' pieces of the tile, in
+// order). One CTA per tile.
 __global__ void __launch_bounds__(256)
     gemm_fixup_kernel(float *__restrict__ c, uint32_t ldc, const float *__restrict__ ws,
-                      uint32_t n_ktiles, uint32_t tiles_n, uint32_t n_tiles, uint32_t n_cta,
-                      float alpha, const uint32_t *err) {
+                      const __grid_constant__ GemmSplit sp, float alpha, const uint32_t *err) {
     if (err && *err) return;  // the product gave up: C is not valid anyway
-    const uint32_t t = blockIdx.x;
-    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
-    const uint64_t a = static_cast<uint64_t>(t) * n_ktiles, z = a + n_ktiles - 1;
-    // the CTAs whose ranges hold k-steps a and z
-    auto owner = [&](uint64_t it) {
-        const uint64_t guess = it * n_cta / total;
-        uint32_t g = guess < n_cta - 1 ? static_cast<uint32_t>(guess) : n_cta - 1;
-        while (g + 1 < n_cta && range_begin(total, g + 1, n_cta) <= it) ++g;
-        while (g > 0 && range_begin(total, g, n_cta) > it) --g;
-        return g;
-    };
-    const uint32_t g0 = owner(a), g1 = owner(z);
-    if (g0 == g1) return;
-    const uint32_t m0 = (t / tiles_n) * kTileM, n0 = (t % tiles_n) * kTileN;
+    const uint32_t t = blockIdx.x, L = sp.n_ktiles - sp.x;
+    const uint64_t tail_total = static_cast<uint64_t>(sp.n_tiles) * L;
+    const uint64_t a = static_cast<uint64_t>(t) * L;
+    const uint32_t n_pieces = tail_owner(a + L - 1, tail_total, sp.helpers) -
+                              tail_owner(a, tail_total, sp.helpers) + 1;
+    const uint32_t m0 = (t / sp.tiles_n) * kTileM, n0 = (t % sp.tiles_n) * kTileN;
     for (uint32_t e = threadIdx.x; e < kTileM * kTileN / 4; e += blockDim.x) {
         const uint32_t r = e / (kTileN / 4), c4 = e % (kTileN / 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t g = g0; g <= g1; ++g) {
-            const uint32_t slot = 2 * g + (range_begin(total, g, n_cta) >= a ? 0u : 1u);
-            const float4 p = reinterpret_cast<const float4 *>(
-                ws + (static_cast<size_t>(slot) * kTileM + r) * kTileN)[c4];
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
+        float4 *cp = reinterpret_cast<float4 *>(c + static_cast<size_t>(m0 + r) * ldc + n0) + c4;
+        float4 acc = *cp;
+        for (uint32_t p = 0; p < n_pieces; ++p) {
+            const float4 v = reinterpret_cast<const float4 *>(
+                ws + (static_cast<size_t>(t * sp.pieces + p) * kTileM + r) * kTileN)[c4];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
         }
-        reinterpret_cast<float4 *>(c + static_cast<size_t>(m0 + r) * ldc + n0)[c4] =
-            make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
+        *cp = make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
     }
 }
 
@@ -410,8 +459,53 @@ size_t gemm_smem_bytes() {
            (2 * kStages + 4) * 8 + 16;
 }
 
-size_t gemm_ws_bytes(uint32_t n_cta) {
-    return 2ull * n_cta * kTileM * kTileN * sizeof(float);
+namespace {
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+// The split of an m x n x k product on this device (x == n_ktiles: none).
+GemmSplit plan_split(uint32_t m, uint32_t n, uint32_t k) {
+    GemmSplit sp{};
+    sp.tiles_n = n / kTileN;
+    sp.n_tiles = sp.tiles_n * (m / kTileM);
+    sp.n_ktiles = k / kTileK;
+    sp.x = sp.n_ktiles;
+    const int n_sm = sm_count();
+    if (n_sm <= 0 || sp.n_tiles >= static_cast<uint32_t>(n_sm)) return sp;
+    const uint64_t total = static_cast<uint64_t>(sp.n_tiles) * sp.n_ktiles;
+    // x near total / SMs, the one whose busiest CTA has the fewest k-steps;
+    // no split unless that beats a whole tile per CTA
+    uint64_t best = sp.n_ktiles;
+    for (uint64_t x = total / n_sm; x <= total / n_sm + 1; ++x) {
+        if (x == 0 || x >= sp.n_ktiles) continue;
+        const uint64_t tail = static_cast<uint64_t>(sp.n_tiles) * (sp.n_ktiles - x);
+        const uint64_t h = std::min<uint64_t>(static_cast<uint64_t>(n_sm) - sp.n_tiles, tail);
+        const uint64_t load = std::max<uint64_t>(x, (tail + h - 1) / h);
+        if (load < best) {
+            best = load;
+            sp.x = static_cast<uint32_t>(x);
+            sp.helpers = static_cast<uint32_t>(h);
+        }
+    }
+    if (sp.x == sp.n_ktiles) return sp;
+    const uint32_t L = sp.n_ktiles - sp.x;
+    const uint64_t share = static_cast<uint64_t>(sp.n_tiles) * L / sp.helpers;  // >= 1
+    // a tail of L k-steps meets at most ceil(L / share) + 1 helper ranges
+    sp.pieces = static_cast<uint32_t>((L + share - 1) / share + 1);
+    return sp;
+}
+}  // namespace
+
+size_t gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k) {
+    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return 0;
+    const GemmSplit sp = plan_split(m, n, k);
+    if (sp.x == sp.n_ktiles) return 0;
+    return static_cast<size_t>(sp.n_tiles) * sp.pieces * kTileM * kTileN * sizeof(float);
 }
 
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
@@ -423,30 +517,17 @@ cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const uint32_t tiles_n = n / kTileN, n_tiles = tiles_n * (m / kTileM), n_ktiles = k / kTileK;
-    // One CTA per SM with an equal share of the k-steps when the tiles fill at
-    // most half the SMs and a workspace is given; else a tile per CTA. Tiles
-    // that run in lockstep through k share each k-slice of A and B in L2;
-    // split ranges sit at different k offsets and read their slices from
-    // DRAM each (at 128 tiles on 148 SMs, K = 65536, the split form measured
-    // 0.64 ms against 0.445 ms for a tile per CTA), so the split pays only
-    // where most SMs would otherwise idle.
-    int dev = 0, n_sm = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return e;
-    uint32_t grid = n_tiles;
-    const uint64_t total = static_cast<uint64_t>(n_tiles) * n_ktiles;
-    if (ws && n_sm > 0 && 2ull * n_tiles <= static_cast<uint64_t>(n_sm) &&
-        total >= static_cast<uint64_t>(n_sm) &&
-        ws_bytes >= gemm_ws_bytes(static_cast<uint32_t>(n_sm)))
-        grid = static_cast<uint32_t>(n_sm);
-    gemm_f16_nt_kernel<<<grid, kGemmThreads, smem, st>>>(map_a, map_b, c, n, n_ktiles, tiles_n,
-                                                          n_tiles, alpha, ws, err);
+    GemmSplit sp = plan_split(m, n, k);
+    const size_t need = static_cast<size_t>(sp.n_tiles) * sp.pieces * kTileM * kTileN * 4;
+    if (sp.x != sp.n_ktiles && (!ws || ws_bytes < need)) {  // no room: a tile per CTA
+        sp.x = sp.n_ktiles;
+        sp.helpers = sp.pieces = 0;
+    }
+    const uint32_t grid = sp.x == sp.n_ktiles ? sp.n_tiles : sp.n_tiles + sp.helpers;
+    gemm_f16_nt_kernel<<<grid, kGemmThreads, smem, st>>>(map_a, map_b, c, n, sp, alpha, ws, err);
     e = cudaGetLastError();
-    if (e != cudaSuccess || grid == n_tiles) return e;
-    gemm_fixup_kernel<<<n_tiles, 256, 0, st>>>(c, n, ws, n_ktiles, tiles_n, n_tiles, grid, alpha,
-                                               err);
+    if (e != cudaSuccess || sp.x == sp.n_ktiles) return e;
+    gemm_fixup_kernel<<<sp.n_tiles, 256, 0, st>>>(c, n, ws, sp, alpha, err);
     return cudaGetLastError();
 }
 

@@ -13,12 +13,12 @@
 namespace kvmret {
 
 size_t gemm_smem_bytes();
-// Workspace of the split (stream-K) form for n_cta CTAs: two 128 x 256 f32
-// partial tiles per CTA.
-size_t gemm_ws_bytes(uint32_t n_cta);
-// With a workspace of at least gemm_ws_bytes(SM count), a product whose tiles
-// fill at most half the SMs runs as one CTA per SM over equal shares of the
-// k-steps plus a fix-up launch; otherwise one tile per CTA.
+// Workspace the split form of an m x n x k product needs on the current
+// device (0: it runs a tile per CTA): the helpers' partial 128 x 256 f32
+// tiles. With at least that much, a product whose tiles would leave SMs idle
+// runs one CTA per SM (main CTAs in lockstep plus helpers on the k tails)
+// and a fix-up launch; otherwise, or without a workspace, a tile per CTA.
+size_t gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k);
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
                                uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
                                cudaStream_t st, float *ws = nullptr, size_t ws_bytes = 0);

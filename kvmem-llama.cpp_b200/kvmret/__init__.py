@@ -218,7 +218,7 @@ SIGNATURES = {
                                                        _PU32, _P]),
     "kvmret_gemm_f16_nt": (ctypes.c_int, [_P, _P, _P, _U32, _U32, _U32, ctypes.c_float, _P,
                                           _P]),
-    "kvmret_gemm_ws_bytes": (ctypes.c_size_t, []),
+    "kvmret_gemm_ws_bytes": (ctypes.c_size_t, [_U32, _U32, _U32]),
     "kvmret_gemm_f16_nt_ws": (ctypes.c_int, [_P, _P, _P, _U32, _U32, _U32, ctypes.c_float, _P,
                                              _P, ctypes.c_size_t, _P]),
     "kvmret_d2d_batched": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P),
@@ -870,15 +870,15 @@ def gemm_f16_nt(a, b, alpha=1.0, stream=0):
 
 
 def gemm_f16_nt_split(a, b, alpha=1.0, stream=0):
-    """gemm_f16_nt through the workspace form (one CTA per SM over equal
-    shares of the k-steps when the tiles would leave SMs idle)."""
+    """gemm_f16_nt through the workspace form (one CTA per SM when the tiles
+    would leave SMs idle: lockstep main CTAs plus helpers on the k tails)."""
     import torch
     m, k = a.shape
     n = b.shape[0]
     c = torch.empty((m, n), dtype=torch.float32, device=a.device)
     err = torch.zeros(4, dtype=torch.int32, device=a.device)
-    nb = int(lib.kvmret_gemm_ws_bytes())
-    ws = torch.empty(nb // 4, dtype=torch.float32, device=a.device)
+    nb = int(lib.kvmret_gemm_ws_bytes(m, n, k))
+    ws = torch.empty(max(1, nb // 4), dtype=torch.float32, device=a.device)
     _check(lib.kvmret_gemm_f16_nt_ws(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, alpha,
                                      err.data_ptr(), ws.data_ptr(), nb, _torch_stream(stream)))
     return c, err
