@@ -512,7 +512,7 @@ int kvmret_gemm_f16_nt(const uint16_t *a_dev, const uint16_t *b_dev, float *c_de
                        uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, void *stream);
 /* The same with a caller workspace of kvmret_gemm_ws_bytes(m, n, k) bytes
  * (0: none needed, ws_dev may be NULL). When the 128 x 256 tiles would leave
- * SMs idle, the grid is one CTA per SM: a CTA per tile runs the first k-steps
+ * enough SMs idle for it to pay, the grid is one CTA per SM: a CTA per tile runs the first k-steps
  * of its tile in lockstep with the others (the k-slices of A and B shared in
  * L2), the remaining CTAs split the k tails of all tiles, and a second launch
  * adds the pieces in a fixed order, so results repeat run to run. */

@@ -42,11 +42,11 @@ def test_gemm_matches_float64(m, n, k):
 @pytest.mark.parametrize("m,n,k", [(128, 768, 8192), (512, 2048, 4096), (256, 512, 64),
                                    (2048, 2048, 1024)])
 def test_split_gemm_matches_float64(m, n, k):
-    """The workspace form: with fewer tiles than SMs (3, 32, 128 tiles) one
-    CTA per SM runs (a lockstep CTA per tile for the first k-steps, helpers on
-    the k tails, the pieces added by the fix-up launch); with a single k-step
-    per tile (256 x 512 x 64) a tile per CTA. Same bound as the plain form,
-    and the same result on a second run."""
+    """The workspace form: with few tiles (3, 32) one CTA per SM runs (a
+    lockstep CTA per tile for the first k-steps, helpers on the k tails, the
+    pieces added by the fix-up launch); with a single k-step per tile
+    (256 x 512 x 64) or 128 tiles, where the split would not pay, a tile per
+    CTA. Same bound as the plain form, and the same result on a second run."""
     g = torch.Generator(device="cuda").manual_seed(m * 3 + n + k)
     a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).half()
     b = (torch.randn(n, k, device="cuda", generator=g) * 0.5).half()
