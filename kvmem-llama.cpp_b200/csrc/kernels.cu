@@ -314,21 +314,31 @@ __global__ void __launch_bounds__(128)
     }
     double acc = 0.0;
     uint32_t nlay = 0;
-    for (uint32_t l0 = 0; l0 < n_layer; l0 += 16) {
-        double v[16];
+    // 16 rows per batch; the next batch's loads are issued before the current
+    // one is summed, so each batch's latency (an NVLink round trip for a
+    // peer's rows) overlaps the previous one
+    double cur[16], nxt[16];
 #pragma unroll
-        for (uint32_t u = 0; u < 16; ++u) {  // 16 independent loads in flight
-            const uint32_t l = l0 + u;
-            v[u] = (l < n_layer && s_act[l]) ? row_load(contrib, rs, l, stride, b) : 0.0;
+    for (uint32_t u = 0; u < 16; ++u)
+        cur[u] = (u < n_layer && s_act[u]) ? row_load(contrib, rs, u, stride, b) : 0.0;
+    for (uint32_t l0 = 0; l0 < n_layer; l0 += 16) {
+        if (l0 + 16 < n_layer) {
+#pragma unroll
+            for (uint32_t u = 0; u < 16; ++u) {
+                const uint32_t l = l0 + 16 + u;
+                nxt[u] = (l < n_layer && s_act[l]) ? row_load(contrib, rs, l, stride, b) : 0.0;
+            }
         }
 #pragma unroll
         for (uint32_t u = 0; u < 16; ++u) {  // summed strictly in layer order
             const uint32_t l = l0 + u;
             if (l < n_layer && s_act[l]) {
-                acc = __dadd_rn(acc, v[u]);
+                acc = __dadd_rn(acc, cur[u]);
                 ++nlay;
             }
         }
+#pragma unroll
+        for (uint32_t u = 0; u < 16; ++u) cur[u] = nxt[u];
     }
     scores[b] = nlay ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
 }
@@ -2444,9 +2454,12 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
 }
 
 // As many units per CTA as it takes for one wave of resident CTAs, then as few
-// CTAs as carry them all: every CTA gets the same share. With fewer units
-// than resident CTAs (few layers per GPU) the tile shrinks to 32 blocks so
-// more CTAs keep loads in flight.
+// CTAs as carry them all: every CTA gets the same share. Of the two tilings
+// (64 blocks per unit with float2 loads, 32 with the latency-hiding loop) the
+// one whose busiest CTA holds fewer blocks wins, the 64-block form unless the
+// other saves at least a tenth: at 64 layers both give 192 blocks per CTA, at
+// 32 layers (a rank of two) 128 against 96, and with fewer units than
+// resident CTAs (8 layers per GPU) the 32-block tiles keep more CTAs busy.
 template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
@@ -2454,22 +2467,25 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            uint32_t cstride, const Peers &peers) {
     int per_sm = 0, n_sm = 0, dev = 0;
     const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
+    const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 2>, 256, smem64);
     if (e != cudaSuccess) return e;
     const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
-    const uint32_t tiles64 = (n_blocks + 63) / 64;
-    if (tiles64 * n_layer >= slots)
-        return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                     tiles64, slots, smem64, st, cstride, peers);
-    const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 1>, 256, smem32);
     if (e != cudaSuccess) return e;
     const uint32_t slots1 = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
+    const uint32_t tiles64 = (n_blocks + 63) / 64, tiles32 = (n_blocks + 31) / 32;
+    const uint64_t busiest64 = 64ull * ((tiles64 * n_layer + slots - 1) / slots);
+    const uint64_t busiest32 = 32ull * ((tiles32 * n_layer + slots1 - 1) / slots1);
+    const bool few_units = tiles64 * n_layer < slots;
+    if (!few_units && 10 * busiest32 > 9 * busiest64)
+        return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                     tiles64, slots, smem64, st, cstride, peers);
     return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                 (n_blocks + 31) / 32, slots1, smem32, st, cstride, peers);
+                                 tiles32, slots1, smem32, st, cstride, peers);
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
