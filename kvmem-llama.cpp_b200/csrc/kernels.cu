@@ -927,6 +927,10 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
 #ifndef KVMRET_F16_MINB
 #define KVMRET_F16_MINB 2
 #endif
+// the fresh (host-link) work of a launch is cut into about this many units
+#ifndef KVMRET_F16_FRESH_UNITS
+#define KVMRET_F16_FRESH_UNITS 16
+#endif
 // S10-S12, f16 K. With device counts (the GPU-resident step) the grid is
 // persistent (one wave) and CTAs take work units from a device counter: first
 // the fresh jobs (host-link bound, started at once), then the moved jobs, one
@@ -949,7 +953,9 @@ __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
     // units (each CTA keeps ~32 KB of host loads in flight) saturate the link
     // without taking more CTAs away from the HBM-bound moved units
     const uint32_t L = a.g.n_layer;
-    const uint32_t LF = min(L, max(1u, (a.counts[1] * L + 15) / 16)), gf = (L + LF - 1) / LF;
+    const uint32_t LF = min(L, max(1u, (a.counts[1] * L + KVMRET_F16_FRESH_UNITS - 1) /
+                                           KVMRET_F16_FRESH_UNITS)),
+                   gf = (L + LF - 1) / LF;
     const uint32_t n_fu = a.counts[1] * gf;
     const uint32_t n_units = n_fu + a.counts[0] * L;
     for (;;) {
