@@ -420,7 +420,7 @@ def run_reference(args, w):
 #       -s 20 -c 1 python bench.py --layers 8 --steps 5 --warmup 3 --config C
 # ). The traffic grows with the blocks a launch moves, so a launch's traffic is
 # this ratio times its algorithmic bytes.
-NCU_TRAFFIC_RATIO = {"assemble_kernel": 1556.8 / 1585.4,
+NCU_TRAFFIC_RATIO = {"assemble_kernel": 1588.2 / 1619.0,
                      "assemble_quant_tma_kernel": 666.9 / 695.2}
 
 

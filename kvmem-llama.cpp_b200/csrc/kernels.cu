@@ -2114,7 +2114,10 @@ __global__ void quantize_kernel(const uint16_t *__restrict__ x, uint8_t *__restr
 // ---------------------------------------------------------------------------
 // Device plan (one CTA). Every array index below derives from n_blocks,
 // win_slots and pool_slots, whose sizes the host checked against the buffers.
-constexpr int kPlanThreads = 1024;
+#ifndef KVMRET_PLAN_THREADS
+#define KVMRET_PLAN_THREADS 1024
+#endif
+constexpr int kPlanThreads = KVMRET_PLAN_THREADS;
 
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     dep_wait();
