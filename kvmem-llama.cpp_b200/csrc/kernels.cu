@@ -2015,8 +2015,7 @@ __global__ void resum_kernel(AppendArgs a, uint32_t block, uint32_t n_tok) {
 // thread e sums its channel over the block's new tokens in token order,
 // continuing the trailing partial block's running sum
 // (raw_kv_store.cpp:215-234), and stores sum * (1 / tokens) (:1000-1005).
-__global__ void append_summary_kernel(AppendArgs a, const float *__restrict__ tail_in,
-                                      float *__restrict__ tail_out) {
+__global__ void append_summary_kernel(AppendArgs a, const float *tail_in, float *tail_out) {
     const uint32_t l = blockIdx.x;
     const uint32_t E = a.n_head_kv * a.d_head;
     const uint32_t T = a.block_tokens;
@@ -2592,17 +2591,21 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {
     if (a.n_tok == 0) return cudaSuccess;
     const uint32_t T = a.block_tokens;
     const uint32_t nb = (a.pos0 + a.n_tok - 1) / T - a.pos0 / T + 1;
-    // Ping-pong the tail sum: the first touched block reads the old tail
-    // while the last one may write the new tail in the same launch.
+    // Ping-pong the tail sum when the append spans blocks: the first touched
+    // block reads the old tail while the last one may write the new tail in
+    // the same launch. Within one block (a decode token) each thread reads and
+    // then writes only its own channel, so the tail is updated in place.
     const size_t E = static_cast<size_t>(a.n_head_kv) * a.d_head;
     float *tail_in = a.tail_sum;
-    float *tail_out = a.tail_sum + static_cast<size_t>(a.n_layer) * E;
+    float *tail_out = nb == 1 ? tail_in : a.tail_sum + static_cast<size_t>(a.n_layer) * E;
     append_summary_kernel<<<dim3(a.n_layer, nb), 256, 0, st>>>(a, tail_in, tail_out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    e = cudaMemcpyAsync(tail_in, tail_out, static_cast<size_t>(a.n_layer) * E * sizeof(float),
-                        cudaMemcpyDeviceToDevice, st);
-    if (e != cudaSuccess) return e;
+    if (nb > 1) {
+        e = cudaMemcpyAsync(tail_in, tail_out, static_cast<size_t>(a.n_layer) * E * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return e;
+    }
     const uint32_t warps_per_cta = 8;
     append_repo_kernel<<<dim3((a.n_tok + warps_per_cta - 1) / warps_per_cta, a.n_layer),
                          warps_per_cta * 32, 0, st>>>(a);
