@@ -1864,6 +1864,7 @@ __device__ __forceinline__ bool gen_slots(const GenWrite &a, uint32_t block, uin
 // f16 K: CTA = (layer, bound block).
 template <int D>
 __global__ void __launch_bounds__(256) gen_write_f16_kernel(const __grid_constant__ GenWrite a) {
+    dep_wait();
     constexpr uint32_t PAIRS = D / 4;
     const AssembleGeom &g = a.g;
     const uint32_t l = blockIdx.x;
@@ -1904,6 +1905,7 @@ __global__ void __launch_bounds__(256) gen_write_f16_kernel(const __grid_constan
 constexpr int kGenQWarps = 4;
 template <int D, int KT>
 __global__ void __launch_bounds__(32 * kGenQWarps) gen_write_quant_kernel(const __grid_constant__ GenWrite a) {
+    dep_wait();
     constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
     constexpr uint32_t HEAD_BYTES = (D / 32) * QBlk<KT>::bytes;
     constexpr uint32_t RPW = SEG / HEAD_BYTES;
@@ -2016,6 +2018,7 @@ __global__ void resum_kernel(AppendArgs a, uint32_t block, uint32_t n_tok) {
 // continuing the trailing partial block's running sum
 // (raw_kv_store.cpp:215-234), and stores sum * (1 / tokens) (:1000-1005).
 __global__ void append_summary_kernel(AppendArgs a, const float *tail_in, float *tail_out) {
+    dep_wait();
     const uint32_t l = blockIdx.x;
     const uint32_t E = a.n_head_kv * a.d_head;
     const uint32_t T = a.block_tokens;
@@ -2044,6 +2047,7 @@ __global__ void append_summary_kernel(AppendArgs a, const float *tail_in, float 
 // Repository rows: each (layer, token) K and V row goes to
 // repo[block][layer][K | V] + token offset, over the mapped host pointer.
 __global__ void append_repo_kernel(AppendArgs a) {
+    dep_wait();
     const uint32_t l = blockIdx.y;
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -2598,8 +2602,8 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {
     const size_t E = static_cast<size_t>(a.n_head_kv) * a.d_head;
     float *tail_in = a.tail_sum;
     float *tail_out = nb == 1 ? tail_in : a.tail_sum + static_cast<size_t>(a.n_layer) * E;
-    append_summary_kernel<<<dim3(a.n_layer, nb), 256, 0, st>>>(a, tail_in, tail_out);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_dep(append_summary_kernel, dim3(a.n_layer, nb), dim3(256), 0, st, a,
+                               static_cast<const float *>(tail_in), tail_out);
     if (e != cudaSuccess) return e;
     if (nb > 1) {
         e = cudaMemcpyAsync(tail_in, tail_out, static_cast<size_t>(a.n_layer) * E * sizeof(float),
@@ -2607,9 +2611,9 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
     }
     const uint32_t warps_per_cta = 8;
-    append_repo_kernel<<<dim3((a.n_tok + warps_per_cta - 1) / warps_per_cta, a.n_layer),
-                         warps_per_cta * 32, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_dep(append_repo_kernel,
+                      dim3((a.n_tok + warps_per_cta - 1) / warps_per_cta, a.n_layer),
+                      dim3(warps_per_cta * 32), 0, st, a);
 }
 
 cudaError_t launch_quantize(const uint16_t *x, uint8_t *y, uint64_t n_blocks, bool q8,
@@ -2645,20 +2649,17 @@ cudaError_t launch_gen_write(const GenWrite &a, cudaStream_t st) {
     const dim3 qb(32 * kGenQWarps);
     switch (a.g.d_head) {
     case 64:
-        if (q8) gen_write_quant_kernel<64, 0><<<grid, qb, 0, st>>>(a);
-        else if (q4) gen_write_quant_kernel<64, 1><<<grid, qb, 0, st>>>(a);
-        else gen_write_f16_kernel<64><<<grid, 256, 0, st>>>(a);
-        break;
+        return q8   ? launch_dep(gen_write_quant_kernel<64, 0>, grid, qb, 0, st, a)
+               : q4 ? launch_dep(gen_write_quant_kernel<64, 1>, grid, qb, 0, st, a)
+                    : launch_dep(gen_write_f16_kernel<64>, grid, dim3(256), 0, st, a);
     case 128:
-        if (q8) gen_write_quant_kernel<128, 0><<<grid, qb, 0, st>>>(a);
-        else if (q4) gen_write_quant_kernel<128, 1><<<grid, qb, 0, st>>>(a);
-        else gen_write_f16_kernel<128><<<grid, 256, 0, st>>>(a);
-        break;
+        return q8   ? launch_dep(gen_write_quant_kernel<128, 0>, grid, qb, 0, st, a)
+               : q4 ? launch_dep(gen_write_quant_kernel<128, 1>, grid, qb, 0, st, a)
+                    : launch_dep(gen_write_f16_kernel<128>, grid, dim3(256), 0, st, a);
     case 256:
-        if (q8) gen_write_quant_kernel<256, 0><<<grid, qb, 0, st>>>(a);
-        else if (q4) gen_write_quant_kernel<256, 1><<<grid, qb, 0, st>>>(a);
-        else gen_write_f16_kernel<256><<<grid, 256, 0, st>>>(a);
-        break;
+        return q8   ? launch_dep(gen_write_quant_kernel<256, 0>, grid, qb, 0, st, a)
+               : q4 ? launch_dep(gen_write_quant_kernel<256, 1>, grid, qb, 0, st, a)
+                    : launch_dep(gen_write_f16_kernel<256>, grid, dim3(256), 0, st, a);
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
