@@ -762,14 +762,16 @@ template <int D, bool FRESH>
 __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
                                               uint8_t *__restrict__ dst,
                                               const float4 *__restrict__ tab, uint32_t n_tok,
-                                              uint32_t n_head_kv, uint8_t *__restrict__ raw_dst) {
+                                              uint32_t n_head_kv, uint8_t *__restrict__ raw_dst,
+                                              uint32_t tid = threadIdx.x,
+                                              uint32_t nthr = blockDim.x) {
     constexpr int HALF = D / 2, CPR = HALF / 8, U = KVMRET_F16_UNROLL;
     const uint32_t n_items = n_tok * n_head_kv * CPR;
-    for (uint32_t w0 = threadIdx.x; w0 < n_items; w0 += U * blockDim.x) {
+    for (uint32_t w0 = tid; w0 < n_items; w0 += U * nthr) {
         uint4 lo[U], hi[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {  // all loads first
-            const uint32_t w = w0 + u * blockDim.x;
+            const uint32_t w = w0 + u * nthr;
             if (w >= n_items) break;
             const uint32_t row = w / CPR, j = w % CPR;
             const uint4 *sp = reinterpret_cast<const uint4 *>(src + static_cast<size_t>(row) * D * 2);
@@ -786,7 +788,7 @@ __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const uint32_t w = w0 + u * blockDim.x;
+            const uint32_t w = w0 + u * nthr;
             if (w >= n_items) break;
             const uint32_t row = w / CPR, j = w % CPR, t = row / n_head_kv;
             uint4 olo, ohi;
@@ -803,11 +805,12 @@ __device__ __forceinline__ void rope_rows_f16(const uint8_t *__restrict__ src,
 // reads host memory (mapped pinned) with plain loads and writes one or two
 // destinations. Four loads are in flight per thread.
 __device__ __forceinline__ void copy16(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
-                                       uint64_t nbytes) {
+                                       uint64_t nbytes, uint32_t tid = threadIdx.x,
+                                       uint32_t nthr = blockDim.x) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
-    const uint64_t n = nbytes / 16, step = blockDim.x;
-    uint64_t w = threadIdx.x;
+    const uint64_t n = nbytes / 16, step = nthr;
+    uint64_t w = tid;
     for (; w + 3 * step < n; w += 4 * step) {
         const uint4 v0 = __ldg(s + w), v1 = __ldg(s + w + step);
         const uint4 v2 = __ldg(s + w + 2 * step), v3 = __ldg(s + w + 3 * step);
@@ -819,12 +822,14 @@ __device__ __forceinline__ void copy16(const uint8_t *__restrict__ src, uint8_t 
     for (; w < n; w += step) d[w] = __ldg(s + w);
 }
 __device__ __forceinline__ void copy16_host(const uint8_t *src, uint8_t *__restrict__ dst,
-                                            uint8_t *__restrict__ dst2, uint64_t nbytes) {
+                                            uint8_t *__restrict__ dst2, uint64_t nbytes,
+                                            uint32_t tid = threadIdx.x,
+                                            uint32_t nthr = blockDim.x) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
     uint4 *d2 = reinterpret_cast<uint4 *>(dst2);
-    const uint64_t n = nbytes / 16, step = blockDim.x;
-    uint64_t w = threadIdx.x;
+    const uint64_t n = nbytes / 16, step = nthr;
+    uint64_t w = tid;
     for (; w + 3 * step < n; w += 4 * step) {
         const uint4 v0 = s[w], v1 = s[w + step], v2 = s[w + 2 * step], v3 = s[w + 3 * step];
         d[w] = v0;
@@ -899,7 +904,9 @@ constexpr int kAsmThreads = 512;
 // its pool slot) at the job's window base; V copied.
 template <int D>
 __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobView &jv,
-                                                  uint32_t l, const float4 *tab) {
+                                                  uint32_t l, const float4 *tab,
+                                                  uint32_t tid = threadIdx.x,
+                                                  uint32_t nthr = blockDim.x) {
     const AssembleGeom &g = a.g;
     const uint8_t *slot = jv.fresh ? a.repo + static_cast<uint64_t>(jv.block) * a.slot_bytes
                                    : a.pool + static_cast<uint64_t>(jv.pool_slot) * a.slot_bytes;
@@ -910,17 +917,17 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
     uint8_t *dk = a.win_k + static_cast<uint64_t>(l) * g.win_k_layer +
                   static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.k_row;
     if (raw)
-        rope_rows_f16<D, true>(src, dk, tab, jv.n_tok, g.n_head_kv, raw);
+        rope_rows_f16<D, true>(src, dk, tab, jv.n_tok, g.n_head_kv, raw, tid, nthr);
     else
-        rope_rows_f16<D, false>(src, dk, tab, jv.n_tok, g.n_head_kv, nullptr);
+        rope_rows_f16<D, false>(src, dk, tab, jv.n_tok, g.n_head_kv, nullptr, tid, nthr);
     if (g.v_row) {
         uint8_t *dv = a.win_v + static_cast<uint64_t>(l) * g.win_v_layer +
                       static_cast<uint64_t>(jv.win_slot) * g.block_tokens * g.v_row;
         const uint64_t vb = static_cast<uint64_t>(jv.n_tok) * g.v_row;
         if (raw)
-            copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb);
+            copy16_host(src + g.unit_k, dv, raw + g.unit_k, vb, tid, nthr);
         else
-            copy16(src + g.unit_k, dv, vb);
+            copy16(src + g.unit_k, dv, vb, tid, nthr);
     }
 }
 
@@ -930,6 +937,11 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
 // the fresh (host-link) work of a launch is cut into about this many units
 #ifndef KVMRET_F16_FRESH_UNITS
 #define KVMRET_F16_FRESH_UNITS 16
+#endif
+// 1: with fresh jobs in a launch, warp 0 of every CTA takes the fresh units
+// and the other warps the moved ones (else whole CTAs take fresh units first)
+#ifndef KVMRET_F16_FRESH_WARP
+#define KVMRET_F16_FRESH_WARP 0
 #endif
 // S10-S12, f16 K. With device counts (the GPU-resident step) the grid is
 // persistent (one wave) and CTAs take work units from a device counter: first
@@ -949,10 +961,57 @@ __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
         return;
     }
     __shared__ uint32_t s_unit;
+    const uint32_t L = a.g.n_layer;
+#if KVMRET_F16_FRESH_WARP
+    if (a.counts[1] > 0) {
+        // Warp 0 of every CTA reads fresh (job, layer) units over the host
+        // link while the other warps move pool blocks: every SM keeps a few
+        // KB of host reads in flight without taking whole CTAs away from the
+        // HBM-bound moves. Counters: a.work (fresh), a.work_moved (moved).
+        const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (warp == 0) {
+            const uint32_t n_fresh_units = a.counts[1] * L;
+            for (;;) {
+                uint32_t u = 0;
+                if (lane == 0) u = atomicAdd(a.work, 1u);
+                u = __shfl_sync(0xffffffffu, u, 0);
+                if (u >= n_fresh_units) break;
+                const Job *jp = a.jobs + a.fresh_offset + u / L;
+                jv.pool_slot = jp->pool_slot;
+                jv.win_slot = jp->win_slot;
+                jv.pos0 = jp->pos0;
+                jv.n_tok = jp->n_tok;
+                jv.block = jp->block;
+                jv.fresh = true;
+                assemble_unit_f16<D>(a, jv, u % L, a.gtab + static_cast<size_t>(jv.pos0) * PAIRS,
+                                     lane, 32);
+            }
+            return;
+        }
+        const uint32_t tid = threadIdx.x - 32, nthr = blockDim.x - 32;
+        const uint32_t n_moved_units = a.counts[0] * L;
+        for (;;) {  // named barrier 1 over the moving warps
+            if (tid == 0) s_unit = atomicAdd(a.work_moved, 1u);
+            asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+            const uint32_t u = s_unit;
+            asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+            if (u >= n_moved_units) break;
+            const Job *jp = a.jobs + u / L;
+            jv.pool_slot = jp->pool_slot;
+            jv.win_slot = jp->win_slot;
+            jv.pos0 = jp->pos0;
+            jv.n_tok = jp->n_tok;
+            jv.block = jp->block;
+            jv.fresh = false;
+            assemble_unit_f16<D>(a, jv, u % L, a.gtab + static_cast<size_t>(jv.pos0) * PAIRS,
+                                 tid, nthr);
+        }
+        return;
+    }
+#endif
     // fresh jobs are host-link bound for most of the launch: about 16 fresh
     // units (each CTA keeps ~32 KB of host loads in flight) saturate the link
     // without taking more CTAs away from the HBM-bound moved units
-    const uint32_t L = a.g.n_layer;
     const uint32_t LF = min(L, max(1u, (a.counts[1] * L + KVMRET_F16_FRESH_UNITS - 1) /
                                            KVMRET_F16_FRESH_UNITS)),
                    gf = (L + LF - 1) / LF;
@@ -2475,6 +2534,9 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
 // other saves at least a tenth: at 64 layers both give 192 blocks per CTA, at
 // 32 layers (a rank of two) 128 against 96, and with fewer units than
 // resident CTAs (8 layers per GPU) the 32-block tiles keep more CTAs busy.
+#ifndef KVMRET_SCORE_V2_ONLY
+#define KVMRET_SCORE_V2_ONLY 0
+#endif
 template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
@@ -2496,7 +2558,7 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
     const uint64_t busiest64 = 64ull * ((tiles64 * n_layer + slots - 1) / slots);
     const uint64_t busiest32 = 32ull * ((tiles32 * n_layer + slots1 - 1) / slots1);
     const bool few_units = tiles64 * n_layer < slots;
-    if (!few_units && 10 * busiest32 > 9 * busiest64)
+    if (KVMRET_SCORE_V2_ONLY || (!few_units && 10 * busiest32 > 9 * busiest64))
         return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
                                      tiles64, slots, smem64, st, cstride, peers);
     return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
