@@ -938,11 +938,6 @@ __device__ __forceinline__ void assemble_unit_f16(const AsmLaunch &a, const JobV
 #ifndef KVMRET_F16_FRESH_UNITS
 #define KVMRET_F16_FRESH_UNITS 16
 #endif
-// 1: with fresh jobs in a launch, warp 0 of every CTA takes the fresh units
-// and the other warps the moved ones (else whole CTAs take fresh units first)
-#ifndef KVMRET_F16_FRESH_WARP
-#define KVMRET_F16_FRESH_WARP 0
-#endif
 // S10-S12, f16 K. With device counts (the GPU-resident step) the grid is
 // persistent (one wave) and CTAs take work units from a device counter: first
 // the fresh jobs (host-link bound, started at once), then the moved jobs, one
@@ -962,53 +957,6 @@ __global__ void __launch_bounds__(kAsmThreads, KVMRET_F16_MINB)
     }
     __shared__ uint32_t s_unit;
     const uint32_t L = a.g.n_layer;
-#if KVMRET_F16_FRESH_WARP
-    if (a.counts[1] > 0) {
-        // Warp 0 of every CTA reads fresh (job, layer) units over the host
-        // link while the other warps move pool blocks: every SM keeps a few
-        // KB of host reads in flight without taking whole CTAs away from the
-        // HBM-bound moves. Counters: a.work (fresh), a.work_moved (moved).
-        const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (warp == 0) {
-            const uint32_t n_fresh_units = a.counts[1] * L;
-            for (;;) {
-                uint32_t u = 0;
-                if (lane == 0) u = atomicAdd(a.work, 1u);
-                u = __shfl_sync(0xffffffffu, u, 0);
-                if (u >= n_fresh_units) break;
-                const Job *jp = a.jobs + a.fresh_offset + u / L;
-                jv.pool_slot = jp->pool_slot;
-                jv.win_slot = jp->win_slot;
-                jv.pos0 = jp->pos0;
-                jv.n_tok = jp->n_tok;
-                jv.block = jp->block;
-                jv.fresh = true;
-                assemble_unit_f16<D>(a, jv, u % L, a.gtab + static_cast<size_t>(jv.pos0) * PAIRS,
-                                     lane, 32);
-            }
-            return;
-        }
-        const uint32_t tid = threadIdx.x - 32, nthr = blockDim.x - 32;
-        const uint32_t n_moved_units = a.counts[0] * L;
-        for (;;) {  // named barrier 1 over the moving warps
-            if (tid == 0) s_unit = atomicAdd(a.work_moved, 1u);
-            asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-            const uint32_t u = s_unit;
-            asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-            if (u >= n_moved_units) break;
-            const Job *jp = a.jobs + u / L;
-            jv.pool_slot = jp->pool_slot;
-            jv.win_slot = jp->win_slot;
-            jv.pos0 = jp->pos0;
-            jv.n_tok = jp->n_tok;
-            jv.block = jp->block;
-            jv.fresh = false;
-            assemble_unit_f16<D>(a, jv, u % L, a.gtab + static_cast<size_t>(jv.pos0) * PAIRS,
-                                 tid, nthr);
-        }
-        return;
-    }
-#endif
     // fresh jobs are host-link bound for most of the launch: about 16 fresh
     // units (each CTA keeps ~32 KB of host loads in flight) saturate the link
     // without taking more CTAs away from the HBM-bound moved units
@@ -2528,15 +2476,12 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
 }
 
 // As many units per CTA as it takes for one wave of resident CTAs, then as few
-// CTAs as carry them all: every CTA gets the same share. Of the two tilings
-// (64 blocks per unit with float2 loads, 32 with the latency-hiding loop) the
-// one whose busiest CTA holds fewer blocks wins, the 64-block form unless the
-// other saves at least a tenth: at 64 layers both give 192 blocks per CTA, at
-// 32 layers (a rank of two) 128 against 96, and with fewer units than
-// resident CTAs (8 layers per GPU) the 32-block tiles keep more CTAs busy.
-#ifndef KVMRET_SCORE_V2_ONLY
-#define KVMRET_SCORE_V2_ONLY 0
-#endif
+// CTAs as carry them all: every CTA gets the same share. With fewer 64-block
+// units than resident CTAs (few layers per GPU) the tile shrinks to 32 blocks
+// so more CTAs keep loads in flight. Measured (score kernel, one GPU, live):
+// 8 layers 24.6 us (32-block) against 39.2 us (64-block), 16 layers 41.1
+// against 47.0, 32 layers 71.9 against 64.9 (there the 64-block tiles fill
+// the resident CTAs and their float2 loads win).
 template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
@@ -2544,25 +2489,22 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            uint32_t cstride, const Peers &peers) {
     int per_sm = 0, n_sm = 0, dev = 0;
     const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
-    const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 2>, 256, smem64);
     if (e != cudaSuccess) return e;
     const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
+    const uint32_t tiles64 = (n_blocks + 63) / 64;
+    if (tiles64 * n_layer >= slots)
+        return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
+                                     tiles64, slots, smem64, st, cstride, peers);
+    const size_t smem32 = static_cast<size_t>(n_head_kv) * (D + 32) * sizeof(float);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_kernel<D, 1>, 256, smem32);
     if (e != cudaSuccess) return e;
     const uint32_t slots1 = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
-    const uint32_t tiles64 = (n_blocks + 63) / 64, tiles32 = (n_blocks + 31) / 32;
-    const uint64_t busiest64 = 64ull * ((tiles64 * n_layer + slots - 1) / slots);
-    const uint64_t busiest32 = 32ull * ((tiles32 * n_layer + slots1 - 1) / slots1);
-    const bool few_units = tiles64 * n_layer < slots;
-    if (KVMRET_SCORE_V2_ONLY || (!few_units && 10 * busiest32 > 9 * busiest64))
-        return launch_score_tv<D, 2>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                     tiles64, slots, smem64, st, cstride, peers);
     return launch_score_tv<D, 1>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                 tiles32, slots1, smem32, st, cstride, peers);
+                                 (n_blocks + 31) / 32, slots1, smem32, st, cstride, peers);
 }
 
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
