@@ -114,9 +114,6 @@ uint32_t hadamard_nrot_k(uint32_t d_head) {
 constexpr int kRing = 4;          // readback slots (steps in flight before a collect)
 constexpr size_t kEventPool = 8192;
 enum { PR_SCORE = 0, PR_ASM, PR_GEMM };
-// d_counts word the TMA-fed scoring kernel sets when a wait gave up (read and
-// cleared by the plan, or by kvmret_score)
-constexpr uint32_t kScoreErrWord = 12;
 enum { OP_APPEND = 0, OP_TRUNCATE, OP_ON_GPU };  // deferred block-table operations
 
 }  // namespace
@@ -436,7 +433,6 @@ int create_impl(const kvmret_config &cfg, kvmret_ctx *c, DeviceScope &ds) {
     TRY(dmalloc(&c->d_slot_ntok, P * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_slot_used, P * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_counts, 16 * sizeof(uint32_t)));
-    CK(cudaMemsetAsync(c->d_counts, 0, 16 * sizeof(uint32_t), c->st));
     TRY(dmalloc(&c->d_ids, W * sizeof(uint32_t)));
     TRY(dmalloc(&c->d_gen_err, 16));
     CK(cudaMemsetAsync(c->d_gen_err, 0, 16, c->st));
@@ -500,11 +496,7 @@ int collect_one(kvmret_ctx *c, uint32_t *ids_out, uint32_t *n_out) {
     --c->rb_pending;
     if (err) {
         apply_deferred(c, c->rb_step[slot]);
-        const char *why = (err & 0x100u)   ? "a rank's score rows never arrived"
-                          : (err & 0x400u) ? "the scoring kernel gave up waiting for its copies"
-                          : (err & 0x200u) ? "the assembly gave up waiting for its copies"
-                                           : "window or pool too small";
-        return fail(KVMRET_ERR_STATE, "device plan error 0x%x (%s)", err, why);
+        return fail(KVMRET_ERR_STATE, "device plan error 0x%x (window or pool too small)", err);
     }
     const uint32_t *ids = r + 8;
     c->last_plan = c->table.set_selection(ids, n_sel, false);
@@ -560,7 +552,6 @@ int plan_and_assemble(kvmret_ctx *c) {
     pa.ext_err = c->ex_world > 1 ? reinterpret_cast<uint32_t *>(c->ex_region + c->ex_tail +
                                                                4 * (kvmret::kMaxRanks + 1))
                                  : nullptr;
-    pa.score_err = c->d_counts + kScoreErrWord;
     CK(kvmret::launch_plan(pa, c->st));
     kvmret::AsmLaunch al{};
     al.jobs = c->jobs_dev;
@@ -657,8 +648,7 @@ int score_layers_impl(kvmret_ctx *c, double *out) {
     const uint32_t n = c->live_blocks();
     const int pr = prof_begin(c, c->st, PR_SCORE);
     CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, dst, c->cfg.n_layer,
-                            c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st, c->cstride,
-                            nullptr, c->d_counts + kScoreErrWord));
+                            c->cfg.n_head_kv, c->cfg.d_head, c->ncap, n, c->st, c->cstride));
     prof_end(c, c->st, pr);
     c->prof.score_bytes += static_cast<uint64_t>(c->cfg.n_layer) * c->E * ((n + 63) / 64 * 64) *
                            sizeof(float);
@@ -1197,14 +1187,7 @@ int kvmret_score(kvmret_ctx *c, double *scores_host) {
     if (scores_host) {
         CK(cudaMemcpyAsync(scores_host, c->scores, c->live_blocks() * sizeof(double),
                            cudaMemcpyDeviceToHost, c->st));
-        uint32_t gave_up = 0;
-        CK(cudaMemcpyAsync(&gave_up, c->d_counts + kScoreErrWord, sizeof(uint32_t),
-                           cudaMemcpyDeviceToHost, c->st));
         CK(cudaStreamSynchronize(c->st));
-        if (gave_up) {
-            CK(cudaMemsetAsync(c->d_counts + kScoreErrWord, 0, sizeof(uint32_t), c->st));
-            return fail(KVMRET_ERR_CUDA, "scoring kernel gave up waiting for its copies");
-        }
     }
     return KVMRET_OK;
 }
@@ -2449,8 +2432,7 @@ int kvmret_score_exchange(kvmret_ctx *c) {
     const uint32_t n = c->live_blocks();
     const int prs = prof_begin(c, c->st, PR_SCORE);
     CK(kvmret::launch_score(c->summ, c->qv, c->nq, c->active, local, L, c->cfg.n_head_kv,
-                            c->cfg.d_head, c->ncap, n, c->st, c->cstride, &pr,
-                            c->d_counts + kScoreErrWord));
+                            c->cfg.d_head, c->ncap, n, c->st, c->cstride, &pr));
     prof_end(c, c->st, prs);
     c->prof.score_bytes += static_cast<uint64_t>(L) * c->E * ((n + 63) / 64 * 64) * sizeof(float);
     CK(kvmret::launch_reduce(nullptr, nullptr, W * L, c->cstride, c->has_block, n, c->scores,

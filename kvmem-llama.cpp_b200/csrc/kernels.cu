@@ -4,7 +4,6 @@
 // fused anywhere on this path.
 #include "kernels.cuh"
 
-#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -1576,138 +1575,6 @@ __device__ __forceinline__ void bulk_store(void *dst, uint32_t src, uint32_t byt
                  : "memory");
 }
 
-// ---------------------------------------------------------------------------
-// S3, TMA-fed form of score_kernel: the same terms, the same arithmetic and
-// order. An item is one (unit, KV head): the 128 d-rows x 64 blocks (32 KB)
-// of the head's summaries in the unit's tile, one 2-D tensor copy (box
-// {64 blocks, 128 rows} of the summaries seen as [L * Hkv * D][ncap] f32, no
-// multicast). One producer lane keeps kScStages items in flight per CTA (one
-// CTA per SM), so the memory system sees 160 KB per SM whatever the layer
-// count; four groups of 64 threads take the items in turn, thread t walking
-// block b0 + t strictly in d order, and after each unit the first group adds
-// the heads' cosines in head order and writes the unit's terms. Every
-// mbarrier wait gives up after 2 s: the CTA then records 1 in *err, drains
-// the copies it issued and stops (the plan fails the step as 0x400).
-constexpr int kScStages = 5;
-constexpr int kScGroups = 4;
-constexpr int kScThreads = 64 * kScGroups + 32;
-constexpr uint32_t kScItemBytes = 64 * 128 * sizeof(float);
-
-__device__ __forceinline__ void tma_load_2d_f32(uint32_t dst, const CUtensorMap *map, int32_t x,
-                                                int32_t y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-template <int D>
-__global__ void __launch_bounds__(kScThreads, 1)
-    score_tma_kernel(const __grid_constant__ CUtensorMap map, const float *__restrict__ qv,
-                     const float *__restrict__ nq, const uint8_t *__restrict__ active,
-                     double *__restrict__ contrib, uint32_t n_head_kv, uint32_t cstride,
-                     uint32_t tiles, uint32_t n_units, uint32_t per_cta, uint32_t *err,
-                     const __grid_constant__ Peers peers) {
-    static_assert(D == 128, "the 2-D item holds 128 d-rows");
-    dep_wait();
-    extern __shared__ __align__(1024) uint8_t sc_smem[];
-    __shared__ __align__(8) uint64_t full[kScStages], empty[kScStages];
-    __shared__ float cosb[2][8][64];  // [unit parity][head][block]
-    __shared__ uint32_t s_fail;
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t u0 = blockIdx.x * per_cta, u1 = min(n_units, u0 + per_cta);
-    const uint32_t H = n_head_kv;
-    const uint32_t n_items = u0 < u1 ? (u1 - u0) * H : 0;
-    const uint32_t stage0 = smem_addr(sc_smem);
-    if (tid == 0) {
-        s_fail = 0;
-        for (int s = 0; s < kScStages; ++s) {
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[s]))
-                         : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 2;" ::"r"(smem_addr(&empty[s]))
-                         : "memory");
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map))
-                     : "memory");
-    }
-    __syncthreads();
-    if (warp == 2 * kScGroups) {  // producer warp
-        if (lane == 0) {
-            uint32_t i = 0;
-            for (; i < n_items; ++i) {
-                const uint32_t s = i % kScStages, round = i / kScStages;
-                if ((round > 0 &&
-                     !mbar_wait_bounded(smem_addr(&empty[s]), (round - 1) & 1u)) ||
-                    *static_cast<volatile uint32_t *>(&s_fail))
-                    break;
-                const uint32_t u = u0 + i / H, h = i % H;
-                const uint32_t l = u / tiles, b0 = (u % tiles) * 64;
-                const uint32_t bar = smem_addr(&full[s]);
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                             "r"(kScItemBytes)
-                             : "memory");
-                tma_load_2d_f32(stage0 + s * kScItemBytes, &map, static_cast<int32_t>(b0),
-                                static_cast<int32_t>((l * H + h) * D), bar);
-            }
-            if (i < n_items) {  // gave up: drain the copies in flight (bounded)
-                atomicExch(&s_fail, 1u);
-                for (uint32_t j = i > kScStages ? i - kScStages : 0; j < i; ++j)
-                    mbar_wait_bounded(smem_addr(&full[j % kScStages]), (j / kScStages) & 1u);
-            }
-        }
-    } else {  // compute groups: group gi = threads 64 gi .. 64 gi + 63
-        const uint32_t gi = tid >> 6, t = tid & 63;
-        bool ok = true;
-        for (uint32_t u = u0; u < u1; ++u) {
-            const uint32_t l = u / tiles, b0 = (u % tiles) * 64, ub = (u - u0) & 1u;
-            const bool act = active[l] != 0;
-            for (uint32_t h = 0; h < H; ++h) {
-                const uint32_t i = (u - u0) * H + h;
-                if (i % kScGroups != gi) continue;
-                const uint32_t s = i % kScStages;
-                if (ok && !mbar_wait_bounded(smem_addr(&full[s]), (i / kScStages) & 1u)) {
-                    ok = false;
-                    atomicExch(&s_fail, 1u);
-                }
-                if (ok && act) {
-                    const float *col = reinterpret_cast<const float *>(sc_smem + s * kScItemBytes) + t;
-                    const float *qh = qv + (static_cast<size_t>(l) * H + h) * D;
-                    float dt = 0.f, nk = 0.f;
-#pragma unroll 16
-                    for (int d = 0; d < D; ++d) {  // strictly in d order (:4179-4185)
-                        const float k = col[d * 64];
-                        dt = __fadd_rn(dt, __fmul_rn(__ldg(qh + d), k));
-                        nk = __fadd_rn(nk, __fmul_rn(k, k));
-                    }
-                    const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * H + h]);
-                    cosb[ub][h][t] = __fdiv_rn(dt, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(nk)), 1e-6f));
-                }
-                // the stage is free again (one arrival per warp of the group)
-                __syncwarp();
-                if (lane == 0)
-                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                                     smem_addr(&empty[s]))
-                                 : "memory");
-            }
-            // every group's heads of unit u are in cosb[ub]
-            asm volatile("bar.sync 1, %0;" ::"r"(64 * kScGroups) : "memory");
-            if (gi == 0) {  // layer += cos (double, head order); term = layer / Hkv
-                double layer = 0.0;
-                if (act)
-                    for (uint32_t h = 0; h < H; ++h)
-                        layer = __dadd_rn(layer, static_cast<double>(cosb[ub][h][t]));
-                contrib[static_cast<size_t>(l) * cstride + b0 + t] =
-                    act ? __ddiv_rn(layer, static_cast<double>(H)) : 0.0;
-            }
-        }
-    }
-    __syncthreads();
-    if (tid == 0 && s_fail && err) atomicExch(err, 1u);
-    if (peers.n > 1) exchange_signal(peers);
-}
-
 // One item of the sequence, resolved: where its bytes come from and go to.
 struct QItem {
     const uint8_t *src;   // pool (moved) or host repository (fresh)
@@ -2281,17 +2148,12 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs a) {
     uint32_t *s_free = psm + 5 * W;  // [P]
     uint32_t *s_cu = psm + 5 * W + P;  // [P] eviction key: slot_used, ~0u if not a candidate
     uint32_t *s_ev = psm + 5 * W + 2 * P;  // [P] evicted slots in slot order
-    if (tid == 0) {  // consumed once
-        s_err = a.ext_err ? atomicExch(a.ext_err, 0u) : 0u;
-        if (a.score_err && atomicExch(a.score_err, 0u)) s_err |= 0x400u;
-    }
+    if (tid == 0) s_err = a.ext_err ? atomicExch(a.ext_err, 0u) : 0u;  // consumed once
     __syncthreads();
-    if (s_err) {  // a rank's score rows never arrived (0x100), or the scoring kernel gave
-                  // up waiting (0x400): keep the window, pool and plan as they are
+    if (s_err) {  // a rank's score rows never arrived: keep the window, pool and plan as they are
         if (tid == 0) {
-            const uint32_t code = (s_err & 0x400u) | ((s_err & ~0x400u) ? 0x100u : 0u);
             for (int i = 0; i < 9; ++i) a.counts[i] = 0;
-            a.counts[4] = code;
+            a.counts[4] = 0x100u;
         }
         return;
     }
@@ -2620,68 +2482,12 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
 // 8 layers 24.6 us (32-block) against 39.2 us (64-block), 16 layers 41.1
 // against 47.0, 32 layers 71.9 against 64.9 (there the 64-block tiles fill
 // the resident CTAs and their float2 loads win).
-#ifndef KVMRET_SCORE_TMA
-#define KVMRET_SCORE_TMA 1
-#endif
-typedef CUresult (*ScEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                               const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                               const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// The summaries [rows][ncap] f32 as a 2-D tensor with {64, 128} boxes.
-cudaError_t encode_summ_map(CUtensorMap *map, const float *summ, uint64_t rows, uint32_t ncap) {
-    static ScEncodeFn fn = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return static_cast<ScEncodeFn>(nullptr);
-        return reinterpret_cast<ScEncodeFn>(p);
-    }();
-    if (!fn) return cudaErrorNotSupported;
-    const cuuint64_t dims[2] = {ncap, rows};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ncap) * sizeof(float)};
-    const cuuint32_t box[2] = {64, 128};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(summ), dims,
-                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
 template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
                            uint32_t n_head_kv, uint32_t ncap, uint32_t n_blocks, cudaStream_t st,
-                           uint32_t cstride, const Peers &peers, uint32_t *err) {
+                           uint32_t cstride, const Peers &peers) {
     int per_sm = 0, n_sm = 0, dev = 0;
-    if constexpr (D == 128) {
-        // the TMA-fed kernel wherever an error word is given (the context's
-        // steps); 64-block tiles of 128 d-rows, at most 8 KV heads
-        if (KVMRET_SCORE_TMA && err && n_head_kv <= 8 && ncap % 64 == 0 &&
-            (reinterpret_cast<uintptr_t>(summ) & 15) == 0) {
-            CUtensorMap map;
-            cudaError_t e = encode_summ_map(&map, summ,
-                                            static_cast<uint64_t>(n_layer) * n_head_kv * D, ncap);
-            if (e != cudaSuccess) return e;
-            if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-            if ((e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev)) !=
-                cudaSuccess)
-                return e;
-            const uint32_t tiles = (n_blocks + 63) / 64, n_units = tiles * n_layer;
-            const uint32_t per_cta = (n_units + n_sm - 1) / n_sm;
-            const uint32_t grid = (n_units + per_cta - 1) / per_cta;
-            const size_t smem = kScStages * static_cast<size_t>(kScItemBytes);
-            auto kfn = score_tma_kernel<D>;
-            if ((e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(smem))) != cudaSuccess)
-                return e;
-            return launch_dep(kfn, dim3(grid), dim3(kScThreads), smem, st, map, qv, nq, active,
-                              contrib, n_head_kv, cstride, tiles, n_units, per_cta, err, peers);
-        }
-    }
     const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
@@ -2704,8 +2510,7 @@ cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
 cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap, uint32_t n_blocks,
-                         cudaStream_t st, uint32_t cstride, const Peers *peers_in,
-                         uint32_t *err) {
+                         cudaStream_t st, uint32_t cstride, const Peers *peers_in) {
     if (cstride == 0) cstride = ncap;
     if (n_blocks == 0) {
         if (peers_in && peers_in->n > 1)
@@ -2717,13 +2522,13 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
     switch (d_head) {
     case 64:
         return launch_score_t<64>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                   n_blocks, st, cstride, peers, err);
+                                   n_blocks, st, cstride, peers);
     case 128:
         return launch_score_t<128>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                   n_blocks, st, cstride, peers, err);
+                                   n_blocks, st, cstride, peers);
     case 256:
         return launch_score_t<256>(summ, qv, nq, active, contrib, n_layer, n_head_kv, ncap,
-                                   n_blocks, st, cstride, peers, err);
+                                   n_blocks, st, cstride, peers);
     default:
         return cudaErrorInvalidValue;
     }

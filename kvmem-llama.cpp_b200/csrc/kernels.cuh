@@ -83,7 +83,7 @@ cudaError_t launch_score(const float *summ, const float *qv, const float *nq,
                          const uint8_t *active, double *contrib, uint32_t n_layer,
                          uint32_t n_head_kv, uint32_t d_head, uint32_t ncap,
                          uint32_t n_blocks, cudaStream_t st, uint32_t cstride = 0,
-                         const Peers *peers = nullptr, uint32_t *err = nullptr);
+                         const Peers *peers = nullptr);
 
 // S3 epilogue: layer-ordered sum, / number of layers with a query. With
 // active == nullptr the flags are read from each row's last column.
@@ -153,7 +153,6 @@ struct PlanArgs {
     uint32_t *counts;   // [9]: 8 read back per step, [7] and [8] work counters
     uint32_t *ids;      // [win_slots]
     uint32_t *ext_err;  // optional: a nonzero word here (read and cleared) fails the step as 0x100
-    uint32_t *score_err;  // optional: the scoring kernel gave up waiting (read and cleared): 0x400
 };
 cudaError_t launch_plan(const PlanArgs &a, cudaStream_t st);
 size_t plan_smem_bytes(uint32_t win_slots, uint32_t pool_slots);
