@@ -1371,83 +1371,6 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// ---------------------------------------------------------------------------
-// S3, staged form of score_kernel: the same terms, arithmetic and order. An
-// item is one (unit, KV head): the D d-rows x 64 blocks of the head's
-// summaries in the unit's 64-block tile (32 KB at D = 128). All 256 threads
-// copy an item into shared memory with 16-byte cp.async (coalesced, every
-// copy of the item in flight at once), kScBufs - 1 items ahead of the one
-// being scored; the first 64 threads score it, thread t walking block b0 + t
-// strictly in d order and summing its cosines over the unit's heads in head
-// order in a double register. A plain-load pipeline (no TMA, no mbarrier):
-// per item one cp.async group and two block barriers.
-constexpr int kScBufs = 3;
-
-template <int D>
-__global__ void __launch_bounds__(256)
-    score_stage_kernel(const float *__restrict__ summ, const float *__restrict__ qv,
-                       const float *__restrict__ nq, const uint8_t *__restrict__ active,
-                       double *__restrict__ contrib, uint32_t n_head_kv, uint32_t ncap,
-                       uint32_t cstride, uint32_t tiles, uint32_t n_units, uint32_t per_cta,
-                       const __grid_constant__ Peers peers) {
-    constexpr uint32_t ROW = 64 * sizeof(float);           // 256 bytes of one d-row
-    constexpr uint32_t ITEM = D * ROW;                      // bytes of one item
-    constexpr uint32_t CHUNKS = ITEM / 16;                  // 16-byte copies per item
-    dep_wait();
-    extern __shared__ __align__(16) uint8_t st_smem[];
-    const uint32_t tid = threadIdx.x;
-    const uint32_t H = n_head_kv;
-    const uint32_t u0 = blockIdx.x * per_cta, u1 = min(n_units, u0 + per_cta);
-    const uint32_t n_items = u0 < u1 ? (u1 - u0) * H : 0;
-    auto issue = [&](uint32_t i) {  // copies of item i into buffer i % kScBufs
-        if (i < n_items) {
-            const uint32_t u = u0 + i / H, h = i % H;
-            const uint32_t l = u / tiles, b0 = (u % tiles) * 64;
-            const uint8_t *src = reinterpret_cast<const uint8_t *>(
-                summ + (static_cast<size_t>(l) * H + h) * D * ncap + b0);
-            uint8_t *dst = st_smem + (i % kScBufs) * ITEM;
-            for (uint32_t c = tid; c < CHUNKS; c += blockDim.x) {
-                const uint32_t row = c / (ROW / 16), col = c % (ROW / 16);
-                cp_async16(dst + row * ROW + col * 16,
-                           src + static_cast<size_t>(row) * ncap * sizeof(float) + col * 16);
-            }
-        }
-        cp_async_commit();  // one group per item index (empty past the end)
-    };
-#pragma unroll
-    for (int k = 0; k < kScBufs - 1; ++k) issue(k);
-    double layer = 0.0;
-    for (uint32_t i = 0; i < n_items; ++i) {
-        issue(i + kScBufs - 1);
-        cp_async_wait<kScBufs - 1>();  // item i's copies (this thread's) have landed
-        __syncthreads();               // ... and everyone's
-        const uint32_t u = u0 + i / H, h = i % H;
-        const uint32_t l = u / tiles;
-        if (tid < 64 && active[l]) {
-            const float *col = reinterpret_cast<const float *>(st_smem + (i % kScBufs) * ITEM) + tid;
-            const float *qh = qv + (static_cast<size_t>(l) * H + h) * D;
-            float dt = 0.f, nk = 0.f;
-#pragma unroll 16
-            for (int d = 0; d < D; ++d) {  // strictly in d order (:4179-4185)
-                const float k = col[d * 64];
-                dt = __fadd_rn(dt, __fmul_rn(__ldg(qh + d), k));
-                nk = __fadd_rn(nk, __fmul_rn(k, k));
-            }
-            const float sn = __fsqrt_rn(nq[static_cast<size_t>(l) * H + h]);
-            const float cs = __fdiv_rn(dt, __fadd_rn(__fmul_rn(sn, __fsqrt_rn(nk)), 1e-6f));
-            layer = __dadd_rn(h == 0 ? 0.0 : layer, static_cast<double>(cs));  // head order
-        }
-        if (tid < 64 && h == H - 1) {  // the unit's term: layer / Hkv (:4186-4188)
-            const uint32_t b0 = (u % tiles) * 64;
-            contrib[static_cast<size_t>(l) * cstride + b0 + tid] =
-                active[l] ? __ddiv_rn(layer, static_cast<double>(H)) : 0.0;
-        }
-        __syncthreads();  // buffer i % kScBufs is free for item i + kScBufs
-    }
-    cp_async_wait<0>();
-    if (peers.n > 1) exchange_signal(peers);
-}
-
 // A warp's walk over the CTA's work items: for each of its layers, the K
 // segments then the V pieces of the job's (block, layer) unit, dealt to the
 // warps round-robin. Advancing costs no division.
@@ -2559,32 +2482,12 @@ cudaError_t launch_score_tv(const float *summ, const float *qv, const float *nq,
 // 8 layers 24.6 us (32-block) against 39.2 us (64-block), 16 layers 41.1
 // against 47.0, 32 layers 71.9 against 64.9 (there the 64-block tiles fill
 // the resident CTAs and their float2 loads win).
-#ifndef KVMRET_SCORE_STAGED
-#define KVMRET_SCORE_STAGED 1
-#endif
 template <int D>
 cudaError_t launch_score_t(const float *summ, const float *qv, const float *nq,
                            const uint8_t *active, double *contrib, uint32_t n_layer,
                            uint32_t n_head_kv, uint32_t ncap, uint32_t n_blocks, cudaStream_t st,
                            uint32_t cstride, const Peers &peers) {
     int per_sm = 0, n_sm = 0, dev = 0;
-    if (KVMRET_SCORE_STAGED && ncap % 64 == 0 && (reinterpret_cast<uintptr_t>(summ) & 15) == 0) {
-        const size_t smem = kScBufs * static_cast<size_t>(D) * 64 * sizeof(float);
-        auto kfn = score_stage_kernel<D>;
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e == cudaSuccess) e = cudaGetDevice(&dev);
-        if (e == cudaSuccess)
-            e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, 256, smem);
-        if (e != cudaSuccess) return e;
-        const uint32_t slots = static_cast<uint32_t>(std::max(1, per_sm) * std::max(1, n_sm));
-        const uint32_t tiles = (n_blocks + 63) / 64, n_units = tiles * n_layer;
-        const uint32_t per_cta = (n_units + slots - 1) / slots;
-        const uint32_t grid = (n_units + per_cta - 1) / per_cta;
-        return launch_dep(kfn, dim3(grid), dim3(256), smem, st, summ, qv, nq, active, contrib,
-                          n_head_kv, ncap, cstride, tiles, n_units, per_cta, peers);
-    }
     const size_t smem64 = static_cast<size_t>(n_head_kv) * (D + 64) * sizeof(float);
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
