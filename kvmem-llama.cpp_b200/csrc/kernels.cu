@@ -153,6 +153,10 @@ __global__ void exchange_signal_kernel(const __grid_constant__ Peers peers) {
 // bytes, and each block's dot / norm is accumulated strictly in d order
 // (score_retrieval :4179-4185). Warp w handles heads w, w + 8, ...; the
 // per-layer head sum is taken in head order from shared memory.
+// d-rows per batch of the 32-block form (two batches in flight per lane)
+#ifndef KVMRET_SCORE_RB
+#define KVMRET_SCORE_RB 16
+#endif
 template <int D, int V>
 __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ summ,
                                                     const float *__restrict__ qv,
@@ -216,7 +220,7 @@ __global__ void __launch_bounds__(256) score_kernel(const float *__restrict__ su
                 // latency-bound form (few layers): the next 16 d rows are loaded
                 // before the current ones are consumed (the compiler barrier
                 // keeps the loads ahead of the dependent sums)
-                constexpr int RB = 16;
+                constexpr int RB = KVMRET_SCORE_RB < D ? KVMRET_SCORE_RB : D;
                 float cur[RB], nxt[RB];
 #pragma unroll
                 for (int v = 0; v < RB; ++v) cur[v] = __ldg(p + static_cast<size_t>(v) * dstep);
