@@ -318,24 +318,23 @@ __global__ void __launch_bounds__(128)
     }
     double acc = 0.0;
     uint32_t nlay = 0;
-    // RB rows per batch; the next batch's loads are issued before the current
+    // 16 rows per batch; the next batch's loads are issued before the current
     // one is summed, so each batch's latency (an NVLink round trip for a
-    // peer's rows) overlaps the previous one, and 64 layers take two batches
-    constexpr uint32_t RB = 32;
-    double cur[RB], nxt[RB];
+    // peer's rows) overlaps the previous one
+    double cur[16], nxt[16];
 #pragma unroll
-    for (uint32_t u = 0; u < RB; ++u)
+    for (uint32_t u = 0; u < 16; ++u)
         cur[u] = (u < n_layer && s_act[u]) ? row_load(contrib, rs, u, stride, b) : 0.0;
-    for (uint32_t l0 = 0; l0 < n_layer; l0 += RB) {
-        if (l0 + RB < n_layer) {
+    for (uint32_t l0 = 0; l0 < n_layer; l0 += 16) {
+        if (l0 + 16 < n_layer) {
 #pragma unroll
-            for (uint32_t u = 0; u < RB; ++u) {
-                const uint32_t l = l0 + RB + u;
+            for (uint32_t u = 0; u < 16; ++u) {
+                const uint32_t l = l0 + 16 + u;
                 nxt[u] = (l < n_layer && s_act[l]) ? row_load(contrib, rs, l, stride, b) : 0.0;
             }
         }
 #pragma unroll
-        for (uint32_t u = 0; u < RB; ++u) {  // summed strictly in layer order
+        for (uint32_t u = 0; u < 16; ++u) {  // summed strictly in layer order
             const uint32_t l = l0 + u;
             if (l < n_layer && s_act[l]) {
                 acc = __dadd_rn(acc, cur[u]);
@@ -343,7 +342,7 @@ __global__ void __launch_bounds__(128)
             }
         }
 #pragma unroll
-        for (uint32_t u = 0; u < RB; ++u) cur[u] = nxt[u];
+        for (uint32_t u = 0; u < 16; ++u) cur[u] = nxt[u];
     }
     scores[b] = nlay ? __ddiv_rn(acc, static_cast<double>(nlay)) : 0.0;
 }
