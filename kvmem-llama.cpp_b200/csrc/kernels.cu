@@ -1046,10 +1046,6 @@ template <> struct QBlk<1> {  // q4_0 {f16 d; u8 q[16]: lo nibble j, hi nibble j
 #ifndef KVMRET_Q_MINB
 #define KVMRET_Q_MINB 2
 #endif
-// 1: the TMA-fed assembly converts q8_0 K in the half-block layout
-#ifndef KVMRET_Q_HALF
-#define KVMRET_Q_HALF 0
-#endif
 constexpr int kQThreads = KVMRET_Q_THREADS;
 constexpr int kQStages = KVMRET_Q_STAGES;
 constexpr int kQSegBlocks = 64;   // quant blocks per warp segment
@@ -1286,195 +1282,6 @@ struct DivU32 {
         return (t + ((n - t) >> 1)) >> (l - 1);
     }
 };
-
-// ---------------------------------------------------------------------------
-// Half-block layout of the q8_0 conversion (KVMRET_Q_HALF): a row of D
-// elements is held by D/32 lanes; sub-lane s = 2q + hh holds the half hh of
-// quant block q (elements 32q + 16hh .. +15) in xl[] and the same half of
-// block D/64 + q in xh[]. Every RoPE pair (i, i + D/2) stays in one lane; the
-// FWHT strides 1-8 and D/2 run in registers, 16 .. D/4 cross lanes. A block's
-// maximum is the max of the two halves' (one shuffle); both lanes compute the
-// same scale. The lane with hh = 0 gathers its partner's four quantised words
-// and writes the whole block. A lane carries 32 values instead of 64, so more
-// warps fit per SM (the conversion is issue-bound; occupancy hides the
-// dependency chains).
-
-#if KVMRET_Q_HALF
-// 16 bytes at an even shared-memory offset a, as four words (byte 4j+k of the
-// run = byte k of p[j]).
-__device__ __forceinline__ void load16_even(const uint8_t *seg, uint32_t a, uint32_t (&p)[4]) {
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(seg + (a & ~3u));
-    const uint32_t sel = (a & 2u) ? 0x5432u : 0x3210u;
-    uint32_t prev = w[0];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t nx = w[j + 1];
-        p[j] = __byte_perm(prev, nx, sel);
-        prev = nx;
-    }
-}
-
-__device__ __forceinline__ uint32_t load_scale(const uint8_t *seg, uint32_t o) {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(seg + (o & ~3u));
-    return (o & 2u) ? (w >> 16) : (w & 0xffffu);
-}
-
-// 16 int8 values -> floats * d (as dequant_qblock for a half block)
-__device__ __forceinline__ void dequant_half_q8(uint32_t d16, const uint32_t (&p)[4],
-                                                float (&x)[16]) {
-    const float d = h2f(static_cast<uint16_t>(d16));
-    const f32x2 D2 = pk2(d, d);
-    const f32x2 M2 = pk2(8388736.0f, 8388736.0f);  // 2^23 + 128
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t u = p[j] ^ 0x80808080u;  // int8 s -> s + 128
-#pragma unroll
-        for (int k = 0; k < 4; k += 2)
-            upk2(mul2(sub2(pk2(byte_float(u, k), byte_float(u, k + 1)), M2), D2),
-                 x[4 * j + k], x[4 * j + k + 1]);
-    }
-}
-
-// quant_q8_0 of a block split over the lane pair (s, s ^ 1): d = amax / 127,
-// q = round(x / d); returns the scale bits and this half's four words.
-__device__ __forceinline__ void requant_half_q8(const float (&x)[16], uint32_t &d16,
-                                                uint32_t (&p)[4]) {
-    float m[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) m[e] = fmaxf(fabsf(x[e]), fabsf(x[e + 8]));
-#pragma unroll
-    for (int w = 4; w >= 1; w /= 2)
-#pragma unroll
-        for (int e = 0; e < w; ++e) m[e] = fmaxf(m[e], m[e + w]);
-    const float amax = fmaxf(0.0f, fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1)));
-    const float dq = __fdiv_rn(amax, 127.0f);
-    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-    d16 = f2h(dq);
-    const f32x2 ID2 = pk2(id, id), M2 = pk2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        uint32_t b[4];
-#pragma unroll
-        for (int k = 0; k < 4; k += 2) {
-            float y0, y1;
-            upk2(mul2(pk2(x[4 * j + k], x[4 * j + k + 1]), ID2), y0, y1);
-            float z0, z1;
-            upk2(add2(pk2(round_away(y0), round_away(y1)), M2), z0, z1);
-            b[k] = __float_as_uint(z0);
-            b[k + 1] = __float_as_uint(z1);
-        }
-        p[j] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-    }
-}
-
-// Converts one pass of 32 / (D/32) rows of a q8_0 K segment in place (rows
-// row_base + r of the job; see the layout above).
-template <int D>
-__device__ __forceinline__ void convert_rows_half_q8(uint8_t *seg, uint32_t lane,
-                                                     uint32_t n_rows_pass, uint32_t row_seg0,
-                                                     uint32_t row_base, const FastDiv &hkv,
-                                                     uint32_t n_rows, const float4 *tab,
-                                                     uint32_t tab_tok0, uint32_t fwht_n,
-                                                     float fwht_scale) {
-    constexpr int LPR = D / 32, BB = QBlk<0>::bytes;
-    constexpr uint32_t HEAD_BYTES = (D / 32) * BB;
-    const uint32_t r = lane / LPR, sub = lane % LPR, q = sub >> 1, hh = sub & 1u;
-    const uint32_t R = min(row_base + r, n_rows - 1);  // idle lanes recompute a valid row
-    const uint32_t tok = hkv.div(R);
-    const uint32_t o_lo = (row_seg0 + r) * HEAD_BYTES + BB * q;
-    const uint32_t o_hi = (row_seg0 + r) * HEAD_BYTES + BB * (D / 64 + q);
-    float xl[16], xh[16];
-    {
-        uint32_t p[4];
-        load16_even(seg, o_lo + 2 + 16 * hh, p);
-        dequant_half_q8(load_scale(seg, o_lo), p, xl);
-        load16_even(seg, o_hi + 2 + 16 * hh, p);
-        dequant_half_q8(load_scale(seg, o_hi), p, xh);
-    }
-    // RoPE, pair (i, i + D/2) with i = 32q + 16hh + e
-    {
-        const float4 *t4 = tab + (tok - tab_tok0) * (D / 4) + 16 * q + 8 * hh;
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-            const float4 cs = t4[e / 2];
-            const f32x2 X0 = pk2(xl[e], xl[e + 1]), X1 = pk2(xh[e], xh[e + 1]);
-            const f32x2 C = pk2(cs.x, cs.y), S = pk2(cs.z, cs.w);
-            upk2(sub2(mul2(X0, C), mul2(X1, S)), xl[e], xl[e + 1]);
-            upk2(add2(mul2(X0, S), mul2(X1, C)), xh[e], xh[e + 1]);
-        }
-    }
-    if (fwht_n) {  // fwht_n == D: scale on input, then strides 1, 2, ..., D/2
-        const f32x2 sc = pk2(fwht_scale, fwht_scale);
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-            upk2(mul2(pk2(xl[e], xl[e + 1]), sc), xl[e], xl[e + 1]);
-            upk2(mul2(pk2(xh[e], xh[e + 1]), sc), xh[e], xh[e + 1]);
-        }
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {  // stride 1
-            float u = xl[e], v = xl[e + 1];
-            xl[e] = __fadd_rn(u, v);
-            xl[e + 1] = __fsub_rn(u, v);
-            u = xh[e];
-            v = xh[e + 1];
-            xh[e] = __fadd_rn(u, v);
-            xh[e + 1] = __fsub_rn(u, v);
-        }
-#pragma unroll
-        for (int H = 2; H <= 8; H *= 2) {  // strides 2, 4, 8 in registers
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                if (e & H) continue;
-                const f32x2 a = pk2(xl[e], xl[e + 1]), b = pk2(xl[e + H], xl[e + H + 1]);
-                upk2(add2(a, b), xl[e], xl[e + 1]);
-                upk2(sub2(a, b), xl[e + H], xl[e + H + 1]);
-                const f32x2 c = pk2(xh[e], xh[e + 1]), d = pk2(xh[e + H], xh[e + H + 1]);
-                upk2(add2(c, d), xh[e], xh[e + 1]);
-                upk2(sub2(c, d), xh[e + H], xh[e + H + 1]);
-            }
-        }
-#pragma unroll
-        for (int m = 1; m < LPR; m *= 2) {  // strides 16m: partner sub-lane sub ^ m
-            const float sg = (sub & m) ? -1.0f : 1.0f;
-            const f32x2 S2 = pk2(sg, sg);
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                const float pl0 = __shfl_xor_sync(0xffffffffu, xl[e], m);
-                const float pl1 = __shfl_xor_sync(0xffffffffu, xl[e + 1], m);
-                const float ph0 = __shfl_xor_sync(0xffffffffu, xh[e], m);
-                const float ph1 = __shfl_xor_sync(0xffffffffu, xh[e + 1], m);
-                upk2(fma2(pk2(xl[e], xl[e + 1]), S2, pk2(pl0, pl1)), xl[e], xl[e + 1]);
-                upk2(fma2(pk2(xh[e], xh[e + 1]), S2, pk2(ph0, ph1)), xh[e], xh[e + 1]);
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {  // stride D/2
-            const f32x2 u = pk2(xl[e], xl[e + 1]), v = pk2(xh[e], xh[e + 1]);
-            upk2(add2(u, v), xl[e], xl[e + 1]);
-            upk2(sub2(u, v), xh[e], xh[e + 1]);
-        }
-    }
-    uint32_t dl, dh, pl[4], ph[4];
-    requant_half_q8(xl, dl, pl);
-    requant_half_q8(xh, dh, ph);
-    // the hh = 0 lane gathers its partner's words and writes the two blocks
-    uint32_t ql[8], qh[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        ql[j] = pl[j];
-        qh[j] = ph[j];
-        ql[4 + j] = __shfl_xor_sync(0xffffffffu, pl[j], 1);
-        qh[4 + j] = __shfl_xor_sync(0xffffffffu, ph[j], 1);
-    }
-    __syncwarp();
-    if (r < n_rows_pass && hh == 0) {
-        store_qblock<0>(seg, o_lo, dl, ql);
-        store_qblock<0>(seg, o_hi, dh, qh);
-    }
-    __syncwarp();
-}
-
-#endif  // KVMRET_Q_HALF
 
 // Converts the rows of one K segment in place. The row of lane pair r is job
 // row row_base + r (token (row_base + r) / n_head_kv); its cos/sin pairs are
@@ -1998,24 +1805,10 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
             }
             {
                 const uint32_t row_base = it.off / HEAD_BYTES;
-                const float4 *tab = d.staged ? reinterpret_cast<const float4 *>(buf + SEG) : it.tab;
-                const uint32_t tab0 = d.staged ? d.t0 : 0u;
-                const uint32_t n_seg_rows = min(RPW, it.n_rows - row_base);
-#if KVMRET_Q_HALF
-                if constexpr (KT == 0) {
-                    constexpr uint32_t RPP = 1024 / D;  // rows per pass of the half layout
-#pragma unroll 1
-                    for (uint32_t r0 = 0; r0 < RPW; r0 += RPP) {
-                        const uint32_t n_pass = n_seg_rows > r0 ? min(RPP, n_seg_rows - r0) : 0u;
-                        convert_rows_half_q8<D>(buf, lane, n_pass, r0, row_base + r0, hkv,
-                                                it.n_rows, tab, tab0, g.fwht_n, g.fwht_scale);
-                    }
-                } else
-#endif
-                {
-                    convert_row<D, KT>(buf, lane, n_seg_rows, row_base, hkv, it.n_rows, tab,
-                                       tab0, g.fwht_n, g.fwht_scale);
-                }
+                convert_row<D, KT>(buf, lane, min(RPW, it.n_rows - row_base), row_base, hkv,
+                                   it.n_rows,
+                                   d.staged ? reinterpret_cast<const float4 *>(buf + SEG) : it.tab,
+                                   d.staged ? d.t0 : 0u, g.fwht_n, g.fwht_scale);
             }
             // the lanes' writes to the stage before the bulk store reads it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
