@@ -1,8 +1,9 @@
 """Layer-sharded retrieval on 2 GPUs: each rank's context owns half of the
 layers; the per-(layer, block) score terms, with each layer's query flag in
-the last column of its row, are exchanged (an NCCL all-gather, or the
-scoring kernel's own writes into every rank's buffer over NVLink peer memory)
-and reduced in global layer order, so every rank
+the last column of its row, are exchanged (an NCCL all-gather, or peer
+memory: each rank's rows in its own region, read by every rank's reduction
+over NVLink after the rank's step flag) and reduced in global layer order,
+so every rank
 selects the same blocks as the single-context oracle, bit for bit, and
 assembles its own layers' windows (skipped with fewer than 2 GPUs). On one
 GPU: the peer-memory exchange's bounded wait when a rank never writes.
@@ -26,7 +27,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, out, exchange="nccl"):
+def _rank(rank, world, port, out, exchange="nccl", quant=False):
     import sys
     from datetime import timedelta
     here = os.path.dirname(os.path.abspath(__file__))
@@ -43,14 +44,20 @@ def _rank(rank, world, port, out, exchange="nccl"):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     w = synth.scaled(synth.CONFIGS[1], n_layer=4, n_blocks=96, budget_blocks=12, n_planted=4)
+    if quant:
+        w = synth.scaled(w, k_type=kvmret.TYPE_Q8_0, v_type=kvmret.TYPE_Q4_0)
     hist = synth.NumpyHistory(w)
     Ll = w.n_layer // world
     sl = slice(rank * Ll, (rank + 1) * Ll)
     r = kvmret.Retriever(config_for(w, n_layer=Ll, device=rank))
     n = w.n_tokens
-    k = np.ascontiguousarray(hist.k.reshape(w.n_layer, n, w.E)[sl])
-    v = np.ascontiguousarray(hist.v.reshape(w.n_layer, n, w.E)[sl])
-    r.append(torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    k = torch.from_numpy(np.ascontiguousarray(hist.k.reshape(w.n_layer, n, w.E)[sl])).cuda()
+    v = torch.from_numpy(np.ascontiguousarray(hist.v.reshape(w.n_layer, n, w.E)[sl])).cuda()
+    if quant:  # q8_0 K rows, q4_0 V rows, summaries from the f16 capture
+        r.append(k, kvmret.quantize_f16(v, w.v_type).view(Ll, n, -1),
+                 k_rows=kvmret.quantize_f16(k, w.k_type).view(Ll, n, -1))
+    else:
+        r.append(k, v)
     stride = r.contrib_stride
     c_loc = torch.zeros(Ll * stride, dtype=torch.float64, device="cuda")
     c_all = torch.zeros(w.n_layer * stride, dtype=torch.float64, device="cuda")
@@ -88,8 +95,8 @@ def _rank(rank, world, port, out, exchange="nccl"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
-def test_two_gpu_layer_sharded_selection_matches_oracle(exchange):
+@pytest.mark.parametrize("exchange,quant", [("nccl", False), ("p2p", False), ("p2p", True)])
+def test_two_gpu_layer_sharded_selection_matches_oracle(exchange, quant):
     import pyoracle as po
     from kvm_helpers import oracle_scores
     from kvmret import synth
@@ -100,7 +107,8 @@ def test_two_gpu_layer_sharded_selection_matches_oracle(exchange):
     mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, out, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, out, exchange, quant))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
