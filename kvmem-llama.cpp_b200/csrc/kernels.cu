@@ -1090,8 +1090,10 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
 // candidates for a wrong carry are the ties y = +-0.5 (sum 1 - 2^-25 rounds
 // to 1, as wanted) and y = +-(0.5 - 2^-25) (sum 1 - 2^-24, exact, truncates
 // to 0). Checked against the host roundf on every float of magnitude < 256.
-__device__ __forceinline__ float round_away(float y) {
-    return truncf(__fadd_rn(y, copysignf(0.49999997f, y)));
+// The truncation is the conversion to an integer (toward zero), whose low
+// byte is then the int8.
+__device__ __forceinline__ int round_away_int(float y) {
+    return __float2int_rz(__fadd_rn(y, copysignf(0.49999997f, y)));
 }
 
 // Reads the quant block at byte offset o of a shared-memory segment: scale
@@ -1171,6 +1173,17 @@ __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uin
     return __byte_perm(__byte_perm(b0, b1, 0x0040u), __byte_perm(b2, b3, 0x0040u), 0x5410u);
 }
 
+// x / 127 correctly rounded, by division by a constant known in advance
+// (Brisebarre, Muller and Raina, IEEE Trans. Computers 53(8), 2004): with
+// zh = RN(1/127) and zl = RN(1/127 - zh), RN(x zh + RN(x zl)) is the
+// correctly rounded quotient. Checked against IEEE division on every
+// non-negative float: it holds for all x >= 2^-100 (below that x zl loses
+// bits to underflow), so smaller x take the division.
+__device__ __forceinline__ float div127_rn(float x) {
+    if (!(x >= 0x1p-100f)) return __fdiv_rn(x, 127.0f);
+    return __fmaf_rn(x, 0x1.020408p-7f, __fmul_rn(x, 0x1.020408p-35f));
+}
+
 template <int KT>
 __device__ __forceinline__ void requant_qblock(const float (&x)[32], uint32_t &d16,
                                                uint32_t (&p)[QBlk<KT>::words]) {
@@ -1185,10 +1198,10 @@ __device__ __forceinline__ void requant_qblock(const float (&x)[32], uint32_t &d
 #pragma unroll
             for (int e = 0; e < w; ++e) m[e] = fmaxf(m[e], m[e + w]);
         const float amax = fmaxf(0.0f, m[0]);
-        const float dq = __fdiv_rn(amax, 127.0f);
-        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        const float dq = div127_rn(amax);
+        const float id = dq != 0.0f ? __frcp_rn(dq) : 0.0f;
         d16 = f2h(dq);
-        const f32x2 ID2 = pk2(id, id), M2 = pk2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+        const f32x2 ID2 = pk2(id, id);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             uint32_t b[4];
@@ -1196,11 +1209,8 @@ __device__ __forceinline__ void requant_qblock(const float (&x)[32], uint32_t &d
             for (int k = 0; k < 4; k += 2) {
                 float y0, y1;
                 upk2(mul2(pk2(x[4 * j + k], x[4 * j + k + 1]), ID2), y0, y1);
-                // |round| <= 127: + 1.5 * 2^23 leaves it in the low byte
-                float z0, z1;
-                upk2(add2(pk2(round_away(y0), round_away(y1)), M2), z0, z1);
-                b[k] = __float_as_uint(z0);
-                b[k + 1] = __float_as_uint(z1);
+                b[k] = static_cast<uint32_t>(round_away_int(y0));
+                b[k + 1] = static_cast<uint32_t>(round_away_int(y1));
             }
             p[j] = pack_low_bytes(b[0], b[1], b[2], b[3]);
         }
@@ -1214,8 +1224,8 @@ __device__ __forceinline__ void requant_qblock(const float (&x)[32], uint32_t &d
                 vmax = x[e];
             }
         }
-        const float dq = __fdiv_rn(vmax, -8.0f);
-        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        const float dq = __fmul_rn(vmax, -0.125f);  // = vmax / -8, the same rounding
+        const float id = dq != 0.0f ? __frcp_rn(dq) : 0.0f;
         d16 = f2h(dq);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -1538,7 +1548,12 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 #ifndef KVMRET_Q_TMA
 #define KVMRET_Q_TMA 1
 #endif
+// 16-byte loads a lane keeps in flight while it copies a V part
+#ifndef KVMRET_Q_VU
+#define KVMRET_Q_VU 16
+#endif
 constexpr uint32_t kQChunk = KVMRET_Q_CHUNK;
+constexpr uint32_t kQVUnroll = KVMRET_Q_VU;
 constexpr uint32_t kQTmaTab = KVMRET_Q_TAB ? kQTabBytes : 0;
 constexpr uint32_t kQNone = 0xffffffffu;
 
@@ -1588,19 +1603,32 @@ struct QItem {
     uint32_t bytes, off, n_rows, is_v;
 };
 
+// The job of the last resolved item, kept by the issuing lane: a chunk's
+// items almost always share one job, so its fields are read from global
+// memory once per job instead of once per item.
+struct JobCache {
+    uint32_t ji = 0xffffffffu;
+    Job job;
+};
+
 // Item idx of the sequence: per job, per layer, the nk K segments of SEG
 // bytes, then the layer's whole V part as one item (copied directly).
 template <int D, int KT>
 __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_t n_fresh,
                                        uint32_t per_job, const DivU32 &div_job, uint32_t nk,
-                                       const DivU32 &div_items, QItem &it) {
+                                       const DivU32 &div_items, JobCache &jc, QItem &it) {
     constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
     const AssembleGeom &g = a.g;
     const bool fresh = idx < n_fresh * per_job;
     const uint32_t rel = fresh ? idx : idx - n_fresh * per_job;
     const uint32_t j = div_job.div(rel), rem = rel - j * per_job;
     const uint32_t l = div_items.div(rem), si = rem - l * (nk + 1);
-    const Job *jp = a.jobs + (fresh ? a.fresh_offset + j : j);
+    const uint32_t ji = fresh ? a.fresh_offset + j : j;
+    if (jc.ji != ji) {
+        jc.job = a.jobs[ji];
+        jc.ji = ji;
+    }
+    const Job *jp = &jc.job;
     const uint32_t n_tok = jp->n_tok;
     it.is_v = si >= nk;
     it.off = it.is_v ? 0u : si * SEG;
@@ -1667,26 +1695,29 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
     }
     __syncwarp();
 
-    // the warp's item sequence: chunks from a work counter, one grabbed ahead;
-    // kind 0 = fresh items (counter a.work), 1 = moved items (a.work_moved)
+    // the warp's item sequence, kept by lane 0 alone: chunks from a work
+    // counter; kind 0 = fresh items (counter a.work), 1 = moved items
+    // (a.work_moved). The chunk after the current one is claimed when the
+    // current one starts, so the atomic's result arrives while the chunk's
+    // items are converted (a claim past the end is harmless: it is ignored).
     uint32_t kind = warp == 0 ? 0u : 1u;
-    auto grab = [&]() {
-        uint32_t c = 0;
-        if (lane == 0) c = atomicAdd(kind == 0 ? a.work : a.work_moved, 1u);
-        return __shfl_sync(0xffffffffu, c, 0);
-    };
+    auto claim = [&]() { return atomicAdd(kind == 0 ? a.work : a.work_moved, 1u); };
     auto n_of = [&]() { return kind == 0 ? n_fi : n_mi; };
     auto chunks = [&]() { return (n_of() + kQChunk - 1) / kQChunk; };
-    uint32_t cur_chunk = grab(), next_chunk = 0, pos = 0;
-    if (cur_chunk < chunks()) next_chunk = grab();
-    auto next_item = [&]() -> uint32_t {
+    uint32_t cur_chunk = 0, next_chunk = 0, pos = 0;
+    if (lane == 0) {
+        cur_chunk = claim();
+        next_chunk = claim();
+    }
+    JobCache jc;
+    auto next_item = [&]() -> uint32_t {  // lane 0 only
         for (;;) {
             if (cur_chunk >= chunks()) {
                 if (kind == 1) return kQNone;
                 kind = 1;  // fresh work done: join the moves
-                cur_chunk = grab();
+                cur_chunk = claim();
+                next_chunk = claim();
                 pos = 0;
-                if (cur_chunk < chunks()) next_chunk = grab();
                 continue;
             }
             const uint32_t idx = cur_chunk * kQChunk + pos;
@@ -1696,22 +1727,22 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
             }
             cur_chunk = next_chunk;
             pos = 0;
-            if (cur_chunk < chunks()) next_chunk = grab();
+            if (cur_chunk < chunks()) next_chunk = claim();
         }
     };
     // issue (lane 0): resolve the next item into the stage's descriptor, arm
     // the stage's barrier and start its bulk copies (moved items)
     auto issue = [&](uint32_t k) {
+        if (lane != 0) return;
         const uint32_t s = k % S;
         const uint32_t idx = next_item();
-        if (lane != 0) return;
         QDesc &d = desc[s];
         d.idx = idx;
         d.kind = 0;
         d.staged = 0;
         d.t0 = 0;
         if (idx == kQNone ||
-            !q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items, d.it))
+            !q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items, jc, d.it))
             return;
         if (d.it.is_v) {
             d.kind = 3;
@@ -1760,13 +1791,13 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         issue(issued++);
         __syncwarp();
         const uint32_t dk = d.kind;
-        if (dk == 3) {  // V: global to global, 8 x 16 bytes in flight per lane
+        if (dk == 3) {  // V: global to global, kQVUnroll x 16 bytes in flight per lane
             const QItem &it = d.it;
             const uint4 *sp = reinterpret_cast<const uint4 *>(it.src);
             uint4 *dp = reinterpret_cast<uint4 *>(it.dst);
             uint4 *rp = reinterpret_cast<uint4 *>(it.raw);
             const uint32_t nq = it.bytes / 16;
-            constexpr uint32_t U = 8;
+            constexpr uint32_t U = kQVUnroll;
             uint32_t q0 = 0;
             for (; q0 + 32 * U <= nq; q0 += 32 * U) {
                 uint4 v[U];
