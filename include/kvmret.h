@@ -505,17 +505,19 @@ int kvmret_lanes_select_apply_async(kvmret_lanes *g, const double *rows_all, uin
 int kvmret_prefill_score(kvmret_ctx *ctx, const uint16_t *q_dev, uint32_t n_tok, uint32_t top_k,
                          uint8_t *sel_dev, float *scores_dev, uint32_t *n_sel_out);
 /* C = alpha * A * B^T on the tensor cores: A [m][k], B [n][k] f16 row-major,
- * C [m][n] f32; m % 128 == 0, n % 256 == 0, k % 64 == 0, 16-byte aligned
- * operands. err_dev (optional device word) is set to 1 if the kernel's
+ * C [m][n] f32; m % 128 == 0, n % 16 == 0, k % 64 == 0, 16-byte aligned
+ * operands. C is computed in 128 x 256 tiles (the last tile of a row may be
+ * partial). err_dev (optional device word) is set to 1 if the kernel's
  * pipeline gave up waiting. The prefill scorer's contraction. */
 int kvmret_gemm_f16_nt(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
                        uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, void *stream);
 /* The same with a caller workspace of kvmret_gemm_ws_bytes(m, n, k) bytes
- * (0: none needed, ws_dev may be NULL). When the 128 x 256 tiles would leave
- * enough SMs idle for it to pay, the grid is one CTA per SM: a CTA per tile runs the first k-steps
- * of its tile in lockstep with the others (the k-slices of A and B shared in
- * L2), the remaining CTAs split the k tails of all tiles, and a second launch
- * adds the pieces in a fixed order, so results repeat run to run. */
+ * (0: none needed, ws_dev may be NULL). When the tiles would leave enough SMs
+ * idle for it to pay, the grid is one CTA per SM: a CTA per tile runs the
+ * first k-steps of its tile in lockstep with the others (the k-slices of A
+ * and B shared in L2), the remaining CTAs split the k tails of all tiles, and
+ * a second launch adds the pieces in a fixed order, so results repeat run to
+ * run. */
 size_t kvmret_gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k);
 int kvmret_gemm_f16_nt_ws(const uint16_t *a_dev, const uint16_t *b_dev, float *c_dev, uint32_t m,
                           uint32_t n, uint32_t k, float alpha, uint32_t *err_dev, float *ws_dev,

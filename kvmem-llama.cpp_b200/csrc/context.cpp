@@ -1660,8 +1660,8 @@ int kvmret_gemm_f16_nt(const uint16_t *a, const uint16_t *b, float *c, uint32_t 
     // the epilogue writes C with 16-byte vector stores
     if (reinterpret_cast<uintptr_t>(c) & 15)
         return fail(KVMRET_ERR_ARG, "gemm output must be 16-byte aligned");
-    if (m % 128 || n % 256 || k % 64 || k == 0)
-        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
+    if (m == 0 || m % 128 || n == 0 || n % 16 || k % 64 || k == 0)
+        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 16 == 0, k %% 64 == 0");
     CUtensorMap ma, mb;
     CK(kvmret::make_gemm_maps(a, b, m, n, k, &ma, &mb));
     CK(kvmret::launch_gemm_f16_nt(ma, mb, c, m, n, k, alpha, err,
@@ -1679,8 +1679,8 @@ int kvmret_gemm_f16_nt_ws(const uint16_t *a, const uint16_t *b, float *c, uint32
     if (!a || !b || !c) return fail(KVMRET_ERR_ARG, "null operand");
     if ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(ws)) & 15)
         return fail(KVMRET_ERR_ARG, "gemm output and workspace must be 16-byte aligned");
-    if (m % 128 || n % 256 || k % 64 || k == 0)
-        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 256 == 0, k %% 64 == 0");
+    if (m == 0 || m % 128 || n == 0 || n % 16 || k % 64 || k == 0)
+        return fail(KVMRET_ERR_ARG, "gemm needs m %% 128 == 0, n %% 16 == 0, k %% 64 == 0");
     const size_t need = kvmret::gemm_ws_bytes(m, n, k);
     if (need && (!ws || ws_bytes < need))
         return fail(KVMRET_ERR_ARG, "gemm workspace of %zu bytes, %zu needed", ws_bytes, need);
@@ -1727,7 +1727,7 @@ int kvmret_prefill_score(kvmret_ctx *c, const uint16_t *q, uint32_t n_tok, uint3
         CK(cudaMemsetAsync(c->pf_a, 0, static_cast<size_t>(rows) * K * 2, c->st));
         c->pf_rows = rows;
     }
-    const uint32_t n_used = (nb + 255) / 256 * 256;
+    const uint32_t n_used = (nb + 15) / 16 * 16;  // C's row length (a multiple of 16)
     CK(kvmret::launch_mhat(c->summ, c->pf_b, L, Hkv, D, c->ncap, c->mhat_valid, nb, K, c->st));
     c->mhat_valid = nb;
     CK(kvmret::launch_qhat(q, c->pf_a, L, n_tok, c->cfg.n_head, Hkv, D, K, c->st));

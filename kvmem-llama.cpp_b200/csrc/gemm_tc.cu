@@ -6,7 +6,8 @@
 //
 // A CTA computes 128 x 256 tiles of C (or k-ranges of them, below) with the
 // accumulator in tensor memory (two 256-column f32 buffers of the SM's 512
-// TMEM columns). Warp roles:
+// TMEM columns); the last tile of a row may be partial (its columns past n
+// are loaded as zeros and not stored). Warp roles:
 //   warp 0      TMA producer: 2-D tiled loads of A (128 x 64) and B (256 x 64)
 //               into a 4-stage shared-memory ring, 128-byte swizzle, no
 //               multicast; completion by mbarrier transaction counts;
@@ -16,6 +17,9 @@
 //               accumulator to the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time (warp w
 //               reads TMEM lanes 32 * (w % 4) ..), scale, 16-byte stores.
+// (A 240-wide tile, 144 CTAs instead of 128 for a 2048 x 2048 product, was
+// built and measured: no faster, 0.448 against 0.445 ms at config 4. The
+// tiles' L2-to-SM traffic, not the idle SMs, sets the pace.)
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in
 // *err, stops issuing, drains what it issued (bounded), frees its TMEM and
 // returns.
@@ -344,22 +348,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t r = 32 * qd + lane;
             float *dst_row;
             const float scale = kind == 0 ? alpha : 1.0f;
+            const uint32_t n0 = (t % tiles_n) * kTileN;
+            // columns of C this tile holds (ldc = n; a row's last tile may be
+            // partial); a workspace slot takes the whole tile
+            const uint32_t ncols =
+                kind < 2 ? min(static_cast<uint32_t>(kTileN), ldc - n0) : kTileN;
             if (kind < 2)
-                dst_row = c + static_cast<size_t>((t / tiles_n) * kTileM + r) * ldc +
-                          (t % tiles_n) * kTileN;
+                dst_row = c + static_cast<size_t>((t / tiles_n) * kTileM + r) * ldc + n0;
             else
                 dst_row = ws + (static_cast<size_t>(slot) * kTileM + r) * kTileN;
+            const uint32_t tacc = tmem + ((32 * qd) << 16) + b * kTileN;
 #pragma unroll 1
-            for (uint32_t col = 0; col < kTileN; col += 32) {
+            for (uint32_t col = 0; col < ncols; col += 32) {  // ncols: a multiple of 16
                 uint32_t v[32];
-                tmem_ld32(tmem + ((32 * qd) << 16) + b * kTileN + col, v);
+                tmem_ld32(tacc + col, v);
                 float4 *dst = reinterpret_cast<float4 *>(dst_row + col);
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    dst[e] = make_float4(scale * __uint_as_float(v[4 * e]),
-                                         scale * __uint_as_float(v[4 * e + 1]),
-                                         scale * __uint_as_float(v[4 * e + 2]),
-                                         scale * __uint_as_float(v[4 * e + 3]));
+                for (uint32_t e = 0; e < 8; ++e)
+                    if (col + 4 * e < ncols)
+                        dst[e] = make_float4(scale * __uint_as_float(v[4 * e]),
+                                             scale * __uint_as_float(v[4 * e + 1]),
+                                             scale * __uint_as_float(v[4 * e + 2]),
+                                             scale * __uint_as_float(v[4 * e + 3]));
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -381,7 +391,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // C = alpha * (the main CTA's sums in C + the helpers' pieces of the tile, in
-// order). One CTA per tile.
+// order). One CTA per tile; columns past n (= ldc) are skipped.
 __global__ void __launch_bounds__(256)
     gemm_fixup_kernel(float *__restrict__ c, uint32_t ldc, const float *__restrict__ ws,
                       const __grid_constant__ GemmSplit sp, float alpha, const uint32_t *err) {
@@ -394,6 +404,7 @@ __global__ void __launch_bounds__(256)
     const uint32_t m0 = (t / sp.tiles_n) * kTileM, n0 = (t % sp.tiles_n) * kTileN;
     for (uint32_t e = threadIdx.x; e < kTileM * kTileN / 4; e += blockDim.x) {
         const uint32_t r = e / (kTileN / 4), c4 = e % (kTileN / 4);
+        if (n0 + 4 * c4 >= ldc) continue;
         float4 *cp = reinterpret_cast<float4 *>(c + static_cast<size_t>(m0 + r) * ldc + n0) + c4;
         float4 acc = *cp;
         for (uint32_t p = 0; p < n_pieces; ++p) {
@@ -442,36 +453,25 @@ cudaError_t encode_kmajor(CUtensorMap *map, const void *base, uint32_t rows, uin
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-}  // namespace
-
-cudaError_t make_gemm_maps(const void *a, const void *b, uint32_t m, uint32_t n, uint32_t k,
-                           CUtensorMap *map_a, CUtensorMap *map_b) {
-    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15)
-        return cudaErrorInvalidValue;
-    cudaError_t e = encode_kmajor(map_a, a, m, k, kTileM);
-    if (e == cudaSuccess) e = encode_kmajor(map_b, b, n, k, kTileN);
-    return e;
-}
-
-size_t gemm_smem_bytes() {
-    return kStages * static_cast<size_t>(kStageBytes) + 1024 /* alignment */ +
-           (2 * kStages + 4) * 8 + 16;
-}
-
-namespace {
 int sm_count() {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return 0;
+    static int n = [] {
+        int dev = 0, v = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return 0;
+        return v;
+    }();
     return n;
+}
+
+bool shape_ok(uint32_t m, uint32_t n, uint32_t k) {
+    return m && m % kTileM == 0 && n && n % 16 == 0 && k && k % kTileK == 0;
 }
 
 // The split of an m x n x k product on this device (x == n_ktiles: none).
 GemmSplit plan_split(uint32_t m, uint32_t n, uint32_t k) {
     GemmSplit sp{};
-    sp.tiles_n = n / kTileN;
+    sp.tiles_n = (n + kTileN - 1) / kTileN;
     sp.n_tiles = sp.tiles_n * (m / kTileM);
     sp.n_ktiles = k / kTileK;
     sp.x = sp.n_ktiles;
@@ -503,10 +503,25 @@ GemmSplit plan_split(uint32_t m, uint32_t n, uint32_t k) {
     sp.pieces = static_cast<uint32_t>((L + share - 1) / share + 1);
     return sp;
 }
+
+size_t smem_bytes() {
+    return kStages * static_cast<size_t>(kStageBytes) + 1024 /* alignment */ +
+           (2 * kStages + 4) * 8 + 16;
+}
 }  // namespace
 
+cudaError_t make_gemm_maps(const void *a, const void *b, uint32_t m, uint32_t n, uint32_t k,
+                           CUtensorMap *map_a, CUtensorMap *map_b) {
+    if (!shape_ok(m, n, k)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15)
+        return cudaErrorInvalidValue;
+    cudaError_t e = encode_kmajor(map_a, a, m, k, kTileM);
+    if (e == cudaSuccess) e = encode_kmajor(map_b, b, n, k, kTileN);
+    return e;
+}
+
 size_t gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k) {
-    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return 0;
+    if (!shape_ok(m, n, k)) return 0;
     const GemmSplit sp = plan_split(m, n, k);
     if (sp.x == sp.n_ktiles) return 0;
     return static_cast<size_t>(sp.n_tiles) * sp.pieces * kTileM * kTileN * sizeof(float);
@@ -515,8 +530,8 @@ size_t gemm_ws_bytes(uint32_t m, uint32_t n, uint32_t k) {
 cudaError_t launch_gemm_f16_nt(const CUtensorMap &map_a, const CUtensorMap &map_b, float *c,
                                uint32_t m, uint32_t n, uint32_t k, float alpha, uint32_t *err,
                                cudaStream_t st, float *ws, size_t ws_bytes) {
-    if (m % kTileM || n % kTileN || k % kTileK || k == 0) return cudaErrorInvalidValue;
-    const size_t smem = gemm_smem_bytes();
+    if (!shape_ok(m, n, k)) return cudaErrorInvalidValue;
+    const size_t smem = smem_bytes();
     cudaError_t e = cudaFuncSetAttribute(gemm_f16_nt_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));

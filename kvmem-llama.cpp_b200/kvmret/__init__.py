@@ -858,7 +858,7 @@ class Lanes:
 
 def gemm_f16_nt(a, b, alpha=1.0, stream=0):
     """C = alpha * a @ b.T on the tensor cores; a [m][k], b [n][k] f16 CUDA tensors
-    (m % 128 == 0, n % 256 == 0, k % 64 == 0). Returns (C f32 CUDA tensor, error flag)."""
+    (m % 128 == 0, n % 16 == 0, k % 64 == 0). Returns (C f32 CUDA tensor, error flag)."""
     import torch
     m, k = a.shape
     n = b.shape[0]

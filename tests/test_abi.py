@@ -55,3 +55,12 @@ def test_gemm_rejects_misaligned_output_before_any_launch():
     rc = kvmret.lib.kvmret_gemm_f16_nt(16, 16, 17, 128, 256, 64, 1.0, None, None)
     assert rc == -1
     assert b"aligned" in kvmret.lib.kvmret_last_error()
+
+
+def test_gemm_rejects_shapes_before_any_launch():
+    # n must be a multiple of 16 (C rows are written as 16-byte vectors), m of
+    # 128 and k of 64; checked on the host, the addresses are never used
+    for m, n, k in ((128, 200, 64), (100, 256, 64), (128, 256, 100), (128, 0, 64)):
+        rc = kvmret.lib.kvmret_gemm_f16_nt(16, 16, 32, m, n, k, 1.0, None, None)
+        assert rc == -1
+        assert b"gemm needs" in kvmret.lib.kvmret_last_error()

@@ -25,8 +25,12 @@ SCORE_TOL = 3e-3  # f16 unit-length operands: |cos error| <= ~2 * 2^-11 per term
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 1024), (128, 768, 8192),
-                                   (128, 256, 65536)])
+                                   (128, 256, 65536), (128, 272, 128), (2048, 2048, 1024),
+                                   (1280, 2000, 512)])
 def test_gemm_matches_float64(m, n, k):
+    """Whole 256-wide tiles (the first four and 2048 x 2048) and partial last
+    tiles: 128 x 272 (a 16-column last tile) and 1280 x 2000 (a 208-column
+    last tile, so one 32-column chunk of the epilogue is cut at 16)."""
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
     a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).half()
     b = (torch.randn(n, k, device="cuda", generator=g) * 0.5).half()
@@ -40,13 +44,14 @@ def test_gemm_matches_float64(m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 768, 8192), (512, 2048, 4096), (256, 512, 64),
-                                   (2048, 2048, 1024)])
+                                   (2048, 2048, 1024), (256, 272, 4096)])
 def test_split_gemm_matches_float64(m, n, k):
-    """The workspace form: with few tiles (3, 32) one CTA per SM runs (a
+    """The workspace form: with few tiles (3, 32, 4) one CTA per SM runs (a
     lockstep CTA per tile for the first k-steps, helpers on the k tails, the
-    pieces added by the fix-up launch); with a single k-step per tile
-    (256 x 512 x 64) or 128 tiles, where the split would not pay, a tile per
-    CTA. Same bound as the plain form, and the same result on a second run."""
+    pieces added by the fix-up launch; 256 x 272 with 16-column last tiles);
+    with a single k-step per tile (256 x 512 x 64) or 128 tiles, where the
+    split would not pay, a tile per CTA. Same bound as the plain form, and
+    the same result on a second run."""
     g = torch.Generator(device="cuda").manual_seed(m * 3 + n + k)
     a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).half()
     b = (torch.randn(n, k, device="cuda", generator=g) * 0.5).half()
