@@ -1513,25 +1513,26 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 // S13, the GPU-resident step's quantised-K assembly: persistent warps fed by
 // TMA bulk copies.
 //
-// Work: the flat sequence of items (job, layer, segment) over all fresh jobs,
-// then all moved jobs; a segment is a 16-row K segment (converted) or the
-// layer's whole V part (copied global to global by the warp's lanes, with no
-// stage: V needs no conversion, and one item per V part keeps the per-item
-// bookkeeping off the issue slots). Warps take chunks of kQChunk items from two
+// Work: the flat sequence of items (job, layer, piece) over all fresh jobs,
+// then all moved jobs; a piece is kQItemSegs 16-row K segments (converted one
+// after the other) or the layer's whole V part (copied global to global by
+// the warp's lanes, with no stage: V needs no conversion, and one item per V
+// part keeps the per-item bookkeeping off the issue slots). Warps take chunks of kQChunk items from two
 // counters the plan zeroes, so all warps finish together: the first warp of
 // every CTA takes fresh chunks (host-link reads) until none is left and then
 // moved ones, the other warps take moved chunks only, so the host-link reads
 // and the HBM moves overlap. A warp streams its
-// items through a ring of kQStages shared-memory stages: one lane resolves the
+// items through a ring of kQTmaStages shared-memory stages: one lane resolves the
 // next item into the stage's descriptor and issues a 1-D bulk copy
 // (cp.async.bulk, no multicast, this GPU's memory only) of its bytes
 // (optionally also the cos/sin rows of the tokens a K segment spans, else
 // those come from the position table through L1), completing on the stage's
-// mbarrier, kQStages - 2 items ahead of the item being converted; the
+// mbarrier, kQTmaStages - 2 items ahead of the item being converted; the
 // converted stage goes back to the window with a bulk store. The conversion
-// (about 1,500 warp instructions per 16-row segment) bounds the kernel, not
-// the copies: the cp.async form above runs at the same speed. Fresh items (host repository, read over the host link) are read
-// with plain loads by the lanes, which also write them to their pool slot.
+// (about 1,300 warp instructions per 16-row segment) and the per-item
+// bookkeeping bound the kernel, not the copies. Fresh items (host repository,
+// read over the host link) are read with plain loads by the lanes, which also
+// write them to their pool slot.
 // Every mbarrier wait is bounded (2 s); on a timeout the warp records error
 // 0x200 in the plan's error word, waits (bounded) for the copies it issued,
 // and stops.
@@ -1552,7 +1553,19 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 #ifndef KVMRET_Q_VU
 #define KVMRET_Q_VU 16
 #endif
+// 16-row K segments per work item (one bulk copy, one descriptor), and the
+// stages of a warp's ring: two segments per item halve the per-item
+// bookkeeping (measured 6.6 % faster than one), and three stages of 4352
+// bytes keep two CTAs of 8 warps per SM
+#ifndef KVMRET_Q_ITEM_SEGS
+#define KVMRET_Q_ITEM_SEGS 2
+#endif
+#ifndef KVMRET_Q_TMA_STAGES
+#define KVMRET_Q_TMA_STAGES 3
+#endif
 constexpr uint32_t kQChunk = KVMRET_Q_CHUNK;
+constexpr uint32_t kQItemSegs = KVMRET_Q_ITEM_SEGS;
+constexpr uint32_t kQTmaStages = KVMRET_Q_TMA_STAGES;
 constexpr uint32_t kQVUnroll = KVMRET_Q_VU;
 constexpr uint32_t kQTmaTab = KVMRET_Q_TAB ? kQTabBytes : 0;
 constexpr uint32_t kQNone = 0xffffffffu;
@@ -1617,7 +1630,7 @@ template <int D, int KT>
 __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_t n_fresh,
                                        uint32_t per_job, const DivU32 &div_job, uint32_t nk,
                                        const DivU32 &div_items, JobCache &jc, QItem &it) {
-    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
+    constexpr uint32_t SEG = kQItemSegs * kQSegBlocks * QBlk<KT>::bytes;
     const AssembleGeom &g = a.g;
     const bool fresh = idx < n_fresh * per_job;
     const uint32_t rel = fresh ? idx : idx - n_fresh * per_job;
@@ -1667,13 +1680,14 @@ template <int D, int KT>
 __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
     assemble_quant_tma_kernel(const __grid_constant__ AsmLaunch a) {
     dep_wait();
-    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;
-    constexpr uint32_t STAGE = SEG + kQTmaTab;
+    constexpr uint32_t SEG = kQSegBlocks * QBlk<KT>::bytes;  // one warp's 16 rows
+    constexpr uint32_t SEGI = kQItemSegs * SEG;               // a K item
+    constexpr uint32_t STAGE = SEGI + kQTmaTab;
     constexpr uint32_t PAIRS = D / 4, TAB_TOK = kQTmaTab / (PAIRS * sizeof(float4));
     constexpr uint32_t HEAD_BYTES = (D / 32) * QBlk<KT>::bytes;
-    constexpr uint32_t RPW = SEG / HEAD_BYTES;
-    constexpr uint32_t S = kQStages, P = kQStages - 2;
-    static_assert(kQStages >= 3, "the ring needs a stage for the store in flight");
+    constexpr uint32_t RPW = SEG / HEAD_BYTES, RPI = kQItemSegs * RPW;
+    constexpr uint32_t S = kQTmaStages, P = kQTmaStages - 2;
+    static_assert(kQTmaStages >= 3, "the ring needs a stage for the store in flight");
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const AssembleGeom &g = a.g;
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
@@ -1681,7 +1695,7 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + nwarp * S * STAGE) + warp * S;
     QDesc *desc = reinterpret_cast<QDesc *>(smem_raw + nwarp * S * (STAGE + 8)) + warp * S;
     const uint32_t T = g.block_tokens;
-    const uint32_t nk = (T * static_cast<uint32_t>(g.k_row) + SEG - 1) / SEG;
+    const uint32_t nk = (T * static_cast<uint32_t>(g.k_row) + SEGI - 1) / SEGI;
     const uint32_t n_items_job = nk + 1, per_job = g.n_layer * n_items_job;
     const DivU32 div_job(per_job), div_items(n_items_job);
     const uint32_t n_moved = a.counts[0], n_fresh = a.counts[1];
@@ -1752,7 +1766,7 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         {
             const uint32_t row_base = d.it.off / HEAD_BYTES;
             d.t0 = hkv.div(row_base);
-            const uint32_t nt = hkv.div(min(row_base + RPW, d.it.n_rows) - 1) - d.t0 + 1;
+            const uint32_t nt = hkv.div(min(row_base + RPI, d.it.n_rows) - 1) - d.t0 + 1;
             if (!d.it.raw && nt <= TAB_TOK) {
                 tab_bytes = nt * PAIRS * static_cast<uint32_t>(sizeof(float4));
                 d.staged = 1;
@@ -1769,7 +1783,7 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
                      : "memory");
         const uint32_t buf = smem_addr(wbuf + s * STAGE);
         bulk_load(buf, d.it.src, d.it.bytes, bar);
-        if (tab_bytes) bulk_load(buf + SEG, d.it.tab + d.t0 * PAIRS, tab_bytes, bar);
+        if (tab_bytes) bulk_load(buf + SEGI, d.it.tab + d.t0 * PAIRS, tab_bytes, bar);
     };
 
     uint32_t phase = 0;  // bit s: parity of stage s's next completion
@@ -1785,7 +1799,7 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         // the stage of item c + P last served item c + P - S, whose store
         // must have read its bytes; the store of item c - 1 may still run
         if (lane == 0)
-            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kQStages - (kQStages - 2) - 1)
+            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(S - P - 1)
                          : "memory");
         __syncwarp();
         issue(issued++);
@@ -1834,11 +1848,14 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
                 }
                 phase ^= 1u << s;
             }
-            {
-                const uint32_t row_base = it.off / HEAD_BYTES;
-                convert_row<D, KT>(buf, lane, min(RPW, it.n_rows - row_base), row_base, hkv,
-                                   it.n_rows,
-                                   d.staged ? reinterpret_cast<const float4 *>(buf + SEG) : it.tab,
+#pragma unroll 1
+            for (uint32_t h = 0; h < kQItemSegs; ++h) {  // the item's 16-row segments
+                const uint32_t row_base = it.off / HEAD_BYTES + h * RPW;
+                if (row_base >= it.n_rows) break;
+                convert_row<D, KT>(buf + h * SEG, lane, min(RPW, it.n_rows - row_base), row_base,
+                                   hkv, it.n_rows,
+                                   d.staged ? reinterpret_cast<const float4 *>(buf + SEGI)
+                                            : it.tab,
                                    d.staged ? d.t0 : 0u, g.fwht_n, g.fwht_scale);
             }
             // the lanes' writes to the stage before the bulk store reads it
@@ -2441,9 +2458,9 @@ cudaError_t launch_assemble_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t 
 template <int D, int KT>
 cudaError_t launch_assemble_quant_t(const AsmLaunch &a, uint32_t n_jobs, cudaStream_t st) {
     if (a.counts && KVMRET_Q_TMA) {  // the GPU-resident step: persistent TMA-fed warps
-        constexpr uint32_t STAGE = kQSegBlocks * QBlk<KT>::bytes + kQTmaTab;
+        constexpr uint32_t STAGE = kQItemSegs * kQSegBlocks * QBlk<KT>::bytes + kQTmaTab;
         const size_t smem =
-            static_cast<size_t>(kQThreads / 32) * kQStages * (STAGE + 8 + sizeof(QDesc));
+            static_cast<size_t>(kQThreads / 32) * kQTmaStages * (STAGE + 8 + sizeof(QDesc));
         auto kfn = assemble_quant_tma_kernel<D, KT>;
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
