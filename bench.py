@@ -421,7 +421,7 @@ def run_reference(args, w):
 # ). The traffic grows with the blocks a launch moves, so a launch's traffic is
 # this ratio times its algorithmic bytes.
 NCU_TRAFFIC_RATIO = {"assemble_kernel": 1588.2 / 1619.0,
-                     "assemble_quant_tma_kernel": 665.2 / 695.2}
+                     "assemble_quant_tma_kernel": 675.3 / 695.2}
 
 
 class OracleCheck:
