@@ -1529,10 +1529,10 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 // those come from the position table through L1), completing on the stage's
 // mbarrier, kQTmaStages - 2 items ahead of the item being converted; the
 // converted stage goes back to the window with a bulk store. The conversion
-// (about 1,300 warp instructions per 16-row segment) and the per-item
-// bookkeeping bound the kernel, not the copies. Fresh items (host repository,
-// read over the host link) are read with plain loads by the lanes, which also
-// write them to their pool slot.
+// and the per-item bookkeeping (about 1,200 warp instructions per 16-row
+// segment in all) bound the kernel, not the copies. Fresh items (host
+// repository, read over the host link) are read with plain loads by the
+// lanes, which also write them to their pool slot.
 // Every mbarrier wait is bounded (2 s); on a timeout the warp records error
 // 0x200 in the plan's error word, waits (bounded) for the copies it issued,
 // and stops.
