@@ -1566,6 +1566,13 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 constexpr uint32_t kQChunk = KVMRET_Q_CHUNK;
 constexpr uint32_t kQItemSegs = KVMRET_Q_ITEM_SEGS;
 constexpr uint32_t kQTmaStages = KVMRET_Q_TMA_STAGES;
+// 1: a K item that follows the previous one in the same (job, layer) is
+// resolved by stepping that item's addresses; 2: the same, checked against
+// the full resolution (a mismatch sets 0x400 in the plan's error word)
+#ifndef KVMRET_Q_CURSOR
+#define KVMRET_Q_CURSOR 1
+#endif
+constexpr uint32_t kQCursor = KVMRET_Q_CURSOR;
 constexpr uint32_t kQVUnroll = KVMRET_Q_VU;
 constexpr uint32_t kQTmaTab = KVMRET_Q_TAB ? kQTabBytes : 0;
 constexpr uint32_t kQNone = 0xffffffffu;
@@ -1629,7 +1636,8 @@ struct JobCache {
 template <int D, int KT>
 __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_t n_fresh,
                                        uint32_t per_job, const DivU32 &div_job, uint32_t nk,
-                                       const DivU32 &div_items, JobCache &jc, QItem &it) {
+                                       const DivU32 &div_items, JobCache &jc, QItem &it,
+                                       uint32_t &si_out, uint32_t &ktotal_out) {
     constexpr uint32_t SEG = kQItemSegs * kQSegBlocks * QBlk<KT>::bytes;
     const AssembleGeom &g = a.g;
     const bool fresh = idx < n_fresh * per_job;
@@ -1643,6 +1651,8 @@ __device__ __forceinline__ bool q_item(const AsmLaunch &a, uint32_t idx, uint32_
     }
     const Job *jp = &jc.job;
     const uint32_t n_tok = jp->n_tok;
+    si_out = si;
+    ktotal_out = n_tok * static_cast<uint32_t>(g.k_row);
     it.is_v = si >= nk;
     it.off = it.is_v ? 0u : si * SEG;
     const uint32_t total = n_tok * static_cast<uint32_t>(it.is_v ? g.v_row : g.k_row);
@@ -1674,6 +1684,8 @@ struct QDesc {
                      // 3 V (copied directly by the warp)
     uint32_t t0;     // first token of a K segment
     uint32_t staged; // its cos/sin rows are in the stage
+    uint32_t si;     // the item's index within its (job, layer)
+    uint32_t ktotal; // K bytes of its (job, layer)
 };
 
 template <int D, int KT>
@@ -1755,9 +1767,43 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
         d.kind = 0;
         d.staged = 0;
         d.t0 = 0;
-        if (idx == kQNone ||
-            !q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items, jc, d.it))
-            return;
+        if (idx == kQNone) return;
+        bool ok;
+        const QDesc &pd = desc[(k + S - 1) % S];  // the item issued before this one
+        if (kQCursor && k > 0 && idx == pd.idx + 1 && (pd.kind == 1 || pd.kind == 2) &&
+            pd.si + 1 < nk) {
+            // the next K piece of the same (job, layer): the previous one, one
+            // piece further on
+            QItem it = pd.it;
+            it.off += SEGI;
+            ok = it.off < pd.ktotal;
+            if (ok) {
+                it.bytes = min(SEGI, pd.ktotal - it.off);
+                it.src += SEGI;
+                it.dst += SEGI;
+                if (it.raw) it.raw += SEGI;
+            }
+            d.si = pd.si + 1;
+            d.ktotal = pd.ktotal;
+            if (kQCursor == 2) {  // checked form: the full resolution decides
+                QItem ref;
+                uint32_t rsi, rkt;
+                const bool rok = q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items,
+                                               jc, ref, rsi, rkt);
+                if (rok != ok || rsi != d.si || rkt != d.ktotal ||
+                    (ok && (ref.src != it.src || ref.dst != it.dst || ref.raw != it.raw ||
+                            ref.tab != it.tab || ref.bytes != it.bytes || ref.off != it.off ||
+                            ref.n_rows != it.n_rows || ref.is_v != it.is_v)))
+                    atomicOr(const_cast<uint32_t *>(a.counts) + 4, 0x400u);
+                it = ref;
+                ok = rok;
+            }
+            d.it = it;
+        } else {
+            ok = q_item<D, KT>(a, idx, n_fresh, per_job, div_job, nk, div_items, jc, d.it, d.si,
+                               d.ktotal);
+        }
+        if (!ok) return;
         if (d.it.is_v) {
             d.kind = 3;
             return;
