@@ -1517,13 +1517,13 @@ __global__ void __launch_bounds__(kQThreads, KVMRET_Q_MINB)
 // then all moved jobs; a piece is kQItemSegs 16-row K segments (converted one
 // after the other) or the layer's whole V part (copied global to global by
 // the warp's lanes, with no stage: V needs no conversion, and one item per V
-// part keeps the per-item bookkeeping off the issue slots). Warps take chunks of kQChunk items from two
-// counters the plan zeroes, so all warps finish together: the first warp of
-// every CTA takes fresh chunks (host-link reads) until none is left and then
-// moved ones, the other warps take moved chunks only, so the host-link reads
-// and the HBM moves overlap. A warp streams its
-// items through a ring of kQTmaStages shared-memory stages: one lane resolves the
-// next item into the stage's descriptor and issues a 1-D bulk copy
+// part keeps the per-item bookkeeping off the issue slots). Warps take chunks
+// of kQChunk items from two counters the plan zeroes, so all warps finish
+// together: the first warp of every CTA takes fresh chunks (host-link reads)
+// until none is left and then moved ones, the other warps take moved chunks
+// only, so the host-link reads and the HBM moves overlap. A warp streams its
+// items through a ring of kQTmaStages shared-memory stages: one lane resolves
+// the next item into the stage's descriptor and issues a 1-D bulk copy
 // (cp.async.bulk, no multicast, this GPU's memory only) of its bytes
 // (optionally also the cos/sin rows of the tokens a K segment spans, else
 // those come from the position table through L1), completing on the stage's
